@@ -1,0 +1,337 @@
+/*
+ * pxb.h -- C ABI of the B200 edge-arena engine (libpxb.so).
+ *
+ * Every entry point takes plain device pointers, element counts and an
+ * opaque CUDA stream (`void *stream`, a `cudaStream_t`; NULL = legacy
+ * default stream). Nothing here allocates device memory: scratch is passed
+ * in by the caller (sizes come from the matching `*_scratch_bytes` query),
+ * and outputs the reference zero-fills are cleared by the callee on the
+ * stream. No call synchronises the host with the device.
+ *
+ * Return value: 0 on success, otherwise a PXB_E* code. `pxb_last_error()`
+ * returns a thread-local message for the last failing call on the calling
+ * host thread. Argument errors are detected on the host before any launch.
+ *
+ * Arena layout (one bucket; every column has `cap` entries, struct of
+ * arrays, slot order = the reference's slot order):
+ *   from_id  int32   source unit of the slot
+ *   to_id    int32   destination unit of the slot
+ *   dead     uint8   1 = tombstoned / never used, 0 = live
+ *   weight   float32
+ *   opt[0..2] float32 optimizer columns (opt/m, opt/v, opt/t ...), optional
+ *
+ * Citations name the reference function (path within the plastax project)
+ * each entry point stands in for.
+ */
+#ifndef PXB_H_
+#define PXB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PXB_ABI_VERSION 1
+
+/* exported from libpxb.so (built with hidden default visibility) */
+#if defined(__GNUC__)
+#define PXB_API __attribute__((visibility("default")))
+#else
+#define PXB_API
+#endif
+
+/* status codes */
+#define PXB_OK 0
+#define PXB_EINVAL 1     /* bad argument (null pointer, size, enum)      */
+#define PXB_ECUDA 2      /* a CUDA runtime call failed                   */
+#define PXB_ESCRATCH 3   /* scratch buffer too small                     */
+#define PXB_EUNSUPPORTED 4
+
+/* monoids: src/plastax/monoid.py:27-59 (identities sum 0, max -inf, min +inf) */
+#define PXB_MONOID_SUM 0
+#define PXB_MONOID_MAX 1
+#define PXB_MONOID_MIN 2
+
+/* unit-side apply and its derivative from the activation */
+#define PXB_ACT_IDENTITY 0
+#define PXB_ACT_TANH 1
+#define PXB_ACT_RELU 2
+#define PXB_ACT_SIGMOID 3
+
+/* connection prune predicates recognised by the fused sweep */
+#define PXB_PRUNE_NONE 0
+#define PXB_PRUNE_ABS_BELOW 1      /* |w| <  threshold                    */
+#define PXB_PRUNE_ABS_BELOW_DST 2  /* |w| <  unit_threshold[to_id]        */
+
+/* optimizer bundles: src/plastax/optim/_sgd.py:121-127, _momentum.py:136-139,
+ * _adam.py:157-172, _rmsprop.py:135-140 */
+#define PXB_OPT_SGD 0
+#define PXB_OPT_MOMENTUM 1
+#define PXB_OPT_ADAM 2
+#define PXB_OPT_RMSPROP 3
+
+typedef struct pxb_optimizer {
+  int32_t kind;        /* PXB_OPT_* */
+  float lr;
+  float b1;            /* momentum: mu; adam: beta1; rmsprop: decay */
+  float b2;            /* adam: beta2 */
+  float eps;           /* adam: outside sqrt; rmsprop: inside sqrt */
+  float weight_decay;  /* adamw */
+} pxb_optimizer;
+
+/* growth score rules for per-unit proposals */
+#define PXB_SCORE_UNIFORM 0       /* score = uniform()                         */
+#define PXB_SCORE_UNIFORM_Q256 1  /* score = floor(uniform() * 256) / 256      */
+#define PXB_SCORE_GRAD_ACT 2      /* score = |grad[dst] * act[src]| (no draw)  */
+
+/* ------------------------------------------------------------------ */
+/* library                                                             */
+/* ------------------------------------------------------------------ */
+PXB_API int pxb_abi_version(void);
+PXB_API const char *pxb_last_error(void);
+/* Number of SMs of the current device (grid sizing). */
+PXB_API int pxb_sm_count(int32_t *out);
+
+/* ------------------------------------------------------------------ */
+/* propagation                                                         */
+/* ------------------------------------------------------------------ */
+
+/* Forward accumulate of one bucket with the linear map w * act[from]:
+ *   acc[to[s]] = acc[to[s]] (+) weight[s] * act[from[s]]   for live s.
+ * `acc` is the carried accumulator (combine_pairwise semantics).
+ * Replaces src/plastax/sweep.py:113-180 (_accumulate_into, target TO_ID)
+ * with the linear_input map of src/plastax/phases.py:535-556. */
+PXB_API int pxb_forward_accumulate(int64_t cap, const int32_t *from_id,
+                           const int32_t *to_id, const uint8_t *dead,
+                           const float *weight, const float *act,
+                           int32_t num_units, int32_t monoid, float *acc,
+                           void *stream);
+
+/* Forward accumulate fused with a prune predicate and the per-block free
+ * counts of the new tombstone mask (one read of every slot).
+ *   accumulate as pxb_forward_accumulate over the PRE-prune dead mask;
+ *   dead_out[s] = dead[s] | pred(s)   (dead_out may alias dead);
+ *   block_free[b] = #dead_out slots in [b*block_len, (b+1)*block_len).
+ * block_free may be NULL; block_len must be a power of two >= 256 when
+ * given. Replaces src/plastax/phases.py:2240-2319 (triton_forward_prune)
+ * and :2595 (free_block_counts). */
+PXB_API int pxb_forward_prune(int64_t cap, const int32_t *from_id,
+                      const int32_t *to_id, const uint8_t *dead,
+                      const float *weight, const float *act,
+                      int32_t num_units, int32_t monoid, float *acc,
+                      int32_t prune_kind, float prune_threshold,
+                      const float *unit_threshold, uint8_t *dead_out,
+                      int32_t block_len, int32_t *block_free, void *stream);
+
+/* Prune sweep on its own: dead_out = dead | pred, plus block counts.
+ * Replaces src/plastax/phases.py:1444-1498 (build_prune_conn_phase). */
+PXB_API int pxb_prune_conn(int64_t cap, const int32_t *to_id, const uint8_t *dead,
+                   const float *weight, int32_t num_units, int32_t prune_kind,
+                   float prune_threshold, const float *unit_threshold,
+                   uint8_t *dead_out, int32_t block_len, int32_t *block_free,
+                   void *stream);
+
+/* Backward accumulate of one bucket: acc[from[s]] (+)= w[s] * grad[to[s]].
+ * Source-major buckets give long source runs: reduced by warp-segmented
+ * shuffles, one atomic per run. Replaces src/plastax/sweep.py:113-180
+ * (target FROM_ID). */
+PXB_API int pxb_backward_accumulate(int64_t cap, const int32_t *from_id,
+                            const int32_t *to_id, const uint8_t *dead,
+                            const float *weight, const float *grad,
+                            int32_t num_units, int32_t monoid, float *acc,
+                            void *stream);
+
+/* Backward accumulate fused with the optimizer's incoming update, one read
+ * of every slot. Reads the OLD weight for the accumulate, then writes
+ *   g = grad[to] * act[from];  weight, opt columns <- optimizer step(g).
+ * Legal only where grad[to] is final when the bucket is swept (the
+ * topological reverse walk) and no update_unit phase intervenes.
+ * Replaces src/plastax/phases.py:1049-1104 + :1196-1242 for the optimizer
+ * bundles (src/plastax/optim). opt_m/opt_v/opt_t may be NULL when the
+ * optimizer keeps no such column; acc may be NULL (update only). */
+PXB_API int pxb_backward_update(int64_t cap, const int32_t *from_id,
+                        const int32_t *to_id, const uint8_t *dead,
+                        float *weight, const float *grad, const float *act,
+                        int32_t num_units, float *acc,
+                        const pxb_optimizer *opt, float *opt_m, float *opt_v,
+                        float *opt_t, void *stream);
+
+/* Unit apply with masked merge (src/plastax/sweep.py:183-230):
+ * a unit i is finalized iff (level == NULL || level[i] == target_level)
+ *   && (is_input == NULL || !is_input[i]) && (pruned == NULL || !pruned[i]).
+ * forward (mode 0):  out[i] = act_fn(acc[i])
+ * backward (mode 1): out[i] = (acc[i] + (seed ? seed[i] : 0)) * act_fn'(act[i])
+ * Finalized units have acc[i] reset to the monoid identity. */
+PXB_API int pxb_unit_apply(int32_t num_units, int32_t mode, int32_t act_kind,
+                   int32_t monoid, float *acc, const float *act,
+                   const float *seed, const int32_t *level,
+                   int32_t target_level, const uint8_t *is_input,
+                   const uint8_t *pruned, float *out, void *stream);
+
+/* Fill n floats with a value (accumulator identity reset). */
+PXB_API int pxb_fill_f32(int64_t n, float value, float *out, void *stream);
+
+/* Mean-squared-error loss over the outputs (scripts/parity/reference.py:338):
+ * seed[out[k]] = act[out[k]] - target[k]; loss_out[0] = 0.5 * sum diff^2
+ * (summed in output order). */
+PXB_API int pxb_mse_loss(int32_t num_outputs, const int32_t *output_ids,
+                 const float *act, const float *target, float *seed,
+                 float *loss_out, void *stream);
+
+/* ------------------------------------------------------------------ */
+/* batched (make_step(batch_size=B)), unit columns laid out [N, B]     */
+/* ------------------------------------------------------------------ */
+
+/* out[to[s], b] += w[s] * x[from[s], b] for live s, all b < B
+ * (B % 4 == 0, B <= 1024, rows 16-byte aligned).
+ * Replaces src/plastax/phases.py:643-705 / :812-840 (bucket_product). */
+PXB_API int pxb_batched_forward(int64_t cap, const int32_t *from_id,
+                        const int32_t *to_id, const uint8_t *dead,
+                        const float *weight, const float *x, int32_t batch,
+                        int32_t num_units, float *out, void *stream);
+/* out[from[s], b] += w[s] * g[to[s], b] (the transpose product). */
+PXB_API int pxb_batched_backward(int64_t cap, const int32_t *from_id,
+                         const int32_t *to_id, const uint8_t *dead,
+                         const float *weight, const float *g, int32_t batch,
+                         int32_t num_units, float *out, void *stream);
+/* Exact batch-mean update (src/plastax/phases.py:434-483):
+ *   stat[s] = (sum_b g[to,b] * a[from,b]) / B, then one optimizer step. */
+PXB_API int pxb_batched_update(int64_t cap, const int32_t *from_id,
+                       const int32_t *to_id, const uint8_t *dead,
+                       float *weight, const float *g, const float *a,
+                       int32_t batch, int32_t num_units,
+                       const pxb_optimizer *opt, float *opt_m, float *opt_v,
+                       float *opt_t, void *stream);
+
+/* ------------------------------------------------------------------ */
+/* growth                                                              */
+/* ------------------------------------------------------------------ */
+
+/* Philox-4x32-10 first word for n (seed, counter) pairs (src/plastax/rng.py:109). */
+PXB_API int pxb_philox32(int64_t n, const uint64_t *seed, const uint64_t *counter,
+                 uint32_t *out, void *stream);
+
+/* The 64-bit seed of one proposal site (src/plastax/rng.py:207-246):
+ * (philox32(network_seed, (step << 8) | stream) << 32) | key. Host-side. */
+PXB_API uint64_t pxb_site_seed(uint64_t network_seed, uint32_t step, uint32_t stream,
+                       uint32_t key);
+
+/* Per-unit proposals (src/plastax/phases.py:3813-3860, rng.py:207-246):
+ * candidate c = i * P + j for unit i < num_units, j < P, drawn from the site
+ * (network_seed, step, stream 1, key i, j):
+ *   src = i; dst = dst_lo + uniform_int(dst_n) [sub 0];
+ *   score per score_kind [sub 1 when it draws];
+ * then the framework validity (src/plastax/phases.py:4041-4108): ids in
+ * range (else clamped to 0 and vetoed), endpoints live (pruned may be NULL),
+ * no self loop unless allow_self_loops, |level gap| <= max_level_gap,
+ * direction (0 any, 1 deeper, 2 same_or_deeper), and the topological
+ * source-level checks: level[src] == bucket_level when bucket_level >= 0,
+ * level[src] < src_level_bound (a bucket exists for it) when the bound is
+ * > 0. Invalid or non-finite -> -inf. */
+PXB_API int pxb_propose_per_unit(int32_t num_units, int32_t proposals,
+                         uint64_t network_seed, int32_t step, int32_t dst_lo,
+                         int32_t dst_n, int32_t score_kind, const float *grad,
+                         const float *act, const int32_t *level,
+                         const uint8_t *pruned, int32_t max_level_gap,
+                         int32_t direction, int32_t allow_self_loops,
+                         int32_t bucket_level, int32_t src_level_bound,
+                         int32_t *src_out, int32_t *dst_out, float *score_out,
+                         void *stream);
+
+/* Scratch bytes for pxb_total_order over n candidates with ids < id_bound. */
+PXB_API int pxb_total_order_scratch_bytes(int64_t n, int32_t id_bound, size_t *bytes);
+
+/* Permutation of the candidates in the total order (-score, src, dst, index)
+ * ascending; NaN sorts as -score = +inf, -0 ties +0. Two stable radix
+ * passes: (src, dst) packed into 2*ceil(log2(id_bound)) bits, then the
+ * score key (src/plastax/phases.py:4208-4321). */
+PXB_API int pxb_total_order(int64_t n, const float *score, const int32_t *src,
+                    const int32_t *dst, int32_t id_bound, int32_t *perm_out,
+                    void *scratch, size_t scratch_bytes, void *stream);
+
+/* Step-scoped selection (level_cap_scope = "step",
+ * src/plastax/phases.py:4891-4903 and level_major :4469-4487): the first
+ * min(k, n) candidates of `perm`, relisted by source level ascending
+ * (stable). Writes win_idx[min(k, n)] and win_count[0]. */
+PXB_API int pxb_select_step_scratch_bytes(int64_t n, int64_t k, size_t *bytes);
+PXB_API int pxb_select_step(int64_t n, const int32_t *perm, const float *score,
+                    const int32_t *src, const int32_t *level, int64_t k,
+                    int32_t *win_idx, int32_t *win_count, void *scratch,
+                    size_t scratch_bytes, void *stream);
+
+/* growth init rules for a committed edge's weight (the rule's `init`) */
+#define PXB_INIT_CONST 0         /* w = a                                      */
+#define PXB_INIT_DYADIC 1        /* w = (((3*src + 5*dst) mod 16) - 8) / 8     */
+#define PXB_INIT_HASH_UNIFORM 2  /* w = a * (2u - 1), u = unit_float(h(src, dst, salt)) */
+
+/* Winners' claim inputs (src/plastax/phases.py:4953-4995): for i < count,
+ * src/dst of candidate win_idx[i], its init weight, and growable =
+ * isfinite(score); entries count..k-1 are not growable. */
+PXB_API int pxb_gather_winners(int64_t k, int64_t count, const int32_t *win_idx,
+                       const int32_t *src, const int32_t *dst,
+                       const float *score, int32_t init_kind, float init_a,
+                       float init_b, uint32_t init_salt, int32_t *src_out,
+                       int32_t *dst_out, float *weight_out,
+                       uint8_t *growable_out, void *stream);
+
+/* ------------------------------------------------------------------ */
+/* slot claim                                                          */
+/* ------------------------------------------------------------------ */
+#define PXB_CLAIM_PIPELINE 0     /* src/plastax/phases.py:2985-3106 */
+#define PXB_CLAIM_TOPOLOGICAL 1  /* src/plastax/phases.py:2853-2982 */
+
+/* Scratch bytes for one claim over `cap` local slots, k candidates and
+ * num_levels (<= 1024) claim domains (1 for the topological claim). */
+PXB_API int pxb_claim_scratch_bytes(int64_t cap, int64_t k, int32_t num_levels,
+                            size_t *bytes);
+
+/* Claim, step 1: count this rank's free slots per domain. PIPELINE: a dead
+ * slot at global position shard_base + s < *tail_start belongs to domain
+ * unit_level[from_id[s]]; TOPOLOGICAL: every dead slot, one domain.
+ * Writes level_counts[num_levels] (device) for the Scheme-A all-gather and
+ * keeps the per-tile counts in `scratch` for step 2. */
+PXB_API int pxb_claim_prepare(int32_t mode, int64_t cap, const int32_t *from_id,
+                      const uint8_t *dead, const int32_t *unit_level,
+                      int32_t num_units, int32_t num_levels,
+                      int64_t shard_base, const int64_t *tail_start,
+                      int64_t k, int32_t *level_counts, void *scratch,
+                      size_t scratch_bytes, void *stream);
+
+/* Claim, step 2: the k candidates in claim order (levels ascending, total
+ * order within a level) with growable[i]; max_new >= 0 caps the growable
+ * ones in claim order (max_new_per_step). Each candidate level's growable
+ * candidates take that domain's free slots in slot order, global rank by
+ * global rank; PIPELINE spills the rest to the tail (global positions
+ * *tail_start + spill rank, levels ascending); past the global capacity a
+ * candidate overflows. Writes from_id/to_id/weight and each extra column
+ * (1- or 4-byte elements, k values each) at the placed slots this rank
+ * owns, clears dead there, advances *tail_start (PIPELINE), and writes
+ * counts_out[4] = {committed, overflowed, tail slots used, committed with
+ * level[dst] <= level[src]} and overflowed_out[k] (either may be NULL).
+ * level_before / level_totals: Scheme-A per-domain counts of the ranks
+ * before this one and of all ranks (device; NULL on one GPU). `scratch`
+ * must hold step 1's results. */
+PXB_API int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id,
+                     int32_t *to_id, uint8_t *dead, float *weight,
+                     const int32_t *unit_level, int32_t num_units,
+                     int32_t num_levels, int64_t shard_base,
+                     int64_t global_cap, int64_t *tail_start, int64_t k,
+                     const int32_t *cand_src, const int32_t *cand_dst,
+                     const float *cand_weight, const uint8_t *growable,
+                     int64_t max_new, const int32_t *level_before,
+                     const int32_t *level_totals, int32_t n_extra,
+                     void *const *extra_cols, const int32_t *extra_bytes,
+                     const void *const *extra_vals, int32_t *counts_out,
+                     uint8_t *overflowed_out, void *scratch,
+                     size_t scratch_bytes, void *stream);
+
+/* Count the dead slots of a bucket into out[0] (device). */
+PXB_API int pxb_count_dead(int64_t cap, const uint8_t *dead, int32_t *out,
+                   void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PXB_H_ */

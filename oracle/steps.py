@@ -1,0 +1,81 @@
+"""Reference-order step restatements built from the oracle primitives.
+
+TEST INFRASTRUCTURE ONLY (the checker and the CPU baseline; the engine never
+imports it). Each step runs the reference's phase order
+(src/plastax/phases.py:87-176) with the oracle's sequential primitives.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from oracle import oracle as orc
+
+
+def lowbias32(x: np.ndarray) -> np.ndarray:
+    """The lowbias32 integer hash (the one the claim-digest tests hash with,
+    tests/test_growth_claim.py:34-41 of the reference)."""
+    x = x.astype(np.uint32)
+    x = x ^ (x >> np.uint32(16))
+    x = (x * np.uint32(0x7FEB352D)).astype(np.uint32)
+    x = x ^ (x >> np.uint32(15))
+    x = (x * np.uint32(0x846CA68B)).astype(np.uint32)
+    return x ^ (x >> np.uint32(16))
+
+
+def init_weight(kind: str, a: float, src: np.ndarray, dst: np.ndarray, salt: int = 0) -> np.ndarray:
+    """Growth init weights of the recognised rules (see plastax_b200.traits)."""
+    if kind == "const":
+        return np.full(src.shape, a, np.float32)
+    if kind == "dyadic":
+        return (((3 * src.astype(np.int64) + 5 * dst) % 16 - 8) / 8.0).astype(np.float32)
+    h = lowbias32(np.uint32(0x9E3779B9) ^ src.astype(np.uint32))
+    h = lowbias32(h ^ dst.astype(np.uint32))
+    h = lowbias32(h ^ np.uint32(salt))
+    u = (h >> np.uint32(8)).astype(np.float32) * np.float32(1.0 / 16777216.0)
+    return (np.float32(a) * (np.float32(2.0) * u - np.float32(1.0))).astype(np.float32)
+
+
+class ReservoirOracle:
+    """The reservoir churn step (PIPELINE: forward, prune, per-unit
+    proposal growth with a step-scoped cap, pipeline claim) on host arrays."""
+
+    def __init__(self, bucket: dict, act: np.ndarray, level: np.ndarray, tail_start: int, *, num_inputs: int,
+                 num_res: int, tau: float, k: int, init_a: float, seed: int = 0, threads: int = 1) -> None:
+        self.b, self.act, self.level = bucket, act, level
+        self.tail = int(tail_start)
+        self.n = act.size
+        self.num_inputs, self.num_res = num_inputs, num_res
+        self.tau, self.k, self.init_a, self.seed = tau, k, init_a, seed
+        self.threads = threads
+        self.is_input = np.zeros(self.n, np.uint8)
+        self.is_input[:num_inputs] = 1
+        self.step_count = 0
+        self.last_counts = np.zeros(4, np.int32)
+
+    def step(self, inputs: np.ndarray) -> None:
+        n, b = self.n, self.b
+        self.act[: self.num_inputs] = inputs
+        acc = np.zeros(n, np.float32)
+        if self.threads > 1:
+            orc.forward_prune_mt(b, self.act, n, self.tau, acc, self.threads)
+        else:
+            orc.forward_accumulate(b, self.act, n, "sum", acc)
+        orc.unit_apply(n, 0, "tanh", "sum", acc, None, None, None, 0, self.is_input, None, self.act)
+        if self.threads <= 1:
+            orc.prune(b, n, 1, self.tau)
+        src, dst, score = orc.propose_per_unit(n, 1, self.seed, self.step_count, self.num_inputs, self.num_res, 0,
+                                               self.level, max_level_gap=1)
+        perm = orc.total_order(score, src, dst)
+        win = orc.select_step(perm, src, self.level, self.k)
+        cs, cd = src[win].copy(), dst[win].copy()
+        cw = init_weight("hash_uniform", self.init_a, cs, cd)
+        grow = np.isfinite(score[win]).astype(np.uint8)
+        if win.size < self.k:  # padding entries are not growable
+            pad = self.k - win.size
+            cs = np.concatenate([cs, np.zeros(pad, np.int32)])
+            cd = np.concatenate([cd, np.zeros(pad, np.int32)])
+            cw = np.concatenate([cw, np.zeros(pad, np.float32)])
+            grow = np.concatenate([grow, np.zeros(pad, np.uint8)])
+        self.last_counts, _, self.tail = orc.claim_pipeline(b, self.level, self.tail, cs, cd, cw, grow)
+        self.step_count += 1

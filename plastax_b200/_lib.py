@@ -1,0 +1,153 @@
+"""ctypes binding of libpxb.so (the C ABI declared in include/pxb.h).
+
+Every entry point is wrapped so a non-zero status raises `PxbError` with the
+library's own message. Loading fails loudly: there is no CPU fallback behind
+these calls, so a missing or unbuildable library is an error, never a silent
+switch to another implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import functools
+import pathlib
+from collections.abc import Callable
+from typing import Any
+
+_PKG = pathlib.Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libpxb.so"
+
+c_i32 = ctypes.c_int32
+c_i64 = ctypes.c_int64
+c_u32 = ctypes.c_uint32
+c_u64 = ctypes.c_uint64
+c_f32 = ctypes.c_float
+c_size = ctypes.c_size_t
+c_ptr = ctypes.c_void_p
+
+# constants of include/pxb.h
+MONOID = {"sum": 0, "max": 1, "min": 2}
+ACT = {"identity": 0, "tanh": 1, "relu": 2, "sigmoid": 3}
+PRUNE_NONE, PRUNE_ABS_BELOW, PRUNE_ABS_BELOW_DST = 0, 1, 2
+OPT = {"sgd": 0, "momentum": 1, "adam": 2, "rmsprop": 3}
+SCORE_UNIFORM, SCORE_UNIFORM_Q256, SCORE_GRAD_ACT = 0, 1, 2
+INIT_CONST, INIT_DYADIC, INIT_HASH_UNIFORM = 0, 1, 2
+CLAIM_PIPELINE, CLAIM_TOPOLOGICAL = 0, 1
+
+
+class PxbError(RuntimeError):
+    """A libpxb entry point returned a non-zero status."""
+
+
+class Optimizer(ctypes.Structure):
+    """`pxb_optimizer`: the optimizer bundle's kind and hyper-parameters."""
+
+    _fields_ = [
+        ("kind", c_i32),
+        ("lr", c_f32),
+        ("b1", c_f32),
+        ("b2", c_f32),
+        ("eps", c_f32),
+        ("weight_decay", c_f32),
+    ]
+
+
+# name -> (restype, argtypes); every int-returning entry point is checked.
+_SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
+    "pxb_abi_version": (c_i32, []),
+    "pxb_last_error": (ctypes.c_char_p, []),
+    "pxb_sm_count": (c_i32, [c_ptr]),
+    "pxb_fill_f32": (c_i32, [c_i64, c_f32, c_ptr, c_ptr]),
+    "pxb_forward_accumulate": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_ptr, c_ptr]),
+    "pxb_forward_prune": (
+        c_i32,
+        [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_ptr, c_i32, c_f32, c_ptr, c_ptr, c_i32, c_ptr,
+         c_ptr],
+    ),
+    "pxb_prune_conn": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_f32, c_ptr, c_ptr, c_i32, c_ptr, c_ptr]),
+    "pxb_backward_accumulate": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_ptr, c_ptr]),
+    "pxb_backward_update": (
+        c_i32,
+        [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, ctypes.POINTER(Optimizer), c_ptr, c_ptr,
+         c_ptr, c_ptr],
+    ),
+    "pxb_unit_apply": (
+        c_i32,
+        [c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr],
+    ),
+    "pxb_mse_loss": (c_i32, [c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
+    "pxb_batched_forward": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_ptr, c_ptr]),
+    "pxb_batched_backward": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_ptr, c_ptr]),
+    "pxb_batched_update": (
+        c_i32,
+        [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, ctypes.POINTER(Optimizer), c_ptr, c_ptr,
+         c_ptr, c_ptr],
+    ),
+    "pxb_philox32": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_ptr]),
+    "pxb_site_seed": (c_u64, [c_u64, c_u32, c_u32, c_u32]),
+    "pxb_propose_per_unit": (
+        c_i32,
+        [c_i32, c_i32, c_u64, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32,
+         c_i32, c_ptr, c_ptr, c_ptr, c_ptr],
+    ),
+    "pxb_total_order_scratch_bytes": (c_i32, [c_i64, c_i32, ctypes.POINTER(c_size)]),
+    "pxb_total_order": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_size, c_ptr]),
+    "pxb_select_step_scratch_bytes": (c_i32, [c_i64, c_i64, ctypes.POINTER(c_size)]),
+    "pxb_select_step": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_size, c_ptr]),
+    "pxb_gather_winners": (
+        c_i32,
+        [c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_f32, c_f32, c_u32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr],
+    ),
+    "pxb_claim_scratch_bytes": (c_i32, [c_i64, c_i64, c_i32, ctypes.POINTER(c_size)]),
+    "pxb_claim_prepare": (
+        c_i32,
+        [c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i64, c_ptr, c_i64, c_ptr, c_ptr, c_size, c_ptr],
+    ),
+    "pxb_claim_commit": (
+        c_i32,
+        [c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i64, c_i64, c_ptr, c_i64, c_ptr, c_ptr,
+         c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_size, c_ptr],
+    ),
+    "pxb_count_dead": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr]),
+}
+
+
+@functools.cache
+def lib() -> ctypes.CDLL:
+    """Load libpxb.so (once) and declare every entry point's signature."""
+    if not LIB_PATH.exists():
+        raise PxbError(
+            f"{LIB_PATH} is missing: build it with `python -m plastax_b200.build` "
+            "(the engine has no CPU fallback)"
+        )
+    handle = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in _SIGNATURES.items():
+        fn = getattr(handle, name)
+        fn.restype = res
+        fn.argtypes = args
+    return handle
+
+
+def exported_names() -> list[str]:
+    """Every entry point this binding declares (the header's function set)."""
+    return list(_SIGNATURES)
+
+
+def last_error() -> str:
+    raw = lib().pxb_last_error()
+    return raw.decode() if raw else ""
+
+
+def call(name: str, *args: Any) -> None:
+    """Call a status-returning entry point; raise PxbError on failure."""
+    fn: Callable[..., int] = getattr(lib(), name)
+    rc = fn(*args)
+    if rc != 0:
+        raise PxbError(f"{name} failed (status {rc}): {last_error()}")
+
+
+def query_size(name: str, *args: Any) -> int:
+    """Call a `*_scratch_bytes` entry point and return the byte count."""
+    out = c_size(0)
+    call(name, *args, ctypes.byref(out))
+    return int(out.value)

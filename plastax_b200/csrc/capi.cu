@@ -1,0 +1,62 @@
+// Library-level entry points: ABI version, error text, device facts, fills.
+#include <mutex>
+#include <vector>
+
+#include "pxb_common.cuh"
+
+namespace pxb {
+
+static thread_local std::string g_last_error;
+
+void set_error(const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+}
+
+const char *last_error() { return g_last_error.c_str(); }
+
+int sm_count() {
+  static std::mutex mu;
+  static std::vector<int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= static_cast<int>(cache.size())) cache.resize(dev + 1, 0);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+__global__ void fill_f32_kernel(int64_t n, float v, float *__restrict__ out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = v;
+}
+
+}  // namespace pxb
+
+extern "C" int pxb_abi_version(void) { return PXB_ABI_VERSION; }
+
+extern "C" const char *pxb_last_error(void) { return pxb::last_error(); }
+
+extern "C" int pxb_sm_count(int32_t *out) {
+  PXB_REQUIRE(out != nullptr, "pxb_sm_count: out is NULL");
+  *out = pxb::sm_count();
+  return PXB_OK;
+}
+
+extern "C" int pxb_fill_f32(int64_t n, float value, float *out, void *stream) {
+  PXB_REQUIRE(n >= 0, "pxb_fill_f32: negative n");
+  if (n == 0) return PXB_OK;
+  PXB_REQUIRE(out != nullptr, "pxb_fill_f32: out is NULL");
+  pxb::fill_f32_kernel<<<pxb::grid_for(n, 1024, 4), 256, 0, pxb::as_stream(stream)>>>(n, value, out);
+  PXB_LAUNCHED("fill_f32_kernel");
+  return PXB_OK;
+}

@@ -1,0 +1,406 @@
+// Growth candidates and their selection: Philox per-unit proposals with the
+// framework validity window, the total candidate order as two stable radix
+// passes (CUB, header-only), the step-scoped top-k relisted levels ascending,
+// and the winners' gather with the growth rule's init values.
+#include <cub/cub.cuh>
+
+#include "pxb_common.cuh"
+
+namespace pxb {
+
+static inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+static inline int bits_for(int64_t bound) {
+  int b = 1;
+  while (b < 62 && (int64_t(1) << b) < bound) ++b;
+  return b;
+}
+
+// ---------------------------------------------------------------------------
+// raw Philox words
+// ---------------------------------------------------------------------------
+__global__ void philox_kernel(int64_t n, const uint64_t *__restrict__ seed, const uint64_t *__restrict__ ctr,
+                              uint32_t *__restrict__ out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = philox32(seed[i], ctr[i]);
+}
+
+// ---------------------------------------------------------------------------
+// per-unit proposals + validity (src/plastax/phases.py:3813-3860,
+// :4041-4108; rng.py:207-246)
+// ---------------------------------------------------------------------------
+struct ProposeArgs {
+  int32_t num_units, proposals;
+  uint64_t keyed_hi;  // philox32(network_seed, (step << 8) | 1): the site seed's high limb
+  int32_t dst_lo, dst_n, score_kind;
+  const float *grad, *act;
+  const int32_t *level;
+  const uint8_t *pruned;
+  int32_t max_level_gap, direction, allow_self_loops, bucket_level, src_level_bound;
+};
+
+__global__ void propose_per_unit_kernel(ProposeArgs a, int32_t *__restrict__ src_out,
+                                        int32_t *__restrict__ dst_out, float *__restrict__ score_out) {
+  const int64_t total = static_cast<int64_t>(a.num_units) * a.proposals;
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < total;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t i = static_cast<int32_t>(c / a.proposals);
+    const uint32_t j = static_cast<uint32_t>(c - static_cast<int64_t>(i) * a.proposals);
+    const uint64_t seed = (a.keyed_hi << 32) | static_cast<uint32_t>(i);
+    int32_t src = i;
+    int32_t dst = a.dst_lo + static_cast<int32_t>(uniform_int(unit_float(site_draw(seed, j, 0)), a.dst_n));
+    float score;
+    if (a.score_kind == PXB_SCORE_UNIFORM) {
+      score = unit_float(site_draw(seed, j, 1));
+    } else if (a.score_kind == PXB_SCORE_UNIFORM_Q256) {
+      const float u = unit_float(site_draw(seed, j, 1));
+      score = static_cast<float>(static_cast<int32_t>(__fmul_rn(u, 256.0f))) * (1.0f / 256.0f);
+    } else {
+      score = (dst >= 0 && dst < a.num_units) ? fabsf(__fmul_rn(a.grad[dst], a.act[src])) : 0.0f;
+    }
+    // _clamp_proposals: out-of-range ids are vetoed and clamped to 0.
+    bool valid = dst >= 0 && dst < a.num_units;
+    if (!valid) {
+      src = 0;
+      dst = 0;
+    }
+    if (valid && a.pruned != nullptr) valid = !a.pruned[src] && !a.pruned[dst];
+    if (valid) {
+      const int32_t ls = a.level[src], ld = a.level[dst];
+      const int32_t gap = ld > ls ? ld - ls : ls - ld;
+      valid = gap <= a.max_level_gap;
+      if (!a.allow_self_loops) valid = valid && src != dst;
+      if (a.direction == 1) valid = valid && ld > ls;
+      else if (a.direction == 2) valid = valid && ld >= ls;
+      if (a.bucket_level >= 0) valid = valid && ls == a.bucket_level;
+      if (a.src_level_bound > 0) valid = valid && ls < a.src_level_bound;
+    }
+    if (!valid || !isfinite(score)) score = -__int_as_float(0x7f800000);
+    src_out[c] = src;
+    dst_out[c] = dst;
+    score_out[c] = score;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// total order (src/plastax/phases.py:4208-4321)
+// ---------------------------------------------------------------------------
+// Order-preserving uint32 image of the leading key: -score, NaN -> +inf,
+// -0 -> +0.
+__device__ __forceinline__ uint32_t score_key(float s) {
+  float neg = isnan(s) ? __int_as_float(0x7f800000) : -s;
+  if (neg == 0.0f) neg = 0.0f;
+  const uint32_t u = __float_as_uint(neg);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void pair_key_kernel(int64_t n, const int32_t *__restrict__ src, const int32_t *__restrict__ dst,
+                                int bits, uint64_t *__restrict__ keys, int32_t *__restrict__ vals) {
+  const uint64_t mask = (uint64_t(1) << bits) - 1;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    keys[i] = ((static_cast<uint64_t>(static_cast<uint32_t>(src[i])) & mask) << bits) |
+              (static_cast<uint64_t>(static_cast<uint32_t>(dst[i])) & mask);
+    vals[i] = static_cast<int32_t>(i);
+  }
+}
+
+__global__ void score_key_kernel(int64_t n, const float *__restrict__ score, const int32_t *__restrict__ perm,
+                                 uint32_t *__restrict__ keys) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    keys[i] = score_key(score[perm[i]]);
+}
+
+struct OrderScratch {
+  uint64_t *pair_in, *pair_out;
+  uint32_t *skey_in, *skey_out;
+  int32_t *val_a, *val_b;
+  void *cub_tmp;
+  size_t cub_bytes;
+  size_t total;
+};
+
+static int order_scratch(int64_t n, int bits, char *base, OrderScratch *o) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = off;
+    off = align_up(off + bytes, 256);
+    return base ? base + at : nullptr;
+  };
+  o->pair_in = reinterpret_cast<uint64_t *>(take(n * sizeof(uint64_t)));
+  o->pair_out = reinterpret_cast<uint64_t *>(take(n * sizeof(uint64_t)));
+  o->skey_in = reinterpret_cast<uint32_t *>(take(n * sizeof(uint32_t)));
+  o->skey_out = reinterpret_cast<uint32_t *>(take(n * sizeof(uint32_t)));
+  o->val_a = reinterpret_cast<int32_t *>(take(n * sizeof(int32_t)));
+  o->val_b = reinterpret_cast<int32_t *>(take(n * sizeof(int32_t)));
+  size_t t1 = 0, t2 = 0;
+  if (cub::DeviceRadixSort::SortPairs(nullptr, t1, o->pair_in, o->pair_out, o->val_a, o->val_b,
+                                      static_cast<int>(n), 0, 2 * bits) != cudaSuccess)
+    return PXB_ECUDA;
+  if (cub::DeviceRadixSort::SortPairs(nullptr, t2, o->skey_in, o->skey_out, o->val_b, o->val_a,
+                                      static_cast<int>(n), 0, 32) != cudaSuccess)
+    return PXB_ECUDA;
+  o->cub_bytes = t1 > t2 ? t1 : t2;
+  o->cub_tmp = take(o->cub_bytes);
+  o->total = off;
+  return PXB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// step-scoped selection (src/plastax/phases.py:4891-4903, level_major
+// :4469-4487): the first k of the total order, relisted levels ascending.
+// ---------------------------------------------------------------------------
+__global__ void winner_level_kernel(int64_t kk, const int32_t *__restrict__ perm, const int32_t *__restrict__ src,
+                                    const int32_t *__restrict__ level, uint32_t *__restrict__ keys,
+                                    int32_t *__restrict__ vals) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < kk;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t c = perm[i];
+    keys[i] = static_cast<uint32_t>(level[src[c]]);
+    vals[i] = c;
+  }
+}
+
+__global__ void set_i32_kernel(int32_t *p, int32_t v) { *p = v; }
+
+struct SelectScratch {
+  uint32_t *key_in, *key_out;
+  int32_t *val_in;
+  void *cub_tmp;
+  size_t cub_bytes, total;
+};
+
+static int select_scratch(int64_t kk, char *base, SelectScratch *o, int32_t *val_out_probe) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = off;
+    off = align_up(off + bytes, 256);
+    return base ? base + at : nullptr;
+  };
+  o->key_in = reinterpret_cast<uint32_t *>(take(kk * sizeof(uint32_t)));
+  o->key_out = reinterpret_cast<uint32_t *>(take(kk * sizeof(uint32_t)));
+  o->val_in = reinterpret_cast<int32_t *>(take(kk * sizeof(int32_t)));
+  size_t t = 0;
+  if (cub::DeviceRadixSort::SortPairs(nullptr, t, o->key_in, o->key_out, o->val_in, val_out_probe,
+                                      static_cast<int>(kk), 0, 32) != cudaSuccess)
+    return PXB_ECUDA;
+  o->cub_bytes = t;
+  o->cub_tmp = take(t);
+  o->total = off;
+  return PXB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// winners' gather: (src, dst, init weight, growable) per selected candidate
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t lowbias32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7FEB352Du;
+  x ^= x >> 15;
+  x *= 0x846CA68Bu;
+  return x ^ (x >> 16);
+}
+
+struct InitArgs {
+  int32_t kind;  // PXB_INIT_*
+  float a, b;
+  uint32_t salt;
+};
+
+__device__ __forceinline__ float init_weight(const InitArgs &ia, int32_t src, int32_t dst) {
+  switch (ia.kind) {
+    case PXB_INIT_CONST: return ia.a;
+    case PXB_INIT_DYADIC: {
+      const int32_t r = ((3 * src + 5 * dst) % 16) - 8;
+      return static_cast<float>(r) / 8.0f;
+    }
+    case PXB_INIT_HASH_UNIFORM: {
+      uint32_t h = lowbias32(0x9E3779B9u ^ static_cast<uint32_t>(src));
+      h = lowbias32(h ^ static_cast<uint32_t>(dst));
+      h = lowbias32(h ^ ia.salt);
+      const float u = unit_float(h);
+      return __fmul_rn(ia.a, __fsub_rn(__fmul_rn(2.0f, u), 1.0f));
+    }
+    default: return 0.0f;
+  }
+}
+
+__global__ void gather_winners_kernel(int64_t k, int64_t count, const int32_t *__restrict__ win,
+                                      const int32_t *__restrict__ src, const int32_t *__restrict__ dst,
+                                      const float *__restrict__ score, InitArgs ia, int32_t *__restrict__ s_out,
+                                      int32_t *__restrict__ d_out, float *__restrict__ w_out,
+                                      uint8_t *__restrict__ growable) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < k;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (i < count) {
+      const int32_t c = win[i];
+      const int32_t s = src[c], d = dst[c];
+      s_out[i] = s;
+      d_out[i] = d;
+      w_out[i] = init_weight(ia, s, d);
+      growable[i] = isfinite(score[c]) ? 1 : 0;
+    } else {
+      s_out[i] = 0;
+      d_out[i] = 0;
+      w_out[i] = 0.0f;
+      growable[i] = 0;
+    }
+  }
+}
+
+}  // namespace pxb
+
+using namespace pxb;
+
+extern "C" int pxb_philox32(int64_t n, const uint64_t *seed, const uint64_t *counter, uint32_t *out,
+                            void *stream) {
+  PXB_REQUIRE(n >= 0, "pxb_philox32: negative n");
+  if (n == 0) return PXB_OK;
+  PXB_REQUIRE(seed && counter && out, "pxb_philox32: a pointer is NULL");
+  philox_kernel<<<grid_for(n, 256, 8), 256, 0, as_stream(stream)>>>(n, seed, counter, out);
+  PXB_LAUNCHED("philox_kernel");
+  return PXB_OK;
+}
+
+extern "C" uint64_t pxb_site_seed(uint64_t network_seed, uint32_t step, uint32_t stream_id, uint32_t key) {
+  return site_seed(network_seed, step, stream_id, key);
+}
+
+extern "C" int pxb_propose_per_unit(int32_t num_units, int32_t proposals, uint64_t network_seed, int32_t step,
+                                    int32_t dst_lo, int32_t dst_n, int32_t score_kind, const float *grad,
+                                    const float *act, const int32_t *level, const uint8_t *pruned,
+                                    int32_t max_level_gap, int32_t direction, int32_t allow_self_loops,
+                                    int32_t bucket_level, int32_t src_level_bound, int32_t *src_out,
+                                    int32_t *dst_out, float *score_out, void *stream) {
+  PXB_REQUIRE(num_units >= 0 && proposals >= 0, "pxb_propose_per_unit: negative sizes");
+  PXB_REQUIRE(dst_n >= 1, "pxb_propose_per_unit: dst_n must be >= 1");
+  PXB_REQUIRE(score_kind >= 0 && score_kind <= 2, "pxb_propose_per_unit: unknown score kind %d", score_kind);
+  PXB_REQUIRE(direction >= 0 && direction <= 2, "pxb_propose_per_unit: unknown direction %d", direction);
+  PXB_REQUIRE(score_kind != PXB_SCORE_GRAD_ACT || (grad && act), "pxb_propose_per_unit: grad/act is NULL");
+  const int64_t total = static_cast<int64_t>(num_units) * proposals;
+  if (total == 0) return PXB_OK;
+  PXB_REQUIRE(total < (int64_t(1) << 31), "pxb_propose_per_unit: more than 2^31 candidates");
+  PXB_REQUIRE(level && src_out && dst_out && score_out, "pxb_propose_per_unit: a pointer is NULL");
+  ProposeArgs a;
+  a.num_units = num_units;
+  a.proposals = proposals;
+  a.keyed_hi = philox32(network_seed, (static_cast<uint64_t>(static_cast<uint32_t>(step)) << 8) | 1u);
+  a.dst_lo = dst_lo;
+  a.dst_n = dst_n;
+  a.score_kind = score_kind;
+  a.grad = grad;
+  a.act = act;
+  a.level = level;
+  a.pruned = pruned;
+  a.max_level_gap = max_level_gap;
+  a.direction = direction;
+  a.allow_self_loops = allow_self_loops;
+  a.bucket_level = bucket_level;
+  a.src_level_bound = src_level_bound;
+  propose_per_unit_kernel<<<grid_for(total, 256, 8), 256, 0, as_stream(stream)>>>(a, src_out, dst_out,
+                                                                                  score_out);
+  PXB_LAUNCHED("propose_per_unit_kernel");
+  return PXB_OK;
+}
+
+extern "C" int pxb_total_order_scratch_bytes(int64_t n, int32_t id_bound, size_t *bytes) {
+  PXB_REQUIRE(bytes != nullptr, "pxb_total_order_scratch_bytes: bytes is NULL");
+  PXB_REQUIRE(n >= 0 && n < (int64_t(1) << 31), "pxb_total_order_scratch_bytes: n out of range");
+  PXB_REQUIRE(id_bound >= 1, "pxb_total_order_scratch_bytes: id_bound must be >= 1");
+  OrderScratch o;
+  if (order_scratch(n, bits_for(id_bound), nullptr, &o) != PXB_OK) {
+    set_error("pxb_total_order_scratch_bytes: CUB size query failed");
+    return PXB_ECUDA;
+  }
+  *bytes = o.total;
+  return PXB_OK;
+}
+
+extern "C" int pxb_total_order(int64_t n, const float *score, const int32_t *src, const int32_t *dst,
+                               int32_t id_bound, int32_t *perm_out, void *scratch, size_t scratch_bytes,
+                               void *stream) {
+  PXB_REQUIRE(n >= 0 && n < (int64_t(1) << 31), "pxb_total_order: n out of range");
+  PXB_REQUIRE(id_bound >= 1, "pxb_total_order: id_bound must be >= 1");
+  if (n == 0) return PXB_OK;
+  PXB_REQUIRE(score && src && dst && perm_out && scratch, "pxb_total_order: a pointer is NULL");
+  const int bits = bits_for(id_bound);
+  OrderScratch o;
+  if (order_scratch(n, bits, static_cast<char *>(scratch), &o) != PXB_OK) {
+    set_error("pxb_total_order: CUB size query failed");
+    return PXB_ECUDA;
+  }
+  PXB_REQUIRE(o.total <= scratch_bytes, "pxb_total_order: scratch has %zu bytes, needs %zu", scratch_bytes,
+              o.total);
+  cudaStream_t st = as_stream(stream);
+  const int grid = grid_for(n, 256, 8);
+  pair_key_kernel<<<grid, 256, 0, st>>>(n, src, dst, bits, o.pair_in, o.val_a);
+  PXB_LAUNCHED("pair_key_kernel");
+  size_t tb = o.cub_bytes;
+  PXB_CUDA(cub::DeviceRadixSort::SortPairs(o.cub_tmp, tb, o.pair_in, o.pair_out, o.val_a, o.val_b,
+                                           static_cast<int>(n), 0, 2 * bits, st));
+  score_key_kernel<<<grid, 256, 0, st>>>(n, score, o.val_b, o.skey_in);
+  PXB_LAUNCHED("score_key_kernel");
+  tb = o.cub_bytes;
+  PXB_CUDA(cub::DeviceRadixSort::SortPairs(o.cub_tmp, tb, o.skey_in, o.skey_out, o.val_b, perm_out,
+                                           static_cast<int>(n), 0, 32, st));
+  return PXB_OK;
+}
+
+extern "C" int pxb_select_step_scratch_bytes(int64_t n, int64_t k, size_t *bytes) {
+  PXB_REQUIRE(bytes != nullptr, "pxb_select_step_scratch_bytes: bytes is NULL");
+  PXB_REQUIRE(n >= 0 && k >= 0, "pxb_select_step_scratch_bytes: negative sizes");
+  const int64_t kk = k < n ? k : n;
+  SelectScratch o;
+  if (select_scratch(kk, nullptr, &o, nullptr) != PXB_OK) {
+    set_error("pxb_select_step_scratch_bytes: CUB size query failed");
+    return PXB_ECUDA;
+  }
+  *bytes = o.total;
+  return PXB_OK;
+}
+
+extern "C" int pxb_select_step(int64_t n, const int32_t *perm, const float *score, const int32_t *src,
+                               const int32_t *level, int64_t k, int32_t *win_idx, int32_t *win_count,
+                               void *scratch, size_t scratch_bytes, void *stream) {
+  (void)score;
+  PXB_REQUIRE(n >= 0 && k >= 0 && n < (int64_t(1) << 31), "pxb_select_step: sizes out of range");
+  const int64_t kk = k < n ? k : n;
+  cudaStream_t st = as_stream(stream);
+  if (win_count != nullptr) {
+    set_i32_kernel<<<1, 1, 0, st>>>(win_count, static_cast<int32_t>(kk));
+    PXB_LAUNCHED("set_i32_kernel");
+  }
+  if (kk == 0) return PXB_OK;
+  PXB_REQUIRE(perm && src && level && win_idx && scratch, "pxb_select_step: a pointer is NULL");
+  SelectScratch o;
+  if (select_scratch(kk, static_cast<char *>(scratch), &o, win_idx) != PXB_OK) {
+    set_error("pxb_select_step: CUB size query failed");
+    return PXB_ECUDA;
+  }
+  PXB_REQUIRE(o.total <= scratch_bytes, "pxb_select_step: scratch has %zu bytes, needs %zu", scratch_bytes,
+              o.total);
+  winner_level_kernel<<<grid_for(kk, 256, 8), 256, 0, st>>>(kk, perm, src, level, o.key_in, o.val_in);
+  PXB_LAUNCHED("winner_level_kernel");
+  size_t tb = o.cub_bytes;
+  PXB_CUDA(cub::DeviceRadixSort::SortPairs(o.cub_tmp, tb, o.key_in, o.key_out, o.val_in, win_idx,
+                                           static_cast<int>(kk), 0, 32, st));
+  return PXB_OK;
+}
+
+extern "C" int pxb_gather_winners(int64_t k, int64_t count, const int32_t *win_idx, const int32_t *src,
+                                  const int32_t *dst, const float *score, int32_t init_kind, float init_a,
+                                  float init_b, uint32_t init_salt, int32_t *src_out, int32_t *dst_out,
+                                  float *weight_out, uint8_t *growable_out, void *stream) {
+  PXB_REQUIRE(k >= 0 && count >= 0 && count <= k, "pxb_gather_winners: sizes out of range");
+  PXB_REQUIRE(init_kind >= 0 && init_kind <= 2, "pxb_gather_winners: unknown init kind %d", init_kind);
+  if (k == 0) return PXB_OK;
+  PXB_REQUIRE(src_out && dst_out && weight_out && growable_out, "pxb_gather_winners: an output is NULL");
+  PXB_REQUIRE(count == 0 || (win_idx && src && dst && score), "pxb_gather_winners: an input is NULL");
+  InitArgs ia{init_kind, init_a, init_b, init_salt};
+  gather_winners_kernel<<<grid_for(k, 256, 8), 256, 0, as_stream(stream)>>>(
+      k, count, win_idx, src, dst, score, ia, src_out, dst_out, weight_out, growable_out);
+  PXB_LAUNCHED("gather_winners_kernel");
+  return PXB_OK;
+}

@@ -1,0 +1,319 @@
+"""Typed torch-tensor front end of the C ABI (include/pxb.h).
+
+Device memory and streams come from PyTorch (plumbing only); every call goes
+straight to a libpxb.so entry point on the current CUDA stream. Arguments
+are checked here (device, dtype, contiguity, length) before the C ABI checks
+them again, so misuse raises a Python exception and never reaches a kernel.
+
+A bucket is a dict of device columns named like the reference's SOA tags:
+``from_id`` int32, ``to_id`` int32, ``dead`` uint8 (the reference's bool),
+``weight`` float32 and any ``opt/...`` float32 optimizer column.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from collections.abc import Mapping
+
+import torch
+
+from plastax_b200 import _lib
+from plastax_b200._lib import call, query_size
+
+Bucket = Mapping[str, torch.Tensor]
+
+_DTYPES = {
+    "from_id": torch.int32,
+    "to_id": torch.int32,
+    "dead": torch.uint8,
+    "weight": torch.float32,
+}
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def ptr(t: torch.Tensor | None) -> ctypes.c_void_p | None:
+    """Device pointer of a contiguous CUDA tensor (None passes NULL)."""
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("engine tensors must live on a CUDA device")
+    if not t.is_contiguous():
+        raise ValueError("engine tensors must be contiguous")
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _check(t: torch.Tensor, dtype: torch.dtype, n: int | None, what: str) -> None:
+    if t.dtype != dtype:
+        raise TypeError(f"{what}: expected {dtype}, got {t.dtype}")
+    if n is not None and t.numel() != n:
+        raise ValueError(f"{what}: expected {n} elements, got {t.numel()}")
+
+
+def _bucket(b: Bucket) -> int:
+    cap = b["dead"].numel()
+    for name, dt in _DTYPES.items():
+        _check(b[name], dt, cap, f"bucket column {name!r}")
+    return cap
+
+
+def fill(t: torch.Tensor, value: float) -> None:
+    _check(t, torch.float32, None, "fill target")
+    call("pxb_fill_f32", ctypes.c_int64(t.numel()), ctypes.c_float(value), ptr(t), _stream())
+
+
+def sm_count() -> int:
+    out = ctypes.c_int32(0)
+    call("pxb_sm_count", ctypes.byref(out))
+    return out.value
+
+
+# ---------------------------------------------------------------------------
+# propagation
+# ---------------------------------------------------------------------------
+def forward_accumulate(b: Bucket, act: torch.Tensor, acc: torch.Tensor, monoid: str = "sum") -> None:
+    cap = _bucket(b)
+    n = acc.numel()
+    _check(act, torch.float32, n, "act")
+    _check(acc, torch.float32, n, "acc")
+    call("pxb_forward_accumulate", ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]), ptr(b["dead"]),
+         ptr(b["weight"]), ptr(act), ctypes.c_int32(n), _lib.MONOID[monoid], ptr(acc), _stream())
+
+
+def forward_prune(b: Bucket, act: torch.Tensor, acc: torch.Tensor, *, monoid: str = "sum",
+                  prune_kind: int = _lib.PRUNE_ABS_BELOW, threshold: float = 0.0,
+                  unit_threshold: torch.Tensor | None = None, dead_out: torch.Tensor | None = None,
+                  block_len: int = 0, block_free: torch.Tensor | None = None) -> None:
+    """Forward accumulate + prune predicate + per-block free counts, one pass."""
+    cap = _bucket(b)
+    n = acc.numel()
+    _check(act, torch.float32, n, "act")
+    _check(acc, torch.float32, n, "acc")
+    out = b["dead"] if dead_out is None else dead_out
+    _check(out, torch.uint8, cap, "dead_out")
+    if block_free is not None:
+        _check(block_free, torch.int32, (cap + block_len - 1) // block_len, "block_free")
+    call("pxb_forward_prune", ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]), ptr(b["dead"]),
+         ptr(b["weight"]), ptr(act), ctypes.c_int32(n), _lib.MONOID[monoid], ptr(acc), ctypes.c_int32(prune_kind),
+         ctypes.c_float(threshold), ptr(unit_threshold), ptr(out), ctypes.c_int32(block_len), ptr(block_free),
+         _stream())
+
+
+def prune_conn(b: Bucket, num_units: int, *, prune_kind: int = _lib.PRUNE_ABS_BELOW, threshold: float = 0.0,
+               unit_threshold: torch.Tensor | None = None, block_len: int = 0,
+               block_free: torch.Tensor | None = None) -> None:
+    cap = _bucket(b)
+    call("pxb_prune_conn", ctypes.c_int64(cap), ptr(b["to_id"]), ptr(b["dead"]), ptr(b["weight"]),
+         ctypes.c_int32(num_units), ctypes.c_int32(prune_kind), ctypes.c_float(threshold), ptr(unit_threshold),
+         ptr(b["dead"]), ctypes.c_int32(block_len), ptr(block_free), _stream())
+
+
+def backward_accumulate(b: Bucket, grad: torch.Tensor, acc: torch.Tensor, monoid: str = "sum") -> None:
+    cap = _bucket(b)
+    n = acc.numel()
+    _check(grad, torch.float32, n, "grad")
+    _check(acc, torch.float32, n, "acc")
+    call("pxb_backward_accumulate", ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]), ptr(b["dead"]),
+         ptr(b["weight"]), ptr(grad), ctypes.c_int32(n), _lib.MONOID[monoid], ptr(acc), _stream())
+
+
+def optimizer_struct(kind: str, lr: float, b1: float = 0.0, b2: float = 0.0, eps: float = 0.0,
+                     weight_decay: float = 0.0) -> _lib.Optimizer:
+    return _lib.Optimizer(_lib.OPT[kind], lr, b1, b2, eps, weight_decay)
+
+
+def backward_update(b: Bucket, grad: torch.Tensor, act: torch.Tensor, acc: torch.Tensor | None,
+                    opt: _lib.Optimizer) -> None:
+    """Backward accumulate (acc may be None) fused with the optimizer update."""
+    cap = _bucket(b)
+    n = grad.numel()
+    _check(act, torch.float32, n, "act")
+    if acc is not None:
+        _check(acc, torch.float32, n, "acc")
+    call("pxb_backward_update", ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]), ptr(b["dead"]),
+         ptr(b["weight"]), ptr(grad), ptr(act), ctypes.c_int32(n), ptr(acc), ctypes.byref(opt),
+         ptr(b.get("opt/m")), ptr(b.get("opt/v")), ptr(b.get("opt/t")), _stream())
+
+
+def unit_apply(acc: torch.Tensor, out: torch.Tensor, *, mode: int, act_kind: str, monoid: str = "sum",
+               act: torch.Tensor | None = None, seed: torch.Tensor | None = None,
+               level: torch.Tensor | None = None, target_level: int = 0, is_input: torch.Tensor | None = None,
+               pruned: torch.Tensor | None = None) -> None:
+    n = acc.numel()
+    call("pxb_unit_apply", ctypes.c_int32(n), ctypes.c_int32(mode), ctypes.c_int32(_lib.ACT[act_kind]),
+         ctypes.c_int32(_lib.MONOID[monoid]), ptr(acc), ptr(act), ptr(seed), ptr(level),
+         ctypes.c_int32(target_level), ptr(is_input), ptr(pruned), ptr(out), _stream())
+
+
+def mse_loss(output_ids: torch.Tensor, act: torch.Tensor, target: torch.Tensor, seed: torch.Tensor,
+             loss_out: torch.Tensor | None) -> None:
+    call("pxb_mse_loss", ctypes.c_int32(output_ids.numel()), ptr(output_ids), ptr(act), ptr(target), ptr(seed),
+         ptr(loss_out), _stream())
+
+
+# ---------------------------------------------------------------------------
+# batched products ([num_units, B] unit rows)
+# ---------------------------------------------------------------------------
+def batched_forward(b: Bucket, x: torch.Tensor, out: torch.Tensor) -> None:
+    cap = _bucket(b)
+    n, batch = x.shape
+    call("pxb_batched_forward", ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]), ptr(b["dead"]),
+         ptr(b["weight"]), ptr(x), ctypes.c_int32(batch), ctypes.c_int32(n), ptr(out), _stream())
+
+
+def batched_backward(b: Bucket, g: torch.Tensor, out: torch.Tensor) -> None:
+    cap = _bucket(b)
+    n, batch = g.shape
+    call("pxb_batched_backward", ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]), ptr(b["dead"]),
+         ptr(b["weight"]), ptr(g), ctypes.c_int32(batch), ctypes.c_int32(n), ptr(out), _stream())
+
+
+def batched_update(b: Bucket, g: torch.Tensor, a: torch.Tensor, opt: _lib.Optimizer) -> None:
+    cap = _bucket(b)
+    n, batch = g.shape
+    call("pxb_batched_update", ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]), ptr(b["dead"]),
+         ptr(b["weight"]), ptr(g), ptr(a), ctypes.c_int32(batch), ctypes.c_int32(n), ctypes.byref(opt),
+         ptr(b.get("opt/m")), ptr(b.get("opt/v")), ptr(b.get("opt/t")), _stream())
+
+
+# ---------------------------------------------------------------------------
+# growth
+# ---------------------------------------------------------------------------
+def philox32(seed: torch.Tensor, counter: torch.Tensor) -> torch.Tensor:
+    out = torch.empty(seed.shape, dtype=torch.int32, device=seed.device)
+    call("pxb_philox32", ctypes.c_int64(seed.numel()), ptr(seed), ptr(counter), ptr(out), _stream())
+    return out
+
+
+def site_seed(network_seed: int, step: int, stream: int, key: int) -> int:
+    return int(_lib.lib().pxb_site_seed(network_seed, step, stream, key))
+
+
+def propose_per_unit(num_units: int, proposals: int, network_seed: int, step: int, *, dst_lo: int, dst_n: int,
+                     score_kind: int, level: torch.Tensor, grad: torch.Tensor | None = None,
+                     act: torch.Tensor | None = None, pruned: torch.Tensor | None = None, max_level_gap: int = 1,
+                     direction: int = 0, allow_self_loops: bool = False, bucket_level: int = -1,
+                     src_level_bound: int = 0,
+                     out: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None
+                     ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    total = num_units * proposals
+    dev = level.device
+    if out is None:
+        out = (torch.empty(total, dtype=torch.int32, device=dev), torch.empty(total, dtype=torch.int32, device=dev),
+               torch.empty(total, dtype=torch.float32, device=dev))
+    src, dst, score = out
+    call("pxb_propose_per_unit", ctypes.c_int32(num_units), ctypes.c_int32(proposals),
+         ctypes.c_uint64(network_seed), ctypes.c_int32(step), ctypes.c_int32(dst_lo), ctypes.c_int32(dst_n),
+         ctypes.c_int32(score_kind), ptr(grad), ptr(act), ptr(level), ptr(pruned), ctypes.c_int32(max_level_gap),
+         ctypes.c_int32(direction), ctypes.c_int32(1 if allow_self_loops else 0), ctypes.c_int32(bucket_level),
+         ctypes.c_int32(src_level_bound), ptr(src), ptr(dst), ptr(score), _stream())
+    return src, dst, score
+
+
+def total_order_scratch(n: int, id_bound: int) -> int:
+    return query_size("pxb_total_order_scratch_bytes", ctypes.c_int64(n), ctypes.c_int32(id_bound))
+
+
+def total_order(score: torch.Tensor, src: torch.Tensor, dst: torch.Tensor, id_bound: int,
+                perm: torch.Tensor | None = None, scratch: torch.Tensor | None = None) -> torch.Tensor:
+    n = score.numel()
+    if perm is None:
+        perm = torch.empty(n, dtype=torch.int32, device=score.device)
+    need = total_order_scratch(n, id_bound)
+    if scratch is None or scratch.numel() < need:
+        scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=score.device)
+    call("pxb_total_order", ctypes.c_int64(n), ptr(score), ptr(src), ptr(dst), ctypes.c_int32(id_bound), ptr(perm),
+         ptr(scratch), ctypes.c_size_t(scratch.numel()), _stream())
+    return perm
+
+
+def select_step_scratch(n: int, k: int) -> int:
+    return query_size("pxb_select_step_scratch_bytes", ctypes.c_int64(n), ctypes.c_int64(k))
+
+
+def select_step(perm: torch.Tensor, score: torch.Tensor, src: torch.Tensor, level: torch.Tensor, k: int,
+                win: torch.Tensor | None = None, scratch: torch.Tensor | None = None) -> torch.Tensor:
+    n = perm.numel()
+    kk = min(k, n)
+    if win is None:
+        win = torch.empty(max(kk, 1), dtype=torch.int32, device=perm.device)
+    need = select_step_scratch(n, k)
+    if scratch is None or scratch.numel() < need:
+        scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=perm.device)
+    call("pxb_select_step", ctypes.c_int64(n), ptr(perm), ptr(score), ptr(src), ptr(level), ctypes.c_int64(k),
+         ptr(win), None, ptr(scratch), ctypes.c_size_t(scratch.numel()), _stream())
+    return win[:kk]
+
+
+def gather_winners(win: torch.Tensor, count: int, k: int, src: torch.Tensor, dst: torch.Tensor,
+                   score: torch.Tensor, *, init_kind: int, init_a: float = 0.0, init_b: float = 0.0,
+                   init_salt: int = 0, out: tuple | None = None) -> tuple[torch.Tensor, ...]:
+    dev = src.device
+    if out is None:
+        out = (torch.empty(k, dtype=torch.int32, device=dev), torch.empty(k, dtype=torch.int32, device=dev),
+               torch.empty(k, dtype=torch.float32, device=dev), torch.empty(k, dtype=torch.uint8, device=dev))
+    s, d, w, g = out
+    call("pxb_gather_winners", ctypes.c_int64(k), ctypes.c_int64(count), ptr(win), ptr(src), ptr(dst), ptr(score),
+         ctypes.c_int32(init_kind), ctypes.c_float(init_a), ctypes.c_float(init_b), ctypes.c_uint32(init_salt),
+         ptr(s), ptr(d), ptr(w), ptr(g), _stream())
+    return s, d, w, g
+
+
+# ---------------------------------------------------------------------------
+# slot claim
+# ---------------------------------------------------------------------------
+def claim_scratch(cap: int, k: int, num_levels: int) -> int:
+    return query_size("pxb_claim_scratch_bytes", ctypes.c_int64(cap), ctypes.c_int64(k), ctypes.c_int32(num_levels))
+
+
+class ClaimWorkspace:
+    """Caller-owned scratch for one claim (allocated once, reused per step)."""
+
+    def __init__(self, cap: int, k: int, num_levels: int, device: torch.device) -> None:
+        self.cap, self.k, self.num_levels = cap, k, num_levels
+        self.scratch = torch.empty(max(claim_scratch(cap, k, num_levels), 1), dtype=torch.uint8, device=device)
+        self.level_counts = torch.zeros(num_levels, dtype=torch.int32, device=device)
+        self.counts = torch.zeros(4, dtype=torch.int32, device=device)
+        self.overflowed = torch.zeros(max(k, 1), dtype=torch.uint8, device=device)
+
+
+def claim_prepare(mode: int, b: Bucket, unit_level: torch.Tensor, tail_start: torch.Tensor | None,
+                  ws: ClaimWorkspace, *, shard_base: int = 0) -> torch.Tensor:
+    cap = _bucket(b)
+    call("pxb_claim_prepare", ctypes.c_int32(mode), ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["dead"]),
+         ptr(unit_level), ctypes.c_int32(unit_level.numel()), ctypes.c_int32(ws.num_levels),
+         ctypes.c_int64(shard_base), ptr(tail_start), ctypes.c_int64(ws.k), ptr(ws.level_counts), ptr(ws.scratch),
+         ctypes.c_size_t(ws.scratch.numel()), _stream())
+    return ws.level_counts
+
+
+def claim_commit(mode: int, b: Bucket, unit_level: torch.Tensor, tail_start: torch.Tensor | None,
+                 ws: ClaimWorkspace, src: torch.Tensor, dst: torch.Tensor, weight: torch.Tensor,
+                 growable: torch.Tensor, *, max_new: int = -1, shard_base: int = 0, global_cap: int | None = None,
+                 level_before: torch.Tensor | None = None, level_totals: torch.Tensor | None = None,
+                 extra: Mapping[str, torch.Tensor] | None = None) -> None:
+    cap = _bucket(b)
+    k = src.numel()
+    if k != ws.k:
+        raise ValueError(f"claim workspace sized for {ws.k} candidates, got {k}")
+    names = sorted(extra or {})
+    n_extra = len(names)
+    cols = (ctypes.c_void_p * 8)(*[b[nm].data_ptr() for nm in names])
+    nbytes = (ctypes.c_int32 * 8)(*[b[nm].element_size() for nm in names])
+    vals = (ctypes.c_void_p * 8)(*[extra[nm].data_ptr() for nm in names])  # type: ignore[index]
+    call("pxb_claim_commit", ctypes.c_int32(mode), ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]),
+         ptr(b["dead"]), ptr(b["weight"]), ptr(unit_level), ctypes.c_int32(unit_level.numel()),
+         ctypes.c_int32(ws.num_levels), ctypes.c_int64(shard_base),
+         ctypes.c_int64(cap + shard_base if global_cap is None else global_cap), ptr(tail_start), ctypes.c_int64(k),
+         ptr(src), ptr(dst), ptr(weight), ptr(growable), ctypes.c_int64(max_new), ptr(level_before),
+         ptr(level_totals), ctypes.c_int32(n_extra), ctypes.cast(cols, ctypes.c_void_p) if n_extra else None,
+         ctypes.cast(nbytes, ctypes.c_void_p) if n_extra else None,
+         ctypes.cast(vals, ctypes.c_void_p) if n_extra else None, ptr(ws.counts), ptr(ws.overflowed), ptr(ws.scratch),
+         ctypes.c_size_t(ws.scratch.numel()), _stream())
+
+
+def count_dead(b: Bucket, out: torch.Tensor) -> None:
+    cap = _bucket(b)
+    call("pxb_count_dead", ctypes.c_int64(cap), ptr(b["dead"]), ptr(out), _stream())

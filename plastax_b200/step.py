@@ -1,0 +1,393 @@
+"""Step assembly (mirrors src/plastax/step.py:45-356 and the phase order of
+src/plastax/phases.py:87-176).
+
+`make_step(net, static)` returns a StepFn: `step(state, inputs) ->
+StepResult(state, overflow, loss, growth_remainder, grown)`. As in the
+reference (jit with donate_argnums=0) the state's buffers pass to the step:
+it updates them in place on the device and returns the same state object.
+All buffers a step needs (accumulators, candidate lists, sort and claim
+scratch) are allocated once when the StepFn is built; a step allocates
+nothing on the device and never synchronises with the host unless the
+growth rule declares `on_overflow = "error"`.
+
+Phase order: forward, loss, backward, update_conn, prune_conn, add_conn
+(update_unit, prune_unit and add_unit have no engine lowering yet and are
+rejected when the Network class is defined). Fusions, each legal only where
+it cannot change a result:
+- prune into forward (src/plastax/phases.py:1629-1700, plan_prune_fusion):
+  a MagnitudePrune reads only the weight, so it rides on the forward's read
+  of every slot when no update_conn writes weights in between;
+- update_conn into backward (TOPOLOGICAL): bucket l's destinations are all
+  finalized before bucket l is swept in the reverse walk, so each slot's
+  optimizer step uses the same grad[dst] the separate update pass would.
+Scheme-A: each rank sweeps its capacity band; the per-unit partials are
+all-reduced with NCCL (the monoid's collective, src/plastax/monoid.py:175)
+before every apply, and the claim all-gathers the per-domain free counts.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+from typing import Any
+
+import numpy as np
+import torch
+
+from plastax_b200 import _lib
+from plastax_b200 import kernels as K
+from plastax_b200.state import NetworkState, NetworkStatic
+from plastax_b200.traits import (
+    DestinationThresholdPrune,
+    MagnitudePrune,
+    MSELoss,
+    Network,
+    ProposeAddConn,
+)
+from plastax_b200.types import ACTIVATION, LEVEL, PRUNED, Propagation
+
+
+@dataclasses.dataclass(frozen=True)
+class StepInputs:
+    """Clamped inputs + targets for one step (src/plastax/phases.py:68-83).
+    Host (numpy) or device tensors; host values are copied to the device."""
+
+    inputs: Any
+    targets: Any = None
+
+
+@dataclasses.dataclass
+class GrowthRemainder:
+    """The claim's inputs and which candidates it dropped
+    (src/plastax/phases.py:2799-2820), for a growth-only retry."""
+
+    src: torch.Tensor
+    dst: torch.Tensor
+    weight: torch.Tensor
+    dropped: torch.Tensor
+
+
+@dataclasses.dataclass
+class StepResult:
+    """src/plastax/step.py:45-67. `overflow`, `grown` and `loss` are device
+    scalars; reading them on the host synchronises."""
+
+    state: NetworkState
+    overflow: torch.Tensor
+    loss: torch.Tensor
+    growth_remainder: GrowthRemainder | None
+    grown: torch.Tensor
+
+
+def _dist():
+    import torch.distributed as dist
+
+    return dist
+
+
+class StepFn:
+    """A built step: preallocated buffers plus the phase sequence."""
+
+    def __init__(self, net: type[Network], static: NetworkStatic, device: torch.device) -> None:
+        self.net, self.static, self.dev = net, static, device
+        n = static.num_units
+        fp = net.forward_pass
+        self.pipeline = static.propagation is Propagation.PIPELINE
+        self.num_buckets = len(static.level_capacities)
+        self.fwd_monoid = fp.combine.lowered()
+        self.fwd_identity = fp.combine.identity
+        self.acc = torch.empty(n, dtype=torch.float32, device=device)
+        self.input_ids = torch.tensor(static.input_ids, dtype=torch.int64, device=device)
+        self.output_ids = torch.tensor(static.output_ids, dtype=torch.int32, device=device)
+        is_input = np.zeros(n, np.uint8)
+        is_input[list(static.input_ids)] = 1
+        self.is_input = torch.from_numpy(is_input).to(device)
+        self.loss_buf = torch.zeros(1, dtype=torch.float32, device=device)
+        self.sharded = static.sharding is not None and static.num_shards > 1
+        self.reduce_op = fp.combine.torch_reduce_op() if self.sharded else None
+        # fusion legality
+        self.fuse_prune = (isinstance(net.prune_conn, MagnitudePrune) and net.update_conn is None)
+        self.fuse_update = (not self.pipeline and net.update_conn is not None and net.backward_pass is not None
+                            and net.update_unit is None)
+        self.opt = net.update_conn.struct() if net.update_conn is not None else None
+        self.ac: ProposeAddConn | None = net.add_conn
+        if self.ac is not None:
+            self._build_growth()
+        self.launches = 0
+
+    # -- growth buffers ------------------------------------------------------
+    def _build_growth(self) -> None:
+        ac, st, dev = self.ac, self.static, self.dev
+        n = st.num_units
+        P = ac.proposals_per_proposer
+        self.n_cand = n * P
+        self.k = max(0, min(int(ac.max_new_per_level), self.n_cand))
+        if ac.level_cap_scope != "step":
+            raise NotImplementedError(
+                "the engine runs level_cap_scope='step' growth; per-source-level caps have no lowering yet")
+        self.cand = (torch.empty(self.n_cand, dtype=torch.int32, device=dev),
+                     torch.empty(self.n_cand, dtype=torch.int32, device=dev),
+                     torch.empty(self.n_cand, dtype=torch.float32, device=dev))
+        self.perm = torch.empty(self.n_cand, dtype=torch.int32, device=dev)
+        self.order_scratch = torch.empty(max(K.total_order_scratch(self.n_cand, n), 1), dtype=torch.uint8,
+                                         device=dev)
+        self.win = torch.empty(max(self.k, 1), dtype=torch.int32, device=dev)
+        self.sel_scratch = torch.empty(max(K.select_step_scratch(self.n_cand, self.k), 1), dtype=torch.uint8,
+                                       device=dev)
+        kk = max(self.k, 1)
+        self.claim_in = (torch.empty(kk, dtype=torch.int32, device=dev), torch.empty(kk, dtype=torch.int32, device=dev),
+                         torch.empty(kk, dtype=torch.float32, device=dev), torch.empty(kk, dtype=torch.uint8, device=dev))
+        self.extra_defaults: dict[str, torch.Tensor] = {}
+        builtin = {"from_id", "to_id", "dead", "weight"}
+        for spec in st.conn_fields:
+            if spec.name in builtin:
+                continue
+            from plastax_b200.state import torch_dtype
+
+            self.extra_defaults[spec.name] = torch.full((kk,), spec.default, dtype=torch_dtype(spec), device=dev)
+        self.num_levels = st.num_levels if self.pipeline else 1
+        self.claim_ws = [K.ClaimWorkspace(st.local_capacity(b), self.k, self.num_levels, dev)
+                         for b in range(self.num_buckets)]
+        self.init_kind = {"const": _lib.INIT_CONST, "dyadic": _lib.INIT_DYADIC,
+                          "hash_uniform": _lib.INIT_HASH_UNIFORM}[ac.init[0]]
+        self.init_a = float(ac.init[1]) if len(ac.init) > 1 else 0.0
+        self.score_kind = {"uniform": _lib.SCORE_UNIFORM, "uniform_q256": _lib.SCORE_UNIFORM_Q256,
+                           "grad_act": _lib.SCORE_GRAD_ACT}[ac.score]
+        self.direction = {"any": 0, "deeper": 1, "same_or_deeper": 2}[ac.direction]
+        self.grown = torch.zeros((), dtype=torch.int32, device=dev)
+        self.overflow = torch.zeros((), dtype=torch.bool, device=dev)
+        if self.sharded:
+            G = st.num_shards
+            self.gather_buf = torch.zeros((G, self.num_levels), dtype=torch.int32, device=dev)
+
+    # -- collectives -----------------------------------------------------------
+    def _combine_partials(self, acc: torch.Tensor) -> None:
+        if self.sharded:
+            _dist().all_reduce(acc, op=self.reduce_op)
+
+    # -- phases -----------------------------------------------------------------
+    def _scatter_inputs(self, state: NetworkState, inputs: StepInputs) -> None:
+        x = inputs.inputs
+        if not isinstance(x, torch.Tensor):
+            x = torch.from_numpy(np.ascontiguousarray(x, np.float32))
+        x = x.to(self.dev, non_blocking=True).reshape(-1)
+        state.units[ACTIVATION.name].index_copy_(0, self.input_ids, x)
+
+    def _forward(self, state: NetworkState) -> None:
+        net, st, units = self.net, self.static, state.units
+        act = units[ACTIVATION.name]
+        pruned = units.get(PRUNED.name)
+        fp = net.forward_pass
+        K.fill(self.acc, self.fwd_identity)
+        if self.pipeline:
+            b = state.conns[0]
+            if self.fuse_prune:
+                K.forward_prune(b, act, self.acc, monoid=self.fwd_monoid, prune_kind=_lib.PRUNE_ABS_BELOW,
+                                threshold=net.prune_conn.threshold)
+            else:
+                K.forward_accumulate(b, act, self.acc, self.fwd_monoid)
+            self._combine_partials(self.acc)
+            K.unit_apply(self.acc, act, mode=0, act_kind=fp.activation, monoid=self.fwd_monoid,
+                         is_input=self.is_input, pruned=pruned)
+            self.launches += 3
+            return
+        level = units[LEVEL.name]
+        for l in range(self.num_buckets):
+            b = state.conns[l]
+            if self.fuse_prune:
+                K.forward_prune(b, act, self.acc, monoid=self.fwd_monoid, prune_kind=_lib.PRUNE_ABS_BELOW,
+                                threshold=net.prune_conn.threshold)
+            else:
+                K.forward_accumulate(b, act, self.acc, self.fwd_monoid)
+            self._combine_partials(self.acc)
+            K.unit_apply(self.acc, act, mode=0, act_kind=fp.activation, monoid=self.fwd_monoid, level=level,
+                         target_level=l + 1, is_input=self.is_input, pruned=pruned)
+            self.launches += 2
+
+    def _loss(self, state: NetworkState, inputs: StepInputs) -> None:
+        loss = self.net.loss
+        if loss is None:
+            return
+        if not isinstance(loss, MSELoss):
+            raise NotImplementedError("only MSELoss has an engine lowering in the streaming step")
+        t = inputs.targets
+        if t is None:
+            raise ValueError("a network with a loss needs StepInputs.targets")
+        if not isinstance(t, torch.Tensor):
+            t = torch.from_numpy(np.ascontiguousarray(t, np.float32))
+        t = t.to(self.dev, non_blocking=True).reshape(-1)
+        K.mse_loss(self.output_ids, state.units[ACTIVATION.name], t, state.units[loss.seed_field.name],
+                   self.loss_buf)
+        self.launches += 1
+
+    def _backward(self, state: NetworkState) -> None:
+        net = self.net
+        bp = net.backward_pass
+        if bp is None:
+            return
+        units = state.units
+        act, grad = units[ACTIVATION.name], units[bp.grad_field.name]
+        seed = units.get(bp.seed_field.name)
+        pruned = units.get(PRUNED.name)
+        K.fill(self.acc, 0.0)
+        if self.pipeline:
+            K.backward_accumulate(state.conns[0], grad, self.acc, "sum")
+            self._combine_partials(self.acc)
+            K.unit_apply(self.acc, grad, mode=1, act_kind=bp.activation, act=act, seed=seed, pruned=pruned)
+            self.launches += 3
+            return
+        level = units[LEVEL.name]
+        L = self.num_buckets
+        K.unit_apply(self.acc, grad, mode=1, act_kind=bp.activation, act=act, seed=seed, level=level,
+                     target_level=L, is_input=self.is_input, pruned=pruned)
+        for l in range(L - 1, 0, -1):
+            b = state.conns[l]
+            if self.fuse_update:
+                K.backward_update(b, grad, act, self.acc, self.opt)
+            else:
+                K.backward_accumulate(b, grad, self.acc, "sum")
+            self._combine_partials(self.acc)
+            K.unit_apply(self.acc, grad, mode=1, act_kind=bp.activation, act=act, seed=seed, level=level,
+                         target_level=l, is_input=self.is_input, pruned=pruned)
+            self.launches += 2
+        if self.fuse_update and L > 0:
+            K.backward_update(state.conns[0], grad, act, None, self.opt)  # bucket 0: update only
+            self.launches += 1
+
+    def _update_conn(self, state: NetworkState) -> None:
+        net = self.net
+        if net.update_conn is None or self.fuse_update:
+            return
+        units = state.units
+        grad, act = units[net.update_conn.grad_field.name], units[ACTIVATION.name]
+        for b in state.conns:
+            K.backward_update(b, grad, act, None, self.opt)
+            self.launches += 1
+
+    def _prune(self, state: NetworkState) -> None:
+        pc = self.net.prune_conn
+        if pc is None or self.fuse_prune:
+            return
+        n = self.static.num_units
+        for b in state.conns:
+            if isinstance(pc, MagnitudePrune):
+                K.prune_conn(b, n, prune_kind=_lib.PRUNE_ABS_BELOW, threshold=pc.threshold)
+            elif isinstance(pc, DestinationThresholdPrune):
+                K.prune_conn(b, n, prune_kind=_lib.PRUNE_ABS_BELOW_DST, unit_threshold=state.units[pc.field.name])
+            self.launches += 1
+
+    def _fires(self, state: NetworkState) -> bool:
+        ac = self.ac
+        interval = int(getattr(self.net, "structural_interval", 1))
+        fire = interval <= 1 or state.step % interval == 0
+        trig = ac.trigger
+        if isinstance(trig, tuple) and trig and trig[0] == "every":
+            fire = fire and state.step % int(trig[1]) == 0
+        elif trig not in ("every_step",):
+            raise NotImplementedError(f"growth trigger {trig!r} has no engine lowering")
+        return fire
+
+    def _add_conn(self, state: NetworkState) -> GrowthRemainder | None:
+        ac = self.ac
+        if ac is None:
+            return None
+        st, units = self.static, state.units
+        self.grown.zero_()
+        self.overflow.zero_()
+        if not self._fires(state) or self.k == 0:
+            state.grown, state.overflow = self.grown, self.overflow
+            return None
+        n = st.num_units
+        level = units[LEVEL.name]
+        pruned = units.get(PRUNED.name)
+        dst_n = ac.dst_n if ac.dst_n is not None else n - ac.dst_lo
+        grad = units.get(ac.grad_field.name) if ac.score == "grad_act" else None
+        K.propose_per_unit(n, ac.proposals_per_proposer, st.seed, state.step, dst_lo=ac.dst_lo, dst_n=dst_n,
+                           score_kind=self.score_kind, level=level, grad=grad, act=units[ACTIVATION.name],
+                           pruned=pruned, max_level_gap=ac.max_level_gap, direction=self.direction,
+                           allow_self_loops=ac.allow_self_loops,
+                           src_level_bound=0 if self.pipeline else self.num_buckets, out=self.cand)
+        src, dst, score = self.cand
+        K.total_order(score, src, dst, n, perm=self.perm, scratch=self.order_scratch)
+        K.select_step(self.perm, score, src, level, self.k, win=self.win, scratch=self.sel_scratch)
+        kk = min(self.k, self.n_cand)
+        K.gather_winners(self.win, kk, self.k, src, dst, score, init_kind=self.init_kind, init_a=self.init_a,
+                         out=self.claim_in)
+        self.launches += 4 + 5
+        cs, cd, cw, grow = self.claim_in
+        max_new = -1 if ac.max_new_per_step is None else int(ac.max_new_per_step)
+        if self.pipeline:
+            mode = _lib.CLAIM_PIPELINE
+            buckets = [(0, grow)]
+        else:
+            mode = _lib.CLAIM_TOPOLOGICAL
+            # step scope: the winners list is level-major; the per-step cap
+            # ranks growable winners in that order across buckets
+            g = grow.bool()
+            if max_new >= 0:
+                g = g & (torch.cumsum(g.to(torch.int32), 0) <= max_new)
+            lv = level[cs.long()]
+            buckets = [(bk, (g & (lv == bk)).to(torch.uint8)) for bk in range(self.num_buckets)]
+            max_new = -1
+        for bk, gb in buckets:
+            b, ws = state.conns[bk], self.claim_ws[bk]
+            base = st.shard_base(bk)
+            K.claim_prepare(mode, b, level, state.tail_start, ws, shard_base=base)
+            before = totals = None
+            if self.sharded:
+                dist = _dist()
+                dist.all_gather_into_tensor(self.gather_buf, ws.level_counts)
+                rank = st.shard_rank
+                before = self.gather_buf[:rank].sum(0, dtype=torch.int32) if rank else torch.zeros_like(
+                    ws.level_counts)
+                totals = self.gather_buf.sum(0, dtype=torch.int32)
+            K.claim_commit(mode, b, level, state.tail_start, ws, cs, cd, cw, gb, max_new=max_new, shard_base=base,
+                           global_cap=st.level_capacities[bk], level_before=before, level_totals=totals,
+                           extra=self.extra_defaults)
+            self.grown += ws.counts[0]
+            self.overflow |= ws.counts[1] > 0
+            state.needs_resort |= ws.counts[3] > 0
+            self.launches += 12
+        state.grown, state.overflow = self.grown, self.overflow
+        if ac.on_overflow == "error" and bool(self.overflow.item()):
+            raise RuntimeError('add_conn overflow: selected candidates exceeded the free connection capacity '
+                               '(the rule declares on_overflow = "error").')
+        return GrowthRemainder(cs, cd, cw, self.claim_ws[0].overflowed)
+
+    def __call__(self, state: NetworkState, inputs: StepInputs) -> StepResult:
+        self._scatter_inputs(state, inputs)
+        self._forward(state)
+        self._loss(state, inputs)
+        self._backward(state)
+        self._update_conn(state)
+        self._prune(state)
+        remainder = self._add_conn(state)
+        state.step += 1
+        grown = state.grown if state.grown is not None else torch.zeros((), dtype=torch.int32, device=self.dev)
+        overflow = state.overflow if state.overflow is not None else torch.zeros((), dtype=torch.bool,
+                                                                                 device=self.dev)
+        return StepResult(state=state, overflow=overflow, loss=self.loss_buf[0], growth_remainder=remainder,
+                          grown=grown)
+
+
+def make_step(net: type[Network], static: NetworkStatic, *, batch_size: int | None = None, layout: str = "auto",
+              fuse_prune: str | bool = "auto", growth: str = "auto", device: torch.device | str = "cuda") -> StepFn:
+    """Build the step for `net` on `static` (src/plastax/step.py:76-237).
+
+    Raises ValueError for an unknown knob, as the reference does.
+    """
+    if layout not in ("auto", "edges", "csr", "triton", "xla"):
+        raise ValueError(f"make_step: unknown layout {layout!r}")
+    if growth not in ("auto", "xla", "triton"):
+        raise ValueError(f"make_step: unknown growth engine {growth!r}")
+    if fuse_prune not in ("auto", True, False):
+        raise ValueError(f"make_step: unknown fuse_prune {fuse_prune!r}")
+    if batch_size is not None:
+        if batch_size < 1:
+            raise ValueError("make_step: batch_size must be >= 1")
+        from plastax_b200.batched import BatchedStepFn
+
+        return BatchedStepFn(net, static, batch_size, torch.device(device))
+    fn = StepFn(net, static, torch.device(device))
+    if fuse_prune is False:
+        fn.fuse_prune = False
+    return fn

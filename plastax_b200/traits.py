@@ -1,0 +1,230 @@
+"""Policy traits and the Network base (mirrors src/plastax/traits.py).
+
+The reference's policies are arbitrary JAX callables traced under vmap; a
+native engine can only run the forms it recognises. Each trait here is that
+recognised form, with the reference's names, attributes and defaults, and
+`Network` validates a subclass's slots the way the reference's
+`__init_subclass__` does, raising at class-definition time for a policy the
+engine cannot run (there is no fallback path).
+
+Recognised forms:
+- ForwardPass: map = weight * activation[src] (the linear_input map of
+  src/plastax/phases.py:535-556), combine = sum/max/min, apply =
+  activation(acc) written into ACTIVATION (identity, tanh, relu, sigmoid).
+- BackwardPass: map = weight * grad_field[dst], combine = sum, apply:
+  grad_field = (acc + seed_field) * activation'(ACTIVATION)
+  (scripts/parity/golden_rules.py relu_mlp_v1 generalised).
+- Loss: MSELoss (scripts/parity/reference.py:338-352).
+- update_conn: an optimizer bundle from plastax_b200.optim (sgd, momentum,
+  adam, adamw, rmsprop; src/plastax/optim).
+- PruneConn: |weight| < threshold (MagnitudePrune) or |weight| <
+  unit[field, dst] (DestinationThresholdPrune).
+- ProposeAddConn: proposer "per_unit", dst = dst_lo + uniform_int(dst_n)
+  [sub 0], score uniform / floor(u*256)/256 [sub 1] or |grad[dst]*act[src]|,
+  init weight constant / dyadic / hashed uniform.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+from typing import Any, ClassVar
+
+from plastax_b200 import monoid as _monoid
+from plastax_b200.types import FieldSpec, Propagation, ShardSpec
+
+ACTIVATIONS = ("identity", "tanh", "relu", "sigmoid")
+
+GRAD_PRE_ACT = FieldSpec.float32("grad_pre_act")
+LOSS_GRAD = FieldSpec.float32("loss_grad")
+
+
+class ForwardPass:
+    """Forward propagation policy (src/plastax/traits.py:39-90)."""
+
+    combine: _monoid.Monoid = _monoid.sum_
+    activation: str = "tanh"
+
+    def __init__(self, activation: str | None = None, combine: _monoid.Monoid | None = None) -> None:
+        if activation is not None:
+            self.activation = activation
+        if combine is not None:
+            self.combine = combine
+
+
+class BackwardPass:
+    """Backward propagation policy (src/plastax/traits.py:92-152)."""
+
+    combine: _monoid.Monoid = _monoid.sum_
+    activation: str = "tanh"
+    grad_field: FieldSpec = GRAD_PRE_ACT
+    seed_field: FieldSpec = LOSS_GRAD
+
+    def __init__(self, activation: str | None = None, grad_field: FieldSpec | None = None,
+                 seed_field: FieldSpec | None = None) -> None:
+        if activation is not None:
+            self.activation = activation
+        if grad_field is not None:
+            self.grad_field = grad_field
+        if seed_field is not None:
+            self.seed_field = seed_field
+
+
+class MSELoss:
+    """L = 0.5 * sum (act - t)^2 over the outputs; seed = act - t
+    (scripts/parity/reference.py:338-352)."""
+
+    def __init__(self, seed_field: FieldSpec = LOSS_GRAD) -> None:
+        self.seed_field = seed_field
+
+
+class PruneConn:
+    """Connection prune policy (src/plastax/traits.py:352-375)."""
+
+
+class MagnitudePrune(PruneConn):
+    """Prune a connection when |weight| < threshold."""
+
+    def __init__(self, threshold: float) -> None:
+        self.threshold = float(threshold)
+
+
+class DestinationThresholdPrune(PruneConn):
+    """Prune a connection when |weight| < unit[field, dst] (the per-unit
+    magnitude threshold of examples/dst_sparse.py:189-199)."""
+
+    def __init__(self, field: FieldSpec) -> None:
+        self.field = field
+
+
+class ResetGlobal:
+    """Globals reset (src/plastax/traits.py:686-703); host-side, O(1)."""
+
+    def reset(self, g: Any) -> Any:
+        return g
+
+
+@dataclasses.dataclass
+class ProposeAddConn:
+    """Proposal growth (src/plastax/traits.py:577-684) in its recognised form."""
+
+    proposals_per_proposer: int
+    max_new_per_level: int
+    dst_lo: int = 0
+    dst_n: int | None = None
+    score: str = "uniform"  # "uniform", "uniform_q256" or "grad_act"
+    init: tuple = ("const", 0.0)  # ("const", a) | ("dyadic",) | ("hash_uniform", a)
+    proposer: str = "per_unit"
+    selection: str = "top_k"
+    level_cap_scope: str = "source_level"
+    max_level_gap: int = 1
+    direction: str = "any"
+    allow_self_loops: bool = False
+    dedupe_live: bool = False
+    dedupe_step: bool = False
+    max_new_per_step: int | None = None
+    trigger: Any = "every_step"
+    on_overflow: str = "flag"
+    grad_field: FieldSpec = GRAD_PRE_ACT
+
+    def validate(self) -> None:
+        if self.proposer != "per_unit":
+            raise NotImplementedError(f"proposer {self.proposer!r} has no engine lowering (per_unit only)")
+        if self.selection != "top_k":
+            raise NotImplementedError(f"selection {self.selection!r} has no engine lowering (top_k only)")
+        if self.level_cap_scope not in ("source_level", "step"):
+            raise ValueError(f"unknown level_cap_scope {self.level_cap_scope!r}")
+        if self.direction not in ("any", "deeper", "same_or_deeper"):
+            raise ValueError(f"unknown direction {self.direction!r}")
+        if self.dedupe_live or self.dedupe_step:
+            raise NotImplementedError("dedupe_live / dedupe_step have no engine lowering yet")
+        if self.score not in ("uniform", "uniform_q256", "grad_act"):
+            raise ValueError(f"unknown proposal score {self.score!r}")
+        if self.init[0] not in ("const", "dyadic", "hash_uniform"):
+            raise ValueError(f"unknown init rule {self.init!r}")
+        if self.proposals_per_proposer < 1 or self.max_new_per_level < 0:
+            raise ValueError("proposals_per_proposer must be >= 1 and max_new_per_level >= 0")
+        if self.on_overflow not in ("flag", "error"):
+            raise ValueError(f"unknown on_overflow {self.on_overflow!r}")
+
+
+class Network:
+    """A network's trait slots (src/plastax/traits.py:874-1072).
+
+    Subclasses set class attributes; a slot left None is elided from the
+    step, as in the reference's phase assembly (src/plastax/phases.py:87-176).
+    """
+
+    forward_pass: ClassVar[ForwardPass]
+    loss: ClassVar[MSELoss | None] = None
+    backward_pass: ClassVar[BackwardPass | None] = None
+    update_unit: ClassVar[Any] = None
+    update_conn: ClassVar[Any] = None  # an optimizer bundle (plastax_b200.optim)
+    prune_unit: ClassVar[Any] = None
+    prune_conn: ClassVar[PruneConn | None] = None
+    add_unit: ClassVar[Any] = None
+    add_conn: ClassVar[ProposeAddConn | None] = None
+    reset_global: ClassVar[ResetGlobal | None] = None
+    propagation: ClassVar[Propagation] = Propagation.TOPOLOGICAL
+    seed: ClassVar[int] = 0
+    extra_conn_fields: ClassVar[tuple[FieldSpec, ...]] = ()
+    extra_unit_fields: ClassVar[tuple[FieldSpec, ...]] = ()
+    unit_capacity: ClassVar[int | None] = None
+    structural_interval: ClassVar[int] = 1
+    sharding: ClassVar[ShardSpec | None] = None
+    kahn_max_depth: ClassVar[int | None] = None
+
+    def __init_subclass__(cls, **kwargs: Any) -> None:
+        super().__init_subclass__(**kwargs)
+        fp = getattr(cls, "forward_pass", None)
+        if fp is None or not isinstance(fp, ForwardPass):
+            raise TypeError(f"{cls.__name__}: forward_pass must be a ForwardPass")
+        if fp.activation not in ACTIVATIONS:
+            raise ValueError(f"{cls.__name__}: unknown activation {fp.activation!r}")
+        fp.combine.lowered()
+        if cls.backward_pass is not None:
+            bp = cls.backward_pass
+            if bp.activation not in ACTIVATIONS:
+                raise ValueError(f"{cls.__name__}: unknown backward activation {bp.activation!r}")
+            if bp.combine.lowered() != "sum":
+                raise NotImplementedError(f"{cls.__name__}: the backward combine must be sum")
+        if cls.prune_conn is not None and not isinstance(cls.prune_conn, (MagnitudePrune, DestinationThresholdPrune)):
+            raise NotImplementedError(f"{cls.__name__}: prune_conn form has no engine lowering")
+        if cls.add_conn is not None:
+            cls.add_conn.validate()
+        if cls.update_unit is not None or cls.prune_unit is not None or cls.add_unit is not None:
+            raise NotImplementedError(
+                f"{cls.__name__}: unit-lifecycle and update_unit phases have no engine lowering yet"
+            )
+
+    @classmethod
+    def unit_fields(cls) -> tuple[FieldSpec, ...]:
+        from plastax_b200.types import ACTIVATION, LEVEL, PRUNED
+
+        fields: list[FieldSpec] = [ACTIVATION, LEVEL]
+        if cls.backward_pass is not None:
+            fields += [cls.backward_pass.grad_field]
+        if cls.loss is not None:
+            fields += [cls.loss.seed_field]
+        if isinstance(cls.prune_conn, DestinationThresholdPrune):
+            fields += [cls.prune_conn.field]
+        fields += list(cls.extra_unit_fields)
+        if cls.unit_capacity is not None:
+            fields += [PRUNED]
+        out: list[FieldSpec] = []
+        for f in fields:
+            if f.name not in {o.name for o in out}:
+                out.append(f)
+        return tuple(out)
+
+    @classmethod
+    def conn_fields(cls) -> tuple[FieldSpec, ...]:
+        from plastax_b200.types import BUILTIN_CONN_FIELDS
+
+        extra = list(cls.extra_conn_fields)
+        if cls.update_conn is not None:
+            extra += list(cls.update_conn.state_fields)
+        out = list(BUILTIN_CONN_FIELDS)
+        for f in extra:
+            if f.name not in {o.name for o in out}:
+                out.append(f)
+        return tuple(out)

@@ -1,0 +1,93 @@
+"""End-to-end parity of the reservoir churn step (make_step on the GPU) with
+the oracle's reference-order step, several steps in a row.
+
+Structure must be bit-exact every step: tombstones, the claimed slots and
+every written column, tail_start, grown. Activations within 1e-5 rel / 1e-6
+abs. At the benchmark's full size the same step is checked through
+size-independent properties (live-edge conservation, claim accounting,
+ids in range) since the oracle needs minutes per step there.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(cuda, cfg, steps, sharded_bands=1):
+    import torch
+
+    from oracle.steps import ReservoirOracle
+    from plastax_b200 import StepInputs, make_step
+    from plastax_b200.configs import build_reservoir
+
+    net, static, state = build_reservoir(cfg, cuda)
+    b = {k: v.cpu().numpy().copy() for k, v in state.conns[0].items()}
+    ref = ReservoirOracle(b, state.units["activation"].cpu().numpy().copy(), state.units["level"].cpu().numpy().copy(),
+                          int(state.tail_start.item()), num_inputs=cfg.num_inputs, num_res=cfg.num_units,
+                          tau=cfg.tau, k=cfg.k, init_a=cfg.sigma * math.sqrt(3.0), seed=cfg.seed)
+    step = make_step(net, static, device=cuda)
+    rng = np.random.default_rng(5)
+    for i in range(steps):
+        x = rng.standard_normal(cfg.num_inputs).astype(np.float32)
+        res = step(state, StepInputs(x))
+        ref.step(x)
+        got = {k: v.cpu().numpy() for k, v in res.state.conns[0].items()}
+        for col in ("from_id", "to_id", "dead", "weight"):
+            np.testing.assert_array_equal(got[col], ref.b[col], err_msg=f"step {i} column {col}")
+        np.testing.assert_allclose(res.state.units["activation"].cpu().numpy(), ref.act, rtol=1e-5, atol=1e-6)
+        assert int(res.state.tail_start.item()) == ref.tail
+        assert int(res.grown.item()) == int(ref.last_counts[0])
+        assert bool(res.overflow.item()) == bool(ref.last_counts[1] > 0)
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("log2,fan_in,churn", [(12, 16, 0.01), (14, 32, 0.001), (10, 8, 0.2)])
+def test_reservoir_churn_matches_oracle(cuda, log2, fan_in, churn):
+    from plastax_b200.configs import ReservoirConfig
+
+    _run(cuda, ReservoirConfig(num_units=1 << log2, fan_in=fan_in, churn=churn, capacity_align=256), steps=6)
+
+
+def test_reservoir_overflow_into_tail_exhaustion(cuda):
+    """A churn larger than the dead slots + tail: the claim overflows and
+    the flag and counts still match the oracle."""
+    from plastax_b200.configs import ReservoirConfig
+
+    cfg = ReservoirConfig(num_units=1 << 10, fan_in=8, churn=0.3, capacity_align=64, capacity_headroom=0.0)
+    _run(cuda, cfg, steps=4)
+
+
+@pytest.mark.slow
+def test_full_size_step_properties(cuda):
+    """The benchmark's full-size step: live edges change by exactly
+    grown - pruned; every live id is in range; tail_start only grows."""
+    import torch
+
+    from plastax_b200 import StepInputs, make_step
+    from plastax_b200.configs import C5, build_reservoir
+
+    net, static, state = build_reservoir(C5, cuda)
+    step = make_step(net, static, device=cuda)
+    n = static.num_units
+    b = state.conns[0]
+    live0 = int((b["dead"] == 0).sum())
+    tail0 = int(state.tail_start.item())
+    for i in range(2):
+        dead_before = b["dead"].clone()
+        w = b["weight"]
+        pruned = int(((dead_before == 0) & (w.abs() < C5.tau)).sum())
+        res = step(state, StepInputs(torch.randn(C5.num_inputs, device=cuda)))
+        live1 = int((b["dead"] == 0).sum())
+        grown = int(res.grown.item())
+        assert live1 == live0 - pruned + grown, (i, live0, pruned, grown, live1)
+        liv = b["dead"] == 0
+        assert int(b["from_id"][liv].min()) >= 0 and int(b["from_id"][liv].max()) < n
+        assert int(b["to_id"][liv].min()) >= C5.num_inputs and int(b["to_id"][liv].max()) < n
+        assert int(state.tail_start.item()) >= tail0
+        live0 = live1
+        del dead_before
