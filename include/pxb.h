@@ -93,6 +93,12 @@ PXB_API int pxb_abi_version(void);
 PXB_API const char *pxb_last_error(void);
 /* Number of SMs of the current device (grid sizing). */
 PXB_API int pxb_sm_count(int32_t *out);
+/* The library links the CUDA runtime statically: these set / read ITS
+ * current device for the calling host thread. A host that switches devices
+ * (one process driving several GPUs, or a device other than 0) binds the
+ * device it launches on before calling the entry points. */
+PXB_API int pxb_set_device(int32_t device);
+PXB_API int pxb_get_device(int32_t *device);
 
 /* ------------------------------------------------------------------ */
 /* propagation                                                         */

@@ -214,7 +214,8 @@ def select_per_segment(perm: np.ndarray, segment: np.ndarray, num_seg: int, k: i
                        ) -> tuple[np.ndarray, np.ndarray]:
     win = np.zeros((num_seg, max(k, 1)), np.int32)
     filled = np.zeros(num_seg, np.int32)
-    lib().pxo_select_per_segment(_i64(perm.size), _p(perm), _p(np.ascontiguousarray(segment, np.int32)),
+    seg = np.ascontiguousarray(segment, np.int32)
+    lib().pxo_select_per_segment(_i64(perm.size), _p(perm), _p(seg),
                                  ctypes.c_int32(num_seg), _i64(k), _p(win), _p(filled))
     return win[:, :k], filled
 
@@ -238,11 +239,12 @@ def claim_pipeline(b: dict, level: np.ndarray, tail_start: int, src: np.ndarray,
     counts = np.zeros(4, np.int32)
     over = np.zeros(max(k, 1), np.uint8)
     tail = ctypes.c_int64(tail_start)
+    grow = np.ascontiguousarray(growable, np.uint8)
     names = sorted(extra or {})
     ex = _extra([b[nm] for nm in names], [np.ascontiguousarray(extra[nm]) for nm in names]) if names else None
     lib().pxo_claim_pipeline(_i64(b["dead"].size), _p(b["from_id"]), _p(b["to_id"]), _p(b["dead"]),
                              _p(b["weight"]), _p(level), ctypes.c_int32(level.size), ctypes.byref(tail), _i64(k),
-                             _p(src), _p(dst), _p(weight), _p(growable.astype(np.uint8)), _i64(max_new),
+                             _p(src), _p(dst), _p(weight), _p(grow), _i64(max_new),
                              ctypes.byref(ex) if ex else None, _p(counts), _p(over))
     return counts, over[:k], int(tail.value)
 
@@ -254,11 +256,12 @@ def claim_topological(b: dict, level: np.ndarray, src: np.ndarray, dst: np.ndarr
     k = src.size
     counts = np.zeros(4, np.int32)
     over = np.zeros(max(k, 1), np.uint8)
+    grow = np.ascontiguousarray(growable, np.uint8)
     names = sorted(extra or {})
     ex = _extra([b[nm] for nm in names], [np.ascontiguousarray(extra[nm]) for nm in names]) if names else None
     lib().pxo_claim_topological(_i64(b["dead"].size), _p(b["from_id"]), _p(b["to_id"]), _p(b["dead"]),
                                 _p(b["weight"]), _p(level), ctypes.c_int32(level.size), _i64(k), _p(src),
-                                _p(dst), _p(weight), _p(growable.astype(np.uint8)), _i64(max_new),
+                                _p(dst), _p(weight), _p(grow), _i64(max_new),
                                 ctypes.byref(ex) if ex else None, _p(counts), _p(over))
     return counts, over[:k]
 

@@ -52,6 +52,19 @@ extern "C" int pxb_sm_count(int32_t *out) {
   return PXB_OK;
 }
 
+extern "C" int pxb_set_device(int32_t device) {
+  PXB_CUDA(cudaSetDevice(device));
+  return PXB_OK;
+}
+
+extern "C" int pxb_get_device(int32_t *device) {
+  PXB_REQUIRE(device != nullptr, "pxb_get_device: device is NULL");
+  int d = -1;
+  PXB_CUDA(cudaGetDevice(&d));
+  *device = d;
+  return PXB_OK;
+}
+
 extern "C" int pxb_fill_f32(int64_t n, float value, float *out, void *stream) {
   PXB_REQUIRE(n >= 0, "pxb_fill_f32: negative n");
   if (n == 0) return PXB_OK;

@@ -30,7 +30,16 @@ _DTYPES = {
 }
 
 
+_bound_device: list[int] = [-1]
+
+
 def _stream() -> ctypes.c_void_p:
+    """The current torch stream, after binding the library's runtime to the
+    current torch device (libpxb links its own CUDA runtime)."""
+    dev = torch.cuda.current_device()
+    if dev != _bound_device[0]:
+        call("pxb_set_device", ctypes.c_int32(dev))
+        _bound_device[0] = dev
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
