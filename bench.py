@@ -259,12 +259,13 @@ def engine_arm(args) -> None:
     gen.manual_seed(1234)
     inputs_dev = torch.randn((W + Kst, cfg.num_inputs), generator=gen, device=dev)
 
-    # per-launch time of the dominant kernel (fused forward + prune), CUDA
-    # events on the launching stream around each launch of the timed steps
+    # per-launch time of the dominant kernel (the fused forward + prune sweep),
+    # CUDA events on the launching stream around each launch of the timed steps
     fwd_events: list[tuple] = []
     import plastax_b200.kernels as K
 
-    orig_fp = K.forward_prune
+    fwd_name = "mirror_forward" if step.use_mirror else "forward_prune"
+    orig_fp = getattr(K, fwd_name)
 
     def timed_forward_prune(*a, **kw):
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -276,11 +277,12 @@ def engine_arm(args) -> None:
     for i in range(W):
         step(state, StepInputs(inputs_dev[i]))
     torch.cuda.synchronize()
+    swept_entries = int(step.mirrors[0].gfill.sum().item()) if step.use_mirror else static.local_capacity(0)
     if world > 1:
         dist.barrier()
     clocks = Clocks(local)
     clocks.start()
-    K.forward_prune = timed_forward_prune
+    setattr(K, fwd_name, timed_forward_prune)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -294,7 +296,7 @@ def engine_arm(args) -> None:
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    K.forward_prune = orig_fp
+    setattr(K, fwd_name, orig_fp)
     elapsed_ms = t0.elapsed_time(t1)
     fwd_ms = [s.elapsed_time(e) for s, e in fwd_events]
 
@@ -327,12 +329,14 @@ def engine_arm(args) -> None:
     value = live * Kst / (elapsed_ms / 1e3)
     e2e = live * Kst / (e2e_ms / 1e3)
 
-    # roofline of the fused forward + prune kernel: algorithmic bytes per
-    # launch = 13 B per local slot (from_id, to_id, weight, dead) + 8 B per
-    # unit (activation gather, accumulator)
+    # roofline of the fused forward + prune sweep: algorithmic bytes per
+    # launch = 8 B per swept mirror entry (packed ids + weight; the canonical
+    # sweep streams 13 B per slot instead) + 8 B per unit (activation read,
+    # accumulator written)
     local_cap = static.local_capacity(0)
     n = static.num_units
-    alg_bytes = 13 * local_cap + 8 * n
+    per_entry = 8 if step.use_mirror else 13
+    alg_bytes = per_entry * swept_entries + 8 * n
     fwd_avg_s = float(np.mean(fwd_ms)) / 1e3 if fwd_ms else float("nan")
     achieved = alg_bytes / fwd_avg_s / 1e9
     peak, peak_kind = measured_peak_hbm()
@@ -347,7 +351,10 @@ def engine_arm(args) -> None:
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4 * cfg.num_inputs, "d2h_bytes_per_step": 8,
                 "ms_per_step": e2e_ms / Kst},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "kernel": "forward_vec4_kernel<sum, prune> (fused forward + prune)",
+                     "traffic": traffic,
+                     "kernel": ("mirror_forward_kernel<sum, prune> (destination-grouped sweep + fused prune)"
+                                if step.use_mirror else "forward_vec4_kernel<sum, prune> (canonical sweep + prune)"),
+                     "bytes_per_entry": per_entry, "entries_per_launch": swept_entries,
                      "kernel_ms": fwd_avg_s * 1e3, "alg_bytes_per_launch": alg_bytes, "peak_kind": peak_kind,
                      "share_of_step": (fwd_avg_s * 1e3) / ms_per_step},
         "clocks": clk,
@@ -382,9 +389,10 @@ def count_launches(step, state, x, dev) -> int:
 
     from plastax_b200 import StepInputs
 
-    names = ("forward_", "backward_", "unit_apply", "prune_kernel", "fill_f32", "propose_", "pair_key",
-             "score_key", "winner_level", "gather_winners", "tile_count", "level_totals", "cand_key", "level_runs",
-             "spill_flag", "need_kernel", "list_fill", "place_kernel", "finish_kernel", "growable_flag",
+    names = ("forward_", "backward_", "unit_apply", "prune_kernel", "fill_f32", "propose_", "pair_key", "mirror_",
+             "tile_count", "list_fill", "bitmap_build",
+             "score_key", "winner_level", "gather_winners", "level_totals", "cand_key", "level_runs",
+             "spill_flag", "need_kernel", "place_kernel", "finish_kernel", "growable_flag",
              "mse_loss", "batched_", "DeviceRadixSort", "DeviceScan", "set_i32")
     try:
         with profile(activities=[ProfilerActivity.CUDA]) as prof:

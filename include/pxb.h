@@ -120,23 +120,30 @@ PXB_API int pxb_forward_accumulate(int64_t cap, const int32_t *from_id,
  *   accumulate as pxb_forward_accumulate over the PRE-prune dead mask;
  *   dead_out[s] = dead[s] | pred(s)   (dead_out may alias dead);
  *   block_free[b] = #dead_out slots in [b*block_len, (b+1)*block_len).
- * block_free may be NULL; block_len must be a power of two >= 256 when
- * given. Replaces src/plastax/phases.py:2240-2319 (triton_forward_prune)
- * and :2595 (free_block_counts). */
+ * block_free may be NULL; block_len must be a power of two >= 128 when
+ * given. free_bitmap (may be NULL): each slot pruned here sets its bit in
+ * the domain row of pxb_free_bitmap_build (row level[from_id] when
+ * bitmap_level is given, the PIPELINE domains; row 0 when it is NULL, the
+ * TOPOLOGICAL claim). Replaces src/plastax/phases.py:2240-2319
+ * (triton_forward_prune) and :2595 (free_block_counts). */
 PXB_API int pxb_forward_prune(int64_t cap, const int32_t *from_id,
                       const int32_t *to_id, const uint8_t *dead,
                       const float *weight, const float *act,
                       int32_t num_units, int32_t monoid, float *acc,
                       int32_t prune_kind, float prune_threshold,
                       const float *unit_threshold, uint8_t *dead_out,
-                      int32_t block_len, int32_t *block_free, void *stream);
+                      int32_t block_len, int32_t *block_free,
+                      uint32_t *free_bitmap, const int32_t *bitmap_level,
+                      void *stream);
 
 /* Prune sweep on its own: dead_out = dead | pred, plus block counts.
  * Replaces src/plastax/phases.py:1444-1498 (build_prune_conn_phase). */
-PXB_API int pxb_prune_conn(int64_t cap, const int32_t *to_id, const uint8_t *dead,
-                   const float *weight, int32_t num_units, int32_t prune_kind,
-                   float prune_threshold, const float *unit_threshold,
-                   uint8_t *dead_out, int32_t block_len, int32_t *block_free,
+PXB_API int pxb_prune_conn(int64_t cap, const int32_t *from_id, const int32_t *to_id,
+                   const uint8_t *dead, const float *weight, int32_t num_units,
+                   int32_t prune_kind, float prune_threshold,
+                   const float *unit_threshold, uint8_t *dead_out,
+                   int32_t block_len, int32_t *block_free,
+                   uint32_t *free_bitmap, const int32_t *bitmap_level,
                    void *stream);
 
 /* Backward accumulate of one bucket: acc[from[s]] (+)= w[s] * grad[to[s]].
@@ -297,12 +304,16 @@ PXB_API int pxb_claim_scratch_bytes(int64_t cap, int64_t k, int32_t num_levels,
  * slot at global position shard_base + s < *tail_start belongs to domain
  * unit_level[from_id[s]]; TOPOLOGICAL: every dead slot, one domain.
  * Writes level_counts[num_levels] (device) for the Scheme-A all-gather and
- * keeps the per-tile counts in `scratch` for step 2. */
+ * keeps the per-tile counts in `scratch` for step 2. With `free_bitmap`
+ * (the per-domain bitmaps of pxb_free_bitmap_build, kept current by the
+ * prune sweeps and the claim) the counts come from the bitmaps and neither
+ * from_id nor dead is read. */
 PXB_API int pxb_claim_prepare(int32_t mode, int64_t cap, const int32_t *from_id,
                       const uint8_t *dead, const int32_t *unit_level,
                       int32_t num_units, int32_t num_levels,
                       int64_t shard_base, const int64_t *tail_start,
-                      int64_t k, int32_t *level_counts, void *scratch,
+                      const uint32_t *free_bitmap, int64_t k,
+                      int32_t *level_counts, void *scratch,
                       size_t scratch_bytes, void *stream);
 
 /* Claim, step 2: the k candidates in claim order (levels ascending, total
@@ -318,7 +329,10 @@ PXB_API int pxb_claim_prepare(int32_t mode, int64_t cap, const int32_t *from_id,
  * level[dst] <= level[src]} and overflowed_out[k] (either may be NULL).
  * level_before / level_totals: Scheme-A per-domain counts of the ranks
  * before this one and of all ranks (device; NULL on one GPU). `scratch`
- * must hold step 1's results. */
+ * must hold step 1's results. With `free_bitmap` (as in step 1) the claimed
+ * own-domain slots are found in and cleared from the bitmaps.
+ * placed_out[k] (may be NULL): the local slot each candidate was written
+ * to on this rank, -1 when none. */
 PXB_API int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id,
                      int32_t *to_id, uint8_t *dead, float *weight,
                      const int32_t *unit_level, int32_t num_units,
@@ -327,15 +341,91 @@ PXB_API int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id,
                      const int32_t *cand_src, const int32_t *cand_dst,
                      const float *cand_weight, const uint8_t *growable,
                      int64_t max_new, const int32_t *level_before,
-                     const int32_t *level_totals, int32_t n_extra,
-                     void *const *extra_cols, const int32_t *extra_bytes,
-                     const void *const *extra_vals, int32_t *counts_out,
-                     uint8_t *overflowed_out, void *scratch,
-                     size_t scratch_bytes, void *stream);
+                     const int32_t *level_totals, uint32_t *free_bitmap,
+                     int32_t n_extra, void *const *extra_cols,
+                     const int32_t *extra_bytes, const void *const *extra_vals,
+                     int32_t *counts_out, uint8_t *overflowed_out,
+                     int32_t *placed_out, void *scratch, size_t scratch_bytes,
+                     void *stream);
+
+/* Per-domain free-slot bitmaps of a bucket: num_levels rows of
+ * ceil(cap / 32) words; bit s of row d is set iff slot s is a claimable free
+ * slot of domain d (PIPELINE: dead, below *tail_start, d = level[from_id];
+ * TOPOLOGICAL: dead, d = 0). */
+PXB_API int pxb_free_bitmap_build(int32_t mode, int64_t cap, const int32_t *from_id,
+                          const uint8_t *dead, const int32_t *unit_level,
+                          int32_t num_units, int32_t num_levels,
+                          int64_t shard_base, const int64_t *tail_start,
+                          uint32_t *bitmap, void *stream);
 
 /* Count the dead slots of a bucket into out[0] (device). */
 PXB_API int pxb_count_dead(int64_t cap, const uint8_t *dead, int32_t *out,
                    void *stream);
+
+/* ------------------------------------------------------------------ */
+/* destination-grouped mirror (the forward sweep's index)              */
+/* ------------------------------------------------------------------ */
+/* A bucket's live edges grouped by destination chunk (2^chunk_bits
+ * consecutive units, chunk_bits <= 13, ceil(log2 num_units) + chunk_bits
+ * <= 32). Group g owns entries [gbase[g], gbase[g+1]) (multiples of 4), of
+ * which the first gfill[g] have ever been used. Entry e: word[e] = src <<
+ * chunk_bits | (dst - g * 2^chunk_bits), or 0xffffffff when empty;
+ * weight[e]; slot[e] = the canonical (local) slot it mirrors. hstack at
+ * gbase[g] holds hcount[g] free entry offsets of group g. The forward
+ * sweeps `items` runs [item_begin, item_end) of group item_group. Edges a
+ * full group cannot take go to the overflow list (ovf_*); status[0] bit 0
+ * is set when that list is full too (the mirror must be rebuilt). All
+ * arrays are device memory owned by the caller. */
+typedef struct pxb_mirror {
+  int32_t num_units;
+  int32_t chunk_bits;
+  int64_t groups;
+  int64_t entries;
+  const int64_t *gbase;
+  int32_t *gfill;
+  uint32_t *word;
+  float *weight;
+  int32_t *slot;
+  int32_t *hstack;
+  int32_t *hcount;
+  int64_t items;
+  const int64_t *item_begin;
+  const int64_t *item_end;
+  const int32_t *item_group;
+  int64_t ovf_cap;
+  int32_t *ovf_count;
+  int32_t *ovf_src;
+  int32_t *ovf_dst;
+  int32_t *ovf_slot;
+  float *ovf_weight;
+  int32_t *status;
+} pxb_mirror;
+
+/* Forward accumulate of the mirrored bucket (acc (+)= w * act[src] per
+ * destination; the same result as pxb_forward_accumulate up to float
+ * summation order) fused with the prune predicate: a pruned edge still
+ * contributes (the forward reads the pre-prune state), then its mirror entry
+ * is emptied and pushed on its group's hole stack, and the canonical record
+ * is written: dead[slot] = 1, its free-bitmap bit (row bitmap_level[src],
+ * or row 0 when bitmap_level is NULL), pruned_count += 1 (may be NULL).
+ * Replaces src/plastax/phases.py:2240-2319 and sweep.py:113-180 for a
+ * bucket that has a mirror. acc must be 16-byte aligned for sum. */
+PXB_API int pxb_mirror_forward(const pxb_mirror *mirror, const float *act,
+                               int32_t monoid, float *acc, int32_t prune_kind,
+                               float prune_threshold,
+                               const float *unit_threshold, uint8_t *dead,
+                               uint32_t *free_bitmap, int64_t bitmap_words,
+                               const int32_t *bitmap_level,
+                               int32_t *pruned_count, void *stream);
+
+/* Insert the claim's placed edges into the mirror: candidate i with
+ * placed[i] >= 0 (pxb_claim_commit's placed_out) goes to a hole of its
+ * destination's group, else the group's unused slack, else the overflow
+ * list. */
+PXB_API int pxb_mirror_insert(const pxb_mirror *mirror, int64_t k,
+                              const int32_t *src, const int32_t *dst,
+                              const float *weight, const int32_t *placed,
+                              void *stream);
 
 #ifdef __cplusplus
 }

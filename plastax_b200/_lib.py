@@ -35,6 +35,18 @@ INIT_CONST, INIT_DYADIC, INIT_HASH_UNIFORM = 0, 1, 2
 CLAIM_PIPELINE, CLAIM_TOPOLOGICAL = 0, 1
 
 
+class Mirror(ctypes.Structure):
+    """`pxb_mirror`: the destination-grouped index of one bucket."""
+
+    _fields_ = [
+        ("num_units", c_i32), ("chunk_bits", c_i32), ("groups", c_i64), ("entries", c_i64),
+        ("gbase", c_ptr), ("gfill", c_ptr), ("word", c_ptr), ("weight", c_ptr), ("slot", c_ptr),
+        ("hstack", c_ptr), ("hcount", c_ptr), ("items", c_i64), ("item_begin", c_ptr), ("item_end", c_ptr),
+        ("item_group", c_ptr), ("ovf_cap", c_i64), ("ovf_count", c_ptr), ("ovf_src", c_ptr), ("ovf_dst", c_ptr),
+        ("ovf_slot", c_ptr), ("ovf_weight", c_ptr), ("status", c_ptr),
+    ]
+
+
 class PxbError(RuntimeError):
     """A libpxb entry point returned a non-zero status."""
 
@@ -64,9 +76,10 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_forward_prune": (
         c_i32,
         [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_ptr, c_i32, c_f32, c_ptr, c_ptr, c_i32, c_ptr,
-         c_ptr],
+         c_ptr, c_ptr, c_ptr],
     ),
-    "pxb_prune_conn": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_f32, c_ptr, c_ptr, c_i32, c_ptr, c_ptr]),
+    "pxb_prune_conn": (
+        c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_f32, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_backward_accumulate": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_ptr, c_ptr]),
     "pxb_backward_update": (
         c_i32,
@@ -103,13 +116,18 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_claim_scratch_bytes": (c_i32, [c_i64, c_i64, c_i32, ctypes.POINTER(c_size)]),
     "pxb_claim_prepare": (
         c_i32,
-        [c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i64, c_ptr, c_i64, c_ptr, c_ptr, c_size, c_ptr],
+        [c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_size, c_ptr],
     ),
     "pxb_claim_commit": (
         c_i32,
         [c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i64, c_i64, c_ptr, c_i64, c_ptr, c_ptr,
-         c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_size, c_ptr],
+         c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_size,
+         c_ptr],
     ),
+    "pxb_free_bitmap_build": (c_i32, [c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i64, c_ptr, c_ptr, c_ptr]),
+    "pxb_mirror_forward": (
+        c_i32, [c_ptr, c_ptr, c_i32, c_ptr, c_i32, c_f32, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr]),
+    "pxb_mirror_insert": (c_i32, [c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_count_dead": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr]),
 }
 

@@ -119,6 +119,8 @@ struct DomainArgs {
   int32_t num_units, num_levels;
   int64_t shard_base;
   const int64_t *tail_start;  // device scalar (global position)
+  const uint32_t *bm;         // per-domain free bitmaps [num_levels][bm_words], or NULL
+  int64_t bm_words;
 };
 
 // Domain of slot s, or -1 when it is not a claimable free slot.
@@ -159,6 +161,25 @@ __global__ void __launch_bounds__(kClaimWarps * 32) tile_count_kernel(DomainArgs
     __syncwarp();
     for (int l = lane; l < g.num_levels; l += 32) tile_counts[static_cast<int64_t>(l) * g.tiles + t] = cnt[wib][l];
     __syncwarp();
+  }
+}
+
+// prepare from the per-domain bitmaps: a tile of 2^tile_shift slots is
+// 2^(tile_shift-5) words; one warp per (tile, domain) pops its words.
+__global__ void __launch_bounds__(kClaimWarps * 32) tile_count_bm_kernel(DomainArgs a, ClaimGeom g,
+                                                                         int32_t *__restrict__ tile_counts) {
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * kClaimWarps;
+  const int64_t words_per_tile = int64_t(1) << (g.tile_shift - 5);
+  const int64_t jobs = g.tiles * g.num_levels;
+  for (int64_t j = static_cast<int64_t>(blockIdx.x) * kClaimWarps + wib; j < jobs; j += warps) {
+    const int64_t l = j / g.tiles, t = j - l * g.tiles;
+    const uint32_t *row = a.bm + l * a.bm_words;
+    int c = 0;
+    for (int64_t w = t * words_per_tile + lane; w < (t + 1) * words_per_tile && w < a.bm_words; w += 32)
+      c += __popc(row[w]);
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (lane == 0) tile_counts[j] = c;
   }
 }
 
@@ -307,6 +328,44 @@ __global__ void __launch_bounds__(kClaimWarps * 32) list_fill_kernel(
   }
 }
 
+// list fill from the bitmaps: one warp per (tile, domain) that still owes
+// needed ranks; each lane owns consecutive words, a warp scan of their
+// popcounts gives each set bit its rank in slot order.
+__global__ void __launch_bounds__(kClaimWarps * 32) list_fill_bm_kernel(
+    DomainArgs a, ClaimGeom g, const int32_t *__restrict__ tile_offsets, const int32_t *__restrict__ level_base,
+    const int32_t *__restrict__ need, const int32_t *__restrict__ need_off, int32_t *__restrict__ list) {
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * kClaimWarps;
+  const int64_t words_per_tile = int64_t(1) << (g.tile_shift - 5);
+  const int64_t jobs = g.tiles * g.num_levels;
+  for (int64_t j = static_cast<int64_t>(blockIdx.x) * kClaimWarps + wib; j < jobs; j += warps) {
+    const int64_t l = j / g.tiles, t = j - l * g.tiles;
+    int32_t run = tile_offsets[j] - level_base[l];
+    const int32_t nl = need[l];
+    if (run >= nl) continue;
+    const uint32_t *row = a.bm + l * a.bm_words;
+    for (int64_t w0 = t * words_per_tile; w0 < (t + 1) * words_per_tile && w0 < a.bm_words && run < nl; w0 += 32) {
+      const int64_t w = w0 + lane;
+      uint32_t bits = (w < (t + 1) * words_per_tile && w < a.bm_words) ? row[w] : 0u;
+      const int pc = __popc(bits);
+      int incl = pc;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      int r = run + incl - pc;
+      while (bits && r < nl) {
+        const int b = __ffs(bits) - 1;
+        bits &= bits - 1;
+        list[need_off[l] + r] = static_cast<int32_t>(w * 32 + b);
+        ++r;
+      }
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+  }
+}
+
 struct WriteArgs {
   int topo;
   int64_t cap, shard_base, global_cap;
@@ -318,6 +377,9 @@ struct WriteArgs {
   void *extra_cols[8];
   int32_t extra_bytes[8];
   const void *extra_vals[8];
+  uint32_t *bm;  // per-domain free bitmaps to clear at placed own slots, or NULL
+  int64_t bm_words;
+  int32_t *placed;  // per candidate: the local slot written, -1 when none
 };
 
 // One thread per sorted claim position: choose the slot and write.
@@ -334,6 +396,7 @@ __global__ void place_kernel(CandArgs c, WriteArgs w, const uint32_t *__restrict
     const uint32_t l = key[p];
     const int32_t i = idx[p];
     if (overflowed) overflowed[i] = 0;
+    if (w.placed) w.placed[i] = -1;
     if (l >= static_cast<uint32_t>(c.num_levels)) continue;
     const int32_t own_rank = static_cast<int32_t>(p) - first[l];
     int64_t slot = -1;
@@ -373,6 +436,9 @@ __global__ void place_kernel(CandArgs c, WriteArgs w, const uint32_t *__restrict
           reinterpret_cast<uint8_t *>(w.extra_cols[e])[slot] = reinterpret_cast<const uint8_t *>(w.extra_vals[e])[i];
       }
       w.dead[slot] = 0;
+      if (w.bm != nullptr && !to_tail)
+        atomicAnd(w.bm + static_cast<int64_t>(l) * w.bm_words + (slot >> 5), ~(1u << (slot & 31)));
+      if (w.placed) w.placed[i] = static_cast<int32_t>(slot);
     }
   }
 }
@@ -415,16 +481,17 @@ static int claim_common_checks(const char *fn, int32_t mode, int64_t cap, int32_
 
 extern "C" int pxb_claim_prepare(int32_t mode, int64_t cap, const int32_t *from_id, const uint8_t *dead,
                                  const int32_t *unit_level, int32_t num_units, int32_t num_levels,
-                                 int64_t shard_base, const int64_t *tail_start, int64_t k, int32_t *level_counts,
-                                 void *scratch, size_t scratch_bytes, void *stream) {
+                                 int64_t shard_base, const int64_t *tail_start, const uint32_t *free_bitmap,
+                                 int64_t k, int32_t *level_counts, void *scratch, size_t scratch_bytes,
+                                 void *stream) {
   int rc = claim_common_checks("pxb_claim_prepare", mode, cap, num_levels);
   if (rc) return rc;
   const int topo = mode == PXB_CLAIM_TOPOLOGICAL;
   if (topo) num_levels = 1;
   PXB_REQUIRE(scratch != nullptr, "pxb_claim_prepare: scratch is NULL");
-  PXB_REQUIRE(topo || (from_id && unit_level && tail_start && num_units > 0),
+  PXB_REQUIRE(free_bitmap || topo || (from_id && unit_level && tail_start && num_units > 0),
               "pxb_claim_prepare: pipeline mode needs from_id, unit_level, num_units and tail_start");
-  PXB_REQUIRE(cap == 0 || dead, "pxb_claim_prepare: dead is NULL");
+  PXB_REQUIRE(free_bitmap || cap == 0 || dead, "pxb_claim_prepare: dead is NULL");
   const ClaimGeom g = geom_of(cap, num_levels);
   ClaimScratch o;
   if (claim_scratch(g, k, static_cast<char *>(scratch), &o) != PXB_OK) {
@@ -437,10 +504,15 @@ extern "C" int pxb_claim_prepare(int32_t mode, int64_t cap, const int32_t *from_
   const int64_t m = g.tiles * g.num_levels;
   PXB_CUDA(cudaMemsetAsync(o.tile_counts, 0, m * 4, st));
   if (cap > 0) {
-    DomainArgs a{topo, cap, from_id, dead, unit_level, num_units, num_levels, shard_base, tail_start};
-    const int grid = grid_for(g.tiles, kClaimWarps, 4);
-    tile_count_kernel<<<grid, kClaimWarps * 32, 0, st>>>(a, g, o.tile_counts);
-    PXB_LAUNCHED("tile_count_kernel");
+    DomainArgs a{topo, cap, from_id, dead, unit_level, num_units, num_levels, shard_base, tail_start,
+                 free_bitmap, (cap + 31) / 32};
+    if (free_bitmap != nullptr) {
+      tile_count_bm_kernel<<<grid_for(m, kClaimWarps, 4), kClaimWarps * 32, 0, st>>>(a, g, o.tile_counts);
+      PXB_LAUNCHED("tile_count_bm_kernel");
+    } else {
+      tile_count_kernel<<<grid_for(g.tiles, kClaimWarps, 4), kClaimWarps * 32, 0, st>>>(a, g, o.tile_counts);
+      PXB_LAUNCHED("tile_count_kernel");
+    }
   }
   size_t tb = o.cub_bytes;
   PXB_CUDA(cub::DeviceScan::ExclusiveSum(o.cub_tmp, tb, o.tile_counts, o.tile_offsets, static_cast<int>(m), st));
@@ -455,9 +527,10 @@ extern "C" int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id, int
                                 int64_t shard_base, int64_t global_cap, int64_t *tail_start, int64_t k,
                                 const int32_t *cand_src, const int32_t *cand_dst, const float *cand_weight,
                                 const uint8_t *growable, int64_t max_new, const int32_t *level_before,
-                                const int32_t *level_totals, int32_t n_extra, void *const *extra_cols,
-                                const int32_t *extra_bytes, const void *const *extra_vals, int32_t *counts_out,
-                                uint8_t *overflowed_out, void *scratch, size_t scratch_bytes, void *stream) {
+                                const int32_t *level_totals, uint32_t *free_bitmap, int32_t n_extra,
+                                void *const *extra_cols, const int32_t *extra_bytes, const void *const *extra_vals,
+                                int32_t *counts_out, uint8_t *overflowed_out, int32_t *placed_out, void *scratch,
+                                size_t scratch_bytes, void *stream) {
   int rc = claim_common_checks("pxb_claim_commit", mode, cap, num_levels);
   if (rc) return rc;
   const int topo = mode == PXB_CLAIM_TOPOLOGICAL;
@@ -489,6 +562,9 @@ extern "C" int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id, int
   w.dead = dead;
   w.weight = weight;
   w.n_extra = n_extra;
+  w.bm = free_bitmap;
+  w.bm_words = (cap + 31) / 32;
+  w.placed = placed_out;
   for (int e = 0; e < n_extra; ++e) {
     PXB_REQUIRE(extra_cols && extra_bytes && extra_vals && extra_cols[e] && extra_vals[e],
                 "pxb_claim_commit: extra column %d is NULL", e);
@@ -531,10 +607,17 @@ extern "C" int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id, int
     need_kernel<<<1, 1, 0, st>>>(num_levels, o.level_first, o.level_end, t, o.need, o.need_off);
     PXB_LAUNCHED("need_kernel");
     if (cap > 0) {
-      DomainArgs a{topo, cap, from_id, dead, unit_level, num_units, num_levels, shard_base, tail_start};
-      list_fill_kernel<<<grid_for(g.tiles, kClaimWarps, 4), kClaimWarps * 32, 0, st>>>(
-          a, g, o.tile_offsets, o.level_base, o.need, o.need_off, o.list);
-      PXB_LAUNCHED("list_fill_kernel");
+      DomainArgs a{topo, cap, from_id, dead, unit_level, num_units, num_levels, shard_base, tail_start,
+                   free_bitmap, (cap + 31) / 32};
+      if (free_bitmap != nullptr) {
+        list_fill_bm_kernel<<<grid_for(g.tiles * g.num_levels, kClaimWarps, 4), kClaimWarps * 32, 0, st>>>(
+            a, g, o.tile_offsets, o.level_base, o.need, o.need_off, o.list);
+        PXB_LAUNCHED("list_fill_bm_kernel");
+      } else {
+        list_fill_kernel<<<grid_for(g.tiles, kClaimWarps, 4), kClaimWarps * 32, 0, st>>>(
+            a, g, o.tile_offsets, o.level_base, o.need, o.need_off, o.list);
+        PXB_LAUNCHED("list_fill_kernel");
+      }
     }
     place_kernel<<<grid, 256, 0, st>>>(c, w, o.ckey_out, o.cidx_out, o.level_first, t, o.rank, o.need, o.need_off,
                                        o.list, cand_weight, o.counts, overflowed_out);
@@ -562,5 +645,38 @@ extern "C" int pxb_count_dead(int64_t cap, const uint8_t *dead, int32_t *out, vo
   PXB_REQUIRE(dead, "pxb_count_dead: dead is NULL");
   count_dead_kernel<<<grid_for(cap, 256, 8), 256, 0, st>>>(cap, dead, out);
   PXB_LAUNCHED("count_dead_kernel");
+  return PXB_OK;
+}
+
+// Per-domain free bitmaps of a bucket (bit s of domain d set iff slot s is a
+// claimable free slot of domain d, as slot_domain() defines it).
+__global__ void bitmap_build_kernel(DomainArgs a, uint32_t *__restrict__ bm) {
+  const int64_t tail = a.topo ? 0 : *a.tail_start;
+  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < a.cap;
+       s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t d = slot_domain(a, s, tail);
+    if (d >= 0) atomicOr(bm + static_cast<int64_t>(d) * a.bm_words + (s >> 5), 1u << (s & 31));
+  }
+}
+
+extern "C" int pxb_free_bitmap_build(int32_t mode, int64_t cap, const int32_t *from_id, const uint8_t *dead,
+                                     const int32_t *unit_level, int32_t num_units, int32_t num_levels,
+                                     int64_t shard_base, const int64_t *tail_start, uint32_t *bitmap,
+                                     void *stream) {
+  int rc = claim_common_checks("pxb_free_bitmap_build", mode, cap, num_levels);
+  if (rc) return rc;
+  const int topo = mode == PXB_CLAIM_TOPOLOGICAL;
+  if (topo) num_levels = 1;
+  PXB_REQUIRE(bitmap != nullptr, "pxb_free_bitmap_build: bitmap is NULL");
+  PXB_REQUIRE(topo || (from_id && unit_level && tail_start && num_units > 0),
+              "pxb_free_bitmap_build: pipeline mode needs from_id, unit_level, num_units and tail_start");
+  const int64_t words = (cap + 31) / 32;
+  cudaStream_t st = as_stream(stream);
+  PXB_CUDA(cudaMemsetAsync(bitmap, 0, static_cast<size_t>(words) * num_levels * 4, st));
+  if (cap == 0) return PXB_OK;
+  PXB_REQUIRE(dead != nullptr, "pxb_free_bitmap_build: dead is NULL");
+  DomainArgs a{topo, cap, from_id, dead, unit_level, num_units, num_levels, shard_base, tail_start, bitmap, words};
+  bitmap_build_kernel<<<grid_for(cap, 256, 8), 256, 0, st>>>(a, bitmap);
+  PXB_LAUNCHED("bitmap_build_kernel");
   return PXB_OK;
 }

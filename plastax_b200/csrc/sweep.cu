@@ -72,7 +72,21 @@ struct PruneArgs {
   bool in_place;       // dead_out == dead: write only the bytes that change
   int block_shift;     // log2(block_len), -1 when no counts
   int32_t *block_free;
+  uint32_t *bm;        // per-domain free bitmaps, or NULL
+  int64_t bm_words;
+  const int32_t *bm_level;  // domain of a freed slot = bm_level[from_id]; NULL: domain 0
 };
+
+// A slot this sweep tombstoned joins its claim domain's free bitmap.
+__device__ __forceinline__ void mark_free(const PruneArgs &pa, int64_t s, int32_t from, uint32_t n) {
+  if (pa.bm == nullptr) return;
+  int64_t row = 0;
+  if (pa.bm_level != nullptr) {
+    const int32_t o = from < 0 ? 0 : (static_cast<uint32_t>(from) >= n ? static_cast<int32_t>(n) - 1 : from);
+    row = pa.bm_level[o];
+  }
+  atomicOr(pa.bm + row * pa.bm_words + (s >> 5), 1u << (s & 31));
+}
 
 __device__ __forceinline__ bool prune_pred(const PruneArgs &pa, float w, int32_t to, uint32_t n) {
   if (pa.kind == PXB_PRUNE_ABS_BELOW) return fabsf(w) < pa.threshold;
@@ -120,7 +134,10 @@ __global__ void __launch_bounds__(256) forward_vec4_kernel(
       uint32_t nd = d;
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        if (prune_pred(pa, ws[i], ts[i], n)) nd |= (1u << (8 * i));
+        if (prune_pred(pa, ws[i], ts[i], n)) {
+          nd |= (1u << (8 * i));
+          if (!((d >> (8 * i)) & 0xffu)) mark_free(pa, g * 4 + i, fs[i], n);
+        }
       if (!pa.in_place || nd != d) reinterpret_cast<uint32_t *>(pa.dead_out)[g] = nd;
       if (pa.block_shift >= 0) count_free(pa, g * 4, __popc(nd & 0x01010101u));
     }
@@ -142,6 +159,7 @@ __global__ void __launch_bounds__(256) forward_scalar_kernel(
       atomic_combine<MONOID>(acc + ts, __fmul_rn(ws, __ldg(act + fs)));
     if (PRUNE) {
       const uint8_t nd = d | (prune_pred(pa, ws, ts, n) ? 1 : 0);
+      if (nd && !d) mark_free(pa, s, fs, n);
       if (!pa.in_place || nd != d) pa.dead_out[s] = nd;
       if (pa.block_shift >= 0) count_free(pa, s, nd ? 1 : 0);
     }
@@ -149,7 +167,8 @@ __global__ void __launch_bounds__(256) forward_scalar_kernel(
 }
 
 // Prune sweep without the forward: reads w (+ to for a per-dst threshold).
-__global__ void __launch_bounds__(256) prune_kernel(int64_t cap, const int32_t *__restrict__ to,
+__global__ void __launch_bounds__(256) prune_kernel(int64_t cap, const int32_t *__restrict__ from,
+                                                    const int32_t *__restrict__ to,
                                                     const uint8_t *__restrict__ dead,
                                                     const float *__restrict__ w, uint32_t n, PruneArgs pa) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -157,6 +176,7 @@ __global__ void __launch_bounds__(256) prune_kernel(int64_t cap, const int32_t *
     const uint8_t d = dead[s];
     const int32_t ts = pa.kind == PXB_PRUNE_ABS_BELOW_DST ? to[s] : 0;
     const uint8_t nd = d | (prune_pred(pa, w[s], ts, n) ? 1 : 0);
+    if (nd && !d) mark_free(pa, s, pa.bm_level ? from[s] : 0, n);
     if (!pa.in_place || nd != d) pa.dead_out[s] = nd;
     if (pa.block_shift >= 0) count_free(pa, s, nd ? 1 : 0);
   }
@@ -356,7 +376,7 @@ extern "C" int pxb_forward_accumulate(int64_t cap, const int32_t *from_id, const
   PXB_REQUIRE(num_units >= 0, "pxb_forward_accumulate: negative num_units");
   if (cap == 0) return PXB_OK;
   PXB_REQUIRE(act && acc, "pxb_forward_accumulate: act/acc is NULL");
-  PruneArgs pa{PXB_PRUNE_NONE, 0.0f, nullptr, nullptr, false, -1, nullptr};
+  PruneArgs pa{PXB_PRUNE_NONE, 0.0f, nullptr, nullptr, false, -1, nullptr, nullptr, 0, nullptr};
   return launch_forward<false>(cap, from_id, to_id, dead, weight, act, num_units, monoid, acc, pa,
                                as_stream(stream));
 }
@@ -365,7 +385,8 @@ extern "C" int pxb_forward_prune(int64_t cap, const int32_t *from_id, const int3
                                  const uint8_t *dead, const float *weight, const float *act,
                                  int32_t num_units, int32_t monoid, float *acc, int32_t prune_kind,
                                  float prune_threshold, const float *unit_threshold, uint8_t *dead_out,
-                                 int32_t block_len, int32_t *block_free, void *stream) {
+                                 int32_t block_len, int32_t *block_free, uint32_t *free_bitmap,
+                                 const int32_t *bitmap_level, void *stream) {
   int rc = check_bucket("pxb_forward_prune", cap, from_id, to_id, dead, weight);
   if (rc) return rc;
   PXB_REQUIRE(monoid >= 0 && monoid <= 2, "pxb_forward_prune: unknown monoid %d", monoid);
@@ -381,14 +402,16 @@ extern "C" int pxb_forward_prune(int64_t cap, const int32_t *from_id, const int3
   if (rc) return rc;
   if (cap == 0) return PXB_OK;
   PXB_REQUIRE(act && acc && dead_out, "pxb_forward_prune: act/acc/dead_out is NULL");
-  PruneArgs pa{prune_kind, prune_threshold, unit_threshold, dead_out, dead_out == dead, shift, block_free};
+  PruneArgs pa{prune_kind, prune_threshold, unit_threshold, dead_out, dead_out == dead, shift, block_free,
+               free_bitmap, (cap + 31) / 32, bitmap_level};
   return launch_forward<true>(cap, from_id, to_id, dead, weight, act, num_units, monoid, acc, pa, st);
 }
 
-extern "C" int pxb_prune_conn(int64_t cap, const int32_t *to_id, const uint8_t *dead, const float *weight,
-                              int32_t num_units, int32_t prune_kind, float prune_threshold,
+extern "C" int pxb_prune_conn(int64_t cap, const int32_t *from_id, const int32_t *to_id, const uint8_t *dead,
+                              const float *weight, int32_t num_units, int32_t prune_kind, float prune_threshold,
                               const float *unit_threshold, uint8_t *dead_out, int32_t block_len,
-                              int32_t *block_free, void *stream) {
+                              int32_t *block_free, uint32_t *free_bitmap, const int32_t *bitmap_level,
+                              void *stream) {
   PXB_REQUIRE(cap >= 0, "pxb_prune_conn: negative capacity");
   PXB_REQUIRE(num_units >= 0, "pxb_prune_conn: negative num_units");
   PXB_REQUIRE(prune_kind >= 0 && prune_kind <= 2, "pxb_prune_conn: unknown prune kind %d", prune_kind);
@@ -402,8 +425,10 @@ extern "C" int pxb_prune_conn(int64_t cap, const int32_t *to_id, const uint8_t *
   if (rc) return rc;
   if (cap == 0) return PXB_OK;
   PXB_REQUIRE(dead && weight && dead_out, "pxb_prune_conn: a column is NULL");
-  PruneArgs pa{prune_kind, prune_threshold, unit_threshold, dead_out, dead_out == dead, shift, block_free};
-  prune_kernel<<<grid_for(cap, 256, 8), 256, 0, st>>>(cap, to_id, dead, weight,
+  PXB_REQUIRE(!bitmap_level || from_id, "pxb_prune_conn: the bitmap domains need from_id");
+  PruneArgs pa{prune_kind, prune_threshold, unit_threshold, dead_out, dead_out == dead, shift, block_free,
+               free_bitmap, (cap + 31) / 32, bitmap_level};
+  prune_kernel<<<grid_for(cap, 256, 8), 256, 0, st>>>(cap, from_id, to_id, dead, weight,
                                                       static_cast<uint32_t>(num_units), pa);
   PXB_LAUNCHED("prune_kernel");
   return PXB_OK;

@@ -94,7 +94,8 @@ def forward_accumulate(b: Bucket, act: torch.Tensor, acc: torch.Tensor, monoid: 
 def forward_prune(b: Bucket, act: torch.Tensor, acc: torch.Tensor, *, monoid: str = "sum",
                   prune_kind: int = _lib.PRUNE_ABS_BELOW, threshold: float = 0.0,
                   unit_threshold: torch.Tensor | None = None, dead_out: torch.Tensor | None = None,
-                  block_len: int = 0, block_free: torch.Tensor | None = None) -> None:
+                  block_len: int = 0, block_free: torch.Tensor | None = None,
+                  free_bitmap: torch.Tensor | None = None, bitmap_level: torch.Tensor | None = None) -> None:
     """Forward accumulate + prune predicate + per-block free counts, one pass."""
     cap = _bucket(b)
     n = acc.numel()
@@ -107,16 +108,18 @@ def forward_prune(b: Bucket, act: torch.Tensor, acc: torch.Tensor, *, monoid: st
     call("pxb_forward_prune", ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]), ptr(b["dead"]),
          ptr(b["weight"]), ptr(act), ctypes.c_int32(n), _lib.MONOID[monoid], ptr(acc), ctypes.c_int32(prune_kind),
          ctypes.c_float(threshold), ptr(unit_threshold), ptr(out), ctypes.c_int32(block_len), ptr(block_free),
-         _stream())
+         ptr(free_bitmap), ptr(bitmap_level), _stream())
 
 
 def prune_conn(b: Bucket, num_units: int, *, prune_kind: int = _lib.PRUNE_ABS_BELOW, threshold: float = 0.0,
                unit_threshold: torch.Tensor | None = None, block_len: int = 0,
-               block_free: torch.Tensor | None = None) -> None:
+               block_free: torch.Tensor | None = None, free_bitmap: torch.Tensor | None = None,
+               bitmap_level: torch.Tensor | None = None) -> None:
     cap = _bucket(b)
-    call("pxb_prune_conn", ctypes.c_int64(cap), ptr(b["to_id"]), ptr(b["dead"]), ptr(b["weight"]),
-         ctypes.c_int32(num_units), ctypes.c_int32(prune_kind), ctypes.c_float(threshold), ptr(unit_threshold),
-         ptr(b["dead"]), ctypes.c_int32(block_len), ptr(block_free), _stream())
+    call("pxb_prune_conn", ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]), ptr(b["dead"]),
+         ptr(b["weight"]), ctypes.c_int32(num_units), ctypes.c_int32(prune_kind), ctypes.c_float(threshold),
+         ptr(unit_threshold), ptr(b["dead"]), ctypes.c_int32(block_len), ptr(block_free), ptr(free_bitmap),
+         ptr(bitmap_level), _stream())
 
 
 def backward_accumulate(b: Bucket, grad: torch.Tensor, acc: torch.Tensor, monoid: str = "sum") -> None:
@@ -289,12 +292,13 @@ class ClaimWorkspace:
 
 
 def claim_prepare(mode: int, b: Bucket, unit_level: torch.Tensor, tail_start: torch.Tensor | None,
-                  ws: ClaimWorkspace, *, shard_base: int = 0) -> torch.Tensor:
+                  ws: ClaimWorkspace, *, shard_base: int = 0, free_bitmap: torch.Tensor | None = None
+                  ) -> torch.Tensor:
     cap = _bucket(b)
     call("pxb_claim_prepare", ctypes.c_int32(mode), ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["dead"]),
          ptr(unit_level), ctypes.c_int32(unit_level.numel()), ctypes.c_int32(ws.num_levels),
-         ctypes.c_int64(shard_base), ptr(tail_start), ctypes.c_int64(ws.k), ptr(ws.level_counts), ptr(ws.scratch),
-         ctypes.c_size_t(ws.scratch.numel()), _stream())
+         ctypes.c_int64(shard_base), ptr(tail_start), ptr(free_bitmap), ctypes.c_int64(ws.k), ptr(ws.level_counts),
+         ptr(ws.scratch), ctypes.c_size_t(ws.scratch.numel()), _stream())
     return ws.level_counts
 
 
@@ -302,7 +306,8 @@ def claim_commit(mode: int, b: Bucket, unit_level: torch.Tensor, tail_start: tor
                  ws: ClaimWorkspace, src: torch.Tensor, dst: torch.Tensor, weight: torch.Tensor,
                  growable: torch.Tensor, *, max_new: int = -1, shard_base: int = 0, global_cap: int | None = None,
                  level_before: torch.Tensor | None = None, level_totals: torch.Tensor | None = None,
-                 extra: Mapping[str, torch.Tensor] | None = None) -> None:
+                 extra: Mapping[str, torch.Tensor] | None = None, free_bitmap: torch.Tensor | None = None,
+                 placed: torch.Tensor | None = None) -> None:
     cap = _bucket(b)
     k = src.numel()
     if k != ws.k:
@@ -317,12 +322,41 @@ def claim_commit(mode: int, b: Bucket, unit_level: torch.Tensor, tail_start: tor
          ctypes.c_int32(ws.num_levels), ctypes.c_int64(shard_base),
          ctypes.c_int64(cap + shard_base if global_cap is None else global_cap), ptr(tail_start), ctypes.c_int64(k),
          ptr(src), ptr(dst), ptr(weight), ptr(growable), ctypes.c_int64(max_new), ptr(level_before),
-         ptr(level_totals), ctypes.c_int32(n_extra), ctypes.cast(cols, ctypes.c_void_p) if n_extra else None,
+         ptr(level_totals), ptr(free_bitmap), ctypes.c_int32(n_extra),
+         ctypes.cast(cols, ctypes.c_void_p) if n_extra else None,
          ctypes.cast(nbytes, ctypes.c_void_p) if n_extra else None,
-         ctypes.cast(vals, ctypes.c_void_p) if n_extra else None, ptr(ws.counts), ptr(ws.overflowed), ptr(ws.scratch),
-         ctypes.c_size_t(ws.scratch.numel()), _stream())
+         ctypes.cast(vals, ctypes.c_void_p) if n_extra else None, ptr(ws.counts), ptr(ws.overflowed), ptr(placed),
+         ptr(ws.scratch), ctypes.c_size_t(ws.scratch.numel()), _stream())
 
 
 def count_dead(b: Bucket, out: torch.Tensor) -> None:
     cap = _bucket(b)
     call("pxb_count_dead", ctypes.c_int64(cap), ptr(b["dead"]), ptr(out), _stream())
+
+
+def free_bitmap_build(mode: int, b: Bucket, unit_level: torch.Tensor, tail_start: torch.Tensor | None,
+                      num_levels: int, *, shard_base: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-domain free-slot bitmaps of a bucket (int32 view of uint32 words)."""
+    cap = _bucket(b)
+    rows = 1 if mode == _lib.CLAIM_TOPOLOGICAL else num_levels
+    words = (cap + 31) // 32
+    if out is None:
+        out = torch.zeros(rows * max(words, 1), dtype=torch.int32, device=b["dead"].device)
+    call("pxb_free_bitmap_build", ctypes.c_int32(mode), ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["dead"]),
+         ptr(unit_level), ctypes.c_int32(unit_level.numel()), ctypes.c_int32(num_levels), ctypes.c_int64(shard_base),
+         ptr(tail_start), ptr(out), _stream())
+    return out
+
+
+def mirror_forward(m, act: torch.Tensor, acc: torch.Tensor, *, monoid: str = "sum", prune_kind: int = 0,
+                   threshold: float = 0.0, unit_threshold: torch.Tensor | None = None,
+                   dead: torch.Tensor | None = None, free_bitmap: torch.Tensor | None = None, bitmap_words: int = 0,
+                   bitmap_level: torch.Tensor | None = None, pruned_count: torch.Tensor | None = None) -> None:
+    call("pxb_mirror_forward", ctypes.byref(m.struct), ptr(act), ctypes.c_int32(_lib.MONOID[monoid]), ptr(acc),
+         ctypes.c_int32(prune_kind), ctypes.c_float(threshold), ptr(unit_threshold), ptr(dead), ptr(free_bitmap),
+         ctypes.c_int64(bitmap_words), ptr(bitmap_level), ptr(pruned_count), _stream())
+
+
+def mirror_insert(m, src: torch.Tensor, dst: torch.Tensor, weight: torch.Tensor, placed: torch.Tensor) -> None:
+    call("pxb_mirror_insert", ctypes.byref(m.struct), ctypes.c_int64(src.numel()), ptr(src), ptr(dst), ptr(weight),
+         ptr(placed), _stream())

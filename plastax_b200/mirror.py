@@ -1,0 +1,97 @@
+"""The destination-grouped mirror of a bucket (see csrc/mirror.cu).
+
+Built once from the canonical columns with device-side sorts (setup, not the
+step), then kept current by the fused prune and the claim's inserts. Live
+edges are grouped by destination chunk, in slot order within a group; each
+group gets `slack` spare entries (at least `min_slack`, a multiple of 4)
+for the edges growth will insert before the next rebuild.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from plastax_b200 import _lib
+
+
+class Mirror:
+    def __init__(self, bucket: dict[str, torch.Tensor], num_units: int, *, slack: float = 0.05,
+                 min_slack: int = 64, item_entries: int = 1 << 16, ovf_cap: int = 1 << 20) -> None:
+        dev = bucket["dead"].device
+        n = int(num_units)
+        src_bits = max(1, (n - 1).bit_length())
+        cb = min(32 - src_bits, 13)
+        if cb < 2:
+            raise ValueError(f"mirror: {n} units leave too few bits for a destination chunk")
+        chunk = 1 << cb
+        groups = (n + chunk - 1) // chunk
+        frm, to = bucket["from_id"], bucket["to_id"]
+        live = torch.nonzero(bucket["dead"] == 0).flatten()
+        f, t = frm[live].long(), to[live].long()
+        ok = (f >= 0) & (f < n) & (t >= 0) & (t < n)
+        live, f, t = live[ok], f[ok], t[ok]
+        g = t >> cb
+        order = torch.sort(g, stable=True).indices
+        live, f, t, g = live[order], f[order], t[order], g[order]
+        counts = torch.bincount(g, minlength=groups)
+        counts_h = counts.cpu().numpy().astype(np.int64)
+        spare = np.maximum(min_slack, np.ceil(counts_h * slack).astype(np.int64))
+        gcap = (counts_h + spare + 3) // 4 * 4
+        gbase = np.concatenate([[0], np.cumsum(gcap)]).astype(np.int64)
+        entries = int(gbase[-1])
+        starts = torch.from_numpy(np.concatenate([[0], np.cumsum(counts_h)[:-1]])).to(dev)
+        rank = torch.arange(live.numel(), device=dev) - starts[g]
+        pos = torch.from_numpy(gbase[:-1]).to(dev)[g] + rank
+        word = torch.full((entries,), -1, dtype=torch.int32, device=dev)
+        packed = (f << cb) | (t & (chunk - 1))
+        packed = packed - (packed >= 2**31).long() * 2**32
+        word[pos] = packed.to(torch.int32)
+        weight = torch.zeros(entries, dtype=torch.float32, device=dev)
+        weight[pos] = bucket["weight"][live]
+        slot = torch.full((entries,), -1, dtype=torch.int32, device=dev)
+        slot[pos] = live.to(torch.int32)
+        del packed, pos, rank, f, t, g, live, order
+        ib, ie, ig = [], [], []
+        for grp in range(groups):
+            lo, hi = int(gbase[grp]), int(gbase[grp + 1])
+            step = max(4, item_entries // 4 * 4)
+            for b in range(lo, hi, step):
+                ib.append(b)
+                ie.append(min(b + step, hi))
+                ig.append(grp)
+        self.chunk_bits, self.groups, self.entries, self.num_units = cb, groups, entries, n
+        self.gbase = torch.from_numpy(gbase).to(dev)
+        self.gfill = counts.to(torch.int32)
+        self.word, self.weight, self.slot = word, weight, slot
+        self.hstack = torch.zeros(max(entries, 4), dtype=torch.int32, device=dev)
+        self.hcount = torch.zeros(groups, dtype=torch.int32, device=dev)
+        self.item_begin = torch.tensor(ib, dtype=torch.int64, device=dev)
+        self.item_end = torch.tensor(ie, dtype=torch.int64, device=dev)
+        self.item_group = torch.tensor(ig, dtype=torch.int32, device=dev)
+        self.ovf_cap = int(ovf_cap)
+        self.ovf_count = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ovf_src = torch.full((max(ovf_cap, 1),), -1, dtype=torch.int32, device=dev)
+        self.ovf_dst = torch.zeros(max(ovf_cap, 1), dtype=torch.int32, device=dev)
+        self.ovf_slot = torch.zeros(max(ovf_cap, 1), dtype=torch.int32, device=dev)
+        self.ovf_weight = torch.zeros(max(ovf_cap, 1), dtype=torch.float32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        p = lambda x: x.data_ptr()  # noqa: E731
+        self.struct = _lib.Mirror(
+            n, cb, groups, entries, p(self.gbase), p(self.gfill), p(self.word), p(self.weight), p(self.slot),
+            p(self.hstack), p(self.hcount), len(ib), p(self.item_begin), p(self.item_end), p(self.item_group),
+            self.ovf_cap, p(self.ovf_count), p(self.ovf_src), p(self.ovf_dst), p(self.ovf_slot), p(self.ovf_weight),
+            p(self.status))
+
+    def healthy(self) -> bool:
+        """False when an edge could not be mirrored (host read; synchronises)."""
+        return int(self.status.item()) == 0
+
+    def bytes_per_sweep(self) -> int:
+        """Bytes the forward streams: word + weight of every used entry."""
+        return int(self.gfill.clamp(max=None).sum().item()) * 8
+
+
+__all__ = ["Mirror", "math"]

@@ -110,9 +110,47 @@ class StepFn:
                             and net.update_unit is None)
         self.opt = net.update_conn.struct() if net.update_conn is not None else None
         self.ac: ProposeAddConn | None = net.add_conn
+        # The forward reads a destination-grouped mirror of each bucket when
+        # no phase rewrites weights in place (the mirror holds its own copy)
+        # and any prune rides on the forward sweep.
+        self.use_mirror = net.update_conn is None and (net.prune_conn is None or self.fuse_prune)
+        self.mirrors: list | None = None
+        self.bitmaps: list[torch.Tensor] | None = None
+        self._bound: int | None = None
         if self.ac is not None:
             self._build_growth()
         self.launches = 0
+
+    # -- per-state device indices ---------------------------------------------
+    def _bind(self, state: NetworkState) -> None:
+        """Build the mirror and free-slot bitmaps of `state` (once per state
+        object; the step owns the state between calls, as with donation)."""
+        if self._bound == id(state):
+            return
+        from plastax_b200.mirror import Mirror
+
+        st = self.static
+        level = state.units[LEVEL.name]
+        if self.use_mirror:
+            self.mirrors = [Mirror(b, st.num_units) for b in state.conns]
+        if self.ac is not None:
+            mode = _lib.CLAIM_PIPELINE if self.pipeline else _lib.CLAIM_TOPOLOGICAL
+            self.bitmaps = [K.free_bitmap_build(mode, b, level, state.tail_start, self.num_levels,
+                                                shard_base=st.shard_base(i)) for i, b in enumerate(state.conns)]
+        self._bound = id(state)
+
+    def invalidate(self) -> None:
+        """Drop the per-state indices (call after editing a state's columns
+        outside the step); they are rebuilt on the next call."""
+        self._bound = None
+        self.mirrors = None
+        self.bitmaps = None
+
+    def _bm(self, bucket: int) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+        """(free bitmap, the level column naming its rows) of a bucket."""
+        if self.bitmaps is None:
+            return None, None
+        return self.bitmaps[bucket], None if not self.pipeline else self._level
 
     # -- growth buffers ------------------------------------------------------
     def _build_growth(self) -> None:
@@ -155,6 +193,7 @@ class StepFn:
         self.direction = {"any": 0, "deeper": 1, "same_or_deeper": 2}[ac.direction]
         self.grown = torch.zeros((), dtype=torch.int32, device=dev)
         self.overflow = torch.zeros((), dtype=torch.bool, device=dev)
+        self.placed = torch.empty(kk, dtype=torch.int32, device=dev)
         if self.sharded:
             G = st.num_shards
             self.gather_buf = torch.zeros((G, self.num_levels), dtype=torch.int32, device=dev)
@@ -172,6 +211,24 @@ class StepFn:
         x = x.to(self.dev, non_blocking=True).reshape(-1)
         state.units[ACTIVATION.name].index_copy_(0, self.input_ids, x)
 
+    def _accumulate_bucket(self, state: NetworkState, i: int, act: torch.Tensor) -> None:
+        """Forward accumulate of bucket i, with the prune fused when legal."""
+        net, b = self.net, state.conns[i]
+        bm, bm_level = self._bm(i)
+        if self.use_mirror:
+            m = self.mirrors[i]
+            if self.fuse_prune:
+                K.mirror_forward(m, act, self.acc, monoid=self.fwd_monoid, prune_kind=_lib.PRUNE_ABS_BELOW,
+                                 threshold=net.prune_conn.threshold, dead=b["dead"], free_bitmap=bm,
+                                 bitmap_words=(b["dead"].numel() + 31) // 32, bitmap_level=bm_level)
+            else:
+                K.mirror_forward(m, act, self.acc, monoid=self.fwd_monoid)
+        elif self.fuse_prune:
+            K.forward_prune(b, act, self.acc, monoid=self.fwd_monoid, prune_kind=_lib.PRUNE_ABS_BELOW,
+                            threshold=net.prune_conn.threshold, free_bitmap=bm, bitmap_level=bm_level)
+        else:
+            K.forward_accumulate(b, act, self.acc, self.fwd_monoid)
+
     def _forward(self, state: NetworkState) -> None:
         net, st, units = self.net, self.static, state.units
         act = units[ACTIVATION.name]
@@ -179,12 +236,7 @@ class StepFn:
         fp = net.forward_pass
         K.fill(self.acc, self.fwd_identity)
         if self.pipeline:
-            b = state.conns[0]
-            if self.fuse_prune:
-                K.forward_prune(b, act, self.acc, monoid=self.fwd_monoid, prune_kind=_lib.PRUNE_ABS_BELOW,
-                                threshold=net.prune_conn.threshold)
-            else:
-                K.forward_accumulate(b, act, self.acc, self.fwd_monoid)
+            self._accumulate_bucket(state, 0, act)
             self._combine_partials(self.acc)
             K.unit_apply(self.acc, act, mode=0, act_kind=fp.activation, monoid=self.fwd_monoid,
                          is_input=self.is_input, pruned=pruned)
@@ -192,12 +244,7 @@ class StepFn:
             return
         level = units[LEVEL.name]
         for l in range(self.num_buckets):
-            b = state.conns[l]
-            if self.fuse_prune:
-                K.forward_prune(b, act, self.acc, monoid=self.fwd_monoid, prune_kind=_lib.PRUNE_ABS_BELOW,
-                                threshold=net.prune_conn.threshold)
-            else:
-                K.forward_accumulate(b, act, self.acc, self.fwd_monoid)
+            self._accumulate_bucket(state, l, act)
             self._combine_partials(self.acc)
             K.unit_apply(self.acc, act, mode=0, act_kind=fp.activation, monoid=self.fwd_monoid, level=level,
                          target_level=l + 1, is_input=self.is_input, pruned=pruned)
@@ -268,11 +315,14 @@ class StepFn:
         if pc is None or self.fuse_prune:
             return
         n = self.static.num_units
-        for b in state.conns:
+        for i, b in enumerate(state.conns):
+            bm, bm_level = self._bm(i)
             if isinstance(pc, MagnitudePrune):
-                K.prune_conn(b, n, prune_kind=_lib.PRUNE_ABS_BELOW, threshold=pc.threshold)
+                K.prune_conn(b, n, prune_kind=_lib.PRUNE_ABS_BELOW, threshold=pc.threshold, free_bitmap=bm,
+                             bitmap_level=bm_level)
             elif isinstance(pc, DestinationThresholdPrune):
-                K.prune_conn(b, n, prune_kind=_lib.PRUNE_ABS_BELOW_DST, unit_threshold=state.units[pc.field.name])
+                K.prune_conn(b, n, prune_kind=_lib.PRUNE_ABS_BELOW_DST, unit_threshold=state.units[pc.field.name],
+                             free_bitmap=bm, bitmap_level=bm_level)
             self.launches += 1
 
     def _fires(self, state: NetworkState) -> bool:
@@ -331,7 +381,8 @@ class StepFn:
         for bk, gb in buckets:
             b, ws = state.conns[bk], self.claim_ws[bk]
             base = st.shard_base(bk)
-            K.claim_prepare(mode, b, level, state.tail_start, ws, shard_base=base)
+            bm, _ = self._bm(bk)
+            K.claim_prepare(mode, b, level, state.tail_start, ws, shard_base=base, free_bitmap=bm)
             before = totals = None
             if self.sharded:
                 dist = _dist()
@@ -342,7 +393,9 @@ class StepFn:
                 totals = self.gather_buf.sum(0, dtype=torch.int32)
             K.claim_commit(mode, b, level, state.tail_start, ws, cs, cd, cw, gb, max_new=max_new, shard_base=base,
                            global_cap=st.level_capacities[bk], level_before=before, level_totals=totals,
-                           extra=self.extra_defaults)
+                           extra=self.extra_defaults, free_bitmap=bm, placed=self.placed)
+            if self.use_mirror:
+                K.mirror_insert(self.mirrors[bk], cs, cd, cw, self.placed)
             self.grown += ws.counts[0]
             self.overflow |= ws.counts[1] > 0
             state.needs_resort |= ws.counts[3] > 0
@@ -354,6 +407,8 @@ class StepFn:
         return GrowthRemainder(cs, cd, cw, self.claim_ws[0].overflowed)
 
     def __call__(self, state: NetworkState, inputs: StepInputs) -> StepResult:
+        self._bind(state)
+        self._level = state.units[LEVEL.name]
         self._scatter_inputs(state, inputs)
         self._forward(state)
         self._loss(state, inputs)

@@ -301,10 +301,11 @@ def _claim_case(rng, cap, n, k, *, pipeline, dead_frac, tail_frac, levels=3):
     return b, level, tail, src, dst, w, grow, age
 
 
+@pytest.mark.parametrize("use_bitmap", [False, True])
 @pytest.mark.parametrize("cap,k,dead_frac,tail_frac,max_new",
                          [(100_000, 5000, 0.02, 0.01, -1), (100_000, 20_000, 0.05, 0.02, -1),
                           (4096, 300, 0.1, 0.0, -1), (1 << 20, 30_000, 0.01, 0.005, 20_000), (777, 1000, 0.3, 0.1, -1)])
-def test_claim_pipeline(cuda, cap, k, dead_frac, tail_frac, max_new):
+def test_claim_pipeline(cuda, cap, k, dead_frac, tail_frac, max_new, use_bitmap):
     import torch
 
     kern = _k()
@@ -319,11 +320,15 @@ def test_claim_pipeline(cuda, cap, k, dead_frac, tail_frac, max_new):
     t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
     d_level = t(level)
     d_tail = torch.tensor([tail], dtype=torch.int64, device=cuda)
-    ws = kern.ClaimWorkspace(cap, k, int(level.max()) + 1, cuda)
-    kern.claim_prepare(0, db, d_level, d_tail, ws)
+    nl = int(level.max()) + 1
+    ws = kern.ClaimWorkspace(cap, k, nl, cuda)
+    bm = kern.free_bitmap_build(0, db, d_level, d_tail, nl) if use_bitmap else None
+    kern.claim_prepare(0, db, d_level, d_tail, ws, free_bitmap=bm)
     kern.claim_commit(0, db, d_level, d_tail, ws, t(src), t(dst), t(w), t(grow), max_new=max_new,
-                      extra={"test/age": t(age)})
+                      extra={"test/age": t(age)}, free_bitmap=bm)
     hb = to_host(db)
+    if use_bitmap:  # the bitmaps stay equal to a rebuild from the new columns
+        np.testing.assert_array_equal(bm.cpu().numpy(), kern.free_bitmap_build(0, db, d_level, d_tail, nl).cpu().numpy())
     for col in ref_b:
         np.testing.assert_array_equal(hb[col], ref_b[col], err_msg=col)
     np.testing.assert_array_equal(ws.counts.cpu().numpy(), ref_counts)
@@ -331,8 +336,9 @@ def test_claim_pipeline(cuda, cap, k, dead_frac, tail_frac, max_new):
     assert int(d_tail.item()) == ref_tail
 
 
+@pytest.mark.parametrize("use_bitmap", [False, True])
 @pytest.mark.parametrize("cap,k,dead_frac", [(100_000, 5000, 0.03), (3000, 500, 0.1), (50_001, 10_000, 0.5)])
-def test_claim_topological(cuda, cap, k, dead_frac):
+def test_claim_topological(cuda, cap, k, dead_frac, use_bitmap):
     import torch
 
     kern = _k()
@@ -345,9 +351,13 @@ def test_claim_topological(cuda, cap, k, dead_frac):
     db = to_device(b, cuda)
     t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
     ws = kern.ClaimWorkspace(cap, k, 1, cuda)
-    kern.claim_prepare(1, db, t(level), None, ws)
-    kern.claim_commit(1, db, t(level), None, ws, t(src), t(dst), t(w), t(grow), extra={"test/age": t(age)})
+    bm = kern.free_bitmap_build(1, db, t(level), None, 1) if use_bitmap else None
+    kern.claim_prepare(1, db, t(level), None, ws, free_bitmap=bm)
+    kern.claim_commit(1, db, t(level), None, ws, t(src), t(dst), t(w), t(grow), extra={"test/age": t(age)},
+                      free_bitmap=bm)
     hb = to_host(db)
+    if use_bitmap:
+        np.testing.assert_array_equal(bm.cpu().numpy(), kern.free_bitmap_build(1, db, t(level), None, 1).cpu().numpy())
     for col in ref_b:
         np.testing.assert_array_equal(hb[col], ref_b[col], err_msg=col)
     np.testing.assert_array_equal(ws.counts.cpu().numpy()[:2], ref_counts[:2])
@@ -395,3 +405,125 @@ def test_claim_scheme_a_bands_match_one_device(cuda, shards, pipeline):
         np.testing.assert_array_equal(got, ref_b[col], err_msg=col)
     for g in range(1, shards):
         assert int(tails[g].item()) == int(tails[0].item())
+
+
+# ---------------------------------------------------------------------------
+# destination-grouped mirror
+# ---------------------------------------------------------------------------
+def _mirror_multiset(m, b):
+    """(slot, src, dst, weight) of every mirrored edge, sorted by slot."""
+    word = m.word.cpu().numpy().view(np.uint32)
+    live = word != 0xFFFFFFFF
+    cb = m.chunk_bits
+    ent = np.flatnonzero(live)
+    grp = np.searchsorted(m.gbase.cpu().numpy(), ent, side="right") - 1
+    src = (word[ent] >> cb).astype(np.int64)
+    dst = (grp.astype(np.int64) << cb) | (word[ent] & ((1 << cb) - 1))
+    out = [np.stack([m.slot.cpu().numpy()[ent].astype(np.int64), src, dst]).T]
+    wts = [m.weight.cpu().numpy()[ent]]
+    nov = int(min(m.ovf_count.item(), m.ovf_cap))
+    if nov:
+        os_ = m.ovf_src.cpu().numpy()[:nov]
+        keep = os_ >= 0
+        out.append(np.stack([m.ovf_slot.cpu().numpy()[:nov][keep], os_[keep],
+                             m.ovf_dst.cpu().numpy()[:nov][keep]]).T.astype(np.int64))
+        wts.append(m.ovf_weight.cpu().numpy()[:nov][keep])
+    rows, w = np.concatenate(out), np.concatenate(wts)
+    order = np.argsort(rows[:, 0], kind="stable")
+    return rows[order], w[order]
+
+
+def _canonical_multiset(hb):
+    live = np.flatnonzero(hb["dead"] == 0)
+    rows = np.stack([live, hb["from_id"][live], hb["to_id"][live]]).T.astype(np.int64)
+    return rows, hb["weight"][live]
+
+
+@pytest.mark.parametrize("n,cap,monoid", [(3000, 200_000, "sum"), (70_000, 400_000, "sum"), (5000, 100_000, "max"),
+                                          (1 << 20, 1 << 20, "sum")])
+def test_mirror_forward_prune(cuda, n, cap, monoid):
+    import torch
+
+    from plastax_b200.mirror import Mirror
+
+    kern = _k()
+    rng = np.random.default_rng(15)
+    b = random_bucket(rng, n, cap, int(cap * 0.9), dead_frac=0.02, weight_scale=0.1)
+    act = rng.standard_normal(n).astype(np.float32)
+    level = rng.integers(0, 3, n).astype(np.int32)
+    thr = 0.004
+    init = 0.0 if monoid == "sum" else -np.inf
+    ref_acc = np.full(n, init, np.float32)
+    orc.forward_accumulate(b, act, n, monoid, ref_acc)
+    ref_b = {kk: v.copy() for kk, v in b.items()}
+    orc.prune(ref_b, n, 1, thr)
+    db = to_device(b, cuda)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    d_level = t(level)
+    tail = torch.tensor([cap], dtype=torch.int64, device=cuda)
+    bm = kern.free_bitmap_build(0, db, d_level, tail, 3)
+    m = Mirror(db, n)
+    acc = torch.full((n,), init, dtype=torch.float32, device=cuda)
+    pruned = torch.zeros(1, dtype=torch.int32, device=cuda)
+    kern.mirror_forward(m, t(act), acc, monoid=monoid, prune_kind=1, threshold=thr, dead=db["dead"], free_bitmap=bm,
+                        bitmap_words=(cap + 31) // 32, bitmap_level=d_level, pruned_count=pruned)
+    if monoid == "sum":
+        _close(acc.cpu().numpy(), ref_acc)
+    else:
+        np.testing.assert_array_equal(acc.cpu().numpy(), ref_acc)
+    np.testing.assert_array_equal(db["dead"].cpu().numpy(), ref_b["dead"])
+    assert int(pruned.item()) == int((ref_b["dead"] != b["dead"]).sum())
+    np.testing.assert_array_equal(bm.cpu().numpy(), kern.free_bitmap_build(0, db, d_level, tail, 3).cpu().numpy())
+    rows, w = _mirror_multiset(m, None)
+    crows, cw = _canonical_multiset(to_host(db))
+    np.testing.assert_array_equal(rows, crows)
+    np.testing.assert_array_equal(w, cw)
+    assert m.healthy()
+
+
+@pytest.mark.parametrize("slack,ovf", [(0.05, 1 << 16), (0.0, 1 << 16)])
+def test_mirror_tracks_claims(cuda, slack, ovf):
+    """Prune + claim + insert for several steps: the mirror always holds
+    exactly the canonical live edges (full groups spill to the overflow
+    list, which the forward still sweeps)."""
+    import torch
+
+    from plastax_b200.mirror import Mirror
+
+    kern = _k()
+    rng = np.random.default_rng(16)
+    n, cap, k = 4096, 300_000, 4000
+    b = random_bucket(rng, n, cap, int(cap * 0.97), dead_frac=0.0, weight_scale=0.1)
+    level = np.ones(n, np.int32)
+    level[:16] = 0
+    db = to_device(b, cuda)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    d_level = t(level)
+    tail = torch.tensor([int(cap * 0.97)], dtype=torch.int64, device=cuda)
+    bm = kern.free_bitmap_build(0, db, d_level, tail, 2)
+    m = Mirror(db, n, slack=slack, min_slack=4 if slack == 0 else 64, ovf_cap=ovf)
+    ws = kern.ClaimWorkspace(cap, k, 2, cuda)
+    placed = torch.empty(k, dtype=torch.int32, device=cuda)
+    hb = to_host(db)
+    for step in range(5):
+        act = rng.standard_normal(n).astype(np.float32)
+        acc = torch.zeros(n, dtype=torch.float32, device=cuda)
+        ref_acc = np.zeros(n, np.float32)
+        orc.forward_accumulate(hb, act, n, "sum", ref_acc)
+        kern.mirror_forward(m, t(act), acc, prune_kind=1, threshold=0.01, dead=db["dead"], free_bitmap=bm,
+                            bitmap_words=(cap + 31) // 32, bitmap_level=d_level)
+        _close(acc.cpu().numpy(), ref_acc)
+        src = rng.integers(16, n, k).astype(np.int32)
+        src = src[np.argsort(level[src], kind="stable")]
+        dst = rng.integers(16, n, k).astype(np.int32)
+        w = (rng.standard_normal(k) * 0.1).astype(np.float32)
+        grow = np.ones(k, np.uint8)
+        kern.claim_prepare(0, db, d_level, tail, ws, free_bitmap=bm)
+        kern.claim_commit(0, db, d_level, tail, ws, t(src), t(dst), t(w), t(grow), free_bitmap=bm, placed=placed)
+        kern.mirror_insert(m, t(src), t(dst), t(w), placed)
+        hb = to_host(db)
+        rows, mw = _mirror_multiset(m, None)
+        crows, cw = _canonical_multiset(hb)
+        np.testing.assert_array_equal(rows, crows, err_msg=f"step {step}")
+        np.testing.assert_array_equal(mw, cw)
+    assert m.healthy()
