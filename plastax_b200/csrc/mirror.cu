@@ -25,6 +25,7 @@ namespace pxb {
 constexpr uint32_t kEmpty = 0xffffffffu;
 
 struct MirrorK {
+  int64_t entries;
   int32_t n;
   int cb;  // chunk bits
   int64_t groups;
@@ -45,6 +46,7 @@ struct MirrorK {
 
 static MirrorK to_k(const pxb_mirror *m) {
   MirrorK k;
+  k.entries = m->entries;
   k.n = m->num_units;
   k.cb = m->chunk_bits;
   k.groups = m->groups;
@@ -103,6 +105,31 @@ __device__ __forceinline__ void smem_combine(float *a, float v) {
   else atomic_min_f32(a, v);
 }
 
+// One entry of the sweep: gather, shared-memory combine, fused prune.
+template <int MONOID, bool PRUNE>
+__device__ __forceinline__ void sweep_entry(const MirrorK &m, const MPrune &p, float *acc_s, int32_t g, int64_t gb,
+                                            uint32_t mask, uint32_t word, float w, float a, int64_t pos) {
+  if (word == kEmpty) return;
+  const uint32_t src = word >> m.cb;
+  if (src >= static_cast<uint32_t>(m.n)) return;
+  const uint32_t dl = word & mask;
+  smem_combine<MONOID>(acc_s + dl, __fmul_rn(w, a));
+  if (PRUNE) {
+    const int32_t dst = (g << m.cb) | static_cast<int32_t>(dl);
+    if (dst < m.n && mprune_pred(p, w, dst)) {
+      m.word[pos] = kEmpty;
+      tombstone(p, m.slot[pos], static_cast<int32_t>(src));
+      const int32_t h = atomicAdd(m.hcount + g, 1);
+      m.hstack[gb + h] = static_cast<int32_t>(pos - gb);
+    }
+  }
+}
+
+// Each CTA sweeps an equal contiguous range of the entry array (balanced by
+// construction), accumulating into shared memory and flushing the chunk's
+// accumulators whenever its range crosses into the next group. Two quads
+// (8 entries, 2 x 32 B of loads) per thread per iteration keep enough bytes
+// in flight to cover the HBM latency.
 template <int MONOID, bool PRUNE>
 __global__ void __launch_bounds__(256) mirror_forward_kernel(MirrorK m, const float *__restrict__ act,
                                                              float *__restrict__ acc, MPrune p) {
@@ -110,50 +137,63 @@ __global__ void __launch_bounds__(256) mirror_forward_kernel(MirrorK m, const fl
   const int chunk = 1 << m.cb;
   const uint32_t mask = static_cast<uint32_t>(chunk - 1);
   const float ident = monoid_identity(MONOID);
-  for (int64_t it = blockIdx.x; it < m.items; it += gridDim.x) {
-    const int32_t g = m.ig[it];
+  const int64_t quads = m.entries / 4;
+  const int64_t per = (quads + gridDim.x - 1) / gridDim.x;
+  const int64_t q_lo = blockIdx.x * per;
+  const int64_t q_hi = q_lo + per < quads ? q_lo + per : quads;
+  if (q_lo >= q_hi) return;
+  // first group whose region holds quad q_lo: the last g with gbase[g] <= 4*q_lo
+  int64_t lo = 0, hi = m.groups - 1;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) / 2;
+    if (m.gbase[mid] <= q_lo * 4) lo = mid; else hi = mid - 1;
+  }
+  const uint4 *w4 = reinterpret_cast<const uint4 *>(m.word);
+  const float4 *f4 = reinterpret_cast<const float4 *>(m.w);
+  for (int64_t g = lo; g < m.groups && m.gbase[g] < q_hi * 4; ++g) {
     const int64_t gb = m.gbase[g], gcap = m.gbase[g + 1] - gb;
     int64_t fill = m.gfill[g];
     fill = fill < gcap ? fill : gcap;
-    const int64_t b = m.ib[it];
-    int64_t e = m.ie[it];
-    if (e > gb + fill) e = gb + ((fill + 3) & ~int64_t(3));
+    const int64_t a_q = gb / 4 > q_lo ? gb / 4 : q_lo;
+    const int64_t e_used = (gb + fill + 3) / 4;
+    const int64_t b_q = e_used < q_hi ? e_used : q_hi;
+    if (a_q >= b_q) continue;
     for (int u = threadIdx.x; u < chunk; u += blockDim.x) acc_s[u] = ident;
     __syncthreads();
-    const uint4 *w4 = reinterpret_cast<const uint4 *>(m.word);
-    const float4 *f4 = reinterpret_cast<const float4 *>(m.w);
-    for (int64_t q = b / 4 + threadIdx.x; q < e / 4; q += blockDim.x) {
-      const uint4 wd = __ldcs(w4 + q);
-      const float4 wv = __ldcs(f4 + q);
-      const uint32_t ws[4] = {wd.x, wd.y, wd.z, wd.w};
-      const float fs[4] = {wv.x, wv.y, wv.z, wv.w};
-      float a[4];
+    const int gi = static_cast<int>(g);
+    int64_t q = a_q + threadIdx.x;
+    for (; q + blockDim.x < b_q; q += 2 * blockDim.x) {
+      const int64_t q2 = q + blockDim.x;
+      const uint4 wa = __ldcs(w4 + q), wb = __ldcs(w4 + q2);
+      const float4 fa = __ldcs(f4 + q), fb = __ldcs(f4 + q2);
+      const uint32_t ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+      const float fs[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
+      float av[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t src = ws[i] >> m.cb;
+        av[i] = (ws[i] != kEmpty && src < static_cast<uint32_t>(m.n)) ? __ldg(act + src) : 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        sweep_entry<MONOID, PRUNE>(m, p, acc_s, gi, gb, mask, ws[i], fs[i], av[i], (i < 4 ? q : q2) * 4 + (i & 3));
+    }
+    if (q < b_q) {
+      const uint4 wa = __ldcs(w4 + q);
+      const float4 fa = __ldcs(f4 + q);
+      const uint32_t ws[4] = {wa.x, wa.y, wa.z, wa.w};
+      const float fs[4] = {fa.x, fa.y, fa.z, fa.w};
+      float av[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint32_t src = ws[i] >> m.cb;
-        a[i] = (ws[i] != kEmpty && src < static_cast<uint32_t>(m.n)) ? __ldg(act + src) : 0.0f;
+        av[i] = (ws[i] != kEmpty && src < static_cast<uint32_t>(m.n)) ? __ldg(act + src) : 0.0f;
       }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (ws[i] == kEmpty) continue;
-        const uint32_t src = ws[i] >> m.cb;
-        if (src >= static_cast<uint32_t>(m.n)) continue;
-        const uint32_t dl = ws[i] & mask;
-        smem_combine<MONOID>(acc_s + dl, __fmul_rn(fs[i], a[i]));
-        if (PRUNE) {
-          const int32_t dst = (g << m.cb) | static_cast<int32_t>(dl);
-          if (dst < m.n && mprune_pred(p, fs[i], dst)) {
-            const int64_t pos = q * 4 + i;
-            m.word[pos] = kEmpty;
-            tombstone(p, m.slot[pos], static_cast<int32_t>(src));
-            const int32_t h = atomicAdd(m.hcount + g, 1);
-            m.hstack[gb + h] = static_cast<int32_t>(pos - gb);
-          }
-        }
-      }
+      for (int i = 0; i < 4; ++i) sweep_entry<MONOID, PRUNE>(m, p, acc_s, gi, gb, mask, ws[i], fs[i], av[i], q * 4 + i);
     }
     __syncthreads();
-    const int32_t base = g << m.cb;
+    const int32_t base = gi << m.cb;
     if (MONOID == PXB_MONOID_SUM && base + chunk <= m.n) {
       float4 *acc4 = reinterpret_cast<float4 *>(acc + base);
       const float4 *s4 = reinterpret_cast<const float4 *>(acc_s);
@@ -273,8 +313,10 @@ extern "C" int pxb_mirror_forward(const pxb_mirror *mirror, const float *act, in
   MPrune p{prune_kind, prune_threshold, unit_threshold, dead, free_bitmap, bitmap_words, bitmap_level, pruned_count};
   cudaStream_t st = as_stream(stream);
   const size_t smem = sizeof(float) << m.cb;
-  if (m.items > 0) {
-    const int grid = static_cast<int>(m.items < int64_t(sm_count()) * 8 ? m.items : int64_t(sm_count()) * 8);
+  if (m.entries > 0) {
+    const int64_t full = int64_t(sm_count()) * 8;
+    const int64_t want = (m.entries / 4 + 1023) / 1024;  // at least 4 K entries per CTA
+    const int grid = static_cast<int>(want < full ? (want > 0 ? want : 1) : full);
 #define PXB_MF(M, P) mirror_forward_kernel<M, P><<<grid, 256, smem, st>>>(m, act, acc, p)
     const bool pr = prune_kind != PXB_PRUNE_NONE;
     if (monoid == PXB_MONOID_SUM) { if (pr) PXB_MF(PXB_MONOID_SUM, true); else PXB_MF(PXB_MONOID_SUM, false); }
