@@ -267,12 +267,14 @@ PXB_API int pxb_total_order(int64_t n, const float *score, const int32_t *src,
 /* Step-scoped selection (level_cap_scope = "step",
  * src/plastax/phases.py:4891-4903 and level_major :4469-4487): the first
  * min(k, n) candidates of `perm`, relisted by source level ascending
- * (stable). Writes win_idx[min(k, n)] and win_count[0]. */
+ * (stable); every level is below num_levels. Writes win_idx[min(k, n)]
+ * and win_count[0]. */
 PXB_API int pxb_select_step_scratch_bytes(int64_t n, int64_t k, size_t *bytes);
 PXB_API int pxb_select_step(int64_t n, const int32_t *perm, const float *score,
-                    const int32_t *src, const int32_t *level, int64_t k,
-                    int32_t *win_idx, int32_t *win_count, void *scratch,
-                    size_t scratch_bytes, void *stream);
+                    const int32_t *src, const int32_t *level,
+                    int32_t num_levels, int64_t k, int32_t *win_idx,
+                    int32_t *win_count, void *scratch, size_t scratch_bytes,
+                    void *stream);
 
 /* growth init rules for a committed edge's weight (the rule's `init`) */
 #define PXB_INIT_CONST 0         /* w = a                                      */
@@ -399,6 +401,7 @@ typedef struct pxb_mirror {
   int32_t *ovf_slot;
   float *ovf_weight;
   int32_t *status;
+  int32_t *ins_count; /* [groups] zeroed scratch of pxb_mirror_insert */
 } pxb_mirror;
 
 /* Forward accumulate of the mirrored bucket (acc (+)= w * act[src] per

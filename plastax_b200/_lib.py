@@ -43,7 +43,7 @@ class Mirror(ctypes.Structure):
         ("gbase", c_ptr), ("gfill", c_ptr), ("word", c_ptr), ("weight", c_ptr), ("slot", c_ptr),
         ("hstack", c_ptr), ("hcount", c_ptr), ("items", c_i64), ("item_begin", c_ptr), ("item_end", c_ptr),
         ("item_group", c_ptr), ("ovf_cap", c_i64), ("ovf_count", c_ptr), ("ovf_src", c_ptr), ("ovf_dst", c_ptr),
-        ("ovf_slot", c_ptr), ("ovf_weight", c_ptr), ("status", c_ptr),
+        ("ovf_slot", c_ptr), ("ovf_weight", c_ptr), ("status", c_ptr), ("ins_count", c_ptr),
     ]
 
 
@@ -108,7 +108,7 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_total_order_scratch_bytes": (c_i32, [c_i64, c_i32, ctypes.POINTER(c_size)]),
     "pxb_total_order": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_size, c_ptr]),
     "pxb_select_step_scratch_bytes": (c_i32, [c_i64, c_i64, ctypes.POINTER(c_size)]),
-    "pxb_select_step": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_size, c_ptr]),
+    "pxb_select_step": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_size, c_ptr]),
     "pxb_gather_winners": (
         c_i32,
         [c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_f32, c_f32, c_u32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr],

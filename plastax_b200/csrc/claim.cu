@@ -41,11 +41,11 @@ struct ClaimGeom {
   int64_t tiles;
 };
 
-static ClaimGeom geom_of(int64_t cap, int32_t num_levels) {
+static ClaimGeom geom_of(int64_t cap, int32_t num_levels, bool bitmap = false) {
   ClaimGeom g;
   g.cap = cap;
   g.num_levels = num_levels;
-  g.tile_shift = 10;
+  g.tile_shift = bitmap ? 13 : 10;
   for (;;) {
     g.tiles = (cap + (int64_t(1) << g.tile_shift) - 1) >> g.tile_shift;
     if (g.tiles < 1) g.tiles = 1;
@@ -176,8 +176,9 @@ __global__ void __launch_bounds__(kClaimWarps * 32) tile_count_bm_kernel(DomainA
     const int64_t l = j / g.tiles, t = j - l * g.tiles;
     const uint32_t *row = a.bm + l * a.bm_words;
     int c = 0;
-    for (int64_t w = t * words_per_tile + lane; w < (t + 1) * words_per_tile && w < a.bm_words; w += 32)
-      c += __popc(row[w]);
+    const int64_t w_end = (t + 1) * words_per_tile < a.bm_words ? (t + 1) * words_per_tile : a.bm_words;
+#pragma unroll 8
+    for (int64_t w = t * words_per_tile + lane; w < w_end; w += 32) c += __popc(__ldg(row + w));
     c = __reduce_add_sync(0xffffffffu, c);
     if (lane == 0) tile_counts[j] = c;
   }
@@ -347,6 +348,7 @@ __global__ void __launch_bounds__(kClaimWarps * 32) list_fill_bm_kernel(
     for (int64_t w0 = t * words_per_tile; w0 < (t + 1) * words_per_tile && w0 < a.bm_words && run < nl; w0 += 32) {
       const int64_t w = w0 + lane;
       uint32_t bits = (w < (t + 1) * words_per_tile && w < a.bm_words) ? row[w] : 0u;
+      if (__ballot_sync(0xffffffffu, bits != 0u) == 0u) continue;
       const int pc = __popc(bits);
       int incl = pc;
 #pragma unroll
@@ -492,7 +494,7 @@ extern "C" int pxb_claim_prepare(int32_t mode, int64_t cap, const int32_t *from_
   PXB_REQUIRE(free_bitmap || topo || (from_id && unit_level && tail_start && num_units > 0),
               "pxb_claim_prepare: pipeline mode needs from_id, unit_level, num_units and tail_start");
   PXB_REQUIRE(free_bitmap || cap == 0 || dead, "pxb_claim_prepare: dead is NULL");
-  const ClaimGeom g = geom_of(cap, num_levels);
+  const ClaimGeom g = geom_of(cap, num_levels, free_bitmap != nullptr);
   ClaimScratch o;
   if (claim_scratch(g, k, static_cast<char *>(scratch), &o) != PXB_OK) {
     set_error("pxb_claim_prepare: CUB size query failed");
@@ -543,7 +545,7 @@ extern "C" int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id, int
   PXB_REQUIRE(cap == 0 || (from_id && to_id && dead && weight), "pxb_claim_commit: a bucket column is NULL");
   PXB_REQUIRE(k == 0 || (cand_src && cand_dst && cand_weight && growable), "pxb_claim_commit: candidates are NULL");
   PXB_REQUIRE(global_cap >= shard_base + cap, "pxb_claim_commit: global_cap below this rank's band");
-  const ClaimGeom g = geom_of(cap, num_levels);
+  const ClaimGeom g = geom_of(cap, num_levels, free_bitmap != nullptr);
   ClaimScratch o;
   if (claim_scratch(g, k, static_cast<char *>(scratch), &o) != PXB_OK) {
     set_error("pxb_claim_commit: CUB size query failed");

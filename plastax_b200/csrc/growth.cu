@@ -362,8 +362,8 @@ extern "C" int pxb_select_step_scratch_bytes(int64_t n, int64_t k, size_t *bytes
 }
 
 extern "C" int pxb_select_step(int64_t n, const int32_t *perm, const float *score, const int32_t *src,
-                               const int32_t *level, int64_t k, int32_t *win_idx, int32_t *win_count,
-                               void *scratch, size_t scratch_bytes, void *stream) {
+                               const int32_t *level, int32_t num_levels, int64_t k, int32_t *win_idx,
+                               int32_t *win_count, void *scratch, size_t scratch_bytes, void *stream) {
   (void)score;
   PXB_REQUIRE(n >= 0 && k >= 0 && n < (int64_t(1) << 31), "pxb_select_step: sizes out of range");
   const int64_t kk = k < n ? k : n;
@@ -381,11 +381,14 @@ extern "C" int pxb_select_step(int64_t n, const int32_t *perm, const float *scor
   }
   PXB_REQUIRE(o.total <= scratch_bytes, "pxb_select_step: scratch has %zu bytes, needs %zu", scratch_bytes,
               o.total);
+  PXB_REQUIRE(num_levels >= 1, "pxb_select_step: num_levels must be >= 1");
   winner_level_kernel<<<grid_for(kk, 256, 8), 256, 0, st>>>(kk, perm, src, level, o.key_in, o.val_in);
   PXB_LAUNCHED("winner_level_kernel");
+  int key_bits = 1;
+  while (key_bits < 32 && (int64_t(1) << key_bits) < num_levels) ++key_bits;
   size_t tb = o.cub_bytes;
   PXB_CUDA(cub::DeviceRadixSort::SortPairs(o.cub_tmp, tb, o.key_in, o.key_out, o.val_in, win_idx,
-                                           static_cast<int>(kk), 0, 32, st));
+                                           static_cast<int>(kk), 0, key_bits, st));
   return PXB_OK;
 }
 

@@ -228,9 +228,13 @@ __global__ void mirror_overflow_kernel(MirrorK m, const float *__restrict__ act,
   }
 }
 
+// Insert, phase 1: each placed edge takes rank r in its destination group
+// (one atomicAdd on the group's insert counter); the r-th insert of a group
+// takes the group's r-th hole from the top of its stack, then its unused
+// slack, then the overflow list. Phase 2 retires the used holes and slack.
 __global__ void mirror_insert_kernel(MirrorK m, int64_t k, const int32_t *__restrict__ src,
                                      const int32_t *__restrict__ dst, const float *__restrict__ w,
-                                     const int32_t *__restrict__ placed) {
+                                     const int32_t *__restrict__ placed, int32_t *__restrict__ ins_count) {
   const uint32_t mask = (1u << m.cb) - 1u;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < k;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -240,18 +244,13 @@ __global__ void mirror_insert_kernel(MirrorK m, int64_t k, const int32_t *__rest
     if (a < 0 || a >= m.n || d < 0 || d >= m.n) continue;
     const int32_t g = d >> m.cb;
     const int64_t gb = m.gbase[g], gcap = m.gbase[g + 1] - gb;
+    const int32_t r = atomicAdd(ins_count + g, 1);
+    const int32_t holes = m.hcount[g];
     int64_t pos = -1;
-    int32_t c = m.hcount[g];
-    while (c > 0) {
-      const int32_t prev = atomicCAS(m.hcount + g, c, c - 1);
-      if (prev == c) {
-        pos = gb + m.hstack[gb + c - 1];
-        break;
-      }
-      c = prev;
-    }
-    if (pos < 0) {
-      const int32_t f = atomicAdd(m.gfill + g, 1);
+    if (r < holes) {
+      pos = gb + m.hstack[gb + holes - 1 - r];
+    } else {
+      const int64_t f = static_cast<int64_t>(m.gfill[g]) + (r - holes);
       if (f < gcap) pos = gb + f;
     }
     if (pos >= 0) {
@@ -269,6 +268,24 @@ __global__ void mirror_insert_kernel(MirrorK m, int64_t k, const int32_t *__rest
         atomicOr(m.status, 1);  // an edge is missing from the mirror: rebuild it
       }
     }
+  }
+}
+
+__global__ void mirror_insert_finish_kernel(MirrorK m, int32_t *__restrict__ ins_count) {
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < m.groups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t ins = ins_count[g];
+    if (ins == 0) continue;
+    const int32_t holes = m.hcount[g];
+    const int64_t gcap = m.gbase[g + 1] - m.gbase[g];
+    if (ins <= holes) {
+      m.hcount[g] = holes - ins;
+    } else {
+      m.hcount[g] = 0;
+      const int64_t f = static_cast<int64_t>(m.gfill[g]) + (ins - holes);
+      m.gfill[g] = static_cast<int32_t>(f < gcap ? f : gcap);
+    }
+    ins_count[g] = 0;
   }
 }
 
@@ -344,8 +361,12 @@ extern "C" int pxb_mirror_insert(const pxb_mirror *mirror, int64_t k, const int3
   PXB_REQUIRE(k >= 0, "pxb_mirror_insert: negative k");
   if (k == 0) return PXB_OK;
   PXB_REQUIRE(src && dst && weight && placed, "pxb_mirror_insert: a pointer is NULL");
-  mirror_insert_kernel<<<grid_for(k, 256, 8), 256, 0, as_stream(stream)>>>(to_k(mirror), k, src, dst, weight,
-                                                                            placed);
+  PXB_REQUIRE(mirror->ins_count != nullptr, "pxb_mirror_insert: ins_count is NULL");
+  cudaStream_t st = as_stream(stream);
+  const MirrorK m = to_k(mirror);
+  mirror_insert_kernel<<<grid_for(k, 256, 8), 256, 0, st>>>(m, k, src, dst, weight, placed, mirror->ins_count);
   PXB_LAUNCHED("mirror_insert_kernel");
+  mirror_insert_finish_kernel<<<grid_for(m.groups, 256, 4), 256, 0, st>>>(m, mirror->ins_count);
+  PXB_LAUNCHED("mirror_insert_finish_kernel");
   return PXB_OK;
 }

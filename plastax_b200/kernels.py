@@ -246,7 +246,8 @@ def select_step_scratch(n: int, k: int) -> int:
 
 
 def select_step(perm: torch.Tensor, score: torch.Tensor, src: torch.Tensor, level: torch.Tensor, k: int,
-                win: torch.Tensor | None = None, scratch: torch.Tensor | None = None) -> torch.Tensor:
+                win: torch.Tensor | None = None, scratch: torch.Tensor | None = None,
+                num_levels: int | None = None) -> torch.Tensor:
     n = perm.numel()
     kk = min(k, n)
     if win is None:
@@ -254,8 +255,11 @@ def select_step(perm: torch.Tensor, score: torch.Tensor, src: torch.Tensor, leve
     need = select_step_scratch(n, k)
     if scratch is None or scratch.numel() < need:
         scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=perm.device)
-    call("pxb_select_step", ctypes.c_int64(n), ptr(perm), ptr(score), ptr(src), ptr(level), ctypes.c_int64(k),
-         ptr(win), None, ptr(scratch), ctypes.c_size_t(scratch.numel()), _stream())
+    if num_levels is None:
+        num_levels = int(level.max().item()) + 1 if level.numel() else 1
+    call("pxb_select_step", ctypes.c_int64(n), ptr(perm), ptr(score), ptr(src), ptr(level),
+         ctypes.c_int32(num_levels), ctypes.c_int64(k), ptr(win), None, ptr(scratch), ctypes.c_size_t(scratch.numel()),
+         _stream())
     return win[:kk]
 
 

@@ -78,12 +78,13 @@ class Mirror:
         self.ovf_slot = torch.zeros(max(ovf_cap, 1), dtype=torch.int32, device=dev)
         self.ovf_weight = torch.zeros(max(ovf_cap, 1), dtype=torch.float32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ins_count = torch.zeros(groups, dtype=torch.int32, device=dev)
         p = lambda x: x.data_ptr()  # noqa: E731
         self.struct = _lib.Mirror(
             n, cb, groups, entries, p(self.gbase), p(self.gfill), p(self.word), p(self.weight), p(self.slot),
             p(self.hstack), p(self.hcount), len(ib), p(self.item_begin), p(self.item_end), p(self.item_group),
             self.ovf_cap, p(self.ovf_count), p(self.ovf_src), p(self.ovf_dst), p(self.ovf_slot), p(self.ovf_weight),
-            p(self.status))
+            p(self.status), p(self.ins_count))
 
     def healthy(self) -> bool:
         """False when an edge could not be mirrored (host read; synchronises)."""

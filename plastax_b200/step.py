@@ -358,7 +358,8 @@ class StepFn:
                            src_level_bound=0 if self.pipeline else self.num_buckets, out=self.cand)
         src, dst, score = self.cand
         K.total_order(score, src, dst, n, perm=self.perm, scratch=self.order_scratch)
-        K.select_step(self.perm, score, src, level, self.k, win=self.win, scratch=self.sel_scratch)
+        K.select_step(self.perm, score, src, level, self.k, win=self.win, scratch=self.sel_scratch,
+                      num_levels=self.static.num_levels)
         kk = min(self.k, self.n_cand)
         K.gather_winners(self.win, kk, self.k, src, dst, score, init_kind=self.init_kind, init_a=self.init_a,
                          out=self.claim_in)
