@@ -369,7 +369,7 @@ PXB_API int pxb_count_dead(int64_t cap, const uint8_t *dead, int32_t *out,
 /* ------------------------------------------------------------------ */
 /* A bucket's live edges grouped by destination chunk (2^chunk_bits
  * consecutive units, chunk_bits <= 13, ceil(log2 num_units) + chunk_bits
- * <= 32). Group g owns entries [gbase[g], gbase[g+1]) (multiples of 4), of
+ * <= 32). Group g owns entries [gbase[g], gbase[g+1]) (multiples of 8), of
  * which the first gfill[g] have ever been used. Entry e: word[e] = src <<
  * chunk_bits | (dst - g * 2^chunk_bits), or 0xffffffff when empty;
  * weight[e]; slot[e] = the canonical (local) slot it mirrors. hstack at

@@ -105,31 +105,28 @@ __device__ __forceinline__ void smem_combine(float *a, float v) {
   else atomic_min_f32(a, v);
 }
 
-// One entry of the sweep: gather, shared-memory combine, fused prune.
-template <int MONOID, bool PRUNE>
-__device__ __forceinline__ void sweep_entry(const MirrorK &m, const MPrune &p, float *acc_s, int32_t g, int64_t gb,
-                                            uint32_t mask, uint32_t word, float w, float a, int64_t pos) {
-  if (word == kEmpty) return;
-  const uint32_t src = word >> m.cb;
-  if (src >= static_cast<uint32_t>(m.n)) return;
-  const uint32_t dl = word & mask;
-  smem_combine<MONOID>(acc_s + dl, __fmul_rn(w, a));
-  if (PRUNE) {
-    const int32_t dst = (g << m.cb) | static_cast<int32_t>(dl);
-    if (dst < m.n && mprune_pred(p, w, dst)) {
-      m.word[pos] = kEmpty;
-      tombstone(p, m.slot[pos], static_cast<int32_t>(src));
-      const int32_t h = atomicAdd(m.hcount + g, 1);
-      m.hstack[gb + h] = static_cast<int32_t>(pos - gb);
-    }
+// Fused prune of one entry (rare path): empty the mirror entry, record the
+// canonical tombstone, push the entry on its group's hole stack.
+template <bool PRUNE>
+__device__ __forceinline__ void prune_entry(const MirrorK &m, const MPrune &p, int32_t g, int64_t gb, uint32_t src,
+                                            uint32_t dl, float w, int64_t pos) {
+  if (!PRUNE) return;
+  const int32_t dst = (g << m.cb) | static_cast<int32_t>(dl);
+  if (dst < m.n && mprune_pred(p, w, dst)) {
+    m.word[pos] = kEmpty;
+    tombstone(p, m.slot[pos], static_cast<int32_t>(src));
+    const int32_t h = atomicAdd(m.hcount + g, 1);
+    m.hstack[gb + h] = static_cast<int32_t>(pos - gb);
   }
 }
 
 // Each CTA sweeps an equal contiguous range of the entry array (balanced by
-// construction), accumulating into shared memory and flushing the chunk's
-// accumulators whenever its range crosses into the next group. Two quads
-// (8 entries, 2 x 32 B of loads) per thread per iteration keep enough bytes
-// in flight to cover the HBM latency.
+// construction); each thread owns 8 consecutive entries per iteration (two
+// adjacent 16-byte loads of ids and of weights). Groups are built sorted by
+// destination, so a thread's entries form runs of one destination: a run is
+// summed in registers and combined into the chunk's shared accumulators with
+// one atomic, and the chunk is flushed to global memory when the range
+// crosses into the next group.
 template <int MONOID, bool PRUNE>
 __global__ void __launch_bounds__(256) mirror_forward_kernel(MirrorK m, const float *__restrict__ act,
                                                              float *__restrict__ acc, MPrune p) {
@@ -137,35 +134,32 @@ __global__ void __launch_bounds__(256) mirror_forward_kernel(MirrorK m, const fl
   const int chunk = 1 << m.cb;
   const uint32_t mask = static_cast<uint32_t>(chunk - 1);
   const float ident = monoid_identity(MONOID);
-  const int64_t quads = m.entries / 4;
-  const int64_t per = (quads + gridDim.x - 1) / gridDim.x;
-  const int64_t q_lo = blockIdx.x * per;
-  const int64_t q_hi = q_lo + per < quads ? q_lo + per : quads;
-  if (q_lo >= q_hi) return;
-  // first group whose region holds quad q_lo: the last g with gbase[g] <= 4*q_lo
+  const int64_t octs = m.entries / 8;  // entries is a multiple of 8 (groups are)
+  const int64_t per = (octs + gridDim.x - 1) / gridDim.x;
+  const int64_t o_lo = blockIdx.x * per;
+  const int64_t o_hi = o_lo + per < octs ? o_lo + per : octs;
+  if (o_lo >= o_hi) return;
   int64_t lo = 0, hi = m.groups - 1;
   while (lo < hi) {
     const int64_t mid = (lo + hi + 1) / 2;
-    if (m.gbase[mid] <= q_lo * 4) lo = mid; else hi = mid - 1;
+    if (m.gbase[mid] <= o_lo * 8) lo = mid; else hi = mid - 1;
   }
   const uint4 *w4 = reinterpret_cast<const uint4 *>(m.word);
   const float4 *f4 = reinterpret_cast<const float4 *>(m.w);
-  for (int64_t g = lo; g < m.groups && m.gbase[g] < q_hi * 4; ++g) {
+  for (int64_t g = lo; g < m.groups && m.gbase[g] < o_hi * 8; ++g) {
     const int64_t gb = m.gbase[g], gcap = m.gbase[g + 1] - gb;
     int64_t fill = m.gfill[g];
     fill = fill < gcap ? fill : gcap;
-    const int64_t a_q = gb / 4 > q_lo ? gb / 4 : q_lo;
-    const int64_t e_used = (gb + fill + 3) / 4;
-    const int64_t b_q = e_used < q_hi ? e_used : q_hi;
-    if (a_q >= b_q) continue;
+    const int64_t a_o = gb / 8 > o_lo ? gb / 8 : o_lo;
+    const int64_t e_used = (gb + fill + 7) / 8;
+    const int64_t b_o = e_used < o_hi ? e_used : o_hi;
+    if (a_o >= b_o) continue;
     for (int u = threadIdx.x; u < chunk; u += blockDim.x) acc_s[u] = ident;
     __syncthreads();
     const int gi = static_cast<int>(g);
-    int64_t q = a_q + threadIdx.x;
-    for (; q + blockDim.x < b_q; q += 2 * blockDim.x) {
-      const int64_t q2 = q + blockDim.x;
-      const uint4 wa = __ldcs(w4 + q), wb = __ldcs(w4 + q2);
-      const float4 fa = __ldcs(f4 + q), fb = __ldcs(f4 + q2);
+    for (int64_t o = a_o + threadIdx.x; o < b_o; o += blockDim.x) {
+      const uint4 wa = __ldcs(w4 + 2 * o), wb = __ldcs(w4 + 2 * o + 1);
+      const float4 fa = __ldcs(f4 + 2 * o), fb = __ldcs(f4 + 2 * o + 1);
       const uint32_t ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
       const float fs[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
       float av[8];
@@ -174,23 +168,24 @@ __global__ void __launch_bounds__(256) mirror_forward_kernel(MirrorK m, const fl
         const uint32_t src = ws[i] >> m.cb;
         av[i] = (ws[i] != kEmpty && src < static_cast<uint32_t>(m.n)) ? __ldg(act + src) : 0.0f;
       }
+      uint32_t cur = kEmpty;
+      float run = ident;
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        sweep_entry<MONOID, PRUNE>(m, p, acc_s, gi, gb, mask, ws[i], fs[i], av[i], (i < 4 ? q : q2) * 4 + (i & 3));
-    }
-    if (q < b_q) {
-      const uint4 wa = __ldcs(w4 + q);
-      const float4 fa = __ldcs(f4 + q);
-      const uint32_t ws[4] = {wa.x, wa.y, wa.z, wa.w};
-      const float fs[4] = {fa.x, fa.y, fa.z, fa.w};
-      float av[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < 8; ++i) {
         const uint32_t src = ws[i] >> m.cb;
-        av[i] = (ws[i] != kEmpty && src < static_cast<uint32_t>(m.n)) ? __ldg(act + src) : 0.0f;
+        if (ws[i] == kEmpty || src >= static_cast<uint32_t>(m.n)) continue;
+        const uint32_t dl = ws[i] & mask;
+        const float v = __fmul_rn(fs[i], av[i]);
+        if (dl != cur) {
+          if (cur != kEmpty) smem_combine<MONOID>(acc_s + cur, run);
+          cur = dl;
+          run = v;
+        } else {
+          run = combine2<MONOID>(run, v);
+        }
+        prune_entry<PRUNE>(m, p, gi, gb, src, dl, fs[i], o * 8 + i);
       }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) sweep_entry<MONOID, PRUNE>(m, p, acc_s, gi, gb, mask, ws[i], fs[i], av[i], q * 4 + i);
+      if (cur != kEmpty) smem_combine<MONOID>(acc_s + cur, run);
     }
     __syncthreads();
     const int32_t base = gi << m.cb;
@@ -295,7 +290,7 @@ static int check_mirror(const char *fn, const pxb_mirror *m) {
   PXB_REQUIRE(m->num_units > 0, "%s: num_units must be > 0", fn);
   PXB_REQUIRE(m->groups == ((int64_t(m->num_units) + (int64_t(1) << m->chunk_bits) - 1) >> m->chunk_bits),
               "%s: groups does not match num_units and chunk_bits", fn);
-  PXB_REQUIRE(m->entries % 4 == 0, "%s: entries must be a multiple of 4", fn);
+  PXB_REQUIRE(m->entries % 8 == 0, "%s: entries must be a multiple of 8", fn);
   int bits = 0;
   while ((int64_t(1) << bits) < m->num_units) ++bits;
   PXB_REQUIRE(bits + m->chunk_bits <= 32, "%s: unit ids need %d bits, too many for %d chunk bits", fn, bits,
@@ -332,9 +327,18 @@ extern "C" int pxb_mirror_forward(const pxb_mirror *mirror, const float *act, in
   const size_t smem = sizeof(float) << m.cb;
   if (m.entries > 0) {
     const int64_t full = int64_t(sm_count()) * 8;
-    const int64_t want = (m.entries / 4 + 1023) / 1024;  // at least 4 K entries per CTA
+    const int64_t want = (m.entries / 8 + 511) / 512;  // at least 4 K entries per CTA
     const int grid = static_cast<int>(want < full ? (want > 0 ? want : 1) : full);
-#define PXB_MF(M, P) mirror_forward_kernel<M, P><<<grid, 256, smem, st>>>(m, act, acc, p)
+#define PXB_MF(M, P)                                                                              \
+  do {                                                                                            \
+    static bool carve_##M##P = false;                                                             \
+    if (!carve_##M##P) {                                                                          \
+      cudaFuncSetAttribute(mirror_forward_kernel<M, P>, cudaFuncAttributePreferredSharedMemoryCarveout, \
+                           cudaSharedmemCarveoutMaxShared);                                       \
+      carve_##M##P = true;                                                                        \
+    }                                                                                             \
+    mirror_forward_kernel<M, P><<<grid, 256, smem, st>>>(m, act, acc, p);                         \
+  } while (0)
     const bool pr = prune_kind != PXB_PRUNE_NONE;
     if (monoid == PXB_MONOID_SUM) { if (pr) PXB_MF(PXB_MONOID_SUM, true); else PXB_MF(PXB_MONOID_SUM, false); }
     else if (monoid == PXB_MONOID_MAX) { if (pr) PXB_MF(PXB_MONOID_MAX, true); else PXB_MF(PXB_MONOID_MAX, false); }

@@ -1,10 +1,11 @@
 """The destination-grouped mirror of a bucket (see csrc/mirror.cu).
 
-Built once from the canonical columns with device-side sorts (setup, not the
-step), then kept current by the fused prune and the claim's inserts. Live
-edges are grouped by destination chunk, in slot order within a group; each
-group gets `slack` spare entries (at least `min_slack`, a multiple of 4)
-for the edges growth will insert before the next rebuild.
+Built once from the canonical columns with one device-side sort (setup, not
+the step), then kept current by the fused prune and the claim's inserts.
+Live edges are grouped by destination chunk and sorted by (destination,
+source) inside a group, so the sweep's per-thread runs of one destination
+are long; each group gets `slack` spare entries (at least `min_slack`,
+rounded to a multiple of 8) for the edges growth inserts.
 """
 
 from __future__ import annotations
@@ -34,12 +35,12 @@ class Mirror:
         ok = (f >= 0) & (f < n) & (t >= 0) & (t < n)
         live, f, t = live[ok], f[ok], t[ok]
         g = t >> cb
-        order = torch.sort(g, stable=True).indices
+        order = torch.sort((t << src_bits) | f, stable=True).indices  # (group, dst, src)
         live, f, t, g = live[order], f[order], t[order], g[order]
         counts = torch.bincount(g, minlength=groups)
         counts_h = counts.cpu().numpy().astype(np.int64)
         spare = np.maximum(min_slack, np.ceil(counts_h * slack).astype(np.int64))
-        gcap = (counts_h + spare + 3) // 4 * 4
+        gcap = (counts_h + spare + 7) // 8 * 8
         gbase = np.concatenate([[0], np.cumsum(gcap)]).astype(np.int64)
         entries = int(gbase[-1])
         starts = torch.from_numpy(np.concatenate([[0], np.cumsum(counts_h)[:-1]])).to(dev)
@@ -57,7 +58,7 @@ class Mirror:
         ib, ie, ig = [], [], []
         for grp in range(groups):
             lo, hi = int(gbase[grp]), int(gbase[grp + 1])
-            step = max(4, item_entries // 4 * 4)
+            step = max(8, item_entries // 8 * 8)
             for b in range(lo, hi, step):
                 ib.append(b)
                 ie.append(min(b + step, hi))
