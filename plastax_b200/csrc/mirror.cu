@@ -98,6 +98,27 @@ __device__ __forceinline__ void tombstone(const MPrune &p, int32_t slot, int32_t
   if (p.pruned) atomicAdd(p.pruned, 1);
 }
 
+// Inclusive segmented combine across the warp of runs keyed by destination
+// (equal keys in lane order form a segment); `tail` marks a segment's last lane.
+template <int MONOID>
+__device__ __forceinline__ float warp_segmented_run(float val, int32_t key, bool &tail, int lane) {
+  const unsigned full = 0xffffffffu;
+  const int32_t prev_key = __shfl_up_sync(full, key, 1);
+  const int32_t next_key = __shfl_down_sync(full, key, 1);
+  bool flag = lane == 0 || prev_key != key;
+  tail = lane == 31 || next_key != key;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const float ov = __shfl_up_sync(full, val, off);
+    const bool of = __shfl_up_sync(full, flag, off);
+    if (lane >= off && !flag) {
+      val = combine2<MONOID>(ov, val);
+      flag = of;
+    }
+  }
+  return val;
+}
+
 template <int MONOID>
 __device__ __forceinline__ void smem_combine(float *a, float v) {
   if (MONOID == PXB_MONOID_SUM) atomicAdd(a, v);
@@ -157,9 +178,21 @@ __global__ void __launch_bounds__(256) mirror_forward_kernel(MirrorK m, const fl
     for (int u = threadIdx.x; u < chunk; u += blockDim.x) acc_s[u] = ident;
     __syncthreads();
     const int gi = static_cast<int>(g);
-    for (int64_t o = a_o + threadIdx.x; o < b_o; o += blockDim.x) {
-      const uint4 wa = __ldcs(w4 + 2 * o), wb = __ldcs(w4 + 2 * o + 1);
-      const float4 fa = __ldcs(f4 + 2 * o), fb = __ldcs(f4 + 2 * o + 1);
+    const int lane = threadIdx.x & 31;
+    // every lane of a warp runs the same number of iterations (the warp-wide
+    // segmented reduction below needs all 32 lanes)
+    const int64_t iters = (b_o - a_o + blockDim.x - 1) / blockDim.x;
+    for (int64_t itn = 0; itn < iters; ++itn) {
+      const int64_t o = a_o + itn * blockDim.x + threadIdx.x;
+      const bool in = o < b_o;
+      uint4 wa = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty), wb = wa;
+      float4 fa = make_float4(0.f, 0.f, 0.f, 0.f), fb = fa;
+      if (in) {
+        wa = __ldcs(w4 + 2 * o);
+        wb = __ldcs(w4 + 2 * o + 1);
+        fa = __ldcs(f4 + 2 * o);
+        fb = __ldcs(f4 + 2 * o + 1);
+      }
       const uint32_t ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
       const float fs[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
       float av[8];
@@ -177,7 +210,7 @@ __global__ void __launch_bounds__(256) mirror_forward_kernel(MirrorK m, const fl
         const uint32_t dl = ws[i] & mask;
         const float v = __fmul_rn(fs[i], av[i]);
         if (dl != cur) {
-          if (cur != kEmpty) smem_combine<MONOID>(acc_s + cur, run);
+          if (cur != kEmpty) smem_combine<MONOID>(acc_s + cur, run);  // a run complete inside this thread
           cur = dl;
           run = v;
         } else {
@@ -185,7 +218,13 @@ __global__ void __launch_bounds__(256) mirror_forward_kernel(MirrorK m, const fl
         }
         prune_entry<PRUNE>(m, p, gi, gb, src, dl, fs[i], o * 8 + i);
       }
-      if (cur != kEmpty) smem_combine<MONOID>(acc_s + cur, run);
+      // the last run of each lane usually continues across lanes (rows are
+      // sorted by destination): one segmented combine over the warp, one
+      // shared atomic per segment
+      const int32_t key = cur == kEmpty ? -1 : static_cast<int32_t>(cur);
+      bool tail;
+      const float part = warp_segmented_run<MONOID>(run, key, tail, lane);
+      if (tail && key >= 0) smem_combine<MONOID>(acc_s + key, part);
     }
     __syncthreads();
     const int32_t base = gi << m.cb;
