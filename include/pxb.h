@@ -276,6 +276,18 @@ PXB_API int pxb_select_step(int64_t n, const int32_t *perm, const float *score,
                     int32_t *win_count, void *scratch, size_t scratch_bytes,
                     void *stream);
 
+/* The first min(k, n) candidates of the total order when (score, src)
+ * already orders them, i.e. src is distinct per candidate (per-unit
+ * proposals with one proposal per unit): out_idx lists them in the total
+ * order. Exact radix select of the k-th unique key (score key, src) in
+ * 11-bit digits, one compaction, one sort of the winners. Same output as
+ * the first k of pxb_total_order on such candidates. */
+PXB_API int pxb_topk_unique_scratch_bytes(int64_t n, int64_t k, int32_t id_bound,
+                                  size_t *bytes);
+PXB_API int pxb_topk_unique(int64_t n, const float *score, const int32_t *src,
+                    int32_t id_bound, int64_t k, int32_t *out_idx,
+                    void *scratch, size_t scratch_bytes, void *stream);
+
 /* growth init rules for a committed edge's weight (the rule's `init`) */
 #define PXB_INIT_CONST 0         /* w = a                                      */
 #define PXB_INIT_DYADIC 1        /* w = (((3*src + 5*dst) mod 16) - 8) / 8     */

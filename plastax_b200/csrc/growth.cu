@@ -250,9 +250,190 @@ __global__ void gather_winners_kernel(int64_t k, int64_t count, const int32_t *_
   }
 }
 
+// ---------------------------------------------------------------------------
+// top-k by unique 64-bit keys: exact radix select of the k-th key, one
+// compaction, a sort of the k winners only
+// ---------------------------------------------------------------------------
+constexpr int kSelBits = 11;
+constexpr int kSelBins = 1 << kSelBits;
+
+struct SelState {
+  unsigned long long prefix;  // selected high digits so far
+  long long remaining;        // rank still to find inside the prefix
+  unsigned long long thr;     // final k-th key
+  int count;                  // compaction cursor
+};
+
+__global__ void unique_key_kernel(int64_t n, const float *__restrict__ score, const int32_t *__restrict__ src,
+                                  int src_bits, uint64_t *__restrict__ keys) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    keys[i] = (static_cast<uint64_t>(score_key(score[i])) << src_bits) |
+              (static_cast<uint64_t>(static_cast<uint32_t>(src[i])) & ((uint64_t(1) << src_bits) - 1));
+}
+
+__global__ void sel_histogram_kernel(int64_t n, const uint64_t *__restrict__ keys, int shift, int width,
+                                     int hi_shift, const SelState *__restrict__ st, unsigned int *__restrict__ hist) {
+  __shared__ unsigned int h[kSelBins];
+  for (int b = threadIdx.x; b < kSelBins; b += blockDim.x) h[b] = 0;
+  __syncthreads();
+  const unsigned long long prefix = st->prefix;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t key = keys[i];
+    if (hi_shift >= 64 || (key >> hi_shift) == prefix) atomicAdd(&h[(key >> shift) & ((1u << width) - 1u)], 1u);
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < kSelBins; b += blockDim.x)
+    if (h[b]) atomicAdd(hist + b, h[b]);
+}
+
+// one block: find the bin holding rank `remaining`, extend the prefix
+__global__ void sel_pick_kernel(unsigned int *__restrict__ hist, SelState *__restrict__ st, int last, int width) {
+  __shared__ unsigned int part[1024];
+  const int t = threadIdx.x;  // 1024 threads, 2 bins each
+  const unsigned int a = hist[2 * t], b = hist[2 * t + 1];
+  part[t] = a + b;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {  // inclusive scan
+    const unsigned int v = t >= off ? part[t - off] : 0u;
+    __syncthreads();
+    part[t] += v;
+    __syncthreads();
+  }
+  const long long rem = st->remaining;
+  const long long before = t ? part[t - 1] : 0;
+  __syncthreads();
+  if (before <= rem && rem < before + a + b) {
+    int bin;
+    long long below;
+    if (rem < before + a) { bin = 2 * t; below = before; }
+    else { bin = 2 * t + 1; below = before + a; }
+    st->prefix = (st->prefix << width) | static_cast<unsigned long long>(bin);
+    st->remaining = rem - below;
+    if (last) st->thr = st->prefix;
+  }
+  hist[2 * t] = 0;
+  hist[2 * t + 1] = 0;
+}
+
+__global__ void sel_compact_kernel(int64_t n, const uint64_t *__restrict__ keys, SelState *__restrict__ st,
+                                   uint64_t *__restrict__ out_keys, int32_t *__restrict__ out_idx) {
+  const unsigned long long thr = st->thr;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t key = keys[i];
+    const bool take = key <= thr;
+    const unsigned mask = __ballot_sync(__activemask(), take);
+    if (!take) continue;
+    const int lane = threadIdx.x & 31;
+    const int leader = __ffs(mask) - 1;
+    int base = 0;
+    if (lane == leader) base = atomicAdd(&st->count, __popc(mask));
+    base = __shfl_sync(mask, base, leader);
+    const int pos = base + __popc(mask & ((1u << lane) - 1u));
+    out_keys[pos] = key;
+    out_idx[pos] = static_cast<int32_t>(i);
+  }
+}
+
+__global__ void sel_init_kernel(SelState *st, long long k) {
+  st->prefix = 0;
+  st->remaining = k - 1;  // rank of the k-th key (0-based)
+  st->thr = 0;
+  st->count = 0;
+}
+
+struct TopkScratch {
+  uint64_t *keys, *ckeys, *skeys;
+  int32_t *cidx;
+  SelState *st;
+  unsigned int *hist;
+  void *cub_tmp;
+  size_t cub_bytes, total;
+};
+
+static int topk_scratch(int64_t n, int64_t k, int key_bits, char *base, TopkScratch *o, int32_t *probe_out) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = off;
+    off = align_up(off + (bytes ? bytes : 1), 256);
+    return base ? base + at : nullptr;
+  };
+  const int64_t kk = k > 0 ? k : 1;
+  o->keys = reinterpret_cast<uint64_t *>(take(n * 8));
+  o->ckeys = reinterpret_cast<uint64_t *>(take(kk * 8));
+  o->skeys = reinterpret_cast<uint64_t *>(take(kk * 8));
+  o->cidx = reinterpret_cast<int32_t *>(take(kk * 4));
+  o->st = reinterpret_cast<SelState *>(take(sizeof(SelState)));
+  o->hist = reinterpret_cast<unsigned int *>(take(kSelBins * 4));
+  size_t t = 0;
+  if (cub::DeviceRadixSort::SortPairs(nullptr, t, o->ckeys, o->skeys, o->cidx, probe_out, static_cast<int>(kk), 0,
+                                      key_bits) != cudaSuccess)
+    return PXB_ECUDA;
+  o->cub_bytes = t;
+  o->cub_tmp = take(t);
+  o->total = off;
+  return PXB_OK;
+}
+
 }  // namespace pxb
 
 using namespace pxb;
+
+extern "C" int pxb_topk_unique_scratch_bytes(int64_t n, int64_t k, int32_t id_bound, size_t *bytes) {
+  PXB_REQUIRE(bytes && n >= 0 && k >= 0 && n < (int64_t(1) << 31) && id_bound >= 1,
+              "pxb_topk_unique_scratch_bytes: bad arguments");
+  TopkScratch o;
+  const int key_bits = 32 + bits_for(id_bound);
+  if (topk_scratch(n, k < n ? k : n, key_bits, nullptr, &o, nullptr) != PXB_OK) {
+    set_error("pxb_topk_unique_scratch_bytes: CUB size query failed");
+    return PXB_ECUDA;
+  }
+  *bytes = o.total;
+  return PXB_OK;
+}
+
+extern "C" int pxb_topk_unique(int64_t n, const float *score, const int32_t *src, int32_t id_bound, int64_t k,
+                               int32_t *out_idx, void *scratch, size_t scratch_bytes, void *stream) {
+  PXB_REQUIRE(n >= 0 && k >= 0 && n < (int64_t(1) << 31) && id_bound >= 1, "pxb_topk_unique: bad sizes");
+  const int64_t kk = k < n ? k : n;
+  if (kk == 0) return PXB_OK;
+  PXB_REQUIRE(score && src && out_idx && scratch, "pxb_topk_unique: a pointer is NULL");
+  const int src_bits = bits_for(id_bound);
+  const int key_bits = 32 + src_bits;
+  TopkScratch o;
+  if (topk_scratch(n, kk, key_bits, static_cast<char *>(scratch), &o, out_idx) != PXB_OK) {
+    set_error("pxb_topk_unique: CUB size query failed");
+    return PXB_ECUDA;
+  }
+  PXB_REQUIRE(o.total <= scratch_bytes, "pxb_topk_unique: scratch has %zu bytes, needs %zu", scratch_bytes, o.total);
+  cudaStream_t st = as_stream(stream);
+  const int grid = grid_for(n, 256, 4);
+  unique_key_kernel<<<grid, 256, 0, st>>>(n, score, src, src_bits, o.keys);
+  PXB_LAUNCHED("unique_key_kernel");
+  sel_init_kernel<<<1, 1, 0, st>>>(o.st, kk);
+  PXB_LAUNCHED("sel_init_kernel");
+  PXB_CUDA(cudaMemsetAsync(o.hist, 0, kSelBins * 4, st));
+  // digits of up to 11 bits from the most significant end; a pass counts
+  // the keys whose higher digits equal the prefix picked so far
+  for (int rem_bits = key_bits; rem_bits > 0;) {
+    const int width = rem_bits < kSelBits ? rem_bits : kSelBits;
+    const int shift = rem_bits - width;
+    const int hi_shift = rem_bits >= key_bits ? 64 : rem_bits;
+    sel_histogram_kernel<<<grid, 256, 0, st>>>(n, o.keys, shift, width, hi_shift, o.st, o.hist);
+    PXB_LAUNCHED("sel_histogram_kernel");
+    sel_pick_kernel<<<1, 1024, 0, st>>>(o.hist, o.st, shift == 0, width);
+    PXB_LAUNCHED("sel_pick_kernel");
+    rem_bits = shift;
+  }
+  sel_compact_kernel<<<grid, 256, 0, st>>>(n, o.keys, o.st, o.ckeys, o.cidx);
+  PXB_LAUNCHED("sel_compact_kernel");
+  size_t tb = o.cub_bytes;
+  PXB_CUDA(cub::DeviceRadixSort::SortPairs(o.cub_tmp, tb, o.ckeys, o.skeys, o.cidx, out_idx, static_cast<int>(kk), 0,
+                                           key_bits, st));
+  return PXB_OK;
+}
 
 extern "C" int pxb_philox32(int64_t n, const uint64_t *seed, const uint64_t *counter, uint32_t *out,
                             void *stream) {

@@ -98,27 +98,6 @@ __device__ __forceinline__ void tombstone(const MPrune &p, int32_t slot, int32_t
   if (p.pruned) atomicAdd(p.pruned, 1);
 }
 
-// Inclusive segmented combine across the warp of runs keyed by destination
-// (equal keys in lane order form a segment); `tail` marks a segment's last lane.
-template <int MONOID>
-__device__ __forceinline__ float warp_segmented_run(float val, int32_t key, bool &tail, int lane) {
-  const unsigned full = 0xffffffffu;
-  const int32_t prev_key = __shfl_up_sync(full, key, 1);
-  const int32_t next_key = __shfl_down_sync(full, key, 1);
-  bool flag = lane == 0 || prev_key != key;
-  tail = lane == 31 || next_key != key;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const float ov = __shfl_up_sync(full, val, off);
-    const bool of = __shfl_up_sync(full, flag, off);
-    if (lane >= off && !flag) {
-      val = combine2<MONOID>(ov, val);
-      flag = of;
-    }
-  }
-  return val;
-}
-
 template <int MONOID>
 __device__ __forceinline__ void smem_combine(float *a, float v) {
   if (MONOID == PXB_MONOID_SUM) atomicAdd(a, v);
@@ -126,28 +105,31 @@ __device__ __forceinline__ void smem_combine(float *a, float v) {
   else atomic_min_f32(a, v);
 }
 
-// Fused prune of one entry (rare path): empty the mirror entry, record the
-// canonical tombstone, push the entry on its group's hole stack.
-template <bool PRUNE>
-__device__ __forceinline__ void prune_entry(const MirrorK &m, const MPrune &p, int32_t g, int64_t gb, uint32_t src,
-                                            uint32_t dl, float w, int64_t pos) {
-  if (!PRUNE) return;
-  const int32_t dst = (g << m.cb) | static_cast<int32_t>(dl);
-  if (dst < m.n && mprune_pred(p, w, dst)) {
-    m.word[pos] = kEmpty;
-    tombstone(p, m.slot[pos], static_cast<int32_t>(src));
-    const int32_t h = atomicAdd(m.hcount + g, 1);
-    m.hstack[gb + h] = static_cast<int32_t>(pos - gb);
+// One entry of the sweep: gather, shared-memory combine, fused prune.
+template <int MONOID, bool PRUNE>
+__device__ __forceinline__ void sweep_entry(const MirrorK &m, const MPrune &p, float *acc_s, int32_t g, int64_t gb,
+                                            uint32_t mask, uint32_t word, float w, float a, int64_t pos) {
+  if (word == kEmpty) return;
+  const uint32_t src = word >> m.cb;
+  if (src >= static_cast<uint32_t>(m.n)) return;
+  const uint32_t dl = word & mask;
+  smem_combine<MONOID>(acc_s + dl, __fmul_rn(w, a));
+  if (PRUNE) {
+    const int32_t dst = (g << m.cb) | static_cast<int32_t>(dl);
+    if (dst < m.n && mprune_pred(p, w, dst)) {
+      m.word[pos] = kEmpty;
+      tombstone(p, m.slot[pos], static_cast<int32_t>(src));
+      const int32_t h = atomicAdd(m.hcount + g, 1);
+      m.hstack[gb + h] = static_cast<int32_t>(pos - gb);
+    }
   }
 }
 
 // Each CTA sweeps an equal contiguous range of the entry array (balanced by
-// construction); each thread owns 8 consecutive entries per iteration (two
-// adjacent 16-byte loads of ids and of weights). Groups are built sorted by
-// destination, so a thread's entries form runs of one destination: a run is
-// summed in registers and combined into the chunk's shared accumulators with
-// one atomic, and the chunk is flushed to global memory when the range
-// crosses into the next group.
+// construction), accumulating into shared memory and flushing the chunk's
+// accumulators whenever its range crosses into the next group. Two quads
+// (8 entries, 2 x 32 B of loads) per thread per iteration keep enough bytes
+// in flight to cover the HBM latency.
 template <int MONOID, bool PRUNE>
 __global__ void __launch_bounds__(256) mirror_forward_kernel(MirrorK m, const float *__restrict__ act,
                                                              float *__restrict__ acc, MPrune p) {
@@ -155,44 +137,35 @@ __global__ void __launch_bounds__(256) mirror_forward_kernel(MirrorK m, const fl
   const int chunk = 1 << m.cb;
   const uint32_t mask = static_cast<uint32_t>(chunk - 1);
   const float ident = monoid_identity(MONOID);
-  const int64_t octs = m.entries / 8;  // entries is a multiple of 8 (groups are)
-  const int64_t per = (octs + gridDim.x - 1) / gridDim.x;
-  const int64_t o_lo = blockIdx.x * per;
-  const int64_t o_hi = o_lo + per < octs ? o_lo + per : octs;
-  if (o_lo >= o_hi) return;
+  const int64_t quads = m.entries / 4;
+  const int64_t per = (quads + gridDim.x - 1) / gridDim.x;
+  const int64_t q_lo = blockIdx.x * per;
+  const int64_t q_hi = q_lo + per < quads ? q_lo + per : quads;
+  if (q_lo >= q_hi) return;
+  // first group whose region holds quad q_lo: the last g with gbase[g] <= 4*q_lo
   int64_t lo = 0, hi = m.groups - 1;
   while (lo < hi) {
     const int64_t mid = (lo + hi + 1) / 2;
-    if (m.gbase[mid] <= o_lo * 8) lo = mid; else hi = mid - 1;
+    if (m.gbase[mid] <= q_lo * 4) lo = mid; else hi = mid - 1;
   }
   const uint4 *w4 = reinterpret_cast<const uint4 *>(m.word);
   const float4 *f4 = reinterpret_cast<const float4 *>(m.w);
-  for (int64_t g = lo; g < m.groups && m.gbase[g] < o_hi * 8; ++g) {
+  for (int64_t g = lo; g < m.groups && m.gbase[g] < q_hi * 4; ++g) {
     const int64_t gb = m.gbase[g], gcap = m.gbase[g + 1] - gb;
     int64_t fill = m.gfill[g];
     fill = fill < gcap ? fill : gcap;
-    const int64_t a_o = gb / 8 > o_lo ? gb / 8 : o_lo;
-    const int64_t e_used = (gb + fill + 7) / 8;
-    const int64_t b_o = e_used < o_hi ? e_used : o_hi;
-    if (a_o >= b_o) continue;
+    const int64_t a_q = gb / 4 > q_lo ? gb / 4 : q_lo;
+    const int64_t e_used = (gb + fill + 3) / 4;
+    const int64_t b_q = e_used < q_hi ? e_used : q_hi;
+    if (a_q >= b_q) continue;
     for (int u = threadIdx.x; u < chunk; u += blockDim.x) acc_s[u] = ident;
     __syncthreads();
     const int gi = static_cast<int>(g);
-    const int lane = threadIdx.x & 31;
-    // every lane of a warp runs the same number of iterations (the warp-wide
-    // segmented reduction below needs all 32 lanes)
-    const int64_t iters = (b_o - a_o + blockDim.x - 1) / blockDim.x;
-    for (int64_t itn = 0; itn < iters; ++itn) {
-      const int64_t o = a_o + itn * blockDim.x + threadIdx.x;
-      const bool in = o < b_o;
-      uint4 wa = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty), wb = wa;
-      float4 fa = make_float4(0.f, 0.f, 0.f, 0.f), fb = fa;
-      if (in) {
-        wa = __ldcs(w4 + 2 * o);
-        wb = __ldcs(w4 + 2 * o + 1);
-        fa = __ldcs(f4 + 2 * o);
-        fb = __ldcs(f4 + 2 * o + 1);
-      }
+    int64_t q = a_q + threadIdx.x;
+    for (; q + blockDim.x < b_q; q += 2 * blockDim.x) {
+      const int64_t q2 = q + blockDim.x;
+      const uint4 wa = __ldcs(w4 + q), wb = __ldcs(w4 + q2);
+      const float4 fa = __ldcs(f4 + q), fb = __ldcs(f4 + q2);
       const uint32_t ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
       const float fs[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
       float av[8];
@@ -201,30 +174,23 @@ __global__ void __launch_bounds__(256) mirror_forward_kernel(MirrorK m, const fl
         const uint32_t src = ws[i] >> m.cb;
         av[i] = (ws[i] != kEmpty && src < static_cast<uint32_t>(m.n)) ? __ldg(act + src) : 0.0f;
       }
-      uint32_t cur = kEmpty;
-      float run = ident;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < 8; ++i)
+        sweep_entry<MONOID, PRUNE>(m, p, acc_s, gi, gb, mask, ws[i], fs[i], av[i], (i < 4 ? q : q2) * 4 + (i & 3));
+    }
+    if (q < b_q) {
+      const uint4 wa = __ldcs(w4 + q);
+      const float4 fa = __ldcs(f4 + q);
+      const uint32_t ws[4] = {wa.x, wa.y, wa.z, wa.w};
+      const float fs[4] = {fa.x, fa.y, fa.z, fa.w};
+      float av[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
         const uint32_t src = ws[i] >> m.cb;
-        if (ws[i] == kEmpty || src >= static_cast<uint32_t>(m.n)) continue;
-        const uint32_t dl = ws[i] & mask;
-        const float v = __fmul_rn(fs[i], av[i]);
-        if (dl != cur) {
-          if (cur != kEmpty) smem_combine<MONOID>(acc_s + cur, run);  // a run complete inside this thread
-          cur = dl;
-          run = v;
-        } else {
-          run = combine2<MONOID>(run, v);
-        }
-        prune_entry<PRUNE>(m, p, gi, gb, src, dl, fs[i], o * 8 + i);
+        av[i] = (ws[i] != kEmpty && src < static_cast<uint32_t>(m.n)) ? __ldg(act + src) : 0.0f;
       }
-      // the last run of each lane usually continues across lanes (rows are
-      // sorted by destination): one segmented combine over the warp, one
-      // shared atomic per segment
-      const int32_t key = cur == kEmpty ? -1 : static_cast<int32_t>(cur);
-      bool tail;
-      const float part = warp_segmented_run<MONOID>(run, key, tail, lane);
-      if (tail && key >= 0) smem_combine<MONOID>(acc_s + key, part);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sweep_entry<MONOID, PRUNE>(m, p, acc_s, gi, gb, mask, ws[i], fs[i], av[i], q * 4 + i);
     }
     __syncthreads();
     const int32_t base = gi << m.cb;
@@ -366,7 +332,7 @@ extern "C" int pxb_mirror_forward(const pxb_mirror *mirror, const float *act, in
   const size_t smem = sizeof(float) << m.cb;
   if (m.entries > 0) {
     const int64_t full = int64_t(sm_count()) * 8;
-    const int64_t want = (m.entries / 8 + 511) / 512;  // at least 4 K entries per CTA
+    const int64_t want = (m.entries / 4 + 1023) / 1024;  // at least 4 K entries per CTA
     const int grid = static_cast<int>(want < full ? (want > 0 ? want : 1) : full);
 #define PXB_MF(M, P)                                                                              \
   do {                                                                                            \

@@ -241,6 +241,25 @@ def total_order(score: torch.Tensor, src: torch.Tensor, dst: torch.Tensor, id_bo
     return perm
 
 
+def topk_unique_scratch(n: int, k: int, id_bound: int) -> int:
+    return query_size("pxb_topk_unique_scratch_bytes", ctypes.c_int64(n), ctypes.c_int64(k), ctypes.c_int32(id_bound))
+
+
+def topk_unique(score: torch.Tensor, src: torch.Tensor, id_bound: int, k: int, out: torch.Tensor | None = None,
+                scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """First min(k, n) of the total order for candidates with distinct src."""
+    n = score.numel()
+    kk = min(k, n)
+    if out is None:
+        out = torch.empty(max(kk, 1), dtype=torch.int32, device=score.device)
+    need = topk_unique_scratch(n, k, id_bound)
+    if scratch is None or scratch.numel() < need:
+        scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=score.device)
+    call("pxb_topk_unique", ctypes.c_int64(n), ptr(score), ptr(src), ctypes.c_int32(id_bound), ctypes.c_int64(k),
+         ptr(out), ptr(scratch), ctypes.c_size_t(scratch.numel()), _stream())
+    return out[:kk]
+
+
 def select_step_scratch(n: int, k: int) -> int:
     return query_size("pxb_select_step_scratch_bytes", ctypes.c_int64(n), ctypes.c_int64(k))
 

@@ -2,10 +2,12 @@
 
 Built once from the canonical columns with one device-side sort (setup, not
 the step), then kept current by the fused prune and the claim's inserts.
-Live edges are grouped by destination chunk and sorted by (destination,
-source) inside a group, so the sweep's per-thread runs of one destination
-are long; each group gets `slack` spare entries (at least `min_slack`,
-rounded to a multiple of 8) for the edges growth inserts.
+Live edges are grouped by destination chunk and kept in slot order (source-
+major, as the builder lays the bucket out) inside a group: consecutive
+entries then read neighbouring activations, so the sweep's gathers coalesce
+(a destination-sorted group makes every gather its own L2 sector and was
+measured 3.5x slower). Each group gets `slack` spare entries (at least
+`min_slack`, rounded to a multiple of 8) for the edges growth inserts.
 """
 
 from __future__ import annotations
@@ -35,7 +37,7 @@ class Mirror:
         ok = (f >= 0) & (f < n) & (t >= 0) & (t < n)
         live, f, t = live[ok], f[ok], t[ok]
         g = t >> cb
-        order = torch.sort((t << src_bits) | f, stable=True).indices  # (group, dst, src)
+        order = torch.sort(g, stable=True).indices  # group, then slot order
         live, f, t, g = live[order], f[order], t[order], g[order]
         counts = torch.bincount(g, minlength=groups)
         counts_h = counts.cpu().numpy().astype(np.int64)

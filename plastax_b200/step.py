@@ -165,9 +165,16 @@ class StepFn:
         self.cand = (torch.empty(self.n_cand, dtype=torch.int32, device=dev),
                      torch.empty(self.n_cand, dtype=torch.int32, device=dev),
                      torch.empty(self.n_cand, dtype=torch.float32, device=dev))
-        self.perm = torch.empty(self.n_cand, dtype=torch.int32, device=dev)
-        self.order_scratch = torch.empty(max(K.total_order_scratch(self.n_cand, n), 1), dtype=torch.uint8,
-                                         device=dev)
+        dst_n = ac.dst_n if ac.dst_n is not None else n - ac.dst_lo
+        if ac.dst_lo < 0 or dst_n < 1 or ac.dst_lo + dst_n > n:
+            raise ValueError(f"ProposeAddConn: destinations [{ac.dst_lo}, {ac.dst_lo + dst_n}) exceed the {n} units")
+        # One proposal per unit: every candidate's source is its own unit, so
+        # (score, src) is a unique key in the total order and a radix select
+        # of the first k replaces the full sort.
+        self.unique_src = P == 1
+        self.perm = torch.empty(self.n_cand if not self.unique_src else max(self.k, 1), dtype=torch.int32, device=dev)
+        need = K.topk_unique_scratch(self.n_cand, self.k, n) if self.unique_src else K.total_order_scratch(self.n_cand, n)
+        self.order_scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
         self.win = torch.empty(max(self.k, 1), dtype=torch.int32, device=dev)
         self.sel_scratch = torch.empty(max(K.select_step_scratch(self.n_cand, self.k), 1), dtype=torch.uint8,
                                        device=dev)
@@ -357,8 +364,11 @@ class StepFn:
                            allow_self_loops=ac.allow_self_loops,
                            src_level_bound=0 if self.pipeline else self.num_buckets, out=self.cand)
         src, dst, score = self.cand
-        K.total_order(score, src, dst, n, perm=self.perm, scratch=self.order_scratch)
-        K.select_step(self.perm, score, src, level, self.k, win=self.win, scratch=self.sel_scratch,
+        if self.unique_src:
+            top = K.topk_unique(score, src, n, self.k, out=self.perm, scratch=self.order_scratch)
+        else:
+            top = K.total_order(score, src, dst, n, perm=self.perm, scratch=self.order_scratch)
+        K.select_step(top, score, src, level, self.k, win=self.win, scratch=self.sel_scratch,
                       num_levels=self.static.num_levels)
         kk = min(self.k, self.n_cand)
         K.gather_winners(self.win, kk, self.k, src, dst, score, init_kind=self.init_kind, init_a=self.init_a,

@@ -267,6 +267,23 @@ def test_total_order(cuda, m, id_bound):
     np.testing.assert_array_equal(got.cpu().numpy(), ref)
 
 
+@pytest.mark.parametrize("m,k", [(1_048_592, 268_435), (5000, 4999), (5000, 5000), (70_000, 1), (300_000, 150_000)])
+def test_topk_unique_is_the_total_order_prefix(cuda, m, k):
+    """Distinct sources (one proposal per unit): the radix-selected top k is
+    exactly the first k of the oracle's total order."""
+    import torch
+
+    kern = _k()
+    rng = np.random.default_rng(17)
+    score = _adversarial_scores(rng, m)
+    src = rng.permutation(m).astype(np.int32)
+    dst = rng.integers(0, m, m).astype(np.int32)
+    ref = orc.total_order(score, src, dst)[:k]
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    got = kern.topk_unique(t(score), t(src), m, k)
+    np.testing.assert_array_equal(got.cpu().numpy(), ref)
+
+
 def test_select_step(cuda):
     import torch
 
