@@ -499,22 +499,22 @@ extern "C" int pxb_total_order_scratch_bytes(int64_t n, int32_t id_bound, size_t
   return PXB_OK;
 }
 
-extern "C" int pxb_total_order(int64_t n, const float *score, const int32_t *src, const int32_t *dst,
-                               int32_t id_bound, int32_t *perm_out, void *scratch, size_t scratch_bytes,
-                               void *stream) {
-  PXB_REQUIRE(n >= 0 && n < (int64_t(1) << 31), "pxb_total_order: n out of range");
-  PXB_REQUIRE(id_bound >= 1, "pxb_total_order: id_bound must be >= 1");
+namespace pxb {
+// The total order over caller-provided scratch (shared by pxb_total_order
+// and its allocation-free variant).
+int total_order_impl(const char *fn, int64_t n, const float *score, const int32_t *src, const int32_t *dst,
+                     int32_t id_bound, int32_t *perm_out, void *scratch, size_t scratch_bytes, cudaStream_t st) {
+  PXB_REQUIRE(n >= 0 && n < (int64_t(1) << 31), "%s: n out of range", fn);
+  PXB_REQUIRE(id_bound >= 1, "%s: id_bound must be >= 1", fn);
   if (n == 0) return PXB_OK;
-  PXB_REQUIRE(score && src && dst && perm_out && scratch, "pxb_total_order: a pointer is NULL");
+  PXB_REQUIRE(score && src && dst && perm_out && scratch, "%s: a pointer is NULL", fn);
   const int bits = bits_for(id_bound);
   OrderScratch o;
   if (order_scratch(n, bits, static_cast<char *>(scratch), &o) != PXB_OK) {
-    set_error("pxb_total_order: CUB size query failed");
+    set_error("%s: CUB size query failed", fn);
     return PXB_ECUDA;
   }
-  PXB_REQUIRE(o.total <= scratch_bytes, "pxb_total_order: scratch has %zu bytes, needs %zu", scratch_bytes,
-              o.total);
-  cudaStream_t st = as_stream(stream);
+  PXB_REQUIRE(o.total <= scratch_bytes, "%s: scratch has %zu bytes, needs %zu", fn, scratch_bytes, o.total);
   const int grid = grid_for(n, 256, 8);
   pair_key_kernel<<<grid, 256, 0, st>>>(n, src, dst, bits, o.pair_in, o.val_a);
   PXB_LAUNCHED("pair_key_kernel");
@@ -527,6 +527,20 @@ extern "C" int pxb_total_order(int64_t n, const float *score, const int32_t *src
   PXB_CUDA(cub::DeviceRadixSort::SortPairs(o.cub_tmp, tb, o.skey_in, o.skey_out, o.val_b, perm_out,
                                            static_cast<int>(n), 0, 32, st));
   return PXB_OK;
+}
+
+size_t total_order_bytes(int64_t n, int32_t id_bound) {
+  OrderScratch o;
+  if (order_scratch(n, bits_for(id_bound), nullptr, &o) != PXB_OK) return ~size_t(0);
+  return o.total;
+}
+}  // namespace pxb
+
+extern "C" int pxb_total_order(int64_t n, const float *score, const int32_t *src, const int32_t *dst,
+                               int32_t id_bound, int32_t *perm_out, void *scratch, size_t scratch_bytes,
+                               void *stream) {
+  return total_order_impl("pxb_total_order", n, score, src, dst, id_bound, perm_out, scratch, scratch_bytes,
+                          as_stream(stream));
 }
 
 extern "C" int pxb_select_step_scratch_bytes(int64_t n, int64_t k, size_t *bytes) {

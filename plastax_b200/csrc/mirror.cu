@@ -334,16 +334,7 @@ extern "C" int pxb_mirror_forward(const pxb_mirror *mirror, const float *act, in
     const int64_t full = int64_t(sm_count()) * 8;
     const int64_t want = (m.entries / 4 + 1023) / 1024;  // at least 4 K entries per CTA
     const int grid = static_cast<int>(want < full ? (want > 0 ? want : 1) : full);
-#define PXB_MF(M, P)                                                                              \
-  do {                                                                                            \
-    static bool carve_##M##P = false;                                                             \
-    if (!carve_##M##P) {                                                                          \
-      cudaFuncSetAttribute(mirror_forward_kernel<M, P>, cudaFuncAttributePreferredSharedMemoryCarveout, \
-                           cudaSharedmemCarveoutMaxShared);                                       \
-      carve_##M##P = true;                                                                        \
-    }                                                                                             \
-    mirror_forward_kernel<M, P><<<grid, 256, smem, st>>>(m, act, acc, p);                         \
-  } while (0)
+#define PXB_MF(M, P) mirror_forward_kernel<M, P><<<grid, 256, smem, st>>>(m, act, acc, p)
     const bool pr = prune_kind != PXB_PRUNE_NONE;
     if (monoid == PXB_MONOID_SUM) { if (pr) PXB_MF(PXB_MONOID_SUM, true); else PXB_MF(PXB_MONOID_SUM, false); }
     else if (monoid == PXB_MONOID_MAX) { if (pr) PXB_MF(PXB_MONOID_MAX, true); else PXB_MF(PXB_MONOID_MAX, false); }
