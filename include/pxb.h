@@ -264,6 +264,19 @@ PXB_API int pxb_total_order(int64_t n, const float *score, const int32_t *src,
                     const int32_t *dst, int32_t id_bound, int32_t *perm_out,
                     void *scratch, size_t scratch_bytes, void *stream);
 
+/* Allocation-free pxb_total_order, for callers that cannot allocate device
+ * memory for the scratch (an FFI handler running under CUDA-graph capture,
+ * a plugin whose host process owns every device allocation): the scratch
+ * is a 16 MiB array inside this library, held on every GPU that loads it
+ * until the process exits. At most 262,144 candidates; larger n is
+ * rejected with PXB_EINVAL. The first call on a device looks the array up
+ * (call it once before any stream capture); all calls share the array, so
+ * calls that overlap on the GPU race. No counterpart in the reference. */
+PXB_API int pxb_total_order_noalloc(int64_t n, const float *score,
+                                    const int32_t *src, const int32_t *dst,
+                                    int32_t id_bound, int32_t *perm_out,
+                                    void *stream);
+
 /* Step-scoped selection (level_cap_scope = "step",
  * src/plastax/phases.py:4891-4903 and level_major :4469-4487): the first
  * min(k, n) candidates of `perm`, relisted by source level ascending

@@ -107,6 +107,7 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     ),
     "pxb_total_order_scratch_bytes": (c_i32, [c_i64, c_i32, ctypes.POINTER(c_size)]),
     "pxb_total_order": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_size, c_ptr]),
+    "pxb_total_order_noalloc": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr]),
     "pxb_topk_unique_scratch_bytes": (c_i32, [c_i64, c_i64, c_i32, ctypes.POINTER(c_size)]),
     "pxb_topk_unique": (c_i32, [c_i64, c_ptr, c_ptr, c_i32, c_i64, c_ptr, c_ptr, c_size, c_ptr]),
     "pxb_select_step_scratch_bytes": (c_i32, [c_i64, c_i64, ctypes.POINTER(c_size)]),
