@@ -242,7 +242,9 @@ PXB_API uint64_t pxb_site_seed(uint64_t network_seed, uint32_t step, uint32_t st
  * direction (0 any, 1 deeper, 2 same_or_deeper), and the topological
  * source-level checks: level[src] == bucket_level when bucket_level >= 0,
  * level[src] < src_level_bound (a bucket exists for it) when the bound is
- * > 0. Invalid or non-finite -> -inf. */
+ * > 0. Invalid or non-finite -> -inf. step_dev (may be NULL): when given,
+ * the step is read from this device int32 instead of `step`, so the same
+ * launch stays valid when replayed from a CUDA graph. */
 PXB_API int pxb_propose_per_unit(int32_t num_units, int32_t proposals,
                          uint64_t network_seed, int32_t step, int32_t dst_lo,
                          int32_t dst_n, int32_t score_kind, const float *grad,
@@ -250,8 +252,8 @@ PXB_API int pxb_propose_per_unit(int32_t num_units, int32_t proposals,
                          const uint8_t *pruned, int32_t max_level_gap,
                          int32_t direction, int32_t allow_self_loops,
                          int32_t bucket_level, int32_t src_level_bound,
-                         int32_t *src_out, int32_t *dst_out, float *score_out,
-                         void *stream);
+                         const int32_t *step_dev, int32_t *src_out,
+                         int32_t *dst_out, float *score_out, void *stream);
 
 /* Scratch bytes for pxb_total_order over n candidates with ids < id_bound. */
 PXB_API int pxb_total_order_scratch_bytes(int64_t n, int32_t id_bound, size_t *bytes);

@@ -103,7 +103,7 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_propose_per_unit": (
         c_i32,
         [c_i32, c_i32, c_u64, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32,
-         c_i32, c_ptr, c_ptr, c_ptr, c_ptr],
+         c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr],
     ),
     "pxb_total_order_scratch_bytes": (c_i32, [c_i64, c_i32, ctypes.POINTER(c_size)]),
     "pxb_total_order": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_size, c_ptr]),

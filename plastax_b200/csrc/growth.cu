@@ -33,6 +33,8 @@ __global__ void philox_kernel(int64_t n, const uint64_t *__restrict__ seed, cons
 struct ProposeArgs {
   int32_t num_units, proposals;
   uint64_t keyed_hi;  // philox32(network_seed, (step << 8) | 1): the site seed's high limb
+  uint64_t network_seed;
+  const int32_t *step_dev;  // when set, the step is read here (graph replay) and keyed_hi derived from it
   int32_t dst_lo, dst_n, score_kind;
   const float *grad, *act;
   const int32_t *level;
@@ -43,6 +45,13 @@ struct ProposeArgs {
 __global__ void propose_per_unit_kernel(ProposeArgs a, int32_t *__restrict__ src_out,
                                         int32_t *__restrict__ dst_out, float *__restrict__ score_out) {
   const int64_t total = static_cast<int64_t>(a.num_units) * a.proposals;
+  if (a.step_dev != nullptr) {
+    __shared__ uint64_t keyed;
+    if (threadIdx.x == 0)
+      keyed = philox32(a.network_seed, (static_cast<uint64_t>(static_cast<uint32_t>(*a.step_dev)) << 8) | 1u);
+    __syncthreads();
+    a.keyed_hi = keyed;
+  }
   for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < total;
        c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int32_t i = static_cast<int32_t>(c / a.proposals);
@@ -453,8 +462,8 @@ extern "C" int pxb_propose_per_unit(int32_t num_units, int32_t proposals, uint64
                                     int32_t dst_lo, int32_t dst_n, int32_t score_kind, const float *grad,
                                     const float *act, const int32_t *level, const uint8_t *pruned,
                                     int32_t max_level_gap, int32_t direction, int32_t allow_self_loops,
-                                    int32_t bucket_level, int32_t src_level_bound, int32_t *src_out,
-                                    int32_t *dst_out, float *score_out, void *stream) {
+                                    int32_t bucket_level, int32_t src_level_bound, const int32_t *step_dev,
+                                    int32_t *src_out, int32_t *dst_out, float *score_out, void *stream) {
   PXB_REQUIRE(num_units >= 0 && proposals >= 0, "pxb_propose_per_unit: negative sizes");
   PXB_REQUIRE(dst_n >= 1, "pxb_propose_per_unit: dst_n must be >= 1");
   PXB_REQUIRE(score_kind >= 0 && score_kind <= 2, "pxb_propose_per_unit: unknown score kind %d", score_kind);
@@ -468,6 +477,8 @@ extern "C" int pxb_propose_per_unit(int32_t num_units, int32_t proposals, uint64
   a.num_units = num_units;
   a.proposals = proposals;
   a.keyed_hi = philox32(network_seed, (static_cast<uint64_t>(static_cast<uint32_t>(step)) << 8) | 1u);
+  a.network_seed = network_seed;
+  a.step_dev = step_dev;
   a.dst_lo = dst_lo;
   a.dst_n = dst_n;
   a.score_kind = score_kind;

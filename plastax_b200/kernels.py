@@ -207,7 +207,7 @@ def propose_per_unit(num_units: int, proposals: int, network_seed: int, step: in
                      score_kind: int, level: torch.Tensor, grad: torch.Tensor | None = None,
                      act: torch.Tensor | None = None, pruned: torch.Tensor | None = None, max_level_gap: int = 1,
                      direction: int = 0, allow_self_loops: bool = False, bucket_level: int = -1,
-                     src_level_bound: int = 0,
+                     src_level_bound: int = 0, step_dev: torch.Tensor | None = None,
                      out: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None
                      ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     total = num_units * proposals
@@ -220,7 +220,7 @@ def propose_per_unit(num_units: int, proposals: int, network_seed: int, step: in
          ctypes.c_uint64(network_seed), ctypes.c_int32(step), ctypes.c_int32(dst_lo), ctypes.c_int32(dst_n),
          ctypes.c_int32(score_kind), ptr(grad), ptr(act), ptr(level), ptr(pruned), ctypes.c_int32(max_level_gap),
          ctypes.c_int32(direction), ctypes.c_int32(1 if allow_self_loops else 0), ctypes.c_int32(bucket_level),
-         ctypes.c_int32(src_level_bound), ptr(src), ptr(dst), ptr(score), _stream())
+         ctypes.c_int32(src_level_bound), ptr(step_dev), ptr(src), ptr(dst), ptr(score), _stream())
     return src, dst, score
 
 

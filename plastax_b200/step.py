@@ -117,6 +117,8 @@ class StepFn:
         self.mirrors: list | None = None
         self.bitmaps: list[torch.Tensor] | None = None
         self._bound: int | None = None
+        self.step_dev = torch.zeros(1, dtype=torch.int32, device=device)
+        self.graph = None  # a captured CUDA graph of the step body (see capture)
         if self.ac is not None:
             self._build_growth()
         self.launches = 0
@@ -137,6 +139,7 @@ class StepFn:
             mode = _lib.CLAIM_PIPELINE if self.pipeline else _lib.CLAIM_TOPOLOGICAL
             self.bitmaps = [K.free_bitmap_build(mode, b, level, state.tail_start, self.num_levels,
                                                 shard_base=st.shard_base(i)) for i, b in enumerate(state.conns)]
+        self.step_dev.fill_(state.step)
         self._bound = id(state)
 
     def invalidate(self) -> None:
@@ -145,6 +148,7 @@ class StepFn:
         self._bound = None
         self.mirrors = None
         self.bitmaps = None
+        self.graph = None
 
     def _bm(self, bucket: int) -> tuple[torch.Tensor | None, torch.Tensor | None]:
         """(free bitmap, the level column naming its rows) of a bucket."""
@@ -362,7 +366,8 @@ class StepFn:
                            score_kind=self.score_kind, level=level, grad=grad, act=units[ACTIVATION.name],
                            pruned=pruned, max_level_gap=ac.max_level_gap, direction=self.direction,
                            allow_self_loops=ac.allow_self_loops,
-                           src_level_bound=0 if self.pipeline else self.num_buckets, out=self.cand)
+                           src_level_bound=0 if self.pipeline else self.num_buckets, step_dev=self.step_dev,
+                           out=self.cand)
         src, dst, score = self.cand
         if self.unique_src:
             top = K.topk_unique(score, src, n, self.k, out=self.perm, scratch=self.order_scratch)
@@ -417,8 +422,8 @@ class StepFn:
                                '(the rule declares on_overflow = "error").')
         return GrowthRemainder(cs, cd, cw, self.claim_ws[0].overflowed)
 
-    def __call__(self, state: NetworkState, inputs: StepInputs) -> StepResult:
-        self._bind(state)
+    def _body(self, state: NetworkState, inputs: StepInputs) -> GrowthRemainder | None:
+        """The device work of one step (no host synchronisation)."""
         self._level = state.units[LEVEL.name]
         self._scatter_inputs(state, inputs)
         self._forward(state)
@@ -427,6 +432,53 @@ class StepFn:
         self._update_conn(state)
         self._prune(state)
         remainder = self._add_conn(state)
+        self.step_dev += 1
+        return remainder
+
+    def capturable(self) -> bool:
+        """Whether every step runs the same device work (a CUDA graph can
+        replay it): growth fires every step and never raises on overflow."""
+        ac = self.ac
+        return ac is None or (ac.trigger == "every_step" and int(getattr(self.net, "structural_interval", 1)) <= 1
+                              and ac.on_overflow != "error")
+
+    def capture(self, state: NetworkState, inputs: StepInputs) -> None:
+        """Capture one step of `state` as a CUDA graph; later calls with the
+        same state replay it (inputs and targets are copied into the graph's
+        input buffers first). Call after at least one eager step, so every
+        kernel and index is initialised; the shapes of `inputs` (and
+        targets) are fixed from then on."""
+        if not self.capturable():
+            raise ValueError("this step's work depends on the step count (trigger or interval); it cannot be "
+                             "replayed from one graph")
+        self._bind(state)
+        x = torch.as_tensor(inputs.inputs, dtype=torch.float32).to(self.dev).reshape(-1).clone()
+        t = None if inputs.targets is None else torch.as_tensor(inputs.targets, dtype=torch.float32).to(
+            self.dev).reshape(-1).clone()
+        self._graph_in = StepInputs(x, t)
+        torch.cuda.synchronize(self.dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._graph_rem = self._body(state, self._graph_in)
+        self.graph = g
+        self._graph_state = id(state)
+
+    def __call__(self, state: NetworkState, inputs: StepInputs) -> StepResult:
+        self._bind(state)
+        if self.graph is not None and self._graph_state == id(state):
+            x = inputs.inputs
+            if not isinstance(x, torch.Tensor):
+                x = torch.from_numpy(np.ascontiguousarray(x, np.float32))
+            self._graph_in.inputs.copy_(x.reshape(-1), non_blocking=True)
+            if inputs.targets is not None and self._graph_in.targets is not None:
+                t = inputs.targets
+                if not isinstance(t, torch.Tensor):
+                    t = torch.from_numpy(np.ascontiguousarray(t, np.float32))
+                self._graph_in.targets.copy_(t.reshape(-1), non_blocking=True)
+            self.graph.replay()
+            remainder = self._graph_rem
+        else:
+            remainder = self._body(state, inputs)
         state.step += 1
         grown = state.grown if state.grown is not None else torch.zeros((), dtype=torch.int32, device=self.dev)
         overflow = state.overflow if state.overflow is not None else torch.zeros((), dtype=torch.bool,

@@ -18,7 +18,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def _run(cuda, cfg, steps, sharded_bands=1):
+def _run(cuda, cfg, steps, sharded_bands=1, graph=False):
     import torch
 
     from oracle.steps import ReservoirOracle
@@ -34,6 +34,8 @@ def _run(cuda, cfg, steps, sharded_bands=1):
     rng = np.random.default_rng(5)
     for i in range(steps):
         x = rng.standard_normal(cfg.num_inputs).astype(np.float32)
+        if graph and i == 1:  # capture after one eager step, replay from then on
+            step.capture(state, StepInputs(x))
         res = step(state, StepInputs(x))
         ref.step(x)
         got = {k: v.cpu().numpy() for k, v in res.state.conns[0].items()}
@@ -51,6 +53,14 @@ def test_reservoir_churn_matches_oracle(cuda, log2, fan_in, churn):
     from plastax_b200.configs import ReservoirConfig
 
     _run(cuda, ReservoirConfig(num_units=1 << log2, fan_in=fan_in, churn=churn, capacity_align=256), steps=6)
+
+
+def test_reservoir_churn_replayed_from_a_cuda_graph_matches_oracle(cuda):
+    """The captured step (device-side step counter keying the proposals)
+    replays the same structure as the eager one, step after step."""
+    from plastax_b200.configs import ReservoirConfig
+
+    _run(cuda, ReservoirConfig(num_units=1 << 12, fan_in=16, churn=0.01, capacity_align=256), steps=6, graph=True)
 
 
 def test_reservoir_overflow_into_tail_exhaustion(cuda):
