@@ -39,10 +39,11 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "propagated edges/sec per step (Scheme-A large reservoir churn step)"
 UNIT = "edges/s"
-# dram bytes per launch of the fused forward+prune kernel, from the ncu capture
-# summarised in profiles/forward_prune_reservoir.md (scaled to a full launch);
-# None until a capture exists.
-NCU_TRAFFIC_BYTES_PER_SLOT = None
+# DRAM bytes (read + write) per swept mirror entry of the fused forward+prune
+# kernel, from one ncu capture of the 2^16-unit reservoir (147.0 MB over
+# 17,859,121 entries per launch); the traffic reported for a full launch is
+# this figure times its swept entries (traffic grows in proportion to them)
+NCU_TRAFFIC_BYTES_PER_ENTRY = 8.23
 
 
 def _env_int(name: str, default: int) -> int:
@@ -80,7 +81,8 @@ def workload_desc(cfg, n_gpus: int) -> dict:
         "churn_per_step": cfg.k,
         "propagation": "pipeline",
         "parallelism": f"scheme_a_conn_shard{n_gpus}",
-        "l2": "inputs larger than L2 (arena 3.7 GB per step)",
+        "l2": f"inputs larger than L2: each rank sweeps {8 * cfg.live_edges / n_gpus / 1e9:.2f} GB of mirror entries "
+              f"per step (L2 126 MB)",
     }
 
 
@@ -248,7 +250,7 @@ def engine_arm(args) -> None:
     if world > 1:
         import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     from plastax_b200 import StepInputs, make_step
     from plastax_b200.configs import build_reservoir
     from plastax_b200.types import ShardSpec
@@ -346,14 +348,13 @@ def engine_arm(args) -> None:
     # launch = 8 B per swept mirror entry (packed ids + weight; the canonical
     # sweep streams 13 B per slot instead) + 8 B per unit (activation read,
     # accumulator written)
-    local_cap = static.local_capacity(0)
     n = static.num_units
     per_entry = 8 if step.use_mirror else 13
     alg_bytes = per_entry * swept_entries + 8 * n
     fwd_avg_s = float(np.mean(fwd_ms)) / 1e3 if fwd_ms else float("nan")
     achieved = alg_bytes / fwd_avg_s / 1e9
     peak, peak_kind = measured_peak_hbm()
-    traffic = None if NCU_TRAFFIC_BYTES_PER_SLOT is None else NCU_TRAFFIC_BYTES_PER_SLOT * local_cap
+    traffic = NCU_TRAFFIC_BYTES_PER_ENTRY * swept_entries if step.use_mirror else None
 
     # launches of this library's kernels per step, counted once by the profiler
     launches_per_step = count_launches(step, state, inputs_dev[0], dev)
@@ -374,10 +375,18 @@ def engine_arm(args) -> None:
         "cuda_graph": use_graph,
         "gpu_launches": launches_per_step * Kst,
     }
+    # a CUDA graph holding NCCL calls must be released before the process
+    # group is destroyed, or the exit waits forever
+    step.release_graph()
+    del step
+    import gc
+
+    gc.collect()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        del state, step
+        del state
         torch.cuda.empty_cache()
         from oracle import oracle as orc
 

@@ -148,7 +148,7 @@ class StepFn:
         self._bound = None
         self.mirrors = None
         self.bitmaps = None
-        self.graph = None
+        self.release_graph()
 
     def _bm(self, bucket: int) -> tuple[torch.Tensor | None, torch.Tensor | None]:
         """(free bitmap, the level column naming its rows) of a bucket."""
@@ -462,6 +462,13 @@ class StepFn:
             self._graph_rem = self._body(state, self._graph_in)
         self.graph = g
         self._graph_state = id(state)
+
+    def release_graph(self) -> None:
+        """Drop the captured graph and its buffers. A graph that holds NCCL
+        calls must be released before the process group is destroyed."""
+        self.graph = None
+        self._graph_rem = None
+        self._graph_in = None
 
     def __call__(self, state: NetworkState, inputs: StepInputs) -> StepResult:
         self._bind(state)
