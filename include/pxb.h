@@ -171,14 +171,22 @@ PXB_API int pxb_backward_update(int64_t cap, const int32_t *from_id,
                         const pxb_optimizer *opt, float *opt_m, float *opt_v,
                         float *opt_t, void *stream);
 
+/* Fractional bits of the exact fixed-point sum accumulators (int64, units
+ * of 2^-PXB_FIXED_FRAC_BITS) that pxb_mirror_forward fills and
+ * pxb_unit_apply reads. */
+#define PXB_FIXED_FRAC_BITS 28
+
 /* Unit apply with masked merge (src/plastax/sweep.py:183-230):
  * a unit i is finalized iff (level == NULL || level[i] == target_level)
  *   && (is_input == NULL || !is_input[i]) && (pruned == NULL || !pruned[i]).
- * forward (mode 0):  out[i] = act_fn(acc[i])
- * backward (mode 1): out[i] = (acc[i] + (seed ? seed[i] : 0)) * act_fn'(act[i])
- * Finalized units have acc[i] reset to the monoid identity. */
+ * The accumulated value x[i] = acc[i], or, when acc_fixed is not NULL,
+ * acc_fixed[i] * 2^-PXB_FIXED_FRAC_BITS + acc[i] rounded once to float.
+ * forward (mode 0):  out[i] = act_fn(x[i])
+ * backward (mode 1): out[i] = (x[i] + (seed ? seed[i] : 0)) * act_fn'(act[i])
+ * Finalized units have acc[i] reset to the monoid identity (and
+ * acc_fixed[i] to 0). */
 PXB_API int pxb_unit_apply(int32_t num_units, int32_t mode, int32_t act_kind,
-                   int32_t monoid, float *acc, const float *act,
+                   int32_t monoid, float *acc, int64_t *acc_fixed, const float *act,
                    const float *seed, const int32_t *level,
                    int32_t target_level, const uint8_t *is_input,
                    const uint8_t *pruned, float *out, void *stream);
@@ -394,17 +402,24 @@ PXB_API int pxb_count_dead(int64_t cap, const uint8_t *dead, int32_t *out,
 /* ------------------------------------------------------------------ */
 /* destination-grouped mirror (the forward sweep's index)              */
 /* ------------------------------------------------------------------ */
+/* Entries per tile of the mirror sweep: group bases and the entry count
+ * are multiples of it. */
+#define PXB_MIRROR_TILE 2048
+
 /* A bucket's live edges grouped by destination chunk (2^chunk_bits
  * consecutive units, chunk_bits <= 13, ceil(log2 num_units) + chunk_bits
- * <= 32). Group g owns entries [gbase[g], gbase[g+1]) (multiples of 8), of
- * which the first gfill[g] have ever been used. Entry e: word[e] = src <<
+ * <= 32). Group g owns entries [gbase[g], gbase[g+1]) (multiples of
+ * PXB_MIRROR_TILE), of which the first gfill[g] have ever been used. Entry e: word[e] = src <<
  * chunk_bits | (dst - g * 2^chunk_bits), or 0xffffffff when empty;
  * weight[e]; slot[e] = the canonical (local) slot it mirrors. hstack at
- * gbase[g] holds hcount[g] free entry offsets of group g. The forward
- * sweeps `items` runs [item_begin, item_end) of group item_group. Edges a
- * full group cannot take go to the overflow list (ovf_*); status[0] bit 0
- * is set when that list is full too (the mirror must be rebuilt). All
- * arrays are device memory owned by the caller. */
+ * gbase[g] holds hcount[g] free entry offsets of group g. items /
+ * item_begin / item_end / item_group describe runs of entries for callers
+ * that split the sweep themselves (the sweep here does not read them).
+ * Edges a full group cannot take go to the overflow list (ovf_*); status[0]
+ * bit 0 is set when that list is full too (the mirror must be rebuilt), bit
+ * 1 when a sweep's pipeline wait timed out (its result is incomplete). All
+ * arrays are device memory owned by the caller; word and weight 16-byte
+ * aligned. */
 typedef struct pxb_mirror {
   int32_t num_units;
   int32_t chunk_bits;
@@ -431,17 +446,24 @@ typedef struct pxb_mirror {
   int32_t *ins_count; /* [groups] zeroed scratch of pxb_mirror_insert */
 } pxb_mirror;
 
-/* Forward accumulate of the mirrored bucket (acc (+)= w * act[src] per
- * destination; the same result as pxb_forward_accumulate up to float
- * summation order) fused with the prune predicate: a pruned edge still
+/* Forward accumulate of the mirrored bucket (w * act[src] combined per
+ * destination) fused with the prune predicate. For sum the products are
+ * accumulated exactly, independent of order: acc_fixed (int64, units of
+ * 2^-PXB_FIXED_FRAC_BITS, non-NULL) += each float32 product rounded to that
+ * unit (exact for |w * act| >= 2^-4), and a product that is not finite or
+ * of magnitude >= 2^20 is added to acc as a float instead; the sum is then
+ * acc_fixed * 2^-PXB_FIXED_FRAC_BITS + acc (pxb_unit_apply reads both).
+ * For max / min, acc (+)= as pxb_forward_accumulate does and acc_fixed is
+ * unused. The prune: a pruned edge still
  * contributes (the forward reads the pre-prune state), then its mirror entry
  * is emptied and pushed on its group's hole stack, and the canonical record
  * is written: dead[slot] = 1, its free-bitmap bit (row bitmap_level[src],
  * or row 0 when bitmap_level is NULL), pruned_count += 1 (may be NULL).
  * Replaces src/plastax/phases.py:2240-2319 and sweep.py:113-180 for a
- * bucket that has a mirror. acc must be 16-byte aligned for sum. */
+ * bucket that has a mirror. */
 PXB_API int pxb_mirror_forward(const pxb_mirror *mirror, const float *act,
-                               int32_t monoid, float *acc, int32_t prune_kind,
+                               int32_t monoid, float *acc, int64_t *acc_fixed,
+                               int32_t prune_kind,
                                float prune_threshold,
                                const float *unit_threshold, uint8_t *dead,
                                uint32_t *free_bitmap, int64_t bitmap_words,

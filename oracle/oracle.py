@@ -116,13 +116,13 @@ class SiteRng:
 # propagation (src/plastax/sweep.py:113-232, phases.py:942-1104)
 # ---------------------------------------------------------------------------
 def forward_accumulate(b: dict, act: np.ndarray, n: int, monoid: str, acc: np.ndarray) -> None:
-    work = np.empty(n, np.float32)
+    work = np.empty(n, np.float64)
     lib().pxo_forward_accumulate(_i64(b["dead"].size), _p(b["from_id"]), _p(b["to_id"]), _p(b["dead"]),
                                  _p(b["weight"]), _p(act), ctypes.c_int32(n), MONOID[monoid], _p(acc), _p(work))
 
 
 def backward_accumulate(b: dict, grad: np.ndarray, n: int, monoid: str, acc: np.ndarray) -> None:
-    work = np.empty(n, np.float32)
+    work = np.empty(n, np.float64)
     lib().pxo_backward_accumulate(_i64(b["dead"].size), _p(b["from_id"]), _p(b["to_id"]), _p(b["dead"]),
                                   _p(b["weight"]), _p(grad), ctypes.c_int32(n), MONOID[monoid], _p(acc),
                                   _p(work))
@@ -270,7 +270,7 @@ def claim_topological(b: dict, level: np.ndarray, src: np.ndarray, dst: np.ndarr
 # CPU baseline (timing only)
 # ---------------------------------------------------------------------------
 def forward_prune_mt(b: dict, act: np.ndarray, n: int, threshold: float, acc: np.ndarray, threads: int) -> None:
-    work = np.empty(max(threads, 1) * n, np.float32)
+    work = np.empty(max(threads, 1) * n, np.float64)
     lib().pxo_forward_prune_mt(_i64(b["dead"].size), _p(b["from_id"]), _p(b["to_id"]), _p(b["dead"]),
                                _p(b["weight"]), _p(act), ctypes.c_int32(n), ctypes.c_float(threshold), _p(acc),
                                ctypes.c_int(threads), _p(work))

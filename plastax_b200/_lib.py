@@ -33,6 +33,8 @@ OPT = {"sgd": 0, "momentum": 1, "adam": 2, "rmsprop": 3}
 SCORE_UNIFORM, SCORE_UNIFORM_Q256, SCORE_GRAD_ACT = 0, 1, 2
 INIT_CONST, INIT_DYADIC, INIT_HASH_UNIFORM = 0, 1, 2
 CLAIM_PIPELINE, CLAIM_TOPOLOGICAL = 0, 1
+MIRROR_TILE = 2048
+FIXED_FRAC_BITS = 28
 
 
 class Mirror(ctypes.Structure):
@@ -88,7 +90,7 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     ),
     "pxb_unit_apply": (
         c_i32,
-        [c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr],
+        [c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr],
     ),
     "pxb_mse_loss": (c_i32, [c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_batched_forward": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_ptr, c_ptr]),
@@ -129,7 +131,7 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     ),
     "pxb_free_bitmap_build": (c_i32, [c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i64, c_ptr, c_ptr, c_ptr]),
     "pxb_mirror_forward": (
-        c_i32, [c_ptr, c_ptr, c_i32, c_ptr, c_i32, c_f32, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr]),
+        c_i32, [c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_i32, c_f32, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr]),
     "pxb_mirror_insert": (c_i32, [c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_count_dead": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr]),
 }

@@ -98,129 +98,360 @@ __device__ __forceinline__ void tombstone(const MPrune &p, int32_t slot, int32_t
   if (p.pruned) atomicAdd(p.pruned, 1);
 }
 
-template <int MONOID>
-__device__ __forceinline__ void smem_combine(float *a, float v) {
-  if (MONOID == PXB_MONOID_SUM) atomicAdd(a, v);
-  else if (MONOID == PXB_MONOID_MAX) atomic_max_f32(a, v);
-  else atomic_min_f32(a, v);
+// The sum is accumulated exactly in fixed point, independent of order. A
+// chunk's shared accumulator is two 32-bit words per unit: lo in units of
+// 2^-28 and hi in units of 1.0 (2^28 lo units); shared-memory integer
+// atomics are native, where a float add is a compare-and-swap loop at a
+// third of the rate. A product of magnitude < 1 is rounded to the nearest
+// unit (exact when >= 2^-4) and added to lo; the adding thread sees a signed
+// wrap of lo exactly, from the value its atomic returns, and carries +-16 (2^32
+// units) into hi. A product in [1, 2^20) is a multiple of 2^-23, so its
+// fixed value is exact: the part above 2^28 units goes to hi, the rest to
+// lo. A product that is not finite or >= 2^20 goes to the float side
+// accumulator. The flush adds hi * 2^28 + lo to the unit's int64 global
+// accumulator; one rounding to float happens in the unit apply.
+constexpr int kFixBits = PXB_FIXED_FRAC_BITS;
+constexpr float kFixScale = 268435456.0f;  // 2^kFixBits
+static_assert(kFixBits == 28, "kFixScale and the carry below assume 28 fractional bits");
+
+__device__ __forceinline__ void lo_add(int32_t *lo, int32_t *hi, int32_t v) {
+  const int32_t old = atomicAdd(lo, v);
+  const int32_t now = static_cast<int32_t>(static_cast<uint32_t>(old) + static_cast<uint32_t>(v));
+  if (((old ^ now) & (v ^ now)) < 0) atomicAdd(hi, v > 0 ? 16 : -16);
 }
 
-// One entry of the sweep: gather, shared-memory combine, fused prune.
-template <int MONOID, bool PRUNE>
-__device__ __forceinline__ void sweep_entry(const MirrorK &m, const MPrune &p, float *acc_s, int32_t g, int64_t gb,
-                                            uint32_t mask, uint32_t word, float w, float a, int64_t pos) {
-  if (word == kEmpty) return;
-  const uint32_t src = word >> m.cb;
-  if (src >= static_cast<uint32_t>(m.n)) return;
-  const uint32_t dl = word & mask;
-  smem_combine<MONOID>(acc_s + dl, __fmul_rn(w, a));
-  if (PRUNE) {
-    const int32_t dst = (g << m.cb) | static_cast<int32_t>(dl);
-    if (dst < m.n && mprune_pred(p, w, dst)) {
-      m.word[pos] = kEmpty;
-      tombstone(p, m.slot[pos], static_cast<int32_t>(src));
-      const int32_t h = atomicAdd(m.hcount + g, 1);
-      m.hstack[gb + h] = static_cast<int32_t>(pos - gb);
+__device__ __forceinline__ void fixed_add(int32_t *lo, int32_t *hi, float *gf, float p) {
+  const float ap = fabsf(p);
+  if (ap < 1.0f) {
+    lo_add(lo, hi, __float2int_rn(p * kFixScale));
+  } else if (ap < 1048576.0f) {
+    const long long v = __float2ll_rn(p * kFixScale);
+    atomicAdd(hi, static_cast<int32_t>(v >> kFixBits));
+    lo_add(lo, hi, static_cast<int32_t>(v & ((1ll << kFixBits) - 1)));
+  } else {
+    atomicAdd(gf, p);
+  }
+}
+
+// The same contribution straight into the global accumulators (the
+// overflow list's edges).
+__device__ __forceinline__ void fixed_add_global(int64_t *af, float *gf, float p) {
+  if (fabsf(p) < 1048576.0f) {
+    atomicAdd(reinterpret_cast<unsigned long long *>(af),
+              static_cast<unsigned long long>(__float2ll_rn(p * kFixScale)));
+  } else {
+    atomicAdd(gf, p);
+  }
+}
+
+template <int MONOID>
+__device__ __forceinline__ void smem_combine(float *acc_s, int chunk, float *acc_g, uint32_t dl, float v) {
+  if (MONOID == PXB_MONOID_SUM) {
+    int32_t *lo = reinterpret_cast<int32_t *>(acc_s);
+    fixed_add(lo + dl, lo + chunk + dl, acc_g + dl, v);
+  } else if (MONOID == PXB_MONOID_MAX) {
+    atomic_max_f32(acc_s + dl, v);
+  } else {
+    atomic_min_f32(acc_s + dl, v);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The sweep: a persistent, warp-specialised kernel. The entry arrays are cut
+// into tiles of kTile entries; group bases are multiples of kTile, so a tile
+// lies in one group. CTA c owns a contiguous run of tiles. One producer thread
+// streams each tile's words and weights (only its used prefix) into a ring of
+// kStages shared-memory stages with cp.async.bulk, completing on the stage's
+// `full` mbarrier; kConsWarps consumer warps gather the activations, combine
+// into the chunk's shared accumulators and release the stage on its `empty`
+// mbarrier. A change of group between two tiles flushes the accumulators to
+// global memory (float4 atomics for sum). Every mbarrier wait is bounded: on
+// timeout the kernel records status bit 1 and stops touching the stage data,
+// while still taking every consumer barrier, so it always terminates.
+// ---------------------------------------------------------------------------
+constexpr int kTile = PXB_MIRROR_TILE;
+constexpr int kStages = 3;
+constexpr int kConsWarps = 8;
+constexpr int kConsThreads = kConsWarps * 32;
+constexpr int kSweepThreads = kConsThreads + 32;
+constexpr uint32_t kWaitPolls = 1u << 24;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Wait for the phase of `parity` to complete, giving up after kWaitPolls polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitPolls; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+// Bulk copy global -> this CTA's shared memory, completing on `bar`; the
+// source is marked evict-first in L2 (it is streamed once per sweep, while
+// the activations it indexes should stay resident).
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                          uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+          "r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsThreads) : "memory"); }
+
+// Advance t to the next tile of [t, t_hi) with used entries; g tracks its
+// group. Producer and consumers walk the same sequence (gfill is not written
+// during the sweep).
+__device__ __forceinline__ bool next_tile(const MirrorK &m, int64_t &t, int64_t t_hi, int64_t &g, int32_t &used) {
+  for (; t < t_hi; ++t) {
+    const int64_t e0 = t * kTile;
+    while (g + 1 < m.groups && __ldg(m.gbase + g + 1) <= e0) ++g;
+    const int64_t off = e0 - __ldg(m.gbase + g);
+    const int64_t fill = __ldg(m.gfill + g);
+    const int64_t u = fill - off;
+    if (u > 0) {
+      used = static_cast<int32_t>(u < kTile ? u : kTile);
+      return true;
+    }
+  }
+  return false;
+}
+
+// One tile of one group, staged in shared memory: each consumer thread takes
+// two quads (8 entries). The gathers of all 8 entries are issued before any
+// combine (an empty word reads a clamped, unused activation instead of
+// branching); the prune predicate only sets a bit per entry, and the rare
+// tombstones are written after the combines. Mirror words are written only
+// by the build and the insert, which keep src < n and dst < n, so the loop
+// carries no range checks (an accumulator past n is dropped at the flush).
+template <int MONOID, int PK>
+__device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, const float *__restrict__ act,
+                                           const uint32_t *word_t, const float *w_t, int used, float *acc_s,
+                                           float *acc_g, int32_t g, int64_t gb, int64_t e0) {
+  const uint32_t mask = (1u << m.cb) - 1u;
+  const int chunk = 1 << m.cb;
+  const uint32_t last = static_cast<uint32_t>(m.n - 1);
+  const int nq = (used + 3) >> 2;
+  const uint4 *wq = reinterpret_cast<const uint4 *>(word_t);
+  const float4 *fq = reinterpret_cast<const float4 *>(w_t);
+  for (int q = threadIdx.x; q < nq; q += 2 * kConsThreads) {
+    const int q2 = q + kConsThreads;
+    const bool two = q2 < nq;
+    const uint4 wa = wq[q];
+    const float4 fa = fq[q];
+    const uint4 wb = two ? wq[q2] : make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
+    const float4 fb = two ? fq[q2] : make_float4(0.f, 0.f, 0.f, 0.f);
+    uint32_t ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    const float fs[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
+    if (used < kTile) {  // the group's used prefix ends inside this tile
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (((j < 4 ? q : q2) * 4 + (j & 3)) >= used) ws[j] = kEmpty;
+    }
+    float av[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) av[j] = __ldg(act + min(ws[j] >> m.cb, last));
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (ws[j] != kEmpty) smem_combine<MONOID>(acc_s, chunk, acc_g, ws[j] & mask, __fmul_rn(fs[j], av[j]));
+    if (PK != PXB_PRUNE_NONE) {
+      // the predicate is rare: one test of the smallest |w| (fminf drops a
+      // NaN, which no predicate prunes) or of any below its destination's
+      // threshold, then the per-entry pass only when it passes
+      bool any;
+      if (PK == PXB_PRUNE_ABS_BELOW) {
+        float mn = fabsf(fs[0]);
+#pragma unroll
+        for (int j = 1; j < 8; ++j) mn = fminf(mn, fabsf(fs[j]));
+        any = mn < p.thr;
+      } else {
+        any = false;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          any |= ws[j] != kEmpty && fabsf(fs[j]) < __ldg(p.unit_thr + ((g << m.cb) | (ws[j] & mask)));
+      }
+      if (any) {
+        for (int j = 0; j < 8; ++j) {
+          if (ws[j] == kEmpty) continue;
+          const float thr = PK == PXB_PRUNE_ABS_BELOW ? p.thr : __ldg(p.unit_thr + ((g << m.cb) | (ws[j] & mask)));
+          if (!(fabsf(fs[j]) < thr)) continue;
+          const int64_t pos = e0 + (j < 4 ? q : q2) * 4 + (j & 3);
+          m.word[pos] = kEmpty;
+          tombstone(p, m.slot[pos], static_cast<int32_t>(ws[j] >> m.cb));
+          const int32_t h = atomicAdd(m.hcount + g, 1);
+          m.hstack[gb + h] = static_cast<int32_t>(pos - gb);
+        }
+      }
     }
   }
 }
 
-// Each CTA sweeps an equal contiguous range of the entry array (balanced by
-// construction), accumulating into shared memory and flushing the chunk's
-// accumulators whenever its range crosses into the next group. Two quads
-// (8 entries, 2 x 32 B of loads) per thread per iteration keep enough bytes
-// in flight to cover the HBM latency.
-template <int MONOID, bool PRUNE>
-__global__ void __launch_bounds__(256) mirror_forward_kernel(MirrorK m, const float *__restrict__ act,
-                                                             float *__restrict__ acc, MPrune p) {
-  extern __shared__ float acc_s[];
+// Flush (unless g < 0) and reset the chunk accumulators; each consumer thread
+// flushes and resets the same indices, so one barrier before and one after.
+template <int MONOID>
+__device__ __forceinline__ void flush_reset(const MirrorK &m, float *acc_s, float *__restrict__ acc,
+                                            int64_t *__restrict__ acc_fixed, int64_t g) {
   const int chunk = 1 << m.cb;
-  const uint32_t mask = static_cast<uint32_t>(chunk - 1);
+  const int32_t base = static_cast<int32_t>(g) << m.cb;
+  if (MONOID == PXB_MONOID_SUM) {
+    int4 *lo4 = reinterpret_cast<int4 *>(acc_s);
+    int4 *hi4 = lo4 + chunk / 4;
+    const int4 z = make_int4(0, 0, 0, 0);
+    for (int u = threadIdx.x; u < chunk / 4; u += kConsThreads) {
+      if (g >= 0) {
+        const int4 l = lo4[u], h = hi4[u];
+        const int32_t ls[4] = {l.x, l.y, l.z, l.w}, hs[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const long long tot = (static_cast<long long>(hs[j]) << kFixBits) + ls[j];
+          if (tot != 0 && base + 4 * u + j < m.n)
+            atomicAdd(reinterpret_cast<unsigned long long *>(acc_fixed + base + 4 * u + j),
+                      static_cast<unsigned long long>(tot));
+        }
+      }
+      lo4[u] = z;
+      hi4[u] = z;
+    }
+    return;
+  }
   const float ident = monoid_identity(MONOID);
-  const int64_t quads = m.entries / 4;
-  const int64_t per = (quads + gridDim.x - 1) / gridDim.x;
-  const int64_t q_lo = blockIdx.x * per;
-  const int64_t q_hi = q_lo + per < quads ? q_lo + per : quads;
-  if (q_lo >= q_hi) return;
-  // first group whose region holds quad q_lo: the last g with gbase[g] <= 4*q_lo
+  float4 *s4 = reinterpret_cast<float4 *>(acc_s);
+  const float4 id4 = make_float4(ident, ident, ident, ident);
+  for (int u = threadIdx.x; u < chunk / 4; u += kConsThreads) {
+    if (g >= 0) {
+      const float4 v = s4[u];
+      const float vs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (vs[j] != ident && base + 4 * u + j < m.n) atomic_combine<MONOID>(acc + base + 4 * u + j, vs[j]);
+    }
+    s4[u] = id4;
+  }
+}
+
+template <int MONOID, int PK>
+__global__ void __launch_bounds__(kSweepThreads, 3) mirror_sweep_kernel(MirrorK m, const float *__restrict__ act,
+                                                                        float *__restrict__ acc,
+                                                                        int64_t *__restrict__ acc_fixed, MPrune p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem_raw);
+  uint64_t *empty = full + kStages;
+  uint32_t *word_s = reinterpret_cast<uint32_t *>(smem_raw + 128);
+  float *w_s = reinterpret_cast<float *>(word_s + kStages * kTile);
+  float *acc_s = w_s + kStages * kTile;
+
+  const int64_t tiles = m.entries / kTile;
+  const int64_t per = (tiles + gridDim.x - 1) / gridDim.x;
+  const int64_t t_lo = blockIdx.x * per;
+  const int64_t t_hi = t_lo + per < tiles ? t_lo + per : tiles;
+  if (t_lo >= t_hi) return;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, kConsWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  // the group of tile t_lo: the last g with gbase[g] <= t_lo * kTile
   int64_t lo = 0, hi = m.groups - 1;
   while (lo < hi) {
     const int64_t mid = (lo + hi + 1) / 2;
-    if (m.gbase[mid] <= q_lo * 4) lo = mid; else hi = mid - 1;
+    if (__ldg(m.gbase + mid) <= t_lo * kTile) lo = mid; else hi = mid - 1;
   }
-  const uint4 *w4 = reinterpret_cast<const uint4 *>(m.word);
-  const float4 *f4 = reinterpret_cast<const float4 *>(m.w);
-  for (int64_t g = lo; g < m.groups && m.gbase[g] < q_hi * 4; ++g) {
-    const int64_t gb = m.gbase[g], gcap = m.gbase[g + 1] - gb;
-    int64_t fill = m.gfill[g];
-    fill = fill < gcap ? fill : gcap;
-    const int64_t a_q = gb / 4 > q_lo ? gb / 4 : q_lo;
-    const int64_t e_used = (gb + fill + 3) / 4;
-    const int64_t b_q = e_used < q_hi ? e_used : q_hi;
-    if (a_q >= b_q) continue;
-    for (int u = threadIdx.x; u < chunk; u += blockDim.x) acc_s[u] = ident;
-    __syncthreads();
-    const int gi = static_cast<int>(g);
-    int64_t q = a_q + threadIdx.x;
-    for (; q + blockDim.x < b_q; q += 2 * blockDim.x) {
-      const int64_t q2 = q + blockDim.x;
-      const uint4 wa = __ldcs(w4 + q), wb = __ldcs(w4 + q2);
-      const float4 fa = __ldcs(f4 + q), fb = __ldcs(f4 + q2);
-      const uint32_t ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-      const float fs[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
-      float av[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint32_t src = ws[i] >> m.cb;
-        av[i] = (ws[i] != kEmpty && src < static_cast<uint32_t>(m.n)) ? __ldg(act + src) : 0.0f;
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == kConsWarps) {
+    // producer: one thread issues the ring's bulk copies
+    if (lane != 0) return;
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    int64_t t = t_lo, g = lo;
+    int32_t used;
+    uint32_t i = 0;
+    bool ok = true;
+    while (next_tile(m, t, t_hi, g, used)) {
+      const int s = static_cast<int>(i % kStages);
+      if (i >= kStages && !mbar_wait(empty + s, ((i / kStages) - 1) & 1)) {
+        ok = false;
+        break;
       }
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        sweep_entry<MONOID, PRUNE>(m, p, acc_s, gi, gb, mask, ws[i], fs[i], av[i], (i < 4 ? q : q2) * 4 + (i & 3));
+      const uint32_t bytes = static_cast<uint32_t>((used + 3) / 4 * 16);
+      mbar_arrive_expect_tx(full + s, 2 * bytes);
+      bulk_load(word_s + s * kTile, m.word + t * kTile, bytes, full + s, policy);
+      bulk_load(w_s + s * kTile, m.w + t * kTile, bytes, full + s, policy);
+      ++t;
+      ++i;
     }
-    if (q < b_q) {
-      const uint4 wa = __ldcs(w4 + q);
-      const float4 fa = __ldcs(f4 + q);
-      const uint32_t ws[4] = {wa.x, wa.y, wa.z, wa.w};
-      const float fs[4] = {fa.x, fa.y, fa.z, fa.w};
-      float av[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t src = ws[i] >> m.cb;
-        av[i] = (ws[i] != kEmpty && src < static_cast<uint32_t>(m.n)) ? __ldg(act + src) : 0.0f;
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) sweep_entry<MONOID, PRUNE>(m, p, acc_s, gi, gb, mask, ws[i], fs[i], av[i], q * 4 + i);
-    }
-    __syncthreads();
-    const int32_t base = gi << m.cb;
-    if (MONOID == PXB_MONOID_SUM && base + chunk <= m.n) {
-      float4 *acc4 = reinterpret_cast<float4 *>(acc + base);
-      const float4 *s4 = reinterpret_cast<const float4 *>(acc_s);
-      for (int u = threadIdx.x; u < chunk / 4; u += blockDim.x) {
-        const float4 v = s4[u];
-        if (v.x != 0.0f || v.y != 0.0f || v.z != 0.0f || v.w != 0.0f) atomicAdd(acc4 + u, v);
-      }
-    } else {
-      for (int u = threadIdx.x; u < chunk; u += blockDim.x) {
-        const float v = acc_s[u];
-        if (v != ident && base + u < m.n) atomic_combine<MONOID>(acc + base + u, v);
-      }
-    }
-    __syncthreads();
+    // never leave with a copy in flight: wait for the last issued stages
+    const uint32_t first = i > kStages ? i - kStages : 0;
+    for (uint32_t j = first; j < i; ++j)
+      if (!mbar_wait(full + (j % kStages), (j / kStages) & 1)) ok = false;
+    if (!ok) atomicOr(m.status, 2);
+    return;
   }
+
+  // consumers
+  int64_t t = t_lo, g = lo, cur = -1;
+  int32_t used;
+  uint32_t i = 0;
+  bool ok = true;
+  while (next_tile(m, t, t_hi, g, used)) {
+    if (g != cur) {
+      consumer_sync();
+      flush_reset<MONOID>(m, acc_s, acc, acc_fixed, cur);
+      consumer_sync();
+      cur = g;
+    }
+    const int s = static_cast<int>(i % kStages);
+    if (ok && !mbar_wait(full + s, (i / kStages) & 1)) ok = false;
+    if (ok)
+      sweep_tile<MONOID, PK>(m, p, act, word_s + s * kTile, w_s + s * kTile, used, acc_s,
+                                acc + (static_cast<int64_t>(g) << m.cb), static_cast<int32_t>(g),
+                                __ldg(m.gbase + g), t * kTile);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + s);
+    ++t;
+    ++i;
+  }
+  if (cur >= 0) {
+    consumer_sync();
+    flush_reset<MONOID>(m, acc_s, acc, acc_fixed, cur);
+  }
+  if (!ok && lane == 0) atomicOr(m.status, 2);
 }
 
 // Edges the mirror had no room for: swept with global atomics.
 template <int MONOID, bool PRUNE>
-__global__ void mirror_overflow_kernel(MirrorK m, const float *__restrict__ act, float *__restrict__ acc, MPrune p) {
+__global__ void mirror_overflow_kernel(MirrorK m, const float *__restrict__ act, float *__restrict__ acc,
+                                       int64_t *__restrict__ acc_fixed, MPrune p) {
   const int64_t cnt = *m.ovf_count < m.ovf_cap ? *m.ovf_count : m.ovf_cap;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < cnt;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int32_t s = m.ovf_src[i], d = m.ovf_dst[i];
     if (s < 0 || s >= m.n || d < 0 || d >= m.n) continue;
     const float w = m.ovf_w[i];
-    atomic_combine<MONOID>(acc + d, __fmul_rn(w, act[s]));
+    if (MONOID == PXB_MONOID_SUM) fixed_add_global(acc_fixed + d, acc + d, __fmul_rn(w, act[s]));
+    else atomic_combine<MONOID>(acc + d, __fmul_rn(w, act[s]));
     if (PRUNE && mprune_pred(p, w, d)) {
       m.ovf_src[i] = -1;
       tombstone(p, m.ovf_slot[i], s);
@@ -295,7 +526,7 @@ static int check_mirror(const char *fn, const pxb_mirror *m) {
   PXB_REQUIRE(m->num_units > 0, "%s: num_units must be > 0", fn);
   PXB_REQUIRE(m->groups == ((int64_t(m->num_units) + (int64_t(1) << m->chunk_bits) - 1) >> m->chunk_bits),
               "%s: groups does not match num_units and chunk_bits", fn);
-  PXB_REQUIRE(m->entries % 8 == 0, "%s: entries must be a multiple of 8", fn);
+  PXB_REQUIRE(m->entries % PXB_MIRROR_TILE == 0, "%s: entries must be a multiple of %d", fn, PXB_MIRROR_TILE);
   int bits = 0;
   while ((int64_t(1) << bits) < m->num_units) ++bits;
   PXB_REQUIRE(bits + m->chunk_bits <= 32, "%s: unit ids need %d bits, too many for %d chunk bits", fn, bits,
@@ -314,7 +545,7 @@ static int check_mirror(const char *fn, const pxb_mirror *m) {
 using namespace pxb;
 
 extern "C" int pxb_mirror_forward(const pxb_mirror *mirror, const float *act, int32_t monoid, float *acc,
-                                  int32_t prune_kind, float prune_threshold, const float *unit_threshold,
+                                  int64_t *acc_fixed, int32_t prune_kind, float prune_threshold, const float *unit_threshold,
                                   uint8_t *dead, uint32_t *free_bitmap, int64_t bitmap_words,
                                   const int32_t *bitmap_level, int32_t *pruned_count, void *stream) {
   int rc = check_mirror("pxb_mirror_forward", mirror);
@@ -325,26 +556,42 @@ extern "C" int pxb_mirror_forward(const pxb_mirror *mirror, const float *act, in
   PXB_REQUIRE(prune_kind == PXB_PRUNE_NONE || dead, "pxb_mirror_forward: pruning needs the canonical dead column");
   PXB_REQUIRE(prune_kind != PXB_PRUNE_ABS_BELOW_DST || unit_threshold,
               "pxb_mirror_forward: per-destination threshold column is NULL");
-  PXB_REQUIRE(monoid != PXB_MONOID_SUM || aligned16(acc), "pxb_mirror_forward: acc must be 16-byte aligned");
+  PXB_REQUIRE(monoid != PXB_MONOID_SUM || acc_fixed != nullptr,
+              "pxb_mirror_forward: the sum needs its fixed-point accumulator acc_fixed");
+  PXB_REQUIRE((reinterpret_cast<uintptr_t>(acc_fixed) & 7u) == 0, "pxb_mirror_forward: acc_fixed must be 8-byte aligned");
   MirrorK m = to_k(mirror);
   MPrune p{prune_kind, prune_threshold, unit_threshold, dead, free_bitmap, bitmap_words, bitmap_level, pruned_count};
   cudaStream_t st = as_stream(stream);
-  const size_t smem = sizeof(float) << m.cb;
   if (m.entries > 0) {
-    const int64_t full = int64_t(sm_count()) * 8;
-    const int64_t want = (m.entries / 4 + 1023) / 1024;  // at least 4 K entries per CTA
-    const int grid = static_cast<int>(want < full ? (want > 0 ? want : 1) : full);
-#define PXB_MF(M, P) mirror_forward_kernel<M, P><<<grid, 256, smem, st>>>(m, act, acc, p)
-    const bool pr = prune_kind != PXB_PRUNE_NONE;
-    if (monoid == PXB_MONOID_SUM) { if (pr) PXB_MF(PXB_MONOID_SUM, true); else PXB_MF(PXB_MONOID_SUM, false); }
-    else if (monoid == PXB_MONOID_MAX) { if (pr) PXB_MF(PXB_MONOID_MAX, true); else PXB_MF(PXB_MONOID_MAX, false); }
-    else { if (pr) PXB_MF(PXB_MONOID_MIN, true); else PXB_MF(PXB_MONOID_MIN, false); }
-#undef PXB_MF
-    PXB_LAUNCHED("mirror_forward_kernel");
+    const size_t smem =
+        128 + size_t(kStages) * kTile * 8 + ((monoid == PXB_MONOID_SUM ? 2 * sizeof(int32_t) : sizeof(float)) << m.cb);
+    const int64_t tiles = m.entries / kTile;
+#define PXB_MS(M, P)                                                                              \
+  do {                                                                                            \
+    auto fn = mirror_sweep_kernel<M, P>;                                                          \
+    PXB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));   \
+    int per_sm = 0;                                                                               \
+    PXB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kSweepThreads, smem));    \
+    const int64_t full = int64_t(sm_count()) * (per_sm > 0 ? per_sm : 1);                        \
+    const int grid = static_cast<int>(tiles < full ? tiles : full);                               \
+    fn<<<grid, kSweepThreads, smem, st>>>(m, act, acc, acc_fixed, p);                             \
+  } while (0)
+#define PXB_MS_K(M)                                                                               \
+  do {                                                                                            \
+    if (prune_kind == PXB_PRUNE_ABS_BELOW) PXB_MS(M, PXB_PRUNE_ABS_BELOW);                        \
+    else if (prune_kind == PXB_PRUNE_ABS_BELOW_DST) PXB_MS(M, PXB_PRUNE_ABS_BELOW_DST);           \
+    else PXB_MS(M, PXB_PRUNE_NONE);                                                               \
+  } while (0)
+    if (monoid == PXB_MONOID_SUM) PXB_MS_K(PXB_MONOID_SUM);
+    else if (monoid == PXB_MONOID_MAX) PXB_MS_K(PXB_MONOID_MAX);
+    else PXB_MS_K(PXB_MONOID_MIN);
+#undef PXB_MS_K
+#undef PXB_MS
+    PXB_LAUNCHED("mirror_sweep_kernel");
   }
   if (m.ovf_cap > 0) {
     const bool pr = prune_kind != PXB_PRUNE_NONE;
-#define PXB_MO(M, P) mirror_overflow_kernel<M, P><<<sm_count(), 256, 0, st>>>(m, act, acc, p)
+#define PXB_MO(M, P) mirror_overflow_kernel<M, P><<<sm_count(), 256, 0, st>>>(m, act, acc, acc_fixed, p)
     if (monoid == PXB_MONOID_SUM) { if (pr) PXB_MO(PXB_MONOID_SUM, true); else PXB_MO(PXB_MONOID_SUM, false); }
     else if (monoid == PXB_MONOID_MAX) { if (pr) PXB_MO(PXB_MONOID_MAX, true); else PXB_MO(PXB_MONOID_MAX, false); }
     else { if (pr) PXB_MO(PXB_MONOID_MIN, true); else PXB_MO(PXB_MONOID_MIN, false); }

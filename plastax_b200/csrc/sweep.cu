@@ -264,7 +264,8 @@ __global__ void __launch_bounds__(256) backward_kernel(
 // unit apply (src/plastax/sweep.py:183-230)
 // ---------------------------------------------------------------------------
 __global__ void unit_apply_kernel(int32_t n, int mode, int act_kind, int monoid, float *__restrict__ acc,
-                                  const float *__restrict__ act, const float *__restrict__ seed,
+                                  int64_t *__restrict__ acc_fixed, const float *__restrict__ act,
+                                  const float *__restrict__ seed,
                                   const int32_t *__restrict__ level, int32_t target_level,
                                   const uint8_t *__restrict__ is_input, const uint8_t *__restrict__ pruned,
                                   float *__restrict__ out) {
@@ -273,7 +274,14 @@ __global__ void unit_apply_kernel(int32_t n, int mode, int act_kind, int monoid,
   if (level != nullptr && level[i] != target_level) return;
   if (is_input != nullptr && is_input[i]) return;
   if (pruned != nullptr && pruned[i]) return;
-  const float a = acc[i];
+  float a = acc[i];
+  if (acc_fixed != nullptr) {
+    // the exact fixed-point sum plus the float side (non-finite or huge
+    // products), rounded to float once
+    a = static_cast<float>(fma(static_cast<double>(acc_fixed[i]), 1.0 / double(1ll << PXB_FIXED_FRAC_BITS),
+                               static_cast<double>(a)));
+    acc_fixed[i] = 0;
+  }
   if (mode == 0) {
     out[i] = act_fn(act_kind, a);
   } else {
@@ -501,7 +509,8 @@ extern "C" int pxb_backward_update(int64_t cap, const int32_t *from_id, const in
 }
 
 extern "C" int pxb_unit_apply(int32_t num_units, int32_t mode, int32_t act_kind, int32_t monoid, float *acc,
-                              const float *act, const float *seed, const int32_t *level, int32_t target_level,
+                              int64_t *acc_fixed, const float *act, const float *seed, const int32_t *level,
+                              int32_t target_level,
                               const uint8_t *is_input, const uint8_t *pruned, float *out, void *stream) {
   PXB_REQUIRE(num_units >= 0, "pxb_unit_apply: negative num_units");
   PXB_REQUIRE(mode == 0 || mode == 1, "pxb_unit_apply: mode must be 0 (forward) or 1 (backward)");
@@ -509,9 +518,10 @@ extern "C" int pxb_unit_apply(int32_t num_units, int32_t mode, int32_t act_kind,
   PXB_REQUIRE(monoid >= 0 && monoid <= 2, "pxb_unit_apply: unknown monoid %d", monoid);
   if (num_units == 0) return PXB_OK;
   PXB_REQUIRE(acc && out, "pxb_unit_apply: acc/out is NULL");
+  PXB_REQUIRE(acc_fixed == nullptr || monoid == PXB_MONOID_SUM, "pxb_unit_apply: acc_fixed is for the sum monoid");
   PXB_REQUIRE(mode == 0 || act, "pxb_unit_apply: backward apply needs the activation column");
   unit_apply_kernel<<<(num_units + 255) / 256, 256, 0, as_stream(stream)>>>(
-      num_units, mode, act_kind, monoid, acc, act, seed, level, target_level, is_input, pruned, out);
+      num_units, mode, act_kind, monoid, acc, acc_fixed, act, seed, level, target_level, is_input, pruned, out);
   PXB_LAUNCHED("unit_apply_kernel");
   return PXB_OK;
 }

@@ -152,10 +152,12 @@ def backward_update(b: Bucket, grad: torch.Tensor, act: torch.Tensor, acc: torch
 def unit_apply(acc: torch.Tensor, out: torch.Tensor, *, mode: int, act_kind: str, monoid: str = "sum",
                act: torch.Tensor | None = None, seed: torch.Tensor | None = None,
                level: torch.Tensor | None = None, target_level: int = 0, is_input: torch.Tensor | None = None,
-               pruned: torch.Tensor | None = None) -> None:
+               pruned: torch.Tensor | None = None, acc_fixed: torch.Tensor | None = None) -> None:
     n = acc.numel()
+    if acc_fixed is not None:
+        _check(acc_fixed, torch.int64, n, "unit_apply acc_fixed")
     call("pxb_unit_apply", ctypes.c_int32(n), ctypes.c_int32(mode), ctypes.c_int32(_lib.ACT[act_kind]),
-         ctypes.c_int32(_lib.MONOID[monoid]), ptr(acc), ptr(act), ptr(seed), ptr(level),
+         ctypes.c_int32(_lib.MONOID[monoid]), ptr(acc), ptr(acc_fixed), ptr(act), ptr(seed), ptr(level),
          ctypes.c_int32(target_level), ptr(is_input), ptr(pruned), ptr(out), _stream())
 
 
@@ -371,12 +373,17 @@ def free_bitmap_build(mode: int, b: Bucket, unit_level: torch.Tensor, tail_start
     return out
 
 
-def mirror_forward(m, act: torch.Tensor, acc: torch.Tensor, *, monoid: str = "sum", prune_kind: int = 0,
+def mirror_forward(m, act: torch.Tensor, acc: torch.Tensor, *, acc_fixed: torch.Tensor | None = None,
+                   monoid: str = "sum", prune_kind: int = 0,
                    threshold: float = 0.0, unit_threshold: torch.Tensor | None = None,
                    dead: torch.Tensor | None = None, free_bitmap: torch.Tensor | None = None, bitmap_words: int = 0,
                    bitmap_level: torch.Tensor | None = None, pruned_count: torch.Tensor | None = None) -> None:
+    """Mirror sweep; for sum, `acc_fixed` (int64, zeroed) receives the exact
+    fixed-point sum and `acc` only non-finite or huge products."""
+    if acc_fixed is not None:
+        _check(acc_fixed, torch.int64, acc.numel(), "mirror_forward acc_fixed")
     call("pxb_mirror_forward", ctypes.byref(m.struct), ptr(act), ctypes.c_int32(_lib.MONOID[monoid]), ptr(acc),
-         ctypes.c_int32(prune_kind), ctypes.c_float(threshold), ptr(unit_threshold), ptr(dead), ptr(free_bitmap),
+         ptr(acc_fixed), ctypes.c_int32(prune_kind), ctypes.c_float(threshold), ptr(unit_threshold), ptr(dead), ptr(free_bitmap),
          ctypes.c_int64(bitmap_words), ptr(bitmap_level), ptr(pruned_count), _stream())
 
 

@@ -7,7 +7,8 @@ major, as the builder lays the bucket out) inside a group: consecutive
 entries then read neighbouring activations, so the sweep's gathers coalesce
 (a destination-sorted group makes every gather its own L2 sector and was
 measured 3.5x slower). Each group gets `slack` spare entries (at least
-`min_slack`, rounded to a multiple of 8) for the edges growth inserts.
+`min_slack`) for the edges growth inserts, and its capacity is rounded up
+to the sweep's tile (PXB_MIRROR_TILE entries), so a tile lies in one group.
 """
 
 from __future__ import annotations
@@ -22,13 +23,18 @@ from plastax_b200 import _lib
 
 class Mirror:
     def __init__(self, bucket: dict[str, torch.Tensor], num_units: int, *, slack: float = 0.05,
-                 min_slack: int = 64, item_entries: int = 1 << 16, ovf_cap: int = 1 << 20) -> None:
+                 min_slack: int = 64, item_entries: int = 1 << 16, ovf_cap: int = 1 << 20,
+                 chunk_bits: int | None = None) -> None:
         dev = bucket["dead"].device
         n = int(num_units)
         src_bits = max(1, (n - 1).bit_length())
         cb = min(32 - src_bits, 13)
         if cb < 2:
             raise ValueError(f"mirror: {n} units leave too few bits for a destination chunk")
+        if chunk_bits is not None:
+            if not 2 <= chunk_bits <= cb:
+                raise ValueError(f"mirror: chunk_bits {chunk_bits} not in [2, {cb}] for {n} units")
+            cb = int(chunk_bits)
         chunk = 1 << cb
         groups = (n + chunk - 1) // chunk
         frm, to = bucket["from_id"], bucket["to_id"]
@@ -42,7 +48,8 @@ class Mirror:
         counts = torch.bincount(g, minlength=groups)
         counts_h = counts.cpu().numpy().astype(np.int64)
         spare = np.maximum(min_slack, np.ceil(counts_h * slack).astype(np.int64))
-        gcap = (counts_h + spare + 7) // 8 * 8
+        tile = _lib.MIRROR_TILE
+        gcap = (counts_h + spare + tile - 1) // tile * tile
         gbase = np.concatenate([[0], np.cumsum(gcap)]).astype(np.int64)
         entries = int(gbase[-1])
         starts = torch.from_numpy(np.concatenate([[0], np.cumsum(counts_h)[:-1]])).to(dev)

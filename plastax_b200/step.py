@@ -116,11 +116,28 @@ class StepFn:
         self.use_mirror = net.update_conn is None and (net.prune_conn is None or self.fuse_prune)
         self.mirrors: list | None = None
         self.bitmaps: list[torch.Tensor] | None = None
+        # the mirror's sum is exact fixed point (int64 accumulators beside
+        # the float side for non-finite or huge products)
+        self.acc_fixed = (torch.zeros(n, dtype=torch.int64, device=device)
+                          if self.use_mirror and self.fwd_monoid == "sum" else None)
+        # Scheme-A over several buckets: each bucket's forward partial is
+        # reduced alone, then combined into the carried accumulator
+        # (src/plastax/sweep.py:157-175, monoid.py:175-204)
+        self.per_bucket_reduce = self.sharded and self.num_buckets > 1
+        if self.per_bucket_reduce:
+            self.part = torch.empty(n, dtype=torch.float32, device=device)
+            self.part_fixed = None if self.acc_fixed is None else torch.zeros_like(self.acc_fixed)
         self._bound: int | None = None
         self.step_dev = torch.zeros(1, dtype=torch.int32, device=device)
         self.graph = None  # a captured CUDA graph of the step body (see capture)
+        self.side = None
         if self.ac is not None:
             self._build_growth()
+            # proposals scored by the site RNG alone depend on the levels and
+            # the step counter only, never on this step's propagation, prune
+            # or update: their selection may overlap the forward sweep
+            if self.ac.score in ("uniform", "uniform_q256") and torch.device(device).type == "cuda":
+                self.side = torch.cuda.Stream(device=device)
         self.launches = 0
 
     # -- per-state device indices ---------------------------------------------
@@ -210,9 +227,11 @@ class StepFn:
             self.gather_buf = torch.zeros((G, self.num_levels), dtype=torch.int32, device=dev)
 
     # -- collectives -----------------------------------------------------------
-    def _combine_partials(self, acc: torch.Tensor) -> None:
+    def _combine_partials(self, acc: torch.Tensor, acc_fixed: torch.Tensor | None = None) -> None:
         if self.sharded:
             _dist().all_reduce(acc, op=self.reduce_op)
+            if acc_fixed is not None:
+                _dist().all_reduce(acc_fixed, op=_dist().ReduceOp.SUM)
 
     # -- phases -----------------------------------------------------------------
     def _scatter_inputs(self, state: NetworkState, inputs: StepInputs) -> None:
@@ -222,23 +241,46 @@ class StepFn:
         x = x.to(self.dev, non_blocking=True).reshape(-1)
         state.units[ACTIVATION.name].index_copy_(0, self.input_ids, x)
 
-    def _accumulate_bucket(self, state: NetworkState, i: int, act: torch.Tensor) -> None:
+    def _accumulate_bucket(self, state: NetworkState, i: int, act: torch.Tensor, acc: torch.Tensor,
+                           acc_fixed: torch.Tensor | None) -> None:
         """Forward accumulate of bucket i, with the prune fused when legal."""
         net, b = self.net, state.conns[i]
         bm, bm_level = self._bm(i)
         if self.use_mirror:
             m = self.mirrors[i]
             if self.fuse_prune:
-                K.mirror_forward(m, act, self.acc, monoid=self.fwd_monoid, prune_kind=_lib.PRUNE_ABS_BELOW,
-                                 threshold=net.prune_conn.threshold, dead=b["dead"], free_bitmap=bm,
-                                 bitmap_words=(b["dead"].numel() + 31) // 32, bitmap_level=bm_level)
+                K.mirror_forward(m, act, acc, acc_fixed=acc_fixed, monoid=self.fwd_monoid,
+                                 prune_kind=_lib.PRUNE_ABS_BELOW, threshold=net.prune_conn.threshold,
+                                 dead=b["dead"], free_bitmap=bm, bitmap_words=(b["dead"].numel() + 31) // 32,
+                                 bitmap_level=bm_level)
             else:
-                K.mirror_forward(m, act, self.acc, monoid=self.fwd_monoid)
+                K.mirror_forward(m, act, acc, acc_fixed=acc_fixed, monoid=self.fwd_monoid)
         elif self.fuse_prune:
-            K.forward_prune(b, act, self.acc, monoid=self.fwd_monoid, prune_kind=_lib.PRUNE_ABS_BELOW,
+            K.forward_prune(b, act, acc, monoid=self.fwd_monoid, prune_kind=_lib.PRUNE_ABS_BELOW,
                             threshold=net.prune_conn.threshold, free_bitmap=bm, bitmap_level=bm_level)
         else:
-            K.forward_accumulate(b, act, self.acc, self.fwd_monoid)
+            K.forward_accumulate(b, act, acc, self.fwd_monoid)
+
+    def _forward_bucket(self, state: NetworkState, i: int, act: torch.Tensor) -> None:
+        """Bucket i's forward partial, reduced across shards, in the carried
+        accumulator."""
+        if not self.per_bucket_reduce:
+            self._accumulate_bucket(state, i, act, self.acc, self.acc_fixed)
+            self._combine_partials(self.acc, self.acc_fixed)
+            return
+        K.fill(self.part, self.fwd_identity)
+        if self.part_fixed is not None:
+            self.part_fixed.zero_()
+        self._accumulate_bucket(state, i, act, self.part, self.part_fixed)
+        self._combine_partials(self.part, self.part_fixed)
+        if self.fwd_monoid == "sum":
+            self.acc.add_(self.part)
+            if self.part_fixed is not None:
+                self.acc_fixed.add_(self.part_fixed)
+        elif self.fwd_monoid == "max":
+            torch.maximum(self.acc, self.part, out=self.acc)
+        else:
+            torch.minimum(self.acc, self.part, out=self.acc)
 
     def _forward(self, state: NetworkState) -> None:
         net, st, units = self.net, self.static, state.units
@@ -246,19 +288,19 @@ class StepFn:
         pruned = units.get(PRUNED.name)
         fp = net.forward_pass
         K.fill(self.acc, self.fwd_identity)
+        if self.acc_fixed is not None:
+            self.acc_fixed.zero_()
         if self.pipeline:
-            self._accumulate_bucket(state, 0, act)
-            self._combine_partials(self.acc)
+            self._forward_bucket(state, 0, act)
             K.unit_apply(self.acc, act, mode=0, act_kind=fp.activation, monoid=self.fwd_monoid,
-                         is_input=self.is_input, pruned=pruned)
+                         is_input=self.is_input, pruned=pruned, acc_fixed=self.acc_fixed)
             self.launches += 3
             return
         level = units[LEVEL.name]
         for l in range(self.num_buckets):
-            self._accumulate_bucket(state, l, act)
-            self._combine_partials(self.acc)
+            self._forward_bucket(state, l, act)
             K.unit_apply(self.acc, act, mode=0, act_kind=fp.activation, monoid=self.fwd_monoid, level=level,
-                         target_level=l + 1, is_input=self.is_input, pruned=pruned)
+                         target_level=l + 1, is_input=self.is_input, pruned=pruned, acc_fixed=self.acc_fixed)
             self.launches += 2
 
     def _loss(self, state: NetworkState, inputs: StepInputs) -> None:
@@ -347,16 +389,11 @@ class StepFn:
             raise NotImplementedError(f"growth trigger {trig!r} has no engine lowering")
         return fire
 
-    def _add_conn(self, state: NetworkState) -> GrowthRemainder | None:
-        ac = self.ac
-        if ac is None:
-            return None
-        st, units = self.static, state.units
-        self.grown.zero_()
-        self.overflow.zero_()
-        if not self._fires(state) or self.k == 0:
-            state.grown, state.overflow = self.grown, self.overflow
-            return None
+    def _select(self, state: NetworkState) -> None:
+        """Growth selection: proposals, the first k in the total order and
+        the level-major winner list (src/plastax/phases.py:3813-3860,
+        :4208-4487, :5043-5058), gathered into the claim's input columns."""
+        ac, st, units = self.ac, self.static, state.units
         n = st.num_units
         level = units[LEVEL.name]
         pruned = units.get(PRUNED.name)
@@ -379,6 +416,22 @@ class StepFn:
         K.gather_winners(self.win, kk, self.k, src, dst, score, init_kind=self.init_kind, init_a=self.init_a,
                          out=self.claim_in)
         self.launches += 4 + 5
+
+    def _add_conn(self, state: NetworkState, selected: bool = False) -> GrowthRemainder | None:
+        """Growth: the selection (unless it already ran on the side stream)
+        and the claim into the post-prune arena."""
+        ac = self.ac
+        if ac is None:
+            return None
+        st = self.static
+        level = state.units[LEVEL.name]
+        self.grown.zero_()
+        self.overflow.zero_()
+        if not self._fires(state) or self.k == 0:
+            state.grown, state.overflow = self.grown, self.overflow
+            return None
+        if not selected:
+            self._select(state)
         cs, cd, cw, grow = self.claim_in
         max_new = -1 if ac.max_new_per_step is None else int(ac.max_new_per_step)
         if self.pipeline:
@@ -425,13 +478,22 @@ class StepFn:
     def _body(self, state: NetworkState, inputs: StepInputs) -> GrowthRemainder | None:
         """The device work of one step (no host synchronisation)."""
         self._level = state.units[LEVEL.name]
+        # selection that reads nothing the step writes runs on the side
+        # stream, concurrently with the propagation passes
+        early = self.side is not None and self._fires(state) and self.k > 0
+        if early:
+            self.side.wait_stream(torch.cuda.current_stream(self.dev))
+            with torch.cuda.stream(self.side):
+                self._select(state)
         self._scatter_inputs(state, inputs)
         self._forward(state)
         self._loss(state, inputs)
         self._backward(state)
         self._update_conn(state)
         self._prune(state)
-        remainder = self._add_conn(state)
+        if early:
+            torch.cuda.current_stream(self.dev).wait_stream(self.side)
+        remainder = self._add_conn(state, selected=early)
         self.step_dev += 1
         return remainder
 

@@ -456,6 +456,15 @@ def _canonical_multiset(hb):
     return rows, hb["weight"][live]
 
 
+def _fixed_total(kern, acc, acc_fixed):
+    """acc_fixed * 2^-28 + acc rounded once, through the unit apply."""
+    import torch
+
+    out = torch.empty_like(acc)
+    kern.unit_apply(acc, out, mode=0, act_kind="identity", acc_fixed=acc_fixed)
+    return out.cpu().numpy()
+
+
 @pytest.mark.parametrize("n,cap,monoid", [(3000, 200_000, "sum"), (70_000, 400_000, "sum"), (5000, 100_000, "max"),
                                           (1 << 20, 1 << 20, "sum")])
 def test_mirror_forward_prune(cuda, n, cap, monoid):
@@ -481,11 +490,13 @@ def test_mirror_forward_prune(cuda, n, cap, monoid):
     bm = kern.free_bitmap_build(0, db, d_level, tail, 3)
     m = Mirror(db, n)
     acc = torch.full((n,), init, dtype=torch.float32, device=cuda)
+    acc_fixed = torch.zeros(n, dtype=torch.int64, device=cuda) if monoid == "sum" else None
     pruned = torch.zeros(1, dtype=torch.int32, device=cuda)
-    kern.mirror_forward(m, t(act), acc, monoid=monoid, prune_kind=1, threshold=thr, dead=db["dead"], free_bitmap=bm,
-                        bitmap_words=(cap + 31) // 32, bitmap_level=d_level, pruned_count=pruned)
+    kern.mirror_forward(m, t(act), acc, acc_fixed=acc_fixed, monoid=monoid, prune_kind=1, threshold=thr,
+                        dead=db["dead"], free_bitmap=bm, bitmap_words=(cap + 31) // 32, bitmap_level=d_level,
+                        pruned_count=pruned)
     if monoid == "sum":
-        _close(acc.cpu().numpy(), ref_acc)
+        _close(_fixed_total(kern, acc, acc_fixed), ref_acc)
     else:
         np.testing.assert_array_equal(acc.cpu().numpy(), ref_acc)
     np.testing.assert_array_equal(db["dead"].cpu().numpy(), ref_b["dead"])
@@ -525,11 +536,12 @@ def test_mirror_tracks_claims(cuda, slack, ovf):
     for step in range(5):
         act = rng.standard_normal(n).astype(np.float32)
         acc = torch.zeros(n, dtype=torch.float32, device=cuda)
+        acc_fixed = torch.zeros(n, dtype=torch.int64, device=cuda)
         ref_acc = np.zeros(n, np.float32)
         orc.forward_accumulate(hb, act, n, "sum", ref_acc)
-        kern.mirror_forward(m, t(act), acc, prune_kind=1, threshold=0.01, dead=db["dead"], free_bitmap=bm,
-                            bitmap_words=(cap + 31) // 32, bitmap_level=d_level)
-        _close(acc.cpu().numpy(), ref_acc)
+        kern.mirror_forward(m, t(act), acc, acc_fixed=acc_fixed, prune_kind=1, threshold=0.01, dead=db["dead"],
+                            free_bitmap=bm, bitmap_words=(cap + 31) // 32, bitmap_level=d_level)
+        _close(_fixed_total(kern, acc, acc_fixed), ref_acc)
         src = rng.integers(16, n, k).astype(np.int32)
         src = src[np.argsort(level[src], kind="stable")]
         dst = rng.integers(16, n, k).astype(np.int32)
@@ -544,3 +556,49 @@ def test_mirror_tracks_claims(cuda, slack, ovf):
         np.testing.assert_array_equal(rows, crows, err_msg=f"step {step}")
         np.testing.assert_array_equal(mw, cw)
     assert m.healthy()
+
+
+def test_mirror_sum_is_exact_fixed_point(cuda):
+    """The mirror's sum equals the int64 sum of every float32 product rounded
+    (half to even) to 2^-28, bit for bit, whatever the atomic order: large
+    products (|p| >= 1), partials far beyond the 32-bit word's +-8 range (the
+    carry into the high word), tiny products (rounded), one non-finite
+    product (the float side), and two sweeps that must agree exactly."""
+    import torch
+
+    from plastax_b200.mirror import Mirror
+
+    kern = _k()
+    rng = np.random.default_rng(21)
+    n, cap = 5000, 400_000
+    b = random_bucket(rng, n, cap, cap - 1000, dead_frac=0.0, weight_scale=1.0)
+    # skew the destinations so some units take thousands of edges
+    hot = rng.random(cap) < 0.3
+    b["to_id"][hot] = rng.integers(0, 8, int(hot.sum())).astype(np.int32)
+    b["weight"][:] = (rng.standard_normal(cap) * rng.choice([1e-4, 0.05, 0.7, 40.0], cap)).astype(np.float32)
+    act = (rng.standard_normal(n) * 2).astype(np.float32)
+    b["weight"][7] = np.float32(3e7)  # a product beyond the fixed range goes to the float side
+    act[b["from_id"][7]] = np.float32(2.0)
+    db = to_device(b, cuda)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    m = Mirror(db, n)
+    live = b["dead"] == 0
+    p = (b["weight"][live] * act[b["from_id"][live]]).astype(np.float32)
+    big = np.abs(p) >= np.float32(2.0 ** 20)
+    units = np.rint(p[~big].astype(np.float64) * 2.0 ** 28).astype(np.int64)
+    want_fixed = np.zeros(n, np.int64)
+    np.add.at(want_fixed, b["to_id"][live][~big], units)
+    got = []
+    for _ in range(2):
+        acc = torch.zeros(n, dtype=torch.float32, device=cuda)
+        acc_fixed = torch.zeros(n, dtype=torch.int64, device=cuda)
+        kern.mirror_forward(m, t(act), acc, acc_fixed=acc_fixed)
+        np.testing.assert_array_equal(acc_fixed.cpu().numpy(), want_fixed)
+        side = np.zeros(n, np.float32)
+        np.add.at(side, b["to_id"][live][big], p[big])
+        np.testing.assert_array_equal(acc.cpu().numpy(), side)
+        got.append(_fixed_total(kern, acc, acc_fixed))
+    assert int((np.abs(want_fixed) > (8 << 28)).sum()) > 0, "no unit exceeded the 32-bit word's range"
+    np.testing.assert_array_equal(got[0], got[1])
+    want = (want_fixed.astype(np.float64) * 2.0 ** -28 + side.astype(np.float64)).astype(np.float32)
+    np.testing.assert_array_equal(got[0], want)
