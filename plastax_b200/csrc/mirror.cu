@@ -169,9 +169,23 @@ __device__ __forceinline__ void smem_combine(float *acc_s, int chunk, float *acc
 // timeout the kernel records status bit 1 and stops touching the stage data,
 // while still taking every consumer barrier, so it always terminates.
 // ---------------------------------------------------------------------------
-constexpr int kTile = PXB_MIRROR_TILE;
-constexpr int kStages = 3;
-constexpr int kConsWarps = 8;
+// Launch shape (overridable at compile time for tuning sweeps).
+#ifndef PXB_SWEEP_STAGES
+#define PXB_SWEEP_STAGES 2
+#endif
+#ifndef PXB_SWEEP_CONS_WARPS
+#define PXB_SWEEP_CONS_WARPS 8
+#endif
+#ifndef PXB_SWEEP_MIN_CTAS
+#define PXB_SWEEP_MIN_CTAS 3
+#endif
+#ifndef PXB_SWEEP_TILE
+#define PXB_SWEEP_TILE PXB_MIRROR_TILE
+#endif
+constexpr int kTile = PXB_SWEEP_TILE;  // divides PXB_MIRROR_TILE: a tile lies in one group
+static_assert(PXB_MIRROR_TILE % kTile == 0 && kTile % 4 == 0, "the sweep tile must divide the mirror tile");
+constexpr int kStages = PXB_SWEEP_STAGES;
+constexpr int kConsWarps = PXB_SWEEP_CONS_WARPS;
 constexpr int kConsThreads = kConsWarps * 32;
 constexpr int kSweepThreads = kConsThreads + 32;
 constexpr uint32_t kWaitPolls = 1u << 24;
@@ -348,7 +362,7 @@ __device__ __forceinline__ void flush_reset(const MirrorK &m, float *acc_s, floa
 }
 
 template <int MONOID, int PK>
-__global__ void __launch_bounds__(kSweepThreads, 3) mirror_sweep_kernel(MirrorK m, const float *__restrict__ act,
+__global__ void __launch_bounds__(kSweepThreads, PXB_SWEEP_MIN_CTAS) mirror_sweep_kernel(MirrorK m, const float *__restrict__ act,
                                                                         float *__restrict__ acc,
                                                                         int64_t *__restrict__ acc_fixed, MPrune p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
