@@ -180,7 +180,9 @@ PXB_API int pxb_backward_update(int64_t cap, const int32_t *from_id,
  * a unit i is finalized iff (level == NULL || level[i] == target_level)
  *   && (is_input == NULL || !is_input[i]) && (pruned == NULL || !pruned[i]).
  * The accumulated value x[i] = acc[i], or, when acc_fixed is not NULL,
- * acc_fixed[i] * 2^-PXB_FIXED_FRAC_BITS + acc[i] rounded once to float.
+ * acc_fixed[i] rounded to float and scaled by 2^-PXB_FIXED_FRAC_BITS (one
+ * rounding), plus acc[i] as a float (the side accumulator, 0 unless a
+ * product was not finite or huge).
  * forward (mode 0):  out[i] = act_fn(x[i])
  * backward (mode 1): out[i] = (x[i] + (seed ? seed[i] : 0)) * act_fn'(act[i])
  * Finalized units have acc[i] reset to the monoid identity (and
@@ -326,11 +328,40 @@ PXB_API int pxb_gather_winners(int64_t k, int64_t count, const int32_t *win_idx,
                        int32_t *dst_out, float *weight_out,
                        uint8_t *growable_out, void *stream);
 
+/* Fused growth selection for one proposal per unit scored by the site RNG
+ * (score_kind PXB_SCORE_UNIFORM or PXB_SCORE_UNIFORM_Q256): the proposals
+ * of every unit (as pxb_propose_per_unit with proposals = 1, bucket_level
+ * -1), the first k of the total order, listed levels ascending with the
+ * total order inside a level, gathered into the claim's input columns (as
+ * pxb_gather_winners) -- the same k rows as pxb_propose_per_unit +
+ * pxb_topk_unique + pxb_select_step + pxb_gather_winners. The keys' bins are
+ * ranked in shared memory, with no sort pass (the score integers are Philox
+ * draws). Requires dst_lo + dst_n <= num_units and num_levels <= 8.
+ * status (device, may be NULL) gets bit 0 when a bin held more than 65,536
+ * keys and the list is incomplete (not reached by RNG scores). Replaces
+ * src/plastax/phases.py:3813-3860 + :4208-4487 + :5043-5058 for this form. */
+PXB_API int pxb_select_unique_scratch_bytes(int32_t num_units, int64_t k,
+                                            int32_t num_levels, int32_t score_kind,
+                                            size_t *bytes);
+PXB_API int pxb_propose_select_unique(
+    int32_t num_units, uint64_t network_seed, int32_t step, int32_t dst_lo,
+    int32_t dst_n, int32_t score_kind, const int32_t *level,
+    const uint8_t *pruned, int32_t max_level_gap, int32_t direction,
+    int32_t allow_self_loops, int32_t src_level_bound,
+    const int32_t *step_dev, int64_t k, int32_t num_levels, int32_t init_kind,
+    float init_a, float init_b, uint32_t init_salt, int32_t *src_out,
+    int32_t *dst_out, float *weight_out, uint8_t *growable_out,
+    int32_t *status, void *scratch, size_t scratch_bytes, void *stream);
+
 /* ------------------------------------------------------------------ */
 /* slot claim                                                          */
 /* ------------------------------------------------------------------ */
 #define PXB_CLAIM_PIPELINE 0     /* src/plastax/phases.py:2985-3106 */
 #define PXB_CLAIM_TOPOLOGICAL 1  /* src/plastax/phases.py:2853-2982 */
+/* pxb_claim_commit mode flag: the candidate list is level-major (the level
+ * of every claiming candidate's source ascends along the list, as the
+ * growth listing makes it), so the claim partitions instead of sorting. */
+#define PXB_CLAIM_LEVEL_MAJOR 0x100
 
 /* Scratch bytes for one claim over `cap` local slots, k candidates and
  * num_levels (<= 1024) claim domains (1 for the topological claim). */
@@ -394,6 +425,15 @@ PXB_API int pxb_free_bitmap_build(int32_t mode, int64_t cap, const int32_t *from
                           int32_t num_units, int32_t num_levels,
                           int64_t shard_base, const int64_t *tail_start,
                           uint32_t *bitmap, void *stream);
+
+/* The step's growth flags from a claim's counts_out (device): grown (+)=
+ * counts[0], overflow |= counts[1] > 0, needs_resort |= counts[3] > 0; with
+ * reset != 0 grown and overflow start from 0 (the step's first bucket).
+ * grown, overflow and needs_resort may each be NULL. The flags of
+ * src/plastax/phases.py:4953-5132 (StepResult.overflow, grown,
+ * needs_resort). */
+PXB_API int pxb_growth_flags(const int32_t *counts, int32_t reset, int32_t *grown,
+                             uint8_t *overflow, uint8_t *needs_resort, void *stream);
 
 /* Count the dead slots of a bucket into out[0] (device). */
 PXB_API int pxb_count_dead(int64_t cap, const uint8_t *dead, int32_t *out,

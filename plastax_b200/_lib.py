@@ -33,6 +33,7 @@ OPT = {"sgd": 0, "momentum": 1, "adam": 2, "rmsprop": 3}
 SCORE_UNIFORM, SCORE_UNIFORM_Q256, SCORE_GRAD_ACT = 0, 1, 2
 INIT_CONST, INIT_DYADIC, INIT_HASH_UNIFORM = 0, 1, 2
 CLAIM_PIPELINE, CLAIM_TOPOLOGICAL = 0, 1
+CLAIM_LEVEL_MAJOR = 0x100
 MIRROR_TILE = 2048
 FIXED_FRAC_BITS = 28
 
@@ -130,9 +131,15 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
          c_ptr],
     ),
     "pxb_free_bitmap_build": (c_i32, [c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i64, c_ptr, c_ptr, c_ptr]),
+    "pxb_select_unique_scratch_bytes": (c_i32, [c_i32, c_i64, c_i32, c_i32, ctypes.POINTER(c_size)]),
+    "pxb_propose_select_unique": (
+        c_i32, [c_i32, ctypes.c_uint64, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32,
+                c_ptr, c_i64, c_i32, c_i32, c_f32, c_f32, ctypes.c_uint32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr,
+                c_ptr, c_size, c_ptr]),
     "pxb_mirror_forward": (
         c_i32, [c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_i32, c_f32, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr]),
     "pxb_mirror_insert": (c_i32, [c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
+    "pxb_growth_flags": (c_i32, [c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_count_dead": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr]),
 }
 

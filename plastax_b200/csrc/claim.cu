@@ -94,9 +94,12 @@ static int claim_scratch(const ClaimGeom &g, int64_t k, char *base, ClaimScratch
   o->flag = reinterpret_cast<int32_t *>(take(kk * 4));
   o->rank = reinterpret_cast<int32_t *>(take(kk * 4));
   o->counts = reinterpret_cast<int32_t *>(take(8 * 4));
-  size_t t1 = 0, t2 = 0, t3 = 0;
+  size_t t1 = 0, t2 = 0, t3 = 0, t4 = 0;
   if (cub::DeviceScan::ExclusiveSum(nullptr, t1, o->tile_counts, o->tile_offsets, static_cast<int>(m)) !=
       cudaSuccess)
+    return PXB_ECUDA;
+  if (cub::DevicePartition::Flagged(nullptr, t4, cub::CountingInputIterator<int32_t>(0), o->ckey_in, o->cidx_out,
+                                    o->counts, static_cast<int>(kk)) != cudaSuccess)
     return PXB_ECUDA;
   if (cub::DeviceRadixSort::SortPairs(nullptr, t2, o->ckey_in, o->ckey_out, o->cidx_in, o->cidx_out,
                                       static_cast<int>(kk), 0, 32) != cudaSuccess)
@@ -105,6 +108,7 @@ static int claim_scratch(const ClaimGeom &g, int64_t k, char *base, ClaimScratch
     return PXB_ECUDA;
   o->cub_bytes = t1 > t2 ? t1 : t2;
   if (t3 > o->cub_bytes) o->cub_bytes = t3;
+  if (t4 > o->cub_bytes) o->cub_bytes = t4;
   o->cub_tmp = take(o->cub_bytes);
   o->total = off;
   return PXB_OK;
@@ -234,6 +238,26 @@ __global__ void cand_key_kernel(CandArgs c, const int32_t *__restrict__ grow_ran
     key[i] = g ? static_cast<uint32_t>(cand_level(c, i)) : static_cast<uint32_t>(c.num_levels);
     idx[i] = static_cast<int32_t>(i);
   }
+}
+
+// Level-major lists: the stable partition's flag (a claiming candidate), then
+// the sort key of each partitioned position (its level, or the sentinel for
+// the non-claiming tail, whose order no later stage reads).
+__global__ void claim_flag_kernel(CandArgs c, const int32_t *__restrict__ grow_rank, uint32_t *__restrict__ flag) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < c.k;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    bool g = c.growable[i] != 0;
+    if (g && c.max_new >= 0 && grow_rank != nullptr) g = grow_rank[i] < c.max_new;
+    flag[i] = g ? 1u : 0u;
+  }
+}
+
+__global__ void partition_key_kernel(CandArgs c, const int32_t *__restrict__ num_sel, const int32_t *__restrict__ idx,
+                                     uint32_t *__restrict__ key) {
+  const int64_t sel = *num_sel;
+  for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < c.k;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    key[p] = p < sel ? static_cast<uint32_t>(cand_level(c, idx[p])) : static_cast<uint32_t>(c.num_levels);
 }
 
 __global__ void level_runs_kernel(int64_t k, const uint32_t *__restrict__ key, int32_t *__restrict__ first,
@@ -454,9 +478,28 @@ __global__ void finish_kernel(int topo, int64_t *tail_start, const int32_t *__re
   }
 }
 
+// The step's growth flags from a claim's counts (committed, overflowed,
+// tail used, resort): grown (+)= committed, overflow |= overflowed > 0,
+// needs_resort |= resort > 0; reset starts grown and overflow afresh.
+__global__ void growth_flags_kernel(const int32_t *__restrict__ counts, int32_t reset, int32_t *grown,
+                                    uint8_t *overflow, uint8_t *needs_resort) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  if (grown) *grown = (reset ? 0 : *grown) + counts[0];
+  if (overflow) *overflow = static_cast<uint8_t>((reset ? 0 : *overflow) | (counts[1] > 0 ? 1 : 0));
+  if (needs_resort) *needs_resort = static_cast<uint8_t>(*needs_resort | (counts[3] > 0 ? 1 : 0));
+}
+
 }  // namespace pxb
 
 using namespace pxb;
+
+extern "C" int pxb_growth_flags(const int32_t *counts, int32_t reset, int32_t *grown, uint8_t *overflow,
+                                uint8_t *needs_resort, void *stream) {
+  PXB_REQUIRE(counts != nullptr, "pxb_growth_flags: counts is NULL");
+  growth_flags_kernel<<<1, 32, 0, as_stream(stream)>>>(counts, reset, grown, overflow, needs_resort);
+  PXB_LAUNCHED("growth_flags_kernel");
+  return PXB_OK;
+}
 
 extern "C" int pxb_claim_scratch_bytes(int64_t cap, int64_t k, int32_t num_levels, size_t *bytes) {
   PXB_REQUIRE(bytes != nullptr, "pxb_claim_scratch_bytes: bytes is NULL");
@@ -486,6 +529,7 @@ extern "C" int pxb_claim_prepare(int32_t mode, int64_t cap, const int32_t *from_
                                  int64_t shard_base, const int64_t *tail_start, const uint32_t *free_bitmap,
                                  int64_t k, int32_t *level_counts, void *scratch, size_t scratch_bytes,
                                  void *stream) {
+  mode &= ~PXB_CLAIM_LEVEL_MAJOR;  // the list's order does not concern the domains' counts
   int rc = claim_common_checks("pxb_claim_prepare", mode, cap, num_levels);
   if (rc) return rc;
   const int topo = mode == PXB_CLAIM_TOPOLOGICAL;
@@ -533,6 +577,8 @@ extern "C" int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id, int
                                 void *const *extra_cols, const int32_t *extra_bytes, const void *const *extra_vals,
                                 int32_t *counts_out, uint8_t *overflowed_out, int32_t *placed_out, void *scratch,
                                 size_t scratch_bytes, void *stream) {
+  const bool level_major = (mode & PXB_CLAIM_LEVEL_MAJOR) != 0;
+  mode &= ~PXB_CLAIM_LEVEL_MAJOR;
   int rc = claim_common_checks("pxb_claim_commit", mode, cap, num_levels);
   if (rc) return rc;
   const int topo = mode == PXB_CLAIM_TOPOLOGICAL;
@@ -590,13 +636,25 @@ extern "C" int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id, int
       PXB_CUDA(cub::DeviceScan::ExclusiveSum(o.cub_tmp, tb, o.flag, o.rank, static_cast<int>(k), st));
       grow_rank = o.rank;
     }
-    cand_key_kernel<<<grid, 256, 0, st>>>(c, grow_rank, o.ckey_in, o.cidx_in);
-    PXB_LAUNCHED("cand_key_kernel");
-    int key_bits = 1;
-    while ((1u << key_bits) <= static_cast<uint32_t>(num_levels)) ++key_bits;
-    tb = o.cub_bytes;
-    PXB_CUDA(cub::DeviceRadixSort::SortPairs(o.cub_tmp, tb, o.ckey_in, o.ckey_out, o.cidx_in, o.cidx_out,
-                                             static_cast<int>(k), 0, key_bits, st));
+    if (level_major) {
+      // claiming candidates already ascend by level: a stable partition
+      // gives the order the level sort would
+      claim_flag_kernel<<<grid, 256, 0, st>>>(c, grow_rank, o.ckey_in);
+      PXB_LAUNCHED("claim_flag_kernel");
+      tb = o.cub_bytes;
+      PXB_CUDA(cub::DevicePartition::Flagged(o.cub_tmp, tb, cub::CountingInputIterator<int32_t>(0), o.ckey_in,
+                                             o.cidx_out, o.counts + 7, static_cast<int>(k), st));
+      partition_key_kernel<<<grid, 256, 0, st>>>(c, o.counts + 7, o.cidx_out, o.ckey_out);
+      PXB_LAUNCHED("partition_key_kernel");
+    } else {
+      cand_key_kernel<<<grid, 256, 0, st>>>(c, grow_rank, o.ckey_in, o.cidx_in);
+      PXB_LAUNCHED("cand_key_kernel");
+      int key_bits = 1;
+      while ((1u << key_bits) <= static_cast<uint32_t>(num_levels)) ++key_bits;
+      tb = o.cub_bytes;
+      PXB_CUDA(cub::DeviceRadixSort::SortPairs(o.cub_tmp, tb, o.ckey_in, o.ckey_out, o.cidx_in, o.cidx_out,
+                                               static_cast<int>(k), 0, key_bits, st));
+    }
     PXB_CUDA(cudaMemsetAsync(o.level_first, 0, (num_levels + 1) * 4, st));
     PXB_CUDA(cudaMemsetAsync(o.level_end, 0, (num_levels + 1) * 4, st));
     level_runs_kernel<<<grid, 256, 0, st>>>(k, o.ckey_out, o.level_first, o.level_end);

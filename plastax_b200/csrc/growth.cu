@@ -42,50 +42,67 @@ struct ProposeArgs {
   int32_t max_level_gap, direction, allow_self_loops, bucket_level, src_level_bound;
 };
 
+// The site seed's high limb for this launch: philox32(network_seed,
+// (step << 8) | 1), the step read from step_dev when set (graph replay).
+__device__ __forceinline__ uint64_t keyed_hi_of(const ProposeArgs &a) {
+  __shared__ uint64_t keyed;
+  if (a.step_dev == nullptr) return a.keyed_hi;
+  if (threadIdx.x == 0)
+    keyed = philox32(a.network_seed, (static_cast<uint64_t>(static_cast<uint32_t>(*a.step_dev)) << 8) | 1u);
+  __syncthreads();
+  return keyed;
+}
+
+// Candidate c = i * proposals + j of unit i: its endpoints and score, the
+// score -inf when the framework's validity window vetoes it.
+__device__ __forceinline__ void propose_one(const ProposeArgs &a, uint64_t keyed_hi, int64_t c, int32_t &src_o,
+                                            int32_t &dst_o, float &score_o) {
+  const int32_t i = static_cast<int32_t>(c / a.proposals);
+  const uint32_t j = static_cast<uint32_t>(c - static_cast<int64_t>(i) * a.proposals);
+  const uint64_t seed = (keyed_hi << 32) | static_cast<uint32_t>(i);
+  int32_t src = i;
+  int32_t dst = a.dst_lo + static_cast<int32_t>(uniform_int(unit_float(site_draw(seed, j, 0)), a.dst_n));
+  float score;
+  if (a.score_kind == PXB_SCORE_UNIFORM) {
+    score = unit_float(site_draw(seed, j, 1));
+  } else if (a.score_kind == PXB_SCORE_UNIFORM_Q256) {
+    const float u = unit_float(site_draw(seed, j, 1));
+    score = static_cast<float>(static_cast<int32_t>(__fmul_rn(u, 256.0f))) * (1.0f / 256.0f);
+  } else {
+    score = (dst >= 0 && dst < a.num_units) ? fabsf(__fmul_rn(a.grad[dst], a.act[src])) : 0.0f;
+  }
+  // _clamp_proposals: out-of-range ids are vetoed and clamped to 0.
+  bool valid = dst >= 0 && dst < a.num_units;
+  if (!valid) {
+    src = 0;
+    dst = 0;
+  }
+  if (valid && a.pruned != nullptr) valid = !a.pruned[src] && !a.pruned[dst];
+  if (valid) {
+    const int32_t ls = a.level[src], ld = a.level[dst];
+    const int32_t gap = ld > ls ? ld - ls : ls - ld;
+    valid = gap <= a.max_level_gap;
+    if (!a.allow_self_loops) valid = valid && src != dst;
+    if (a.direction == 1) valid = valid && ld > ls;
+    else if (a.direction == 2) valid = valid && ld >= ls;
+    if (a.bucket_level >= 0) valid = valid && ls == a.bucket_level;
+    if (a.src_level_bound > 0) valid = valid && ls < a.src_level_bound;
+  }
+  if (!valid || !isfinite(score)) score = -__int_as_float(0x7f800000);
+  src_o = src;
+  dst_o = dst;
+  score_o = score;
+}
+
 __global__ void propose_per_unit_kernel(ProposeArgs a, int32_t *__restrict__ src_out,
                                         int32_t *__restrict__ dst_out, float *__restrict__ score_out) {
   const int64_t total = static_cast<int64_t>(a.num_units) * a.proposals;
-  if (a.step_dev != nullptr) {
-    __shared__ uint64_t keyed;
-    if (threadIdx.x == 0)
-      keyed = philox32(a.network_seed, (static_cast<uint64_t>(static_cast<uint32_t>(*a.step_dev)) << 8) | 1u);
-    __syncthreads();
-    a.keyed_hi = keyed;
-  }
+  const uint64_t keyed_hi = keyed_hi_of(a);
   for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < total;
        c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int32_t i = static_cast<int32_t>(c / a.proposals);
-    const uint32_t j = static_cast<uint32_t>(c - static_cast<int64_t>(i) * a.proposals);
-    const uint64_t seed = (a.keyed_hi << 32) | static_cast<uint32_t>(i);
-    int32_t src = i;
-    int32_t dst = a.dst_lo + static_cast<int32_t>(uniform_int(unit_float(site_draw(seed, j, 0)), a.dst_n));
+    int32_t src, dst;
     float score;
-    if (a.score_kind == PXB_SCORE_UNIFORM) {
-      score = unit_float(site_draw(seed, j, 1));
-    } else if (a.score_kind == PXB_SCORE_UNIFORM_Q256) {
-      const float u = unit_float(site_draw(seed, j, 1));
-      score = static_cast<float>(static_cast<int32_t>(__fmul_rn(u, 256.0f))) * (1.0f / 256.0f);
-    } else {
-      score = (dst >= 0 && dst < a.num_units) ? fabsf(__fmul_rn(a.grad[dst], a.act[src])) : 0.0f;
-    }
-    // _clamp_proposals: out-of-range ids are vetoed and clamped to 0.
-    bool valid = dst >= 0 && dst < a.num_units;
-    if (!valid) {
-      src = 0;
-      dst = 0;
-    }
-    if (valid && a.pruned != nullptr) valid = !a.pruned[src] && !a.pruned[dst];
-    if (valid) {
-      const int32_t ls = a.level[src], ld = a.level[dst];
-      const int32_t gap = ld > ls ? ld - ls : ls - ld;
-      valid = gap <= a.max_level_gap;
-      if (!a.allow_self_loops) valid = valid && src != dst;
-      if (a.direction == 1) valid = valid && ld > ls;
-      else if (a.direction == 2) valid = valid && ld >= ls;
-      if (a.bucket_level >= 0) valid = valid && ls == a.bucket_level;
-      if (a.src_level_bound > 0) valid = valid && ls < a.src_level_bound;
-    }
-    if (!valid || !isfinite(score)) score = -__int_as_float(0x7f800000);
+    propose_one(a, keyed_hi, c, src, dst, score);
     src_out[c] = src;
     dst_out[c] = dst;
     score_out[c] = score;
@@ -545,6 +562,345 @@ size_t total_order_bytes(int64_t n, int32_t id_bound) {
   if (order_scratch(n, bits_for(id_bound), nullptr, &o) != PXB_OK) return ~size_t(0);
   return o.total;
 }
+// ---------------------------------------------------------------------------
+// Fused selection for one Philox-scored proposal per unit (score uniform or
+// uniform_q256): the proposals, the first k of the total order and their
+// level-major listing, gathered into the claim's input columns.
+//
+// Each candidate gets a unique key whose order is the total order: a valid
+// candidate 0 | (2^b - 1 - m) | src, with m the score's b-bit integer
+// (score = m * 2^-b), an invalid one 1 | src | 0. The top bin_bits of the
+// key name its bin; bins are sized for ~256 candidates (the score integers
+// are Philox draws, and an invalid bin spans a fixed range of sources), so
+// a bin is ordered by ranking its members in shared memory. The threshold
+// bin is found from the (level, bin) histogram, the winners of full bins are
+// scattered into level-major bins, and the threshold bin's best r are
+// ranked apart. A bin larger than kFsRankCap is ranked from global memory
+// (up to kFsSlowCap members; beyond that status bit 0 is set and the list
+// is incomplete -- never reached by Philox-scored proposals in practice).
+// ---------------------------------------------------------------------------
+constexpr int kFsMaxLevels = 8;
+constexpr int kFsRankCap = 4096;
+constexpr int kFsSlowCap = 1 << 16;
+constexpr int kFsThreads = 256;
+constexpr int kFsMaxBinBits = 13;
+constexpr int kFsMaxIpt = (1 << kFsMaxBinBits) / 1024;
+
+struct FsGeom {
+  int32_t n, L, nb;
+  int64_t k;
+  int src_bits, score_bits, key_bits, bin_bits;
+};
+
+struct FsInfo {
+  int32_t tb, r, count, tcount;
+  int32_t C[kFsMaxLevels], R[kFsMaxLevels], F[kFsMaxLevels], T[kFsMaxLevels];
+};
+
+struct FsScratch {
+  uint64_t *keys, *tk, *bk;
+  int32_t *dst, *ti, *bi, *byrank;
+  uint32_t *hist, *cursor, *toff;
+  FsInfo *info;
+  size_t total;
+};
+
+__device__ __forceinline__ uint64_t fs_key(const FsGeom &g, int kind, float score, int32_t src) {
+  const uint64_t s = static_cast<uint32_t>(src);
+  if (!(score >= 0.0f)) return (uint64_t(1) << (g.key_bits - 1)) | (s << g.score_bits);
+  const uint32_t m = kind == PXB_SCORE_UNIFORM ? static_cast<uint32_t>(score * 16777216.0f)
+                                                : static_cast<uint32_t>(score * 256.0f);
+  const uint64_t d = ((uint64_t(1) << g.score_bits) - 1) - m;
+  return (d << g.src_bits) | s;
+}
+__device__ __forceinline__ bool fs_valid(const FsGeom &g, uint64_t key) { return !(key >> (g.key_bits - 1)); }
+__device__ __forceinline__ int32_t fs_src(const FsGeom &g, uint64_t key) {
+  const uint64_t mask = (uint64_t(1) << g.src_bits) - 1;
+  return static_cast<int32_t>(fs_valid(g, key) ? (key & mask) : ((key >> g.score_bits) & mask));
+}
+__device__ __forceinline__ int32_t fs_bin(const FsGeom &g, uint64_t key) {
+  return static_cast<int32_t>(key >> (g.key_bits - g.bin_bits));
+}
+__device__ __forceinline__ int32_t fs_level(const FsGeom &g, const int32_t *level, int32_t src) {
+  const int32_t l = level[src];
+  return l < 0 ? 0 : (l >= g.L ? g.L - 1 : l);
+}
+
+__global__ void __launch_bounds__(kFsThreads) fs_propose_kernel(ProposeArgs a, FsGeom g, FsScratch o) {
+  const uint64_t keyed_hi = keyed_hi_of(a);
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < g.n;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int32_t src, dst;
+    float score;
+    propose_one(a, keyed_hi, c, src, dst, score);
+    const uint64_t key = fs_key(g, a.score_kind, score, src);
+    o.keys[c] = key;
+    o.dst[c] = dst;
+    atomicAdd(o.hist + fs_level(g, a.level, src) * g.nb + fs_bin(g, key), 1u);
+  }
+}
+
+// One block: the threshold bin, the level counts and the temp offsets of the
+// full bins (level-major), cursors zeroed. Thread t owns the consecutive bins
+// [t * ipt, (t + 1) * ipt): one block scan finds the threshold bin and one
+// per level lays out the full bins.
+__global__ void __launch_bounds__(1024) fs_threshold_kernel(FsGeom g, FsScratch o) {
+  using Scan = cub::BlockScan<int32_t, 1024>;
+  __shared__ typename Scan::TempStorage ts;
+  __shared__ int32_t s_tb, s_excl;
+  FsInfo *info = o.info;
+  const int ipt = (g.nb + 1023) / 1024;  // <= kFsMaxIpt (bins are capped at 8192)
+  const int b0 = threadIdx.x * ipt;
+  if (threadIdx.x == 0) {
+    s_tb = g.nb;
+    s_excl = 0;
+  }
+  // this thread's bin totals over the levels, every load issued at once
+  int32_t tot[kFsMaxIpt];
+#pragma unroll
+  for (int j = 0; j < kFsMaxIpt; ++j) tot[j] = 0;
+  for (int l = 0; l < g.L; ++l) {
+#pragma unroll
+    for (int j = 0; j < kFsMaxIpt; ++j)
+      if (j < ipt && b0 + j < g.nb) tot[j] += static_cast<int32_t>(o.hist[l * g.nb + b0 + j]);
+  }
+  int32_t mine = 0;
+#pragma unroll
+  for (int j = 0; j < kFsMaxIpt; ++j) mine += tot[j];
+  int32_t ex, agg;
+  Scan(ts).ExclusiveSum(mine, ex, agg);
+  if (g.k < g.n && ex < g.k && ex + mine >= g.k) {  // the crossing lies in my bins
+    int32_t cum = ex;
+    bool found = false;
+#pragma unroll
+    for (int j = 0; j < kFsMaxIpt; ++j) {
+      if (!found && j < ipt && cum + tot[j] >= g.k) {
+        s_tb = b0 + j;
+        s_excl = cum;
+        found = true;
+      }
+      cum += tot[j];
+    }
+  }
+  __syncthreads();
+  const int32_t tb = s_tb;
+  int32_t t_run = 0;
+  for (int l = 0; l < g.L; ++l) {
+    int32_t v[kFsMaxIpt];
+    int32_t lm = 0;
+#pragma unroll
+    for (int j = 0; j < kFsMaxIpt; ++j) {
+      v[j] = (j < ipt && b0 + j < tb) ? static_cast<int32_t>(o.hist[l * g.nb + b0 + j]) : 0;
+      lm += v[j];
+    }
+    int32_t lex, lagg;
+    __syncthreads();  // the scan storage is reused
+    Scan(ts).ExclusiveSum(lm, lex, lagg);
+    int32_t run = t_run + lex;
+#pragma unroll
+    for (int j = 0; j < kFsMaxIpt; ++j) {
+      if (j < ipt && b0 + j < g.nb) {
+        o.toff[l * g.nb + b0 + j] = static_cast<uint32_t>(run);
+        o.cursor[l * g.nb + b0 + j] = 0;
+      }
+      run += v[j];
+    }
+    if (threadIdx.x == 0) {
+      info->C[l] = lagg;
+      info->T[l] = t_run;
+    }
+    t_run += lagg;
+  }
+  if (threadIdx.x == 0) {
+    info->tb = tb;
+    info->r = tb < g.nb ? static_cast<int32_t>(g.k - s_excl) : 0;
+    info->count = static_cast<int32_t>(g.k < g.n ? g.k : g.n);
+    info->tcount = 0;
+  }
+}
+
+__global__ void __launch_bounds__(kFsThreads) fs_scatter_kernel(FsGeom g, const int32_t *__restrict__ level,
+                                                                 FsScratch o) {
+  const int32_t tb = o.info->tb;
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < g.n;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t key = o.keys[c];
+    const int32_t b = fs_bin(g, key);
+    if (b < tb) {
+      const int32_t slot = fs_level(g, level, fs_src(g, key)) * g.nb + b;
+      const uint32_t pos = o.toff[slot] + atomicAdd(o.cursor + slot, 1u);
+      o.bk[pos] = key;
+      o.bi[pos] = static_cast<int32_t>(c);
+    } else if (b == tb) {
+      const int32_t p = atomicAdd(&o.info->tcount, 1);
+      o.tk[p] = key;
+      o.ti[p] = static_cast<int32_t>(c);
+    }
+  }
+}
+
+// Rank of each of m unique keys (the number of smaller keys), from shared
+// memory when they fit, else from global memory. Returns false (and ranks
+// nothing) past kFsSlowCap.
+__device__ __forceinline__ bool fs_rank(const uint64_t *keys_g, int32_t m, uint64_t *keys_s, int32_t *rank_out) {
+  if (m > kFsSlowCap) return false;
+  const bool in_smem = m <= kFsRankCap;
+  if (in_smem) {
+    for (int e = threadIdx.x; e < m; e += blockDim.x) keys_s[e] = keys_g[e];
+    __syncthreads();
+  }
+  const uint64_t *src = in_smem ? keys_s : keys_g;
+  for (int e = threadIdx.x; e < m; e += blockDim.x) {
+    const uint64_t ke = src[e];
+    int32_t r = 0;
+    for (int f = 0; f < m; ++f) r += src[f] < ke ? 1 : 0;
+    rank_out[e] = r;
+  }
+  __syncthreads();
+  return true;
+}
+
+__device__ __forceinline__ void fs_emit(const FsGeom &g, const FsScratch &o, const InitArgs &ia, uint64_t key,
+                                        int32_t c, int64_t pos, int32_t *s_out, int32_t *d_out, float *w_out,
+                                        uint8_t *grow_out) {
+  const int32_t s = fs_src(g, key), d = o.dst[c];
+  s_out[pos] = s;
+  d_out[pos] = d;
+  w_out[pos] = init_weight(ia, s, d);
+  grow_out[pos] = fs_valid(g, key) ? 1 : 0;
+}
+
+// One block: the threshold bin's best r, their level counts, the level
+// bases of the final list, and the zero fill past min(k, n).
+__global__ void __launch_bounds__(1024) fs_threshold_bin_kernel(FsGeom g, const int32_t *__restrict__ level,
+                                                                InitArgs ia, FsScratch o, int32_t *s_out,
+                                                                int32_t *d_out, float *w_out, uint8_t *grow_out,
+                                                                int32_t *status) {
+  using Scan = cub::BlockScan<int32_t, 1024>;
+  __shared__ typename Scan::TempStorage ts;
+  __shared__ uint64_t keys_s[kFsRankCap];
+  __shared__ int32_t s_carry;
+  FsInfo *info = o.info;
+  const int32_t m = info->tcount;
+  int32_t r = info->r;
+  int32_t *rank = o.ti + g.n;  // member ranks, then level positions (the scratch holds 3n)
+  if (r > 0 && !fs_rank(o.tk, m, keys_s, rank)) {
+    // unreachable for Philox scores; the list is flagged and the threshold
+    // bin's winners are left out, every write staying in range
+    if (threadIdx.x == 0 && status) atomicOr(status, 1);
+    r = 0;
+  }
+  // winners by rank
+  if (r > 0)
+    for (int e = threadIdx.x; e < m; e += blockDim.x)
+      if (rank[e] < r) o.byrank[rank[e]] = e;
+  __syncthreads();
+  int32_t R[kFsMaxLevels];
+  for (int l = 0; l < g.L; ++l) {
+    if (threadIdx.x == 0) s_carry = 0;
+    __syncthreads();
+    for (int base = 0; base < r; base += 1024) {
+      const int p = base + threadIdx.x;
+      int32_t f = 0;
+      if (p < r) f = fs_level(g, level, fs_src(g, o.tk[o.byrank[p]])) == l ? 1 : 0;
+      int32_t ex, agg;
+      Scan(ts).ExclusiveSum(f, ex, agg);
+      if (f) rank[g.n + p] = s_carry + ex;  // position among level-l winners (scratch after ranks)
+      __syncthreads();
+      if (threadIdx.x == 0) s_carry += agg;
+      __syncthreads();
+    }
+    R[l] = s_carry;
+    __syncthreads();
+  }
+  int32_t F[kFsMaxLevels];
+  int32_t run = 0;
+  for (int l = 0; l < g.L; ++l) {
+    F[l] = run;
+    run += info->C[l] + R[l];
+  }
+  for (int p = threadIdx.x; p < r; p += blockDim.x) {
+    const int32_t e = o.byrank[p];
+    const uint64_t key = o.tk[e];
+    const int32_t l = fs_level(g, level, fs_src(g, key));
+    fs_emit(g, o, ia, key, o.ti[e], F[l] + info->C[l] + rank[g.n + p], s_out, d_out, w_out, grow_out);
+  }
+  const int64_t filled = r == info->r ? info->count : run;
+  for (int64_t p = filled + threadIdx.x; p < g.k; p += blockDim.x) {
+    s_out[p] = 0;
+    d_out[p] = 0;
+    w_out[p] = 0.0f;
+    grow_out[p] = 0;
+  }
+  if (threadIdx.x == 0)
+    for (int l = 0; l < g.L; ++l) {
+      info->R[l] = R[l];
+      info->F[l] = F[l];
+    }
+}
+
+// The full bins: each (level, bin) pair ranked and emitted at its final
+// position.
+__global__ void __launch_bounds__(kFsThreads) fs_bins_kernel(FsGeom g, InitArgs ia, FsScratch o, int32_t *s_out,
+                                                             int32_t *d_out, float *w_out, uint8_t *grow_out,
+                                                             int32_t *rank_scratch, int32_t *status) {
+  __shared__ uint64_t keys_s[kFsRankCap];
+  const FsInfo *info = o.info;
+  const int32_t tb = info->tb < g.nb ? info->tb : g.nb;
+  const int64_t pairs = static_cast<int64_t>(g.L) * tb;
+  for (int64_t q = blockIdx.x; q < pairs; q += gridDim.x) {
+    const int32_t l = static_cast<int32_t>(q / tb), b = static_cast<int32_t>(q % tb);
+    const int32_t m = static_cast<int32_t>(o.hist[l * g.nb + b]);
+    if (m == 0) continue;
+    const uint32_t t0 = o.toff[l * g.nb + b];
+    int32_t *rank = rank_scratch + t0;
+    if (!fs_rank(o.bk + t0, m, keys_s, rank)) {
+      if (threadIdx.x == 0 && status) atomicOr(status, 1);
+      continue;
+    }
+    const int64_t base = static_cast<int64_t>(info->F[l]) + (t0 - info->T[l]);
+    for (int e = threadIdx.x; e < m; e += blockDim.x)
+      fs_emit(g, o, ia, o.bk[t0 + e], o.bi[t0 + e], base + rank[e], s_out, d_out, w_out, grow_out);
+    __syncthreads();
+  }
+}
+
+static int fs_geom(int32_t num_units, int64_t k, int32_t num_levels, int32_t score_kind, FsGeom *g) {
+  g->n = num_units;
+  g->k = k;
+  g->L = num_levels;
+  g->src_bits = bits_for(num_units);
+  g->score_bits = score_kind == PXB_SCORE_UNIFORM ? 24 : 8;
+  g->key_bits = 1 + g->score_bits + g->src_bits;
+  int bb = 1;
+  while (bb < kFsMaxBinBits && (int64_t(num_units) >> bb) > 128) ++bb;  // ~256 valid candidates per bin
+  g->bin_bits = bb < g->key_bits ? bb : g->key_bits;
+  g->nb = 1 << g->bin_bits;
+  return g->key_bits <= 64 ? PXB_OK : PXB_EINVAL;
+}
+
+static void fs_layout(const FsGeom &g, char *base, FsScratch *o) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = off;
+    off = align_up(off + (bytes ? bytes : 1), 256);
+    return base ? base + at : nullptr;
+  };
+  const int64_t n = g.n, kk = g.k > 0 ? g.k : 1, hb = int64_t(g.L) * g.nb;
+  o->keys = reinterpret_cast<uint64_t *>(take(n * 8));
+  o->dst = reinterpret_cast<int32_t *>(take(n * 4));
+  o->tk = reinterpret_cast<uint64_t *>(take(n * 8));
+  o->ti = reinterpret_cast<int32_t *>(take(n * 4 * 3));  // members, their ranks, level positions
+  o->bk = reinterpret_cast<uint64_t *>(take(kk * 8));
+  o->bi = reinterpret_cast<int32_t *>(take(kk * 4 * 2));  // indices, then ranks
+  o->byrank = reinterpret_cast<int32_t *>(take(n * 4));
+  o->hist = reinterpret_cast<uint32_t *>(take(hb * 4));
+  o->cursor = reinterpret_cast<uint32_t *>(take(hb * 4));
+  o->toff = reinterpret_cast<uint32_t *>(take(hb * 4));
+  o->info = reinterpret_cast<FsInfo *>(take(sizeof(FsInfo)));
+  o->total = off;
+}
+
 }  // namespace pxb
 
 extern "C" int pxb_total_order(int64_t n, const float *score, const int32_t *src, const int32_t *dst,
@@ -611,5 +967,72 @@ extern "C" int pxb_gather_winners(int64_t k, int64_t count, const int32_t *win_i
   gather_winners_kernel<<<grid_for(k, 256, 8), 256, 0, as_stream(stream)>>>(
       k, count, win_idx, src, dst, score, ia, src_out, dst_out, weight_out, growable_out);
   PXB_LAUNCHED("gather_winners_kernel");
+  return PXB_OK;
+}
+
+extern "C" int pxb_select_unique_scratch_bytes(int32_t num_units, int64_t k, int32_t num_levels, int32_t score_kind,
+                                               size_t *bytes) {
+  PXB_REQUIRE(bytes && num_units >= 1 && k >= 0 && num_levels >= 1 && num_levels <= kFsMaxLevels,
+              "pxb_select_unique_scratch_bytes: bad arguments");
+  PXB_REQUIRE(score_kind == PXB_SCORE_UNIFORM || score_kind == PXB_SCORE_UNIFORM_Q256,
+              "pxb_select_unique_scratch_bytes: the score must be uniform or uniform_q256");
+  FsGeom g;
+  if (fs_geom(num_units, k, num_levels, score_kind, &g) != PXB_OK) {
+    set_error("pxb_select_unique_scratch_bytes: %d units need too many key bits", num_units);
+    return PXB_EINVAL;
+  }
+  FsScratch o;
+  fs_layout(g, nullptr, &o);
+  *bytes = o.total;
+  return PXB_OK;
+}
+
+extern "C" int pxb_propose_select_unique(int32_t num_units, uint64_t network_seed, int32_t step, int32_t dst_lo,
+                                         int32_t dst_n, int32_t score_kind, const int32_t *level,
+                                         const uint8_t *pruned, int32_t max_level_gap, int32_t direction,
+                                         int32_t allow_self_loops, int32_t src_level_bound,
+                                         const int32_t *step_dev, int64_t k, int32_t num_levels, int32_t init_kind,
+                                         float init_a, float init_b, uint32_t init_salt, int32_t *src_out,
+                                         int32_t *dst_out, float *weight_out, uint8_t *growable_out,
+                                         int32_t *status, void *scratch, size_t scratch_bytes, void *stream) {
+  PXB_REQUIRE(num_units >= 1 && k >= 0, "pxb_propose_select_unique: bad sizes");
+  PXB_REQUIRE(num_levels >= 1 && num_levels <= kFsMaxLevels, "pxb_propose_select_unique: num_levels %d not in [1, %d]",
+              num_levels, kFsMaxLevels);
+  PXB_REQUIRE(score_kind == PXB_SCORE_UNIFORM || score_kind == PXB_SCORE_UNIFORM_Q256,
+              "pxb_propose_select_unique: the score must be uniform or uniform_q256");
+  PXB_REQUIRE(dst_n >= 1 && dst_lo >= 0 && int64_t(dst_lo) + dst_n <= num_units,
+              "pxb_propose_select_unique: destinations [%d, %lld) exceed the %d units", dst_lo,
+              static_cast<long long>(dst_lo) + dst_n, num_units);
+  PXB_REQUIRE(init_kind >= 0 && init_kind <= 2, "pxb_propose_select_unique: unknown init kind %d", init_kind);
+  if (k == 0) return PXB_OK;
+  PXB_REQUIRE(level && src_out && dst_out && weight_out && growable_out && scratch,
+              "pxb_propose_select_unique: a pointer is NULL");
+  FsGeom g;
+  if (fs_geom(num_units, k, num_levels, score_kind, &g) != PXB_OK) {
+    set_error("pxb_propose_select_unique: %d units need too many key bits", num_units);
+    return PXB_EINVAL;
+  }
+  FsScratch o;
+  fs_layout(g, static_cast<char *>(scratch), &o);
+  PXB_REQUIRE(o.total <= scratch_bytes, "pxb_propose_select_unique: scratch has %zu bytes, needs %zu",
+              scratch_bytes, o.total);
+  ProposeArgs a{num_units, 1, 0, network_seed, step_dev, dst_lo, dst_n, score_kind, nullptr, nullptr, level,
+                pruned, max_level_gap, direction, allow_self_loops, -1, src_level_bound};
+  if (step_dev == nullptr) a.keyed_hi = philox32(network_seed, (static_cast<uint64_t>(static_cast<uint32_t>(step)) << 8) | 1u);
+  InitArgs ia{init_kind, init_a, init_b, init_salt};
+  cudaStream_t st = as_stream(stream);
+  PXB_CUDA(cudaMemsetAsync(o.hist, 0, size_t(g.L) * g.nb * 4, st));
+  const int grid = grid_for(num_units, kFsThreads, 8);
+  fs_propose_kernel<<<grid, kFsThreads, 0, st>>>(a, g, o);
+  PXB_LAUNCHED("fs_propose_kernel");
+  fs_threshold_kernel<<<1, 1024, 0, st>>>(g, o);
+  PXB_LAUNCHED("fs_threshold_kernel");
+  fs_scatter_kernel<<<grid, kFsThreads, 0, st>>>(g, level, o);
+  PXB_LAUNCHED("fs_scatter_kernel");
+  fs_threshold_bin_kernel<<<1, 1024, 0, st>>>(g, level, ia, o, src_out, dst_out, weight_out, growable_out, status);
+  PXB_LAUNCHED("fs_threshold_bin_kernel");
+  fs_bins_kernel<<<sm_count() * 8, kFsThreads, 0, st>>>(g, ia, o, src_out, dst_out, weight_out, growable_out,
+                                                        o.bi + (g.k > 0 ? g.k : 1), status);
+  PXB_LAUNCHED("fs_bins_kernel");
   return PXB_OK;
 }

@@ -276,11 +276,13 @@ __global__ void unit_apply_kernel(int32_t n, int mode, int act_kind, int monoid,
   if (pruned != nullptr && pruned[i]) return;
   float a = acc[i];
   if (acc_fixed != nullptr) {
-    // the exact fixed-point sum plus the float side (non-finite or huge
-    // products), rounded to float once
-    a = static_cast<float>(fma(static_cast<double>(acc_fixed[i]), 1.0 / double(1ll << PXB_FIXED_FRAC_BITS),
-                               static_cast<double>(a)));
-    acc_fixed[i] = 0;
+    // the exact fixed-point sum, rounded to float once (the scale is a power
+    // of two), plus the float side (non-finite or huge products, normally 0)
+    const long long f = acc_fixed[i];
+    if (f != 0) {
+      a = __fadd_rn(__fmul_rn(__ll2float_rn(f), 1.0f / float(1 << PXB_FIXED_FRAC_BITS)), a);
+      acc_fixed[i] = 0;
+    }
   }
   if (mode == 0) {
     out[i] = act_fn(act_kind, a);

@@ -262,6 +262,38 @@ def topk_unique(score: torch.Tensor, src: torch.Tensor, id_bound: int, k: int, o
     return out[:kk]
 
 
+def select_unique_scratch(num_units: int, k: int, num_levels: int, score_kind: int) -> int:
+    return query_size("pxb_select_unique_scratch_bytes", ctypes.c_int32(num_units), ctypes.c_int64(k),
+                      ctypes.c_int32(num_levels), ctypes.c_int32(score_kind))
+
+
+def propose_select_unique(num_units: int, network_seed: int, step: int, *, dst_lo: int, dst_n: int, score_kind: int,
+                          level: torch.Tensor, k: int, num_levels: int, init_kind: int, init_a: float = 0.0,
+                          init_b: float = 0.0, init_salt: int = 0, pruned: torch.Tensor | None = None,
+                          max_level_gap: int = 1, direction: int = 0, allow_self_loops: bool = False,
+                          src_level_bound: int = 0, step_dev: torch.Tensor | None = None,
+                          status: torch.Tensor | None = None, scratch: torch.Tensor | None = None,
+                          out: tuple | None = None) -> tuple[torch.Tensor, ...]:
+    """One proposal per unit scored by the site RNG: proposals, the first k of
+    the total order listed levels ascending, gathered as the claim's inputs
+    (src, dst, init weight, growable)."""
+    dev = level.device
+    if out is None:
+        out = (torch.empty(k, dtype=torch.int32, device=dev), torch.empty(k, dtype=torch.int32, device=dev),
+               torch.empty(k, dtype=torch.float32, device=dev), torch.empty(k, dtype=torch.uint8, device=dev))
+    if scratch is None:
+        need = select_unique_scratch(num_units, k, num_levels, score_kind)
+        scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    s, d, w, g = out
+    call("pxb_propose_select_unique", ctypes.c_int32(num_units), ctypes.c_uint64(network_seed), ctypes.c_int32(step),
+         ctypes.c_int32(dst_lo), ctypes.c_int32(dst_n), ctypes.c_int32(score_kind), ptr(level), ptr(pruned),
+         ctypes.c_int32(max_level_gap), ctypes.c_int32(direction), ctypes.c_int32(1 if allow_self_loops else 0),
+         ctypes.c_int32(src_level_bound), ptr(step_dev), ctypes.c_int64(k), ctypes.c_int32(num_levels),
+         ctypes.c_int32(init_kind), ctypes.c_float(init_a), ctypes.c_float(init_b), ctypes.c_uint32(init_salt),
+         ptr(s), ptr(d), ptr(w), ptr(g), ptr(status), ptr(scratch), ctypes.c_size_t(scratch.numel()), _stream())
+    return s, d, w, g
+
+
 def select_step_scratch(n: int, k: int) -> int:
     return query_size("pxb_select_step_scratch_bytes", ctypes.c_int64(n), ctypes.c_int64(k))
 
@@ -354,6 +386,16 @@ def claim_commit(mode: int, b: Bucket, unit_level: torch.Tensor, tail_start: tor
          ptr(ws.scratch), ctypes.c_size_t(ws.scratch.numel()), _stream())
 
 
+def growth_flags(counts: torch.Tensor, *, reset: bool, grown: torch.Tensor | None,
+                 overflow: torch.Tensor | None, needs_resort: torch.Tensor | None) -> None:
+    """grown (+)= counts[0]; overflow |= counts[1] > 0; needs_resort |= counts[3] > 0."""
+    for t, dt in ((grown, torch.int32), (overflow, torch.bool), (needs_resort, torch.bool)):
+        if t is not None:
+            _check(t, dt, 1, "growth_flags")
+    call("pxb_growth_flags", ptr(counts), ctypes.c_int32(1 if reset else 0), ptr(grown), ptr(overflow),
+         ptr(needs_resort), _stream())
+
+
 def count_dead(b: Bucket, out: torch.Tensor) -> None:
     cap = _bucket(b)
     call("pxb_count_dead", ctypes.c_int64(cap), ptr(b["dead"]), ptr(out), _stream())
@@ -363,7 +405,7 @@ def free_bitmap_build(mode: int, b: Bucket, unit_level: torch.Tensor, tail_start
                       num_levels: int, *, shard_base: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
     """Per-domain free-slot bitmaps of a bucket (int32 view of uint32 words)."""
     cap = _bucket(b)
-    rows = 1 if mode == _lib.CLAIM_TOPOLOGICAL else num_levels
+    rows = 1 if (mode & ~_lib.CLAIM_LEVEL_MAJOR) == _lib.CLAIM_TOPOLOGICAL else num_levels
     words = (cap + 31) // 32
     if out is None:
         out = torch.zeros(rows * max(words, 1), dtype=torch.int32, device=b["dead"].device)

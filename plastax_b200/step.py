@@ -219,6 +219,15 @@ class StepFn:
         self.score_kind = {"uniform": _lib.SCORE_UNIFORM, "uniform_q256": _lib.SCORE_UNIFORM_Q256,
                            "grad_act": _lib.SCORE_GRAD_ACT}[ac.score]
         self.direction = {"any": 0, "deeper": 1, "same_or_deeper": 2}[ac.direction]
+        # one proposal per unit scored by the site RNG: the fused selection
+        # (keys binned and ranked, no sort pass) replaces propose + top-k +
+        # level listing + gather
+        self.fast_select = (self.unique_src and ac.score in ("uniform", "uniform_q256")
+                            and self.static.num_levels <= 8 and self.k > 0)
+        if self.fast_select:
+            need = K.select_unique_scratch(n, self.k, self.static.num_levels, self.score_kind)
+            self.fs_scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+            self.fs_status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.grown = torch.zeros((), dtype=torch.int32, device=dev)
         self.overflow = torch.zeros((), dtype=torch.bool, device=dev)
         self.placed = torch.empty(kk, dtype=torch.int32, device=dev)
@@ -399,6 +408,16 @@ class StepFn:
         pruned = units.get(PRUNED.name)
         dst_n = ac.dst_n if ac.dst_n is not None else n - ac.dst_lo
         grad = units.get(ac.grad_field.name) if ac.score == "grad_act" else None
+        if self.fast_select:
+            K.propose_select_unique(n, st.seed, state.step, dst_lo=ac.dst_lo, dst_n=dst_n, score_kind=self.score_kind,
+                                    level=level, k=self.k, num_levels=st.num_levels, init_kind=self.init_kind,
+                                    init_a=self.init_a, pruned=pruned, max_level_gap=ac.max_level_gap,
+                                    direction=self.direction, allow_self_loops=ac.allow_self_loops,
+                                    src_level_bound=0 if self.pipeline else self.num_buckets,
+                                    step_dev=self.step_dev, status=self.fs_status, scratch=self.fs_scratch,
+                                    out=self.claim_in)
+            self.launches += 6
+            return
         K.propose_per_unit(n, ac.proposals_per_proposer, st.seed, state.step, dst_lo=ac.dst_lo, dst_n=dst_n,
                            score_kind=self.score_kind, level=level, grad=grad, act=units[ACTIVATION.name],
                            pruned=pruned, max_level_gap=ac.max_level_gap, direction=self.direction,
@@ -425,9 +444,9 @@ class StepFn:
             return None
         st = self.static
         level = state.units[LEVEL.name]
-        self.grown.zero_()
-        self.overflow.zero_()
         if not self._fires(state) or self.k == 0:
+            self.grown.zero_()
+            self.overflow.zero_()
             state.grown, state.overflow = self.grown, self.overflow
             return None
         if not selected:
@@ -435,7 +454,8 @@ class StepFn:
         cs, cd, cw, grow = self.claim_in
         max_new = -1 if ac.max_new_per_step is None else int(ac.max_new_per_step)
         if self.pipeline:
-            mode = _lib.CLAIM_PIPELINE
+            # the winners are listed levels ascending: the claim partitions
+            mode = _lib.CLAIM_PIPELINE | _lib.CLAIM_LEVEL_MAJOR
             buckets = [(0, grow)]
         else:
             mode = _lib.CLAIM_TOPOLOGICAL
@@ -447,7 +467,7 @@ class StepFn:
             lv = level[cs.long()]
             buckets = [(bk, (g & (lv == bk)).to(torch.uint8)) for bk in range(self.num_buckets)]
             max_new = -1
-        for bk, gb in buckets:
+        for bi, (bk, gb) in enumerate(buckets):
             b, ws = state.conns[bk], self.claim_ws[bk]
             base = st.shard_base(bk)
             bm, _ = self._bm(bk)
@@ -465,9 +485,8 @@ class StepFn:
                            extra=self.extra_defaults, free_bitmap=bm, placed=self.placed)
             if self.use_mirror:
                 K.mirror_insert(self.mirrors[bk], cs, cd, cw, self.placed)
-            self.grown += ws.counts[0]
-            self.overflow |= ws.counts[1] > 0
-            state.needs_resort |= ws.counts[3] > 0
+            K.growth_flags(ws.counts, reset=bi == 0, grown=self.grown, overflow=self.overflow,
+                           needs_resort=state.needs_resort)
             self.launches += 12
         state.grown, state.overflow = self.grown, self.overflow
         if ac.on_overflow == "error" and bool(self.overflow.item()):

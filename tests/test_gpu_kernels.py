@@ -318,11 +318,14 @@ def _claim_case(rng, cap, n, k, *, pipeline, dead_frac, tail_frac, levels=3):
     return b, level, tail, src, dst, w, grow, age
 
 
+@pytest.mark.parametrize("level_major", [False, True])
 @pytest.mark.parametrize("use_bitmap", [False, True])
 @pytest.mark.parametrize("cap,k,dead_frac,tail_frac,max_new",
                          [(100_000, 5000, 0.02, 0.01, -1), (100_000, 20_000, 0.05, 0.02, -1),
                           (4096, 300, 0.1, 0.0, -1), (1 << 20, 30_000, 0.01, 0.005, 20_000), (777, 1000, 0.3, 0.1, -1)])
-def test_claim_pipeline(cuda, cap, k, dead_frac, tail_frac, max_new, use_bitmap):
+def test_claim_pipeline(cuda, cap, k, dead_frac, tail_frac, max_new, use_bitmap, level_major):
+    """The list is level-major (non-growable entries interleaved); the
+    level-major mode partitions where the other sorts, same result."""
     import torch
 
     kern = _k()
@@ -340,8 +343,9 @@ def test_claim_pipeline(cuda, cap, k, dead_frac, tail_frac, max_new, use_bitmap)
     nl = int(level.max()) + 1
     ws = kern.ClaimWorkspace(cap, k, nl, cuda)
     bm = kern.free_bitmap_build(0, db, d_level, d_tail, nl) if use_bitmap else None
-    kern.claim_prepare(0, db, d_level, d_tail, ws, free_bitmap=bm)
-    kern.claim_commit(0, db, d_level, d_tail, ws, t(src), t(dst), t(w), t(grow), max_new=max_new,
+    mode = 0x100 if level_major else 0
+    kern.claim_prepare(mode, db, d_level, d_tail, ws, free_bitmap=bm)
+    kern.claim_commit(mode, db, d_level, d_tail, ws, t(src), t(dst), t(w), t(grow), max_new=max_new,
                       extra={"test/age": t(age)}, free_bitmap=bm)
     hb = to_host(db)
     if use_bitmap:  # the bitmaps stay equal to a rebuild from the new columns
@@ -600,5 +604,65 @@ def test_mirror_sum_is_exact_fixed_point(cuda):
         got.append(_fixed_total(kern, acc, acc_fixed))
     assert int((np.abs(want_fixed) > (8 << 28)).sum()) > 0, "no unit exceeded the 32-bit word's range"
     np.testing.assert_array_equal(got[0], got[1])
-    want = (want_fixed.astype(np.float64) * 2.0 ** -28 + side.astype(np.float64)).astype(np.float32)
+    # one rounding of the exact sum, then the float side added as a float
+    want = want_fixed.astype(np.float32) * np.float32(2.0 ** -28) + side
     np.testing.assert_array_equal(got[0], want)
+
+
+@pytest.mark.parametrize("n,k,levels,kind,opts", [
+    (5000, 1300, 2, 0, {}), (1 << 16, 20_000, 3, 0, {"direction": 1}), (70_000, 70_000, 2, 0, {}),
+    (3000, 5000, 1, 1, {}), (40_000, 9000, 5, 1, {"pruned": True}), (1_048_592, 268_435, 2, 0, {"step_dev": True}),
+    (20_000, 19_990, 8, 0, {"gap": 0}), (777, 1, 2, 0, {})])
+def test_propose_select_unique_matches_the_staged_path(cuda, n, k, levels, kind, opts):
+    """The fused selection gives exactly the rows of propose + top-k +
+    level listing + gather: every candidate wins (k >= n), many invalid
+    candidates (pruned units, a zero level gap), one winner, the full-size
+    reservoir case with the device step counter."""
+    import torch
+
+    kern = _k()
+    rng = np.random.default_rng(31)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    level = np.sort(rng.integers(0, levels, n)).astype(np.int32)
+    pruned = (rng.random(n) < 0.2).astype(np.uint8) if opts.get("pruned") else None
+    seed, step, dst_lo = 11, 37, 3
+    dst_n = n - dst_lo
+    gap = opts.get("gap", 1)
+    direction = opts.get("direction", 0)
+    step_dev = torch.tensor([step], dtype=torch.int32, device=cuda) if opts.get("step_dev") else None
+    d_level = t(level)
+    d_pruned = None if pruned is None else t(pruned)
+    src, dst, score = kern.propose_per_unit(n, 1, seed, step, dst_lo=dst_lo, dst_n=dst_n, score_kind=kind,
+                                            level=d_level, pruned=d_pruned, max_level_gap=gap, direction=direction,
+                                            step_dev=step_dev)
+    perm = kern.topk_unique(score, src, n, k)
+    win = kern.select_step(perm, score, src, d_level, k, num_levels=levels)
+    want = kern.gather_winners(win, min(k, n), k, src, dst, score, init_kind=2, init_a=0.05)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    got = kern.propose_select_unique(n, seed, step, dst_lo=dst_lo, dst_n=dst_n, score_kind=kind, level=d_level, k=k,
+                                     num_levels=levels, init_kind=2, init_a=0.05, pruned=d_pruned, max_level_gap=gap,
+                                     direction=direction, step_dev=step_dev, status=status)
+    for name, a, b in zip(("src", "dst", "weight", "growable"), got, want, strict=True):
+        np.testing.assert_array_equal(a.cpu().numpy(), b.cpu().numpy(), err_msg=name)
+    assert int(status.item()) == 0
+
+
+def test_propose_select_unique_matches_the_oracle(cuda):
+    """The same rows from the oracle's proposals, total order and level-major
+    step selection (q256 scores: many score ties, broken by source)."""
+    import torch
+
+    kern = _k()
+    rng = np.random.default_rng(32)
+    n, k, levels = 6000, 2500, 3
+    level = rng.integers(0, levels, n).astype(np.int32)
+    seed, step, dst_lo = 5, 9, 0
+    src, dst, score = orc.propose_per_unit(n, 1, seed, step, dst_lo, n, 1, level)
+    perm = orc.total_order(score, src, dst)
+    win = orc.select_step(perm, src, level, k)
+    got = kern.propose_select_unique(n, seed, step, dst_lo=dst_lo, dst_n=n, score_kind=1,
+                                     level=torch.from_numpy(level).to(cuda), k=k, num_levels=levels, init_kind=0,
+                                     init_a=0.5)
+    np.testing.assert_array_equal(got[0].cpu().numpy(), src[win])
+    np.testing.assert_array_equal(got[1].cpu().numpy(), dst[win])
+    np.testing.assert_array_equal(got[3].cpu().numpy(), np.isfinite(score[win]).astype(np.uint8))
