@@ -376,8 +376,9 @@ def engine_arm(args) -> None:
         "gpu_launches": launches_per_step * Kst,
     }
     # a CUDA graph holding NCCL calls must be released before the process
-    # group is destroyed, or the exit waits forever
-    step.release_graph()
+    # group is destroyed, or the exit waits forever; the peer-memory group is
+    # unmapped collectively
+    step.close()
     del step
     import gc
 

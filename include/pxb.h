@@ -519,6 +519,49 @@ PXB_API int pxb_mirror_insert(const pxb_mirror *mirror, int64_t k,
                               const float *weight, const int32_t *placed,
                               void *stream);
 
+/* ------------------------------------------------------------------ */
+/* Scheme-A reduction over NVLink peer memory                          */
+/* ------------------------------------------------------------------ */
+/* Device memory shared with peer processes through CUDA IPC: alloc returns
+ * a zeroed region and its 64-byte IPC handle; a peer opens the handle to map
+ * the region (close before the owner frees it). */
+PXB_API int pxb_peer_alloc(size_t bytes, void **ptr_out, uint8_t *ipc_handle_out);
+PXB_API int pxb_peer_open(const uint8_t *ipc_handle, void **ptr_out);
+PXB_API int pxb_peer_close(void *ptr);
+PXB_API int pxb_peer_free(void *ptr);
+
+/* One rank's view of a Scheme-A group: device arrays of `world` pointers
+ * (entry q = rank q's buffer, mapped here; entry rank = this rank's own):
+ * the int64 fixed-point partials (units of 2^-PXB_FIXED_FRAC_BITS, as
+ * pxb_mirror_forward fills them), the float side partials, the activation
+ * column, and each rank's flag rows ([2][world] uint32, zero at creation).
+ * epoch, done and status are this rank's device words (zero at creation). */
+typedef struct pxb_peer_group {
+  int32_t rank;
+  int32_t world;
+  int64_t *const *acc_fixed;
+  float *const *acc_side;
+  float *const *act;
+  uint32_t *const *flags;
+  uint32_t *epoch;
+  uint32_t *done;
+  int32_t *status;
+} pxb_peer_group;
+
+/* The forward's Scheme-A combine and apply in one kernel: waits until every
+ * rank's partials are complete, reduces this rank's slice of the units from
+ * every rank (exact int64 sum rounded once, plus the float side in rank
+ * order), applies act_kind (units not input and not pruned, as
+ * pxb_unit_apply) and stores the activation into every rank's activation
+ * column, then waits until every rank is done. Every rank calls it once per
+ * step. A wait gives up after wait_polls polls and sets status bit 0.
+ * Replaces the all-reduce of src/plastax/monoid.py:175-204 plus
+ * src/plastax/sweep.py:183-230 for the pipeline sweep's sum. */
+PXB_API int pxb_scheme_a_apply(const pxb_peer_group *group, int32_t num_units,
+                               int32_t act_kind, const uint8_t *is_input,
+                               const uint8_t *pruned, uint32_t wait_polls,
+                               void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -50,6 +50,15 @@ class Mirror(ctypes.Structure):
     ]
 
 
+class PeerGroup(ctypes.Structure):
+    """`pxb_peer_group`: one rank's view of a Scheme-A group."""
+
+    _fields_ = [
+        ("rank", c_i32), ("world", c_i32), ("acc_fixed", c_ptr), ("acc_side", c_ptr), ("act", c_ptr),
+        ("flags", c_ptr), ("epoch", c_ptr), ("done", c_ptr), ("status", c_ptr),
+    ]
+
+
 class PxbError(RuntimeError):
     """A libpxb entry point returned a non-zero status."""
 
@@ -140,6 +149,11 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         c_i32, [c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_i32, c_f32, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr]),
     "pxb_mirror_insert": (c_i32, [c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_growth_flags": (c_i32, [c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr]),
+    "pxb_peer_alloc": (c_i32, [c_size, ctypes.POINTER(c_ptr), c_ptr]),
+    "pxb_peer_open": (c_i32, [c_ptr, ctypes.POINTER(c_ptr)]),
+    "pxb_peer_close": (c_i32, [c_ptr]),
+    "pxb_peer_free": (c_i32, [c_ptr]),
+    "pxb_scheme_a_apply": (c_i32, [c_ptr, c_i32, c_i32, c_ptr, c_ptr, ctypes.c_uint32, c_ptr]),
     "pxb_count_dead": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr]),
 }
 

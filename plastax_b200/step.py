@@ -28,6 +28,7 @@ before every apply, and the claim all-gathers the per-domain free counts.
 from __future__ import annotations
 
 import dataclasses
+import os
 from typing import Any
 
 import numpy as np
@@ -124,6 +125,12 @@ class StepFn:
         # reduced alone, then combined into the carried accumulator
         # (src/plastax/sweep.py:157-175, monoid.py:175-204)
         self.per_bucket_reduce = self.sharded and self.num_buckets > 1
+        # the pipeline sweep's Scheme-A combine + apply as one kernel over
+        # NVLink peer memory (the group is built at the first bind)
+        self.peers = None
+        self.peer_reduce = (self.sharded and self.pipeline and self.acc_fixed is not None
+                            and torch.device(device).type == "cuda"
+                            and os.environ.get("PLASTAX_B200_PEER_REDUCE", "1") != "0")
         if self.per_bucket_reduce:
             self.part = torch.empty(n, dtype=torch.float32, device=device)
             self.part_fixed = None if self.acc_fixed is None else torch.zeros_like(self.acc_fixed)
@@ -152,6 +159,16 @@ class StepFn:
         level = state.units[LEVEL.name]
         if self.use_mirror:
             self.mirrors = [Mirror(b, st.num_units) for b in state.conns]
+        if self.peer_reduce:
+            from plastax_b200.peers import PeerGroup
+
+            if self.peers is None:
+                self.peers = PeerGroup(st.num_units, self.dev)
+                self.acc_fixed = self.peers.acc_fixed
+                self.acc = self.peers.acc_side
+            # the activation column lives in the group's region: peers write it
+            self.peers.act.copy_(state.units[ACTIVATION.name])
+            state.units[ACTIVATION.name] = self.peers.act
         if self.ac is not None:
             mode = _lib.CLAIM_PIPELINE if self.pipeline else _lib.CLAIM_TOPOLOGICAL
             self.bitmaps = [K.free_bitmap_build(mode, b, level, state.tail_start, self.num_levels,
@@ -300,6 +317,13 @@ class StepFn:
         if self.acc_fixed is not None:
             self.acc_fixed.zero_()
         if self.pipeline:
+            if self.peers is not None:
+                from plastax_b200.peers import scheme_a_apply
+
+                self._accumulate_bucket(state, 0, act, self.acc, self.acc_fixed)
+                scheme_a_apply(self.peers, fp.activation, is_input=self.is_input, pruned=pruned)
+                self.launches += 3
+                return
             self._forward_bucket(state, 0, act)
             K.unit_apply(self.acc, act, mode=0, act_kind=fp.activation, monoid=self.fwd_monoid,
                          is_input=self.is_input, pruned=pruned, acc_fixed=self.acc_fixed)
@@ -550,6 +574,14 @@ class StepFn:
         self.graph = None
         self._graph_rem = None
         self._graph_in = None
+
+    def close(self) -> None:
+        """Release the graph and the peer-memory group (collective under
+        Scheme-A: every rank calls it, before the process group goes)."""
+        self.release_graph()
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None
 
     def __call__(self, state: NetworkState, inputs: StepInputs) -> StepResult:
         self._bind(state)

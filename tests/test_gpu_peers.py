@@ -1,0 +1,147 @@
+"""Scheme-A combine + apply over NVLink peer memory (csrc/peer.cu).
+
+The two-rank test needs two GPUs (run on a multi-GPU box; skipped on one):
+the sharded step with the peer-memory combine must equal the one-GPU step bit
+for bit -- the forward's sums are exact fixed point, so sharding cannot
+change them, and the claim's bands concatenate to the one-arena claim. The
+bounded wait is checked on one GPU: a peer that never signals makes the wait
+give up, report status bit 0, and return.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import socket
+import time
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def test_peer_wait_gives_up_and_reports(cuda):
+    import torch
+
+    from plastax_b200 import _lib
+    from plastax_b200.peers import scheme_a_apply
+
+    n, world = 4096, 2
+    # two "ranks" in this process; rank 1 never runs, so its flags stay 0
+    fixed = [torch.zeros(n, dtype=torch.int64, device=cuda) for _ in range(world)]
+    side = [torch.zeros(n, dtype=torch.float32, device=cuda) for _ in range(world)]
+    act = [torch.full((n,), 7.0, dtype=torch.float32, device=cuda) for _ in range(world)]
+    flags = [torch.zeros(2 * world, dtype=torch.int32, device=cuda) for _ in range(world)]
+    fixed[0][5] = 3 << 28
+    arr = lambda ts: torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device=cuda)  # noqa: E731
+    p_fixed, p_side, p_act, p_flags = arr(fixed), arr(side), arr(act), arr(flags)
+    words = torch.zeros(4, dtype=torch.int32, device=cuda)
+    w = words.data_ptr()
+
+    class G:
+        struct = _lib.PeerGroup(0, world, p_fixed.data_ptr(), p_side.data_ptr(), p_act.data_ptr(),
+                                p_flags.data_ptr(), w, w + 4, w + 8)
+
+    G.n = n
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    scheme_a_apply(G, "identity", wait_polls=2000)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 5.0
+    assert int(words[2].item()) & 1, "the timed-out wait must be reported"
+    assert int(words[0].item()) == 1, "the epoch still advances"
+    # nothing was reduced: the activations are untouched
+    assert float(act[0][5].item()) == 7.0
+    # rank 0 did signal both rows of its own flags and of the silent peer
+    assert flags[1].cpu().tolist()[0] == 1 and flags[1].cpu().tolist()[2] == 1
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _cfg():
+    from plastax_b200.configs import ReservoirConfig
+
+    return ReservoirConfig(num_units=1 << 12, fan_in=16, churn=0.01, capacity_align=256)
+
+
+def _inputs(steps, m):
+    return np.random.default_rng(8).standard_normal((steps, m)).astype(np.float32)
+
+
+def _run(rank, world, port, steps, q):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from plastax_b200 import StepInputs, make_step
+        from plastax_b200.configs import build_reservoir
+        from plastax_b200.types import ShardSpec
+
+        cfg = _cfg()
+        net, static, state = build_reservoir(cfg, dev, sharding=ShardSpec("conns", world), shard_rank=rank)
+        step = make_step(net, static, device=dev)
+        assert step.peer_reduce
+        xs = _inputs(steps, cfg.num_inputs)
+        for i in range(steps):
+            if i == 2:
+                step.capture(state, StepInputs(torch.from_numpy(xs[i]).to(dev)))
+            step(state, StepInputs(torch.from_numpy(xs[i]).to(dev)))
+        torch.cuda.synchronize()
+        out = {k: v.cpu().numpy() for k, v in state.conns[0].items()}
+        out["activation"] = state.units["activation"].cpu().numpy()
+        out["status"] = int(step.peers.status.item())
+        out["tail"] = int(state.tail_start.item())
+        step.close()
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(600)
+def test_two_rank_peer_step_equals_one_gpu_step(cuda):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from plastax_b200 import StepInputs, make_step
+    from plastax_b200.configs import build_reservoir
+
+    steps = 6
+    cfg = _cfg()
+    net, static, state = build_reservoir(cfg, cuda)
+    step = make_step(net, static, device=cuda)
+    xs = _inputs(steps, cfg.num_inputs)
+    for i in range(steps):
+        step(state, StepInputs(torch.from_numpy(xs[i]).to(cuda)))
+    torch.cuda.synchronize()
+    want = {k: v.cpu().numpy() for k, v in state.conns[0].items()}
+    want_act = state.units["activation"].cpu().numpy()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_run, args=(r, 2, port, steps, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=500) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(2):
+        assert got[r]["status"] == 0
+        np.testing.assert_array_equal(got[r]["activation"], want_act, err_msg=f"rank {r} activations")
+        assert got[r]["tail"] == int(state.tail_start.item())
+    for col in want:
+        np.testing.assert_array_equal(np.concatenate([got[0][col], got[1][col]]), want[col], err_msg=col)
