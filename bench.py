@@ -40,10 +40,11 @@ sys.path.insert(0, str(ROOT))
 METRIC = "propagated edges/sec per step (Scheme-A large reservoir churn step)"
 UNIT = "edges/s"
 # DRAM bytes (read + write) per swept mirror entry of the fused forward+prune
-# kernel, from one ncu capture of the 2^16-unit reservoir (147.0 MB over
-# 17,859,121 entries per launch); the traffic reported for a full launch is
-# this figure times its swept entries (traffic grows in proportion to them)
-NCU_TRAFFIC_BYTES_PER_ENTRY = 8.23
+# sweep, from one ncu capture of the 2^18-unit reservoir with the full-size
+# chunk of 2048 units (581.0 MB over 71,303,168 entries per launch); the
+# traffic reported for a full launch is this figure times its swept entries
+# (traffic grows in proportion to them)
+NCU_TRAFFIC_BYTES_PER_ENTRY = 8.15
 
 
 def _env_int(name: str, default: int) -> int:
@@ -61,6 +62,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
     ap.add_argument("--units-log2", type=int, default=20, help="reservoir size (2**x units)")
     ap.add_argument("--fan-in", type=int, default=256)
+    ap.add_argument("--chunk-bits", type=int, default=None,
+                    help="mirror destination chunk (2**x units); default: the largest the unit count allows, "
+                         "capped at 13 (11 for the full-size reservoir)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=3)
     return ap.parse_args()
@@ -260,6 +264,7 @@ def engine_arm(args) -> None:
     net, static, state = build_reservoir(cfg, dev, sharding=sharding, shard_rank=rank)
     torch.cuda.synchronize()
     step = make_step(net, static, device=dev)
+    step.mirror_chunk_bits = args.chunk_bits
     W, Kst = max(args.warmup, 3), args.steps
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234)

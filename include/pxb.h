@@ -530,12 +530,17 @@ PXB_API int pxb_peer_open(const uint8_t *ipc_handle, void **ptr_out);
 PXB_API int pxb_peer_close(void *ptr);
 PXB_API int pxb_peer_free(void *ptr);
 
+/* Levels a Scheme-A group's counts area holds per rank. */
+#define PXB_PEER_MAX_LEVELS 8
+
 /* One rank's view of a Scheme-A group: device arrays of `world` pointers
  * (entry q = rank q's buffer, mapped here; entry rank = this rank's own):
  * the int64 fixed-point partials (units of 2^-PXB_FIXED_FRAC_BITS, as
  * pxb_mirror_forward fills them), the float side partials, the activation
- * column, and each rank's flag rows ([2][world] uint32, zero at creation).
- * epoch, done and status are this rank's device words (zero at creation). */
+ * column, each rank's flag rows ([2][world] uint32, zero at creation) and
+ * each rank's counts area ([world][PXB_PEER_MAX_LEVELS] int32; may be NULL
+ * when no counts ride on the barrier). epoch, done and status are this
+ * rank's device words (zero at creation). */
 typedef struct pxb_peer_group {
   int32_t rank;
   int32_t world;
@@ -543,6 +548,7 @@ typedef struct pxb_peer_group {
   float *const *acc_side;
   float *const *act;
   uint32_t *const *flags;
+  int32_t *const *counts;
   uint32_t *epoch;
   uint32_t *done;
   int32_t *status;
@@ -555,12 +561,19 @@ typedef struct pxb_peer_group {
  * pxb_unit_apply) and stores the activation into every rank's activation
  * column, then waits until every rank is done. Every rank calls it once per
  * step. A wait gives up after wait_polls polls and sets status bit 0.
+ * With level_counts (this rank's per-domain free counts from
+ * pxb_claim_prepare, device, [num_levels]) the counts of every rank ride on
+ * the first barrier, and level_before / level_totals receive the sums over
+ * the ranks before this one and over all ranks (pxb_claim_commit's
+ * Scheme-A inputs; the all-gather of src/plastax/phases.py:3046-3053).
  * Replaces the all-reduce of src/plastax/monoid.py:175-204 plus
  * src/plastax/sweep.py:183-230 for the pipeline sweep's sum. */
 PXB_API int pxb_scheme_a_apply(const pxb_peer_group *group, int32_t num_units,
                                int32_t act_kind, const uint8_t *is_input,
-                               const uint8_t *pruned, uint32_t wait_polls,
-                               void *stream);
+                               const uint8_t *pruned,
+                               const int32_t *level_counts, int32_t num_levels,
+                               int32_t *level_before, int32_t *level_totals,
+                               uint32_t wait_polls, void *stream);
 
 #ifdef __cplusplus
 }

@@ -35,6 +35,7 @@ INIT_CONST, INIT_DYADIC, INIT_HASH_UNIFORM = 0, 1, 2
 CLAIM_PIPELINE, CLAIM_TOPOLOGICAL = 0, 1
 CLAIM_LEVEL_MAJOR = 0x100
 MIRROR_TILE = 2048
+PEER_MAX_LEVELS = 8
 FIXED_FRAC_BITS = 28
 
 
@@ -55,7 +56,7 @@ class PeerGroup(ctypes.Structure):
 
     _fields_ = [
         ("rank", c_i32), ("world", c_i32), ("acc_fixed", c_ptr), ("acc_side", c_ptr), ("act", c_ptr),
-        ("flags", c_ptr), ("epoch", c_ptr), ("done", c_ptr), ("status", c_ptr),
+        ("flags", c_ptr), ("counts", c_ptr), ("epoch", c_ptr), ("done", c_ptr), ("status", c_ptr),
     ]
 
 
@@ -153,7 +154,8 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_peer_open": (c_i32, [c_ptr, ctypes.POINTER(c_ptr)]),
     "pxb_peer_close": (c_i32, [c_ptr]),
     "pxb_peer_free": (c_i32, [c_ptr]),
-    "pxb_scheme_a_apply": (c_i32, [c_ptr, c_i32, c_i32, c_ptr, c_ptr, ctypes.c_uint32, c_ptr]),
+    "pxb_scheme_a_apply": (c_i32, [c_ptr, c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, ctypes.c_uint32,
+                                   c_ptr]),
     "pxb_count_dead": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr]),
 }
 

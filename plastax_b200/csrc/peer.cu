@@ -31,8 +31,17 @@ struct PeerK {
   float *const *acc_side;
   float *const *act;
   uint32_t *const *flags;
+  int32_t *const *counts;
   uint32_t *epoch, *done;
   int32_t *status;
+};
+
+// The claim's per-domain free counts riding on the barrier: this rank's
+// counts go into row `rank` of every peer's counts area before the release.
+struct CountsK {
+  const int32_t *local;  // [num_levels], or NULL
+  int32_t num_levels;
+  int32_t *before, *totals;  // [num_levels] out
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
@@ -58,18 +67,40 @@ __device__ bool wait_row(const uint32_t *row, int world, uint32_t epoch, uint32_
 }
 
 constexpr float kFixUnitP = 1.0f / float(1 << PXB_FIXED_FRAC_BITS);
+constexpr int kPeerMaxLevels = PXB_PEER_MAX_LEVELS;
 
 __global__ void __launch_bounds__(256) scheme_a_apply_kernel(PeerK g, int32_t n, int32_t act_kind,
                                                             const uint8_t *__restrict__ is_input,
-                                                            const uint8_t *__restrict__ pruned, uint32_t polls) {
+                                                            const uint8_t *__restrict__ pruned, uint32_t polls,
+                                                            CountsK c) {
   __shared__ int s_ok;
   const uint32_t epoch = *g.epoch + 1u;
-  if (blockIdx.x == 0 && threadIdx.x < static_cast<unsigned>(g.world)) {
-    __threadfence_system();
-    st_release_sys(g.flags[threadIdx.x] + g.rank, epoch);  // row A of peer threadIdx.x
+  if (blockIdx.x == 0) {
+    if (c.local != nullptr)
+      for (int i = threadIdx.x; i < g.world * c.num_levels; i += blockDim.x) {
+        const int q = i / c.num_levels, l = i - q * c.num_levels;
+        g.counts[q][g.rank * kPeerMaxLevels + l] = c.local[l];
+      }
+    __syncthreads();
+    if (threadIdx.x < static_cast<unsigned>(g.world)) {
+      __threadfence_system();
+      st_release_sys(g.flags[threadIdx.x] + g.rank, epoch);  // row A of peer threadIdx.x
+    }
   }
   if (threadIdx.x == 0) s_ok = wait_row(g.flags[g.rank], g.world, epoch, polls) ? 1 : 0;
   __syncthreads();
+  if (blockIdx.x == 0 && c.local != nullptr && threadIdx.x < static_cast<unsigned>(c.num_levels)) {
+    // every rank's counts are here now: the ranks before this one and the total
+    const int32_t *rows = g.counts[g.rank];
+    int32_t before = 0, total = 0;
+    for (int q = 0; q < g.world; ++q) {
+      const int32_t v = rows[q * kPeerMaxLevels + threadIdx.x];
+      if (q < g.rank) before += v;
+      total += v;
+    }
+    c.before[threadIdx.x] = before;
+    c.totals[threadIdx.x] = total;
+  }
   if (s_ok) {
     const int32_t per = (n + g.world - 1) / g.world;
     const int32_t lo = g.rank * per;
@@ -146,8 +177,9 @@ extern "C" int pxb_peer_free(void *ptr) {
 }
 
 extern "C" int pxb_scheme_a_apply(const pxb_peer_group *group, int32_t num_units, int32_t act_kind,
-                                  const uint8_t *is_input, const uint8_t *pruned, uint32_t wait_polls,
-                                  void *stream) {
+                                  const uint8_t *is_input, const uint8_t *pruned, const int32_t *level_counts,
+                                  int32_t num_levels, int32_t *level_before, int32_t *level_totals,
+                                  uint32_t wait_polls, void *stream) {
   PXB_REQUIRE(group != nullptr, "pxb_scheme_a_apply: group is NULL");
   PXB_REQUIRE(group->world >= 1 && group->world <= 64 && group->rank >= 0 && group->rank < group->world,
               "pxb_scheme_a_apply: rank %d / world %d out of range", group->rank, group->world);
@@ -157,11 +189,17 @@ extern "C" int pxb_scheme_a_apply(const pxb_peer_group *group, int32_t num_units
   PXB_REQUIRE(num_units >= 0, "pxb_scheme_a_apply: negative num_units");
   PXB_REQUIRE(act_kind >= 0 && act_kind <= 3, "pxb_scheme_a_apply: unknown activation %d", act_kind);
   PXB_REQUIRE(wait_polls >= 1, "pxb_scheme_a_apply: wait_polls must be >= 1");
-  PeerK g{group->rank,  group->world, group->acc_fixed, group->acc_side, group->act,
-          group->flags, group->epoch, group->done,      group->status};
+  PXB_REQUIRE(level_counts == nullptr ||
+                  (group->counts && level_before && level_totals && num_levels >= 1 && num_levels <= kPeerMaxLevels),
+              "pxb_scheme_a_apply: level counts need the group's counts areas, outputs and 1..%d levels",
+              kPeerMaxLevels);
+  PeerK g{group->rank,   group->world,  group->acc_fixed, group->acc_side, group->act, group->flags,
+          group->counts, group->epoch,  group->done,      group->status};
+  CountsK c{level_counts, num_levels, level_before, level_totals};
   const int32_t per = (num_units + group->world - 1) / group->world;
   const int grid = grid_for(per > 0 ? per : 1, 256, 2);
-  scheme_a_apply_kernel<<<grid, 256, 0, as_stream(stream)>>>(g, num_units, act_kind, is_input, pruned, wait_polls);
+  scheme_a_apply_kernel<<<grid, 256, 0, as_stream(stream)>>>(g, num_units, act_kind, is_input, pruned, wait_polls,
+                                                               c);
   PXB_LAUNCHED("scheme_a_apply_kernel");
   return PXB_OK;
 }

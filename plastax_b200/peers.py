@@ -57,7 +57,8 @@ class PeerGroup:
         self.off_side = _align(self.off_fixed + 8 * n)
         self.off_act = _align(self.off_side + 4 * n)
         self.off_flags = _align(self.off_act + 4 * n)
-        self.bytes = _align(self.off_flags + 4 * 2 * self.world)
+        self.off_counts = _align(self.off_flags + 4 * 2 * self.world)
+        self.bytes = _align(self.off_counts + 4 * self.world * _lib.PEER_MAX_LEVELS)
         lib = _lib.lib()
         lib.pxb_set_device(self.dev.index)
         base = ctypes.c_void_p()
@@ -79,12 +80,13 @@ class PeerGroup:
             self.bases.append(int(p.value))
             self.opened.append(int(p.value))
         mk = lambda off: torch.tensor([b + off for b in self.bases], dtype=torch.int64, device=self.dev)  # noqa: E731
-        self.p_fixed, self.p_side, self.p_act, self.p_flags = (mk(self.off_fixed), mk(self.off_side),
-                                                              mk(self.off_act), mk(self.off_flags))
+        self.p_fixed, self.p_side, self.p_act, self.p_flags, self.p_counts = (
+            mk(self.off_fixed), mk(self.off_side), mk(self.off_act), mk(self.off_flags), mk(self.off_counts))
         self.words = torch.zeros(4, dtype=torch.int32, device=self.dev)  # epoch, done, status, pad
         w = self.words.data_ptr()
         self.struct = _lib.PeerGroup(self.rank, self.world, self.p_fixed.data_ptr(), self.p_side.data_ptr(),
-                                     self.p_act.data_ptr(), self.p_flags.data_ptr(), w, w + 4, w + 8)
+                                     self.p_act.data_ptr(), self.p_flags.data_ptr(), self.p_counts.data_ptr(),
+                                     w, w + 4, w + 8)
         # this rank's buffers as tensors (the region outlives them: close() last)
         self.acc_fixed = _view(self.base + self.off_fixed, n, torch.int64, self.dev)
         self.acc_side = _view(self.base + self.off_side, n, torch.float32, self.dev)
@@ -111,11 +113,18 @@ class PeerGroup:
 
 
 def scheme_a_apply(group: PeerGroup, act_kind: str, *, is_input: torch.Tensor | None = None,
-                   pruned: torch.Tensor | None = None, wait_polls: int = DEFAULT_WAIT_POLLS) -> None:
+                   pruned: torch.Tensor | None = None, level_counts: torch.Tensor | None = None,
+                   level_before: torch.Tensor | None = None, level_totals: torch.Tensor | None = None,
+                   wait_polls: int = DEFAULT_WAIT_POLLS) -> None:
+    """The combine + apply; with `level_counts` (this rank's per-domain free
+    counts) the counts of every rank ride on the barrier and `level_before` /
+    `level_totals` receive the claim's Scheme-A inputs."""
     from plastax_b200.kernels import _stream, ptr
 
+    nl = 0 if level_counts is None else level_counts.numel()
     _lib.call("pxb_scheme_a_apply", ctypes.byref(group.struct), ctypes.c_int32(group.n),
-              ctypes.c_int32(_lib.ACT[act_kind]), ptr(is_input), ptr(pruned), ctypes.c_uint32(wait_polls), _stream())
+              ctypes.c_int32(_lib.ACT[act_kind]), ptr(is_input), ptr(pruned), ptr(level_counts),
+              ctypes.c_int32(nl), ptr(level_before), ptr(level_totals), ctypes.c_uint32(wait_polls), _stream())
 
 
 __all__ = ["PeerGroup", "scheme_a_apply", "DEFAULT_WAIT_POLLS"]

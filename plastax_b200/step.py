@@ -116,6 +116,7 @@ class StepFn:
         # and any prune rides on the forward sweep.
         self.use_mirror = net.update_conn is None and (net.prune_conn is None or self.fuse_prune)
         self.mirrors: list | None = None
+        self.mirror_chunk_bits: int | None = None  # destination chunk of the mirror (None: the largest allowed)
         self.bitmaps: list[torch.Tensor] | None = None
         # the mirror's sum is exact fixed point (int64 accumulators beside
         # the float side for non-finite or huge products)
@@ -128,6 +129,8 @@ class StepFn:
         # the pipeline sweep's Scheme-A combine + apply as one kernel over
         # NVLink peer memory (the group is built at the first bind)
         self.peers = None
+        self._counts_on_barrier = False
+        self.level_before = self.level_totals = None
         self.peer_reduce = (self.sharded and self.pipeline and self.acc_fixed is not None
                             and torch.device(device).type == "cuda"
                             and os.environ.get("PLASTAX_B200_PEER_REDUCE", "1") != "0")
@@ -158,7 +161,7 @@ class StepFn:
         st = self.static
         level = state.units[LEVEL.name]
         if self.use_mirror:
-            self.mirrors = [Mirror(b, st.num_units) for b in state.conns]
+            self.mirrors = [Mirror(b, st.num_units, chunk_bits=self.mirror_chunk_bits) for b in state.conns]
         if self.peer_reduce:
             from plastax_b200.peers import PeerGroup
 
@@ -251,6 +254,8 @@ class StepFn:
         if self.sharded:
             G = st.num_shards
             self.gather_buf = torch.zeros((G, self.num_levels), dtype=torch.int32, device=dev)
+            self.level_before = torch.zeros(self.num_levels, dtype=torch.int32, device=dev)
+            self.level_totals = torch.zeros(self.num_levels, dtype=torch.int32, device=dev)
 
     # -- collectives -----------------------------------------------------------
     def _combine_partials(self, acc: torch.Tensor, acc_fixed: torch.Tensor | None = None) -> None:
@@ -321,7 +326,20 @@ class StepFn:
                 from plastax_b200.peers import scheme_a_apply
 
                 self._accumulate_bucket(state, 0, act, self.acc, self.acc_fixed)
-                scheme_a_apply(self.peers, fp.activation, is_input=self.is_input, pruned=pruned)
+                # with the prune in the sweep nothing touches the arena before
+                # the claim: its per-domain free counts are final here and ride
+                # on the combine's barrier instead of an all-gather
+                counts = None
+                self._counts_on_barrier = (self.ac is not None and self.k > 0 and self._fires(state)
+                                           and self.num_levels <= _lib.PEER_MAX_LEVELS)
+                if self._counts_on_barrier:
+                    ws = self.claim_ws[0]
+                    bm, _ = self._bm(0)
+                    K.claim_prepare(_lib.CLAIM_PIPELINE, state.conns[0], units[LEVEL.name], state.tail_start, ws,
+                                    shard_base=self.static.shard_base(0), free_bitmap=bm)
+                    counts = ws.level_counts
+                scheme_a_apply(self.peers, fp.activation, is_input=self.is_input, pruned=pruned,
+                               level_counts=counts, level_before=self.level_before, level_totals=self.level_totals)
                 self.launches += 3
                 return
             self._forward_bucket(state, 0, act)
@@ -495,9 +513,13 @@ class StepFn:
             b, ws = state.conns[bk], self.claim_ws[bk]
             base = st.shard_base(bk)
             bm, _ = self._bm(bk)
-            K.claim_prepare(mode, b, level, state.tail_start, ws, shard_base=base, free_bitmap=bm)
             before = totals = None
-            if self.sharded:
+            if self._counts_on_barrier:
+                # the counts pass ran after the sweep and rode on the peer barrier
+                before, totals = self.level_before, self.level_totals
+            else:
+                K.claim_prepare(mode, b, level, state.tail_start, ws, shard_base=base, free_bitmap=bm)
+            if self.sharded and not self._counts_on_barrier:
                 dist = _dist()
                 dist.all_gather_into_tensor(self.gather_buf, ws.level_counts)
                 rank = st.shard_rank

@@ -41,7 +41,7 @@ def test_peer_wait_gives_up_and_reports(cuda):
 
     class G:
         struct = _lib.PeerGroup(0, world, p_fixed.data_ptr(), p_side.data_ptr(), p_act.data_ptr(),
-                                p_flags.data_ptr(), w, w + 4, w + 8)
+                                p_flags.data_ptr(), None, w, w + 4, w + 8)
 
     G.n = n
     torch.cuda.synchronize()
