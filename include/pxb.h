@@ -219,6 +219,32 @@ PXB_API int pxb_batched_backward(int64_t cap, const int32_t *from_id,
                          const int32_t *to_id, const uint8_t *dead,
                          const float *weight, const float *g, int32_t batch,
                          int32_t num_units, float *out, void *stream);
+/* Losses of pxb_batched_loss. */
+#define PXB_LOSS_MSE 0        /* scripts/parity/reference.py:338-352 */
+#define PXB_LOSS_SOFTMAX_CE 1 /* src/plastax/traits.py:205-250 */
+
+/* pxb_unit_apply (sum monoid) for every (unit, sample) of [N, B] rows:
+ * acc, act, seed and out are [N, B]; level / is_input are per unit. */
+PXB_API int pxb_batched_unit_apply(int32_t num_units, int32_t batch, int32_t mode,
+                                   int32_t act_kind, float *acc, const float *act,
+                                   const float *seed, const int32_t *level,
+                                   int32_t target_level, const uint8_t *is_input,
+                                   float *out, void *stream);
+/* Per-sample loss over the outputs (act and seed [N, B], target [B,
+ * num_outputs] row-major): seed rows of the outputs, loss_per_sample[b], and
+ * loss_out[0] = their sum in sample order / B (StepResult.loss of a batched
+ * step, src/plastax/step.py:76-237). MSE: seed = a - t, L = sum 0.5 d^2;
+ * softmax cross-entropy: z = a - max(a), s = sum exp(z), seed = exp(z)/s - t,
+ * L = sum t * (log s - z); sums in output order. */
+PXB_API int pxb_batched_loss(int32_t kind, int32_t num_outputs,
+                             const int32_t *output_ids, int32_t batch,
+                             const float *act, const float *target, float *seed,
+                             float *loss_per_sample, float *loss_out, void *stream);
+/* out[u] = (sum_b x[u, b] in sample order) / B: the batch mean of a float
+ * unit column (MeanFloatFirstRest, src/plastax/traits.py BatchReduction). */
+PXB_API int pxb_batch_mean(int32_t num_units, int32_t batch, const float *x,
+                           float *out, void *stream);
+
 /* Exact batch-mean update (src/plastax/phases.py:434-483):
  *   stat[s] = (sum_b g[to,b] * a[from,b]) / B, then one optimizer step. */
 PXB_API int pxb_batched_update(int64_t cap, const int32_t *from_id,
@@ -352,6 +378,27 @@ PXB_API int pxb_propose_select_unique(
     float init_a, float init_b, uint32_t init_salt, int32_t *src_out,
     int32_t *dst_out, float *weight_out, uint8_t *growable_out,
     int32_t *status, void *scratch, size_t scratch_bytes, void *stream);
+
+/* Growth dedupe (src/plastax/phases.py:4111-4205): the step's candidate
+ * pairs in a hash table (scratch of pxb_dedupe_scratch_bytes(n), reset by
+ * every pxb_pair_table_build). pxb_pair_table_mark passes over a bucket,
+ * marks the table pairs that are live edges there and writes live_hit[i]
+ * for every candidate (marks accumulate over calls, one per bucket;
+ * live_pair_member, :2481-2537; under Scheme-A OR the marks across ranks
+ * before applying). pxb_dedupe_apply then sets score = -inf where live_hit
+ * (may be NULL) is set and, with step_repeats, for every copy of a pair but
+ * the first in the stable order of -score (dedupe_step / repeats_earlier,
+ * :4156, :2540-2575; NaN scores order last). One table: build, mark, apply. */
+PXB_API int pxb_dedupe_scratch_bytes(int64_t n, size_t *bytes);
+PXB_API int pxb_pair_table_build(int64_t n, const int32_t *src, const int32_t *dst,
+                                 void *scratch, size_t scratch_bytes, void *stream);
+PXB_API int pxb_pair_table_mark(int64_t n, int64_t cap, const int32_t *from_id,
+                                const int32_t *to_id, const uint8_t *dead,
+                                uint8_t *live_hit, void *scratch,
+                                size_t scratch_bytes, void *stream);
+PXB_API int pxb_dedupe_apply(int64_t n, float *score, const uint8_t *live_hit,
+                             int32_t step_repeats, void *scratch,
+                             size_t scratch_bytes, void *stream);
 
 /* ------------------------------------------------------------------ */
 /* slot claim                                                          */

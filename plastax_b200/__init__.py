@@ -19,11 +19,13 @@ from plastax_b200.traits import (
     DestinationThresholdPrune,
     ForwardPass,
     MagnitudePrune,
+    MeanFloatFirstRest,
     MSELoss,
     Network,
     ProposeAddConn,
     PruneConn,
     ResetGlobal,
+    SoftmaxCrossEntropyLoss,
 )
 from plastax_b200.types import (
     ACTIVATION,
@@ -41,7 +43,7 @@ from plastax_b200.types import (
 __all__ = [
     "ACTIVATION", "DEAD", "FROM_ID", "GRAD_PRE_ACT", "LEVEL", "LOSS_GRAD", "PRUNED", "TO_ID", "WEIGHT",
     "BackwardPass", "DestinationThresholdPrune", "FieldSpec", "ForwardPass", "GrowthRemainder", "MSELoss",
-    "MagnitudePrune", "Network", "NetworkBuilder", "NetworkState", "NetworkStatic", "Propagation", "ProposeAddConn",
-    "PruneConn", "ResetGlobal", "ShardSpec", "StepFn", "StepInputs", "StepResult", "live_conn_count",
+    "MagnitudePrune", "MeanFloatFirstRest", "Network", "NetworkBuilder", "NetworkState", "NetworkStatic", "Propagation", "ProposeAddConn",
+    "PruneConn", "ResetGlobal", "ShardSpec", "SoftmaxCrossEntropyLoss", "StepFn", "StepInputs", "StepResult", "live_conn_count",
     "make_empty_state", "make_step", "monoid", "optim",
 ]

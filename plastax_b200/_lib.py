@@ -34,6 +34,7 @@ SCORE_UNIFORM, SCORE_UNIFORM_Q256, SCORE_GRAD_ACT = 0, 1, 2
 INIT_CONST, INIT_DYADIC, INIT_HASH_UNIFORM = 0, 1, 2
 CLAIM_PIPELINE, CLAIM_TOPOLOGICAL = 0, 1
 CLAIM_LEVEL_MAJOR = 0x100
+LOSS_MSE, LOSS_SOFTMAX_CE = 0, 1
 MIRROR_TILE = 2048
 PEER_MAX_LEVELS = 8
 FIXED_FRAC_BITS = 28
@@ -156,6 +157,14 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_peer_free": (c_i32, [c_ptr]),
     "pxb_scheme_a_apply": (c_i32, [c_ptr, c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, ctypes.c_uint32,
                                    c_ptr]),
+    "pxb_dedupe_scratch_bytes": (c_i32, [c_i64, ctypes.POINTER(c_size)]),
+    "pxb_pair_table_build": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_size, c_ptr]),
+    "pxb_pair_table_mark": (c_i32, [c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_size, c_ptr]),
+    "pxb_dedupe_apply": (c_i32, [c_i64, c_ptr, c_ptr, c_i32, c_ptr, c_size, c_ptr]),
+    "pxb_batched_unit_apply": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr,
+                                       c_ptr]),
+    "pxb_batched_loss": (c_i32, [c_i32, c_i32, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
+    "pxb_batch_mean": (c_i32, [c_i32, c_i32, c_ptr, c_ptr, c_ptr]),
     "pxb_count_dead": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr]),
 }
 

@@ -223,6 +223,103 @@ static int check_batch(const char *fn, int64_t cap, const void *from, const void
 }
 
 
+// ---------------------------------------------------------------------------
+// the batched step's unit side: masked apply, per-sample loss, batch mean
+// ---------------------------------------------------------------------------
+// As pxb_unit_apply (sum monoid) for every (unit, sample) of [N, B] rows.
+__global__ void batched_apply_kernel(int32_t n, int32_t batch, int mode, int act_kind, float *__restrict__ acc,
+                                     const float *__restrict__ act, const float *__restrict__ seed,
+                                     const int32_t *__restrict__ level, int32_t target_level,
+                                     const uint8_t *__restrict__ is_input, float *__restrict__ out) {
+  const int64_t total = static_cast<int64_t>(n) * batch;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t u = static_cast<int32_t>(i / batch);
+    if (level != nullptr && level[u] != target_level) continue;
+    if (is_input != nullptr && is_input[u]) continue;
+    const float a = acc[i];
+    if (mode == 0) {
+      out[i] = act_fn(act_kind, a);
+    } else {
+      const float sd = seed != nullptr ? seed[i] : 0.0f;
+      out[i] = __fmul_rn(__fadd_rn(a, sd), act_prime_from_act(act_kind, act[i]));
+    }
+    acc[i] = 0.0f;
+  }
+}
+
+// One block per sample b: the loss of sample b and the seed rows of the
+// outputs. MSE: seed = a - t, L = sum 0.5 d^2 in output order
+// (scripts/parity/reference.py:338-352). Softmax cross-entropy
+// (src/plastax/traits.py:205-250): m = max(a), z = a - m, s = sum exp(z) in
+// output order, seed = exp(z) / s - t, L = sum t * (log(s) - z).
+__global__ void batched_loss_kernel(int kind, int32_t k, const int32_t *__restrict__ ids, int32_t batch,
+                                    const float *__restrict__ act, const float *__restrict__ target,
+                                    float *__restrict__ seed, float *__restrict__ loss_b) {
+  extern __shared__ float ez[];  // exp(z) per output
+  __shared__ float s_max, s_sum;
+  const int32_t b = blockIdx.x;
+  const float *t = target + static_cast<int64_t>(b) * k;
+  if (kind == PXB_LOSS_MSE) {
+    for (int32_t j = threadIdx.x; j < k; j += blockDim.x)
+      seed[static_cast<int64_t>(ids[j]) * batch + b] = __fsub_rn(act[static_cast<int64_t>(ids[j]) * batch + b], t[j]);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float total = 0.0f;
+      for (int32_t j = 0; j < k; ++j) {
+        const float d = seed[static_cast<int64_t>(ids[j]) * batch + b];
+        total = __fadd_rn(total, __fmul_rn(__fmul_rn(0.5f, d), d));
+      }
+      loss_b[b] = total;
+    }
+    return;
+  }
+  if (threadIdx.x == 0) {
+    float m = act[static_cast<int64_t>(ids[0]) * batch + b];
+    for (int32_t j = 1; j < k; ++j) m = fmaxf(m, act[static_cast<int64_t>(ids[j]) * batch + b]);
+    s_max = m;
+  }
+  __syncthreads();
+  for (int32_t j = threadIdx.x; j < k; j += blockDim.x)
+    ez[j] = expf(__fsub_rn(act[static_cast<int64_t>(ids[j]) * batch + b], s_max));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float total = 0.0f;
+    for (int32_t j = 0; j < k; ++j) total = __fadd_rn(total, ez[j]);
+    s_sum = total;
+  }
+  __syncthreads();
+  for (int32_t j = threadIdx.x; j < k; j += blockDim.x)
+    seed[static_cast<int64_t>(ids[j]) * batch + b] = __fsub_rn(__fdiv_rn(ez[j], s_sum), t[j]);
+  if (threadIdx.x == 0) {
+    const float lse = logf(s_sum);
+    float total = 0.0f;
+    for (int32_t j = 0; j < k; ++j) {
+      const float z = __fsub_rn(act[static_cast<int64_t>(ids[j]) * batch + b], s_max);
+      total = __fadd_rn(total, __fmul_rn(t[j], __fsub_rn(lse, z)));
+    }
+    loss_b[b] = total;
+  }
+}
+
+// loss = (sum of the per-sample losses in sample order) / B.
+__global__ void batch_mean_scalar_kernel(int32_t batch, const float *__restrict__ loss_b, float *__restrict__ loss) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  float total = 0.0f;
+  for (int32_t b = 0; b < batch; ++b) total = __fadd_rn(total, loss_b[b]);
+  loss[0] = __fdiv_rn(total, static_cast<float>(batch));
+}
+
+// out[u] = (sum_b x[u, b] in sample order) / B.
+__global__ void batch_mean_rows_kernel(int32_t n, int32_t batch, const float *__restrict__ x, float *__restrict__ out) {
+  for (int32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < n; u += gridDim.x * blockDim.x) {
+    const float *row = x + static_cast<int64_t>(u) * batch;
+    float total = 0.0f;
+    for (int32_t b = 0; b < batch; ++b) total = __fadd_rn(total, row[b]);
+    out[u] = __fdiv_rn(total, static_cast<float>(batch));
+  }
+}
+
 }  // namespace pxb
 
 using namespace pxb;
@@ -294,5 +391,44 @@ extern "C" int pxb_batched_update(int64_t cap, const int32_t *from_id, const int
   else PXB_BU(8);
 #undef PXB_BU
   PXB_LAUNCHED("batched_update_kernel");
+  return PXB_OK;
+}
+
+extern "C" int pxb_batched_unit_apply(int32_t num_units, int32_t batch, int32_t mode, int32_t act_kind, float *acc,
+                                      const float *act, const float *seed, const int32_t *level,
+                                      int32_t target_level, const uint8_t *is_input, float *out, void *stream) {
+  PXB_REQUIRE(num_units >= 0 && batch >= 1, "pxb_batched_unit_apply: bad sizes");
+  PXB_REQUIRE(mode == 0 || mode == 1, "pxb_batched_unit_apply: mode must be 0 (forward) or 1 (backward)");
+  PXB_REQUIRE(act_kind >= 0 && act_kind <= 3, "pxb_batched_unit_apply: unknown activation %d", act_kind);
+  if (num_units == 0) return PXB_OK;
+  PXB_REQUIRE(acc && out && (mode == 0 || act), "pxb_batched_unit_apply: a pointer is NULL");
+  const int64_t total = int64_t(num_units) * batch;
+  batched_apply_kernel<<<grid_for(total, 256, 8), 256, 0, as_stream(stream)>>>(
+      num_units, batch, mode, act_kind, acc, act, seed, level, target_level, is_input, out);
+  PXB_LAUNCHED("batched_apply_kernel");
+  return PXB_OK;
+}
+
+extern "C" int pxb_batched_loss(int32_t kind, int32_t num_outputs, const int32_t *output_ids, int32_t batch,
+                                const float *act, const float *target, float *seed, float *loss_per_sample,
+                                float *loss_out, void *stream) {
+  PXB_REQUIRE(kind == PXB_LOSS_MSE || kind == PXB_LOSS_SOFTMAX_CE, "pxb_batched_loss: unknown loss %d", kind);
+  PXB_REQUIRE(num_outputs >= 1 && num_outputs <= 8192 && batch >= 1, "pxb_batched_loss: bad sizes");
+  PXB_REQUIRE(output_ids && act && target && seed && loss_per_sample && loss_out, "pxb_batched_loss: a pointer is NULL");
+  cudaStream_t st = as_stream(stream);
+  batched_loss_kernel<<<batch, 256, num_outputs * sizeof(float), st>>>(kind, num_outputs, output_ids, batch, act,
+                                                                      target, seed, loss_per_sample);
+  PXB_LAUNCHED("batched_loss_kernel");
+  batch_mean_scalar_kernel<<<1, 32, 0, st>>>(batch, loss_per_sample, loss_out);
+  PXB_LAUNCHED("batch_mean_scalar_kernel");
+  return PXB_OK;
+}
+
+extern "C" int pxb_batch_mean(int32_t num_units, int32_t batch, const float *x, float *out, void *stream) {
+  PXB_REQUIRE(num_units >= 0 && batch >= 1, "pxb_batch_mean: bad sizes");
+  if (num_units == 0) return PXB_OK;
+  PXB_REQUIRE(x && out, "pxb_batch_mean: a pointer is NULL");
+  batch_mean_rows_kernel<<<grid_for(num_units, 256, 8), 256, 0, as_stream(stream)>>>(num_units, batch, x, out);
+  PXB_LAUNCHED("batch_mean_rows_kernel");
   return PXB_OK;
 }

@@ -13,7 +13,7 @@ A bucket is a dict of device columns named like the reference's SOA tags:
 from __future__ import annotations
 
 import ctypes
-from collections.abc import Mapping
+from collections.abc import Mapping, Sequence
 
 import torch
 
@@ -182,6 +182,30 @@ def batched_backward(b: Bucket, g: torch.Tensor, out: torch.Tensor) -> None:
     n, batch = g.shape
     call("pxb_batched_backward", ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]), ptr(b["dead"]),
          ptr(b["weight"]), ptr(g), ctypes.c_int32(batch), ctypes.c_int32(n), ptr(out), _stream())
+
+
+def batched_unit_apply(acc: torch.Tensor, out: torch.Tensor, *, mode: int, act_kind: str,
+                       act: torch.Tensor | None = None, seed: torch.Tensor | None = None,
+                       level: torch.Tensor | None = None, target_level: int = 0,
+                       is_input: torch.Tensor | None = None) -> None:
+    """Masked apply over [N, B] rows (sum monoid)."""
+    n, batch = acc.shape
+    call("pxb_batched_unit_apply", ctypes.c_int32(n), ctypes.c_int32(batch), ctypes.c_int32(mode),
+         ctypes.c_int32(_lib.ACT[act_kind]), ptr(acc), ptr(act), ptr(seed), ptr(level), ctypes.c_int32(target_level),
+         ptr(is_input), ptr(out), _stream())
+
+
+def batched_loss(kind: int, output_ids: torch.Tensor, batch: int, act: torch.Tensor, target: torch.Tensor,
+                 seed: torch.Tensor, loss_per_sample: torch.Tensor, loss_out: torch.Tensor) -> None:
+    """Per-sample MSE or softmax cross-entropy; loss_out = the batch mean."""
+    call("pxb_batched_loss", ctypes.c_int32(kind), ctypes.c_int32(output_ids.numel()), ptr(output_ids),
+         ctypes.c_int32(batch), ptr(act), ptr(target), ptr(seed), ptr(loss_per_sample), ptr(loss_out), _stream())
+
+
+def batch_mean(x: torch.Tensor, out: torch.Tensor) -> None:
+    """out[u] = mean over the batch of x[u, :] (sample order)."""
+    n, batch = x.shape
+    call("pxb_batch_mean", ctypes.c_int32(n), ctypes.c_int32(batch), ptr(x), ptr(out), _stream())
 
 
 def batched_update(b: Bucket, g: torch.Tensor, a: torch.Tensor, opt: _lib.Optimizer) -> None:
@@ -394,6 +418,35 @@ def growth_flags(counts: torch.Tensor, *, reset: bool, grown: torch.Tensor | Non
             _check(t, dt, 1, "growth_flags")
     call("pxb_growth_flags", ptr(counts), ctypes.c_int32(1 if reset else 0), ptr(grown), ptr(overflow),
          ptr(needs_resort), _stream())
+
+
+def dedupe_scratch(n: int) -> int:
+    return query_size("pxb_dedupe_scratch_bytes", ctypes.c_int64(n))
+
+
+def dedupe(src: torch.Tensor, dst: torch.Tensor, score: torch.Tensor, *, buckets: Sequence[Bucket] = (),
+           step_repeats: bool = False, live_hit: torch.Tensor | None = None, scratch: torch.Tensor | None = None,
+           combine_hits=None) -> None:
+    """Veto (score = -inf) candidates whose pair is live in any of `buckets`
+    and, with `step_repeats`, every copy of a pair but its first in the
+    stable order of -score. `combine_hits(live_hit)` may OR the live marks
+    across ranks between the marks and the veto (Scheme-A)."""
+    n = src.numel()
+    if scratch is None:
+        scratch = torch.empty(max(dedupe_scratch(n), 1), dtype=torch.uint8, device=src.device)
+    call("pxb_pair_table_build", ctypes.c_int64(n), ptr(src), ptr(dst), ptr(scratch),
+         ctypes.c_size_t(scratch.numel()), _stream())
+    if buckets:
+        if live_hit is None:
+            live_hit = torch.empty(n, dtype=torch.uint8, device=src.device)
+        for b in buckets:
+            call("pxb_pair_table_mark", ctypes.c_int64(n), ctypes.c_int64(_bucket(b)), ptr(b["from_id"]),
+                 ptr(b["to_id"]), ptr(b["dead"]), ptr(live_hit), ptr(scratch), ctypes.c_size_t(scratch.numel()),
+                 _stream())
+        if combine_hits is not None:
+            combine_hits(live_hit)
+    call("pxb_dedupe_apply", ctypes.c_int64(n), ptr(score), ptr(live_hit if buckets else None),
+         ctypes.c_int32(1 if step_repeats else 0), ptr(scratch), ctypes.c_size_t(scratch.numel()), _stream())
 
 
 def count_dead(b: Bucket, out: torch.Tensor) -> None:

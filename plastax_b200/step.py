@@ -43,6 +43,7 @@ from plastax_b200.traits import (
     MSELoss,
     Network,
     ProposeAddConn,
+    SoftmaxCrossEntropyLoss,
 )
 from plastax_b200.types import ACTIVATION, LEVEL, PRUNED, Propagation
 
@@ -103,6 +104,7 @@ class StepFn:
         is_input[list(static.input_ids)] = 1
         self.is_input = torch.from_numpy(is_input).to(device)
         self.loss_buf = torch.zeros(1, dtype=torch.float32, device=device)
+        self.loss_b1 = torch.zeros(1, dtype=torch.float32, device=device)
         self.sharded = static.sharding is not None and static.num_shards > 1
         self.reduce_op = fp.combine.torch_reduce_op() if self.sharded else None
         # fusion legality
@@ -146,7 +148,8 @@ class StepFn:
             # proposals scored by the site RNG alone depend on the levels and
             # the step counter only, never on this step's propagation, prune
             # or update: their selection may overlap the forward sweep
-            if self.ac.score in ("uniform", "uniform_q256") and torch.device(device).type == "cuda":
+            if (self.ac.score in ("uniform", "uniform_q256") and not self.ac.dedupe_live
+                    and torch.device(device).type == "cuda"):
                 self.side = torch.cuda.Stream(device=device)
         self.launches = 0
 
@@ -243,7 +246,12 @@ class StepFn:
         # (keys binned and ranked, no sort pass) replaces propose + top-k +
         # level listing + gather
         self.fast_select = (self.unique_src and ac.score in ("uniform", "uniform_q256")
-                            and self.static.num_levels <= 8 and self.k > 0)
+                            and self.static.num_levels <= 8 and self.k > 0
+                            and not ac.dedupe_live and not ac.dedupe_step)
+        self.dedupe = ac.dedupe_live or ac.dedupe_step
+        if self.dedupe:
+            self.dedupe_scratch = torch.empty(max(K.dedupe_scratch(self.n_cand), 1), dtype=torch.uint8, device=dev)
+            self.live_hit = torch.empty(max(self.n_cand, 1), dtype=torch.uint8, device=dev)
         if self.fast_select:
             need = K.select_unique_scratch(n, self.k, self.static.num_levels, self.score_kind)
             self.fs_scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
@@ -358,16 +366,21 @@ class StepFn:
         loss = self.net.loss
         if loss is None:
             return
-        if not isinstance(loss, MSELoss):
-            raise NotImplementedError("only MSELoss has an engine lowering in the streaming step")
         t = inputs.targets
         if t is None:
             raise ValueError("a network with a loss needs StepInputs.targets")
         if not isinstance(t, torch.Tensor):
             t = torch.from_numpy(np.ascontiguousarray(t, np.float32))
         t = t.to(self.dev, non_blocking=True).reshape(-1)
-        K.mse_loss(self.output_ids, state.units[ACTIVATION.name], t, state.units[loss.seed_field.name],
-                   self.loss_buf)
+        if isinstance(loss, MSELoss):
+            K.mse_loss(self.output_ids, state.units[ACTIVATION.name], t, state.units[loss.seed_field.name],
+                       self.loss_buf)
+        elif isinstance(loss, SoftmaxCrossEntropyLoss):
+            # the one-sample case of the batched loss ([N] == [N, 1] rows)
+            K.batched_loss(_lib.LOSS_SOFTMAX_CE, self.output_ids, 1, state.units[ACTIVATION.name], t,
+                           state.units[loss.seed_field.name], self.loss_b1, self.loss_buf)
+        else:
+            raise NotImplementedError(f"loss {type(loss).__name__} has no engine lowering")
         self.launches += 1
 
     def _backward(self, state: NetworkState) -> None:
@@ -467,6 +480,16 @@ class StepFn:
                            src_level_bound=0 if self.pipeline else self.num_buckets, step_dev=self.step_dev,
                            out=self.cand)
         src, dst, score = self.cand
+        if self.dedupe:
+            combine = None
+            if self.sharded and ac.dedupe_live:
+                # a pair live on any rank is a duplicate everywhere (the
+                # reference's pmax of the local marks)
+                combine = lambda hit: _dist().all_reduce(hit, op=_dist().ReduceOp.MAX)  # noqa: E731
+            K.dedupe(src, dst, score, buckets=list(state.conns) if ac.dedupe_live else [],
+                     step_repeats=ac.dedupe_step, live_hit=self.live_hit, scratch=self.dedupe_scratch,
+                     combine_hits=combine)
+            self.launches += 4
         if self.unique_src:
             top = K.topk_unique(score, src, n, self.k, out=self.perm, scratch=self.order_scratch)
         else:
@@ -644,6 +667,12 @@ def make_step(net: type[Network], static: NetworkStatic, *, batch_size: int | No
     if batch_size is not None:
         if batch_size < 1:
             raise ValueError("make_step: batch_size must be >= 1")
+        if net.propagation is Propagation.PIPELINE:
+            raise ValueError("make_step: batch_size is for TOPOLOGICAL (feed-forward) nets; a PIPELINE net carries "
+                             "per-sample recurrent state between steps")
+        if net.batch_reduction is None:
+            raise ValueError(f"make_step: a batched step needs {net.__name__}.batch_reduction (e.g. "
+                             "MeanFloatFirstRest())")
         from plastax_b200.batched import BatchedStepFn
 
         return BatchedStepFn(net, static, batch_size, torch.device(device))

@@ -14,14 +14,18 @@ Recognised forms:
 - BackwardPass: map = weight * grad_field[dst], combine = sum, apply:
   grad_field = (acc + seed_field) * activation'(ACTIVATION)
   (scripts/parity/golden_rules.py relu_mlp_v1 generalised).
-- Loss: MSELoss (scripts/parity/reference.py:338-352).
+- Loss: MSELoss (scripts/parity/reference.py:338-352) and
+  SoftmaxCrossEntropyLoss (src/plastax/traits.py:205-250).
+- batch_reduction: MeanFloatFirstRest for a batched step.
 - update_conn: an optimizer bundle from plastax_b200.optim (sgd, momentum,
   adam, adamw, rmsprop; src/plastax/optim).
 - PruneConn: |weight| < threshold (MagnitudePrune) or |weight| <
   unit[field, dst] (DestinationThresholdPrune).
 - ProposeAddConn: proposer "per_unit", dst = dst_lo + uniform_int(dst_n)
   [sub 0], score uniform / floor(u*256)/256 [sub 1] or |grad[dst]*act[src]|,
-  init weight constant / dyadic / hashed uniform.
+  init weight constant / dyadic / hashed uniform; dedupe_live (a candidate
+  equal to a live edge is vetoed) and dedupe_step (a pair's copies after the
+  first in score order are vetoed).
 """
 
 from __future__ import annotations
@@ -75,6 +79,25 @@ class MSELoss:
 
     def __init__(self, seed_field: FieldSpec = LOSS_GRAD) -> None:
         self.seed_field = seed_field
+
+
+class SoftmaxCrossEntropyLoss:
+    """Softmax over the output activations, cross-entropy against a target
+    distribution (src/plastax/traits.py:205-250): z = a - max(a), s = sum
+    exp(z), loss = sum t * (log s - z), seed = exp(z) / s - t."""
+
+    def __init__(self, seed_field: FieldSpec = LOSS_GRAD) -> None:
+        self.seed_field = seed_field
+
+
+class MeanFloatFirstRest:
+    """Batch reduction (src/plastax/traits.py:811-838): the batch mean of every
+    floating unit column, sample 0 of any other, LEVEL and PRUNED not batched."""
+
+    def reduction(self, field: FieldSpec) -> str:
+        if field.name in ("level", "pruned"):
+            return "not_batched"
+        return "mean" if field.dtype.kind == "f" else "first"
 
 
 class PruneConn:
@@ -135,8 +158,6 @@ class ProposeAddConn:
             raise ValueError(f"unknown level_cap_scope {self.level_cap_scope!r}")
         if self.direction not in ("any", "deeper", "same_or_deeper"):
             raise ValueError(f"unknown direction {self.direction!r}")
-        if self.dedupe_live or self.dedupe_step:
-            raise NotImplementedError("dedupe_live / dedupe_step have no engine lowering yet")
         if self.score not in ("uniform", "uniform_q256", "grad_act"):
             raise ValueError(f"unknown proposal score {self.score!r}")
         if self.init[0] not in ("const", "dyadic", "hash_uniform"):
@@ -155,7 +176,7 @@ class Network:
     """
 
     forward_pass: ClassVar[ForwardPass]
-    loss: ClassVar[MSELoss | None] = None
+    loss: ClassVar[MSELoss | SoftmaxCrossEntropyLoss | None] = None
     backward_pass: ClassVar[BackwardPass | None] = None
     update_unit: ClassVar[Any] = None
     update_conn: ClassVar[Any] = None  # an optimizer bundle (plastax_b200.optim)
@@ -172,6 +193,7 @@ class Network:
     structural_interval: ClassVar[int] = 1
     sharding: ClassVar[ShardSpec | None] = None
     kahn_max_depth: ClassVar[int | None] = None
+    batch_reduction: ClassVar[Any] = None  # e.g. MeanFloatFirstRest(), required by a batched step
 
     def __init_subclass__(cls, **kwargs: Any) -> None:
         super().__init_subclass__(**kwargs)

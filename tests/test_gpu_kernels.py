@@ -666,3 +666,48 @@ def test_propose_select_unique_matches_the_oracle(cuda):
     np.testing.assert_array_equal(got[0].cpu().numpy(), src[win])
     np.testing.assert_array_equal(got[1].cpu().numpy(), dst[win])
     np.testing.assert_array_equal(got[3].cpu().numpy(), np.isfinite(score[win]).astype(np.uint8))
+
+
+def _ref_dedupe(src, dst, score, live_pairs, dedupe_live, dedupe_step):
+    """src/plastax/phases.py:4111-4205 restated: live pairs vetoed, then every
+    copy of a pair after its first in the stable order of -score (NaN last)."""
+    s = score.copy()
+    if dedupe_live:
+        hit = np.array([(int(a), int(b)) in live_pairs for a, b in zip(src, dst, strict=True)], bool)
+        s[hit] = -np.inf
+    if dedupe_step:
+        seen, rep = set(), np.zeros(s.size, bool)
+        for i in np.argsort(-s, kind="stable"):
+            key = (int(src[i]), int(dst[i]))
+            rep[i] = key in seen
+            seen.add(key)
+        s[rep] = -np.inf
+    return s
+
+
+@pytest.mark.parametrize("live,step", [(True, False), (False, True), (True, True)])
+def test_dedupe_matches_the_reference_rule(cuda, live, step):
+    import torch
+
+    kern = _k()
+    rng = np.random.default_rng(41)
+    n_units, m, cap = 300, 60_000, 50_000
+    src = rng.integers(0, n_units, m).astype(np.int32)
+    dst = rng.integers(0, 40, m).astype(np.int32)  # narrow destinations: many repeated pairs
+    score = (rng.integers(0, 50, m) / 8.0).astype(np.float32)  # ties
+    score[rng.random(m) < 0.05] = -np.inf
+    score[rng.random(m) < 0.01] = np.nan
+    score[rng.random(m) < 0.02] = -0.0
+    b = random_bucket(rng, n_units, cap, cap - 2000, dead_frac=0.1)
+    b["to_id"][:] = np.clip(b["to_id"], 0, 39)
+    live_pairs = {(int(a), int(c)) for a, c, d in zip(b["from_id"], b["to_id"], b["dead"], strict=True) if d == 0}
+    want = _ref_dedupe(src, dst, score, live_pairs, live, step)
+    db = to_device(b, cuda)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    d_score = t(score.copy())
+    kern.dedupe(t(src), t(dst), d_score, buckets=[db] if live else [], step_repeats=step)
+    got = d_score.cpu().numpy()
+    np.testing.assert_array_equal(np.isnan(got), np.isnan(want))
+    ok = ~np.isnan(want)
+    np.testing.assert_array_equal(got[ok], want[ok])
+    assert (got == -np.inf).sum() > (score == -np.inf).sum()  # something was vetoed

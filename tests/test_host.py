@@ -185,3 +185,41 @@ def test_optimizer_bundles_declare_their_columns():
     assert [f.name for f in optim.momentum(0.1).state_fields] == ["opt/v"]
     assert optim.sgd(0.1).state_fields == ()
     assert optim.adamw(1e-3).weight_decay == 1e-4
+
+
+def test_batched_step_rejects_what_it_cannot_run():
+    """src/plastax/step.py:188-202: a batched step is for TOPOLOGICAL nets
+    with a batch_reduction; the engine moves [N, B] rows as float4."""
+    import plastax_b200 as px
+
+    class Pipe(px.Network):
+        forward_pass = px.ForwardPass("tanh")
+        propagation = px.Propagation.PIPELINE
+        batch_reduction = px.MeanFloatFirstRest()
+
+    class NoReduce(px.Network):
+        forward_pass = px.ForwardPass("tanh")
+        propagation = px.Propagation.TOPOLOGICAL
+
+    class Topo(px.Network):
+        forward_pass = px.ForwardPass("tanh")
+        propagation = px.Propagation.TOPOLOGICAL
+        batch_reduction = px.MeanFloatFirstRest()
+
+    for net in (Pipe, NoReduce):
+        static, _ = px.NetworkBuilder.from_edges(net, 4, [0], [1], input_ids=(0,), output_ids=(1,), device="cpu")
+        with pytest.raises(ValueError):
+            px.make_step(net, static, batch_size=8, device="cpu")
+    static, _ = px.NetworkBuilder.from_edges(Topo, 4, [0], [1], input_ids=(0,), output_ids=(1,), device="cpu")
+    with pytest.raises(ValueError, match="multiple of 4"):
+        px.make_step(Topo, static, batch_size=6, device="cpu")
+
+
+def test_mean_float_first_rest_declares_every_column():
+    import plastax_b200 as px
+
+    r = px.MeanFloatFirstRest()
+    assert r.reduction(px.ACTIVATION) == "mean"
+    assert r.reduction(px.LEVEL) == "not_batched"
+    assert r.reduction(px.PRUNED) == "not_batched"
+    assert r.reduction(px.FieldSpec.int32("test/count")) == "first"
