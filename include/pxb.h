@@ -354,6 +354,54 @@ PXB_API int pxb_gather_winners(int64_t k, int64_t count, const int32_t *win_idx,
                        int32_t *dst_out, float *weight_out,
                        uint8_t *growable_out, void *stream);
 
+/* The global proposer (src/plastax/phases.py:3766-3810): proposal j at key
+ * 0, src = src_lo + uniform_int(src_n) [sub 0], dst = dst_lo +
+ * uniform_int(dst_n) [sub 1], score [sub 2] (kinds as pxb_propose_per_unit),
+ * candidate index j; the same validity window. */
+PXB_API int pxb_propose_global(int32_t proposals, uint64_t network_seed, int32_t step,
+                               int32_t num_units, int32_t src_lo, int32_t src_n,
+                               int32_t dst_lo, int32_t dst_n, int32_t score_kind,
+                               const float *grad, const float *act,
+                               const int32_t *level, const uint8_t *pruned,
+                               int32_t max_level_gap, int32_t direction,
+                               int32_t allow_self_loops, int32_t bucket_level,
+                               int32_t src_level_bound, const int32_t *step_dev,
+                               int32_t *src_out, int32_t *dst_out,
+                               float *score_out, void *stream);
+
+/* The per-connection proposer (src/plastax/phases.py:3921-4039) over one
+ * bucket-major arena of cap slots: the live connections ranked ascending by
+ * (src, dst, occurrence in slot order), dead slots after them in slot order;
+ * connection rank r proposes candidates r * P + j: src = its source, dst =
+ * dst_lo + uniform_int(dst_n) [sub 0], score [sub 1], at the site key
+ * philox32((src << 32) | dst, occurrence); a dead proposer's candidates are
+ * vetoed. cap * P candidates; scratch of pxb_conn_rank_scratch_bytes. */
+PXB_API int pxb_conn_rank_scratch_bytes(int64_t cap, int32_t num_units, size_t *bytes);
+PXB_API int pxb_propose_per_conn(int64_t cap, const int32_t *from_id,
+                                 const int32_t *to_id, const uint8_t *dead,
+                                 int32_t proposals, uint64_t network_seed,
+                                 int32_t step, int32_t num_units, int32_t dst_lo,
+                                 int32_t dst_n, int32_t score_kind,
+                                 const float *grad, const float *act,
+                                 const int32_t *level, const uint8_t *pruned,
+                                 int32_t max_level_gap, int32_t direction,
+                                 int32_t allow_self_loops, int32_t bucket_level,
+                                 int32_t src_level_bound, const int32_t *step_dev,
+                                 int32_t *src_out, int32_t *dst_out,
+                                 float *score_out, void *scratch,
+                                 size_t scratch_bytes, void *stream);
+
+/* The per-source-level cap (level_cap_scope "source_level",
+ * src/plastax/phases.py:4324-4487): over a level-major list idx of n
+ * candidates (pxb_select_step with k = n), the first k of every level's
+ * run, listed levels ascending into out_idx (capacity num_levels * k; fill
+ * it with -1 first, pxb_gather_winners treats -1 as no candidate);
+ * out_count (device) = their number. scratch: 3 * num_levels + 1 int32. */
+PXB_API int pxb_cap_per_level(int64_t n, const int32_t *idx, const int32_t *src,
+                              const int32_t *level, int32_t num_levels, int64_t k,
+                              int32_t *out_idx, int32_t *out_count, int32_t *scratch,
+                              void *stream);
+
 /* Fused growth selection for one proposal per unit scored by the site RNG
  * (score_kind PXB_SCORE_UNIFORM or PXB_SCORE_UNIFORM_Q256): the proposals
  * of every unit (as pxb_propose_per_unit with proposals = 1, bucket_level

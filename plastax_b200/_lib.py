@@ -142,6 +142,14 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
          c_ptr],
     ),
     "pxb_free_bitmap_build": (c_i32, [c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i64, c_ptr, c_ptr, c_ptr]),
+    "pxb_propose_global": (c_i32, [c_i32, ctypes.c_uint64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_ptr,
+                                   c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_ptr,
+                                   c_ptr, c_ptr]),
+    "pxb_conn_rank_scratch_bytes": (c_i32, [c_i64, c_i32, ctypes.POINTER(c_size)]),
+    "pxb_propose_per_conn": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_i32, ctypes.c_uint64, c_i32, c_i32, c_i32, c_i32,
+                                     c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32, c_i32, c_ptr,
+                                     c_ptr, c_ptr, c_ptr, c_ptr, c_size, c_ptr]),
+    "pxb_cap_per_level": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_select_unique_scratch_bytes": (c_i32, [c_i32, c_i64, c_i32, c_i32, ctypes.POINTER(c_size)]),
     "pxb_propose_select_unique": (
         c_i32, [c_i32, ctypes.c_uint64, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32,

@@ -53,27 +53,15 @@ __device__ __forceinline__ uint64_t keyed_hi_of(const ProposeArgs &a) {
   return keyed;
 }
 
-// Candidate c = i * proposals + j of unit i: its endpoints and score, the
-// score -inf when the framework's validity window vetoes it.
-__device__ __forceinline__ void propose_one(const ProposeArgs &a, uint64_t keyed_hi, int64_t c, int32_t &src_o,
-                                            int32_t &dst_o, float &score_o) {
-  const int32_t i = static_cast<int32_t>(c / a.proposals);
-  const uint32_t j = static_cast<uint32_t>(c - static_cast<int64_t>(i) * a.proposals);
-  const uint64_t seed = (keyed_hi << 32) | static_cast<uint32_t>(i);
-  int32_t src = i;
-  int32_t dst = a.dst_lo + static_cast<int32_t>(uniform_int(unit_float(site_draw(seed, j, 0)), a.dst_n));
-  float score;
-  if (a.score_kind == PXB_SCORE_UNIFORM) {
-    score = unit_float(site_draw(seed, j, 1));
-  } else if (a.score_kind == PXB_SCORE_UNIFORM_Q256) {
-    const float u = unit_float(site_draw(seed, j, 1));
-    score = static_cast<float>(static_cast<int32_t>(__fmul_rn(u, 256.0f))) * (1.0f / 256.0f);
-  } else {
-    score = (dst >= 0 && dst < a.num_units) ? fabsf(__fmul_rn(a.grad[dst], a.act[src])) : 0.0f;
-  }
-  // _clamp_proposals: out-of-range ids are vetoed and clamped to 0.
-  bool valid = dst >= 0 && dst < a.num_units;
-  if (!valid) {
+// The framework's validity window (src/plastax/phases.py:4041-4108): an
+// out-of-range id is vetoed and clamped to 0 (_clamp_proposals); pruned
+// endpoints, self-loops, the level gap, the direction, the bucket's source
+// level and a non-finite score veto the candidate (score -inf), as does a
+// dead proposing connection.
+__device__ __forceinline__ void apply_window(const ProposeArgs &a, int32_t &src, int32_t &dst, float &score,
+                                             bool proposer_live) {
+  bool valid = proposer_live && src >= 0 && src < a.num_units && dst >= 0 && dst < a.num_units;
+  if (!(src >= 0 && src < a.num_units && dst >= 0 && dst < a.num_units)) {
     src = 0;
     dst = 0;
   }
@@ -89,6 +77,32 @@ __device__ __forceinline__ void propose_one(const ProposeArgs &a, uint64_t keyed
     if (a.src_level_bound > 0) valid = valid && ls < a.src_level_bound;
   }
   if (!valid || !isfinite(score)) score = -__int_as_float(0x7f800000);
+}
+
+// A proposal's score at draw `sub` of its site: uniform, floor(u*256)/256,
+// or |grad[dst] * act[src]| (no draw).
+__device__ __forceinline__ float proposal_score(const ProposeArgs &a, uint64_t seed, uint32_t j, uint32_t sub,
+                                                int32_t src, int32_t dst) {
+  if (a.score_kind == PXB_SCORE_UNIFORM) return unit_float(site_draw(seed, j, sub));
+  if (a.score_kind == PXB_SCORE_UNIFORM_Q256) {
+    const float u = unit_float(site_draw(seed, j, sub));
+    return static_cast<float>(static_cast<int32_t>(__fmul_rn(u, 256.0f))) * (1.0f / 256.0f);
+  }
+  const bool in = dst >= 0 && dst < a.num_units && src >= 0 && src < a.num_units;
+  return in ? fabsf(__fmul_rn(a.grad[dst], a.act[src])) : 0.0f;
+}
+
+// Candidate c = i * proposals + j of unit i: its endpoints and score, the
+// score -inf when the framework's validity window vetoes it.
+__device__ __forceinline__ void propose_one(const ProposeArgs &a, uint64_t keyed_hi, int64_t c, int32_t &src_o,
+                                            int32_t &dst_o, float &score_o) {
+  const int32_t i = static_cast<int32_t>(c / a.proposals);
+  const uint32_t j = static_cast<uint32_t>(c - static_cast<int64_t>(i) * a.proposals);
+  const uint64_t seed = (keyed_hi << 32) | static_cast<uint32_t>(i);
+  int32_t src = i;
+  int32_t dst = a.dst_lo + static_cast<int32_t>(uniform_int(unit_float(site_draw(seed, j, 0)), a.dst_n));
+  float score = proposal_score(a, seed, j, 1, src, dst);
+  apply_window(a, src, dst, score, true);
   src_o = src;
   dst_o = dst;
   score_o = score;
@@ -260,7 +274,7 @@ __global__ void gather_winners_kernel(int64_t k, int64_t count, const int32_t *_
                                       uint8_t *__restrict__ growable) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < k;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    if (i < count) {
+    if (i < count && win[i] >= 0) {
       const int32_t c = win[i];
       const int32_t s = src[c], d = dst[c];
       s_out[i] = s;
@@ -901,6 +915,160 @@ static void fs_layout(const FsGeom &g, char *base, FsScratch *o) {
   o->total = off;
 }
 
+// ---------------------------------------------------------------------------
+// the global and per-connection proposers (src/plastax/phases.py:3766-3810,
+// :3921-4039) and the per-source-level cap (:4324-4487)
+// ---------------------------------------------------------------------------
+// Global: proposal j at key 0: src [sub 0], dst [sub 1], score [sub 2];
+// candidate index j.
+__global__ void propose_global_kernel(ProposeArgs a, int32_t src_lo, int32_t src_n, int32_t *__restrict__ src_out,
+                                      int32_t *__restrict__ dst_out, float *__restrict__ score_out) {
+  const uint64_t keyed_hi = keyed_hi_of(a);
+  const uint64_t seed = keyed_hi << 32;
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < a.proposals;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t j = static_cast<uint32_t>(c);
+    int32_t src = src_lo + static_cast<int32_t>(uniform_int(unit_float(site_draw(seed, j, 0)), src_n));
+    int32_t dst = a.dst_lo + static_cast<int32_t>(uniform_int(unit_float(site_draw(seed, j, 1)), a.dst_n));
+    float score = proposal_score(a, seed, j, 2, src, dst);
+    apply_window(a, src, dst, score, true);
+    src_out[c] = src;
+    dst_out[c] = dst;
+    score_out[c] = score;
+  }
+}
+
+// Live connections ranked ascending by (src, dst, slot), dead slots after
+// them: the packed key of slot s (dead: every bit set), its slot as value.
+__global__ void conn_key_kernel(int64_t cap, const int32_t *__restrict__ from, const int32_t *__restrict__ to,
+                                const uint8_t *__restrict__ dead, int id_bits, uint64_t *__restrict__ key,
+                                int32_t *__restrict__ val) {
+  const uint64_t all = (id_bits >= 32) ? ~0ull : ((uint64_t(1) << (2 * id_bits)) - 1);
+  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < cap;
+       s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    key[s] = dead[s] ? all
+                     : ((static_cast<uint64_t>(static_cast<uint32_t>(from[s])) << id_bits) |
+                        static_cast<uint32_t>(to[s]));
+    val[s] = static_cast<int32_t>(s);
+  }
+}
+
+// The run start of each sorted position (max-scan input): p where the key
+// changes, 0 elsewhere.
+__global__ void run_start_kernel(int64_t cap, const uint64_t *__restrict__ key, int32_t *__restrict__ start) {
+  for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < cap;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    start[p] = (p == 0 || key[p] != key[p - 1]) ? static_cast<int32_t>(p) : 0;
+}
+
+// Proposals of the connection at rank r = c / P: src = its source, dst
+// [sub 0], score [sub 1] at key philox32((src << 32) | dst, occurrence); a
+// dead proposer's candidates are vetoed.
+__global__ void propose_per_conn_kernel(ProposeArgs a, int64_t cap, const int32_t *__restrict__ from,
+                                        const int32_t *__restrict__ to, const uint8_t *__restrict__ dead,
+                                        const int32_t *__restrict__ rank_slot, const int32_t *__restrict__ run_start,
+                                        int32_t *__restrict__ src_out, int32_t *__restrict__ dst_out,
+                                        float *__restrict__ score_out) {
+  const uint64_t keyed_hi = keyed_hi_of(a);
+  const int64_t total = cap * a.proposals;
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < total;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = c / a.proposals;
+    const uint32_t j = static_cast<uint32_t>(c - r * a.proposals);
+    const int32_t slot = rank_slot[r];
+    const uint32_t occ = static_cast<uint32_t>(r - run_start[r]);
+    const int32_t cs = from[slot], cd = to[slot];
+    const uint32_t key = philox32((static_cast<uint64_t>(static_cast<uint32_t>(cs)) << 32) | static_cast<uint32_t>(cd),
+                                  occ);
+    const uint64_t seed = (keyed_hi << 32) | key;
+    int32_t src = cs;
+    int32_t dst = a.dst_lo + static_cast<int32_t>(uniform_int(unit_float(site_draw(seed, j, 0)), a.dst_n));
+    float score = proposal_score(a, seed, j, 1, src, dst);
+    apply_window(a, src, dst, score, dead[slot] == 0);
+    src_out[c] = src;
+    dst_out[c] = dst;
+    score_out[c] = score;
+  }
+}
+
+// The per-level cap over a level-major ordered list (pxb_select_step with
+// k = n): the first k of every level's run, listed levels ascending.
+__global__ void level_bounds_kernel(int64_t n, const int32_t *__restrict__ idx, const int32_t *__restrict__ src,
+                                    const int32_t *__restrict__ level, int32_t num_levels, int32_t *__restrict__ first,
+                                    int32_t *__restrict__ end) {
+  for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < n;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    auto lv = [&](int64_t q) {
+      const int32_t l = level[src[idx[q]]];
+      return l < 0 ? 0 : (l >= num_levels ? num_levels - 1 : l);
+    };
+    const int32_t l = lv(p);
+    if (p == 0 || lv(p - 1) != l) first[l] = static_cast<int32_t>(p);
+    if (p == n - 1 || lv(p + 1) != l) end[l] = static_cast<int32_t>(p + 1);
+  }
+}
+
+__global__ void level_caps_kernel(int32_t num_levels, int64_t k, const int32_t *__restrict__ first,
+                                  const int32_t *__restrict__ end, int32_t *__restrict__ off, int32_t *count) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int32_t acc = 0;
+  for (int l = 0; l < num_levels; ++l) {
+    off[l] = acc;
+    const int64_t m = end[l] - first[l];
+    acc += static_cast<int32_t>(m < k ? m : k);
+  }
+  off[num_levels] = acc;
+  if (count) *count = acc;
+}
+
+__global__ void level_cap_compact_kernel(int64_t n, const int32_t *__restrict__ idx, const int32_t *__restrict__ src,
+                                         const int32_t *__restrict__ level, int32_t num_levels, int64_t k,
+                                         const int32_t *__restrict__ first, const int32_t *__restrict__ off,
+                                         int32_t *__restrict__ out) {
+  for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < n;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int32_t l = level[src[idx[p]]];
+    l = l < 0 ? 0 : (l >= num_levels ? num_levels - 1 : l);
+    const int64_t r = p - first[l];
+    if (r < k) out[off[l] + r] = idx[p];
+  }
+}
+
+struct ConnRankScratch {
+  uint64_t *key_in, *key_out;
+  int32_t *val_in, *val_out, *start_in, *start_out;
+  void *cub_tmp;
+  size_t cub_bytes, total;
+};
+
+static int conn_rank_scratch(int64_t cap, int id_bits, char *base, ConnRankScratch *o) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = off;
+    off = align_up(off + (bytes ? bytes : 1), 256);
+    return base ? base + at : nullptr;
+  };
+  const int64_t c = cap > 0 ? cap : 1;
+  o->key_in = reinterpret_cast<uint64_t *>(take(c * 8));
+  o->key_out = reinterpret_cast<uint64_t *>(take(c * 8));
+  o->val_in = reinterpret_cast<int32_t *>(take(c * 4));
+  o->val_out = reinterpret_cast<int32_t *>(take(c * 4));
+  o->start_in = reinterpret_cast<int32_t *>(take(c * 4));
+  o->start_out = reinterpret_cast<int32_t *>(take(c * 4));
+  size_t t1 = 0, t2 = 0;
+  const int bits = 2 * id_bits < 64 ? 2 * id_bits : 64;
+  if (cub::DeviceRadixSort::SortPairs(nullptr, t1, o->key_in, o->key_out, o->val_in, o->val_out,
+                                      static_cast<int>(c), 0, bits) != cudaSuccess)
+    return PXB_ECUDA;
+  if (cub::DeviceScan::InclusiveScan(nullptr, t2, o->start_in, o->start_out, cub::Max(), static_cast<int>(c)) !=
+      cudaSuccess)
+    return PXB_ECUDA;
+  o->cub_bytes = t1 > t2 ? t1 : t2;
+  o->cub_tmp = take(o->cub_bytes);
+  o->total = off;
+  return PXB_OK;
+}
+
 }  // namespace pxb
 
 extern "C" int pxb_total_order(int64_t n, const float *score, const int32_t *src, const int32_t *dst,
@@ -1034,5 +1202,118 @@ extern "C" int pxb_propose_select_unique(int32_t num_units, uint64_t network_see
   fs_bins_kernel<<<sm_count() * 8, kFsThreads, 0, st>>>(g, ia, o, src_out, dst_out, weight_out, growable_out,
                                                         o.bi + (g.k > 0 ? g.k : 1), status);
   PXB_LAUNCHED("fs_bins_kernel");
+  return PXB_OK;
+}
+
+static ProposeArgs propose_args(int32_t num_units, int32_t proposals, uint64_t network_seed, int32_t step,
+                                const int32_t *step_dev, int32_t dst_lo, int32_t dst_n, int32_t score_kind,
+                                const float *grad, const float *act, const int32_t *level, const uint8_t *pruned,
+                                int32_t max_level_gap, int32_t direction, int32_t allow_self_loops,
+                                int32_t bucket_level, int32_t src_level_bound) {
+  ProposeArgs a{num_units, proposals, 0, network_seed, step_dev, dst_lo, dst_n, score_kind, grad, act, level,
+                pruned, max_level_gap, direction, allow_self_loops, bucket_level, src_level_bound};
+  if (step_dev == nullptr)
+    a.keyed_hi = philox32(network_seed, (static_cast<uint64_t>(static_cast<uint32_t>(step)) << 8) | 1u);
+  return a;
+}
+
+extern "C" int pxb_propose_global(int32_t proposals, uint64_t network_seed, int32_t step, int32_t num_units,
+                                  int32_t src_lo, int32_t src_n, int32_t dst_lo, int32_t dst_n, int32_t score_kind,
+                                  const float *grad, const float *act, const int32_t *level, const uint8_t *pruned,
+                                  int32_t max_level_gap, int32_t direction, int32_t allow_self_loops,
+                                  int32_t bucket_level, int32_t src_level_bound, const int32_t *step_dev,
+                                  int32_t *src_out, int32_t *dst_out, float *score_out, void *stream) {
+  PXB_REQUIRE(proposals >= 0 && num_units >= 1 && src_n >= 1 && dst_n >= 1, "pxb_propose_global: bad sizes");
+  PXB_REQUIRE(score_kind >= 0 && score_kind <= 2, "pxb_propose_global: unknown score kind %d", score_kind);
+  if (proposals == 0) return PXB_OK;
+  PXB_REQUIRE(level && src_out && dst_out && score_out, "pxb_propose_global: a pointer is NULL");
+  PXB_REQUIRE(score_kind != PXB_SCORE_GRAD_ACT || (grad && act), "pxb_propose_global: grad_act needs grad and act");
+  const ProposeArgs a = propose_args(num_units, proposals, network_seed, step, step_dev, dst_lo, dst_n, score_kind,
+                                     grad, act, level, pruned, max_level_gap, direction, allow_self_loops, bucket_level,
+                                     src_level_bound);
+  propose_global_kernel<<<grid_for(proposals, 256, 4), 256, 0, as_stream(stream)>>>(a, src_lo, src_n, src_out,
+                                                                                      dst_out, score_out);
+  PXB_LAUNCHED("propose_global_kernel");
+  return PXB_OK;
+}
+
+extern "C" int pxb_conn_rank_scratch_bytes(int64_t cap, int32_t num_units, size_t *bytes) {
+  PXB_REQUIRE(bytes && cap >= 0 && cap < (int64_t(1) << 31) && num_units >= 1,
+              "pxb_conn_rank_scratch_bytes: bad arguments");
+  ConnRankScratch o;
+  if (conn_rank_scratch(cap, bits_for(int64_t(num_units) + 1), nullptr, &o) != PXB_OK) {
+    set_error("pxb_conn_rank_scratch_bytes: CUB size query failed");
+    return PXB_ECUDA;
+  }
+  *bytes = o.total;
+  return PXB_OK;
+}
+
+extern "C" int pxb_propose_per_conn(int64_t cap, const int32_t *from_id, const int32_t *to_id, const uint8_t *dead,
+                                    int32_t proposals, uint64_t network_seed, int32_t step, int32_t num_units,
+                                    int32_t dst_lo, int32_t dst_n, int32_t score_kind, const float *grad,
+                                    const float *act, const int32_t *level, const uint8_t *pruned,
+                                    int32_t max_level_gap, int32_t direction, int32_t allow_self_loops,
+                                    int32_t bucket_level, int32_t src_level_bound, const int32_t *step_dev,
+                                    int32_t *src_out, int32_t *dst_out, float *score_out, void *scratch,
+                                    size_t scratch_bytes, void *stream) {
+  PXB_REQUIRE(cap >= 0 && cap < (int64_t(1) << 31) && proposals >= 0 && num_units >= 1 && dst_n >= 1,
+              "pxb_propose_per_conn: bad sizes");
+  PXB_REQUIRE(cap * int64_t(proposals) < (int64_t(1) << 31), "pxb_propose_per_conn: too many candidates");
+  PXB_REQUIRE(score_kind >= 0 && score_kind <= 2, "pxb_propose_per_conn: unknown score kind %d", score_kind);
+  if (cap == 0 || proposals == 0) return PXB_OK;
+  PXB_REQUIRE(from_id && to_id && dead && level && src_out && dst_out && score_out && scratch,
+              "pxb_propose_per_conn: a pointer is NULL");
+  PXB_REQUIRE(score_kind != PXB_SCORE_GRAD_ACT || (grad && act), "pxb_propose_per_conn: grad_act needs grad and act");
+  const int id_bits = bits_for(int64_t(num_units) + 1);
+  ConnRankScratch o;
+  if (conn_rank_scratch(cap, id_bits, static_cast<char *>(scratch), &o) != PXB_OK) {
+    set_error("pxb_propose_per_conn: CUB size query failed");
+    return PXB_ECUDA;
+  }
+  PXB_REQUIRE(o.total <= scratch_bytes, "pxb_propose_per_conn: scratch has %zu bytes, needs %zu", scratch_bytes,
+              o.total);
+  cudaStream_t st = as_stream(stream);
+  const int grid = grid_for(cap, 256, 8);
+  conn_key_kernel<<<grid, 256, 0, st>>>(cap, from_id, to_id, dead, id_bits, o.key_in, o.val_in);
+  PXB_LAUNCHED("conn_key_kernel");
+  size_t tb = o.cub_bytes;
+  const int bits = 2 * id_bits < 64 ? 2 * id_bits : 64;
+  PXB_CUDA(cub::DeviceRadixSort::SortPairs(o.cub_tmp, tb, o.key_in, o.key_out, o.val_in, o.val_out,
+                                           static_cast<int>(cap), 0, bits, st));
+  run_start_kernel<<<grid, 256, 0, st>>>(cap, o.key_out, o.start_in);
+  PXB_LAUNCHED("run_start_kernel");
+  tb = o.cub_bytes;
+  PXB_CUDA(cub::DeviceScan::InclusiveScan(o.cub_tmp, tb, o.start_in, o.start_out, cub::Max(), static_cast<int>(cap),
+                                          st));
+  const ProposeArgs a = propose_args(num_units, proposals, network_seed, step, step_dev, dst_lo, dst_n, score_kind,
+                                     grad, act, level, pruned, max_level_gap, direction, allow_self_loops, bucket_level,
+                                     src_level_bound);
+  propose_per_conn_kernel<<<grid_for(cap * proposals, 256, 8), 256, 0, st>>>(
+      a, cap, from_id, to_id, dead, o.val_out, o.start_out, src_out, dst_out, score_out);
+  PXB_LAUNCHED("propose_per_conn_kernel");
+  return PXB_OK;
+}
+
+extern "C" int pxb_cap_per_level(int64_t n, const int32_t *idx, const int32_t *src, const int32_t *level,
+                                 int32_t num_levels, int64_t k, int32_t *out_idx, int32_t *out_count,
+                                 int32_t *scratch, void *stream) {
+  PXB_REQUIRE(n >= 0 && n < (int64_t(1) << 31) && k >= 0 && num_levels >= 1, "pxb_cap_per_level: bad sizes");
+  PXB_REQUIRE(scratch && out_count, "pxb_cap_per_level: scratch / out_count is NULL");
+  cudaStream_t st = as_stream(stream);
+  int32_t *first = scratch, *end = scratch + num_levels, *off = scratch + 2 * num_levels;
+  PXB_CUDA(cudaMemsetAsync(scratch, 0, sizeof(int32_t) * (3 * num_levels + 1), st));
+  if (n > 0) {
+    PXB_REQUIRE(idx && src && level && out_idx, "pxb_cap_per_level: a pointer is NULL");
+    level_bounds_kernel<<<grid_for(n, 256, 8), 256, 0, st>>>(n, idx, src, level, num_levels, first, end);
+    PXB_LAUNCHED("level_bounds_kernel");
+  }
+  level_caps_kernel<<<1, 32, 0, st>>>(num_levels, k, first, end, off, out_count);
+  PXB_LAUNCHED("level_caps_kernel");
+  if (n > 0) {
+    level_cap_compact_kernel<<<grid_for(n, 256, 8), 256, 0, st>>>(n, idx, src, level, num_levels, k, first, off,
+                                                                  out_idx);
+    PXB_LAUNCHED("level_cap_compact_kernel");
+  }
   return PXB_OK;
 }

@@ -250,6 +250,69 @@ def propose_per_unit(num_units: int, proposals: int, network_seed: int, step: in
     return src, dst, score
 
 
+def _window_args(level, pruned, max_level_gap, direction, allow_self_loops, bucket_level, src_level_bound):
+    return (ptr(level), ptr(pruned), ctypes.c_int32(max_level_gap), ctypes.c_int32(direction),
+            ctypes.c_int32(1 if allow_self_loops else 0), ctypes.c_int32(bucket_level), ctypes.c_int32(src_level_bound))
+
+
+def propose_global(proposals: int, network_seed: int, step: int, num_units: int, *, src_lo: int, src_n: int,
+                   dst_lo: int, dst_n: int, score_kind: int, level: torch.Tensor, grad: torch.Tensor | None = None,
+                   act: torch.Tensor | None = None, pruned: torch.Tensor | None = None, max_level_gap: int = 1,
+                   direction: int = 0, allow_self_loops: bool = False, bucket_level: int = -1,
+                   src_level_bound: int = 0, step_dev: torch.Tensor | None = None,
+                   out: tuple | None = None) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    dev = level.device
+    if out is None:
+        out = (torch.empty(proposals, dtype=torch.int32, device=dev),
+               torch.empty(proposals, dtype=torch.int32, device=dev),
+               torch.empty(proposals, dtype=torch.float32, device=dev))
+    src, dst, score = out
+    call("pxb_propose_global", ctypes.c_int32(proposals), ctypes.c_uint64(network_seed), ctypes.c_int32(step),
+         ctypes.c_int32(num_units), ctypes.c_int32(src_lo), ctypes.c_int32(src_n), ctypes.c_int32(dst_lo),
+         ctypes.c_int32(dst_n), ctypes.c_int32(score_kind), ptr(grad), ptr(act),
+         *_window_args(level, pruned, max_level_gap, direction, allow_self_loops, bucket_level, src_level_bound),
+         ptr(step_dev), ptr(src), ptr(dst), ptr(score), _stream())
+    return src, dst, score
+
+
+def conn_rank_scratch(cap: int, num_units: int) -> int:
+    return query_size("pxb_conn_rank_scratch_bytes", ctypes.c_int64(cap), ctypes.c_int32(num_units))
+
+
+def propose_per_conn(b: Bucket, proposals: int, network_seed: int, step: int, num_units: int, *, dst_lo: int,
+                     dst_n: int, score_kind: int, level: torch.Tensor, grad: torch.Tensor | None = None,
+                     act: torch.Tensor | None = None, pruned: torch.Tensor | None = None, max_level_gap: int = 1,
+                     direction: int = 0, allow_self_loops: bool = False, bucket_level: int = -1,
+                     src_level_bound: int = 0, step_dev: torch.Tensor | None = None,
+                     scratch: torch.Tensor | None = None,
+                     out: tuple | None = None) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Per-connection proposals over one (bucket-major) arena `b`."""
+    cap = _bucket(b)
+    dev = level.device
+    total = cap * proposals
+    if out is None:
+        out = (torch.empty(total, dtype=torch.int32, device=dev), torch.empty(total, dtype=torch.int32, device=dev),
+               torch.empty(total, dtype=torch.float32, device=dev))
+    if scratch is None:
+        scratch = torch.empty(max(conn_rank_scratch(cap, num_units), 1), dtype=torch.uint8, device=dev)
+    src, dst, score = out
+    call("pxb_propose_per_conn", ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]), ptr(b["dead"]),
+         ctypes.c_int32(proposals), ctypes.c_uint64(network_seed), ctypes.c_int32(step), ctypes.c_int32(num_units),
+         ctypes.c_int32(dst_lo), ctypes.c_int32(dst_n), ctypes.c_int32(score_kind), ptr(grad), ptr(act),
+         *_window_args(level, pruned, max_level_gap, direction, allow_self_loops, bucket_level, src_level_bound),
+         ptr(step_dev), ptr(src), ptr(dst), ptr(score), ptr(scratch), ctypes.c_size_t(scratch.numel()), _stream())
+    return src, dst, score
+
+
+def cap_per_level(idx: torch.Tensor, src: torch.Tensor, level: torch.Tensor, num_levels: int, k: int,
+                  out: torch.Tensor, count: torch.Tensor, scratch: torch.Tensor) -> None:
+    """First k of every level's run of the level-major list `idx` (out filled
+    with -1 beyond the winners; count = their number, device)."""
+    out.fill_(-1)
+    call("pxb_cap_per_level", ctypes.c_int64(idx.numel()), ptr(idx), ptr(src), ptr(level), ctypes.c_int32(num_levels),
+         ctypes.c_int64(k), ptr(out), ptr(count), ptr(scratch), _stream())
+
+
 def total_order_scratch(n: int, id_bound: int) -> int:
     return query_size("pxb_total_order_scratch_bytes", ctypes.c_int64(n), ctypes.c_int32(id_bound))
 

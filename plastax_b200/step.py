@@ -201,11 +201,28 @@ class StepFn:
         ac, st, dev = self.ac, self.static, self.dev
         n = st.num_units
         P = ac.proposals_per_proposer
-        self.n_cand = n * P
-        self.k = max(0, min(int(ac.max_new_per_level), self.n_cand))
-        if ac.level_cap_scope != "step":
-            raise NotImplementedError(
-                "the engine runs level_cap_scope='step' growth; per-source-level caps have no lowering yet")
+        if ac.proposer == "per_unit":
+            self.n_cand = n * P
+        elif ac.proposer == "global":
+            self.n_cand = P
+        else:
+            if self.sharded:
+                raise NotImplementedError("the per-connection proposer under Scheme-A has no engine lowering (it "
+                                          "ranks every rank's connections)")
+            self.conn_slots = sum(int(c) for c in st.level_capacities)
+            self.n_cand = self.conn_slots * P
+            self.conn_scratch = torch.empty(max(K.conn_rank_scratch(self.conn_slots, n), 1), dtype=torch.uint8,
+                                            device=dev)
+        src_n = ac.src_n if ac.src_n is not None else n - ac.src_lo
+        if ac.proposer == "global" and (ac.src_lo < 0 or src_n < 1 or ac.src_lo + src_n > n):
+            raise ValueError(f"ProposeAddConn: sources [{ac.src_lo}, {ac.src_lo + src_n}) exceed the {n} units")
+        self.src_n = src_n
+        # the cap: per source level (the default) or once per step; "all"
+        # keeps every finite candidate
+        self.k_sel = self.n_cand if ac.selection == "all" else max(0, min(int(ac.max_new_per_level), self.n_cand))
+        self.per_level = ac.level_cap_scope == "source_level" and ac.selection != "all"
+        self.sel_levels = st.num_levels
+        self.k = min(self.n_cand, self.sel_levels * self.k_sel) if self.per_level else self.k_sel
         self.cand = (torch.empty(self.n_cand, dtype=torch.int32, device=dev),
                      torch.empty(self.n_cand, dtype=torch.int32, device=dev),
                      torch.empty(self.n_cand, dtype=torch.float32, device=dev))
@@ -215,13 +232,18 @@ class StepFn:
         # One proposal per unit: every candidate's source is its own unit, so
         # (score, src) is a unique key in the total order and a radix select
         # of the first k replaces the full sort.
-        self.unique_src = P == 1
+        self.unique_src = P == 1 and ac.proposer == "per_unit" and not self.per_level
         self.perm = torch.empty(self.n_cand if not self.unique_src else max(self.k, 1), dtype=torch.int32, device=dev)
         need = K.topk_unique_scratch(self.n_cand, self.k, n) if self.unique_src else K.total_order_scratch(self.n_cand, n)
         self.order_scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
         self.win = torch.empty(max(self.k, 1), dtype=torch.int32, device=dev)
-        self.sel_scratch = torch.empty(max(K.select_step_scratch(self.n_cand, self.k), 1), dtype=torch.uint8,
+        k_listed = self.n_cand if self.per_level else self.k
+        self.sel_scratch = torch.empty(max(K.select_step_scratch(self.n_cand, k_listed), 1), dtype=torch.uint8,
                                        device=dev)
+        if self.per_level:
+            self.win_all = torch.empty(max(self.n_cand, 1), dtype=torch.int32, device=dev)
+            self.win_count = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.cap_scratch = torch.zeros(3 * self.sel_levels + 1, dtype=torch.int32, device=dev)
         kk = max(self.k, 1)
         self.claim_in = (torch.empty(kk, dtype=torch.int32, device=dev), torch.empty(kk, dtype=torch.int32, device=dev),
                          torch.empty(kk, dtype=torch.float32, device=dev), torch.empty(kk, dtype=torch.uint8, device=dev))
@@ -246,6 +268,7 @@ class StepFn:
         # (keys binned and ranked, no sort pass) replaces propose + top-k +
         # level listing + gather
         self.fast_select = (self.unique_src and ac.score in ("uniform", "uniform_q256")
+                            and ac.level_cap_scope == "step" and ac.selection == "top_k"
                             and self.static.num_levels <= 8 and self.k > 0
                             and not ac.dedupe_live and not ac.dedupe_step)
         self.dedupe = ac.dedupe_live or ac.dedupe_step
@@ -473,12 +496,27 @@ class StepFn:
                                     out=self.claim_in)
             self.launches += 6
             return
-        K.propose_per_unit(n, ac.proposals_per_proposer, st.seed, state.step, dst_lo=ac.dst_lo, dst_n=dst_n,
-                           score_kind=self.score_kind, level=level, grad=grad, act=units[ACTIVATION.name],
-                           pruned=pruned, max_level_gap=ac.max_level_gap, direction=self.direction,
-                           allow_self_loops=ac.allow_self_loops,
-                           src_level_bound=0 if self.pipeline else self.num_buckets, step_dev=self.step_dev,
-                           out=self.cand)
+        window = dict(level=level, grad=grad, act=units[ACTIVATION.name], pruned=pruned,
+                      max_level_gap=ac.max_level_gap, direction=self.direction,
+                      allow_self_loops=ac.allow_self_loops,
+                      src_level_bound=0 if self.pipeline else self.num_buckets, step_dev=self.step_dev)
+        if ac.proposer == "per_unit":
+            K.propose_per_unit(n, ac.proposals_per_proposer, st.seed, state.step, dst_lo=ac.dst_lo, dst_n=dst_n,
+                               score_kind=self.score_kind, out=self.cand, **window)
+        elif ac.proposer == "global":
+            K.propose_global(ac.proposals_per_proposer, st.seed, state.step, n, src_lo=ac.src_lo, src_n=self.src_n,
+                             dst_lo=ac.dst_lo, dst_n=dst_n, score_kind=self.score_kind, out=self.cand, **window)
+        else:
+            conns = state.conns
+            arena = conns[0] if len(conns) == 1 else {
+                c: torch.cat([b[c] for b in conns]) for c in ("from_id", "to_id", "dead")}
+            K.propose_per_conn(arena, ac.proposals_per_proposer, st.seed, state.step, n, dst_lo=ac.dst_lo,
+                               dst_n=dst_n, score_kind=self.score_kind, scratch=self.conn_scratch, out=self.cand,
+                               **window)
+        if ac.selection == "threshold":
+            # below the threshold is a veto (src/plastax/phases.py:4324-4487)
+            sc = self.cand[2]
+            sc.masked_fill_(sc < float(ac.threshold), float("-inf"))
         src, dst, score = self.cand
         if self.dedupe:
             combine = None
@@ -494,8 +532,15 @@ class StepFn:
             top = K.topk_unique(score, src, n, self.k, out=self.perm, scratch=self.order_scratch)
         else:
             top = K.total_order(score, src, dst, n, perm=self.perm, scratch=self.order_scratch)
-        K.select_step(top, score, src, level, self.k, win=self.win, scratch=self.sel_scratch,
-                      num_levels=self.static.num_levels)
+        if self.per_level:
+            # every candidate listed levels ascending, then each level's first k
+            K.select_step(top, score, src, level, self.n_cand, win=self.win_all, scratch=self.sel_scratch,
+                          num_levels=self.sel_levels)
+            K.cap_per_level(self.win_all, src, level, self.sel_levels, self.k_sel, self.win, self.win_count,
+                            self.cap_scratch)
+        else:
+            K.select_step(top, score, src, level, self.k, win=self.win, scratch=self.sel_scratch,
+                          num_levels=self.static.num_levels)
         kk = min(self.k, self.n_cand)
         K.gather_winners(self.win, kk, self.k, src, dst, score, init_kind=self.init_kind, init_a=self.init_a,
                          out=self.claim_in)

@@ -21,8 +21,12 @@ Recognised forms:
   adam, adamw, rmsprop; src/plastax/optim).
 - PruneConn: |weight| < threshold (MagnitudePrune) or |weight| <
   unit[field, dst] (DestinationThresholdPrune).
-- ProposeAddConn: proposer "per_unit", dst = dst_lo + uniform_int(dst_n)
-  [sub 0], score uniform / floor(u*256)/256 [sub 1] or |grad[dst]*act[src]|,
+- ProposeAddConn: proposer "per_unit" (dst = dst_lo + uniform_int(dst_n)
+  [sub 0], score [sub 1]), "global" (src = src_lo + uniform_int(src_n) [sub
+  0], dst [sub 1], score [sub 2]) or "per_connection" (src = the proposing
+  connection's source, dst [sub 0], score [sub 1]); score uniform /
+  floor(u*256)/256 or |grad[dst]*act[src]|; selection top_k, threshold (a
+  constant) or all, capped per source level or per step;
   init weight constant / dyadic / hashed uniform; dedupe_live (a candidate
   equal to a live edge is vetoed) and dedupe_step (a pair's copies after the
   first in score order are vetoed).
@@ -134,6 +138,8 @@ class ProposeAddConn:
     max_new_per_level: int
     dst_lo: int = 0
     dst_n: int | None = None
+    src_lo: int = 0  # the global proposer's source range
+    src_n: int | None = None
     score: str = "uniform"  # "uniform", "uniform_q256" or "grad_act"
     init: tuple = ("const", 0.0)  # ("const", a) | ("dyadic",) | ("hash_uniform", a)
     proposer: str = "per_unit"
@@ -148,12 +154,15 @@ class ProposeAddConn:
     trigger: Any = "every_step"
     on_overflow: str = "flag"
     grad_field: FieldSpec = GRAD_PRE_ACT
+    threshold: float | None = None  # selection "threshold": keep scores >= threshold
 
     def validate(self) -> None:
-        if self.proposer != "per_unit":
-            raise NotImplementedError(f"proposer {self.proposer!r} has no engine lowering (per_unit only)")
-        if self.selection != "top_k":
-            raise NotImplementedError(f"selection {self.selection!r} has no engine lowering (top_k only)")
+        if self.proposer not in ("per_unit", "global", "per_connection"):
+            raise ValueError(f"unknown proposer {self.proposer!r}")
+        if self.selection not in ("top_k", "threshold", "all"):
+            raise ValueError(f"unknown selection {self.selection!r}")
+        if self.selection == "threshold" and self.threshold is None:
+            raise ValueError("selection 'threshold' needs ProposeAddConn.threshold")
         if self.level_cap_scope not in ("source_level", "step"):
             raise ValueError(f"unknown level_cap_scope {self.level_cap_scope!r}")
         if self.direction not in ("any", "deeper", "same_or_deeper"):

@@ -158,10 +158,14 @@ def test_traits_reject_forms_without_a_lowering():
     with pytest.raises(NotImplementedError, match="prod"):
         class Bad2(px.Network):  # noqa: F841
             forward_pass = px.ForwardPass("tanh", px.monoid.prod)
-    with pytest.raises(NotImplementedError, match="per_unit"):
+    with pytest.raises(ValueError, match="unknown proposer"):
         class Bad3(px.Network):  # noqa: F841
             forward_pass = px.ForwardPass("tanh")
-            add_conn = px.ProposeAddConn(proposals_per_proposer=1, max_new_per_level=1, proposer="global")
+            add_conn = px.ProposeAddConn(proposals_per_proposer=1, max_new_per_level=1, proposer="shortlist")
+    with pytest.raises(ValueError, match="threshold"):
+        class Bad5(px.Network):  # noqa: F841
+            forward_pass = px.ForwardPass("tanh")
+            add_conn = px.ProposeAddConn(proposals_per_proposer=1, max_new_per_level=1, selection="threshold")
     with pytest.raises(NotImplementedError, match="unit-lifecycle"):
         class Bad4(px.Network):  # noqa: F841
             forward_pass = px.ForwardPass("tanh")
