@@ -448,6 +448,15 @@ PXB_API int pxb_dedupe_apply(int64_t n, float *score, const uint8_t *live_hit,
                              int32_t step_repeats, void *scratch,
                              size_t scratch_bytes, void *stream);
 
+/* The resort's compaction order (src/plastax/topo.py:303-452): perm_out =
+ * the bucket's slots stably ordered by dead * num_units + from_id (live
+ * edges grouped by source, old relative order kept within a source, dead
+ * slots last); the caller gathers every column through it. */
+PXB_API int pxb_resort_order_scratch_bytes(int64_t cap, size_t *bytes);
+PXB_API int pxb_resort_order(int64_t cap, const uint8_t *dead, const int32_t *from_id,
+                             int32_t num_units, int32_t *perm_out, void *scratch,
+                             size_t scratch_bytes, void *stream);
+
 /* ------------------------------------------------------------------ */
 /* slot claim                                                          */
 /* ------------------------------------------------------------------ */

@@ -11,7 +11,9 @@ a missing libpxb.so is an error.
 from plastax_b200 import monoid, optim
 from plastax_b200.builder import NetworkBuilder
 from plastax_b200.state import NetworkState, NetworkStatic, live_conn_count, make_empty_state
-from plastax_b200.step import GrowthRemainder, StepFn, StepInputs, StepResult, make_step
+from plastax_b200.state import grow_bucket
+from plastax_b200.step import GrowthRemainder, StepFn, StepInputs, StepResult, make_growth_retry, make_step
+from plastax_b200.topo import resort
 from plastax_b200.traits import (
     GRAD_PRE_ACT,
     LOSS_GRAD,
@@ -45,5 +47,5 @@ __all__ = [
     "BackwardPass", "DestinationThresholdPrune", "FieldSpec", "ForwardPass", "GrowthRemainder", "MSELoss",
     "MagnitudePrune", "MeanFloatFirstRest", "Network", "NetworkBuilder", "NetworkState", "NetworkStatic", "Propagation", "ProposeAddConn",
     "PruneConn", "ResetGlobal", "ShardSpec", "SoftmaxCrossEntropyLoss", "StepFn", "StepInputs", "StepResult", "live_conn_count",
-    "make_empty_state", "make_step", "monoid", "optim",
+    "grow_bucket", "make_empty_state", "make_growth_retry", "make_step", "monoid", "optim", "resort",
 ]

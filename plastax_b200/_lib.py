@@ -150,6 +150,8 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
                                      c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32, c_i32, c_ptr,
                                      c_ptr, c_ptr, c_ptr, c_ptr, c_size, c_ptr]),
     "pxb_cap_per_level": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_ptr]),
+    "pxb_resort_order_scratch_bytes": (c_i32, [c_i64, ctypes.POINTER(c_size)]),
+    "pxb_resort_order": (c_i32, [c_i64, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_size, c_ptr]),
     "pxb_select_unique_scratch_bytes": (c_i32, [c_i32, c_i64, c_i32, c_i32, ctypes.POINTER(c_size)]),
     "pxb_propose_select_unique": (
         c_i32, [c_i32, ctypes.c_uint64, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32,

@@ -1069,6 +1069,21 @@ static int conn_rank_scratch(int64_t cap, int id_bits, char *base, ConnRankScrat
   return PXB_OK;
 }
 
+// ---------------------------------------------------------------------------
+// resort compaction order (src/plastax/topo.py:303-452): a stable order of a
+// bucket's slots by dead * num_units + from_id
+// ---------------------------------------------------------------------------
+__global__ void resort_key_kernel(int64_t cap, const uint8_t *__restrict__ dead, const int32_t *__restrict__ from,
+                                  int32_t num_units, uint32_t *__restrict__ key, int32_t *__restrict__ val) {
+  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < cap;
+       s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int32_t f = from[s];
+    f = f < 0 ? 0 : (f >= num_units ? num_units - 1 : f);
+    key[s] = (dead[s] ? static_cast<uint32_t>(num_units) : 0u) + static_cast<uint32_t>(f);
+    val[s] = static_cast<int32_t>(s);
+  }
+}
+
 }  // namespace pxb
 
 extern "C" int pxb_total_order(int64_t n, const float *score, const int32_t *src, const int32_t *dst,
@@ -1315,5 +1330,45 @@ extern "C" int pxb_cap_per_level(int64_t n, const int32_t *idx, const int32_t *s
                                                                   out_idx);
     PXB_LAUNCHED("level_cap_compact_kernel");
   }
+  return PXB_OK;
+}
+
+extern "C" int pxb_resort_order_scratch_bytes(int64_t cap, size_t *bytes) {
+  PXB_REQUIRE(bytes && cap >= 0 && cap < (int64_t(1) << 31), "pxb_resort_order_scratch_bytes: bad arguments");
+  const int64_t c = cap > 0 ? cap : 1;
+  size_t t = 0;
+  if (cub::DeviceRadixSort::SortPairs(nullptr, t, static_cast<uint32_t *>(nullptr), static_cast<uint32_t *>(nullptr),
+                                      static_cast<int32_t *>(nullptr), static_cast<int32_t *>(nullptr),
+                                      static_cast<int>(c), 0, 32) != cudaSuccess) {
+    set_error("pxb_resort_order_scratch_bytes: CUB size query failed");
+    return PXB_ECUDA;
+  }
+  *bytes = align_up(c * 4, 256) * 3 + align_up(t, 256);
+  return PXB_OK;
+}
+
+extern "C" int pxb_resort_order(int64_t cap, const uint8_t *dead, const int32_t *from_id, int32_t num_units,
+                                int32_t *perm_out, void *scratch, size_t scratch_bytes, void *stream) {
+  PXB_REQUIRE(cap >= 0 && cap < (int64_t(1) << 31) && num_units >= 1 && num_units < (1 << 30),
+              "pxb_resort_order: sizes out of range");
+  if (cap == 0) return PXB_OK;
+  PXB_REQUIRE(dead && from_id && perm_out && scratch, "pxb_resort_order: a pointer is NULL");
+  size_t need = 0;
+  int rc = pxb_resort_order_scratch_bytes(cap, &need);
+  if (rc) return rc;
+  PXB_REQUIRE(need <= scratch_bytes, "pxb_resort_order: scratch has %zu bytes, needs %zu", scratch_bytes, need);
+  char *base = static_cast<char *>(scratch);
+  const size_t col = align_up(cap * 4, 256);
+  uint32_t *key_in = reinterpret_cast<uint32_t *>(base), *key_out = reinterpret_cast<uint32_t *>(base + col);
+  int32_t *val_in = reinterpret_cast<int32_t *>(base + 2 * col);
+  void *tmp = base + 3 * col;
+  size_t tb = scratch_bytes - 3 * col;
+  int bits = 1;
+  while (bits < 32 && (int64_t(1) << bits) < 2 * int64_t(num_units)) ++bits;
+  cudaStream_t st = as_stream(stream);
+  resort_key_kernel<<<grid_for(cap, 256, 8), 256, 0, st>>>(cap, dead, from_id, num_units, key_in, val_in);
+  PXB_LAUNCHED("resort_key_kernel");
+  PXB_CUDA(cub::DeviceRadixSort::SortPairs(tmp, tb, key_in, key_out, val_in, perm_out, static_cast<int>(cap), 0, bits,
+                                           st));
   return PXB_OK;
 }

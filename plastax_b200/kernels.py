@@ -313,6 +313,17 @@ def cap_per_level(idx: torch.Tensor, src: torch.Tensor, level: torch.Tensor, num
          ctypes.c_int64(k), ptr(out), ptr(count), ptr(scratch), _stream())
 
 
+def resort_order(b: Bucket, num_units: int) -> torch.Tensor:
+    """The bucket's slots stably ordered by dead * num_units + from_id."""
+    cap = _bucket(b)
+    perm = torch.empty(max(cap, 1), dtype=torch.int32, device=b["dead"].device)
+    scratch = torch.empty(max(query_size("pxb_resort_order_scratch_bytes", ctypes.c_int64(cap)), 1),
+                          dtype=torch.uint8, device=b["dead"].device)
+    call("pxb_resort_order", ctypes.c_int64(cap), ptr(b["dead"]), ptr(b["from_id"]), ctypes.c_int32(num_units),
+         ptr(perm), ptr(scratch), ctypes.c_size_t(scratch.numel()), _stream())
+    return perm[:cap]
+
+
 def total_order_scratch(n: int, id_bound: int) -> int:
     return query_size("pxb_total_order_scratch_bytes", ctypes.c_int64(n), ctypes.c_int32(id_bound))
 

@@ -104,3 +104,36 @@ def live_conn_count(state: NetworkState, level: int | None = None) -> int:
 def live_unit_mask(units: Columns) -> torch.Tensor | None:
     pruned = units.get(PRUNED.name)
     return None if pruned is None else pruned == 0
+
+
+def grow_bucket(static: NetworkStatic, state: NetworkState, level: int) -> tuple[NetworkStatic, NetworkState]:
+    """Pad one bucket with never-used slots (src/plastax/state.py:238-313).
+
+    The new capacity is the sizing policy for live + 1 edges, at least twice
+    the old (1.5x with an alignment). The padding takes every column's
+    default (tombstoned), so in PIPELINE mode it extends the never-used tail
+    and `tail_start` stays put. Returns a new (static, state); the step is
+    rebuilt for the new static (make_step), as the reference retraces.
+    """
+    from plastax_b200.topo import capacity_policy
+
+    if static.num_shards > 1:
+        raise NotImplementedError("grow_bucket under Scheme-A has no engine lowering (the bands would move)")
+    old = static.level_capacities[level]
+    live = live_conn_count(state, level)
+    policy = capacity_policy(live + 1, headroom=static.capacity_headroom, align=static.capacity_align)
+    if static.capacity_align is None:
+        floor = old * 2
+    else:
+        floor = capacity_policy(old + old // 2, align=static.capacity_align)
+    new_cap = max(policy, floor)
+    pad = new_cap - old
+    cols = state.conns[level]
+    dev = cols["dead"].device
+    grown = {s.name: torch.cat([cols[s.name], torch.full((pad,), s.default, dtype=torch_dtype(s), device=dev)])
+             for s in static.conn_fields}
+    conns = tuple(grown if i == level else c for i, c in enumerate(state.conns))
+    caps = tuple(new_cap if i == level else c for i, c in enumerate(static.level_capacities))
+    new_static = dataclasses.replace(static, level_capacities=caps)
+    new_state = dataclasses.replace(state, conns=conns)
+    return new_static, new_state

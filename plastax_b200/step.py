@@ -163,6 +163,7 @@ class StepFn:
 
         st = self.static
         level = state.units[LEVEL.name]
+        self._level = level
         if self.use_mirror:
             self.mirrors = [Mirror(b, st.num_units, chunk_bits=self.mirror_chunk_bits) for b in state.conns]
         if self.peer_reduce:
@@ -563,6 +564,21 @@ class StepFn:
             self._select(state)
         cs, cd, cw, grow = self.claim_in
         max_new = -1 if ac.max_new_per_step is None else int(ac.max_new_per_step)
+        remainder = self._claim(state, cs, cd, cw, grow, max_new, fresh=True)
+        if ac.on_overflow == "error" and bool(self.overflow.item()):
+            raise RuntimeError('add_conn overflow: selected candidates exceeded the free connection capacity '
+                               '(the rule declares on_overflow = "error").')
+        return remainder
+
+    def _claim(self, state: NetworkState, cs: torch.Tensor, cd: torch.Tensor, cw: torch.Tensor, grow: torch.Tensor,
+               max_new: int, *, fresh: bool) -> GrowthRemainder:
+        """The claim of a level-major candidate list into every bucket
+        (src/plastax/phases.py:2853-3106): grown (+)= the committed count
+        (from 0 when `fresh`), overflow = whether any growable candidate was
+        dropped, needs_resort |= a committed edge into a level <= its
+        source's. Returns the list with its dropped flags."""
+        st = self.static
+        level = state.units[LEVEL.name]
         if self.pipeline:
             # the winners are listed levels ascending: the claim partitions
             mode = _lib.CLAIM_PIPELINE | _lib.CLAIM_LEVEL_MAJOR
@@ -577,17 +593,20 @@ class StepFn:
             lv = level[cs.long()]
             buckets = [(bk, (g & (lv == bk)).to(torch.uint8)) for bk in range(self.num_buckets)]
             max_new = -1
+        if not fresh:
+            self.overflow.zero_()
         for bi, (bk, gb) in enumerate(buckets):
             b, ws = state.conns[bk], self.claim_ws[bk]
             base = st.shard_base(bk)
             bm, _ = self._bm(bk)
             before = totals = None
-            if self._counts_on_barrier:
+            counts_ready = self._counts_on_barrier and fresh
+            if counts_ready:
                 # the counts pass ran after the sweep and rode on the peer barrier
                 before, totals = self.level_before, self.level_totals
             else:
                 K.claim_prepare(mode, b, level, state.tail_start, ws, shard_base=base, free_bitmap=bm)
-            if self.sharded and not self._counts_on_barrier:
+            if self.sharded and not counts_ready:
                 dist = _dist()
                 dist.all_gather_into_tensor(self.gather_buf, ws.level_counts)
                 rank = st.shard_rank
@@ -599,14 +618,38 @@ class StepFn:
                            extra=self.extra_defaults, free_bitmap=bm, placed=self.placed)
             if self.use_mirror:
                 K.mirror_insert(self.mirrors[bk], cs, cd, cw, self.placed)
-            K.growth_flags(ws.counts, reset=bi == 0, grown=self.grown, overflow=self.overflow,
+            K.growth_flags(ws.counts, reset=fresh and bi == 0, grown=self.grown, overflow=self.overflow,
                            needs_resort=state.needs_resort)
             self.launches += 12
         state.grown, state.overflow = self.grown, self.overflow
-        if ac.on_overflow == "error" and bool(self.overflow.item()):
-            raise RuntimeError('add_conn overflow: selected candidates exceeded the free connection capacity '
-                               '(the rule declares on_overflow = "error").')
-        return GrowthRemainder(cs, cd, cw, self.claim_ws[0].overflowed)
+        if len(buckets) == 1:
+            dropped = self.claim_ws[buckets[0][0]].overflowed
+        else:
+            # each candidate belongs to one bucket: the buckets' flags OR
+            dropped = self.claim_ws[0].overflowed.clone()
+            for bk in range(1, len(buckets)):
+                dropped |= self.claim_ws[bk].overflowed
+        return GrowthRemainder(cs, cd, cw, dropped)
+
+    def retry(self, state: NetworkState, remainder: GrowthRemainder) -> tuple[NetworkState, GrowthRemainder]:
+        """Claim a remainder's dropped candidates into `state` (after a
+        regrow), in the list order, with the step's claim rule
+        (src/plastax/phases.py:5206-5290): grown adds the new edges to the
+        state's, overflow says whether candidates are still left; no other
+        phase runs and the step counter is untouched."""
+        if self.ac is None:
+            raise ValueError("growth retry: the network has no add_conn rule")
+        self._bind(state)
+        self._level = state.units[LEVEL.name]
+        self._counts_on_barrier = False
+        k = remainder.src.numel()
+        if k != self.k:
+            raise ValueError(f"growth retry: the remainder holds {k} candidates, the step's list {self.k}")
+        if state.grown is not None:
+            self.grown.copy_(state.grown)
+        grow = remainder.dropped.to(torch.uint8)
+        out = self._claim(state, remainder.src, remainder.dst, remainder.weight, grow, -1, fresh=False)
+        return state, out
 
     def _body(self, state: NetworkState, inputs: StepInputs) -> GrowthRemainder | None:
         """The device work of one step (no host synchronisation)."""
@@ -725,3 +768,10 @@ def make_step(net: type[Network], static: NetworkStatic, *, batch_size: int | No
     if fuse_prune is False:
         fn.fuse_prune = False
     return fn
+
+
+def make_growth_retry(net: type[Network], static: NetworkStatic, *, device: torch.device | str = "cuda"):
+    """The growth-only retry for a regrown static (src/plastax/step.py:320-356):
+    `(state, remainder) -> (state, still dropped)`."""
+    fn = StepFn(net, static, torch.device(device))
+    return fn.retry

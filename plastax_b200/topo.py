@@ -68,3 +68,61 @@ def capacity_policy(live: int, *, min_bucket: int = 64, headroom: float = 0.0, a
     if live <= 0:
         return min_bucket
     return max(1 << (target - 1).bit_length(), min_bucket)
+
+
+def resort(static, state):
+    """Recompute levels, redistribute the live edges into buckets and compact
+    each bucket (src/plastax/topo.py:303-452).
+
+    Levels come from the live edges (longest path; a TOPOLOGICAL cycle
+    raises). Each new bucket takes, in their old relative order, the live
+    edges whose source now sits at its level (PIPELINE: one bucket of every
+    live edge), stably ordered by source on the device (pxb_resort_order),
+    at capacity max(policy(live), old capacity); PIPELINE's tail_start
+    becomes the live count. Returns a new (static, state).
+    """
+    import dataclasses
+
+    import torch
+
+    from plastax_b200 import kernels as K
+    from plastax_b200.state import torch_dtype
+    from plastax_b200.types import LEVEL, Propagation
+
+    if static.num_shards > 1:
+        raise NotImplementedError("resort under Scheme-A has no engine lowering (it moves edges across bands)")
+    n = static.num_units
+    pipeline = static.propagation is Propagation.PIPELINE
+    flat = {s.name: torch.cat([b[s.name] for b in state.conns]) for s in static.conn_fields}
+    dev = flat["dead"].device
+    live = flat["dead"] == 0
+    lv_dev = initial_levels(n, flat["from_id"][live], flat["to_id"][live], allow_cycles=pipeline,
+                            input_ids=tuple(static.input_ids)).to(device=dev, dtype=torch.int32)
+    max_level = int(lv_dev.max().item()) if n else 0
+    if pipeline:
+        num_buckets = 1
+        in_bucket = [live]
+    else:
+        num_buckets = max(max_level + (1 if static.deepest_grows else 0), 1)
+        owner = lv_dev[flat["from_id"].clamp(0, n - 1).long()]
+        in_bucket = [live & (owner == b) for b in range(num_buckets)]
+    counts = [int(m.sum().item()) for m in in_bucket]
+    old_caps = static.level_capacities
+    caps = tuple(max(capacity_policy(c, headroom=static.capacity_headroom, align=static.capacity_align),
+                     old_caps[i] if i < len(old_caps) else 0) for i, c in enumerate(counts))
+    conns = []
+    for b, mask in enumerate(in_bucket):
+        idx = torch.nonzero(mask).flatten()
+        cols = {s.name: torch.full((caps[b],), s.default, dtype=torch_dtype(s), device=dev)
+                for s in static.conn_fields}
+        for s in static.conn_fields:
+            cols[s.name][: idx.numel()] = flat[s.name][idx]
+        perm = K.resort_order(cols, n).long()
+        conns.append({name: col[perm] for name, col in cols.items()})
+    units = dict(state.units)
+    units[LEVEL.name] = lv_dev
+    new_static = dataclasses.replace(static, level_capacities=caps, num_levels=max_level + 1)
+    tail = torch.tensor([counts[0] if pipeline else 0], dtype=torch.int64, device=dev)
+    new_state = dataclasses.replace(state, units=units, conns=tuple(conns),
+                                    needs_resort=torch.zeros((), dtype=torch.bool, device=dev), tail_start=tail)
+    return new_static, new_state
