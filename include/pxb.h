@@ -391,6 +391,59 @@ PXB_API int pxb_propose_per_conn(int64_t cap, const int32_t *from_id,
                                  float *score_out, void *scratch,
                                  size_t scratch_bytes, void *stream);
 
+/* ScoreAddConn's lowered pair scores and importances
+ * (src/plastax/traits.py:467-560; the rule's score(u, src, dst, g) and
+ * importance(u, i, g)):
+ *   ABS_PRODUCT  |x_src[src] * x_dst[dst]|   (importance: |x_src[i]|)
+ *   PRODUCT      x_src[src] * x_dst[dst]     (importance: x_src[i])
+ *   MODULAR      (((a*src + b*dst) mod m) - c) * scale, floor mod
+ *                (importance: (((a*i) mod m) - c) * scale)
+ *   MODULAR_PREDICATE  0 when ((a*src + b*dst) mod m) == c, else -inf
+ *                (the should_add predicate adapter)
+ * The modular forms are the versioned conformance rules of the reference's
+ * goldens (scripts/parity/golden_rules.py:57-77: grid_score_v1 =
+ * MODULAR(3, 5, 17, 8, 1/8), importance_v1 = MODULAR(7, -, 13, 0, 1/4),
+ * predicate_v1 = MODULAR_PREDICATE(1, 1, 2, 0)). */
+#define PXB_PAIR_ABS_PRODUCT 0
+#define PXB_PAIR_PRODUCT 1
+#define PXB_PAIR_MODULAR 2
+#define PXB_PAIR_MODULAR_PREDICATE 3
+
+typedef struct pxb_pair_score {
+  int32_t form;
+  const float *x_src, *x_dst; /* unit columns of the product forms */
+  int32_t a, b, m, c;
+  float scale;
+} pxb_pair_score;
+
+/* Per-unit importance (src/plastax/phases.py:3640-3665) under `form`, -inf
+ * for a pruned unit (the live mask of :4705-4712) and, with mask_kind 1,
+ * for a unit whose level is not `bucket` (the per-level shortlist's
+ * sources), with mask_kind 2 for one outside the bucket's destination
+ * window (level gap <= max_level_gap and the direction 0 any / 1 deeper /
+ * 2 same_or_deeper; src/plastax/phases.py:3704-3746). */
+PXB_API int pxb_unit_importance(int32_t num_units, const pxb_pair_score *form,
+                                const uint8_t *pruned, const int32_t *level,
+                                int32_t mask_kind, int32_t bucket,
+                                int32_t max_level_gap, int32_t direction,
+                                float *out, void *stream);
+
+/* ScoreAddConn candidates (src/plastax/phases.py:3668-3746, :4760-4860):
+ * `grids` grids of rows x cols, listed grid after grid, row-major inside;
+ * candidate (g, r, q): src = row_ids[g * rows + r] (r when row_ids is NULL:
+ * the exhaustive grid, index src * num_units + dst), dst = col_ids[g * cols
+ * + q] (q when NULL); its score from `score`, then the validity window of
+ * pxb_propose_per_unit (with per_grid_bucket, grid g admits only sources at
+ * level g: the per-level shortlist). grids * rows * cols < 2^31. */
+PXB_API int pxb_propose_grid(int32_t num_units, int32_t grids, int32_t rows,
+                             int32_t cols, const int32_t *row_ids,
+                             const int32_t *col_ids, int32_t per_grid_bucket,
+                             const pxb_pair_score *score, const int32_t *level,
+                             const uint8_t *pruned, int32_t max_level_gap,
+                             int32_t direction, int32_t allow_self_loops,
+                             int32_t src_level_bound, int32_t *src_out,
+                             int32_t *dst_out, float *score_out, void *stream);
+
 /* The per-source-level cap (level_cap_scope "source_level",
  * src/plastax/phases.py:4324-4487): over a level-major list idx of n
  * candidates (pxb_select_step with k = n), the first k of every level's

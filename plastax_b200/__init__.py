@@ -27,7 +27,9 @@ from plastax_b200.traits import (
     ProposeAddConn,
     PruneConn,
     ResetGlobal,
+    ScoreAddConn,
     SoftmaxCrossEntropyLoss,
+    predicate_add_conn,
 )
 from plastax_b200.types import (
     ACTIVATION,
@@ -46,6 +48,7 @@ __all__ = [
     "ACTIVATION", "DEAD", "FROM_ID", "GRAD_PRE_ACT", "LEVEL", "LOSS_GRAD", "PRUNED", "TO_ID", "WEIGHT",
     "BackwardPass", "DestinationThresholdPrune", "FieldSpec", "ForwardPass", "GrowthRemainder", "MSELoss",
     "MagnitudePrune", "MeanFloatFirstRest", "Network", "NetworkBuilder", "NetworkState", "NetworkStatic", "Propagation", "ProposeAddConn",
-    "PruneConn", "ResetGlobal", "ShardSpec", "SoftmaxCrossEntropyLoss", "StepFn", "StepInputs", "StepResult", "live_conn_count",
-    "grow_bucket", "make_empty_state", "make_growth_retry", "make_step", "monoid", "optim", "resort",
+    "PruneConn", "ResetGlobal", "ScoreAddConn", "ShardSpec", "SoftmaxCrossEntropyLoss", "StepFn", "StepInputs", "StepResult", "live_conn_count",
+    "grow_bucket", "make_empty_state", "make_growth_retry", "make_step", "monoid", "optim", "predicate_add_conn",
+    "resort",
 ]

@@ -38,6 +38,7 @@ LOSS_MSE, LOSS_SOFTMAX_CE = 0, 1
 MIRROR_TILE = 2048
 PEER_MAX_LEVELS = 8
 FIXED_FRAC_BITS = 28
+PAIR_ABS_PRODUCT, PAIR_PRODUCT, PAIR_MODULAR, PAIR_MODULAR_PREDICATE = 0, 1, 2, 3
 
 
 class Mirror(ctypes.Structure):
@@ -58,6 +59,15 @@ class PeerGroup(ctypes.Structure):
     _fields_ = [
         ("rank", c_i32), ("world", c_i32), ("acc_fixed", c_ptr), ("acc_side", c_ptr), ("act", c_ptr),
         ("flags", c_ptr), ("counts", c_ptr), ("epoch", c_ptr), ("done", c_ptr), ("status", c_ptr),
+    ]
+
+
+class PairScore(ctypes.Structure):
+    """`pxb_pair_score`: a ScoreAddConn rule's lowered score or importance."""
+
+    _fields_ = [
+        ("form", c_i32), ("x_src", c_ptr), ("x_dst", c_ptr), ("a", c_i32), ("b", c_i32), ("m", c_i32),
+        ("c", c_i32), ("scale", c_f32),
     ]
 
 
@@ -176,6 +186,9 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_batched_loss": (c_i32, [c_i32, c_i32, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_batch_mean": (c_i32, [c_i32, c_i32, c_ptr, c_ptr, c_ptr]),
     "pxb_count_dead": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr]),
+    "pxb_unit_importance": (c_i32, [c_i32, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr]),
+    "pxb_propose_grid": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_i32, c_i32,
+                                 c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_ptr]),
 }
 
 

@@ -43,6 +43,7 @@ class BatchedStepFn:
         self.inner.use_mirror = False  # rows move per edge; the mirror serves the streaming sweep
         self.inner.acc_fixed = None
         self.inner.peer_reduce = False
+        self.inner.ahead = False  # the structural phases run on the reduced state, in the step
         n, B = static.num_units, self.batch
         z = lambda: torch.zeros((n, B), dtype=torch.float32, device=device)  # noqa: E731
         self.act_b, self.acc_b = z(), z()

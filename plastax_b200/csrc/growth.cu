@@ -1372,3 +1372,141 @@ extern "C" int pxb_resort_order(int64_t cap, const uint8_t *dead, const int32_t 
                                            st));
   return PXB_OK;
 }
+
+// ---------------------------------------------------------------------------
+// ScoreAddConn candidates (src/plastax/phases.py:3640-3746, :4690-4790):
+// the exhaustive grid, the importance shortlist and the per-level shortlists,
+// each candidate scored by the rule's lowered pair score and passed through
+// the validity window.
+// ---------------------------------------------------------------------------
+namespace pxb {
+
+__device__ __forceinline__ int64_t floor_mod(int64_t x, int64_t m) {
+  const int64_t r = x % m;
+  return r < 0 ? r + m : r;
+}
+
+__device__ __forceinline__ float pair_score(const pxb_pair_score &f, int32_t src, int32_t dst) {
+  switch (f.form) {
+    case PXB_PAIR_ABS_PRODUCT:
+      return fabsf(__fmul_rn(f.x_src[src], f.x_dst[dst]));
+    case PXB_PAIR_PRODUCT:
+      return __fmul_rn(f.x_src[src], f.x_dst[dst]);
+    case PXB_PAIR_MODULAR: {
+      const int64_t r = floor_mod(int64_t(f.a) * src + int64_t(f.b) * dst, f.m);
+      return __fmul_rn(static_cast<float>(r - f.c), f.scale);
+    }
+    default: {  // PXB_PAIR_MODULAR_PREDICATE
+      const int64_t r = floor_mod(int64_t(f.a) * src + int64_t(f.b) * dst, f.m);
+      return r == f.c ? 0.0f : -__int_as_float(0x7f800000);
+    }
+  }
+}
+
+// Importance of unit i under the rule's lowered form; -inf for a pruned unit
+// or one outside the mask (the per-level shortlist's source level or the
+// level's destination window).
+__global__ void unit_importance_kernel(int32_t n, pxb_pair_score f, const uint8_t *__restrict__ pruned,
+                                       const int32_t *__restrict__ level, int32_t mask_kind, int32_t bucket,
+                                       int32_t max_level_gap, int32_t direction, float *__restrict__ out) {
+  for (int32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    float v;
+    if (f.form == PXB_PAIR_ABS_PRODUCT) v = fabsf(f.x_src[i]);
+    else if (f.form == PXB_PAIR_PRODUCT) v = f.x_src[i];
+    else v = __fmul_rn(static_cast<float>(floor_mod(int64_t(f.a) * i, f.m) - f.c), f.scale);
+    bool keep = pruned == nullptr || !pruned[i];
+    if (mask_kind == 1) {
+      keep = keep && level[i] == bucket;
+    } else if (mask_kind == 2) {
+      const int32_t ld = level[i], gap = ld > bucket ? ld - bucket : bucket - ld;
+      keep = keep && gap <= max_level_gap;
+      if (direction == 1) keep = keep && ld > bucket;
+      else if (direction == 2) keep = keep && ld >= bucket;
+    }
+    out[i] = keep ? v : -__int_as_float(0x7f800000);
+  }
+}
+
+// Candidate c of `grids` grids of rows x cols: grid g, row r, column q
+// (row-major inside a grid, grids in order); src = row_ids[g * rows + r]
+// (r itself without row_ids), dst likewise from col_ids.
+__global__ void propose_grid_kernel(ProposeArgs a, int32_t grids, int32_t rows, int32_t cols,
+                                    const int32_t *__restrict__ row_ids, const int32_t *__restrict__ col_ids,
+                                    int32_t per_grid_bucket, pxb_pair_score f, int32_t *__restrict__ src_out,
+                                    int32_t *__restrict__ dst_out, float *__restrict__ score_out) {
+  const int64_t per = static_cast<int64_t>(rows) * cols, total = per * grids;
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < total;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t g = static_cast<int32_t>(c / per);
+    const int64_t rc = c - static_cast<int64_t>(g) * per;
+    const int32_t r = static_cast<int32_t>(rc / cols), q = static_cast<int32_t>(rc - static_cast<int64_t>(r) * cols);
+    int32_t src = row_ids ? row_ids[static_cast<int64_t>(g) * rows + r] : r;
+    int32_t dst = col_ids ? col_ids[static_cast<int64_t>(g) * cols + q] : q;
+    const bool in = src >= 0 && src < a.num_units && dst >= 0 && dst < a.num_units;
+    float score = in ? pair_score(f, src, dst) : 0.0f;
+    ProposeArgs ag = a;
+    if (per_grid_bucket) ag.bucket_level = g;
+    apply_window(ag, src, dst, score, true);
+    src_out[c] = src;
+    dst_out[c] = dst;
+    score_out[c] = score;
+  }
+}
+
+static bool pair_score_ok(const pxb_pair_score *f, bool two_columns) {
+  if (f == nullptr) return false;
+  switch (f->form) {
+    case PXB_PAIR_ABS_PRODUCT:
+    case PXB_PAIR_PRODUCT:
+      return f->x_src != nullptr && (!two_columns || f->x_dst != nullptr);
+    case PXB_PAIR_MODULAR:
+    case PXB_PAIR_MODULAR_PREDICATE:
+      return f->m >= 1;
+    default:
+      return false;
+  }
+}
+
+}  // namespace pxb
+
+using namespace pxb;
+
+extern "C" int pxb_unit_importance(int32_t num_units, const pxb_pair_score *form, const uint8_t *pruned,
+                                   const int32_t *level, int32_t mask_kind, int32_t bucket, int32_t max_level_gap,
+                                   int32_t direction, float *out, void *stream) {
+  PXB_REQUIRE(num_units >= 0, "pxb_unit_importance: negative num_units");
+  PXB_REQUIRE(pair_score_ok(form, false) && form->form != PXB_PAIR_MODULAR_PREDICATE,
+              "pxb_unit_importance: unknown or incomplete importance form");
+  PXB_REQUIRE(mask_kind >= 0 && mask_kind <= 2 && (mask_kind == 0 || level != nullptr),
+              "pxb_unit_importance: mask kind %d needs the level column", mask_kind);
+  PXB_REQUIRE(direction >= 0 && direction <= 2, "pxb_unit_importance: unknown direction %d", direction);
+  if (num_units == 0) return PXB_OK;
+  PXB_REQUIRE(out != nullptr, "pxb_unit_importance: out is NULL");
+  unit_importance_kernel<<<grid_for(num_units, 256, 4), 256, 0, as_stream(stream)>>>(
+      num_units, *form, pruned, level, mask_kind, bucket, max_level_gap, direction, out);
+  PXB_LAUNCHED("unit_importance_kernel");
+  return PXB_OK;
+}
+
+extern "C" int pxb_propose_grid(int32_t num_units, int32_t grids, int32_t rows, int32_t cols, const int32_t *row_ids,
+                                const int32_t *col_ids, int32_t per_grid_bucket, const pxb_pair_score *score,
+                                const int32_t *level, const uint8_t *pruned, int32_t max_level_gap, int32_t direction,
+                                int32_t allow_self_loops, int32_t src_level_bound, int32_t *src_out, int32_t *dst_out,
+                                float *score_out, void *stream) {
+  PXB_REQUIRE(num_units >= 1 && grids >= 0 && rows >= 0 && cols >= 0, "pxb_propose_grid: bad sizes");
+  const int64_t total = int64_t(grids) * rows * cols;
+  PXB_REQUIRE(total < (int64_t(1) << 31), "pxb_propose_grid: %lld candidates exceed the int32 candidate index",
+              static_cast<long long>(total));
+  PXB_REQUIRE(pair_score_ok(score, true), "pxb_propose_grid: unknown or incomplete score form");
+  PXB_REQUIRE(direction >= 0 && direction <= 2, "pxb_propose_grid: unknown direction %d", direction);
+  if (total == 0) return PXB_OK;
+  PXB_REQUIRE(level && src_out && dst_out && score_out, "pxb_propose_grid: a pointer is NULL");
+  PXB_REQUIRE((row_ids != nullptr || rows <= num_units) && (col_ids != nullptr || cols <= num_units),
+              "pxb_propose_grid: an identity axis longer than the units");
+  ProposeArgs a{num_units, 1, 0, 0, nullptr, 0, num_units, PXB_SCORE_UNIFORM, nullptr, nullptr, level,
+                pruned, max_level_gap, direction, allow_self_loops, -1, src_level_bound};
+  propose_grid_kernel<<<grid_for(total, 256, 8), 256, 0, as_stream(stream)>>>(
+      a, grids, rows, cols, row_ids, col_ids, per_grid_bucket, *score, src_out, dst_out, score_out);
+  PXB_LAUNCHED("propose_grid_kernel");
+  return PXB_OK;
+}

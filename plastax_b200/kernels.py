@@ -275,6 +275,42 @@ def propose_global(proposals: int, network_seed: int, step: int, num_units: int,
     return src, dst, score
 
 
+def pair_score(form: int, *, x_src: torch.Tensor | None = None, x_dst: torch.Tensor | None = None, a: int = 0,
+               b: int = 0, m: int = 1, c: int = 0, scale: float = 1.0) -> _lib.PairScore:
+    """A `pxb_pair_score` (the caller keeps x_src / x_dst alive)."""
+    return _lib.PairScore(form, ptr(x_src), ptr(x_dst), a, b, m, c, scale)
+
+
+def unit_importance(num_units: int, form: _lib.PairScore, *, pruned: torch.Tensor | None = None,
+                    level: torch.Tensor | None = None, mask_kind: int = 0, bucket: int = 0, max_level_gap: int = 1,
+                    direction: int = 0, out: torch.Tensor | None = None, device=None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(num_units, dtype=torch.float32, device=device if device is not None else level.device)
+    call("pxb_unit_importance", ctypes.c_int32(num_units), ctypes.byref(form), ptr(pruned), ptr(level),
+         ctypes.c_int32(mask_kind), ctypes.c_int32(bucket), ctypes.c_int32(max_level_gap), ctypes.c_int32(direction),
+         ptr(out), _stream())
+    return out
+
+
+def propose_grid(num_units: int, grids: int, rows: int, cols: int, score: _lib.PairScore, *, level: torch.Tensor,
+                 row_ids: torch.Tensor | None = None, col_ids: torch.Tensor | None = None,
+                 per_grid_bucket: bool = False, pruned: torch.Tensor | None = None, max_level_gap: int = 1,
+                 direction: int = 0, allow_self_loops: bool = False, src_level_bound: int = 0,
+                 out: tuple | None = None) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    n = grids * rows * cols
+    dev = level.device
+    if out is None:
+        out = (torch.empty(n, dtype=torch.int32, device=dev), torch.empty(n, dtype=torch.int32, device=dev),
+               torch.empty(n, dtype=torch.float32, device=dev))
+    src, dst, sc = out
+    call("pxb_propose_grid", ctypes.c_int32(num_units), ctypes.c_int32(grids), ctypes.c_int32(rows),
+         ctypes.c_int32(cols), ptr(row_ids), ptr(col_ids), ctypes.c_int32(1 if per_grid_bucket else 0),
+         ctypes.byref(score), ptr(level), ptr(pruned), ctypes.c_int32(max_level_gap), ctypes.c_int32(direction),
+         ctypes.c_int32(1 if allow_self_loops else 0), ctypes.c_int32(src_level_bound), ptr(src), ptr(dst), ptr(sc),
+         _stream())
+    return src, dst, sc
+
+
 def conn_rank_scratch(cap: int, num_units: int) -> int:
     return query_size("pxb_conn_rank_scratch_bytes", ctypes.c_int64(cap), ctypes.c_int32(num_units))
 

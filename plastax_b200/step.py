@@ -43,6 +43,7 @@ from plastax_b200.traits import (
     MSELoss,
     Network,
     ProposeAddConn,
+    ScoreAddConn,
     SoftmaxCrossEntropyLoss,
 )
 from plastax_b200.types import ACTIVATION, LEVEL, PRUNED, Propagation
@@ -112,7 +113,8 @@ class StepFn:
         self.fuse_update = (not self.pipeline and net.update_conn is not None and net.backward_pass is not None
                             and net.update_unit is None)
         self.opt = net.update_conn.struct() if net.update_conn is not None else None
-        self.ac: ProposeAddConn | None = net.add_conn
+        self.ac: ProposeAddConn | ScoreAddConn | None = net.add_conn
+        self.is_score = isinstance(self.ac, ScoreAddConn)
         # The forward reads a destination-grouped mirror of each bucket when
         # no phase rewrites weights in place (the mirror holds its own copy)
         # and any prune rides on the forward sweep.
@@ -147,10 +149,18 @@ class StepFn:
             self._build_growth()
             # proposals scored by the site RNG alone depend on the levels and
             # the step counter only, never on this step's propagation, prune
-            # or update: their selection may overlap the forward sweep
-            if (self.ac.score in ("uniform", "uniform_q256") and not self.ac.dedupe_live
-                    and torch.device(device).type == "cuda"):
+            # or update: their selection may overlap the forward sweep (not
+            # per-connection proposals, which come from the post-prune arena)
+            if (not self.is_score and self.ac.score in ("uniform", "uniform_q256") and not self.ac.dedupe_live
+                    and self.ac.proposer != "per_connection" and torch.device(device).type == "cuda"):
                 self.side = torch.cuda.Stream(device=device)
+        # ... and, when growth fires every step, the next step's selection
+        # runs a whole step ahead, beside this step's passes and claim
+        self.ahead = self.side is not None and self.capturable() and self.ac is not None and self.k > 0
+        self._ahead_ready = False
+        if self.ahead:
+            self.claim_next = tuple(torch.empty_like(t) for t in self.claim_in)
+            self.sel_step_dev = torch.zeros(1, dtype=torch.int32, device=device)
         self.launches = 0
 
     # -- per-state device indices ---------------------------------------------
@@ -181,6 +191,7 @@ class StepFn:
             self.bitmaps = [K.free_bitmap_build(mode, b, level, state.tail_start, self.num_levels,
                                                 shard_base=st.shard_base(i)) for i, b in enumerate(state.conns)]
         self.step_dev.fill_(state.step)
+        self._ahead_ready = False
         self._bound = id(state)
 
     def invalidate(self) -> None:
@@ -197,12 +208,102 @@ class StepFn:
             return None, None
         return self.bitmaps[bucket], None if not self.pipeline else self._level
 
+    # -- ScoreAddConn candidates ----------------------------------------------
+    def _build_score_candidates(self) -> None:
+        """The grid a ScoreAddConn draws (src/plastax/phases.py:4655-4690):
+        a shortlist of M units when 0 < M < num_units (per source level for
+        shortlist_per_level), else every ordered pair."""
+        ac, st, dev = self.ac, self.static, self.dev
+        n = st.num_units
+        M = ac.shortlist_size
+        self.use_shortlist = ac.candidates in ("shortlist", "shortlist_per_level") and M is not None and 0 < M < n
+        self.use_per_level = self.use_shortlist and ac.candidates == "shortlist_per_level"
+        side = int(M) if self.use_shortlist else n
+        self.grids = self.num_buckets if self.use_per_level else 1
+        self.pool_side = side
+        self.n_cand = self.grids * side * side
+        if self.n_cand >= 1 << 31:
+            raise NotImplementedError(f"ScoreAddConn: {self.grids} x {side}^2 candidates exceed the int32 candidate "
+                                      f"index (declare a shortlist)")
+        if self.use_shortlist:
+            self.unit_ids = torch.arange(n, dtype=torch.int32, device=dev)
+            self.imp = torch.empty(n, dtype=torch.float32, device=dev)
+            self.rows = torch.empty(self.grids * side, dtype=torch.int32, device=dev)
+            self.cols = torch.empty(self.grids * side, dtype=torch.int32, device=dev) if self.use_per_level else None
+            need = K.topk_unique_scratch(n, side, n)
+            self.imp_scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+
+    @staticmethod
+    def _field(units: dict, f) -> torch.Tensor:
+        name = f if isinstance(f, str) else f.name
+        if name not in units:
+            raise ValueError(f"ScoreAddConn: the state has no unit field {name!r}")
+        return units[name]
+
+    def _score_form(self, units: dict):
+        form = self.ac.score
+        kind = form[0]
+        if kind == "grad_act":
+            return K.pair_score(_lib.PAIR_ABS_PRODUCT, x_src=units[ACTIVATION.name],
+                                x_dst=self._field(units, self.ac.grad_field))
+        if kind in ("abs_product", "product"):
+            return K.pair_score(_lib.PAIR_ABS_PRODUCT if kind == "abs_product" else _lib.PAIR_PRODUCT,
+                                x_src=self._field(units, form[1]), x_dst=self._field(units, form[2]))
+        if kind == "modular":
+            return K.pair_score(_lib.PAIR_MODULAR, a=int(form[1]), b=int(form[2]), m=int(form[3]), c=int(form[4]),
+                                scale=float(form[5]))
+        return K.pair_score(_lib.PAIR_MODULAR_PREDICATE, a=int(form[1]), b=int(form[2]), m=int(form[3]),
+                            c=int(form[4]))
+
+    def _importance_form(self, units: dict):
+        form = self.ac.importance
+        if form[0] == "abs_field":
+            return K.pair_score(_lib.PAIR_ABS_PRODUCT, x_src=self._field(units, form[1]))
+        if form[0] == "field":
+            return K.pair_score(_lib.PAIR_PRODUCT, x_src=self._field(units, form[1]))
+        return K.pair_score(_lib.PAIR_MODULAR, a=int(form[1]), m=int(form[2]), c=int(form[3]), scale=float(form[4]))
+
+    def _score_candidates(self, state: NetworkState, window: dict) -> None:
+        """The step's scored grid into the candidate columns: importance
+        ranked on the device (ties by ascending id, the first M of the
+        (-importance, id) order), then one pass that scores and windows every
+        (row, column) pair (src/plastax/phases.py:3668-3746, :4760-4860)."""
+        ac, units = self.ac, state.units
+        n = self.static.num_units
+        score = self._score_form(units)
+        grid = dict(level=window["level"], pruned=window["pruned"], max_level_gap=ac.max_level_gap,
+                    direction=self.direction, allow_self_loops=ac.allow_self_loops,
+                    src_level_bound=window["src_level_bound"], out=self.cand)
+        if not self.use_shortlist:
+            K.propose_grid(n, 1, n, n, score, **grid)
+            self.launches += 1
+            return
+        imp = self._importance_form(units)
+        M, pruned, level = self.pool_side, window["pruned"], window["level"]
+        if not self.use_per_level:
+            K.unit_importance(n, imp, pruned=pruned, level=level, out=self.imp)
+            K.topk_unique(self.imp, self.unit_ids, n, M, out=self.rows, scratch=self.imp_scratch)
+            K.propose_grid(n, 1, M, M, score, row_ids=self.rows, col_ids=self.rows, **grid)
+            self.launches += 4
+            return
+        for b in range(self.grids):
+            K.unit_importance(n, imp, pruned=pruned, level=level, mask_kind=1, bucket=b, out=self.imp)
+            K.topk_unique(self.imp, self.unit_ids, n, M, out=self.rows[b * M:(b + 1) * M], scratch=self.imp_scratch)
+            K.unit_importance(n, imp, pruned=pruned, level=level, mask_kind=2, bucket=b,
+                              max_level_gap=ac.max_level_gap, direction=self.direction, out=self.imp)
+            K.topk_unique(self.imp, self.unit_ids, n, M, out=self.cols[b * M:(b + 1) * M], scratch=self.imp_scratch)
+        K.propose_grid(n, self.grids, M, M, score, row_ids=self.rows, col_ids=self.cols, per_grid_bucket=True,
+                       **grid)
+        self.launches += 1 + 6 * self.grids
+
     # -- growth buffers ------------------------------------------------------
     def _build_growth(self) -> None:
         ac, st, dev = self.ac, self.static, self.dev
         n = st.num_units
-        P = ac.proposals_per_proposer
-        if ac.proposer == "per_unit":
+        P = getattr(ac, "proposals_per_proposer", 0)
+        if self.is_score:
+            self._build_score_candidates()
+        elif ac.proposer == "per_unit":
             self.n_cand = n * P
         elif ac.proposer == "global":
             self.n_cand = P
@@ -214,9 +315,11 @@ class StepFn:
             self.n_cand = self.conn_slots * P
             self.conn_scratch = torch.empty(max(K.conn_rank_scratch(self.conn_slots, n), 1), dtype=torch.uint8,
                                             device=dev)
-        src_n = ac.src_n if ac.src_n is not None else n - ac.src_lo
-        if ac.proposer == "global" and (ac.src_lo < 0 or src_n < 1 or ac.src_lo + src_n > n):
-            raise ValueError(f"ProposeAddConn: sources [{ac.src_lo}, {ac.src_lo + src_n}) exceed the {n} units")
+        src_lo, dst_lo = getattr(ac, "src_lo", 0), getattr(ac, "dst_lo", 0)
+        src_n = getattr(ac, "src_n", None)
+        src_n = src_n if src_n is not None else n - src_lo
+        if getattr(ac, "proposer", "") == "global" and (src_lo < 0 or src_n < 1 or src_lo + src_n > n):
+            raise ValueError(f"ProposeAddConn: sources [{src_lo}, {src_lo + src_n}) exceed the {n} units")
         self.src_n = src_n
         # the cap: per source level (the default) or once per step; "all"
         # keeps every finite candidate
@@ -227,13 +330,14 @@ class StepFn:
         self.cand = (torch.empty(self.n_cand, dtype=torch.int32, device=dev),
                      torch.empty(self.n_cand, dtype=torch.int32, device=dev),
                      torch.empty(self.n_cand, dtype=torch.float32, device=dev))
-        dst_n = ac.dst_n if ac.dst_n is not None else n - ac.dst_lo
-        if ac.dst_lo < 0 or dst_n < 1 or ac.dst_lo + dst_n > n:
-            raise ValueError(f"ProposeAddConn: destinations [{ac.dst_lo}, {ac.dst_lo + dst_n}) exceed the {n} units")
+        dst_n = getattr(ac, "dst_n", None)
+        dst_n = dst_n if dst_n is not None else n - dst_lo
+        if dst_lo < 0 or dst_n < 1 or dst_lo + dst_n > n:
+            raise ValueError(f"ProposeAddConn: destinations [{dst_lo}, {dst_lo + dst_n}) exceed the {n} units")
         # One proposal per unit: every candidate's source is its own unit, so
         # (score, src) is a unique key in the total order and a radix select
         # of the first k replaces the full sort.
-        self.unique_src = P == 1 and ac.proposer == "per_unit" and not self.per_level
+        self.unique_src = P == 1 and getattr(ac, "proposer", "") == "per_unit" and not self.per_level
         self.perm = torch.empty(self.n_cand if not self.unique_src else max(self.k, 1), dtype=torch.int32, device=dev)
         need = K.topk_unique_scratch(self.n_cand, self.k, n) if self.unique_src else K.total_order_scratch(self.n_cand, n)
         self.order_scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
@@ -262,13 +366,14 @@ class StepFn:
         self.init_kind = {"const": _lib.INIT_CONST, "dyadic": _lib.INIT_DYADIC,
                           "hash_uniform": _lib.INIT_HASH_UNIFORM}[ac.init[0]]
         self.init_a = float(ac.init[1]) if len(ac.init) > 1 else 0.0
-        self.score_kind = {"uniform": _lib.SCORE_UNIFORM, "uniform_q256": _lib.SCORE_UNIFORM_Q256,
-                           "grad_act": _lib.SCORE_GRAD_ACT}[ac.score]
+        self.score_kind = -1 if self.is_score else {"uniform": _lib.SCORE_UNIFORM,
+                                                    "uniform_q256": _lib.SCORE_UNIFORM_Q256,
+                                                    "grad_act": _lib.SCORE_GRAD_ACT}[ac.score]
         self.direction = {"any": 0, "deeper": 1, "same_or_deeper": 2}[ac.direction]
         # one proposal per unit scored by the site RNG: the fused selection
         # (keys binned and ranked, no sort pass) replaces propose + top-k +
         # level listing + gather
-        self.fast_select = (self.unique_src and ac.score in ("uniform", "uniform_q256")
+        self.fast_select = (self.unique_src and not self.is_score and ac.score in ("uniform", "uniform_q256")
                             and ac.level_cap_scope == "step" and ac.selection == "top_k"
                             and self.static.num_levels <= 8 and self.k > 0
                             and not ac.dedupe_live and not ac.dedupe_step)
@@ -477,14 +582,22 @@ class StepFn:
             raise NotImplementedError(f"growth trigger {trig!r} has no engine lowering")
         return fire
 
-    def _select(self, state: NetworkState) -> None:
+    def _select(self, state: NetworkState, out: tuple | None = None, step_dev: torch.Tensor | None = None) -> None:
         """Growth selection: proposals, the first k in the total order and
         the level-major winner list (src/plastax/phases.py:3813-3860,
-        :4208-4487, :5043-5058), gathered into the claim's input columns."""
+        :4208-4487, :5043-5058), gathered into the claim's input columns
+        (`out`, default the claim's own), for the step `step_dev` holds."""
+        out = self.claim_in if out is None else out
+        step_dev = self.step_dev if step_dev is None else step_dev
         ac, st, units = self.ac, self.static, state.units
         n = st.num_units
         level = units[LEVEL.name]
         pruned = units.get(PRUNED.name)
+        if self.is_score:
+            self._score_candidates(state, dict(level=level, pruned=pruned,
+                                               src_level_bound=0 if self.pipeline else self.num_buckets))
+            self._select_candidates(state, out)
+            return
         dst_n = ac.dst_n if ac.dst_n is not None else n - ac.dst_lo
         grad = units.get(ac.grad_field.name) if ac.score == "grad_act" else None
         if self.fast_select:
@@ -493,14 +606,14 @@ class StepFn:
                                     init_a=self.init_a, pruned=pruned, max_level_gap=ac.max_level_gap,
                                     direction=self.direction, allow_self_loops=ac.allow_self_loops,
                                     src_level_bound=0 if self.pipeline else self.num_buckets,
-                                    step_dev=self.step_dev, status=self.fs_status, scratch=self.fs_scratch,
-                                    out=self.claim_in)
+                                    step_dev=step_dev, status=self.fs_status, scratch=self.fs_scratch,
+                                    out=out)
             self.launches += 6
             return
         window = dict(level=level, grad=grad, act=units[ACTIVATION.name], pruned=pruned,
                       max_level_gap=ac.max_level_gap, direction=self.direction,
                       allow_self_loops=ac.allow_self_loops,
-                      src_level_bound=0 if self.pipeline else self.num_buckets, step_dev=self.step_dev)
+                      src_level_bound=0 if self.pipeline else self.num_buckets, step_dev=step_dev)
         if ac.proposer == "per_unit":
             K.propose_per_unit(n, ac.proposals_per_proposer, st.seed, state.step, dst_lo=ac.dst_lo, dst_n=dst_n,
                                score_kind=self.score_kind, out=self.cand, **window)
@@ -514,6 +627,14 @@ class StepFn:
             K.propose_per_conn(arena, ac.proposals_per_proposer, st.seed, state.step, n, dst_lo=ac.dst_lo,
                                dst_n=dst_n, score_kind=self.score_kind, scratch=self.conn_scratch, out=self.cand,
                                **window)
+        self._select_candidates(state, out)
+
+    def _select_candidates(self, state: NetworkState, out: tuple) -> None:
+        """The candidate list's threshold veto, dedupes, total order, caps and
+        level-major winner list, gathered into `out`."""
+        ac = self.ac
+        n = self.static.num_units
+        level = state.units[LEVEL.name]
         if ac.selection == "threshold":
             # below the threshold is a veto (src/plastax/phases.py:4324-4487)
             sc = self.cand[2]
@@ -544,7 +665,7 @@ class StepFn:
                           num_levels=self.static.num_levels)
         kk = min(self.k, self.n_cand)
         K.gather_winners(self.win, kk, self.k, src, dst, score, init_kind=self.init_kind, init_a=self.init_a,
-                         out=self.claim_in)
+                         out=out)
         self.launches += 4 + 5
 
     def _add_conn(self, state: NetworkState, selected: bool = False) -> GrowthRemainder | None:
@@ -654,6 +775,8 @@ class StepFn:
     def _body(self, state: NetworkState, inputs: StepInputs) -> GrowthRemainder | None:
         """The device work of one step (no host synchronisation)."""
         self._level = state.units[LEVEL.name]
+        if self.ahead:
+            return self._body_ahead(state, inputs)
         # selection that reads nothing the step writes runs on the side
         # stream, concurrently with the propagation passes
         early = self.side is not None and self._fires(state) and self.k > 0
@@ -671,6 +794,32 @@ class StepFn:
             torch.cuda.current_stream(self.dev).wait_stream(self.side)
         remainder = self._add_conn(state, selected=early)
         self.step_dev += 1
+        return remainder
+
+    def _body_ahead(self, state: NetworkState, inputs: StepInputs) -> GrowthRemainder | None:
+        """The step with its selection computed one step earlier: this step's
+        winners come from the buffer the previous step's side branch filled,
+        and the side stream selects the next step's while the passes, the
+        claim and the insert run (it joins at the end of the step)."""
+        main = torch.cuda.current_stream(self.dev)
+        if not self._ahead_ready:  # the first step of a bound state selects its own
+            self._select(state, out=self.claim_next, step_dev=self.step_dev)
+            self._ahead_ready = True
+        for dst_t, src_t in zip(self.claim_in, self.claim_next, strict=True):
+            dst_t.copy_(src_t)
+        torch.add(self.step_dev, 1, out=self.sel_step_dev)
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            self._select(state, out=self.claim_next, step_dev=self.sel_step_dev)
+        self._scatter_inputs(state, inputs)
+        self._forward(state)
+        self._loss(state, inputs)
+        self._backward(state)
+        self._update_conn(state)
+        self._prune(state)
+        remainder = self._add_conn(state, selected=True)
+        self.step_dev += 1
+        main.wait_stream(self.side)
         return remainder
 
     def capturable(self) -> bool:

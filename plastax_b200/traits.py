@@ -30,6 +30,11 @@ Recognised forms:
   init weight constant / dyadic / hashed uniform; dedupe_live (a candidate
   equal to a live edge is vetoed) and dedupe_step (a pair's copies after the
   first in score order are vetoed).
+- ScoreAddConn: the exhaustive grid, the importance shortlist or the
+  per-level shortlists, scored by a lowered pair score (|x[src]*y[dst]|,
+  x[src]*y[dst], |grad[dst]*act[src]|, the modular conformance rules) with
+  the same selection, caps, dedupes and init as ProposeAddConn;
+  predicate_add_conn for a boolean rule.
 """
 
 from __future__ import annotations
@@ -177,6 +182,112 @@ class ProposeAddConn:
             raise ValueError(f"unknown on_overflow {self.on_overflow!r}")
 
 
+_SCORE_FORMS = {"abs_product": 3, "product": 3, "grad_act": 1, "modular": 6, "modular_predicate": 5}
+_IMPORTANCE_FORMS = {"abs_field": 2, "field": 2, "modular": 5}
+
+
+@dataclasses.dataclass
+class ScoreAddConn:
+    """Scored-candidate growth (src/plastax/traits.py:467-575) in its
+    recognised form.
+
+    `candidates`: "exhaustive" (every ordered unit pair, index src * N +
+    dst), "shortlist" (the M x M grid over the top-M units by importance,
+    ties by ascending id; M = shortlist_size) or "shortlist_per_level"
+    (TOPOLOGICAL only: per source level, its top-M sources x the top-M
+    destinations inside its window). A shortlist with M >= num_units is the
+    exhaustive grid, as in the reference.
+
+    `score` (the rule's score(u, src, dst, g)), one of
+    ("abs_product", src_field, dst_field): |u[src_field][src] * u[dst_field][dst]|;
+    ("product", src_field, dst_field): u[src_field][src] * u[dst_field][dst];
+    ("grad_act",): |grad_field[dst] * activation[src]|;
+    ("modular", a, b, m, c, scale): (((a*src + b*dst) mod m) - c) * scale;
+    ("modular_predicate", a, b, m, r): 0 if (a*src + b*dst) mod m == r else -inf.
+    `importance` (importance(u, i, g)): ("abs_field", field), ("field",
+    field) or ("modular", a, m, c, scale) = (((a*i) mod m) - c) * scale.
+    A non-finite score vetoes the candidate. The modular forms are the
+    reference's versioned conformance rules (scripts/parity/golden_rules.py:
+    grid_score_v1 = ("modular", 3, 5, 17, 8, 0.125), importance_v1 =
+    ("modular", 7, 13, 0, 0.25), predicate_v1 = ("modular_predicate", 1, 1, 2, 0)).
+    """
+
+    score: tuple
+    max_new_per_level: int | None = None
+    candidates: str = "exhaustive"
+    shortlist_size: int | None = None
+    importance: tuple | None = None
+    init: tuple = ("const", 0.0)
+    selection: str = "top_k"
+    threshold: float | None = None
+    level_cap_scope: str = "source_level"
+    max_new_per_step: int | None = None
+    max_level_gap: int = 1
+    direction: str = "any"
+    allow_self_loops: bool = False
+    dedupe_live: bool = False
+    dedupe_step: bool = False
+    trigger: Any = "every_step"
+    on_overflow: str = "flag"
+    grad_field: FieldSpec = GRAD_PRE_ACT
+
+    def validate(self) -> None:
+        """The reference's knob checks (src/plastax/traits.py:1390-1520),
+        TypeError as there, plus the lowered forms' own."""
+        if self.candidates not in ("exhaustive", "shortlist", "shortlist_per_level"):
+            raise TypeError(f"add_conn.candidates must be exhaustive / shortlist / shortlist_per_level; got "
+                            f"{self.candidates!r}")
+        if self.candidates != "exhaustive":
+            size = self.shortlist_size
+            if not isinstance(size, int) or isinstance(size, bool) or size < 1:
+                raise TypeError(f"add_conn.shortlist_size must be an int >= 1 for candidates = "
+                                f"{self.candidates!r}; got {size!r}")
+            if self.importance is None:
+                raise TypeError(f"add_conn: candidates = {self.candidates!r} requires an importance form")
+        if self.selection not in ("top_k", "threshold", "all"):
+            raise TypeError(f"add_conn.selection must be top_k / threshold / all; got {self.selection!r}")
+        mnpl = self.max_new_per_level
+        if self.selection != "all" or mnpl is not None:
+            if not isinstance(mnpl, int) or isinstance(mnpl, bool) or mnpl < 1:
+                raise TypeError(f"add_conn.max_new_per_level must be an int >= 1 (required unless selection = "
+                                f"'all'); got {mnpl!r}")
+        if self.selection == "threshold" and self.threshold is None:
+            raise TypeError("add_conn: selection = 'threshold' requires a threshold")
+        if self.level_cap_scope not in ("source_level", "step"):
+            raise TypeError(f"add_conn.level_cap_scope must be source_level / step; got {self.level_cap_scope!r}")
+        mnps = self.max_new_per_step
+        if mnps is not None and (not isinstance(mnps, int) or isinstance(mnps, bool) or mnps < 1):
+            raise TypeError(f"add_conn.max_new_per_step must be an int >= 1 or None; got {mnps!r}")
+        if self.direction not in ("any", "deeper", "same_or_deeper"):
+            raise TypeError(f"add_conn.direction must be any / deeper / same_or_deeper; got {self.direction!r}")
+        if self.on_overflow not in ("flag", "error"):
+            raise TypeError(f"add_conn.on_overflow must be 'flag' or 'error'; got {self.on_overflow!r}")
+        for flag in ("dedupe_live", "dedupe_step", "allow_self_loops"):
+            if not isinstance(getattr(self, flag), bool):
+                raise TypeError(f"add_conn.{flag} must be a bool")
+        form = self.score
+        if not isinstance(form, tuple) or not form or form[0] not in _SCORE_FORMS \
+                or len(form) != _SCORE_FORMS[form[0]]:
+            raise NotImplementedError(f"add_conn.score form {form!r} has no engine lowering")
+        if self.importance is not None:
+            imp = self.importance
+            if not isinstance(imp, tuple) or not imp or imp[0] not in _IMPORTANCE_FORMS \
+                    or len(imp) != _IMPORTANCE_FORMS[imp[0]]:
+                raise NotImplementedError(f"add_conn.importance form {imp!r} has no engine lowering")
+        if self.init[0] not in ("const", "dyadic", "hash_uniform"):
+            raise NotImplementedError(f"add_conn.init rule {self.init!r} has no engine lowering")
+
+
+def predicate_add_conn(should_add: tuple, init: tuple = ("const", 0.0), **params: Any) -> ScoreAddConn:
+    """A boolean growth predicate as a ScoreAddConn (src/plastax/traits.py:
+    1523-1580): score 0 (grow) or -inf (veto), selection "all" and
+    dedupe_step True unless `params` override them. `should_add` is
+    ("modular_predicate", a, b, m, r)."""
+    params.setdefault("selection", "all")
+    params.setdefault("dedupe_step", True)
+    return ScoreAddConn(score=should_add, init=init, **params)
+
+
 class Network:
     """A network's trait slots (src/plastax/traits.py:874-1072).
 
@@ -192,7 +303,7 @@ class Network:
     prune_unit: ClassVar[Any] = None
     prune_conn: ClassVar[PruneConn | None] = None
     add_unit: ClassVar[Any] = None
-    add_conn: ClassVar[ProposeAddConn | None] = None
+    add_conn: ClassVar[ProposeAddConn | ScoreAddConn | None] = None
     reset_global: ClassVar[ResetGlobal | None] = None
     propagation: ClassVar[Propagation] = Propagation.TOPOLOGICAL
     seed: ClassVar[int] = 0
@@ -222,6 +333,10 @@ class Network:
             raise NotImplementedError(f"{cls.__name__}: prune_conn form has no engine lowering")
         if cls.add_conn is not None:
             cls.add_conn.validate()
+            if (isinstance(cls.add_conn, ScoreAddConn) and cls.add_conn.candidates == "shortlist_per_level"
+                    and cls.propagation is Propagation.PIPELINE):
+                raise ValueError('candidates = "shortlist_per_level" is levels-based and so topological-only; '
+                                 "PIPELINE networks use the global shortlist")
         if cls.update_unit is not None or cls.prune_unit is not None or cls.add_unit is not None:
             raise NotImplementedError(
                 f"{cls.__name__}: unit-lifecycle and update_unit phases have no engine lowering yet"

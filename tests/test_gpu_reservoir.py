@@ -18,7 +18,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def _run(cuda, cfg, steps, sharded_bands=1, graph=False):
+def _run(cuda, cfg, steps, sharded_bands=1, graph=False, ahead=True):
     import torch
 
     from oracle.steps import ReservoirOracle
@@ -31,6 +31,9 @@ def _run(cuda, cfg, steps, sharded_bands=1, graph=False):
                           int(state.tail_start.item()), num_inputs=cfg.num_inputs, num_res=cfg.num_units,
                           tau=cfg.tau, k=cfg.k, init_a=cfg.sigma * math.sqrt(3.0), seed=cfg.seed)
     step = make_step(net, static, device=cuda)
+    # the site-RNG selection runs one step ahead on the side stream by default
+    assert step.ahead
+    step.ahead = ahead
     rng = np.random.default_rng(5)
     for i in range(steps):
         x = rng.standard_normal(cfg.num_inputs).astype(np.float32)
@@ -61,6 +64,16 @@ def test_reservoir_churn_replayed_from_a_cuda_graph_matches_oracle(cuda):
     from plastax_b200.configs import ReservoirConfig
 
     _run(cuda, ReservoirConfig(num_units=1 << 12, fan_in=16, churn=0.01, capacity_align=256), steps=6, graph=True)
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_reservoir_churn_with_selection_in_step_matches_oracle(cuda, graph):
+    """The selection run inside its own step (beside the sweep, not one
+    step ahead) gives the same structure."""
+    from plastax_b200.configs import ReservoirConfig
+
+    _run(cuda, ReservoirConfig(num_units=1 << 12, fan_in=16, churn=0.01, capacity_align=256), steps=5, graph=graph,
+         ahead=False)
 
 
 def test_reservoir_overflow_into_tail_exhaustion(cuda):

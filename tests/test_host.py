@@ -172,6 +172,57 @@ def test_traits_reject_forms_without_a_lowering():
             prune_unit = object()
 
 
+@pytest.mark.parametrize("kwargs,exc,match", [
+    (dict(candidates="grid"), TypeError, "candidates"),
+    (dict(candidates="shortlist", importance=("field", "activation")), TypeError, "shortlist_size"),
+    (dict(candidates="shortlist", shortlist_size=4), TypeError, "importance"),
+    (dict(candidates="shortlist", shortlist_size=True, importance=("field", "activation")), TypeError,
+     "shortlist_size"),
+    (dict(max_new_per_level=None), TypeError, "max_new_per_level"),
+    (dict(selection="threshold"), TypeError, "threshold"),
+    (dict(level_cap_scope="bucket"), TypeError, "level_cap_scope"),
+    (dict(max_new_per_step=0), TypeError, "max_new_per_step"),
+    (dict(direction="shallower"), TypeError, "direction"),
+    (dict(dedupe_step=1), TypeError, "dedupe_step"),
+    (dict(score=("cosine", "a", "b")), NotImplementedError, "score form"),
+    (dict(score=("modular", 3, 5)), NotImplementedError, "score form"),
+    (dict(candidates="shortlist", shortlist_size=4, importance=("random",)), NotImplementedError, "importance"),
+])
+def test_score_add_conn_validation(kwargs, exc, match):
+    """ScoreAddConn's knob checks raise as the reference's
+    (src/plastax/traits.py:1390-1520): TypeError for a bad knob, and
+    NotImplementedError for a score form with no lowering."""
+    import plastax_b200 as px
+
+    base = dict(score=("modular", 3, 5, 17, 8, 0.125), max_new_per_level=4)
+    base.update(kwargs)
+    with pytest.raises(exc, match=match):
+        class Bad(px.Network):  # noqa: F841
+            forward_pass = px.ForwardPass("tanh")
+            add_conn = px.ScoreAddConn(**base)
+
+
+def test_score_add_conn_forms_and_predicate_adapter():
+    import plastax_b200 as px
+
+    with pytest.raises(ValueError, match="topological-only"):
+        class Bad(px.Network):  # noqa: F841
+            forward_pass = px.ForwardPass("tanh")
+            propagation = px.Propagation.PIPELINE
+            add_conn = px.ScoreAddConn(score=("modular", 3, 5, 17, 8, 0.125), max_new_per_level=2,
+                                       candidates="shortlist_per_level", shortlist_size=2,
+                                       importance=("modular", 7, 13, 0, 0.25))
+    rule = px.predicate_add_conn(("modular_predicate", 1, 1, 2, 0))
+    assert rule.selection == "all" and rule.dedupe_step and rule.max_new_per_level is None
+
+    class Ok(px.Network):  # noqa: F841
+        forward_pass = px.ForwardPass("tanh")
+        add_conn = rule
+    over = px.predicate_add_conn(("modular_predicate", 1, 1, 2, 0), selection="top_k", max_new_per_level=3,
+                                 dedupe_step=False)
+    assert over.selection == "top_k" and not over.dedupe_step
+
+
 def test_make_step_rejects_unknown_knobs():
     import plastax_b200 as px
 

@@ -73,6 +73,67 @@ def test_registry_selection_and_claim(case):
         assert last_commit == case["expect"]
 
 
+# the reference's versioned conformance rules as the engine's lowered forms
+# (scripts/parity/golden_rules.py: grid_score_v1, predicate_score_v1,
+# importance_v1)
+SCORE_RULES = {"grid_score_v1": ("modular", 3, 5, 17, 8, 0.125),
+               "predicate_score_v1": ("modular_predicate", 1, 1, 2, 0)}
+IMPORTANCE_RULES = {"importance_v1": ("modular", 7, 13, 0, 0.25)}
+SCORE_CASES = [c for c in REGISTRY if c["name"].startswith("grow_score")]
+
+
+@pytest.mark.parametrize("case", SCORE_CASES, ids=[c["name"] for c in SCORE_CASES])
+def test_score_grids_reproduce_the_registry_candidates(case):
+    """ScoreAddConn's exhaustive grid, shortlist and per-level shortlists:
+    the oracle's ranking and lowered score forms give the spec's candidate
+    lists (endpoints, scores, indices) exactly."""
+    p, rules = case["params"], case["rules"]
+    sel = case["calls"][0][1]
+    got = og.score_grid_spec(sel["units"], capacity=p["capacity"], candidates=p["candidates"],
+                             shortlist_size=p.get("shortlist_size"), score=SCORE_RULES[rules["score"]],
+                             importance_form=IMPORTANCE_RULES.get(rules.get("importance")),
+                             max_level_gap=p.get("max_level_gap", 1), direction=p.get("direction", "any"))
+    want = [[c[0], c[1], (float("-inf") if c[2] == "-inf" else float(c[2])), c[3]] for c in sel["cands"]]
+    assert got == want
+
+
+def test_score_grid_engine_layout_holds_the_spec_candidates():
+    """The engine's layout (every unit slot, shortlists padded with
+    ineligible units, the window applied) lists the spec's valid candidates
+    in the same relative order."""
+    for case in SCORE_CASES:
+        p, rules = case["params"], case["rules"]
+        sel = case["calls"][0][1]
+        n = p["capacity"]
+        level = np.zeros(n, np.int32)
+        pruned = np.ones(n, np.uint8)
+        for uid, lv, pr in sel["units"]:
+            level[uid], pruned[uid] = lv, pr
+        nb = int(level[pruned == 0].max()) + 1
+        src, dst, sc = og.score_grid_engine(level, pruned, candidates=p["candidates"],
+                                            shortlist_size=p.get("shortlist_size"),
+                                            score=SCORE_RULES[rules["score"]],
+                                            importance_form=IMPORTANCE_RULES.get(rules.get("importance")), cols={},
+                                            num_buckets=nb, topological=True, max_level_gap=p.get("max_level_gap", 1),
+                                            direction=p.get("direction", "any"))
+        got = [(int(a), int(b), float(c)) for a, b, c in zip(src, dst, sc, strict=True) if np.isfinite(c)]
+        spec = [[c[0], c[1], c[2], c[3]] for c in sel["cands"]]
+        spec_units = [[u[0], u[1], u[2]] for u in sel["units"]]
+        level_of = {u[0]: u[1] for u in spec_units}
+        want = []
+        for s_, d, score, _ in spec:
+            score = float("-inf") if score == "-inf" else float(score)
+            ok = s_ != d and abs(level_of[d] - level_of[s_]) <= p.get("max_level_gap", 1)
+            direction = p.get("direction", "any")
+            if direction == "deeper":
+                ok = ok and level_of[d] > level_of[s_]
+            elif direction == "same_or_deeper":
+                ok = ok and level_of[d] >= level_of[s_]
+            if ok and np.isfinite(score):
+                want.append((s_, d, score))
+        assert got == want, case["name"]
+
+
 RANDOM = _load("growth_random.json")
 
 
