@@ -308,13 +308,17 @@ class StepFn:
         elif ac.proposer == "global":
             self.n_cand = P
         else:
-            if self.sharded:
-                raise NotImplementedError("the per-connection proposer under Scheme-A has no engine lowering (it "
-                                          "ranks every rank's connections)")
+            # every rank's connections take part (under Scheme-A the bands are
+            # gathered into the whole arena first: gather_arena)
             self.conn_slots = sum(int(c) for c in st.level_capacities)
             self.n_cand = self.conn_slots * P
             self.conn_scratch = torch.empty(max(K.conn_rank_scratch(self.conn_slots, n), 1), dtype=torch.uint8,
                                             device=dev)
+            self.arena_all = None
+            if self.sharded:
+                self.arena_all = {"from_id": torch.empty(self.conn_slots, dtype=torch.int32, device=dev),
+                                  "to_id": torch.empty(self.conn_slots, dtype=torch.int32, device=dev),
+                                  "dead": torch.empty(self.conn_slots, dtype=torch.uint8, device=dev)}
         src_lo, dst_lo = getattr(ac, "src_lo", 0), getattr(ac, "dst_lo", 0)
         src_n = getattr(ac, "src_n", None)
         src_n = src_n if src_n is not None else n - src_lo
@@ -622,8 +626,12 @@ class StepFn:
                              dst_lo=ac.dst_lo, dst_n=dst_n, score_kind=self.score_kind, out=self.cand, **window)
         else:
             conns = state.conns
-            arena = conns[0] if len(conns) == 1 else {
-                c: torch.cat([b[c] for b in conns]) for c in ("from_id", "to_id", "dead")}
+            if self.sharded:
+                arena = gather_arena(conns, st, out=self.arena_all)
+                self.launches += 3 * len(conns)
+            else:
+                arena = conns[0] if len(conns) == 1 else {
+                    c: torch.cat([b[c] for b in conns]) for c in ("from_id", "to_id", "dead")}
             K.propose_per_conn(arena, ac.proposals_per_proposer, st.seed, state.step, n, dst_lo=ac.dst_lo,
                                dst_n=dst_n, score_kind=self.score_kind, scratch=self.conn_scratch, out=self.cand,
                                **window)
@@ -887,6 +895,28 @@ class StepFn:
                                                                                  device=self.dev)
         return StepResult(state=state, overflow=overflow, loss=self.loss_buf[0], growth_remainder=remainder,
                           grown=grown)
+
+
+def gather_arena(conns, static: NetworkStatic, out: dict | None = None, group=None) -> dict[str, torch.Tensor]:
+    """The whole arena's (from_id, to_id, dead), bucket-major in global slot
+    order, on every rank (src/plastax/phases.py:3863-3917, the per-connection
+    proposer's `_gather_replicated` of the edge keys): rank r holds positions
+    [r * cap / G, (r + 1) * cap / G) of each bucket, so one all-gather per
+    column and bucket lays the bands end to end."""
+    caps = [int(c) for c in static.level_capacities]
+    total = sum(caps)
+    dev = conns[0]["dead"].device
+    if out is None:
+        out = {"from_id": torch.empty(total, dtype=torch.int32, device=dev),
+               "to_id": torch.empty(total, dtype=torch.int32, device=dev),
+               "dead": torch.empty(total, dtype=torch.uint8, device=dev)}
+    dist = _dist()
+    off = 0
+    for b, bucket in enumerate(conns):
+        for col in ("from_id", "to_id", "dead"):
+            dist.all_gather_into_tensor(out[col][off:off + caps[b]], bucket[col].contiguous(), group=group)
+        off += caps[b]
+    return out
 
 
 def make_step(net: type[Network], static: NetworkStatic, *, batch_size: int | None = None, layout: str = "auto",

@@ -145,3 +145,87 @@ def test_two_rank_peer_step_equals_one_gpu_step(cuda):
         assert got[r]["tail"] == int(state.tail_start.item())
     for col in want:
         np.testing.assert_array_equal(np.concatenate([got[0][col], got[1][col]]), want[col], err_msg=col)
+
+
+def _per_conn_case(dev, world=1, rank=0):
+    import plastax_b200 as px
+
+    class Net(px.Network):
+        forward_pass = px.ForwardPass("tanh")
+        propagation = px.Propagation.PIPELINE
+        prune_conn = px.MagnitudePrune(0.02)
+        add_conn = px.ProposeAddConn(proposals_per_proposer=2, max_new_per_level=120, dst_lo=2,
+                                     proposer="per_connection", score="uniform_q256", init=("hash_uniform", 0.1),
+                                     level_cap_scope="step")
+
+    rng = np.random.default_rng(31)
+    n, e = 700, 9000
+    src, dst = rng.integers(0, n, e), rng.integers(2, n, e)
+    w = (rng.standard_normal(e) * 0.1).astype(np.float32)
+    kw = dict(sharding=px.ShardSpec("conns", world), shard_rank=rank) if world > 1 else {}
+    static, state = px.NetworkBuilder.from_edges(Net, n, src, dst, weights=w, input_ids=(0, 1), output_ids=(),
+                                                 capacity_headroom=0.1, capacity_align=256, device=dev, **kw)
+    return Net, static, state
+
+
+def _run_per_conn(rank, world, port, steps, q):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from plastax_b200 import StepInputs, make_step
+
+        Net, static, state = _per_conn_case(dev, world, rank)
+        step = make_step(Net, static, device=dev)
+        xs = _inputs(steps, 2)
+        for i in range(steps):
+            step(state, StepInputs(torch.from_numpy(xs[i]).to(dev)))
+        torch.cuda.synchronize()
+        out = {k: v.cpu().numpy() for k, v in state.conns[0].items()}
+        out["grown"] = int(state.grown.item())
+        step.close()
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(600)
+def test_two_rank_per_connection_proposer_equals_one_gpu(cuda):
+    """The per-connection proposer under Scheme-A ranks every rank's
+    connections (the bands gathered into the whole arena): two ranks grow
+    exactly the edges one GPU grows."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from plastax_b200 import StepInputs, make_step
+
+    steps = 3
+    Net, static, state = _per_conn_case(cuda)
+    step = make_step(Net, static, device=cuda)
+    xs = _inputs(steps, 2)
+    for i in range(steps):
+        step(state, StepInputs(torch.from_numpy(xs[i]).to(cuda)))
+    torch.cuda.synchronize()
+    want = {k: v.cpu().numpy() for k, v in state.conns[0].items()}
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_run_per_conn, args=(r, 2, port, steps, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=500) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert got[0]["grown"] == got[1]["grown"] == int(state.grown.item()) > 0
+    for col in want:
+        np.testing.assert_array_equal(np.concatenate([got[0][col], got[1][col]]), want[col], err_msg=col)

@@ -162,3 +162,71 @@ def test_scheme_a_two_gloo_ranks_equal_one_arena():
     for col in ("from_id", "to_id", "dead", "weight"):
         got = np.concatenate([np.asarray(band[col]) for band in out["bands"]]).astype(b[col].dtype)
         np.testing.assert_array_equal(got, b[col], err_msg=col)
+
+
+def _gather_worker(rank: int, port: int, q) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        import plastax_b200 as px
+        from plastax_b200.step import gather_arena
+
+        Net, n, src, dst = _layered_net()
+        static, state = px.NetworkBuilder.from_edges(
+            Net, n, src, dst, input_ids=(0, 1), output_ids=(), capacity_align=64, capacity_headroom=0.2,
+            sharding=px.ShardSpec("conns", WORLD), shard_rank=rank, device="cpu")
+        for b in state.conns:  # a few tombstones, so dead slots sit among the live ones
+            b["dead"][::7] = 1
+        got = gather_arena(state.conns, static)
+        if rank == 0:
+            q.put({k: v.numpy().copy() for k, v in got.items()})
+    finally:
+        dist.destroy_process_group()
+
+
+def _layered_net():
+    import plastax_b200 as px
+
+    class Net(px.Network):
+        forward_pass = px.ForwardPass("tanh")
+        add_conn = px.ProposeAddConn(proposals_per_proposer=2, max_new_per_level=8, proposer="per_connection")
+
+    rng = np.random.default_rng(12)
+    n = 120
+    src = np.concatenate([rng.integers(0, 40, 300), rng.integers(40, 80, 300)])
+    dst = np.concatenate([rng.integers(40, 80, 300), rng.integers(80, 120, 300)])
+    return Net, n, src, dst
+
+
+@pytest.mark.timeout(300)
+def test_per_connection_arena_gather_equals_the_whole_arena():
+    """Under Scheme-A the per-connection proposer ranks every rank's
+    connections: the gathered bands, bucket-major, are the unsharded arena's
+    (from_id, to_id, dead) slot for slot (src/plastax/phases.py:3863-3917)."""
+    import plastax_b200 as px
+
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gather_worker, args=(r, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    got = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    Net, n, src, dst = _layered_net()
+    static, full = px.NetworkBuilder.from_edges(Net, n, src, dst, input_ids=(0, 1), output_ids=(), capacity_align=64,
+                                                capacity_headroom=0.2, device="cpu")
+    assert len(full.conns) >= 2
+    G = WORLD
+    for col in ("from_id", "to_id", "dead"):
+        parts = []
+        for b in full.conns:
+            c = b[col].numpy().copy()
+            if col == "dead":
+                band = c.size // G
+                for r in range(G):  # each rank tombstoned every 7th slot of its own band
+                    c[r * band:(r + 1) * band][::7] = 1
+            parts.append(c)
+        np.testing.assert_array_equal(got[col], np.concatenate(parts), err_msg=col)
