@@ -444,6 +444,41 @@ PXB_API int pxb_propose_grid(int32_t num_units, int32_t grids, int32_t rows,
                              int32_t src_level_bound, int32_t *src_out,
                              int32_t *dst_out, float *score_out, void *stream);
 
+/* A chunk of steps as one device-side loop (src/plastax/driver.py:170-317,
+ * Driver.scan). `step_graph` is the cudaGraph_t of one captured step; the
+ * loop runs it as the body of a conditional WHILE node: before each step
+ * row *counter of in_chunk [count, in_cols] (and tgt_chunk) is copied into
+ * the step's input buffers; after it the loss goes to loss_rec[row], the
+ * activations of out_ids to out_rec[row, :], *counter advances and the
+ * loop stops when it reaches `count` or right after a step whose *overflow
+ * (or, with resorts, *needs_resort) is set. *status = rows done * 2 +
+ * halted. Launch with pxb_loop_launch after setting *counter to the first
+ * row; the graph is cloned, so step_graph may be released afterwards. */
+typedef struct pxb_loop_desc {
+  int32_t *counter;
+  int32_t count;
+  const float *in_chunk;
+  int32_t in_cols;
+  float *in_buf;
+  const float *tgt_chunk; /* or NULL */
+  int32_t tgt_cols;
+  float *tgt_buf;
+  const float *loss;      /* the step's loss scalar, or NULL */
+  float *loss_rec;        /* [count], or NULL */
+  const float *act;       /* the activation column, for out_rec */
+  const int32_t *out_ids; /* [n_out] */
+  int32_t n_out;
+  float *out_rec;         /* [count, n_out], or NULL */
+  const uint8_t *overflow;
+  const uint8_t *needs_resort;
+  int32_t resorts;
+  int32_t *status;
+} pxb_loop_desc;
+
+PXB_API int pxb_loop_build(void *step_graph, const pxb_loop_desc *desc, void **loop_out);
+PXB_API int pxb_loop_launch(void *loop, void *stream);
+PXB_API int pxb_loop_destroy(void *loop);
+
 /* The per-source-level cap (level_cap_scope "source_level",
  * src/plastax/phases.py:4324-4487): over a level-major list idx of n
  * candidates (pxb_select_step with k = n), the first k of every level's

@@ -12,6 +12,7 @@ from plastax_b200 import monoid, optim
 from plastax_b200.builder import NetworkBuilder
 from plastax_b200.state import NetworkState, NetworkStatic, live_conn_count, make_empty_state
 from plastax_b200.state import grow_bucket
+from plastax_b200.driver import Driver
 from plastax_b200.step import GrowthRemainder, StepFn, StepInputs, StepResult, make_growth_retry, make_step
 from plastax_b200.topo import resort
 from plastax_b200.traits import (
@@ -46,7 +47,7 @@ from plastax_b200.types import (
 
 __all__ = [
     "ACTIVATION", "DEAD", "FROM_ID", "GRAD_PRE_ACT", "LEVEL", "LOSS_GRAD", "PRUNED", "TO_ID", "WEIGHT",
-    "BackwardPass", "DestinationThresholdPrune", "FieldSpec", "ForwardPass", "GrowthRemainder", "MSELoss",
+    "BackwardPass", "DestinationThresholdPrune", "Driver", "FieldSpec", "ForwardPass", "GrowthRemainder", "MSELoss",
     "MagnitudePrune", "MeanFloatFirstRest", "Network", "NetworkBuilder", "NetworkState", "NetworkStatic", "Propagation", "ProposeAddConn",
     "PruneConn", "ResetGlobal", "ScoreAddConn", "ShardSpec", "SoftmaxCrossEntropyLoss", "StepFn", "StepInputs", "StepResult", "live_conn_count",
     "grow_bucket", "make_empty_state", "make_growth_retry", "make_step", "monoid", "optim", "predicate_add_conn",

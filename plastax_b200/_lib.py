@@ -71,6 +71,17 @@ class PairScore(ctypes.Structure):
     ]
 
 
+class LoopDesc(ctypes.Structure):
+    """`pxb_loop_desc`: the buffers of a device-side chunk loop."""
+
+    _fields_ = [
+        ("counter", c_ptr), ("count", c_i32), ("in_chunk", c_ptr), ("in_cols", c_i32), ("in_buf", c_ptr),
+        ("tgt_chunk", c_ptr), ("tgt_cols", c_i32), ("tgt_buf", c_ptr), ("loss", c_ptr), ("loss_rec", c_ptr),
+        ("act", c_ptr), ("out_ids", c_ptr), ("n_out", c_i32), ("out_rec", c_ptr), ("overflow", c_ptr),
+        ("needs_resort", c_ptr), ("resorts", c_i32), ("status", c_ptr),
+    ]
+
+
 class PxbError(RuntimeError):
     """A libpxb entry point returned a non-zero status."""
 
@@ -186,6 +197,9 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_batched_loss": (c_i32, [c_i32, c_i32, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_batch_mean": (c_i32, [c_i32, c_i32, c_ptr, c_ptr, c_ptr]),
     "pxb_count_dead": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr]),
+    "pxb_loop_build": (c_i32, [c_ptr, c_ptr, ctypes.POINTER(c_ptr)]),
+    "pxb_loop_launch": (c_i32, [c_ptr, c_ptr]),
+    "pxb_loop_destroy": (c_i32, [c_ptr]),
     "pxb_unit_importance": (c_i32, [c_i32, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr]),
     "pxb_propose_grid": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_i32, c_i32,
                                  c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_ptr]),

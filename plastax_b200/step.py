@@ -837,12 +837,13 @@ class StepFn:
         return ac is None or (ac.trigger == "every_step" and int(getattr(self.net, "structural_interval", 1)) <= 1
                               and ac.on_overflow != "error")
 
-    def capture(self, state: NetworkState, inputs: StepInputs) -> None:
+    def capture(self, state: NetworkState, inputs: StepInputs, *, keep_graph: bool = False) -> None:
         """Capture one step of `state` as a CUDA graph; later calls with the
         same state replay it (inputs and targets are copied into the graph's
         input buffers first). Call after at least one eager step, so every
         kernel and index is initialised; the shapes of `inputs` (and
-        targets) are fixed from then on."""
+        targets) are fixed from then on. `keep_graph` keeps the cudaGraph_t
+        (`self.graph.raw_cuda_graph()`), for a device-side loop over it."""
         if not self.capturable():
             raise ValueError("this step's work depends on the step count (trigger or interval); it cannot be "
                              "replayed from one graph")
@@ -852,11 +853,12 @@ class StepFn:
             self.dev).reshape(-1).clone()
         self._graph_in = StepInputs(x, t)
         torch.cuda.synchronize(self.dev)
-        g = torch.cuda.CUDAGraph()
+        g = torch.cuda.CUDAGraph(keep_graph=keep_graph)
         with torch.cuda.graph(g):
             self._graph_rem = self._body(state, self._graph_in)
         self.graph = g
         self._graph_state = id(state)
+        self._graph_kept = keep_graph
 
     def release_graph(self) -> None:
         """Drop the captured graph and its buffers. A graph that holds NCCL

@@ -278,3 +278,10 @@ def test_mean_float_first_rest_declares_every_column():
     assert r.reduction(px.LEVEL) == "not_batched"
     assert r.reduction(px.PRUNED) == "not_batched"
     assert r.reduction(px.FieldSpec.int32("test/count")) == "first"
+
+
+def test_driver_rejects_check_every_below_one():
+    import plastax_b200 as px
+
+    with pytest.raises(ValueError, match="check_every"):
+        px.Driver(None, None, None, check_every=0, device="cpu")
