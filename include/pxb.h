@@ -71,14 +71,24 @@ extern "C" {
 #define PXB_OPT_MOMENTUM 1
 #define PXB_OPT_ADAM 2
 #define PXB_OPT_RMSPROP 3
+/* Utility-based perturbed gradient descent (examples/upgd.py:135-208), per
+ * live edge with g = grad[dst] * act[src], U = opt_m (utility), t = opt_t:
+ *   t' = t + 1;  U' = b1*U + (1 - b1)*(-g * w)
+ *   gate = sigmoid((U' / max(1 - b1^t', eps)) / max(unit_scale[dst], eps))
+ *   noise = b2 * sqrt(-2 ln max(h(src, dst, t'), 1e-7)) * cos(2 pi h(dst, src, t'))
+ *   w' = w - lr * (g + noise) * (1 - gate)
+ * with h the three-word integer hash to [0, 1) of examples/dst_sparse.py:77-85
+ * and t' truncated to int32 as its third word (b1 = beta, b2 = sigma). */
+#define PXB_OPT_UPGD 4
 
 typedef struct pxb_optimizer {
   int32_t kind;        /* PXB_OPT_* */
   float lr;
-  float b1;            /* momentum: mu; adam: beta1; rmsprop: decay */
-  float b2;            /* adam: beta2 */
-  float eps;           /* adam: outside sqrt; rmsprop: inside sqrt */
+  float b1;            /* momentum: mu; adam: beta1; rmsprop: decay; upgd: beta */
+  float b2;            /* adam: beta2; upgd: sigma */
+  float eps;           /* adam: outside sqrt; rmsprop: inside sqrt; upgd: floors */
   float weight_decay;  /* adamw */
+  const float *unit_scale; /* upgd: the utility scale (eta) per destination unit */
 } pxb_optimizer;
 
 /* growth score rules for per-unit proposals */

@@ -29,7 +29,7 @@ c_ptr = ctypes.c_void_p
 MONOID = {"sum": 0, "max": 1, "min": 2}
 ACT = {"identity": 0, "tanh": 1, "relu": 2, "sigmoid": 3}
 PRUNE_NONE, PRUNE_ABS_BELOW, PRUNE_ABS_BELOW_DST = 0, 1, 2
-OPT = {"sgd": 0, "momentum": 1, "adam": 2, "rmsprop": 3}
+OPT = {"sgd": 0, "momentum": 1, "adam": 2, "rmsprop": 3, "upgd": 4}
 SCORE_UNIFORM, SCORE_UNIFORM_Q256, SCORE_GRAD_ACT = 0, 1, 2
 INIT_CONST, INIT_DYADIC, INIT_HASH_UNIFORM = 0, 1, 2
 CLAIM_PIPELINE, CLAIM_TOPOLOGICAL = 0, 1
@@ -96,6 +96,7 @@ class Optimizer(ctypes.Structure):
         ("b2", c_f32),
         ("eps", c_f32),
         ("weight_decay", c_f32),
+        ("unit_scale", c_ptr),
     ]
 
 

@@ -33,6 +33,9 @@ class BatchedStepFn:
         if batch_size % 4 != 0 or batch_size > 1024:
             raise ValueError(f"make_step: the batched engine moves unit rows as float4: batch_size must be a "
                              f"multiple of 4 and at most 1024, got {batch_size}")
+        if net.update_conn is not None and net.update_conn.kind == "upgd":
+            raise NotImplementedError("a batched step has no UPGD lowering (the rule declares no exact "
+                                      "per-sample / batch pair)")
         if net.forward_pass.combine.lowered() != "sum":
             raise NotImplementedError("a batched step lowers the linear (sum) forward only")
         if static.sharding is not None and static.num_shards > 1:

@@ -19,11 +19,46 @@ namespace pxb {
 struct OptParams {
   int kind;
   float lr, b1, b2, eps, wd;
+  const float *scale;  // upgd: eta per destination unit
 };
 
+// examples/dst_sparse.py:77-85: three words hashed to a float in [0, 1).
+__device__ __forceinline__ float hash01(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t h = (a + 0x9E3779B1u) * 0x85EBCA77u;
+  h = (h ^ b) * 0xC2B2AE3Du;
+  h = (h ^ c) * 0x27D4EB2Fu;
+  h ^= h >> 15;
+  h *= 0x2C1B3C6Du;
+  h ^= h >> 13;
+  return __fdiv_rn(static_cast<float>(h >> 8), 16777216.0f);
+}
+
+// examples/upgd.py:160-199, float32 operation by operation.
+__device__ __forceinline__ void upgd_step(const OptParams &p, float grad, float &w, float *u_col, float *t_col,
+                                          int64_t s, int32_t src, int32_t dst) {
+  const float inst = __fmul_rn(-grad, w);
+  const float step = __fadd_rn(t_col[s], 1.0f);
+  const float util = __fadd_rn(__fmul_rn(p.b1, u_col[s]), __fmul_rn(__fsub_rn(1.0f, p.b1), inst));
+  const float corrected = __fdiv_rn(util, fmaxf(__fsub_rn(1.0f, powf(p.b1, step)), p.eps));
+  const float scale = fmaxf(p.scale[dst], p.eps);
+  const float gated = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-__fdiv_rn(corrected, scale))));
+  const uint32_t salt = static_cast<uint32_t>(static_cast<int32_t>(step));
+  const float u1 = fmaxf(hash01(static_cast<uint32_t>(src), static_cast<uint32_t>(dst), salt), 1e-7f);
+  const float u2 = hash01(static_cast<uint32_t>(dst), static_cast<uint32_t>(src), salt);
+  const float gauss = __fmul_rn(__fsqrt_rn(__fmul_rn(-2.0f, logf(u1))), cosf(__fmul_rn(6.2831855f, u2)));
+  const float noise = __fmul_rn(p.b2, gauss);
+  w = __fsub_rn(w, __fmul_rn(__fmul_rn(p.lr, __fadd_rn(grad, noise)), __fsub_rn(1.0f, gated)));
+  u_col[s] = util;
+  t_col[s] = step;
+}
+
 __device__ __forceinline__ void opt_step(const OptParams &p, float grad, float &w, float *m_col,
-                                         float *v_col, float *t_col, int64_t s) {
+                                         float *v_col, float *t_col, int64_t s, int32_t src = 0,
+                                         int32_t dst = 0) {
   switch (p.kind) {
+    case PXB_OPT_UPGD:
+      upgd_step(p, grad, w, m_col, t_col, s, src, dst);
+      break;
     case PXB_OPT_SGD:
       w = __fsub_rn(w, __fmul_rn(p.lr, grad));
       break;
@@ -253,7 +288,7 @@ __global__ void __launch_bounds__(256) backward_kernel(
         const int64_t s = c * chunk_slots + u * 32 + lane;
         const float gr = __fmul_rn(g[u], __ldg(act + f[u]));
         float wn = w[u];
-        opt_step(op, gr, wn, m_col, v_col, t_col, s);
+        opt_step(op, gr, wn, m_col, v_col, t_col, s, f[u], t[u]);
         weight[s] = wn;
       }
     }
@@ -449,9 +484,9 @@ static int launch_backward(int64_t cap, const int32_t *from, const int32_t *to, 
                            int32_t monoid, float *acc, const pxb_optimizer *opt, float *m, float *v, float *t,
                            cudaStream_t st) {
   const uint32_t n = static_cast<uint32_t>(num_units);
-  OptParams op{0, 0, 0, 0, 0, 0};
+  OptParams op{0, 0, 0, 0, 0, 0, nullptr};
   const bool update = opt != nullptr;
-  if (update) op = OptParams{opt->kind, opt->lr, opt->b1, opt->b2, opt->eps, opt->weight_decay};
+  if (update) op = OptParams{opt->kind, opt->lr, opt->b1, opt->b2, opt->eps, opt->weight_decay, opt->unit_scale};
   const bool accum = acc != nullptr;
   const int64_t chunks = (cap + 32 * kBwdUnroll - 1) / (32 * kBwdUnroll);
   const int grid = grid_for(chunks, 8, 8);  // 8 warps per CTA
@@ -488,7 +523,9 @@ extern "C" int pxb_backward_accumulate(int64_t cap, const int32_t *from_id, cons
 
 static int check_opt(const char *fn, const pxb_optimizer *opt, const float *m, const float *v, const float *t) {
   PXB_REQUIRE(opt != nullptr, "%s: optimizer is NULL", fn);
-  PXB_REQUIRE(opt->kind >= 0 && opt->kind <= 3, "%s: unknown optimizer kind %d", fn, opt->kind);
+  PXB_REQUIRE(opt->kind >= 0 && opt->kind <= 4, "%s: unknown optimizer kind %d", fn, opt->kind);
+  PXB_REQUIRE(opt->kind != PXB_OPT_UPGD || (m && t && opt->unit_scale),
+              "%s: upgd needs its utility (opt_m) and step (opt_t) columns and the unit scale", fn);
   PXB_REQUIRE(opt->kind != PXB_OPT_MOMENTUM || v, "%s: momentum needs its velocity column (opt_v)", fn);
   PXB_REQUIRE(opt->kind != PXB_OPT_ADAM || (m && v && t), "%s: adam needs opt/m, opt/v and opt/t", fn);
   PXB_REQUIRE(opt->kind != PXB_OPT_RMSPROP || v, "%s: rmsprop needs its mean-square column (opt_v)", fn);

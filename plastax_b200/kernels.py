@@ -136,9 +136,13 @@ def optimizer_struct(kind: str, lr: float, b1: float = 0.0, b2: float = 0.0, eps
     return _lib.Optimizer(_lib.OPT[kind], lr, b1, b2, eps, weight_decay)
 
 
+OPT_COLS = ("opt/m", "opt/v", "opt/t")
+
+
 def backward_update(b: Bucket, grad: torch.Tensor, act: torch.Tensor, acc: torch.Tensor | None,
-                    opt: _lib.Optimizer) -> None:
-    """Backward accumulate (acc may be None) fused with the optimizer update."""
+                    opt: _lib.Optimizer, cols: tuple[str, str, str] = OPT_COLS) -> None:
+    """Backward accumulate (acc may be None) fused with the optimizer update;
+    `cols` names the bucket's (m, v, t) state columns."""
     cap = _bucket(b)
     n = grad.numel()
     _check(act, torch.float32, n, "act")
@@ -146,7 +150,7 @@ def backward_update(b: Bucket, grad: torch.Tensor, act: torch.Tensor, acc: torch
         _check(acc, torch.float32, n, "acc")
     call("pxb_backward_update", ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]), ptr(b["dead"]),
          ptr(b["weight"]), ptr(grad), ptr(act), ctypes.c_int32(n), ptr(acc), ctypes.byref(opt),
-         ptr(b.get("opt/m")), ptr(b.get("opt/v")), ptr(b.get("opt/t")), _stream())
+         ptr(b.get(cols[0])), ptr(b.get(cols[1])), ptr(b.get(cols[2])), _stream())
 
 
 def unit_apply(acc: torch.Tensor, out: torch.Tensor, *, mode: int, act_kind: str, monoid: str = "sum",

@@ -20,6 +20,11 @@ _V = FieldSpec.float32("opt/v")
 _T = FieldSpec.float32("opt/t")
 
 
+UPGD_UTIL = FieldSpec.float32("upgd/util")
+UPGD_T = FieldSpec.float32("upgd/t")
+UPGD_ETA = FieldSpec.float32("upgd/eta")
+
+
 @dataclasses.dataclass(frozen=True)
 class Optimizer:
     kind: str
@@ -31,11 +36,20 @@ class Optimizer:
     weight_decay: float = 0.0
     state_fields: tuple[FieldSpec, ...] = ()
     needs_step_counter: bool = False
+    # the bucket columns the kernel reads as (m, v, t)
+    cols: tuple[str, str, str] = ("opt/m", "opt/v", "opt/t")
+    unit_fields: tuple[FieldSpec, ...] = ()
+    # upgd: the unit column of the utility scale, and who writes it: "local"
+    # (the step, as the max of each destination's incoming utilities) or
+    # "global" (the caller, e.g. upgd_global_eta)
+    scale_field: FieldSpec | None = None
+    eta: str = "local"
 
-    def struct(self):
+    def struct(self, unit_scale=None):
         from plastax_b200._lib import OPT, Optimizer as COpt
 
-        return COpt(OPT[self.kind], self.lr, self.b1, self.b2, self.eps, self.weight_decay)
+        scale = None if unit_scale is None else unit_scale.data_ptr()
+        return COpt(OPT[self.kind], self.lr, self.b1, self.b2, self.eps, self.weight_decay, scale)
 
     def oracle_args(self) -> dict:
         return dict(kind=self.kind, lr=self.lr, b1=self.b1, b2=self.b2, eps=self.eps, wd=self.weight_decay)
@@ -62,3 +76,31 @@ def adamw(lr: float, grad_field: FieldSpec = GRAD_PRE_ACT, weight_decay: float =
 
 def rmsprop(lr: float, grad_field: FieldSpec = GRAD_PRE_ACT, decay: float = 0.9, eps: float = 1e-8) -> Optimizer:
     return Optimizer("rmsprop", lr, grad_field, b1=decay, eps=eps, state_fields=(_V,))
+
+
+def upgd(lr: float = 0.01, beta: float = 0.999, sigma: float = 0.001, eps: float = 1e-8,
+         grad_field: FieldSpec = GRAD_PRE_ACT, eta: str = "local") -> Optimizer:
+    """Utility-based perturbed gradient descent (examples/upgd.py:135-208):
+    per-edge utility trace `upgd/util` and step `upgd/t`, the utility scale
+    per destination in the unit column `upgd/eta` -- the max of its incoming
+    edges' stored utilities, computed by the step before the update
+    (eta="local", the example's v1), or written by the caller between steps
+    (eta="global", v0: see upgd_global_eta)."""
+    if eta not in ("local", "global"):
+        raise ValueError(f"upgd: eta must be 'local' or 'global', got {eta!r}")
+    return Optimizer("upgd", lr, grad_field, b1=beta, b2=sigma, eps=eps, state_fields=(UPGD_UTIL, UPGD_T),
+                     cols=(UPGD_UTIL.name, "", UPGD_T.name), unit_fields=(UPGD_ETA,), scale_field=UPGD_ETA, eta=eta)
+
+
+def upgd_global_eta(state) -> None:
+    """v0's scale (examples/upgd.py:211-230): max(1e-8, max(0, every live
+    edge's utility)) broadcast into `upgd/eta`, in place (device reductions,
+    one host read)."""
+    import torch
+
+    best = torch.zeros((), dtype=torch.float32, device=state.units[UPGD_ETA.name].device)
+    for b in state.conns:
+        live = b["dead"] == 0
+        if bool(live.any()):
+            best = torch.maximum(best, b[UPGD_UTIL.name][live].max())
+    state.units[UPGD_ETA.name].fill_(max(float(best.item()), 1e-8))

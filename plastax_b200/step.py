@@ -113,6 +113,10 @@ class StepFn:
         self.fuse_update = (not self.pipeline and net.update_conn is not None and net.backward_pass is not None
                             and net.update_unit is None)
         self.opt = net.update_conn.struct() if net.update_conn is not None else None
+        self.opt_cols = net.update_conn.cols if net.update_conn is not None else K.OPT_COLS
+        # UPGD: the utility scale per destination unit, in the state's column
+        self.upgd_local = net.update_conn is not None and net.update_conn.kind == "upgd" \
+            and net.update_conn.eta == "local"
         self.ac: ProposeAddConn | ScoreAddConn | None = net.add_conn
         self.is_score = isinstance(self.ac, ScoreAddConn)
         # The forward reads a destination-grouped mirror of each bucket when
@@ -190,6 +194,9 @@ class StepFn:
             mode = _lib.CLAIM_PIPELINE if self.pipeline else _lib.CLAIM_TOPOLOGICAL
             self.bitmaps = [K.free_bitmap_build(mode, b, level, state.tail_start, self.num_levels,
                                                 shard_base=st.shard_base(i)) for i, b in enumerate(state.conns)]
+        uc = self.net.update_conn
+        if uc is not None and uc.scale_field is not None:
+            self.opt = uc.struct(state.units[uc.scale_field.name])
         self.step_dev.fill_(state.step)
         self._ahead_ready = False
         self._bound = id(state)
@@ -454,7 +461,32 @@ class StepFn:
         else:
             torch.minimum(self.acc, self.part, out=self.acc)
 
+    def _upgd_eta(self, state: NetworkState) -> None:
+        """UPGD's local utility scale (examples/upgd.py:83-128, v1): every
+        destination's max over its incoming live edges' stored utilities
+        (the previous step's), -inf without one, written for the live
+        non-input units; a max sweep with the utilities as weights and unit
+        activations of one (each product is the utility itself)."""
+        uc = self.net.update_conn
+        n = self.static.num_units
+        if getattr(self, "_eta_acc", None) is None:
+            self._eta_acc = torch.empty(n, dtype=torch.float32, device=self.dev)
+            self._ones = torch.ones(n, dtype=torch.float32, device=self.dev)
+        K.fill(self._eta_acc, float("-inf"))
+        util = uc.cols[0]
+        for b in state.conns:
+            K.forward_accumulate({"from_id": b["from_id"], "to_id": b["to_id"], "dead": b["dead"], "weight": b[util]},
+                                 self._ones, self._eta_acc, "max")
+            self.launches += 1
+        if self.sharded:
+            _dist().all_reduce(self._eta_acc, op=_dist().ReduceOp.MAX)
+        K.unit_apply(self._eta_acc, state.units[uc.scale_field.name], mode=0, act_kind="identity", monoid="max",
+                     is_input=self.is_input, pruned=state.units.get(PRUNED.name))
+        self.launches += 2
+
     def _forward(self, state: NetworkState) -> None:
+        if self.upgd_local:
+            self._upgd_eta(state)
         net, st, units = self.net, self.static, state.units
         act = units[ACTIVATION.name]
         pruned = units.get(PRUNED.name)
@@ -539,7 +571,7 @@ class StepFn:
         for l in range(L - 1, 0, -1):
             b = state.conns[l]
             if self.fuse_update:
-                K.backward_update(b, grad, act, self.acc, self.opt)
+                K.backward_update(b, grad, act, self.acc, self.opt, self.opt_cols)
             else:
                 K.backward_accumulate(b, grad, self.acc, "sum")
             self._combine_partials(self.acc)
@@ -547,7 +579,7 @@ class StepFn:
                          target_level=l, is_input=self.is_input, pruned=pruned)
             self.launches += 2
         if self.fuse_update and L > 0:
-            K.backward_update(state.conns[0], grad, act, None, self.opt)  # bucket 0: update only
+            K.backward_update(state.conns[0], grad, act, None, self.opt, self.opt_cols)  # bucket 0: update only
             self.launches += 1
 
     def _update_conn(self, state: NetworkState) -> None:
@@ -557,7 +589,7 @@ class StepFn:
         units = state.units
         grad, act = units[net.update_conn.grad_field.name], units[ACTIVATION.name]
         for b in state.conns:
-            K.backward_update(b, grad, act, None, self.opt)
+            K.backward_update(b, grad, act, None, self.opt, self.opt_cols)
             self.launches += 1
 
     def _prune(self, state: NetworkState) -> None:

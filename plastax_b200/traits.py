@@ -354,6 +354,8 @@ class Network:
         if isinstance(cls.prune_conn, DestinationThresholdPrune):
             fields += [cls.prune_conn.field]
         fields += list(cls.extra_unit_fields)
+        if cls.update_conn is not None:
+            fields += list(getattr(cls.update_conn, "unit_fields", ()))
         if cls.unit_capacity is not None:
             fields += [PRUNED]
         out: list[FieldSpec] = []
