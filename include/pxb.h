@@ -489,6 +489,81 @@ PXB_API int pxb_loop_build(void *step_graph, const pxb_loop_desc *desc, void **l
 PXB_API int pxb_loop_launch(void *loop, void *stream);
 PXB_API int pxb_loop_destroy(void *loop);
 
+/* ------------------------------------------------------------------ */
+/* unit lifecycle (src/plastax/phases.py:1148-1193, :1245-1425)        */
+/* ------------------------------------------------------------------ */
+/* Unit columns reset to their declared defaults (a pruned unit's, a new
+ * child's): up to PXB_MAX_UNIT_COLUMNS columns of 1 or 4 bytes, each with
+ * its default's bit pattern. LEVEL and PRUNED are never listed. */
+#define PXB_MAX_UNIT_COLUMNS 16
+typedef struct pxb_unit_columns {
+  int32_t count;
+  void *cols[PXB_MAX_UNIT_COLUMNS];
+  int32_t bytes[PXB_MAX_UNIT_COLUMNS];
+  uint32_t defaults[PXB_MAX_UNIT_COLUMNS];
+} pxb_unit_columns;
+
+/* update_unit's lowered forms, on every live unit (inputs and outputs
+ * included; pruned slots skipped), each unit reading only its own slot:
+ *   AFFINE     field = field * a + b
+ *   TRACE_ABS  field = (1 - a) * field + a * |src|
+ *   TRACE      field = (1 - a) * field + a * src */
+#define PXB_UNIT_UPDATE_AFFINE 0
+#define PXB_UNIT_UPDATE_TRACE_ABS 1
+#define PXB_UNIT_UPDATE_TRACE 2
+PXB_API int pxb_unit_update(int32_t num_units, int32_t kind, float *field, const float *src,
+                            float a, float b, const uint8_t *pruned, void *stream);
+
+/* The q-quantile of `field` over the live non-exempt units (NaN values
+ * excluded): the value at rank floor(q * m) (0-based, clamped to m - 1) of
+ * the m values ascending, into *out (device); -inf when m == 0. */
+PXB_API int pxb_unit_quantile_scratch_bytes(int32_t num_units, size_t *bytes);
+PXB_API int pxb_unit_quantile(int32_t num_units, const float *field, const uint8_t *pruned,
+                              const uint8_t *exempt, float q, float *out, void *scratch,
+                              size_t scratch_bytes, void *stream);
+
+/* prune_unit (src/plastax/phases.py:1245-1307) for the predicate
+ * field[i] < *threshold (device scalar): a live unit that is not exempt
+ * (inputs and outputs) and that the predicate selects is doomed: doomed[i]
+ * = 1, pruned[i] = 1, its `reset` columns back to their defaults (LEVEL
+ * kept). Then pxb_kill_unit_edges over every bucket. */
+PXB_API int pxb_unit_prune(int32_t num_units, const float *field, const float *threshold,
+                           const uint8_t *exempt, uint8_t *pruned, uint8_t *doomed,
+                           const pxb_unit_columns *reset, void *stream);
+
+/* Tombstone every live connection with a doomed endpoint; each joins its
+ * claim domain's free bitmap (row bitmap_level[from_id], or 0 when
+ * bitmap_level is NULL; no bitmap when free_bitmap is NULL). */
+PXB_API int pxb_kill_unit_edges(int64_t cap, const int32_t *from_id, const int32_t *to_id,
+                                uint8_t *dead, int32_t num_units, const uint8_t *doomed,
+                                uint32_t *free_bitmap, const int32_t *bitmap_level,
+                                void *stream);
+
+/* add_unit (src/plastax/phases.py:1310-1425). Spawners, from the pre-phase
+ * state: FIELD_AT_LEAST every live unit with field >= threshold; ARGMAX the
+ * live unit with the largest non-NaN field (lowest id on ties). Parents in
+ * ascending id take the free slots (PRUNED at the start of the phase) in
+ * ascending id; a parent past the last free slot is dropped
+ * (*unit_overflow = 1). A child's slot takes its `reset` defaults, becomes
+ * live, gets level clamp(level[parent] + offset, 1, max_level), and, with
+ * init_dst, init_dst[child] = init_src[parent] * init_scale.
+ * *units_added = children placed. scratch: 2 * num_units int32. One CTA. */
+#define PXB_SPAWN_FIELD_AT_LEAST 0
+#define PXB_SPAWN_ARGMAX 1
+typedef struct pxb_unit_spawn {
+  int32_t kind;
+  const float *field;
+  float threshold;
+  int32_t offset;
+  int32_t max_level;
+  float *init_dst;
+  const float *init_src;
+  float init_scale;
+} pxb_unit_spawn;
+PXB_API int pxb_unit_add(int32_t num_units, const pxb_unit_spawn *spawn, uint8_t *pruned,
+                         int32_t *level, const pxb_unit_columns *reset, int32_t *scratch,
+                         int32_t *units_added, uint8_t *unit_overflow, void *stream);
+
 /* The per-source-level cap (level_cap_scope "source_level",
  * src/plastax/phases.py:4324-4487): over a level-major list idx of n
  * candidates (pxb_select_step with k = n), the first k of every level's

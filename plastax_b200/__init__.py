@@ -18,6 +18,14 @@ from plastax_b200.topo import resort
 from plastax_b200.traits import (
     GRAD_PRE_ACT,
     LOSS_GRAD,
+    AddUnit,
+    AffineUnitUpdate,
+    ArgmaxSpawn,
+    FieldBelowPrune,
+    FieldSpawn,
+    PruneUnit,
+    TraceUnitUpdate,
+    UpdateUnit,
     BackwardPass,
     DestinationThresholdPrune,
     ForwardPass,
@@ -46,6 +54,8 @@ from plastax_b200.types import (
 )
 
 __all__ = [
+    "AddUnit", "AffineUnitUpdate", "ArgmaxSpawn", "FieldBelowPrune", "FieldSpawn", "PruneUnit", "TraceUnitUpdate",
+    "UpdateUnit",
     "ACTIVATION", "DEAD", "FROM_ID", "GRAD_PRE_ACT", "LEVEL", "LOSS_GRAD", "PRUNED", "TO_ID", "WEIGHT",
     "BackwardPass", "DestinationThresholdPrune", "Driver", "FieldSpec", "ForwardPass", "GrowthRemainder", "MSELoss",
     "MagnitudePrune", "MeanFloatFirstRest", "Network", "NetworkBuilder", "NetworkState", "NetworkStatic", "Propagation", "ProposeAddConn",

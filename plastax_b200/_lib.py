@@ -39,6 +39,9 @@ MIRROR_TILE = 2048
 PEER_MAX_LEVELS = 8
 FIXED_FRAC_BITS = 28
 PAIR_ABS_PRODUCT, PAIR_PRODUCT, PAIR_MODULAR, PAIR_MODULAR_PREDICATE = 0, 1, 2, 3
+UNIT_UPDATE_AFFINE, UNIT_UPDATE_TRACE_ABS, UNIT_UPDATE_TRACE = 0, 1, 2
+SPAWN_FIELD_AT_LEAST, SPAWN_ARGMAX = 0, 1
+MAX_UNIT_COLUMNS = 16
 
 
 class Mirror(ctypes.Structure):
@@ -80,6 +83,19 @@ class LoopDesc(ctypes.Structure):
         ("act", c_ptr), ("out_ids", c_ptr), ("n_out", c_i32), ("out_rec", c_ptr), ("overflow", c_ptr),
         ("needs_resort", c_ptr), ("resorts", c_i32), ("status", c_ptr),
     ]
+
+
+class UnitColumns(ctypes.Structure):
+    """`pxb_unit_columns`: unit columns with their default bit patterns."""
+
+    _fields_ = [("count", c_i32), ("cols", c_ptr * 16), ("bytes", c_i32 * 16), ("defaults", ctypes.c_uint32 * 16)]
+
+
+class UnitSpawn(ctypes.Structure):
+    """`pxb_unit_spawn`: an add_unit rule's lowered form."""
+
+    _fields_ = [("kind", c_i32), ("field", c_ptr), ("threshold", c_f32), ("offset", c_i32), ("max_level", c_i32),
+                ("init_dst", c_ptr), ("init_src", c_ptr), ("init_scale", c_f32)]
 
 
 class PxbError(RuntimeError):
@@ -201,6 +217,12 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_loop_build": (c_i32, [c_ptr, c_ptr, ctypes.POINTER(c_ptr)]),
     "pxb_loop_launch": (c_i32, [c_ptr, c_ptr]),
     "pxb_loop_destroy": (c_i32, [c_ptr]),
+    "pxb_unit_update": (c_i32, [c_i32, c_i32, c_ptr, c_ptr, c_f32, c_f32, c_ptr, c_ptr]),
+    "pxb_unit_quantile_scratch_bytes": (c_i32, [c_i32, ctypes.POINTER(c_size)]),
+    "pxb_unit_quantile": (c_i32, [c_i32, c_ptr, c_ptr, c_ptr, c_f32, c_ptr, c_ptr, c_size, c_ptr]),
+    "pxb_unit_prune": (c_i32, [c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
+    "pxb_kill_unit_edges": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr]),
+    "pxb_unit_add": (c_i32, [c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_unit_importance": (c_i32, [c_i32, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr]),
     "pxb_propose_grid": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_i32, c_i32,
                                  c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_ptr]),

@@ -315,6 +315,69 @@ def propose_grid(num_units: int, grids: int, rows: int, cols: int, score: _lib.P
     return src, dst, sc
 
 
+# -- unit lifecycle --------------------------------------------------------
+def unit_columns(cols: Sequence[tuple[torch.Tensor, float | int | bool]]) -> _lib.UnitColumns:
+    """A `pxb_unit_columns` of (column, default) pairs (4-byte float/int32
+    or 1-byte columns); the caller keeps the columns alive."""
+    import struct as _struct
+
+    if len(cols) > _lib.MAX_UNIT_COLUMNS:
+        raise ValueError(f"unit_columns: at most {_lib.MAX_UNIT_COLUMNS} columns, got {len(cols)}")
+    out = _lib.UnitColumns()
+    out.count = len(cols)
+    for k, (col, default) in enumerate(cols):
+        out.cols[k] = col.data_ptr()
+        if col.dtype == torch.float32:
+            out.bytes[k], out.defaults[k] = 4, _struct.unpack("<I", _struct.pack("<f", float(default)))[0]
+        elif col.dtype == torch.int32:
+            out.bytes[k], out.defaults[k] = 4, int(default) & 0xFFFFFFFF
+        elif col.dtype in (torch.uint8, torch.bool, torch.int8):
+            out.bytes[k], out.defaults[k] = 1, int(default) & 0xFF
+        else:
+            raise ValueError(f"unit_columns: unsupported column dtype {col.dtype}")
+    return out
+
+
+def unit_update(kind: int, field: torch.Tensor, *, src: torch.Tensor | None = None, a: float = 1.0, b: float = 0.0,
+                pruned: torch.Tensor | None = None) -> None:
+    call("pxb_unit_update", ctypes.c_int32(field.numel()), ctypes.c_int32(kind), ptr(field), ptr(src), ctypes.c_float(a),
+         ctypes.c_float(b), ptr(pruned), _stream())
+
+
+def unit_quantile_scratch(n: int) -> int:
+    return query_size("pxb_unit_quantile_scratch_bytes", ctypes.c_int32(n))
+
+
+def unit_quantile(field: torch.Tensor, q: float, out: torch.Tensor, *, pruned: torch.Tensor | None = None,
+                  exempt: torch.Tensor | None = None, scratch: torch.Tensor | None = None) -> torch.Tensor:
+    n = field.numel()
+    need = unit_quantile_scratch(n)
+    if scratch is None or scratch.numel() < need:
+        scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=field.device)
+    call("pxb_unit_quantile", ctypes.c_int32(n), ptr(field), ptr(pruned), ptr(exempt), ctypes.c_float(q), ptr(out),
+         ptr(scratch), ctypes.c_size_t(scratch.numel()), _stream())
+    return out
+
+
+def unit_prune(field: torch.Tensor, threshold: torch.Tensor, pruned: torch.Tensor, doomed: torch.Tensor,
+               reset: _lib.UnitColumns, *, exempt: torch.Tensor | None = None) -> None:
+    call("pxb_unit_prune", ctypes.c_int32(field.numel()), ptr(field), ptr(threshold), ptr(exempt), ptr(pruned),
+         ptr(doomed), ctypes.byref(reset), _stream())
+
+
+def kill_unit_edges(b: Bucket, doomed: torch.Tensor, *, free_bitmap: torch.Tensor | None = None,
+                    bitmap_level: torch.Tensor | None = None) -> None:
+    cap = _bucket(b)
+    call("pxb_kill_unit_edges", ctypes.c_int64(cap), ptr(b["from_id"]), ptr(b["to_id"]), ptr(b["dead"]),
+         ctypes.c_int32(doomed.numel()), ptr(doomed), ptr(free_bitmap), ptr(bitmap_level), _stream())
+
+
+def unit_add(spawn: _lib.UnitSpawn, pruned: torch.Tensor, level: torch.Tensor, reset: _lib.UnitColumns,
+             scratch: torch.Tensor, units_added: torch.Tensor, unit_overflow: torch.Tensor) -> None:
+    call("pxb_unit_add", ctypes.c_int32(pruned.numel()), ctypes.byref(spawn), ptr(pruned), ptr(level),
+         ctypes.byref(reset), ptr(scratch), ptr(units_added), ptr(unit_overflow), _stream())
+
+
 def conn_rank_scratch(cap: int, num_units: int) -> int:
     return query_size("pxb_conn_rank_scratch_bytes", ctypes.c_int64(cap), ctypes.c_int32(num_units))
 

@@ -10,10 +10,9 @@ scratch) are allocated once when the StepFn is built; a step allocates
 nothing on the device and never synchronises with the host unless the
 growth rule declares `on_overflow = "error"`.
 
-Phase order: forward, loss, backward, update_conn, prune_conn, add_conn
-(update_unit, prune_unit and add_unit have no engine lowering yet and are
-rejected when the Network class is defined). Fusions, each legal only where
-it cannot change a result:
+Phase order: forward, loss, backward, update_unit, update_conn, prune_unit,
+prune_conn, add_unit (every structural_interval steps), add_conn. Fusions,
+each legal only where it cannot change a result:
 - prune into forward (src/plastax/phases.py:1629-1700, plan_prune_fusion):
   a MagnitudePrune reads only the weight, so it rides on the forward's read
   of every slot when no update_conn writes weights in between;
@@ -42,6 +41,7 @@ from plastax_b200.traits import (
     MagnitudePrune,
     MSELoss,
     Network,
+    AffineUnitUpdate,
     ProposeAddConn,
     ScoreAddConn,
     SoftmaxCrossEntropyLoss,
@@ -122,7 +122,8 @@ class StepFn:
         # The forward reads a destination-grouped mirror of each bucket when
         # no phase rewrites weights in place (the mirror holds its own copy)
         # and any prune rides on the forward sweep.
-        self.use_mirror = net.update_conn is None and (net.prune_conn is None or self.fuse_prune)
+        self.use_mirror = (net.update_conn is None and (net.prune_conn is None or self.fuse_prune)
+                           and net.prune_unit is None)  # unit pruning tombstones edges outside the sweep
         self.mirrors: list | None = None
         self.mirror_chunk_bits: int | None = None  # destination chunk of the mirror (None: the largest allowed)
         self.bitmaps: list[torch.Tensor] | None = None
@@ -149,13 +150,21 @@ class StepFn:
         self.step_dev = torch.zeros(1, dtype=torch.int32, device=device)
         self.graph = None  # a captured CUDA graph of the step body (see capture)
         self.side = None
+        self.unit_lifecycle = net.prune_unit is not None or net.add_unit is not None
+        if self.unit_lifecycle and self.sharded:
+            raise NotImplementedError("the unit lifecycle under Scheme-A has no lowering (single device only, as in "
+                                      "the reference)")
+        if net.add_unit is not None and self.pipeline:
+            raise NotImplementedError("add_unit on a PIPELINE net has no engine lowering (its claim domains are the "
+                                      "static levels)")
         if self.ac is not None:
             self._build_growth()
             # proposals scored by the site RNG alone depend on the levels and
             # the step counter only, never on this step's propagation, prune
             # or update: their selection may overlap the forward sweep (not
             # per-connection proposals, which come from the post-prune arena)
-            if (not self.is_score and self.ac.score in ("uniform", "uniform_q256") and not self.ac.dedupe_live
+            if (not self.is_score and not self.unit_lifecycle and self.ac.score in ("uniform", "uniform_q256")
+                    and not self.ac.dedupe_live
                     and self.ac.proposer != "per_connection" and torch.device(device).type == "cuda"):
                 self.side = torch.cuda.Stream(device=device)
         # ... and, when growth fires every step, the next step's selection
@@ -197,6 +206,8 @@ class StepFn:
         uc = self.net.update_conn
         if uc is not None and uc.scale_field is not None:
             self.opt = uc.struct(state.units[uc.scale_field.name])
+        if self.unit_lifecycle:
+            self._bind_units(state)
         self.step_dev.fill_(state.step)
         self._ahead_ready = False
         self._bound = id(state)
@@ -592,6 +603,96 @@ class StepFn:
             K.backward_update(b, grad, act, None, self.opt, self.opt_cols)
             self.launches += 1
 
+    # -- unit lifecycle (src/plastax/phases.py:1148-1193, :1245-1425) ---------
+    def _bind_units(self, state: NetworkState) -> None:
+        st, net, dev = self.static, self.net, self.dev
+        n = st.num_units
+        specs = {spec.name: spec for spec in st.unit_fields}
+        cols = [(state.units[name], spec.default) for name, spec in specs.items()
+                if name not in (LEVEL.name, PRUNED.name)]
+        self.unit_reset = K.unit_columns(cols)
+        exempt = torch.zeros(n, dtype=torch.uint8, device=dev)
+        io = list(st.input_ids) + list(st.output_ids)
+        if io:
+            exempt[torch.tensor(io, dtype=torch.long, device=dev)] = 1
+        self.unit_exempt = exempt
+        self.unit_doomed = torch.zeros(n, dtype=torch.uint8, device=dev)
+        pu = net.prune_unit
+        if pu is not None:
+            self.unit_thr = torch.full((1,), float(pu.threshold) if pu.threshold is not None else 0.0,
+                                       dtype=torch.float32, device=dev)
+            if pu.quantile is not None:
+                self.unit_q_scratch = torch.empty(max(K.unit_quantile_scratch(n), 1), dtype=torch.uint8, device=dev)
+        au = net.add_unit
+        if au is not None:
+            self.unit_add_scratch = torch.empty(2 * n, dtype=torch.int32, device=dev)
+            self.units_added = torch.zeros((), dtype=torch.int32, device=dev)
+            self.unit_overflow = torch.zeros((), dtype=torch.uint8, device=dev)
+            init_dst = init_src = None
+            scale = 1.0
+            if au.init is not None:
+                from plastax_b200.traits import _field_name
+
+                init_dst = state.units[_field_name(au.init[1])]
+                init_src = state.units[_field_name(au.init[2])]
+                scale = float(au.init[3])
+            kind = _lib.SPAWN_ARGMAX if type(au).__name__ == "ArgmaxSpawn" else _lib.SPAWN_FIELD_AT_LEAST
+            self.unit_spawn = _lib.UnitSpawn(kind, self._unit_col(state, au.field).data_ptr(),
+                                             float(getattr(au, "threshold", 0.0)), int(au.offset),
+                                             int(net.max_levels) - 1, K.ptr(init_dst), K.ptr(init_src), scale)
+
+    @staticmethod
+    def _unit_col(state: NetworkState, f) -> torch.Tensor:
+        from plastax_b200.traits import _field_name
+
+        name = _field_name(f)
+        if name not in state.units:
+            raise ValueError(f"unit rule: the state has no unit field {name!r}")
+        return state.units[name]
+
+    def _update_unit(self, state: NetworkState) -> None:
+        uu = self.net.update_unit
+        if uu is None:
+            return
+        pruned = state.units.get(PRUNED.name)
+        field = self._unit_col(state, uu.field)
+        if isinstance(uu, AffineUnitUpdate):
+            K.unit_update(_lib.UNIT_UPDATE_AFFINE, field, a=uu.scale, b=uu.shift, pruned=pruned)
+        else:
+            kind = _lib.UNIT_UPDATE_TRACE_ABS if uu.absolute else _lib.UNIT_UPDATE_TRACE
+            K.unit_update(kind, field, src=self._unit_col(state, uu.source), a=uu.rate, pruned=pruned)
+        self.launches += 1
+
+    def _prune_unit(self, state: NetworkState) -> None:
+        pu = self.net.prune_unit
+        if pu is None:
+            return
+        pruned = state.units[PRUNED.name]
+        field = self._unit_col(state, pu.field)
+        if pu.quantile is not None:
+            K.unit_quantile(field, float(pu.quantile), self.unit_thr, pruned=pruned, exempt=self.unit_exempt,
+                            scratch=self.unit_q_scratch)
+            self.launches += 3
+        K.unit_prune(field, self.unit_thr, pruned, self.unit_doomed, self.unit_reset, exempt=self.unit_exempt)
+        for i, b in enumerate(state.conns):
+            bm, bm_level = self._bm(i)
+            K.kill_unit_edges(b, self.unit_doomed, free_bitmap=bm, bitmap_level=bm_level)
+        self.launches += 1 + len(state.conns)
+
+    def _add_unit(self, state: NetworkState) -> None:
+        au = self.net.add_unit
+        if au is None:
+            return
+        interval = int(getattr(self.net, "structural_interval", 1))
+        if interval > 1 and state.step % interval != 0:
+            self.units_added.zero_()
+            self.unit_overflow.zero_()
+        else:
+            K.unit_add(self.unit_spawn, state.units[PRUNED.name], state.units[LEVEL.name], self.unit_reset,
+                       self.unit_add_scratch, self.units_added, self.unit_overflow)
+            self.launches += 1
+        state.units_added, state.unit_overflow = self.units_added, self.unit_overflow
+
     def _prune(self, state: NetworkState) -> None:
         pc = self.net.prune_conn
         if pc is None or self.fuse_prune:
@@ -828,8 +929,11 @@ class StepFn:
         self._forward(state)
         self._loss(state, inputs)
         self._backward(state)
+        self._update_unit(state)
         self._update_conn(state)
+        self._prune_unit(state)
         self._prune(state)
+        self._add_unit(state)
         if early:
             torch.cuda.current_stream(self.dev).wait_stream(self.side)
         remainder = self._add_conn(state, selected=early)
@@ -855,6 +959,7 @@ class StepFn:
         self._forward(state)
         self._loss(state, inputs)
         self._backward(state)
+        self._update_unit(state)
         self._update_conn(state)
         self._prune(state)
         remainder = self._add_conn(state, selected=True)
@@ -866,8 +971,10 @@ class StepFn:
         """Whether every step runs the same device work (a CUDA graph can
         replay it): growth fires every step and never raises on overflow."""
         ac = self.ac
-        return ac is None or (ac.trigger == "every_step" and int(getattr(self.net, "structural_interval", 1)) <= 1
-                              and ac.on_overflow != "error")
+        interval = int(getattr(self.net, "structural_interval", 1))
+        if self.net.add_unit is not None and interval > 1:
+            return False
+        return ac is None or (ac.trigger == "every_step" and interval <= 1 and ac.on_overflow != "error")
 
     def capture(self, state: NetworkState, inputs: StepInputs, *, keep_graph: bool = False) -> None:
         """Capture one step of `state` as a CUDA graph; later calls with the

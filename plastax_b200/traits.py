@@ -182,6 +182,88 @@ class ProposeAddConn:
             raise ValueError(f"unknown on_overflow {self.on_overflow!r}")
 
 
+def _field_name(f) -> str:
+    return f if isinstance(f, str) else f.name
+
+
+class UpdateUnit:
+    """Unit update policy (src/plastax/traits.py:254-278): one write per live
+    unit, inputs and outputs included, after the backward pass and before
+    the connection update."""
+
+
+@dataclasses.dataclass(frozen=True)
+class AffineUnitUpdate(UpdateUnit):
+    """field = field * scale + shift (scripts/parity/golden_rules.py:
+    unit_update_v1 is AffineUnitUpdate("activation", 1.0, 0.125))."""
+
+    field: Any
+    scale: float = 1.0
+    shift: float = 0.0
+
+
+@dataclasses.dataclass(frozen=True)
+class TraceUnitUpdate(UpdateUnit):
+    """field = (1 - rate) * field + rate * |source| (or source when
+    `absolute` is False): a running trace such as the examples' activation
+    EMA (examples/upgd.py:113-128)."""
+
+    field: Any
+    source: Any
+    rate: float
+    absolute: bool = True
+
+
+class PruneUnit:
+    """Unit prune policy (src/plastax/traits.py:377-406): the predicate on
+    the pre-phase state; inputs and outputs are never pruned; a pruned unit's
+    columns reset to their defaults (LEVEL kept) and every incident
+    connection is tombstoned."""
+
+
+@dataclasses.dataclass(frozen=True)
+class FieldBelowPrune(PruneUnit):
+    """Prune a unit when u[field] < threshold: a constant, or (quantile q)
+    the value at rank floor(q * m) of the m live non-I/O units' values
+    ascending, computed on the device before the phase
+    (scripts/parity/golden_rules.py: unit_prune_v1 is
+    FieldBelowPrune("activation", threshold=-0.5))."""
+
+    field: Any
+    threshold: float | None = None
+    quantile: float | None = None
+
+
+class AddUnit:
+    """Unit addition policy (src/plastax/traits.py:409-465): live parents
+    spawn one child each into the lowest free slots, ascending parent id; the
+    child's level is clamp(level(parent) + offset, 1, max_levels - 1)."""
+
+
+@dataclasses.dataclass(frozen=True)
+class FieldSpawn(AddUnit):
+    """Every live unit with u[field] >= threshold spawns; `init` is None or
+    ("scale_parent", child_field, parent_field, scale): child_field of the
+    child = parent_field of the parent * scale (golden rules unit_spawn_v1 =
+    FieldSpawn("activation", 0.5, 1), unit_child_init_v1 = ("scale_parent",
+    "activation", "activation", 0.5))."""
+
+    field: Any
+    threshold: float
+    offset: int = 1
+    init: tuple | None = None
+
+
+@dataclasses.dataclass(frozen=True)
+class ArgmaxSpawn(AddUnit):
+    """The live unit with the largest u[field] (lowest id on ties) spawns
+    one child: with structural_interval N, one unit every N steps."""
+
+    field: Any
+    offset: int = 1
+    init: tuple | None = None
+
+
 _SCORE_FORMS = {"abs_product": 3, "product": 3, "grad_act": 1, "modular": 6, "modular_predicate": 5}
 _IMPORTANCE_FORMS = {"abs_field": 2, "field": 2, "modular": 5}
 
@@ -298,11 +380,11 @@ class Network:
     forward_pass: ClassVar[ForwardPass]
     loss: ClassVar[MSELoss | SoftmaxCrossEntropyLoss | None] = None
     backward_pass: ClassVar[BackwardPass | None] = None
-    update_unit: ClassVar[Any] = None
+    update_unit: ClassVar[UpdateUnit | None] = None
     update_conn: ClassVar[Any] = None  # an optimizer bundle (plastax_b200.optim)
-    prune_unit: ClassVar[Any] = None
+    prune_unit: ClassVar[PruneUnit | None] = None
     prune_conn: ClassVar[PruneConn | None] = None
-    add_unit: ClassVar[Any] = None
+    add_unit: ClassVar[AddUnit | None] = None
     add_conn: ClassVar[ProposeAddConn | ScoreAddConn | None] = None
     reset_global: ClassVar[ResetGlobal | None] = None
     propagation: ClassVar[Propagation] = Propagation.TOPOLOGICAL
@@ -310,6 +392,7 @@ class Network:
     extra_conn_fields: ClassVar[tuple[FieldSpec, ...]] = ()
     extra_unit_fields: ClassVar[tuple[FieldSpec, ...]] = ()
     unit_capacity: ClassVar[int | None] = None
+    max_levels: ClassVar[int] = 1024  # a child's level is clamped to [1, max_levels - 1]
     structural_interval: ClassVar[int] = 1
     sharding: ClassVar[ShardSpec | None] = None
     kahn_max_depth: ClassVar[int | None] = None
@@ -337,10 +420,26 @@ class Network:
                     and cls.propagation is Propagation.PIPELINE):
                 raise ValueError('candidates = "shortlist_per_level" is levels-based and so topological-only; '
                                  "PIPELINE networks use the global shortlist")
-        if cls.update_unit is not None or cls.prune_unit is not None or cls.add_unit is not None:
-            raise NotImplementedError(
-                f"{cls.__name__}: unit-lifecycle and update_unit phases have no engine lowering yet"
-            )
+        if cls.update_unit is not None and not isinstance(cls.update_unit, (AffineUnitUpdate, TraceUnitUpdate)):
+            raise NotImplementedError(f"{cls.__name__}: update_unit form has no engine lowering")
+        if cls.prune_unit is not None:
+            pu = cls.prune_unit
+            if not isinstance(pu, FieldBelowPrune):
+                raise NotImplementedError(f"{cls.__name__}: prune_unit form has no engine lowering")
+            if (pu.threshold is None) == (pu.quantile is None):
+                raise ValueError(f"{cls.__name__}: FieldBelowPrune takes exactly one of threshold and quantile")
+            if pu.quantile is not None and not 0.0 <= pu.quantile <= 1.0:
+                raise ValueError(f"{cls.__name__}: FieldBelowPrune quantile must be in [0, 1]")
+        if cls.add_unit is not None:
+            au = cls.add_unit
+            if not isinstance(au, (FieldSpawn, ArgmaxSpawn)):
+                raise NotImplementedError(f"{cls.__name__}: add_unit form has no engine lowering")
+            if au.init is not None and (len(au.init) != 4 or au.init[0] != "scale_parent"):
+                raise NotImplementedError(f"{cls.__name__}: add_unit init {au.init!r} has no engine lowering")
+        if (cls.prune_unit is not None or cls.add_unit is not None) and cls.unit_capacity is None:
+            raise TypeError(f"{cls.__name__}: prune_unit and add_unit require Network.unit_capacity")
+        if int(cls.max_levels) < 2:
+            raise ValueError(f"{cls.__name__}: max_levels must be >= 2")
 
     @classmethod
     def unit_fields(cls) -> tuple[FieldSpec, ...]:

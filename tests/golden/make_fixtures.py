@@ -18,7 +18,8 @@ Writes, next to this script:
   spec (ties, vetoes, windows, every claim model);
 - passes.json: the passes_v1 goldens (exact dyadic forward/backward values);
 - claim_digests.json: the churn configurations and final-state sha256 digests
-  the reference pins its claim to (tests/test_growth_claim.py).
+  the reference pins its claim to (tests/test_growth_claim.py);
+- unit_lifecycle.json: the unit_lifecycle_v1 goldens (update, prune, add).
 """
 
 from __future__ import annotations
@@ -205,6 +206,17 @@ def claim_digests(ref_root: pathlib.Path):
     return out
 
 
+def unit_goldens(ref_root: pathlib.Path):
+    """The unit_lifecycle_v1 goldens (tests/golden/unit_*.json of the
+    reference): initial units and edges, the rules, the expected outcome."""
+    out = []
+    for path in sorted((ref_root / "tests" / "golden").glob("unit_*.json")):
+        doc = json.loads(path.read_text())
+        out.append({k: doc[k] for k in ("name", "capacity", "field_defaults", "max_levels", "rules", "initial_units",
+                                        "initial_edges", "expect")})
+    return out
+
+
 def main() -> int:
     ref_root = pathlib.Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference").resolve()
     ref, emit = _load_spec(ref_root)
@@ -215,6 +227,7 @@ def main() -> int:
     (HERE / "rng_vectors.json").write_text(json.dumps(rng_vectors(ref, rng), indent=0))
     (HERE / "passes.json").write_text(json.dumps(passes, indent=0, default=_f))
     (HERE / "claim_digests.json").write_text(json.dumps(claim_digests(ref_root), indent=1))
+    (HERE / "unit_lifecycle.json").write_text(json.dumps(unit_goldens(ref_root), indent=0))
     print(f"wrote {len(registry)} registry growth cases, {len(passes)} passes goldens")
     return 0
 

@@ -166,7 +166,7 @@ def test_traits_reject_forms_without_a_lowering():
         class Bad5(px.Network):  # noqa: F841
             forward_pass = px.ForwardPass("tanh")
             add_conn = px.ProposeAddConn(proposals_per_proposer=1, max_new_per_level=1, selection="threshold")
-    with pytest.raises(NotImplementedError, match="unit-lifecycle"):
+    with pytest.raises(NotImplementedError, match="prune_unit form"):
         class Bad4(px.Network):  # noqa: F841
             forward_pass = px.ForwardPass("tanh")
             prune_unit = object()

@@ -222,3 +222,79 @@ def test_passes_are_exact(doc):
                 orc.backward_accumulate(bl, grad, n, "sum", acc)
                 orc.unit_apply(n, 1, "relu", "sum", acc, act, seed, level, lv, is_input, None, grad)
             assert [abs(g) for g in grad.tolist()] == [abs(g) for g in st["expect"]["grad_pre_act"]]
+
+
+UNIT_GOLDENS = _load("unit_lifecycle.json")
+
+
+def unit_rules(rules: dict):
+    """The unit_lifecycle_v1 rules (scripts/parity/golden_rules.py:160-199) as
+    the engine's lowered forms."""
+    import plastax_b200 as px
+
+    init = ("scale_parent", "activation", "activation", 0.5) if rules.get("init_unit") == "unit_child_init_v1" else None
+    spawn = {"unit_spawn_v1": 1, "unit_spawn_deep_v1": 30000}
+    return {
+        "update_unit": px.AffineUnitUpdate("activation", 1.0, 0.125) if "update_unit" in rules else None,
+        "prune_unit": px.FieldBelowPrune("activation", threshold=-0.5) if "prune_unit" in rules else None,
+        "add_unit": (px.FieldSpawn("activation", 0.5, spawn[rules["add_unit"]], init) if "add_unit" in rules
+                     else None),
+    }
+
+
+def unit_case_arrays(case):
+    n = case["capacity"]
+    act = np.zeros(n, np.float32)
+    level = np.zeros(n, np.int32)
+    pruned = np.ones(n, np.uint8)
+    exempt = np.zeros(n, bool)
+    for u in case["initial_units"]:
+        i = u["id"]
+        act[i], level[i], pruned[i] = u["fields"]["activation"], u["level"], u["pruned"]
+        exempt[i] = u["is_input"] or u["is_output"]
+    edges = case["initial_edges"]
+    b = {"from_id": np.array([e["src"] for e in edges], np.int32), "to_id": np.array([e["dst"] for e in edges], np.int32),
+         "dead": np.zeros(len(edges), np.uint8),
+         "weight": np.array([e["fields"]["weight"] for e in edges], np.float32)}
+    return act, level, pruned, exempt, b
+
+
+def check_unit_outcome(case, act, level, pruned, live_edges, children=None, overflow=None):
+    want = case["expect"]
+    listed = set()
+    for u in want["units"]:
+        i = u["id"]
+        listed.add(i)
+        assert bool(pruned[i]) == u["pruned"], (case["name"], i)
+        assert int(level[i]) == u["level"], (case["name"], i)
+        assert float(act[i]) == u["fields"]["activation"], (case["name"], i)
+    for i in range(case["capacity"]):
+        if i not in listed:
+            assert pruned[i], (case["name"], i)
+    assert sorted(live_edges) == sorted((e["src"], e["dst"], e["fields"]["weight"]) for e in want["edges"])
+    if children is not None and "children" in want:
+        assert children == want["children"], case["name"]
+    if overflow is not None and "unit_overflow" in want:
+        assert overflow == want["unit_overflow"], case["name"]
+
+
+@pytest.mark.parametrize("case", UNIT_GOLDENS, ids=[c["name"] for c in UNIT_GOLDENS])
+def test_unit_lifecycle_goldens(case):
+    """update_unit, prune_unit (exempt I/O, permanent, incident edges die) and
+    add_unit (lowest free ids, same-step reuse, overflow, level clamp)."""
+    from oracle import units as ou
+
+    act, level, pruned, exempt, b = unit_case_arrays(case)
+    cols = {"activation": act}
+    defaults = {"activation": np.float32(case["field_defaults"]["activation"])}
+    rules = unit_rules(case["rules"])
+    children, overflow = None, None
+    if rules["update_unit"] is not None:
+        ou.update_unit(cols, pruned, rules["update_unit"])
+    if rules["prune_unit"] is not None:
+        ou.prune_unit(cols, pruned, exempt, defaults, [b], rules["prune_unit"])
+    if rules["add_unit"] is not None:
+        children, overflow = ou.add_unit(cols, pruned, level, defaults, rules["add_unit"], case["max_levels"])
+    live = [(int(s), int(d), float(w)) for s, d, w, x in zip(b["from_id"], b["to_id"], b["weight"], b["dead"],
+                                                                strict=True) if x == 0]
+    check_unit_outcome(case, act, level, pruned, live, children, overflow)
