@@ -156,6 +156,21 @@ PXB_API int pxb_prune_conn(int64_t cap, const int32_t *from_id, const int32_t *t
                    uint32_t *free_bitmap, const int32_t *bitmap_level,
                    void *stream);
 
+/* The k-lowest-|w| prune (the lowest-magnitude churn of the benchmark
+ * configurations, as a prune phase): every bucket writes its candidates at
+ * global slots [base, base + cap) of one list -- score -|w| (-inf for a dead
+ * slot), id the global slot -- so the first k of the total order
+ * (pxb_topk_unique with id_bound = the arena's slots) are the k lowest |w|
+ * live edges, ties by ascending slot; pxb_prune_selected then tombstones
+ * those of the bucket (skipping the -inf ones, a NaN weight included) and
+ * adds them to its claim domain's free bitmap. */
+PXB_API int pxb_lowest_keys(int64_t cap, const uint8_t *dead, const float *weight, int64_t base,
+                            float *score_out, int32_t *slot_out, void *stream);
+PXB_API int pxb_prune_selected(int64_t k, const int32_t *idx, const float *score, int64_t base,
+                               int64_t cap, const int32_t *from_id, uint8_t *dead,
+                               int32_t num_units, uint32_t *free_bitmap,
+                               const int32_t *bitmap_level, void *stream);
+
 /* Backward accumulate of one bucket: acc[from[s]] (+)= w[s] * grad[to[s]].
  * Source-major buckets give long source runs: reduced by warp-segmented
  * shuffles, one atomic per run. Replaces src/plastax/sweep.py:113-180

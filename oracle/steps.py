@@ -36,6 +36,23 @@ def init_weight(kind: str, a: float, src: np.ndarray, dst: np.ndarray, salt: int
     return (np.float32(a) * (np.float32(2.0) * u - np.float32(1.0))).astype(np.float32)
 
 
+def lowest_prune(buckets: list[dict], k: int) -> int:
+    """Tombstone the k live edges of lowest |w| over the buckets in order
+    (ties by ascending global slot; NaN weights never selected), in place;
+    returns the number pruned. The engine's LowestMagnitudePrune."""
+    w = np.concatenate([np.abs(b["weight"].astype(np.float32)) for b in buckets])
+    live = np.concatenate([b["dead"] == 0 for b in buckets]) & ~np.isnan(w)
+    slots = np.flatnonzero(live)
+    order = slots[np.lexsort((slots, w[slots]))][:k]
+    base = 0
+    for b in buckets:
+        cap = b["dead"].size
+        sel = order[(order >= base) & (order < base + cap)] - base
+        b["dead"][sel] = 1
+        base += cap
+    return int(order.size)
+
+
 class ReservoirOracle:
     """The reservoir churn step (PIPELINE: forward, prune, per-unit
     proposal growth with a step-scoped cap, pipeline claim) on host arrays."""

@@ -19,6 +19,7 @@ from plastax_b200.traits import (
     GRAD_PRE_ACT,
     LOSS_GRAD,
     AddUnit,
+    LowestMagnitudePrune,
     AffineUnitUpdate,
     ArgmaxSpawn,
     FieldBelowPrune,
@@ -54,7 +55,7 @@ from plastax_b200.types import (
 )
 
 __all__ = [
-    "AddUnit", "AffineUnitUpdate", "ArgmaxSpawn", "FieldBelowPrune", "FieldSpawn", "PruneUnit", "TraceUnitUpdate",
+    "AddUnit", "AffineUnitUpdate", "LowestMagnitudePrune", "ArgmaxSpawn", "FieldBelowPrune", "FieldSpawn", "PruneUnit", "TraceUnitUpdate",
     "UpdateUnit",
     "ACTIVATION", "DEAD", "FROM_ID", "GRAD_PRE_ACT", "LEVEL", "LOSS_GRAD", "PRUNED", "TO_ID", "WEIGHT",
     "BackwardPass", "DestinationThresholdPrune", "Driver", "FieldSpec", "ForwardPass", "GrowthRemainder", "MSELoss",

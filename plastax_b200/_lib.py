@@ -217,6 +217,8 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_loop_build": (c_i32, [c_ptr, c_ptr, ctypes.POINTER(c_ptr)]),
     "pxb_loop_launch": (c_i32, [c_ptr, c_ptr]),
     "pxb_loop_destroy": (c_i32, [c_ptr]),
+    "pxb_lowest_keys": (c_i32, [c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr]),
+    "pxb_prune_selected": (c_i32, [c_i64, c_ptr, c_ptr, c_i64, c_i64, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr]),
     "pxb_unit_update": (c_i32, [c_i32, c_i32, c_ptr, c_ptr, c_f32, c_f32, c_ptr, c_ptr]),
     "pxb_unit_quantile_scratch_bytes": (c_i32, [c_i32, ctypes.POINTER(c_size)]),
     "pxb_unit_quantile": (c_i32, [c_i32, c_ptr, c_ptr, c_ptr, c_f32, c_ptr, c_ptr, c_size, c_ptr]),

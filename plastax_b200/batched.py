@@ -21,7 +21,14 @@ from plastax_b200 import _lib
 from plastax_b200 import kernels as K
 from plastax_b200.state import NetworkState, NetworkStatic
 from plastax_b200.step import StepFn, StepInputs, StepResult
-from plastax_b200.traits import DestinationThresholdPrune, MagnitudePrune, MSELoss, Network, SoftmaxCrossEntropyLoss
+from plastax_b200.traits import (
+    DestinationThresholdPrune,
+    LowestMagnitudePrune,
+    MagnitudePrune,
+    MSELoss,
+    Network,
+    SoftmaxCrossEntropyLoss,
+)
 from plastax_b200.types import ACTIVATION, LEVEL
 
 
@@ -80,6 +87,9 @@ class BatchedStepFn:
     def _prune(self, state: NetworkState) -> None:
         pc = self.net.prune_conn
         if pc is None:
+            return
+        if isinstance(pc, LowestMagnitudePrune):
+            self.inner._prune_lowest(state, pc)
             return
         n = self.static.num_units
         for i, b in enumerate(state.conns):

@@ -574,3 +574,61 @@ extern "C" int pxb_mse_loss(int32_t num_outputs, const int32_t *output_ids, cons
   PXB_LAUNCHED("mse_loss_kernel");
   return PXB_OK;
 }
+
+// ---------------------------------------------------------------------------
+// lowest-|w| prune: keys for the selection, then the selected slots
+// ---------------------------------------------------------------------------
+namespace pxb {
+
+// Candidate s of the bucket at global slot base + s: score -|w| (a dead
+// slot -inf), id its global slot, so the total order's first k are the k
+// lowest |w| with ties by ascending slot.
+__global__ void lowest_keys_kernel(int64_t cap, const uint8_t *__restrict__ dead, const float *__restrict__ w,
+                                   int64_t base, float *__restrict__ score, int32_t *__restrict__ slot) {
+  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < cap;
+       s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    score[base + s] = dead[s] ? -__int_as_float(0x7f800000) : -fabsf(w[s]);
+    slot[base + s] = static_cast<int32_t>(base + s);
+  }
+}
+
+__global__ void prune_selected_kernel(int64_t k, const int32_t *__restrict__ idx, const float *__restrict__ score,
+                                      int64_t base, int64_t cap, const int32_t *__restrict__ from,
+                                      uint8_t *__restrict__ dead, uint32_t n, PruneArgs pa) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < k;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t g = idx[i];
+    if (g < base || g >= base + cap) continue;
+    if (!(score[g] > -__int_as_float(0x7f800000))) continue;  // a dead slot (or NaN weight) is not selected
+    const int64_t s = g - base;
+    if (dead[s]) continue;
+    dead[s] = 1;
+    mark_free(pa, s, pa.bm_level ? from[s] : 0, n);
+  }
+}
+
+}  // namespace pxb
+
+extern "C" int pxb_lowest_keys(int64_t cap, const uint8_t *dead, const float *weight, int64_t base, float *score_out,
+                               int32_t *slot_out, void *stream) {
+  PXB_REQUIRE(cap >= 0 && base >= 0 && base + cap < (int64_t(1) << 31), "pxb_lowest_keys: slots out of range");
+  if (cap == 0) return PXB_OK;
+  PXB_REQUIRE(dead && weight && score_out && slot_out, "pxb_lowest_keys: a pointer is NULL");
+  pxb::lowest_keys_kernel<<<pxb::grid_for(cap, 256, 8), 256, 0, pxb::as_stream(stream)>>>(cap, dead, weight, base,
+                                                                                         score_out, slot_out);
+  PXB_LAUNCHED("lowest_keys_kernel");
+  return PXB_OK;
+}
+
+extern "C" int pxb_prune_selected(int64_t k, const int32_t *idx, const float *score, int64_t base, int64_t cap,
+                                  const int32_t *from_id, uint8_t *dead, int32_t num_units, uint32_t *free_bitmap,
+                                  const int32_t *bitmap_level, void *stream) {
+  PXB_REQUIRE(k >= 0 && cap >= 0 && base >= 0, "pxb_prune_selected: sizes out of range");
+  if (k == 0 || cap == 0) return PXB_OK;
+  PXB_REQUIRE(idx && score && from_id && dead, "pxb_prune_selected: a pointer is NULL");
+  pxb::PruneArgs pa{PXB_PRUNE_NONE, 0.0f, nullptr, dead, true, -1, nullptr, free_bitmap, (cap + 31) / 32, bitmap_level};
+  pxb::prune_selected_kernel<<<pxb::grid_for(k, 256, 4), 256, 0, pxb::as_stream(stream)>>>(
+      k, idx, score, base, cap, from_id, dead, static_cast<uint32_t>(num_units), pa);
+  PXB_LAUNCHED("prune_selected_kernel");
+  return PXB_OK;
+}

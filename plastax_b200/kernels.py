@@ -315,6 +315,19 @@ def propose_grid(num_units: int, grids: int, rows: int, cols: int, score: _lib.P
     return src, dst, sc
 
 
+def lowest_keys(b: Bucket, base: int, score: torch.Tensor, slot: torch.Tensor) -> None:
+    cap = _bucket(b)
+    call("pxb_lowest_keys", ctypes.c_int64(cap), ptr(b["dead"]), ptr(b["weight"]), ctypes.c_int64(base), ptr(score),
+         ptr(slot), _stream())
+
+
+def prune_selected(b: Bucket, k: int, idx: torch.Tensor, score: torch.Tensor, base: int, num_units: int, *,
+                   free_bitmap: torch.Tensor | None = None, bitmap_level: torch.Tensor | None = None) -> None:
+    cap = _bucket(b)
+    call("pxb_prune_selected", ctypes.c_int64(k), ptr(idx), ptr(score), ctypes.c_int64(base), ctypes.c_int64(cap),
+         ptr(b["from_id"]), ptr(b["dead"]), ctypes.c_int32(num_units), ptr(free_bitmap), ptr(bitmap_level), _stream())
+
+
 # -- unit lifecycle --------------------------------------------------------
 def unit_columns(cols: Sequence[tuple[torch.Tensor, float | int | bool]]) -> _lib.UnitColumns:
     """A `pxb_unit_columns` of (column, default) pairs (4-byte float/int32

@@ -42,6 +42,7 @@ from plastax_b200.traits import (
     MSELoss,
     Network,
     AffineUnitUpdate,
+    LowestMagnitudePrune,
     ProposeAddConn,
     ScoreAddConn,
     SoftmaxCrossEntropyLoss,
@@ -151,6 +152,9 @@ class StepFn:
         self.graph = None  # a captured CUDA graph of the step body (see capture)
         self.side = None
         self.unit_lifecycle = net.prune_unit is not None or net.add_unit is not None
+        if isinstance(net.prune_conn, LowestMagnitudePrune) and self.sharded:
+            raise NotImplementedError("the lowest-|w| prune under Scheme-A has no lowering (its selection spans "
+                                      "every rank's band)")
         if self.unit_lifecycle and self.sharded:
             raise NotImplementedError("the unit lifecycle under Scheme-A has no lowering (single device only, as in "
                                       "the reference)")
@@ -698,6 +702,9 @@ class StepFn:
         if pc is None or self.fuse_prune:
             return
         n = self.static.num_units
+        if isinstance(pc, LowestMagnitudePrune):
+            self._prune_lowest(state, pc)
+            return
         for i, b in enumerate(state.conns):
             bm, bm_level = self._bm(i)
             if isinstance(pc, MagnitudePrune):
@@ -707,6 +714,37 @@ class StepFn:
                 K.prune_conn(b, n, prune_kind=_lib.PRUNE_ABS_BELOW_DST, unit_threshold=state.units[pc.field.name],
                              free_bitmap=bm, bitmap_level=bm_level)
             self.launches += 1
+
+    def _prune_lowest(self, state: NetworkState, pc: LowestMagnitudePrune) -> None:
+        """The k live edges of lowest |w| (ties by ascending slot, buckets in
+        order) are tombstoned, on the steps `pc.every` divides."""
+        if pc.every > 1 and state.step % pc.every != 0:
+            return
+        st = self.static
+        caps = [int(b["dead"].numel()) for b in state.conns]
+        total = sum(caps)
+        k = min(int(pc.k), total)
+        if k == 0:
+            return
+        if getattr(self, "_low_score", None) is None or self._low_score.numel() != total:
+            self._low_score = torch.empty(max(total, 1), dtype=torch.float32, device=self.dev)
+            self._low_slot = torch.empty(max(total, 1), dtype=torch.int32, device=self.dev)
+            self._low_idx = torch.empty(max(k, 1), dtype=torch.int32, device=self.dev)
+            self._low_scratch = torch.empty(max(K.topk_unique_scratch(total, k, total), 1), dtype=torch.uint8,
+                                            device=self.dev)
+        base = 0
+        for b, cap in zip(state.conns, caps, strict=True):
+            K.lowest_keys(b, base, self._low_score, self._low_slot)
+            base += cap
+        K.topk_unique(self._low_score[:total], self._low_slot[:total], total, k, out=self._low_idx,
+                      scratch=self._low_scratch)
+        base = 0
+        for i, (b, cap) in enumerate(zip(state.conns, caps, strict=True)):
+            bm, bm_level = self._bm(i)
+            K.prune_selected(b, k, self._low_idx, self._low_score, base, st.num_units, free_bitmap=bm,
+                             bitmap_level=bm_level)
+            base += cap
+        self.launches += 2 * len(caps) + 4
 
     def _fires(self, state: NetworkState) -> bool:
         ac = self.ac
@@ -973,6 +1011,8 @@ class StepFn:
         ac = self.ac
         interval = int(getattr(self.net, "structural_interval", 1))
         if self.net.add_unit is not None and interval > 1:
+            return False
+        if isinstance(self.net.prune_conn, LowestMagnitudePrune) and self.net.prune_conn.every > 1:
             return False
         return ac is None or (ac.trigger == "every_step" and interval <= 1 and ac.on_overflow != "error")
 

@@ -128,6 +128,21 @@ class DestinationThresholdPrune(PruneConn):
         self.field = field
 
 
+class LowestMagnitudePrune(PruneConn):
+    """Prune the k live connections of lowest |weight| (ties by ascending
+    slot, buckets in order), on the steps `every` divides: the
+    lowest-magnitude churn of the dynamic-sparse-training configurations
+    (the reference states it as a predicate against a threshold the host
+    computes into the globals; here the selection runs on the device and
+    prunes exactly min(k, live) edges). A NaN weight is never selected."""
+
+    def __init__(self, k: int, every: int = 1) -> None:
+        if int(k) < 0 or int(every) < 1:
+            raise ValueError("LowestMagnitudePrune: k must be >= 0 and every >= 1")
+        self.k = int(k)
+        self.every = int(every)
+
+
 class ResetGlobal:
     """Globals reset (src/plastax/traits.py:686-703); host-side, O(1)."""
 
@@ -412,7 +427,8 @@ class Network:
                 raise ValueError(f"{cls.__name__}: unknown backward activation {bp.activation!r}")
             if bp.combine.lowered() != "sum":
                 raise NotImplementedError(f"{cls.__name__}: the backward combine must be sum")
-        if cls.prune_conn is not None and not isinstance(cls.prune_conn, (MagnitudePrune, DestinationThresholdPrune)):
+        if cls.prune_conn is not None and not isinstance(cls.prune_conn, (MagnitudePrune, DestinationThresholdPrune,
+                                                                          LowestMagnitudePrune)):
             raise NotImplementedError(f"{cls.__name__}: prune_conn form has no engine lowering")
         if cls.add_conn is not None:
             cls.add_conn.validate()
