@@ -201,9 +201,17 @@ PXB_API int pxb_backward_update(int64_t cap, const int32_t *from_id,
  * pxb_unit_apply reads. */
 #define PXB_FIXED_FRAC_BITS 28
 
+/* Activation codes of the apply entry points: the low byte is a
+ * PXB_ACT_* kind; a non-zero second byte, kind + 1, is the kind of the
+ * output units instead (a linear readout under tanh units: PXB_ACT_TANH |
+ * ((PXB_ACT_IDENTITY + 1) << 8)). The `is_input` argument of the apply
+ * entry points is a unit role column: 0 hidden, 1 input (skipped), 2
+ * output. */
+#define PXB_ACT_CODE(kind, output_kind) ((kind) | (((output_kind) + 1) << 8))
+
 /* Unit apply with masked merge (src/plastax/sweep.py:183-230):
  * a unit i is finalized iff (level == NULL || level[i] == target_level)
- *   && (is_input == NULL || !is_input[i]) && (pruned == NULL || !pruned[i]).
+ *   && (is_input == NULL || is_input[i] != 1) && (pruned == NULL || !pruned[i]).
  * The accumulated value x[i] = acc[i], or, when acc_fixed is not NULL,
  * acc_fixed[i] rounded to float and scaled by 2^-PXB_FIXED_FRAC_BITS (one
  * rounding), plus acc[i] as a float (the side accumulator, 0 unless a

@@ -48,10 +48,21 @@ def _segment(idx: np.ndarray, vals: np.ndarray, n: int) -> np.ndarray:
 
 
 def batched_step(buckets: list[dict], level: np.ndarray, is_input: np.ndarray, input_ids, output_ids,
-                 x: np.ndarray, t: np.ndarray, *, fwd_act: str, bwd_act: str, loss: str, opt: dict) -> dict:
+                 x: np.ndarray, t: np.ndarray, *, fwd_act: str, bwd_act: str, loss: str, opt: dict,
+                 out_act: str | None = None) -> dict:
     """One batched step; `buckets` are updated in place. Returns the batch
-    loss and the reduced activation / grad / seed columns."""
+    loss and the reduced activation / grad / seed columns. `out_act` is the
+    output units' activation (and derivative) when it differs."""
     n = level.size
+    is_out = np.zeros(n, bool)
+    if out_act is not None:
+        is_out[np.asarray(output_ids)] = True
+
+    def fwd(sel, v):
+        return np.where(is_out[sel][:, None], act_fn(out_act or fwd_act, v), act_fn(fwd_act, v)).astype(F32)
+
+    def prime(sel, a):
+        return np.where(is_out[sel][:, None], act_prime(out_act or bwd_act, a), act_prime(bwd_act, a)).astype(F32)
     B = x.shape[0]
     L = len(buckets)
     act = np.zeros((n, B), F32)
@@ -63,7 +74,7 @@ def batched_step(buckets: list[dict], level: np.ndarray, is_input: np.ndarray, i
         f, d, w = b["from_id"][live], b["to_id"][live], b["weight"][live]
         acc = (acc.astype(np.float64) + _segment(d, w[:, None] * act[f], n)).astype(F32)
         sel = (level == lv + 1) & applyable
-        act[sel] = act_fn(fwd_act, acc[sel])
+        act[sel] = fwd(sel, acc[sel])
         acc[sel] = 0
     out = np.asarray(output_ids)
     seed = np.zeros((n, B), F32)
@@ -97,14 +108,14 @@ def batched_step(buckets: list[dict], level: np.ndarray, is_input: np.ndarray, i
     batch_loss = F32(tot / F32(B))
     grad = np.zeros((n, B), F32)
     sel = (level == L) & applyable
-    grad[sel] = ((seed[sel]) * act_prime(bwd_act, act[sel])).astype(F32)
+    grad[sel] = ((seed[sel]) * prime(sel, act[sel])).astype(F32)
     for lv in range(L - 1, 0, -1):
         b = buckets[lv]
         live = b["dead"] == 0
         f, d, w = b["from_id"][live], b["to_id"][live], b["weight"][live]
         acc = _segment(f, w[:, None] * grad[d], n)
         sel = (level == lv) & applyable
-        grad[sel] = ((acc[sel] + seed[sel]) * act_prime(bwd_act, act[sel])).astype(F32)
+        grad[sel] = ((acc[sel] + seed[sel]) * prime(sel, act[sel])).astype(F32)
     for b in buckets:
         live = b["dead"] == 0
         f, d = b["from_id"][live], b["to_id"][live]

@@ -96,3 +96,34 @@ class ReservoirOracle:
             grow = np.concatenate([grow, np.zeros(pad, np.uint8)])
         self.last_counts, _, self.tail = orc.claim_pipeline(b, self.level, self.tail, cs, cd, cw, grow)
         self.step_count += 1
+
+
+class EsnOracle:
+    """The ESN step (PIPELINE): inputs scattered, one forward sweep from the
+    previous activations (sum accumulated in double, rounded once), tanh on
+    the reservoir and identity on the readout, the MSE seed on the readout,
+    then LMS on every live edge (w -= lr * seed[dst] * act[src]; zero seed
+    on every other unit, an exact no-op there)."""
+
+    def __init__(self, bucket: dict, act: np.ndarray, *, input_id: int, output_id: int, lr: float) -> None:
+        self.b, self.act = bucket, act
+        self.n = act.size
+        self.input_id, self.output_id, self.lr = input_id, output_id, lr
+        self.seed = np.zeros(self.n, np.float32)
+        self.skip = np.zeros(self.n, np.uint8)
+        self.skip[[input_id, output_id]] = 1
+
+    def step(self, x: float, target: float) -> float:
+        n = self.n
+        self.act[self.input_id] = np.float32(x)
+        acc = np.zeros(n, np.float32)
+        orc.forward_accumulate(self.b, self.act, n, "sum", acc)
+        new = self.act.copy()
+        orc.unit_apply(n, 0, "tanh", "sum", acc, None, None, None, 0, self.skip, None, new)
+        new[self.output_id] = acc[self.output_id]
+        self.act = new
+        err = np.float32(new[self.output_id] - np.float32(target))
+        self.seed[:] = 0
+        self.seed[self.output_id] = err
+        orc.update_conn(self.b, self.seed, self.act, n, dict(kind="sgd", lr=self.lr))
+        return float(np.float32(np.float32(0.5) * err * err))

@@ -44,6 +44,15 @@ SPAWN_FIELD_AT_LEAST, SPAWN_ARGMAX = 0, 1
 MAX_UNIT_COLUMNS = 16
 
 
+def act_code(kind) -> int:
+    """An apply entry point's activation code: a kind name, or a (kind,
+    output kind) pair whose second kind applies to the output units."""
+    if isinstance(kind, tuple):
+        base, out = kind
+        return ACT[base] if out is None else ACT[base] | ((ACT[out] + 1) << 8)
+    return ACT[kind]
+
+
 class Mirror(ctypes.Structure):
     """`pxb_mirror`: the destination-grouped index of one bucket."""
 

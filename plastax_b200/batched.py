@@ -115,7 +115,7 @@ class BatchedStepFn:
         self.acc_b.zero_()
         for lv in range(L):
             K.batched_forward(state.conns[lv], self.act_b, self.acc_b)
-            K.batched_unit_apply(self.acc_b, self.act_b, mode=0, act_kind=fp.activation, level=level,
+            K.batched_unit_apply(self.acc_b, self.act_b, mode=0, act_kind=inner.fwd_act, level=level,
                                  target_level=lv + 1, is_input=is_input)
             self.launches += 2
         # loss, per sample; the batch mean to StepResult.loss
@@ -134,11 +134,11 @@ class BatchedStepFn:
         bp = net.backward_pass
         if bp is not None:
             self.acc_b.zero_()
-            K.batched_unit_apply(self.acc_b, self.grad_b, mode=1, act_kind=bp.activation, act=self.act_b,
+            K.batched_unit_apply(self.acc_b, self.grad_b, mode=1, act_kind=inner.bwd_act, act=self.act_b,
                                  seed=self.seed_b, level=level, target_level=L, is_input=is_input)
             for lv in range(L - 1, 0, -1):
                 K.batched_backward(state.conns[lv], self.grad_b, self.acc_b)
-                K.batched_unit_apply(self.acc_b, self.grad_b, mode=1, act_kind=bp.activation, act=self.act_b,
+                K.batched_unit_apply(self.acc_b, self.grad_b, mode=1, act_kind=inner.bwd_act, act=self.act_b,
                                      seed=self.seed_b, level=level, target_level=lv, is_input=is_input)
                 self.launches += 2
         # the exact batch-mean connection update (src/plastax/phases.py:434-483)

@@ -116,3 +116,70 @@ def build_reservoir(cfg: ReservoirConfig, device: torch.device | str = "cuda", *
         shard_rank=shard_rank, device=device)
     del src, dst, w
     return net, static, state
+
+
+@dataclasses.dataclass(frozen=True)
+class EsnConfig:
+    """The streaming echo-state reservoir (the reference's CPU-runnable
+    configuration; examples/echo_state_network.py): one input unit, `units`
+    tanh reservoir units with recurrent fan-in 16 from uniform sources
+    without self-loops, weights N(0, 1/16) rescaled to spectral radius `rho`,
+    every reservoir unit fed by the input with weight U(-1, 1), and one
+    linear readout unit fed by every reservoir unit (weights start at 0),
+    trained online by LMS (SGD on the MSE seed) to reproduce the input
+    delayed `delay` steps."""
+
+    units: int = 1024
+    fan_in: int = 16
+    rho: float = 0.9
+    lr: float = 1e-3
+    delay: int = 5
+    seed: int = 0
+
+
+C1 = EsnConfig()
+
+
+def esn_net(cfg: EsnConfig) -> type[Network]:
+    from plastax_b200 import optim
+    from plastax_b200.traits import LOSS_GRAD, MSELoss
+
+    class EchoStateNetwork(Network):
+        forward_pass = ForwardPass("tanh", monoid.sum_, output_activation="identity")
+        loss = MSELoss()
+        update_conn = optim.sgd(cfg.lr, grad_field=LOSS_GRAD)
+        propagation = Propagation.PIPELINE
+        seed = cfg.seed
+
+    return EchoStateNetwork
+
+
+def esn_edges(cfg: EsnConfig):
+    """(src, dst, weight) numpy arrays of the ESN, seeded (the spectral
+    radius from the dense eigenvalues of the recurrent matrix)."""
+    import numpy as np
+
+    rng = np.random.default_rng(cfg.seed)
+    n = cfg.units
+    res = np.arange(n) + 1  # unit 0 is the input, n + 1 the readout
+    rec_dst = np.repeat(res, cfg.fan_in)
+    off = rng.integers(1, n, rec_dst.size)  # a uniform source other than the destination
+    rec_src = (rec_dst - 1 + off) % n + 1
+    rec_w = rng.standard_normal(rec_dst.size) / math.sqrt(cfg.fan_in)
+    dense = np.zeros((n, n))
+    np.add.at(dense, (rec_dst - 1, rec_src - 1), rec_w)
+    radius = float(np.max(np.abs(np.linalg.eigvals(dense))))
+    rec_w = rec_w * (cfg.rho / radius)
+    in_w = rng.uniform(-1.0, 1.0, n)
+    src = np.concatenate([rec_src, np.zeros(n, np.int64), res])
+    dst = np.concatenate([rec_dst, res, np.full(n, n + 1)])
+    w = np.concatenate([rec_w, in_w, np.zeros(n)]).astype(np.float32)
+    return src.astype(np.int32), dst.astype(np.int32), w
+
+
+def build_esn(cfg: EsnConfig = C1, device: torch.device | str = "cuda"):
+    net = esn_net(cfg)
+    src, dst, w = esn_edges(cfg)
+    static, state = NetworkBuilder.from_edges(net, cfg.units + 2, src, dst, weights=w, input_ids=(0,),
+                                              output_ids=(cfg.units + 1,), device=device)
+    return net, static, state

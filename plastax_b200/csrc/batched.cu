@@ -236,13 +236,15 @@ __global__ void batched_apply_kernel(int32_t n, int32_t batch, int mode, int act
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int32_t u = static_cast<int32_t>(i / batch);
     if (level != nullptr && level[u] != target_level) continue;
-    if (is_input != nullptr && is_input[u]) continue;
+    const uint8_t role = is_input != nullptr ? is_input[u] : 0;
+    if (role == 1) continue;
+    const int kind = unit_act_kind(act_kind, role);
     const float a = acc[i];
     if (mode == 0) {
-      out[i] = act_fn(act_kind, a);
+      out[i] = act_fn(kind, a);
     } else {
       const float sd = seed != nullptr ? seed[i] : 0.0f;
-      out[i] = __fmul_rn(__fadd_rn(a, sd), act_prime_from_act(act_kind, act[i]));
+      out[i] = __fmul_rn(__fadd_rn(a, sd), act_prime_from_act(kind, act[i]));
     }
     acc[i] = 0.0f;
   }
@@ -399,7 +401,7 @@ extern "C" int pxb_batched_unit_apply(int32_t num_units, int32_t batch, int32_t 
                                       int32_t target_level, const uint8_t *is_input, float *out, void *stream) {
   PXB_REQUIRE(num_units >= 0 && batch >= 1, "pxb_batched_unit_apply: bad sizes");
   PXB_REQUIRE(mode == 0 || mode == 1, "pxb_batched_unit_apply: mode must be 0 (forward) or 1 (backward)");
-  PXB_REQUIRE(act_kind >= 0 && act_kind <= 3, "pxb_batched_unit_apply: unknown activation %d", act_kind);
+  PXB_REQUIRE(act_code_ok(act_kind), "pxb_batched_unit_apply: unknown activation code %d", act_kind);
   if (num_units == 0) return PXB_OK;
   PXB_REQUIRE(acc && out && (mode == 0 || act), "pxb_batched_unit_apply: a pointer is NULL");
   const int64_t total = int64_t(num_units) * batch;

@@ -106,7 +106,8 @@ __global__ void __launch_bounds__(256) scheme_a_apply_kernel(PeerK g, int32_t n,
     const int32_t lo = g.rank * per;
     const int32_t hi = lo + per < n ? lo + per : n;
     for (int32_t u = lo + blockIdx.x * blockDim.x + threadIdx.x; u < hi; u += gridDim.x * blockDim.x) {
-      if ((is_input != nullptr && is_input[u]) || (pruned != nullptr && pruned[u])) continue;
+      const uint8_t role = is_input != nullptr ? is_input[u] : 0;
+      if (role == 1 || (pruned != nullptr && pruned[u])) continue;
       long long f = 0;
       float side = 0.0f;
       for (int q = 0; q < g.world; ++q) {
@@ -114,7 +115,7 @@ __global__ void __launch_bounds__(256) scheme_a_apply_kernel(PeerK g, int32_t n,
         side = __fadd_rn(side, g.acc_side[q][u]);
       }
       const float x = f != 0 ? __fadd_rn(__fmul_rn(__ll2float_rn(f), kFixUnitP), side) : side;
-      const float a = act_fn(act_kind, x);
+      const float a = act_fn(unit_act_kind(act_kind, role), x);
       for (int q = 0; q < g.world; ++q) g.act[q][u] = a;
     }
   }
@@ -187,7 +188,7 @@ extern "C" int pxb_scheme_a_apply(const pxb_peer_group *group, int32_t num_units
                   group->status,
               "pxb_scheme_a_apply: a group array is NULL");
   PXB_REQUIRE(num_units >= 0, "pxb_scheme_a_apply: negative num_units");
-  PXB_REQUIRE(act_kind >= 0 && act_kind <= 3, "pxb_scheme_a_apply: unknown activation %d", act_kind);
+  PXB_REQUIRE(act_code_ok(act_kind), "pxb_scheme_a_apply: unknown activation code %d", act_kind);
   PXB_REQUIRE(wait_polls >= 1, "pxb_scheme_a_apply: wait_polls must be >= 1");
   PXB_REQUIRE(level_counts == nullptr ||
                   (group->counts && level_before && level_totals && num_levels >= 1 && num_levels <= kPeerMaxLevels),

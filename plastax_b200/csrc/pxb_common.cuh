@@ -101,6 +101,18 @@ __device__ __forceinline__ float combine2(float a, float b) {
 // ---------------------------------------------------------------------------
 // unit activation functions and their derivative from the activation value
 // ---------------------------------------------------------------------------
+// A unit's activation kind from an apply's `act_kind` code and the unit's
+// role (0 hidden, 1 input, 2 output): the code's low byte is the kind, and a
+// non-zero second byte (kind + 1) overrides it for output units.
+__device__ __forceinline__ int unit_act_kind(int32_t code, uint8_t role) {
+  const int out = (code >> 8) & 0xff;
+  return (role == 2 && out != 0) ? out - 1 : (code & 0xff);
+}
+
+__host__ __device__ __forceinline__ bool act_code_ok(int32_t code) {
+  return code >= 0 && (code & 0xff) <= 3 && ((code >> 8) & 0xff) <= 4 && (code >> 16) == 0;
+}
+
 __device__ __forceinline__ float act_fn(int kind, float x) {
   switch (kind) {
     case PXB_ACT_TANH: return tanhf(x);

@@ -307,7 +307,8 @@ __global__ void unit_apply_kernel(int32_t n, int mode, int act_kind, int monoid,
   const int32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   if (level != nullptr && level[i] != target_level) return;
-  if (is_input != nullptr && is_input[i]) return;
+  const uint8_t role = is_input != nullptr ? is_input[i] : 0;
+  if (role == 1) return;
   if (pruned != nullptr && pruned[i]) return;
   float a = acc[i];
   if (acc_fixed != nullptr) {
@@ -320,10 +321,10 @@ __global__ void unit_apply_kernel(int32_t n, int mode, int act_kind, int monoid,
     }
   }
   if (mode == 0) {
-    out[i] = act_fn(act_kind, a);
+    out[i] = act_fn(unit_act_kind(act_kind, role), a);
   } else {
     const float s = seed != nullptr ? seed[i] : 0.0f;
-    out[i] = __fmul_rn(__fadd_rn(a, s), act_prime_from_act(act_kind, act[i]));
+    out[i] = __fmul_rn(__fadd_rn(a, s), act_prime_from_act(unit_act_kind(act_kind, role), act[i]));
   }
   acc[i] = monoid_identity(monoid);
 }
@@ -553,7 +554,7 @@ extern "C" int pxb_unit_apply(int32_t num_units, int32_t mode, int32_t act_kind,
                               const uint8_t *is_input, const uint8_t *pruned, float *out, void *stream) {
   PXB_REQUIRE(num_units >= 0, "pxb_unit_apply: negative num_units");
   PXB_REQUIRE(mode == 0 || mode == 1, "pxb_unit_apply: mode must be 0 (forward) or 1 (backward)");
-  PXB_REQUIRE(act_kind >= 0 && act_kind <= 3, "pxb_unit_apply: unknown activation %d", act_kind);
+  PXB_REQUIRE(act_code_ok(act_kind), "pxb_unit_apply: unknown activation code %d", act_kind);
   PXB_REQUIRE(monoid >= 0 && monoid <= 2, "pxb_unit_apply: unknown monoid %d", monoid);
   if (num_units == 0) return PXB_OK;
   PXB_REQUIRE(acc && out, "pxb_unit_apply: acc/out is NULL");

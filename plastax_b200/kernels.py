@@ -160,7 +160,7 @@ def unit_apply(acc: torch.Tensor, out: torch.Tensor, *, mode: int, act_kind: str
     n = acc.numel()
     if acc_fixed is not None:
         _check(acc_fixed, torch.int64, n, "unit_apply acc_fixed")
-    call("pxb_unit_apply", ctypes.c_int32(n), ctypes.c_int32(mode), ctypes.c_int32(_lib.ACT[act_kind]),
+    call("pxb_unit_apply", ctypes.c_int32(n), ctypes.c_int32(mode), ctypes.c_int32(_lib.act_code(act_kind)),
          ctypes.c_int32(_lib.MONOID[monoid]), ptr(acc), ptr(acc_fixed), ptr(act), ptr(seed), ptr(level),
          ctypes.c_int32(target_level), ptr(is_input), ptr(pruned), ptr(out), _stream())
 
@@ -195,7 +195,7 @@ def batched_unit_apply(acc: torch.Tensor, out: torch.Tensor, *, mode: int, act_k
     """Masked apply over [N, B] rows (sum monoid)."""
     n, batch = acc.shape
     call("pxb_batched_unit_apply", ctypes.c_int32(n), ctypes.c_int32(batch), ctypes.c_int32(mode),
-         ctypes.c_int32(_lib.ACT[act_kind]), ptr(acc), ptr(act), ptr(seed), ptr(level), ctypes.c_int32(target_level),
+         ctypes.c_int32(_lib.act_code(act_kind)), ptr(acc), ptr(act), ptr(seed), ptr(level), ctypes.c_int32(target_level),
          ptr(is_input), ptr(out), _stream())
 
 

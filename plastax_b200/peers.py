@@ -123,7 +123,7 @@ def scheme_a_apply(group: PeerGroup, act_kind: str, *, is_input: torch.Tensor | 
 
     nl = 0 if level_counts is None else level_counts.numel()
     _lib.call("pxb_scheme_a_apply", ctypes.byref(group.struct), ctypes.c_int32(group.n),
-              ctypes.c_int32(_lib.ACT[act_kind]), ptr(is_input), ptr(pruned), ptr(level_counts),
+              ctypes.c_int32(_lib.act_code(act_kind)), ptr(is_input), ptr(pruned), ptr(level_counts),
               ctypes.c_int32(nl), ptr(level_before), ptr(level_totals), ctypes.c_uint32(wait_polls), _stream())
 
 

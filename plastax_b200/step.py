@@ -102,7 +102,16 @@ class StepFn:
         self.acc = torch.empty(n, dtype=torch.float32, device=device)
         self.input_ids = torch.tensor(static.input_ids, dtype=torch.int64, device=device)
         self.output_ids = torch.tensor(static.output_ids, dtype=torch.int32, device=device)
+        # unit roles for the applies: 1 input (skipped), 2 output (its own
+        # activation when the passes declare one), 0 hidden
+        fp, bp = net.forward_pass, net.backward_pass
+        out_fwd = fp.output_activation
+        out_bwd = None if bp is None else (bp.output_activation or out_fwd)
+        self.fwd_act = fp.activation if out_fwd is None else (fp.activation, out_fwd)
+        self.bwd_act = None if bp is None else (bp.activation if out_bwd is None else (bp.activation, out_bwd))
         is_input = np.zeros(n, np.uint8)
+        if out_fwd is not None or out_bwd is not None:
+            is_input[list(static.output_ids)] = 2
         is_input[list(static.input_ids)] = 1
         self.is_input = torch.from_numpy(is_input).to(device)
         self.loss_buf = torch.zeros(1, dtype=torch.float32, device=device)
@@ -526,19 +535,19 @@ class StepFn:
                     K.claim_prepare(_lib.CLAIM_PIPELINE, state.conns[0], units[LEVEL.name], state.tail_start, ws,
                                     shard_base=self.static.shard_base(0), free_bitmap=bm)
                     counts = ws.level_counts
-                scheme_a_apply(self.peers, fp.activation, is_input=self.is_input, pruned=pruned,
+                scheme_a_apply(self.peers, self.fwd_act, is_input=self.is_input, pruned=pruned,
                                level_counts=counts, level_before=self.level_before, level_totals=self.level_totals)
                 self.launches += 3
                 return
             self._forward_bucket(state, 0, act)
-            K.unit_apply(self.acc, act, mode=0, act_kind=fp.activation, monoid=self.fwd_monoid,
+            K.unit_apply(self.acc, act, mode=0, act_kind=self.fwd_act, monoid=self.fwd_monoid,
                          is_input=self.is_input, pruned=pruned, acc_fixed=self.acc_fixed)
             self.launches += 3
             return
         level = units[LEVEL.name]
         for l in range(self.num_buckets):
             self._forward_bucket(state, l, act)
-            K.unit_apply(self.acc, act, mode=0, act_kind=fp.activation, monoid=self.fwd_monoid, level=level,
+            K.unit_apply(self.acc, act, mode=0, act_kind=self.fwd_act, monoid=self.fwd_monoid, level=level,
                          target_level=l + 1, is_input=self.is_input, pruned=pruned, acc_fixed=self.acc_fixed)
             self.launches += 2
 
@@ -576,12 +585,12 @@ class StepFn:
         if self.pipeline:
             K.backward_accumulate(state.conns[0], grad, self.acc, "sum")
             self._combine_partials(self.acc)
-            K.unit_apply(self.acc, grad, mode=1, act_kind=bp.activation, act=act, seed=seed, pruned=pruned)
+            K.unit_apply(self.acc, grad, mode=1, act_kind=self.bwd_act, act=act, seed=seed, pruned=pruned)
             self.launches += 3
             return
         level = units[LEVEL.name]
         L = self.num_buckets
-        K.unit_apply(self.acc, grad, mode=1, act_kind=bp.activation, act=act, seed=seed, level=level,
+        K.unit_apply(self.acc, grad, mode=1, act_kind=self.bwd_act, act=act, seed=seed, level=level,
                      target_level=L, is_input=self.is_input, pruned=pruned)
         for l in range(L - 1, 0, -1):
             b = state.conns[l]
@@ -590,7 +599,7 @@ class StepFn:
             else:
                 K.backward_accumulate(b, grad, self.acc, "sum")
             self._combine_partials(self.acc)
-            K.unit_apply(self.acc, grad, mode=1, act_kind=bp.activation, act=act, seed=seed, level=level,
+            K.unit_apply(self.acc, grad, mode=1, act_kind=self.bwd_act, act=act, seed=seed, level=level,
                          target_level=l, is_input=self.is_input, pruned=pruned)
             self.launches += 2
         if self.fuse_update and L > 0:

@@ -10,7 +10,8 @@ engine cannot run (there is no fallback path).
 Recognised forms:
 - ForwardPass: map = weight * activation[src] (the linear_input map of
   src/plastax/phases.py:535-556), combine = sum/max/min, apply =
-  activation(acc) written into ACTIVATION (identity, tanh, relu, sigmoid).
+  activation(acc) written into ACTIVATION (identity, tanh, relu, sigmoid),
+  optionally another activation for the output units (a linear readout).
 - BackwardPass: map = weight * grad_field[dst], combine = sum, apply:
   grad_field = (acc + seed_field) * activation'(ACTIVATION)
   (scripts/parity/golden_rules.py relu_mlp_v1 generalised).
@@ -56,12 +57,17 @@ class ForwardPass:
 
     combine: _monoid.Monoid = _monoid.sum_
     activation: str = "tanh"
+    # the output units' activation, when it differs (a linear readout)
+    output_activation: str | None = None
 
-    def __init__(self, activation: str | None = None, combine: _monoid.Monoid | None = None) -> None:
+    def __init__(self, activation: str | None = None, combine: _monoid.Monoid | None = None,
+                 output_activation: str | None = None) -> None:
         if activation is not None:
             self.activation = activation
         if combine is not None:
             self.combine = combine
+        if output_activation is not None:
+            self.output_activation = output_activation
 
 
 class BackwardPass:
@@ -71,9 +77,14 @@ class BackwardPass:
     activation: str = "tanh"
     grad_field: FieldSpec = GRAD_PRE_ACT
     seed_field: FieldSpec = LOSS_GRAD
+    # the output units' activation derivative (None: the forward pass's
+    # output_activation, else `activation`)
+    output_activation: str | None = None
 
     def __init__(self, activation: str | None = None, grad_field: FieldSpec | None = None,
-                 seed_field: FieldSpec | None = None) -> None:
+                 seed_field: FieldSpec | None = None, output_activation: str | None = None) -> None:
+        if output_activation is not None:
+            self.output_activation = output_activation
         if activation is not None:
             self.activation = activation
         if grad_field is not None:
@@ -420,6 +431,11 @@ class Network:
             raise TypeError(f"{cls.__name__}: forward_pass must be a ForwardPass")
         if fp.activation not in ACTIVATIONS:
             raise ValueError(f"{cls.__name__}: unknown activation {fp.activation!r}")
+        if fp.output_activation is not None and fp.output_activation not in ACTIVATIONS:
+            raise ValueError(f"{cls.__name__}: unknown output activation {fp.output_activation!r}")
+        bp_out = getattr(cls.backward_pass, "output_activation", None)
+        if bp_out is not None and bp_out not in ACTIVATIONS:
+            raise ValueError(f"{cls.__name__}: unknown backward output activation {bp_out!r}")
         fp.combine.lowered()
         if cls.backward_pass is not None:
             bp = cls.backward_pass

@@ -27,8 +27,11 @@ def _mlp(widths, density, rng):
     return int(offsets[-1]), list(range(widths[0])), list(range(int(offsets[-2]), int(offsets[-1]))), frm, to, w
 
 
-@pytest.mark.parametrize("loss_kind,opt_kind", [("mse", "sgd"), ("softmax", "adam")])
-def test_batched_step_matches_the_restatement(cuda, loss_kind, opt_kind):
+@pytest.mark.parametrize("loss_kind,opt_kind,hidden,out_act", [
+    ("mse", "sgd", "tanh", None), ("softmax", "adam", "tanh", None),
+    ("softmax", "sgd", "relu", "identity"),  # the sparse-MLP shape: ReLU hidden units, linear logits
+])
+def test_batched_step_matches_the_restatement(cuda, loss_kind, opt_kind, hidden, out_act):
     import torch
 
     import plastax_b200 as px
@@ -39,8 +42,8 @@ def test_batched_step_matches_the_restatement(cuda, loss_kind, opt_kind):
     opt = px.optim.sgd(0.05) if opt_kind == "sgd" else px.optim.adam(0.01)
 
     class Net(px.Network):
-        forward_pass = px.ForwardPass("tanh")
-        backward_pass = px.BackwardPass("tanh")
+        forward_pass = px.ForwardPass(hidden, output_activation=out_act)
+        backward_pass = px.BackwardPass(hidden)
         loss = px.MSELoss() if loss_kind == "mse" else px.SoftmaxCrossEntropyLoss()
         update_conn = opt
         batch_reduction = px.MeanFloatFirstRest()
@@ -60,8 +63,9 @@ def test_batched_step_matches_the_restatement(cuda, loss_kind, opt_kind):
         else:
             t = np.eye(len(outputs), dtype=np.float32)[rng.integers(0, len(outputs), 8)]
         res = step(state, px.StepInputs(x, t))
-        want = batched_step(host, level, is_input, inputs, outputs, x, t, fwd_act="tanh", bwd_act="tanh",
-                            loss="mse" if loss_kind == "mse" else "softmax", opt=opt.oracle_args())
+        want = batched_step(host, level, is_input, inputs, outputs, x, t, fwd_act=hidden, bwd_act=hidden,
+                            loss="mse" if loss_kind == "mse" else "softmax", opt=opt.oracle_args(),
+                            out_act=out_act)
         np.testing.assert_allclose(float(res.loss.item()), float(want["loss"]), rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(state.units["activation"].cpu().numpy(), want["activation"], rtol=1e-5,
                                    atol=1e-6, err_msg=f"step {it} activation")
