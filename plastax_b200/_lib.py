@@ -10,12 +10,14 @@ from __future__ import annotations
 
 import ctypes
 import functools
+import os
 import pathlib
 from collections.abc import Callable
 from typing import Any
 
 _PKG = pathlib.Path(__file__).resolve().parent
-LIB_PATH = _PKG / "libpxb.so"
+# the in-tree build, or another build of the same sources (PLASTAX_B200_LIB)
+LIB_PATH = pathlib.Path(os.environ.get("PLASTAX_B200_LIB", str(_PKG / "libpxb.so")))
 
 c_i32 = ctypes.c_int32
 c_i64 = ctypes.c_int64

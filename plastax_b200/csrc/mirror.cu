@@ -182,6 +182,7 @@ __device__ __forceinline__ void smem_combine(float *acc_s, int chunk, float *acc
 #ifndef PXB_SWEEP_TILE
 #define PXB_SWEEP_TILE PXB_MIRROR_TILE
 #endif
+
 constexpr int kTile = PXB_SWEEP_TILE;  // divides PXB_MIRROR_TILE: a tile lies in one group
 static_assert(PXB_MIRROR_TILE % kTile == 0 && kTile % 4 == 0, "the sweep tile must divide the mirror tile");
 constexpr int kStages = PXB_SWEEP_STAGES;
@@ -283,9 +284,35 @@ __device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, co
     float av[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) av[j] = __ldg(act + min(ws[j] >> m.cb, last));
+    if (MONOID == PXB_MONOID_SUM) {
+      // branch-free common case: every product of the eight below 1 in
+      // magnitude (a NaN fails the test); an empty entry adds an exact 0
+      // into the chunk's last unit (kEmpty & mask) instead of branching
+      float pv[8];
+      bool small = true;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (ws[j] != kEmpty) smem_combine<MONOID>(acc_s, chunk, acc_g, ws[j] & mask, __fmul_rn(fs[j], av[j]));
+      for (int j = 0; j < 8; ++j) {
+        const float pr = __fmul_rn(fs[j], av[j]);
+        pv[j] = ws[j] != kEmpty ? pr : 0.0f;
+        small &= fabsf(pv[j]) < 1.0f;
+      }
+      int32_t *lo = reinterpret_cast<int32_t *>(acc_s);
+      if (small) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t dl = ws[j] & mask;
+          lo_add(lo + dl, lo + chunk + dl, __float2int_rn(pv[j] * kFixScale));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (ws[j] != kEmpty) fixed_add(lo + (ws[j] & mask), lo + chunk + (ws[j] & mask), acc_g + (ws[j] & mask), pv[j]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (ws[j] != kEmpty) smem_combine<MONOID>(acc_s, chunk, acc_g, ws[j] & mask, __fmul_rn(fs[j], av[j]));
+    }
     if (PK != PXB_PRUNE_NONE) {
       // the predicate is rare: one test of the smallest |w| (fminf drops a
       // NaN, which no predicate prunes) or of any below its destination's
@@ -577,18 +604,20 @@ extern "C" int pxb_mirror_forward(const pxb_mirror *mirror, const float *act, in
   MPrune p{prune_kind, prune_threshold, unit_threshold, dead, free_bitmap, bitmap_words, bitmap_level, pruned_count};
   cudaStream_t st = as_stream(stream);
   if (m.entries > 0) {
-    const size_t smem =
-        128 + size_t(kStages) * kTile * 8 + ((monoid == PXB_MONOID_SUM ? 2 * sizeof(int32_t) : sizeof(float)) << m.cb);
+    const size_t acc_bytes = (monoid == PXB_MONOID_SUM ? 2 * sizeof(int32_t) : sizeof(float)) << m.cb;
+    const size_t smem = 128 + size_t(kStages) * kTile * 8 + acc_bytes;
+    const int threads = kSweepThreads;
+#define PXB_SWEEP_FN mirror_sweep_kernel
     const int64_t tiles = m.entries / kTile;
 #define PXB_MS(M, P)                                                                              \
   do {                                                                                            \
-    auto fn = mirror_sweep_kernel<M, P>;                                                          \
+    auto fn = PXB_SWEEP_FN<M, P>;                                                                 \
     PXB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));   \
     int per_sm = 0;                                                                               \
-    PXB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kSweepThreads, smem));    \
+    PXB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem));          \
     const int64_t full = int64_t(sm_count()) * (per_sm > 0 ? per_sm : 1);                        \
     const int grid = static_cast<int>(tiles < full ? tiles : full);                               \
-    fn<<<grid, kSweepThreads, smem, st>>>(m, act, acc, acc_fixed, p);                             \
+    fn<<<grid, threads, smem, st>>>(m, act, acc, acc_fixed, p);                                   \
   } while (0)
 #define PXB_MS_K(M)                                                                               \
   do {                                                                                            \
@@ -601,6 +630,7 @@ extern "C" int pxb_mirror_forward(const pxb_mirror *mirror, const float *act, in
     else PXB_MS_K(PXB_MONOID_MIN);
 #undef PXB_MS_K
 #undef PXB_MS
+#undef PXB_SWEEP_FN
     PXB_LAUNCHED("mirror_sweep_kernel");
   }
   if (m.ovf_cap > 0) {
