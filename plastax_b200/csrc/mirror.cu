@@ -232,16 +232,29 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 }
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsThreads) : "memory"); }
 
-// Advance t to the next tile of [t, t_hi) with used entries; g tracks its
-// group. Producer and consumers walk the same sequence (gfill is not written
-// during the sweep).
-__device__ __forceinline__ bool next_tile(const MirrorK &m, int64_t &t, int64_t t_hi, int64_t &g, int32_t &used) {
+// The group a sweep is in, with its bounds and fill held in registers.
+struct GroupCursor {
+  int64_t g, base, next, fill;
+};
+
+__device__ __forceinline__ void cursor_load(const MirrorK &m, GroupCursor &c) {
+  c.base = __ldg(m.gbase + c.g);
+  c.next = c.g + 1 < m.groups ? __ldg(m.gbase + c.g + 1) : INT64_MAX;
+  c.fill = __ldg(m.gfill + c.g);
+}
+
+// Advance t to the next tile of [t, t_hi) with used entries; the cursor
+// tracks its group. Producer and consumers walk the same sequence (gfill is
+// not written during the sweep).
+__device__ __forceinline__ bool next_tile(const MirrorK &m, int64_t &t, int64_t t_hi, GroupCursor &c,
+                                          int32_t &used) {
   for (; t < t_hi; ++t) {
     const int64_t e0 = t * kTile;
-    while (g + 1 < m.groups && __ldg(m.gbase + g + 1) <= e0) ++g;
-    const int64_t off = e0 - __ldg(m.gbase + g);
-    const int64_t fill = __ldg(m.gfill + g);
-    const int64_t u = fill - off;
+    while (e0 >= c.next) {
+      ++c.g;
+      cursor_load(m, c);
+    }
+    const int64_t u = c.fill - (e0 - c.base);
     if (u > 0) {
       used = static_cast<int32_t>(u < kTile ? u : kTile);
       return true;
@@ -275,25 +288,29 @@ __device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, co
     const uint4 wb = two ? wq[q2] : make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
     const float4 fb = two ? fq[q2] : make_float4(0.f, 0.f, 0.f, 0.f);
     uint32_t ws[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-    const float fs[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
+    float fs[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
     if (used < kTile) {  // the group's used prefix ends inside this tile
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (((j < 4 ? q : q2) * 4 + (j & 3)) >= used) ws[j] = kEmpty;
+        if (((j < 4 ? q : q2) * 4 + (j & 3)) >= used) {
+          ws[j] = kEmpty;
+          fs[j] = 0.0f;
+        }
     }
     float av[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) av[j] = __ldg(act + min(ws[j] >> m.cb, last));
     if (MONOID == PXB_MONOID_SUM) {
       // branch-free common case: every product of the eight below 1 in
-      // magnitude (a NaN fails the test); an empty entry adds an exact 0
-      // into the chunk's last unit (kEmpty & mask) instead of branching
+      // magnitude (a NaN fails the test). An empty entry's weight is 0 (the
+      // prune zeroes it, the build and the tail mask leave 0), so it adds an
+      // exact 0 into the chunk's last unit (kEmpty & mask); a non-finite
+      // activation behind it fails the test and the slow path skips it
       float pv[8];
       bool small = true;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float pr = __fmul_rn(fs[j], av[j]);
-        pv[j] = ws[j] != kEmpty ? pr : 0.0f;
+        pv[j] = __fmul_rn(fs[j], av[j]);
         small &= fabsf(pv[j]) < 1.0f;
       }
       int32_t *lo = reinterpret_cast<int32_t *>(acc_s);
@@ -336,6 +353,7 @@ __device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, co
           if (!(fabsf(fs[j]) < thr)) continue;
           const int64_t pos = e0 + (j < 4 ? q : q2) * 4 + (j & 3);
           m.word[pos] = kEmpty;
+          m.w[pos] = 0.0f;
           tombstone(p, m.slot[pos], static_cast<int32_t>(ws[j] >> m.cb));
           const int32_t h = atomicAdd(m.hcount + g, 1);
           m.hstack[gb + h] = static_cast<int32_t>(pos - gb);
@@ -426,11 +444,13 @@ __global__ void __launch_bounds__(kSweepThreads, PXB_SWEEP_MIN_CTAS) mirror_swee
     if (lane != 0) return;
     uint64_t policy;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-    int64_t t = t_lo, g = lo;
+    int64_t t = t_lo;
+    GroupCursor c{lo, 0, 0, 0};
+    cursor_load(m, c);
     int32_t used;
     uint32_t i = 0;
     bool ok = true;
-    while (next_tile(m, t, t_hi, g, used)) {
+    while (next_tile(m, t, t_hi, c, used)) {
       const int s = static_cast<int>(i % kStages);
       if (i >= kStages && !mbar_wait(empty + s, ((i / kStages) - 1) & 1)) {
         ok = false;
@@ -452,11 +472,14 @@ __global__ void __launch_bounds__(kSweepThreads, PXB_SWEEP_MIN_CTAS) mirror_swee
   }
 
   // consumers
-  int64_t t = t_lo, g = lo, cur = -1;
+  int64_t t = t_lo, cur = -1;
+  GroupCursor c{lo, 0, 0, 0};
+  cursor_load(m, c);
   int32_t used;
   uint32_t i = 0;
   bool ok = true;
-  while (next_tile(m, t, t_hi, g, used)) {
+  while (next_tile(m, t, t_hi, c, used)) {
+    const int64_t g = c.g;
     if (g != cur) {
       consumer_sync();
       flush_reset<MONOID>(m, acc_s, acc, acc_fixed, cur);
@@ -467,8 +490,8 @@ __global__ void __launch_bounds__(kSweepThreads, PXB_SWEEP_MIN_CTAS) mirror_swee
     if (ok && !mbar_wait(full + s, (i / kStages) & 1)) ok = false;
     if (ok)
       sweep_tile<MONOID, PK>(m, p, act, word_s + s * kTile, w_s + s * kTile, used, acc_s,
-                                acc + (static_cast<int64_t>(g) << m.cb), static_cast<int32_t>(g),
-                                __ldg(m.gbase + g), t * kTile);
+                                acc + (static_cast<int64_t>(g) << m.cb), static_cast<int32_t>(g), c.base,
+                                t * kTile);
     __syncwarp();
     if (lane == 0) mbar_arrive(empty + s);
     ++t;
