@@ -44,7 +44,7 @@ UNIT = "edges/s"
 # chunk of 2048 units (581.0 MB over 71,303,168 entries per launch); the
 # traffic reported for a full launch is this figure times its swept entries
 # (traffic grows in proportion to them)
-NCU_TRAFFIC_BYTES_PER_ENTRY = 8.12
+NCU_TRAFFIC_BYTES_PER_ENTRY = 8.13
 
 
 def _env_int(name: str, default: int) -> int:
