@@ -67,6 +67,9 @@ def parse() -> argparse.Namespace:
                          "capped at 13 (11 for the full-size reservoir)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--kernel-breakdown", action="store_true",
+                    help="after the timing, print (stderr, rank 0) every kernel's device time per step over five "
+                         "graph replays, from the profiler's activity records")
     return ap.parse_args()
 
 
@@ -371,8 +374,9 @@ def engine_arm(args) -> None:
                 "ms_per_step": e2e_ms / Kst},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic,
-                     "kernel": ("mirror_forward_kernel<sum, prune> (destination-grouped sweep + fused prune)"
-                                if step.use_mirror else "forward_vec4_kernel<sum, prune> (canonical sweep + prune)"),
+                     "kernel": ("mirror_sweep_kernel<sum, abs-below prune> (destination-grouped sweep + fused "
+                                "prune)" if step.use_mirror else
+                                "forward_vec4_kernel<sum, prune> (canonical sweep + prune)"),
                      "bytes_per_entry": per_entry, "entries_per_launch": swept_entries,
                      "kernel_ms": fwd_avg_s * 1e3, "alg_bytes_per_launch": alg_bytes, "peak_kind": peak_kind,
                      "share_of_step": (fwd_avg_s * 1e3) / ms_per_step},
@@ -380,6 +384,8 @@ def engine_arm(args) -> None:
         "cuda_graph": use_graph,
         "gpu_launches": launches_per_step * Kst,
     }
+    if args.kernel_breakdown:
+        kernel_breakdown(step, state, inputs_dev[0], rank)
     # a CUDA graph holding NCCL calls must be released before the process
     # group is destroyed, or the exit waits forever; the peer-memory group is
     # unmapped collectively
@@ -409,6 +415,35 @@ def engine_arm(args) -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def kernel_breakdown(step, state, x, rank: int, replays: int = 5) -> None:
+    """Every kernel's device time per step over `replays` graph replays (or
+    eager steps), from the profiler's activity records; rank 0 prints it to
+    stderr. Every rank runs the same steps (collectives stay matched)."""
+    import collections
+    import sys
+
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    from plastax_b200 import StepInputs
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(replays):
+            step(state, StepInputs(x))
+        torch.cuda.synchronize()
+    if rank != 0:
+        return
+    tot: dict = collections.defaultdict(lambda: [0, 0.0])
+    for evt in prof.events():
+        if evt.device_type == torch.autograd.DeviceType.CUDA:
+            name = evt.name.split("(")[0][:80]
+            tot[name][0] += 1
+            tot[name][1] += evt.device_time_total
+    print(f"kernel breakdown: {replays} steps, device time per step", file=sys.stderr)
+    for name, (cnt, us) in sorted(tot.items(), key=lambda kv: -kv[1][1]):
+        print(f"  {cnt / replays:5.1f}/step {us / replays:10.1f} us  {name}", file=sys.stderr)
 
 
 def count_launches(step, state, x, dev) -> int:
