@@ -613,8 +613,10 @@ struct FsInfo {
 
 struct FsScratch {
   uint64_t *keys, *tk, *bk;
+  // byrank: each candidate's slot inside its (level, bin) from the propose
+  // pass to the scatter, then the threshold bin's members by rank
   int32_t *dst, *ti, *bi, *byrank;
-  uint32_t *hist, *cursor, *toff;
+  uint32_t *hist, *toff;
   FsInfo *info;
   size_t total;
 };
@@ -650,12 +652,14 @@ __global__ void __launch_bounds__(kFsThreads) fs_propose_kernel(ProposeArgs a, F
     const uint64_t key = fs_key(g, a.score_kind, score, src);
     o.keys[c] = key;
     o.dst[c] = dst;
-    atomicAdd(o.hist + fs_level(g, a.level, src) * g.nb + fs_bin(g, key), 1u);
+    // the count's old value is the candidate's slot inside its (level, bin):
+    // the scatter needs no atomic of its own
+    o.byrank[c] = static_cast<int32_t>(atomicAdd(o.hist + fs_level(g, a.level, src) * g.nb + fs_bin(g, key), 1u));
   }
 }
 
 // One block: the threshold bin, the level counts and the temp offsets of the
-// full bins (level-major), cursors zeroed. Thread t owns the consecutive bins
+// full bins (level-major). Thread t owns the consecutive bins
 // [t * ipt, (t + 1) * ipt): one block scan finds the threshold bin and one
 // per level lays out the full bins.
 __global__ void __launch_bounds__(1024) fs_threshold_kernel(FsGeom g, FsScratch o) {
@@ -715,7 +719,6 @@ __global__ void __launch_bounds__(1024) fs_threshold_kernel(FsGeom g, FsScratch 
     for (int j = 0; j < kFsMaxIpt; ++j) {
       if (j < ipt && b0 + j < g.nb) {
         o.toff[l * g.nb + b0 + j] = static_cast<uint32_t>(run);
-        o.cursor[l * g.nb + b0 + j] = 0;
       }
       run += v[j];
     }
@@ -742,7 +745,7 @@ __global__ void __launch_bounds__(kFsThreads) fs_scatter_kernel(FsGeom g, const 
     const int32_t b = fs_bin(g, key);
     if (b < tb) {
       const int32_t slot = fs_level(g, level, fs_src(g, key)) * g.nb + b;
-      const uint32_t pos = o.toff[slot] + atomicAdd(o.cursor + slot, 1u);
+      const uint32_t pos = o.toff[slot] + static_cast<uint32_t>(o.byrank[c]);
       o.bk[pos] = key;
       o.bi[pos] = static_cast<int32_t>(c);
     } else if (b == tb) {
@@ -909,7 +912,6 @@ static void fs_layout(const FsGeom &g, char *base, FsScratch *o) {
   o->bi = reinterpret_cast<int32_t *>(take(kk * 4 * 2));  // indices, then ranks
   o->byrank = reinterpret_cast<int32_t *>(take(n * 4));
   o->hist = reinterpret_cast<uint32_t *>(take(hb * 4));
-  o->cursor = reinterpret_cast<uint32_t *>(take(hb * 4));
   o->toff = reinterpret_cast<uint32_t *>(take(hb * 4));
   o->info = reinterpret_cast<FsInfo *>(take(sizeof(FsInfo)));
   o->total = off;
