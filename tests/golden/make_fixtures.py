@@ -218,7 +218,9 @@ def unit_goldens(ref_root: pathlib.Path):
 
 
 def main() -> int:
-    ref_root = pathlib.Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference").resolve()
+    if len(sys.argv) < 2:
+        raise SystemExit("usage: python tests/golden/make_fixtures.py <plastax checkout>")
+    ref_root = pathlib.Path(sys.argv[1]).resolve()
     ref, emit = _load_spec(ref_root)
     rng = np.random.default_rng(2024)
     registry, passes = capture_registry(ref, emit)
