@@ -44,6 +44,46 @@ def test_abi_version_and_errors_without_a_gpu():
                   ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), 4, 7, ctypes.c_void_p(16), None)
 
 
+def test_newer_entry_points_reject_bad_arguments_on_the_host():
+    """The grid, unit-lifecycle, lowest-prune, loop and UPGD entry points
+    check their arguments before any device work (no GPU needed)."""
+    from plastax_b200 import _lib
+
+    lib = _lib.lib()
+    p = ctypes.c_void_p(16)
+
+    def err(rc, text):
+        assert rc != 0 and text in _lib.last_error(), (rc, _lib.last_error())
+
+    score = _lib.PairScore(_lib.PAIR_MODULAR, None, None, 3, 5, 17, 8, 0.125)
+    err(lib.pxb_propose_grid(1 << 20, 2, 1 << 15, 1 << 15, None, None, 0, ctypes.byref(score), p, None, 1, 0, 0, 0,
+                             p, p, p, None), "exceed the int32 candidate index")
+    bad = _lib.PairScore(9, None, None, 0, 0, 1, 0, 1.0)
+    err(lib.pxb_propose_grid(8, 1, 8, 8, None, None, 0, ctypes.byref(bad), p, None, 1, 0, 0, 0, p, p, p, None),
+        "unknown or incomplete score form")
+    pred = _lib.PairScore(_lib.PAIR_MODULAR_PREDICATE, None, None, 1, 1, 2, 0, 1.0)
+    err(lib.pxb_unit_importance(8, ctypes.byref(pred), None, None, 0, 0, 1, 0, p, None), "importance form")
+    err(lib.pxb_unit_update(8, 7, p, None, ctypes.c_float(1.0), ctypes.c_float(0.0), None, None), "unknown kind")
+    err(lib.pxb_unit_quantile(8, p, None, None, ctypes.c_float(1.5), p, p, ctypes.c_size_t(1 << 20), None),
+        "bad arguments")
+    cols = _lib.UnitColumns()
+    cols.count = 17
+    err(lib.pxb_unit_prune(8, p, p, None, p, p, ctypes.byref(cols), None), "bad column list")
+    spawn = _lib.UnitSpawn(5, 16, 0.5, 1, 10, None, None, 1.0)
+    err(lib.pxb_unit_add(8, ctypes.byref(spawn), p, p, ctypes.byref(_lib.UnitColumns()), p, p, p, None),
+        "unknown spawn kind")
+    spawn = _lib.UnitSpawn(_lib.SPAWN_ARGMAX, 16, 0.5, 1, 0, None, None, 1.0)
+    err(lib.pxb_unit_add(8, ctypes.byref(spawn), p, p, ctypes.byref(_lib.UnitColumns()), p, p, p, None),
+        "max_level")
+    err(lib.pxb_lowest_keys(ctypes.c_int64(1 << 30), p, p, ctypes.c_int64(1 << 30), p, p, None), "out of range")
+    err(lib.pxb_loop_build(None, None, None), "NULL")
+    err(lib.pxb_unit_apply(8, 0, 6 << 8, 0, p, None, None, None, None, 0, None, None, p, None),
+        "unknown activation code")
+    upgd = _lib.Optimizer(_lib.OPT["upgd"], 0.01, 0.9, 0.01, 1e-8, 0.0, None)
+    err(lib.pxb_backward_update(ctypes.c_int64(0), None, None, None, None, None, None, 8, None, ctypes.byref(upgd),
+                                p, None, p, None), "upgd needs")
+
+
 @pytest.mark.parametrize("live,headroom,align,want", [
     (0, 0.0, None, 64), (1, 0.0, None, 64), (100, 0.0, None, 128), (128, 0.0, None, 128), (129, 0.0, None, 256),
     (1000, 0.1, None, 2048), (1000, 0.0, 256, 1024), (285_212_672, 0.01, 8192, 288_071_680), (10, 0.0, 7, 70)])
