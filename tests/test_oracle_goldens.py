@@ -298,3 +298,40 @@ def test_unit_lifecycle_goldens(case):
     live = [(int(s), int(d), float(w)) for s, d, w, x in zip(b["from_id"], b["to_id"], b["weight"], b["dead"],
                                                                 strict=True) if x == 0]
     check_unit_outcome(case, act, level, pruned, live, children, overflow)
+
+
+def test_upgd_hash_matches_its_formula():
+    """oracle/upgd.hash01 in uint32 numpy equals the three-word hash of
+    examples/dst_sparse.py:77-85 evaluated with Python integers mod 2^32."""
+    from oracle.upgd import hash01
+
+    M = 0xFFFFFFFF
+
+    def ref(a, b, c):
+        h = ((a + 0x9E3779B1) & M) * 0x85EBCA77 & M
+        h = ((h ^ b) * 0xC2B2AE3D) & M
+        h = ((h ^ c) * 0x27D4EB2F) & M
+        h ^= h >> 15
+        h = (h * 0x2C1B3C6D) & M
+        h ^= h >> 13
+        return np.float32(h >> 8) / np.float32(1 << 24)
+
+    rng = np.random.default_rng(5)
+    a, b, c = (rng.integers(0, 1 << 31, 200) for _ in range(3))
+    got = hash01(a, b, c)
+    want = np.array([ref(int(x), int(y), int(z)) for x, y, z in zip(a, b, c, strict=True)], np.float32)
+    np.testing.assert_array_equal(got, want)
+    assert ((got >= 0) & (got < 1)).all()
+
+
+def test_unit_quantile_threshold_edges():
+    """The quantile rule: rank floor(q * m) of the m candidate values
+    ascending, NaN excluded, -inf when nothing is a candidate."""
+    from oracle.units import quantile_threshold
+
+    v = np.array([5, 1, 4, np.nan, 2, 3], np.float32)
+    cand = np.array([1, 1, 1, 1, 1, 0], bool)  # the last unit is exempt
+    assert quantile_threshold(v, cand, 0.0) == 1.0
+    assert quantile_threshold(v, cand, 0.5) == 4.0  # m = 4 (NaN out): sorted 1 2 4 5, rank 2
+    assert quantile_threshold(v, cand, 1.0) == 5.0  # clamped to m - 1
+    assert quantile_threshold(v, np.zeros(6, bool), 0.3) == np.float32(-np.inf)
