@@ -40,6 +40,9 @@ class BatchedStepFn:
         if batch_size % 4 != 0 or batch_size > 1024:
             raise ValueError(f"make_step: the batched engine moves unit rows as float4: batch_size must be a "
                              f"multiple of 4 and at most 1024, got {batch_size}")
+        if net.update_unit is not None or net.prune_unit is not None or net.add_unit is not None:
+            raise NotImplementedError("a batched step has no unit-lifecycle lowering yet (update_unit runs per "
+                                      "sample, prune_unit and add_unit on the reduced state)")
         if net.update_conn is not None and net.update_conn.kind == "upgd":
             raise NotImplementedError("a batched step has no UPGD lowering (the rule declares no exact "
                                       "per-sample / batch pair)")

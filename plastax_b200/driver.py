@@ -241,9 +241,14 @@ class Driver:
             # the remainder's columns live in the old step's buffers: keep them
             remainder = GrowthRemainder(remainder.src.clone(), remainder.dst.clone(), remainder.weight.clone(),
                                         remainder.dropped.clone())
+            grew = False
             for level in range(len(self._static.level_capacities)):
                 if self._free_slots(state, level) == 0:
                     self._static, state = grow_bucket(self._static, state, level)
+                    grew = True
+            if not grew:
+                raise RuntimeError("Driver: the growth overflowed but no bucket is full; the dropped candidates "
+                                   "have nowhere to go")
             self._rebuild()
             state, remainder = self._step.retry(state, remainder)
         return state

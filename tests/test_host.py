@@ -309,6 +309,16 @@ def test_batched_step_rejects_what_it_cannot_run():
     with pytest.raises(ValueError, match="multiple of 4"):
         px.make_step(Topo, static, batch_size=6, device="cpu")
 
+    class Units(px.Network):
+        forward_pass = px.ForwardPass("tanh")
+        propagation = px.Propagation.TOPOLOGICAL
+        batch_reduction = px.MeanFloatFirstRest()
+        update_unit = px.AffineUnitUpdate("activation", 1.0, 0.125)
+
+    static, _ = px.NetworkBuilder.from_edges(Units, 4, [0], [1], input_ids=(0,), output_ids=(1,), device="cpu")
+    with pytest.raises(NotImplementedError, match="unit-lifecycle"):
+        px.make_step(Units, static, batch_size=8, device="cpu")
+
 
 def test_mean_float_first_rest_declares_every_column():
     import plastax_b200 as px
