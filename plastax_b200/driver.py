@@ -116,6 +116,7 @@ class Driver:
         result = self._step(self._state, inputs)
         self.last_loss = result.loss
         state = self._complete_growth(result.state, result.growth_remainder)
+        self._check_mirrors()
         self._state = self._resort_if_due(state)
 
     def scan(self, inputs: StepInputs, *, record: str | None = None, steps: int | None = None) -> torch.Tensor:
@@ -173,6 +174,7 @@ class Driver:
             done, halted = divmod(int(self._status.item()), 2)
             ran = done - start
             self._state.step += ran
+            self._check_mirrors()
             if halted:
                 # finish step done - 1 on the host (its remainder is the graph's)
                 state = self._complete_growth(self._state, fn._graph_rem)
@@ -211,6 +213,15 @@ class Driver:
             self._loop.close()
         self._loop = None
         self._loop_key = None
+
+    def _check_mirrors(self) -> None:
+        """Rebuild the step's mirrors when one lost an edge (its inserts found
+        no room): the canonical arena stays complete, so a rebuild restores
+        the sweep's input exactly."""
+        fn = self._step
+        if isinstance(fn, StepFn) and not fn.mirrors_healthy():
+            self._drop_loop()
+            fn.invalidate()
 
     def _make_step(self):
         return make_step(self._net, self._static, batch_size=self._batch_size, layout=self._layout,

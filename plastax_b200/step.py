@@ -225,6 +225,19 @@ class StepFn:
         self._ahead_ready = False
         self._bound = id(state)
 
+    def mirrors_healthy(self) -> bool:
+        """Whether every mirror still holds every live edge (one host read).
+        An insert that found neither a hole, nor slack, nor room in the
+        overflow list sets bit 0 of the mirror's status: `invalidate()` then
+        rebuilds the mirror from the canonical arena. Bit 1 (a sweep gave up
+        waiting on its copies) is a device fault and raises."""
+        if not self.mirrors:
+            return True
+        codes = torch.cat([m.status for m in self.mirrors]).cpu()
+        if bool((codes & 2).any()):
+            raise RuntimeError("mirror sweep: a bulk copy never completed (status bit 1)")
+        return not bool((codes != 0).any())
+
     def invalidate(self) -> None:
         """Drop the per-state indices (call after editing a state's columns
         outside the step); they are rebuilt on the next call."""
