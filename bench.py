@@ -7,8 +7,9 @@ step = forward propagation of every live edge with the 0.1% magnitude prune
 fused in, the tanh apply, per-unit Philox proposals, the total-order
 selection of 0.1% of the recurrent edges and the pipeline slot claim.
 Scheme-A: the capacity axis is split into N contiguous bands, one per rank;
-the per-unit partials are NCCL all-reduced before the apply and the claim
-all-gathers per-level free counts (strong scaling: the arena is fixed).
+the per-unit partials are combined over NVLink peer memory in one kernel with
+the apply, the claim's per-level free counts riding on the same barrier
+(strong scaling: the arena is fixed).
 
 value  = live edges x steps x N-independent / max-over-ranks device time of K
          steps (inputs resident in HBM, arena 3.7 GB >> 126 MB L2).
@@ -41,7 +42,7 @@ METRIC = "propagated edges/sec per step (Scheme-A large reservoir churn step)"
 UNIT = "edges/s"
 # DRAM bytes (read + write) per swept mirror entry of the fused forward+prune
 # sweep, from one ncu capture of the 2^18-unit reservoir with the full-size
-# chunk of 2048 units (581.0 MB over 71,303,168 entries per launch); the
+# chunk of 2048 units (579.7 MB over 71,303,168 entries per launch); the
 # traffic reported for a full launch is this figure times its swept entries
 # (traffic grows in proportion to them)
 NCU_TRAFFIC_BYTES_PER_ENTRY = 8.13
@@ -167,8 +168,9 @@ def reference_arm(args) -> None:
     per_step = float(np.median(times))
     value = live / per_step
     sample = (f"{steps} timed full-size churn steps (median) after {warmup} warm-up, of the "
-              f"{args.steps} requested: the oracle restatement of the reference's step, forward+prune on "
-              f"{threads} threads, growth and claim single-threaded")
+              f"{args.steps} requested: the oracle restatement of the reference's step on {threads} host "
+              f"threads (forward+prune, proposals, total order, the claim's free-slot lists; the in-order "
+              f"candidate assignment sequential)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": steps, "warmup": warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
@@ -407,8 +409,9 @@ def engine_arm(args) -> None:
         per = float(np.median(times))
         line["cpu_baseline"] = {
             "value": live / per, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{len(times)} full-size churn steps of the oracle restatement (median), forward+prune on "
-                      f"{threads} threads, growth and claim single-threaded",
+            "sample": f"{len(times)} full-size churn steps of the oracle restatement (median) on {threads} host "
+                      f"threads (forward+prune, proposals, total order, the claim's free-slot lists; the in-order "
+                      f"candidate assignment sequential)",
             "ms_per_step": per * 1e3}
     if rank == 0:
         print(json.dumps(line), flush=True)

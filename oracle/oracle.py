@@ -181,26 +181,37 @@ def propose_per_unit(n: int, proposals: int, network_seed: int, step: int, dst_l
                      score_kind: int, level: np.ndarray, *, grad: np.ndarray | None = None,
                      act: np.ndarray | None = None, pruned: np.ndarray | None = None, max_level_gap: int = 1,
                      direction: int = 0, allow_self_loops: bool = False, bucket_level: int = -1,
-                     src_level_bound: int = 0) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+                     src_level_bound: int = 0, threads: int = 1) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Per-unit proposals; `threads` > 1 splits the units over host threads
+    (the same output)."""
     total = n * proposals
     src = np.empty(total, np.int32)
     dst = np.empty(total, np.int32)
     score = np.empty(total, np.float32)
-    lib().pxo_propose_per_unit(ctypes.c_int32(n), ctypes.c_int32(proposals), ctypes.c_uint64(network_seed),
-                               ctypes.c_int32(step), ctypes.c_int32(dst_lo), ctypes.c_int32(dst_n),
-                               ctypes.c_int(score_kind), _p(grad), _p(act), _p(level), _p(pruned),
-                               ctypes.c_int32(max_level_gap), ctypes.c_int(direction),
-                               ctypes.c_int(1 if allow_self_loops else 0), ctypes.c_int32(bucket_level),
-                               ctypes.c_int32(src_level_bound), _p(src), _p(dst), _p(score))
+    args = [ctypes.c_int32(n), ctypes.c_int32(proposals), ctypes.c_uint64(network_seed),
+            ctypes.c_int32(step), ctypes.c_int32(dst_lo), ctypes.c_int32(dst_n),
+            ctypes.c_int(score_kind), _p(grad), _p(act), _p(level), _p(pruned),
+            ctypes.c_int32(max_level_gap), ctypes.c_int(direction),
+            ctypes.c_int(1 if allow_self_loops else 0), ctypes.c_int32(bucket_level),
+            ctypes.c_int32(src_level_bound), _p(src), _p(dst), _p(score)]
+    if threads > 1:
+        lib().pxo_propose_per_unit_mt(*args, ctypes.c_int(threads))
+    else:
+        lib().pxo_propose_per_unit(*args)
     return src, dst, score
 
 
-def total_order(score: np.ndarray, src: np.ndarray, dst: np.ndarray) -> np.ndarray:
+def total_order(score: np.ndarray, src: np.ndarray, dst: np.ndarray, threads: int = 1) -> np.ndarray:
+    """The total order's permutation; `threads` > 1 sorts chunks on host
+    threads and merges them (the same permutation)."""
     score = np.ascontiguousarray(score, np.float32)
     src = np.ascontiguousarray(src, np.int32)
     dst = np.ascontiguousarray(dst, np.int32)
     perm = np.empty(score.size, np.int32)
-    lib().pxo_total_order(_i64(score.size), _p(score), _p(src), _p(dst), _p(perm))
+    if threads > 1:
+        lib().pxo_total_order_mt(_i64(score.size), _p(score), _p(src), _p(dst), _p(perm), ctypes.c_int(threads))
+    else:
+        lib().pxo_total_order(_i64(score.size), _p(score), _p(src), _p(dst), _p(perm))
     return perm
 
 
@@ -232,9 +243,10 @@ def _extra(cols: list[np.ndarray], vals: list[np.ndarray]) -> _Extra:
 
 def claim_pipeline(b: dict, level: np.ndarray, tail_start: int, src: np.ndarray, dst: np.ndarray,
                    weight: np.ndarray, growable: np.ndarray, *, max_new: int = -1,
-                   extra: dict[str, np.ndarray] | None = None) -> tuple[np.ndarray, np.ndarray, int]:
+                   extra: dict[str, np.ndarray] | None = None, threads: int = 1) -> tuple[np.ndarray, np.ndarray, int]:
     """Pipeline claim in place (src/plastax/phases.py:2985-3106). Returns
-    (counts[4], overflowed[k], new tail_start)."""
+    (counts[4], overflowed[k], new tail_start); `threads` > 1 builds the
+    free-slot lists on host threads (the same claim)."""
     k = src.size
     counts = np.zeros(4, np.int32)
     over = np.zeros(max(k, 1), np.uint8)
@@ -242,10 +254,13 @@ def claim_pipeline(b: dict, level: np.ndarray, tail_start: int, src: np.ndarray,
     grow = np.ascontiguousarray(growable, np.uint8)
     names = sorted(extra or {})
     ex = _extra([b[nm] for nm in names], [np.ascontiguousarray(extra[nm]) for nm in names]) if names else None
-    lib().pxo_claim_pipeline(_i64(b["dead"].size), _p(b["from_id"]), _p(b["to_id"]), _p(b["dead"]),
-                             _p(b["weight"]), _p(level), ctypes.c_int32(level.size), ctypes.byref(tail), _i64(k),
-                             _p(src), _p(dst), _p(weight), _p(grow), _i64(max_new),
-                             ctypes.byref(ex) if ex else None, _p(counts), _p(over))
+    args = [_i64(b["dead"].size), _p(b["from_id"]), _p(b["to_id"]), _p(b["dead"]), _p(b["weight"]), _p(level),
+            ctypes.c_int32(level.size), ctypes.byref(tail), _i64(k), _p(src), _p(dst), _p(weight), _p(grow),
+            _i64(max_new), ctypes.byref(ex) if ex else None, _p(counts), _p(over)]
+    if threads > 1:
+        lib().pxo_claim_pipeline_mt(*args, ctypes.c_int(threads))
+    else:
+        lib().pxo_claim_pipeline(*args)
     return counts, over[:k], int(tail.value)
 
 

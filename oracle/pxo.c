@@ -256,11 +256,41 @@ void pxo_unit_apply(int32_t n, int mode, int act_kind, int monoid, float *acc, c
  * dst = dst_lo + uniform_int(dst_n) at sub 0, score at sub 1 (kind 0
  * uniform, 1 floor(u*256)/256 as scripts/parity/golden_rules.py
  * hash_propose_v1, 2 |grad[dst]*act[src]|). */
+static void propose_unit(int32_t i, int32_t n, int32_t P, uint64_t network_seed, int32_t step, int32_t dst_lo,
+                         int32_t dst_n, int score_kind, const float *grad, const float *act, const int32_t *level,
+                         const uint8_t *pruned, int32_t max_gap, int direction, int self_loops,
+                         int32_t bucket_level, int32_t src_level_bound, int32_t *src_out, int32_t *dst_out,
+                         float *score_out);
+
 void pxo_propose_per_unit(int32_t n, int32_t P, uint64_t network_seed, int32_t step, int32_t dst_lo, int32_t dst_n,
                           int score_kind, const float *grad, const float *act, const int32_t *level,
                           const uint8_t *pruned, int32_t max_gap, int direction, int self_loops, int32_t bucket_level,
                           int32_t src_level_bound, int32_t *src_out, int32_t *dst_out, float *score_out) {
-  for (int32_t i = 0; i < n; ++i) {
+  for (int32_t i = 0; i < n; ++i)
+    propose_unit(i, n, P, network_seed, step, dst_lo, dst_n, score_kind, grad, act, level, pruned, max_gap,
+                 direction, self_loops, bucket_level, src_level_bound, src_out, dst_out, score_out);
+}
+
+/* The same proposals with the units split over `threads` threads (each
+ * unit's candidates depend on the unit alone). */
+void pxo_propose_per_unit_mt(int32_t n, int32_t P, uint64_t network_seed, int32_t step, int32_t dst_lo,
+                             int32_t dst_n, int score_kind, const float *grad, const float *act,
+                             const int32_t *level, const uint8_t *pruned, int32_t max_gap, int direction,
+                             int self_loops, int32_t bucket_level, int32_t src_level_bound, int32_t *src_out,
+                             int32_t *dst_out, float *score_out, int threads) {
+  if (threads < 1) threads = 1;
+#pragma omp parallel for schedule(static) num_threads(threads)
+  for (int32_t i = 0; i < n; ++i)
+    propose_unit(i, n, P, network_seed, step, dst_lo, dst_n, score_kind, grad, act, level, pruned, max_gap,
+                 direction, self_loops, bucket_level, src_level_bound, src_out, dst_out, score_out);
+}
+
+static void propose_unit(int32_t i, int32_t n, int32_t P, uint64_t network_seed, int32_t step, int32_t dst_lo,
+                         int32_t dst_n, int score_kind, const float *grad, const float *act, const int32_t *level,
+                         const uint8_t *pruned, int32_t max_gap, int direction, int self_loops,
+                         int32_t bucket_level, int32_t src_level_bound, int32_t *src_out, int32_t *dst_out,
+                         float *score_out) {
+  {
     uint64_t seed = pxo_site_seed(network_seed, (uint32_t)step, 1, (uint32_t)i);
     for (int32_t j = 0; j < P; ++j) {
       int64_t c = (int64_t)i * P + j;
@@ -329,6 +359,57 @@ void pxo_total_order(int64_t n, const float *score, const int32_t *src, const in
   free(it);
 }
 
+/* The same order with the items sorted in `threads` chunks, then merged
+ * pairwise (the order is total, so the result is the sequential one). */
+void pxo_total_order_mt(int64_t n, const float *score, const int32_t *src, const int32_t *dst, int32_t *perm,
+                        int threads) {
+  if (threads < 1) threads = 1;
+  if (n < 2 * (int64_t)threads || threads == 1) {
+    pxo_total_order(n, score, src, dst, perm);
+    return;
+  }
+  order_item *a = (order_item *)malloc(sizeof(order_item) * n);
+  order_item *b = (order_item *)malloc(sizeof(order_item) * n);
+  int64_t *bound = (int64_t *)malloc(sizeof(int64_t) * (threads + 1));
+  for (int t = 0; t <= threads; ++t) bound[t] = n * t / threads;
+#pragma omp parallel for schedule(static) num_threads(threads)
+  for (int64_t i = 0; i < n; ++i) {
+    float k = isnan(score[i]) ? INFINITY : -score[i];
+    if (k == 0.0f) k = 0.0f;
+    a[i].key = k;
+    a[i].src = src[i];
+    a[i].dst = dst[i];
+    a[i].idx = (int32_t)i;
+  }
+#pragma omp parallel for schedule(static, 1) num_threads(threads)
+  for (int t = 0; t < threads; ++t) qsort(a + bound[t], (size_t)(bound[t + 1] - bound[t]), sizeof(order_item), order_cmp);
+  int runs = threads;
+  int64_t *rb = bound;
+  while (runs > 1) {
+    int pairs = runs / 2;
+#pragma omp parallel for schedule(static, 1) num_threads(threads)
+    for (int q = 0; q < pairs; ++q) {
+      int64_t i = rb[2 * q], mid = rb[2 * q + 1], end = rb[2 * q + 2], j = mid, o = rb[2 * q];
+      while (i < mid && j < end) b[o++] = order_cmp(&a[j], &a[i]) < 0 ? a[j++] : a[i++];
+      while (i < mid) b[o++] = a[i++];
+      while (j < end) b[o++] = a[j++];
+    }
+    if (runs % 2) {  /* the odd run out is copied as it is */
+      for (int64_t i = rb[runs - 1]; i < rb[runs]; ++i) b[i] = a[i];
+    }
+    for (int q = 0; q < pairs; ++q) rb[q + 1] = rb[2 * q + 2];
+    if (runs % 2) rb[pairs + 1] = rb[runs];
+    runs = pairs + runs % 2;
+    order_item *tmp = a;
+    a = b;
+    b = tmp;
+  }
+  for (int64_t i = 0; i < n; ++i) perm[i] = a[i].idx;
+  free(a);
+  free(b);
+  free(bound);
+}
+
 /* Step-scoped selection + level-major relisting (src/plastax/phases.py:
  * 4891-4903, 4469-4487): the first min(k, n) of perm, stable by level. */
 int64_t pxo_select_step(int64_t n, const int32_t *perm, const int32_t *src, const int32_t *level, int64_t k,
@@ -388,6 +469,17 @@ static void write_slot(int64_t slot, int64_t i, int32_t *from, int32_t *to, uint
  * (domain = level[from_id]); the rest spill to tail_start + spill rank,
  * levels ascending, up to cap. counts = {committed, overflowed, tail used,
  * violating}. max_new >= 0 caps the growable candidates in claim order. */
+static void claim_pipeline_assign(int64_t cap, int32_t *from, int32_t *to, uint8_t *dead, float *w,
+                                  const int32_t *level, int32_t n, int32_t num_levels, int64_t *tail_start, int64_t k,
+                                  const int32_t *cs, const int32_t *cd, const float *cw, const uint8_t *growable_in,
+                                  int64_t max_new, const pxo_extra *ex, int32_t *counts, uint8_t *overflowed,
+                                  int64_t *cnt, int64_t *start, int64_t *lists);
+
+static inline int32_t slot_domain(const int32_t *from, const int32_t *level, int32_t n, int64_t s) {
+  int32_t o = from[s] < 0 ? 0 : (from[s] >= n ? n - 1 : from[s]);
+  return level[o];
+}
+
 void pxo_claim_pipeline(int64_t cap, int32_t *from, int32_t *to, uint8_t *dead, float *w, const int32_t *level,
                         int32_t n, int64_t *tail_start, int64_t k, const int32_t *cs, const int32_t *cd,
                         const float *cw, const uint8_t *growable_in, int64_t max_new, const pxo_extra *ex,
@@ -398,20 +490,75 @@ void pxo_claim_pipeline(int64_t cap, int32_t *from, int32_t *to, uint8_t *dead, 
   /* per-level dead slot lists in slot order */
   int64_t *cnt = (int64_t *)calloc(num_levels, sizeof(int64_t));
   for (int64_t s = 0; s < cap && s < tail; ++s)
-    if (dead[s]) {
-      int32_t o = from[s] < 0 ? 0 : (from[s] >= n ? n - 1 : from[s]);
-      cnt[level[o]]++;
-    }
+    if (dead[s]) cnt[slot_domain(from, level, n, s)]++;
   int64_t *start = (int64_t *)calloc(num_levels + 1, sizeof(int64_t));
   for (int32_t l = 0; l < num_levels; ++l) start[l + 1] = start[l] + cnt[l];
   int64_t *lists = (int64_t *)malloc(sizeof(int64_t) * (start[num_levels] > 0 ? start[num_levels] : 1));
   int64_t *fill = (int64_t *)calloc(num_levels, sizeof(int64_t));
   for (int64_t s = 0; s < cap && s < tail; ++s)
     if (dead[s]) {
-      int32_t o = from[s] < 0 ? 0 : (from[s] >= n ? n - 1 : from[s]);
-      int32_t l = level[o];
+      int32_t l = slot_domain(from, level, n, s);
       lists[start[l] + fill[l]++] = s;
     }
+  free(fill);
+  claim_pipeline_assign(cap, from, to, dead, w, level, n, num_levels, tail_start, k, cs, cd, cw, growable_in, max_new,
+                        ex, counts, overflowed, cnt, start, lists);
+}
+
+/* The same claim with the per-domain dead-slot lists built by `threads`
+ * threads over contiguous slot ranges (each range's entries land after the
+ * ranges before it, so the lists keep slot order); the assignment of the
+ * candidates, in list order, is the sequential one. */
+void pxo_claim_pipeline_mt(int64_t cap, int32_t *from, int32_t *to, uint8_t *dead, float *w, const int32_t *level,
+                           int32_t n, int64_t *tail_start, int64_t k, const int32_t *cs, const int32_t *cd,
+                           const float *cw, const uint8_t *growable_in, int64_t max_new, const pxo_extra *ex,
+                           int32_t *counts, uint8_t *overflowed, int threads) {
+  if (threads < 1) threads = 1;
+  int32_t num_levels = 1;
+  for (int32_t i = 0; i < n; ++i) if (level[i] + 1 > num_levels) num_levels = level[i] + 1;
+  const int64_t tail = *tail_start, lim = cap < tail ? cap : tail;
+  int64_t *tc = (int64_t *)calloc((size_t)threads * num_levels, sizeof(int64_t));
+#pragma omp parallel for schedule(static, 1) num_threads(threads)
+  for (int t = 0; t < threads; ++t) {
+    const int64_t lo = lim * t / threads, hi = lim * (t + 1) / threads;
+    int64_t *mine = tc + (int64_t)t * num_levels;
+    for (int64_t s = lo; s < hi; ++s)
+      if (dead[s]) mine[slot_domain(from, level, n, s)]++;
+  }
+  int64_t *cnt = (int64_t *)calloc(num_levels, sizeof(int64_t));
+  int64_t *start = (int64_t *)calloc(num_levels + 1, sizeof(int64_t));
+  for (int32_t l = 0; l < num_levels; ++l)
+    for (int t = 0; t < threads; ++t) cnt[l] += tc[(int64_t)t * num_levels + l];
+  for (int32_t l = 0; l < num_levels; ++l) start[l + 1] = start[l] + cnt[l];
+  /* each thread's first list position per domain */
+  int64_t *toff = (int64_t *)calloc((size_t)threads * num_levels, sizeof(int64_t));
+  for (int32_t l = 0; l < num_levels; ++l) {
+    int64_t run = start[l];
+    for (int t = 0; t < threads; ++t) {
+      toff[(int64_t)t * num_levels + l] = run;
+      run += tc[(int64_t)t * num_levels + l];
+    }
+  }
+  int64_t *lists = (int64_t *)malloc(sizeof(int64_t) * (start[num_levels] > 0 ? start[num_levels] : 1));
+#pragma omp parallel for schedule(static, 1) num_threads(threads)
+  for (int t = 0; t < threads; ++t) {
+    const int64_t lo = lim * t / threads, hi = lim * (t + 1) / threads;
+    int64_t *pos = toff + (int64_t)t * num_levels;
+    for (int64_t s = lo; s < hi; ++s)
+      if (dead[s]) lists[pos[slot_domain(from, level, n, s)]++] = s;
+  }
+  free(tc);
+  free(toff);
+  claim_pipeline_assign(cap, from, to, dead, w, level, n, num_levels, tail_start, k, cs, cd, cw, growable_in, max_new,
+                        ex, counts, overflowed, cnt, start, lists);
+}
+
+static void claim_pipeline_assign(int64_t cap, int32_t *from, int32_t *to, uint8_t *dead, float *w,
+                                  const int32_t *level, int32_t n, int32_t num_levels, int64_t *tail_start, int64_t k,
+                                  const int32_t *cs, const int32_t *cd, const float *cw, const uint8_t *growable_in,
+                                  int64_t max_new, const pxo_extra *ex, int32_t *counts, uint8_t *overflowed,
+                                  int64_t *cnt, int64_t *start, int64_t *lists) {
+  const int64_t tail = *tail_start;
   uint8_t *grow = (uint8_t *)malloc(k > 0 ? k : 1);
   int64_t rank = 0;
   for (int64_t i = 0; i < k; ++i) {
@@ -447,7 +594,7 @@ void pxo_claim_pipeline(int64_t cap, int32_t *from, int32_t *to, uint8_t *dead, 
     }
   }
   *tail_start = tail + counts[2];
-  free(cnt); free(start); free(lists); free(fill); free(grow); free(taken);
+  free(cnt); free(start); free(lists); free(grow); free(taken);
 }
 
 /* Topological claim of one bucket (src/plastax/phases.py:2853-2982): the

@@ -81,9 +81,10 @@ class ReservoirOracle:
         orc.unit_apply(n, 0, "tanh", "sum", acc, None, None, None, 0, self.is_input, None, self.act)
         if self.threads <= 1:
             orc.prune(b, n, 1, self.tau)
+        th = self.threads
         src, dst, score = orc.propose_per_unit(n, 1, self.seed, self.step_count, self.num_inputs, self.num_res, 0,
-                                               self.level, max_level_gap=1)
-        perm = orc.total_order(score, src, dst)
+                                               self.level, max_level_gap=1, threads=th)
+        perm = orc.total_order(score, src, dst, threads=th)
         win = orc.select_step(perm, src, self.level, self.k)
         cs, cd = src[win].copy(), dst[win].copy()
         cw = init_weight("hash_uniform", self.init_a, cs, cd)
@@ -94,7 +95,7 @@ class ReservoirOracle:
             cd = np.concatenate([cd, np.zeros(pad, np.int32)])
             cw = np.concatenate([cw, np.zeros(pad, np.float32)])
             grow = np.concatenate([grow, np.zeros(pad, np.uint8)])
-        self.last_counts, _, self.tail = orc.claim_pipeline(b, self.level, self.tail, cs, cd, cw, grow)
+        self.last_counts, _, self.tail = orc.claim_pipeline(b, self.level, self.tail, cs, cd, cw, grow, threads=th)
         self.step_count += 1
 
 
