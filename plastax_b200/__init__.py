@@ -14,6 +14,7 @@ from plastax_b200.state import NetworkState, NetworkStatic, live_conn_count, mak
 from plastax_b200.state import grow_bucket
 from plastax_b200.driver import Driver
 from plastax_b200.step import GrowthRemainder, StepFn, StepInputs, StepResult, make_growth_retry, make_step
+from plastax_b200.shortlist import ShortlistCoverage, recommended_shortlist, shortlist_coverage
 from plastax_b200.topo import resort
 from plastax_b200.traits import (
     GRAD_PRE_ACT,
@@ -62,5 +63,5 @@ __all__ = [
     "MagnitudePrune", "MeanFloatFirstRest", "Network", "NetworkBuilder", "NetworkState", "NetworkStatic", "Propagation", "ProposeAddConn",
     "PruneConn", "ResetGlobal", "ScoreAddConn", "ShardSpec", "SoftmaxCrossEntropyLoss", "StepFn", "StepInputs", "StepResult", "live_conn_count",
     "grow_bucket", "make_empty_state", "make_growth_retry", "make_step", "monoid", "optim", "predicate_add_conn",
-    "resort",
+    "recommended_shortlist", "resort", "shortlist_coverage", "ShortlistCoverage",
 ]

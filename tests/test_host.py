@@ -335,3 +335,37 @@ def test_driver_rejects_check_every_below_one():
 
     with pytest.raises(ValueError, match="check_every"):
         px.Driver(None, None, None, check_every=0, device="cpu")
+
+
+def test_shortlist_coverage_reports():
+    """src/plastax/phases.py:3540-3637: per bucket, the sources at its level,
+    the destinations strictly deeper within the gap, and whether M reaches
+    them; the recommendation is the widest bucket's destination count."""
+    import plastax_b200 as px
+
+    class Net(px.Network):
+        forward_pass = px.ForwardPass("tanh")
+        add_conn = px.ScoreAddConn(score=("modular", 3, 5, 17, 8, 0.125), max_new_per_level=2,
+                                   candidates="shortlist_per_level", shortlist_size=3,
+                                   importance=("modular", 7, 13, 0, 0.25))
+
+    src = np.array([0, 0, 1, 2, 2, 3, 4])
+    dst = np.array([2, 3, 3, 4, 5, 5, 6])
+    static, state = px.NetworkBuilder.from_edges(Net, 7, src, dst, input_ids=(0, 1), output_ids=(6,), device="cpu")
+    cov = px.shortlist_coverage(Net, static, state)
+    lv = state.units["level"].numpy()
+    assert len(cov) == len(static.level_capacities)
+    for c in cov:
+        assert c.source_units == int((lv == c.bucket).sum())
+        assert c.destination_units == int(((lv > c.bucket) & (lv <= c.bucket + 1)).sum())
+        assert c.covered == (3 >= c.destination_units)
+    assert px.recommended_shortlist(Net, static, state) == max(c.destination_units for c in cov)
+
+    class NoShort(px.Network):
+        forward_pass = px.ForwardPass("tanh")
+        add_conn = px.ScoreAddConn(score=("modular", 3, 5, 17, 8, 0.125), max_new_per_level=2)
+
+    static2, state2 = px.NetworkBuilder.from_edges(NoShort, 7, src, dst, input_ids=(0, 1), output_ids=(6,),
+                                                   device="cpu")
+    assert px.shortlist_coverage(NoShort, static2, state2) == ()
+    assert px.recommended_shortlist(NoShort, static2, state2) == 0
