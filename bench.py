@@ -1,11 +1,15 @@
 """Benchmark: propagated edges/sec of the Scheme-A large-reservoir churn step.
 
-Workload (the configuration the metric's 1/2/4/8-GPU
+Workload (the large-reservoir churn configuration the metric's 1/2/4/8-GPU
 figures are quoted on): 1,048,576 tanh units + 16 inputs, fan-in 256
 (268,435,456 recurrent + 16,777,216 input edges, one PIPELINE bucket), one
-step = forward propagation of every live edge with the 0.1% magnitude prune
-fused in, the tanh apply, per-unit Philox proposals, the total-order
-selection of 0.1% of the recurrent edges and the pipeline slot claim.
+step = forward propagation of every live edge with the exact 0.1% lowest-|w|
+prune fused in (k = 268,435 edges, ties by slot), the tanh apply, per-unit
+Philox proposals, the total-order selection of k winners and the pipeline
+slot claim: k edges leave and k enter every step, so the live-edge count
+is constant. The line's `churn` object holds the device-counted pruned,
+grown and overflowed totals of the timed steps, and the run fails unless
+every timed step pruned and grew exactly k.
 Scheme-A: the capacity axis is split into N contiguous bands, one per rank;
 the per-unit partials are combined over NVLink peer memory in one kernel with
 the apply, the claim's per-level free counts riding on the same barrier
@@ -58,7 +62,7 @@ def _env_int(name: str, default: int) -> int:
 def parse() -> argparse.Namespace:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
     ap.add_argument("--units-log2", type=int, default=20, help="reservoir size (2**x units)")
@@ -82,11 +86,14 @@ def config(args):
 
 def workload_desc(cfg, n_gpus: int) -> dict:
     return {
-        "workload": "scheme_a_reservoir_churn (BASELINE configs[4])",
+        "workload": f"scheme_a_reservoir_churn: 2^{cfg.num_units.bit_length() - 1} tanh units + {cfg.num_inputs} "
+                    f"inputs, fan-in {cfg.fan_in}, exact {cfg.churn:.1%} lowest-|w| prune + per-unit proposal "
+                    f"regrowth every step",
         "units": cfg.num_units + cfg.num_inputs,
         "fan_in": cfg.fan_in,
         "live_edges": cfg.live_edges,
         "churn_per_step": cfg.k,
+        "prune": "lowest_k (exact, ties by slot)" if cfg.prune == "lowest_k" else f"|w| < {cfg.tau:.4g}",
         "propagation": "pipeline",
         "parallelism": f"scheme_a_conn_shard{n_gpus}",
         "l2": f"inputs larger than L2: each rank sweeps {8 * cfg.live_edges / n_gpus / 1e9:.2f} GB of mirror entries "
@@ -141,7 +148,8 @@ def cpu_run(cfg, steps: int, warmup: int, threads: int):
     n = cfg.num_inputs + cfg.num_units
     act = np.zeros(n, np.float32)
     ro = ReservoirOracle(b, act, level, live, num_inputs=cfg.num_inputs, num_res=cfg.num_units, tau=cfg.tau,
-                         k=cfg.k, init_a=cfg.sigma * math.sqrt(3.0), seed=cfg.seed, threads=threads)
+                         k=cfg.k, init_a=cfg.sigma * math.sqrt(3.0), seed=cfg.seed, threads=threads,
+                         prune=cfg.prune)
     rng = np.random.default_rng(1)
     times = []
     for i in range(warmup + steps):
@@ -154,23 +162,30 @@ def cpu_run(cfg, steps: int, warmup: int, threads: int):
     return times, live
 
 
+def host_threads() -> int:
+    """Every host core this process may run on (whatever OMP_NUM_THREADS a
+    launcher exported: torchrun sets it to 1)."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:
+        return max(1, os.cpu_count() or 1)
+
+
 def reference_arm(args) -> None:
     rank = _env_int("RANK", 0)
     if rank != 0:
         return
-    from oracle import oracle as orc
-
     cfg = config(args)
-    threads = orc.max_threads()
+    threads = host_threads()
     steps = max(1, min(args.steps, 5))
     warmup = min(args.warmup, 1)
     times, live = cpu_run(cfg, steps, warmup, threads)
     per_step = float(np.median(times))
     value = live / per_step
     sample = (f"{steps} timed full-size churn steps (median) after {warmup} warm-up, of the "
-              f"{args.steps} requested: the oracle restatement of the reference's step on {threads} host "
-              f"threads (forward+prune, proposals, total order, the claim's free-slot lists; the in-order "
-              f"candidate assignment sequential)")
+              f"{args.steps} requested, each pruning and regrowing k = {cfg.k} edges: the oracle restatement of "
+              f"the reference's step on {threads} host threads (forward, the exact lowest-|w| prune, proposals, "
+              f"total order, the claim's free-slot lists; the in-order candidate assignment sequential)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": steps, "warmup": warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
@@ -187,7 +202,10 @@ def reference_arm(args) -> None:
 # ---------------------------------------------------------------------------
 class Clocks:
     """SM clocks and throttle reasons of one GPU, sampled every 5 ms by NVML
-    in a background thread while the timed region runs (reads only)."""
+    in a background thread while the timed regions run (reads only).
+    `start()` returns once the first sample is taken, so a short timed
+    region is covered; `pause()` / `resume()` bracket the untimed work
+    between two timed regions."""
 
     HW_SLOWDOWN, HW_THERMAL, SW_THERMAL, SW_POWER_CAP = 0x8, 0x40, 0x20, 0x4
 
@@ -198,39 +216,58 @@ class Clocks:
         self.samples: list[tuple[float, int]] = []
         self.max_mhz = None
         self._stop = threading.Event()
+        self._ready = threading.Event()
+        self._on = threading.Event()
         self._thread = None
+        self.error = None
 
     def _run(self) -> None:
-        import pynvml
+        try:
+            import pynvml
 
-        pynvml.nvmlInit()
-        h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
-        self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception as e:  # noqa: BLE001 -- reported in the line
+            self.error = f"nvml: {e}"
+            self._ready.set()
+            return
+        first = True
         while not self._stop.is_set():
-            mhz = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
-            reasons = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
-            self.samples.append((mhz, reasons))
+            if self._on.is_set():
+                mhz = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                reasons = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.samples.append((mhz, reasons))
+                if first:
+                    self._ready.set()
+                    first = False
             self._stop.wait(0.005)
         pynvml.nvmlShutdown()
 
     def start(self) -> None:
         import threading
 
-        try:
-            import pynvml  # noqa: F401
-        except ImportError:
-            return
+        self._on.set()
         self._thread = threading.Thread(target=self._run, daemon=True)
         self._thread.start()
+        self._ready.wait(timeout=30)
+
+    def pause(self) -> None:
+        self._on.clear()
+
+    def resume(self) -> None:
+        self._on.set()
 
     def stop(self) -> dict:
         if self._thread is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["sampler not started"], "samples": 0}
         self._stop.set()
         self._thread.join(timeout=5)
         names = {self.HW_SLOWDOWN: "hw_slowdown", self.HW_THERMAL: "hw_thermal_slowdown",
                  self.SW_THERMAL: "sw_thermal_slowdown", self.SW_POWER_CAP: "sw_power_cap"}
         seen = sorted({nm for _, r in self.samples for bit, nm in names.items() if r & bit})
+        if self.error:
+            seen.append(self.error)
         mhz = [m for m, _ in self.samples]
         return {"sm_mhz": float(np.median(mhz)) if mhz else None, "sm_max_mhz": self.max_mhz, "reasons": seen,
                 "samples": len(mhz)}
@@ -242,6 +279,31 @@ def measured_peak_hbm() -> tuple[float, str]:
         return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
         return 6650.0, "fallback"
+
+
+class _EventTimer:
+    """CUDA events around every call of a wrapped function, on the stream
+    it launches on (torch's current stream)."""
+
+    def __init__(self, fn) -> None:
+        self.fn = fn
+        self.events: list[tuple] = []
+        self.on = True
+
+    def __call__(self, *a, **kw):
+        import torch
+
+        if not self.on:
+            return self.fn(*a, **kw)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        out = self.fn(*a, **kw)
+        e.record()
+        self.events.append((s, e))
+        return out
+
+    def ms(self) -> list[float]:
+        return [s.elapsed_time(e) for s, e in self.events]
 
 
 # ---------------------------------------------------------------------------
@@ -275,33 +337,37 @@ def engine_arm(args) -> None:
     gen.manual_seed(1234)
     inputs_dev = torch.randn((W + 2 * Kst, cfg.num_inputs), generator=gen, device=dev)
 
-    # per-launch time of the dominant kernel (the fused forward + prune sweep),
-    # CUDA events on the launching stream around each launch of the timed steps
-    fwd_events: list[tuple] = []
-    import plastax_b200.kernels as K
-
-    fwd_name = "mirror_forward" if step.use_mirror else "forward_prune"
-    orig_fp = getattr(K, fwd_name)
-
-    def timed_forward_prune(*a, **kw):
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        orig_fp(*a, **kw)
-        e.record()
-        fwd_events.append((s, e))
-
     for i in range(W):
         step(state, StepInputs(inputs_dev[i]))
     torch.cuda.synchronize()
+    if not step.check_status():
+        raise RuntimeError("bench: a mirror lost an edge during the warm-up")
     swept_entries = int(step.mirrors[0].gfill.sum().item()) if step.use_mirror else static.local_capacity(0)
     # eager steps with CUDA events on the launching stream around every launch
-    # of the dominant kernel (a graph replay hides per-kernel boundaries)
-    setattr(K, fwd_name, timed_forward_prune)
+    # of the dominant kernel (the fused forward + prune sweep) and of the
+    # mirror's upkeep (the claim's inserts); a graph replay hides per-kernel
+    # boundaries
+    import plastax_b200.kernels as K
+
+    if step.lowk is not None:
+        sweep_t = _EventTimer(step.lowk.sweep)
+        step.lowk.sweep = sweep_t
+        sel_t = _EventTimer(step.lowk.select)
+        step.lowk.select = sel_t
+    else:
+        fwd_name = "mirror_forward" if step.use_mirror else "forward_prune"
+        sweep_t = _EventTimer(getattr(K, fwd_name))
+        setattr(K, fwd_name, sweep_t)
+        sel_t = None
+    ins_t = _EventTimer(K.mirror_insert)
+    K.mirror_insert = ins_t
     n_eager = min(Kst, 10)
     for i in range(n_eager):
         step(state, StepInputs(inputs_dev[W + i]))
     torch.cuda.synchronize()
-    setattr(K, fwd_name, orig_fp)
+    sweep_t.on = ins_t.on = False
+    if sel_t is not None:
+        sel_t.on = False
     use_graph = step.capturable()
     if use_graph:
         step.capture(state, StepInputs(inputs_dev[0]))
@@ -309,6 +375,7 @@ def engine_arm(args) -> None:
         dist.barrier()
     clocks = Clocks(local)
     clocks.start()
+    totals0 = step.lowk.totals.clone() if step.lowk is not None else None
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -320,10 +387,11 @@ def engine_arm(args) -> None:
         step(state, StepInputs(inputs_dev[(W + i) % inputs_dev.shape[0]]))
     t1.record()
     torch.cuda.synchronize()
+    clocks.pause()
     if world > 1:
         dist.barrier()
     elapsed_ms = t0.elapsed_time(t1)
-    fwd_ms = [s.elapsed_time(e) for s, e in fwd_events]
+    churn_dev = (step.lowk.totals - totals0) if step.lowk is not None else None
 
     # e2e: host inputs in pinned memory, H2D inside the region, D2H of the
     # step's overflow flag + grown count
@@ -332,18 +400,33 @@ def engine_arm(args) -> None:
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    clocks.resume()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
+    short = 0
     for i in range(Kst):
         res = step(state, StepInputs(host_in[i]))
         out = torch.stack([res.grown.to(torch.int32), res.overflow.to(torch.int32)])
         readback.copy_(out, non_blocking=True)
         torch.cuda.current_stream().synchronize()  # the Driver reads the flag every step
+        short += int(readback[0]) != cfg.k or int(readback[1]) != 0
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
     clk = clocks.stop()
+    step.check_status()  # raises on any device fault bit
+
+    # churn over the timed steps, device-counted (pruned summed over ranks)
+    churn = None
+    if churn_dev is not None:
+        if world > 1:
+            dist.all_reduce(churn_dev[:1], op=dist.ReduceOp.SUM)
+        pruned, grown, overflowed, firings = (int(v) for v in churn_dev.cpu().tolist())
+        churn = {"steps": firings, "pruned": pruned, "grown": grown, "overflowed": overflowed,
+                 "k_per_step": cfg.k, "e2e_steps_short_of_k": short}
+        if firings != Kst or pruned != Kst * cfg.k or grown != Kst * cfg.k or overflowed != 0 or short:
+            raise RuntimeError(f"bench: the timed steps did not churn k = {cfg.k} edges each: {churn}")
 
     if world > 1:
         t = torch.tensor([elapsed_ms, e2e_ms], dtype=torch.float64, device=dev)
@@ -361,10 +444,16 @@ def engine_arm(args) -> None:
     n = static.num_units
     per_entry = 8 if step.use_mirror else 13
     alg_bytes = per_entry * swept_entries + 8 * n
+    fwd_ms = sweep_t.ms()
     fwd_avg_s = float(np.mean(fwd_ms)) / 1e3 if fwd_ms else float("nan")
     achieved = alg_bytes / fwd_avg_s / 1e9
     peak, peak_kind = measured_peak_hbm()
     traffic = NCU_TRAFFIC_BYTES_PER_ENTRY * swept_entries if step.use_mirror else None
+    # the same launch against the canonical arena's 13 B per live slot (the
+    # bytes a sweep of the canonical columns would stream for these edges)
+    canon_bytes = 13 * (live // world) + 8 * n
+    ins_ms = float(np.mean(ins_t.ms())) if ins_t.events else None
+    sel_ms = float(np.mean(sel_t.ms())) if sel_t is not None and sel_t.events else None
 
     # launches of this library's kernels per step, counted once by the profiler
     launches_per_step = count_launches(step, state, inputs_dev[0], dev)
@@ -376,12 +465,18 @@ def engine_arm(args) -> None:
                 "ms_per_step": e2e_ms / Kst},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic,
-                     "kernel": ("mirror_sweep_kernel<sum, abs-below prune> (destination-grouped sweep + fused "
-                                "prune)" if step.use_mirror else
+                     "kernel": ("mirror_sweep_kernel<sum, lowest-k prune> (destination-grouped sweep + fused exact "
+                                "prune)" if step.lowk is not None else
+                                "mirror_sweep_kernel<sum, abs-below prune>" if step.use_mirror else
                                 "forward_vec4_kernel<sum, prune> (canonical sweep + prune)"),
                      "bytes_per_entry": per_entry, "entries_per_launch": swept_entries,
                      "kernel_ms": fwd_avg_s * 1e3, "alg_bytes_per_launch": alg_bytes, "peak_kind": peak_kind,
-                     "share_of_step": (fwd_avg_s * 1e3) / ms_per_step},
+                     "share_of_step": (fwd_avg_s * 1e3) / ms_per_step,
+                     "canonical_13B_per_slot": {"bytes": canon_bytes,
+                                                "achieved": canon_bytes / fwd_avg_s / 1e9,
+                                                "frac": canon_bytes / fwd_avg_s / 1e9 / peak},
+                     "upkeep_ms": {"mirror_insert": ins_ms, "lowk_select": sel_ms}},
+        "churn": churn,
         "clocks": clk,
         "cuda_graph": use_graph,
         "gpu_launches": launches_per_step * Kst,
@@ -402,16 +497,15 @@ def engine_arm(args) -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         del state
         torch.cuda.empty_cache()
-        from oracle import oracle as orc
-
-        threads = orc.max_threads()
+        threads = host_threads()
         times, _ = cpu_run(cfg, args.cpu_steps, 0, threads)
         per = float(np.median(times))
         line["cpu_baseline"] = {
             "value": live / per, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{len(times)} full-size churn steps of the oracle restatement (median) on {threads} host "
-                      f"threads (forward+prune, proposals, total order, the claim's free-slot lists; the in-order "
-                      f"candidate assignment sequential)",
+            "sample": f"{len(times)} full-size churn steps of the oracle restatement (median), each pruning and "
+                      f"regrowing k = {cfg.k} edges, on {threads} host threads (forward, the exact lowest-|w| "
+                      f"prune, proposals, total order, the claim's free-slot lists; the in-order candidate "
+                      f"assignment sequential)",
             "ms_per_step": per * 1e3}
     if rank == 0:
         print(json.dumps(line), flush=True)

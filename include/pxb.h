@@ -700,7 +700,8 @@ PXB_API int pxb_claim_prepare(int32_t mode, int64_t cap, const int32_t *from_id,
  * must hold step 1's results. With `free_bitmap` (as in step 1) the claimed
  * own-domain slots are found in and cleared from the bitmaps.
  * placed_out[k] (may be NULL): the local slot each candidate was written
- * to on this rank, -1 when none. */
+ * to on this rank, -1 when none. committed_out[k] (may be NULL): 1 for a
+ * candidate committed on any rank (the same on every rank), else 0. */
 PXB_API int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id,
                      int32_t *to_id, uint8_t *dead, float *weight,
                      const int32_t *unit_level, int32_t num_units,
@@ -713,8 +714,8 @@ PXB_API int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id,
                      int32_t n_extra, void *const *extra_cols,
                      const int32_t *extra_bytes, const void *const *extra_vals,
                      int32_t *counts_out, uint8_t *overflowed_out,
-                     int32_t *placed_out, void *scratch, size_t scratch_bytes,
-                     void *stream);
+                     int32_t *placed_out, uint8_t *committed_out,
+                     void *scratch, size_t scratch_bytes, void *stream);
 
 /* Per-domain free-slot bitmaps of a bucket: num_levels rows of
  * ceil(cap / 32) words; bit s of row d is set iff slot s is a claimable free
@@ -817,6 +818,122 @@ PXB_API int pxb_mirror_forward(const pxb_mirror *mirror, const float *act,
 PXB_API int pxb_mirror_insert(const pxb_mirror *mirror, int64_t k,
                               const int32_t *src, const int32_t *dst,
                               const float *weight, const int32_t *placed,
+                              void *stream);
+
+/* ------------------------------------------------------------------ */
+/* exact lowest-|w| prune fused into the mirror sweep                  */
+/* ------------------------------------------------------------------ */
+/* The k live edges of lowest |w| (ties by ascending global slot, a NaN
+ * weight never) are pruned every firing, as pxb_lowest_keys +
+ * pxb_topk_unique + pxb_prune_selected do, but without a selection over
+ * every slot: the order key of an edge is (bits(|w|), global slot), and two
+ * histograms of bits(|w|) over the live non-NaN edges are kept current on
+ * the device -- coarse bins (bits >> PXB_LOWK_SHIFT, 2^16) and fine bins
+ * (bits >> PXB_LOWK_FINE_SHIFT, 2^24; a fine bin spans 2^-16 of its
+ * value) -- built once (pxb_lowk_hist_build), cut by every plan (the bins a
+ * plan prunes are emptied) and raised by every committed growth edge
+ * (pxb_lowk_hist_add). Under Scheme-A every rank holds the same whole-arena
+ * histograms: each plan and each committed edge is the same on every rank.
+ *
+ * One firing:
+ *   1. pxb_lowk_make_plan: from the histograms, the fine threshold bin b* of
+ *      the k-th smallest key -- every edge in a bin below b* is pruned; of
+ *      the bin itself the `take` smallest keys, unless the whole bin is
+ *      needed (two launches: one CTA plans, a grid empties the fine bins
+ *      the plan prunes);
+ *   2. pxb_mirror_forward_lowk: the forward sweep; an edge below the bin is
+ *      tombstoned there (as the fused threshold prune does), an edge in the
+ *      bin is listed (key, source level, mirror position);
+ *   3. pxb_lowk_select (after every rank's sweep has finished: after
+ *      pxb_scheme_a_apply's barrier under Scheme-A): one CTA radix-selects
+ *      the take-th smallest key over every rank's list and tombstones this
+ *      rank's listed edges up to it; under Scheme-A it also adds every
+ *      rank's selected edges to level_before / level_totals (their claim
+ *      domains), so the per-domain counts that rode on the barrier stay
+ *      exact.
+ * The lists are double-buffered by the plan's parity, so a rank one step
+ * ahead never overwrites a list a peer still reads. plan->status: bit 0 a
+ * list overflowed list_cap (the threshold bin held more edges than the
+ * list -- only when that many live edges share a |w| to 2^-16; the step's
+ * prune is incomplete), bit 1 the swept counts disagree with the histogram
+ * (the histogram is stale: rebuild it). Replaces the lowest-magnitude prune
+ * phase (src/plastax/phases.py:1444-1498, with the k-th smallest |w| as the
+ * predicate's threshold, examples/dst_sparse.py:88-140) for a single-bucket
+ * arena with a mirror. */
+#define PXB_PRUNE_LOWEST_K 3
+#define PXB_LOWK_SHIFT 15
+#define PXB_LOWK_BINS 65536
+#define PXB_LOWK_FINE_SHIFT 7
+#define PXB_LOWK_FINE_BINS 16777216
+
+typedef struct pxb_lowk_plan { /* device memory, written by pxb_lowk_make_plan */
+  uint32_t lo_bits;     /* every live edge with bits(|w|) < lo_bits is pruned  */
+  uint32_t hi_bits;     /* lo_bits <= bits(|w|) < hi_bits: listed              */
+  int64_t take;         /* the listed edges pruned (smallest keys, all ranks)  */
+  int64_t below_expect; /* edges below lo_bits, all ranks (from the histogram) */
+  int64_t listed_expect;/* edges in [lo_bits, hi_bits), all ranks             */
+  int32_t parity;       /* the list buffer this firing writes                   */
+  int32_t status;       /* bit 0 list overflow, bit 1 counts disagree          */
+  int64_t pruned;       /* edges this rank pruned in the last firing           */
+  uint32_t floor;       /* no fine bin below this one holds an edge            */
+  uint32_t zero_lo;     /* fine bins [zero_lo, zero_hi) the last plan emptied  */
+  uint32_t zero_hi;
+  uint32_t pad;
+} pxb_lowk_plan;
+
+typedef struct pxb_lowk {
+  int32_t rank, world;
+  int64_t k;            /* edges pruned per firing (whole arena)               */
+  int64_t list_cap;     /* entries per list buffer                             */
+  int64_t slot_base;    /* this rank's first global slot                       */
+  uint32_t *hist;       /* [PXB_LOWK_BINS] coarse bins                         */
+  uint32_t *fine;       /* [PXB_LOWK_FINE_BINS] fine bins                      */
+  pxb_lowk_plan *plan;  /* device; zero it, then set floor = 0xFFFFFFFF, before
+                           the first pxb_lowk_hist_build                      */
+  /* this rank's lists (device; under Scheme-A inside its peer region) */
+  uint64_t *key;        /* [2 * list_cap] (bits(|w|) << 32) | global slot      */
+  int32_t *level;       /* [2 * list_cap] the listed slot's claim domain       */
+  unsigned long long *count; /* [4]: per parity {listed, pruned below lo_bits} */
+  int64_t *pos;         /* [2 * list_cap] mirror positions (-1 - i for the
+                           mirror's overflow entry i); never read by a peer    */
+  /* every rank's key / level / count (device arrays of `world` pointers,
+   * peers mapped into this rank's address space); NULL when world == 1 */
+  uint64_t *const *peer_key;
+  int32_t *const *peer_level;
+  unsigned long long *const *peer_count;
+} pxb_lowk;
+
+/* Both histograms += every live slot of a bucket whose weight is not NaN,
+ * and plan->floor lowered to the lowest fine bin seen (the caller zeroes the
+ * histograms and sets the plan first). */
+PXB_API int pxb_lowk_hist_build(const pxb_lowk *lowk, int64_t cap,
+                                const uint8_t *dead, const float *weight,
+                                void *stream);
+/* Step 1 above; one CTA. */
+PXB_API int pxb_lowk_make_plan(const pxb_lowk *lowk, void *stream);
+/* Step 2 above: pxb_mirror_forward with the plan's prune; bitmap_level
+ * (PIPELINE, else NULL) names the claim domain of a pruned or listed slot. */
+PXB_API int pxb_mirror_forward_lowk(const pxb_mirror *mirror, const float *act,
+                                    int32_t monoid, float *acc,
+                                    int64_t *acc_fixed, const pxb_lowk *lowk,
+                                    uint8_t *dead, uint32_t *free_bitmap,
+                                    int64_t bitmap_words,
+                                    const int32_t *bitmap_level, void *stream);
+/* Step 3 above; one CTA. level_before / level_totals ([num_levels], may be
+ * NULL) receive every rank's selected edges per claim domain. */
+PXB_API int pxb_lowk_select(const pxb_lowk *lowk, const pxb_mirror *mirror,
+                            uint8_t *dead, uint32_t *free_bitmap,
+                            int64_t bitmap_words, const int32_t *bitmap_level,
+                            int32_t num_levels, int32_t *level_before,
+                            int32_t *level_totals, void *stream);
+/* hist[bin(weight[i])] += 1 for every committed[i] (pxb_claim_commit's
+ * committed_out) whose weight is not NaN: the growth edges of a firing.
+ * totals ([4] int64, may be NULL) accumulate {edges this rank pruned in
+ * the firing, claim_counts[0] committed, claim_counts[1] overflowed,
+ * firings} (claim_counts: pxb_claim_commit's counts_out, may be NULL). */
+PXB_API int pxb_lowk_hist_add(const pxb_lowk *lowk, int64_t k,
+                              const float *weight, const uint8_t *committed,
+                              const int32_t *claim_counts, int64_t *totals,
                               void *stream);
 
 /* ------------------------------------------------------------------ */

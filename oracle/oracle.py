@@ -56,6 +56,7 @@ def lib() -> ctypes.CDLL:
     h.pxo_unit_float.argtypes = [ctypes.c_uint32]
     h.pxo_select_step.restype = ctypes.c_int64
     h.pxo_max_threads.restype = ctypes.c_int
+    h.pxo_lowest_prune.restype = ctypes.c_int64
     return h
 
 
@@ -289,6 +290,15 @@ def forward_prune_mt(b: dict, act: np.ndarray, n: int, threshold: float, acc: np
     lib().pxo_forward_prune_mt(_i64(b["dead"].size), _p(b["from_id"]), _p(b["to_id"]), _p(b["dead"]),
                                _p(b["weight"]), _p(act), ctypes.c_int32(n), ctypes.c_float(threshold), _p(acc),
                                ctypes.c_int(threads), _p(work))
+
+
+def lowest_prune(b: dict, k: int, threads: int = 1) -> int:
+    """Tombstone the k live edges of lowest |w| of one bucket (ties by
+    ascending slot, NaN never), in place; returns the number pruned
+    (src/plastax/phases.py:1444-1498 with the k-th smallest |w| as the
+    threshold, examples/dst_sparse.py:88-140)."""
+    return int(lib().pxo_lowest_prune(_i64(b["dead"].size), _p(b["dead"]), _p(b["weight"]), _i64(k),
+                                      ctypes.c_int(threads)))
 
 
 def max_threads() -> int:

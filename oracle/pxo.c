@@ -679,6 +679,115 @@ void pxo_forward_prune_mt(int64_t cap, const int32_t *from, const int32_t *to, u
 #endif
 }
 
+/* ------------------------------------------------------------------ */
+/* The lowest-magnitude prune of the churn configurations: the k live   */
+/* edges of lowest |w| (ties by ascending slot, a NaN weight never) are */
+/* tombstoned -- the predicate prune of src/plastax/phases.py:1444-1498 */
+/* with the k-th smallest |w| as its threshold, the one the reference's */
+/* churn computes from the current weights before each firing           */
+/* (examples/dst_sparse.py:88-140), ties cut by slot so exactly k go.   */
+/* Found by a histogram of bits(|w|) >> 15 (|w|'s bit pattern is        */
+/* monotone in |w|), then a sort of the threshold bin's (bits, slot).   */
+/* Returns the number pruned.                                           */
+/* ------------------------------------------------------------------ */
+#define PXO_LOWK_BINS 65536
+#define PXO_INF_BITS 0x7f800000u
+
+static inline uint32_t abs_bits(float w) {
+  uint32_t u;
+  memcpy(&u, &w, 4);
+  return u & 0x7fffffffu;
+}
+
+static int key_cmp(const void *pa, const void *pb) {
+  const uint64_t a = *(const uint64_t *)pa, b = *(const uint64_t *)pb;
+  return a < b ? -1 : (a > b ? 1 : 0);
+}
+
+int64_t pxo_lowest_prune(int64_t cap, uint8_t *dead, const float *w, int64_t k, int threads) {
+  if (k <= 0 || cap <= 0) return 0;
+  if (threads < 1) threads = 1;
+  int64_t *hist = (int64_t *)calloc((size_t)threads * PXO_LOWK_BINS, sizeof(int64_t));
+#ifdef _OPENMP
+#pragma omp parallel num_threads(threads)
+#endif
+  {
+#ifdef _OPENMP
+    const int tid = omp_get_thread_num(), nt = omp_get_num_threads();
+#else
+    const int tid = 0, nt = 1;
+#endif
+    int64_t *mine = hist + (int64_t)tid * PXO_LOWK_BINS;
+    const int64_t lo = cap * tid / nt, hi = cap * (tid + 1) / nt;
+    for (int64_t s = lo; s < hi; ++s) {
+      if (dead[s]) continue;
+      const uint32_t b = abs_bits(w[s]);
+      if (b <= PXO_INF_BITS) mine[b >> 15]++;
+    }
+  }
+  for (int t = 1; t < threads; ++t)
+    for (int j = 0; j < PXO_LOWK_BINS; ++j) hist[j] += hist[(int64_t)t * PXO_LOWK_BINS + j];
+  int64_t below = 0, total = 0;
+  int bin = -1;
+  for (int j = 0; j < PXO_LOWK_BINS; ++j) total += hist[j];
+  if (total > k) {
+    for (int j = 0; j < PXO_LOWK_BINS; ++j) {
+      if (below + hist[j] >= k) {
+        bin = j;
+        break;
+      }
+      below += hist[j];
+    }
+  }
+  /* edges with bits < lo go; of [lo, hi) the `take` smallest (bits, slot) */
+  uint32_t lo_bits, hi_bits;
+  int64_t take = 0, in_bin = 0;
+  if (bin < 0) {
+    lo_bits = hi_bits = PXO_INF_BITS + 1;
+  } else {
+    take = k - below;
+    in_bin = hist[bin];
+    lo_bits = (uint32_t)bin << 15;
+    hi_bits = (uint32_t)(bin + 1) << 15;
+    if (hi_bits > PXO_INF_BITS + 1) hi_bits = PXO_INF_BITS + 1;
+    if (take == in_bin) {
+      lo_bits = hi_bits;
+      take = 0;
+    }
+  }
+  free(hist);
+  uint64_t *ties = take > 0 ? (uint64_t *)malloc((size_t)in_bin * sizeof(uint64_t)) : NULL;
+  int64_t n_ties = 0, pruned = 0;
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static) num_threads(threads) reduction(+ : pruned)
+#endif
+  for (int64_t s = 0; s < cap; ++s) {
+    if (dead[s]) continue;
+    const uint32_t b = abs_bits(w[s]);
+    if (b < lo_bits) {
+      dead[s] = 1;
+      ++pruned;
+    } else if (b < hi_bits && ties != NULL) {
+      int64_t i;
+#ifdef _OPENMP
+#pragma omp atomic capture
+#endif
+      i = n_ties++;
+      if (i < in_bin) ties[i] = ((uint64_t)b << 32) | (uint64_t)(uint32_t)s;
+    }
+  }
+  if (ties != NULL) {
+    if (n_ties > in_bin) n_ties = in_bin;
+    qsort(ties, (size_t)n_ties, sizeof(uint64_t), key_cmp);
+    for (int64_t i = 0; i < take && i < n_ties; ++i) {
+      dead[(int64_t)(uint32_t)ties[i]] = 1;
+      ++pruned;
+    }
+    free(ties);
+  }
+  return pruned;
+}
+
 int pxo_max_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();

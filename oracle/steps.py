@@ -55,15 +55,22 @@ def lowest_prune(buckets: list[dict], k: int) -> int:
 
 class ReservoirOracle:
     """The reservoir churn step (PIPELINE: forward, prune, per-unit
-    proposal growth with a step-scoped cap, pipeline claim) on host arrays."""
+    proposal growth with a step-scoped cap, pipeline claim) on host arrays.
+    `prune` "lowest_k": the k live edges of lowest |w| go every step (ties
+    by slot); "threshold": every edge with |w| < tau."""
 
     def __init__(self, bucket: dict, act: np.ndarray, level: np.ndarray, tail_start: int, *, num_inputs: int,
-                 num_res: int, tau: float, k: int, init_a: float, seed: int = 0, threads: int = 1) -> None:
+                 num_res: int, tau: float, k: int, init_a: float, seed: int = 0, threads: int = 1,
+                 prune: str = "lowest_k") -> None:
+        if prune not in ("lowest_k", "threshold"):
+            raise ValueError(f"unknown prune {prune!r}")
         self.b, self.act, self.level = bucket, act, level
         self.tail = int(tail_start)
         self.n = act.size
         self.num_inputs, self.num_res = num_inputs, num_res
         self.tau, self.k, self.init_a, self.seed = tau, k, init_a, seed
+        self.prune = prune
+        self.last_pruned = 0
         self.threads = threads
         self.is_input = np.zeros(self.n, np.uint8)
         self.is_input[:num_inputs] = 1
@@ -74,13 +81,20 @@ class ReservoirOracle:
         n, b = self.n, self.b
         self.act[: self.num_inputs] = inputs
         acc = np.zeros(n, np.float32)
+        lowest = self.prune == "lowest_k"
         if self.threads > 1:
-            orc.forward_prune_mt(b, self.act, n, self.tau, acc, self.threads)
+            # the forward with the threshold prune fused (a threshold of 0
+            # prunes nothing: the lowest-k prune runs after it)
+            orc.forward_prune_mt(b, self.act, n, 0.0 if lowest else self.tau, acc, self.threads)
         else:
             orc.forward_accumulate(b, self.act, n, "sum", acc)
         orc.unit_apply(n, 0, "tanh", "sum", acc, None, None, None, 0, self.is_input, None, self.act)
-        if self.threads <= 1:
+        if lowest:
+            self.last_pruned = orc.lowest_prune(b, self.k, self.threads)
+        elif self.threads <= 1:
+            dead0 = int(b["dead"].sum())
             orc.prune(b, n, 1, self.tau)
+            self.last_pruned = int(b["dead"].sum()) - dead0
         th = self.threads
         src, dst, score = orc.propose_per_unit(n, 1, self.seed, self.step_count, self.num_inputs, self.num_res, 0,
                                                self.level, max_level_gap=1, threads=th)

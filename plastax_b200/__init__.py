@@ -9,6 +9,7 @@ a missing libpxb.so is an error.
 """
 
 from plastax_b200 import monoid, optim
+from plastax_b200._lib import PxbError
 from plastax_b200.builder import NetworkBuilder
 from plastax_b200.state import NetworkState, NetworkStatic, live_conn_count, make_empty_state
 from plastax_b200.state import grow_bucket
@@ -61,7 +62,7 @@ __all__ = [
     "ACTIVATION", "DEAD", "FROM_ID", "GRAD_PRE_ACT", "LEVEL", "LOSS_GRAD", "PRUNED", "TO_ID", "WEIGHT",
     "BackwardPass", "DestinationThresholdPrune", "Driver", "FieldSpec", "ForwardPass", "GrowthRemainder", "MSELoss",
     "MagnitudePrune", "MeanFloatFirstRest", "Network", "NetworkBuilder", "NetworkState", "NetworkStatic", "Propagation", "ProposeAddConn",
-    "PruneConn", "ResetGlobal", "ScoreAddConn", "ShardSpec", "SoftmaxCrossEntropyLoss", "StepFn", "StepInputs", "StepResult", "live_conn_count",
+    "PruneConn", "PxbError", "ResetGlobal", "ScoreAddConn", "ShardSpec", "SoftmaxCrossEntropyLoss", "StepFn", "StepInputs", "StepResult", "live_conn_count",
     "grow_bucket", "make_empty_state", "make_growth_retry", "make_step", "monoid", "optim", "predicate_add_conn",
     "recommended_shortlist", "resort", "shortlist_coverage", "ShortlistCoverage",
 ]

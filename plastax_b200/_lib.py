@@ -30,7 +30,9 @@ c_ptr = ctypes.c_void_p
 # constants of include/pxb.h
 MONOID = {"sum": 0, "max": 1, "min": 2}
 ACT = {"identity": 0, "tanh": 1, "relu": 2, "sigmoid": 3}
-PRUNE_NONE, PRUNE_ABS_BELOW, PRUNE_ABS_BELOW_DST = 0, 1, 2
+PRUNE_NONE, PRUNE_ABS_BELOW, PRUNE_ABS_BELOW_DST, PRUNE_LOWEST_K = 0, 1, 2, 3
+LOWK_BINS, LOWK_SHIFT = 65536, 15
+LOWK_FINE_BINS, LOWK_FINE_SHIFT = 1 << 24, 7
 OPT = {"sgd": 0, "momentum": 1, "adam": 2, "rmsprop": 3, "upgd": 4}
 SCORE_UNIFORM, SCORE_UNIFORM_Q256, SCORE_GRAD_ACT = 0, 1, 2
 INIT_CONST, INIT_DYADIC, INIT_HASH_UNIFORM = 0, 1, 2
@@ -73,6 +75,17 @@ class PeerGroup(ctypes.Structure):
     _fields_ = [
         ("rank", c_i32), ("world", c_i32), ("acc_fixed", c_ptr), ("acc_side", c_ptr), ("act", c_ptr),
         ("flags", c_ptr), ("counts", c_ptr), ("epoch", c_ptr), ("done", c_ptr), ("status", c_ptr),
+    ]
+
+
+class Lowk(ctypes.Structure):
+    """`pxb_lowk`: the exact lowest-|w| prune's histogram, plan and lists."""
+
+    _fields_ = [
+        ("rank", c_i32), ("world", c_i32), ("k", c_i64), ("list_cap", c_i64), ("slot_base", c_i64),
+        ("hist", c_ptr), ("fine", c_ptr), ("plan", c_ptr), ("key", c_ptr), ("level", c_ptr), ("count", c_ptr),
+        ("pos", c_ptr),
+        ("peer_key", c_ptr), ("peer_level", c_ptr), ("peer_count", c_ptr),
     ]
 
 
@@ -187,8 +200,8 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_claim_commit": (
         c_i32,
         [c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i64, c_i64, c_ptr, c_i64, c_ptr, c_ptr,
-         c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_size,
-         c_ptr],
+         c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr,
+         c_size, c_ptr],
     ),
     "pxb_free_bitmap_build": (c_i32, [c_i32, c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i64, c_ptr, c_ptr, c_ptr]),
     "pxb_propose_global": (c_i32, [c_i32, ctypes.c_uint64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_ptr,
@@ -209,6 +222,11 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_mirror_forward": (
         c_i32, [c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_i32, c_f32, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr]),
     "pxb_mirror_insert": (c_i32, [c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
+    "pxb_lowk_hist_build": (c_i32, [c_ptr, c_i64, c_ptr, c_ptr, c_ptr]),
+    "pxb_lowk_make_plan": (c_i32, [c_ptr, c_ptr]),
+    "pxb_mirror_forward_lowk": (c_i32, [c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr]),
+    "pxb_lowk_select": (c_i32, [c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_i32, c_ptr, c_ptr, c_ptr]),
+    "pxb_lowk_hist_add": (c_i32, [c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_growth_flags": (c_i32, [c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_peer_alloc": (c_i32, [c_size, ctypes.POINTER(c_ptr), c_ptr]),
     "pxb_peer_open": (c_i32, [c_ptr, ctypes.POINTER(c_ptr)]),

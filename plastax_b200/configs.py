@@ -8,8 +8,14 @@ input weights U(-1, 1), every reservoir unit fed by every input).
 
 The churn rule, frozen here so the oracle and the engine run the same
 network:
-- PruneConn: |w| < tau with tau = 0.0012533 * sigma, the threshold that
-  removes 0.1% of N(0, sigma^2) weights (the half-normal 0.1% quantile);
+- PruneConn: the k = 0.1% x recurrent-edge-count live edges of lowest |w|,
+  every step (the k-th smallest |w| of the state before the step as the
+  threshold, as the reference's churn recomputes it from the current
+  weights, examples/dst_sparse.py:88-140; ties by ascending slot, so
+  exactly k go and the live-edge count stays constant under regrowth).
+  `prune="threshold"` keeps the older fixed rule |w| < tau with
+  tau = 0.0012533 * sigma (the half-normal 0.1% quantile of the initial
+  weights), which prunes 0.1% only on the first step;
 - ProposeAddConn(per_unit, P=1): src = proposing unit, dst = a uniform
   reservoir unit [sub 0], score = uniform() [sub 1], the step's
   max_new_per_level = 0.1% of the recurrent edges under
@@ -27,7 +33,7 @@ import torch
 
 from plastax_b200 import monoid
 from plastax_b200.builder import NetworkBuilder
-from plastax_b200.traits import ForwardPass, MagnitudePrune, Network, ProposeAddConn
+from plastax_b200.traits import ForwardPass, LowestMagnitudePrune, MagnitudePrune, Network, ProposeAddConn
 from plastax_b200.types import Propagation, ShardSpec
 
 
@@ -41,6 +47,7 @@ class ReservoirConfig:
     capacity_align: int = 8192
     capacity_headroom: float = 0.01
     seed: int = 0
+    prune: str = "lowest_k"  # or "threshold"
 
     @property
     def sigma(self) -> float:
@@ -73,7 +80,7 @@ C5 = ReservoirConfig()
 def reservoir_net(cfg: ReservoirConfig, sharding: ShardSpec | None = None) -> type[Network]:
     class ReservoirChurn(Network):
         forward_pass = ForwardPass("tanh", monoid.sum_)
-        prune_conn = MagnitudePrune(cfg.tau)
+        prune_conn = LowestMagnitudePrune(cfg.k) if cfg.prune == "lowest_k" else MagnitudePrune(cfg.tau)
         add_conn = ProposeAddConn(
             proposals_per_proposer=1, max_new_per_level=cfg.k, dst_lo=cfg.num_inputs, dst_n=cfg.num_units,
             score="uniform", init=("hash_uniform", cfg.sigma * math.sqrt(3.0)), level_cap_scope="step")

@@ -406,6 +406,7 @@ struct WriteArgs {
   uint32_t *bm;  // per-domain free bitmaps to clear at placed own slots, or NULL
   int64_t bm_words;
   int32_t *placed;  // per candidate: the local slot written, -1 when none
+  uint8_t *committed;  // per candidate: 1 when committed on any rank, or NULL
 };
 
 // One thread per sorted claim position: choose the slot and write.
@@ -423,6 +424,7 @@ __global__ void place_kernel(CandArgs c, WriteArgs w, const uint32_t *__restrict
     const int32_t i = idx[p];
     if (overflowed) overflowed[i] = 0;
     if (w.placed) w.placed[i] = -1;
+    if (w.committed) w.committed[i] = 0;
     if (l >= static_cast<uint32_t>(c.num_levels)) continue;
     const int32_t own_rank = static_cast<int32_t>(p) - first[l];
     int64_t slot = -1;
@@ -443,6 +445,7 @@ __global__ void place_kernel(CandArgs c, WriteArgs w, const uint32_t *__restrict
       }
     }
     if (committed) {
+      if (w.committed) w.committed[i] = 1;
       atomicAdd(counts + 0, 1);
       if (to_tail) atomicAdd(counts + 2, 1);
       const int32_t s = c.src[i], d = c.dst[i];
@@ -575,8 +578,8 @@ extern "C" int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id, int
                                 const uint8_t *growable, int64_t max_new, const int32_t *level_before,
                                 const int32_t *level_totals, uint32_t *free_bitmap, int32_t n_extra,
                                 void *const *extra_cols, const int32_t *extra_bytes, const void *const *extra_vals,
-                                int32_t *counts_out, uint8_t *overflowed_out, int32_t *placed_out, void *scratch,
-                                size_t scratch_bytes, void *stream) {
+                                int32_t *counts_out, uint8_t *overflowed_out, int32_t *placed_out,
+                                uint8_t *committed_out, void *scratch, size_t scratch_bytes, void *stream) {
   const bool level_major = (mode & PXB_CLAIM_LEVEL_MAJOR) != 0;
   mode &= ~PXB_CLAIM_LEVEL_MAJOR;
   int rc = claim_common_checks("pxb_claim_commit", mode, cap, num_levels);
@@ -613,6 +616,7 @@ extern "C" int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id, int
   w.bm = free_bitmap;
   w.bm_words = (cap + 31) / 32;
   w.placed = placed_out;
+  w.committed = committed_out;
   for (int e = 0; e < n_extra; ++e) {
     PXB_REQUIRE(extra_cols && extra_bytes && extra_vals && extra_cols[e] && extra_vals[e],
                 "pxb_claim_commit: extra column %d is NULL", e);

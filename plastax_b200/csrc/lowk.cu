@@ -1,0 +1,467 @@
+// The exact lowest-|w| prune fused into the mirror sweep: the k live edges
+// of lowest |w| (ties by ascending global slot, a NaN weight never) leave
+// the arena every firing, the same set pxb_lowest_keys + pxb_topk_unique +
+// pxb_prune_selected would choose, without a selection over every slot.
+//
+// An edge's order key is (bits(|w|), global slot): bits(|w|) of a float
+// without its sign is monotone in |w|. A histogram of the key's top 16 bits
+// over the live non-NaN edges is kept current on the device, so the plan
+// before each sweep knows the threshold bin b*: every edge in a lower bin is
+// pruned by the sweep itself; the sweep lists the edges of bin b* (a few
+// thousand at the benchmark's size, out of 285 M), and one CTA
+// radix-selects the `take` smallest of them afterwards. The histogram is
+// then cut by the plan and raised by every committed growth edge, which
+// keeps it equal to the arena's (checked every firing: the counts the
+// sweeps saw must equal the counts the plan expected).
+//
+// Under Scheme-A the lists sit in every rank's peer region and the select
+// reads every rank's list after the peer barrier of the forward's combine;
+// each rank tombstones its own selected edges and adds every rank's to the
+// claim's per-domain counts that rode on that barrier. The lists are
+// double-buffered by the plan's parity, so a rank a step ahead never
+// overwrites a list a peer still reads.
+#include <cub/block/block_scan.cuh>
+
+#include "mirror.cuh"
+
+namespace pxb {
+
+constexpr int kLowkShift = PXB_LOWK_SHIFT;
+constexpr int kLowkBins = PXB_LOWK_BINS;
+constexpr int kFineShift = PXB_LOWK_FINE_SHIFT;
+constexpr int kFinePer = 1 << (kLowkShift - kFineShift);  // fine bins per coarse bin
+constexpr uint32_t kFineBins = PXB_LOWK_FINE_BINS;
+constexpr uint32_t kInfBits = 0x7f800000u;  // +inf; anything above is a NaN
+constexpr uint32_t kAllBits = kInfBits + 1;   // a cut that prunes every non-NaN edge
+constexpr int kPlanThreads = 1024;
+constexpr int kBinsPerThread = kLowkBins / kPlanThreads;
+constexpr int kSelectThreads = 1024;
+constexpr int kMaxWorld = 64;
+constexpr int kMaxLevels = PXB_PEER_MAX_LEVELS;
+static_assert(kLowkBins == (1 << (31 - kLowkShift)), "the coarse bins cover bits(|w|) >> PXB_LOWK_SHIFT");
+static_assert(kFineBins == (1u << (31 - kFineShift)), "the fine bins cover bits(|w|) >> PXB_LOWK_FINE_SHIFT");
+static_assert(kFinePer <= kPlanThreads, "one plan thread per fine bin of the threshold's coarse bin");
+
+__global__ void lowk_hist_build_kernel(int64_t cap, const uint8_t *__restrict__ dead,
+                                       const float *__restrict__ weight, uint32_t *__restrict__ hist,
+                                       uint32_t *__restrict__ fine, pxb_lowk_plan *plan) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t span = (cap + stride - 1) / stride * stride;  // every lane of a warp runs every iteration
+  uint32_t lowest = 0xffffffffu;
+  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < span; s += stride) {
+    uint32_t b = 0xffffffffu;
+    if (s < cap && dead[s] == 0) {
+      b = abs_bits(weight[s]);
+      if (b > kInfBits) b = 0xffffffffu;
+    }
+    const uint32_t bin = b == 0xffffffffu ? b : b >> kLowkShift;
+    // lanes of one coarse bin add once (the weights crowd a few hundred bins)
+    const uint32_t same = __match_any_sync(0xffffffffu, bin);
+    if (bin != 0xffffffffu && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(hist + bin, __popc(same));
+    if (b != 0xffffffffu) {
+      atomicAdd(fine + (b >> kFineShift), 1u);
+      lowest = min(lowest, b >> kFineShift);
+    }
+  }
+  lowest = __reduce_min_sync(0xffffffffu, lowest);
+  if ((threadIdx.x & 31) == 0 && lowest != 0xffffffffu) atomicMin(&plan->floor, lowest);
+}
+
+// One CTA: the fine threshold bin of the k-th smallest key (the coarse bin
+// first, then its fine bins), the plan, the coarse histogram's cut and the
+// fine bin's part; the fine bins wholly pruned are emptied by
+// lowk_zero_kernel from the plan's [zero_lo, zero_hi). This rank's list
+// counters of the new parity are reset.
+__global__ void __launch_bounds__(kPlanThreads) lowk_plan_kernel(uint32_t *__restrict__ hist,
+                                                                 uint32_t *__restrict__ fine, pxb_lowk_plan *plan,
+                                                                 int64_t k, unsigned long long *count) {
+  using Scan = cub::BlockScan<long long, kPlanThreads>;
+  __shared__ typename Scan::TempStorage scan_tmp;
+  __shared__ int s_bin, s_fbin;
+  __shared__ long long s_below_c, s_below, s_in_bin;
+  const int t = threadIdx.x;
+  uint32_t mine[kBinsPerThread];
+  long long sum = 0;
+#pragma unroll 8
+  for (int j = 0; j < kBinsPerThread; ++j) {
+    mine[j] = hist[t * kBinsPerThread + j];
+    sum += mine[j];
+  }
+  long long excl, total;
+  Scan(scan_tmp).ExclusiveSum(sum, excl, total);
+  if (t == 0) {
+    s_bin = -1;
+    s_fbin = -1;
+  }
+  __syncthreads();
+  if (k > 0 && total > k && excl < k && excl + sum >= k) {
+    long long c = excl;
+    for (int j = 0; j < kBinsPerThread; ++j) {
+      if (c + mine[j] >= k) {
+        s_bin = t * kBinsPerThread + j;
+        s_below_c = c;
+        break;
+      }
+      c += mine[j];
+    }
+  }
+  __syncthreads();
+  const int b = s_bin;
+  if (b >= 0) {
+    // the coarse bin's fine bins, one per thread
+    const uint32_t f = t < kFinePer ? fine[static_cast<int64_t>(b) * kFinePer + t] : 0u;
+    long long fexcl, ftotal;
+    __syncthreads();  // scan_tmp is reused
+    Scan(scan_tmp).ExclusiveSum(static_cast<long long>(f), fexcl, ftotal);
+    const long long want = k - s_below_c;  // the rank inside the coarse bin, 1-based
+    if (t < kFinePer && fexcl < want && fexcl + f >= want) {
+      s_fbin = b * kFinePer + t;
+      s_below = s_below_c + fexcl;
+      s_in_bin = f;
+    }
+    __syncthreads();
+  }
+  const int fb = s_fbin;
+  const uint32_t old_floor = plan->floor;
+  // the fine bins of the coarse bin must hold its count; if they do not,
+  // the histograms are stale: prune nothing and report it
+  const bool stale = b >= 0 && fb < 0;
+  if (stale) k = 0;
+  long long take = 0;
+  bool whole = false;
+  uint32_t cut;  // fine bins below `cut` are emptied
+  if (k <= 0) {
+    cut = 0u;
+  } else if (fb < 0) {
+    cut = kFineBins;  // k >= every counted edge: all of them go
+  } else {
+    take = k - s_below;
+    whole = take == s_in_bin;
+    cut = whole ? static_cast<uint32_t>(fb) + 1u : static_cast<uint32_t>(fb);
+    if (whole) take = 0;
+  }
+  __syncthreads();  // every thread has read plan->floor
+  if (t == 0) {
+    pxb_lowk_plan p = *plan;
+    p.parity ^= 1;
+    if (k <= 0) {
+      p.lo_bits = p.hi_bits = 0u;
+      p.below_expect = 0;
+    } else if (fb < 0) {
+      p.lo_bits = p.hi_bits = kAllBits;
+      p.below_expect = total;
+    } else {
+      const uint32_t end = static_cast<uint32_t>(fb + 1) << kFineShift;
+      const uint32_t hi = end < kAllBits ? end : kAllBits;
+      p.lo_bits = whole ? hi : static_cast<uint32_t>(fb) << kFineShift;
+      p.hi_bits = hi;
+      p.below_expect = whole ? k : s_below;
+    }
+    p.take = take;
+    p.listed_expect = take > 0 ? s_in_bin : 0;
+    p.pruned = 0;
+    if (stale) p.status |= 2;
+    p.zero_lo = old_floor < cut ? old_floor : cut;
+    p.zero_hi = cut;
+    if (k > 0) p.floor = cut > old_floor ? cut : old_floor;
+    *plan = p;
+    count[2 * p.parity] = 0ull;
+    count[2 * p.parity + 1] = 0ull;
+    if (fb >= 0 && !whole) fine[fb] -= static_cast<uint32_t>(take);
+  }
+  // the coarse cut: bins wholly below the threshold's emptied, its own bin
+  // loses what its fine bins lose
+  if (k > 0) {
+    const int cb = fb < 0 ? kLowkBins : b;
+    const long long removed_in_b = fb < 0 ? 0 : (s_below - s_below_c) + (whole ? s_in_bin : take);
+#pragma unroll 8
+    for (int j = 0; j < kBinsPerThread; ++j) {
+      const int bin = t * kBinsPerThread + j;
+      if (bin < cb) {
+        if (mine[j]) hist[bin] = 0u;
+      } else if (bin == cb && removed_in_b > 0) {
+        hist[bin] = mine[j] - static_cast<uint32_t>(removed_in_b);
+      }
+    }
+  }
+}
+
+// The fine bins the plan prunes wholly: [zero_lo, zero_hi) (between the
+// lowest bin that may hold an edge and the threshold bin).
+__global__ void lowk_zero_kernel(uint32_t *__restrict__ fine, const pxb_lowk_plan *plan) {
+  const uint32_t lo = plan->zero_lo, hi = plan->zero_hi;
+  for (int64_t i = lo + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < hi;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    fine[i] = 0u;
+}
+
+struct SelectArgs {
+  pxb_lowk_plan *plan;
+  int32_t rank, world;
+  int64_t cap, slot_base;
+  const uint64_t *my_key;
+  const int32_t *my_level;
+  const int64_t *my_pos;
+  const unsigned long long *my_count;
+  uint64_t *const *peer_key;
+  int32_t *const *peer_level;
+  unsigned long long *const *peer_count;
+  uint8_t *dead;
+  uint32_t *bm;
+  int64_t bm_words;
+  const int32_t *bm_level;
+  int32_t num_levels;
+  int32_t *level_before, *level_totals;
+};
+
+// The group holding mirror position pos: the last g with gbase[g] <= pos.
+__device__ __forceinline__ int64_t group_of(const MirrorK &m, int64_t pos) {
+  int64_t lo = 0, hi = m.groups - 1;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) / 2;
+    if (m.gbase[mid] <= pos) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ const uint64_t *keys_of(const SelectArgs &a, int q) {
+  return a.world == 1 ? a.my_key : a.peer_key[q];
+}
+
+// One CTA: every rank's listed keys of this firing, the take-th smallest by
+// an 8-bit MSD radix select, this rank's listed edges up to it tombstoned.
+__global__ void __launch_bounds__(kSelectThreads) lowk_select_kernel(SelectArgs a, MirrorK m) {
+  __shared__ unsigned int digit_hist[256];
+  __shared__ int64_t s_n[kMaxWorld];
+  __shared__ unsigned long long s_prefix, s_mask;
+  __shared__ long long s_want;
+  __shared__ int s_sel[kMaxWorld * kMaxLevels];
+  __shared__ int s_pruned;
+  const int t = threadIdx.x;
+  const int parity = a.plan->parity;
+  const long long take = a.plan->take;
+  const int64_t base = static_cast<int64_t>(parity) * a.cap;
+  if (t == 0) {
+    long long listed = 0, below = 0;
+    int status = 0;
+    for (int q = 0; q < a.world; ++q) {
+      const unsigned long long *cnt = a.world == 1 ? a.my_count : a.peer_count[q];
+      unsigned long long n = cnt[2 * parity];
+      if (n > static_cast<unsigned long long>(a.cap)) {
+        status |= 1;
+        n = static_cast<unsigned long long>(a.cap);
+      }
+      s_n[q] = static_cast<int64_t>(n);
+      listed += static_cast<long long>(n);
+      below += static_cast<long long>(cnt[2 * parity + 1]);
+    }
+    if (listed != a.plan->listed_expect || below != a.plan->below_expect) status |= 2;
+    if (status) atomicOr(&a.plan->status, status);
+    s_prefix = 0ull;
+    s_mask = 0ull;
+    s_want = take;
+    s_pruned = 0;
+  }
+  for (int i = t; i < kMaxWorld * kMaxLevels; i += kSelectThreads) s_sel[i] = 0;
+  __syncthreads();
+  long long listed_total = 0;
+  for (int q = 0; q < a.world; ++q) listed_total += s_n[q];
+  if (take <= 0) {
+    if (t == 0) a.plan->pruned = static_cast<int64_t>(a.my_count[2 * parity + 1]);
+    return;
+  }
+  unsigned long long kstar = ~0ull;  // take >= every listed key: all of them
+  if (take < listed_total) {
+    for (int shift = 56; shift >= 0; shift -= 8) {
+      for (int d = t; d < 256; d += kSelectThreads) digit_hist[d] = 0u;
+      __syncthreads();
+      const unsigned long long prefix = s_prefix, mask = s_mask;
+      for (int q = 0; q < a.world; ++q) {
+        const uint64_t *keys = keys_of(a, q) + base;
+        for (int64_t i = t; i < s_n[q]; i += kSelectThreads) {
+          const unsigned long long key = keys[i];
+          if ((key & mask) == prefix) atomicAdd(&digit_hist[(key >> shift) & 255u], 1u);
+        }
+      }
+      __syncthreads();
+      if (t == 0) {
+        long long cum = 0;
+        const long long want = s_want;
+        int d = 0;
+        for (; d < 255; ++d) {
+          if (cum + digit_hist[d] >= want) break;
+          cum += digit_hist[d];
+        }
+        s_prefix = prefix | (static_cast<unsigned long long>(d) << shift);
+        s_mask = mask | (255ull << shift);
+        s_want = want - cum;
+      }
+      __syncthreads();
+    }
+    kstar = s_prefix;  // the keys are unique: exactly `take` of them are <= kstar
+  }
+  // this rank's selected edges leave the arena and the mirror
+  int mine = 0;
+  const uint64_t *my_keys = a.my_key + base;
+  for (int64_t i = t; i < s_n[a.rank]; i += kSelectThreads) {
+    const unsigned long long key = my_keys[i];
+    if (key > kstar) continue;
+    const int32_t slot = static_cast<int32_t>(static_cast<uint32_t>(key) - static_cast<uint32_t>(a.slot_base));
+    const int64_t pos = a.my_pos[base + i];
+    int32_t src;
+    if (pos >= 0) {
+      src = static_cast<int32_t>(m.word[pos] >> m.cb);
+      const int64_t g = group_of(m, pos);
+      empty_entry(m, pos, g, m.gbase[g]);
+    } else {
+      const int64_t o = -1 - pos;
+      src = m.ovf_src[o];
+      m.ovf_src[o] = -1;
+    }
+    a.dead[slot] = 1;
+    if (a.bm != nullptr) {
+      const int64_t row = a.bm_level ? a.bm_level[src] : 0;
+      atomicOr(a.bm + row * a.bm_words + (slot >> 5), 1u << (slot & 31));
+    }
+    ++mine;
+  }
+  // every rank's selected edges per claim domain, for the Scheme-A counts
+  if (a.level_totals != nullptr) {
+    for (int q = 0; q < a.world; ++q) {
+      const uint64_t *keys = keys_of(a, q) + base;
+      const int32_t *lv = a.world == 1 ? a.my_level : a.peer_level[q];
+      for (int64_t i = t; i < s_n[q]; i += kSelectThreads) {
+        if (keys[i] > kstar) continue;
+        const int l = lv[base + i];
+        if (l >= 0 && l < a.num_levels) atomicAdd(&s_sel[q * kMaxLevels + l], 1);
+      }
+    }
+  }
+  atomicAdd(&s_pruned, mine);
+  __syncthreads();
+  if (a.level_totals != nullptr && t < a.num_levels) {
+    int before = 0, total = 0;
+    for (int q = 0; q < a.world; ++q) {
+      const int v = s_sel[q * kMaxLevels + t];
+      if (q < a.rank) before += v;
+      total += v;
+    }
+    a.level_totals[t] += total;
+    if (a.level_before != nullptr) a.level_before[t] += before;
+  }
+  if (t == 0) a.plan->pruned = static_cast<int64_t>(a.my_count[2 * parity + 1]) + s_pruned;
+}
+
+__global__ void lowk_hist_add_kernel(uint32_t *__restrict__ hist, uint32_t *__restrict__ fine, int64_t k,
+                                     const float *__restrict__ weight, const uint8_t *__restrict__ committed,
+                                     pxb_lowk_plan *plan, const int32_t *claim_counts, long long *totals) {
+  if (totals != nullptr && blockIdx.x == 0 && threadIdx.x == 0) {
+    totals[0] += plan->pruned;
+    if (claim_counts != nullptr) {
+      totals[1] += claim_counts[0];
+      totals[2] += claim_counts[1];
+    }
+    totals[3] += 1;
+  }
+  uint32_t lowest = 0xffffffffu;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < k;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (!committed[i]) continue;
+    const uint32_t b = abs_bits(weight[i]);
+    if (b > kInfBits) continue;
+    atomicAdd(hist + (b >> kLowkShift), 1u);
+    atomicAdd(fine + (b >> kFineShift), 1u);
+    lowest = min(lowest, b >> kFineShift);
+  }
+  lowest = __reduce_min_sync(0xffffffffu, lowest);
+  if ((threadIdx.x & 31) == 0 && lowest != 0xffffffffu) atomicMin(&plan->floor, lowest);
+}
+
+static int check_lowk(const char *fn, const pxb_lowk *lk) {
+  PXB_REQUIRE(lk != nullptr, "%s: lowk is NULL", fn);
+  PXB_REQUIRE(lk->hist && lk->fine && lk->plan && lk->key && lk->level && lk->count && lk->pos,
+              "%s: a lowk array is NULL", fn);
+  PXB_REQUIRE(lk->world >= 1 && lk->world <= kMaxWorld && lk->rank >= 0 && lk->rank < lk->world,
+              "%s: rank %d / world %d out of range (world <= %d)", fn, lk->rank, lk->world, kMaxWorld);
+  PXB_REQUIRE(lk->world == 1 || (lk->peer_key && lk->peer_level && lk->peer_count),
+              "%s: the peer lists are NULL", fn);
+  PXB_REQUIRE(lk->list_cap > 0, "%s: list_cap must be > 0", fn);
+  PXB_REQUIRE(lk->k >= 0, "%s: negative k", fn);
+  return PXB_OK;
+}
+
+}  // namespace pxb
+
+using namespace pxb;
+
+extern "C" int pxb_lowk_hist_build(const pxb_lowk *lowk, int64_t cap, const uint8_t *dead, const float *weight,
+                                   void *stream) {
+  int rc = check_lowk("pxb_lowk_hist_build", lowk);
+  if (rc) return rc;
+  PXB_REQUIRE(cap >= 0, "pxb_lowk_hist_build: negative cap");
+  if (cap == 0) return PXB_OK;
+  PXB_REQUIRE(dead && weight, "pxb_lowk_hist_build: dead/weight is NULL");
+  lowk_hist_build_kernel<<<grid_for(cap, 256, 8), 256, 0, as_stream(stream)>>>(cap, dead, weight, lowk->hist,
+                                                                               lowk->fine, lowk->plan);
+  PXB_LAUNCHED("lowk_hist_build_kernel");
+  return PXB_OK;
+}
+
+extern "C" int pxb_lowk_make_plan(const pxb_lowk *lowk, void *stream) {
+  int rc = check_lowk("pxb_lowk_make_plan", lowk);
+  if (rc) return rc;
+  cudaStream_t st = as_stream(stream);
+  lowk_plan_kernel<<<1, kPlanThreads, 0, st>>>(lowk->hist, lowk->fine, lowk->plan, lowk->k, lowk->count);
+  PXB_LAUNCHED("lowk_plan_kernel");
+  lowk_zero_kernel<<<grid_for(int64_t(1) << 20, 256, 4), 256, 0, st>>>(lowk->fine, lowk->plan);
+  PXB_LAUNCHED("lowk_zero_kernel");
+  return PXB_OK;
+}
+
+extern "C" int pxb_lowk_select(const pxb_lowk *lowk, const pxb_mirror *mirror, uint8_t *dead, uint32_t *free_bitmap,
+                               int64_t bitmap_words, const int32_t *bitmap_level, int32_t num_levels,
+                               int32_t *level_before, int32_t *level_totals, void *stream) {
+  int rc = check_lowk("pxb_lowk_select", lowk);
+  if (rc) return rc;
+  rc = check_mirror("pxb_lowk_select", mirror);
+  if (rc) return rc;
+  PXB_REQUIRE(dead != nullptr, "pxb_lowk_select: dead is NULL");
+  PXB_REQUIRE(level_totals == nullptr || (num_levels >= 1 && num_levels <= kMaxLevels),
+              "pxb_lowk_select: 1..%d claim domains when level_totals is given", kMaxLevels);
+  SelectArgs a;
+  a.plan = lowk->plan;
+  a.rank = lowk->rank;
+  a.world = lowk->world;
+  a.cap = lowk->list_cap;
+  a.slot_base = lowk->slot_base;
+  a.my_key = lowk->key;
+  a.my_level = lowk->level;
+  a.my_pos = lowk->pos;
+  a.my_count = lowk->count;
+  a.peer_key = lowk->peer_key;
+  a.peer_level = lowk->peer_level;
+  a.peer_count = lowk->peer_count;
+  a.dead = dead;
+  a.bm = free_bitmap;
+  a.bm_words = bitmap_words;
+  a.bm_level = bitmap_level;
+  a.num_levels = num_levels;
+  a.level_before = level_before;
+  a.level_totals = level_totals;
+  lowk_select_kernel<<<1, kSelectThreads, 0, as_stream(stream)>>>(a, to_k(mirror));
+  PXB_LAUNCHED("lowk_select_kernel");
+  return PXB_OK;
+}
+
+extern "C" int pxb_lowk_hist_add(const pxb_lowk *lowk, int64_t k, const float *weight, const uint8_t *committed,
+                                 const int32_t *claim_counts, int64_t *totals, void *stream) {
+  int rc = check_lowk("pxb_lowk_hist_add", lowk);
+  if (rc) return rc;
+  PXB_REQUIRE(k >= 0, "pxb_lowk_hist_add: negative k");
+  PXB_REQUIRE(k == 0 || (weight && committed), "pxb_lowk_hist_add: weight/committed is NULL");
+  lowk_hist_add_kernel<<<grid_for(k > 0 ? k : 1, 256, 4), 256, 0, as_stream(stream)>>>(
+      lowk->hist, lowk->fine, k, weight, committed, lowk->plan, claim_counts, reinterpret_cast<long long *>(totals));
+  PXB_LAUNCHED("lowk_hist_add_kernel");
+  return PXB_OK;
+}

@@ -18,85 +18,9 @@
 // - the claim's placed edges are inserted by pxb_mirror_insert: a hole of
 //   the destination's group if one is left, else the group's never-used
 //   slack, else an overflow list that the forward sweeps with atomics.
-#include "pxb_common.cuh"
+#include "mirror.cuh"
 
 namespace pxb {
-
-constexpr uint32_t kEmpty = 0xffffffffu;
-
-struct MirrorK {
-  int64_t entries;
-  int32_t n;
-  int cb;  // chunk bits
-  int64_t groups;
-  const int64_t *gbase;
-  int32_t *gfill;
-  uint32_t *word;
-  float *w;
-  int32_t *slot;
-  int32_t *hstack, *hcount;
-  int64_t items;
-  const int64_t *ib, *ie;
-  const int32_t *ig;
-  int64_t ovf_cap;
-  int32_t *ovf_count, *ovf_src, *ovf_dst, *ovf_slot;
-  float *ovf_w;
-  int32_t *status;
-};
-
-static MirrorK to_k(const pxb_mirror *m) {
-  MirrorK k;
-  k.entries = m->entries;
-  k.n = m->num_units;
-  k.cb = m->chunk_bits;
-  k.groups = m->groups;
-  k.gbase = m->gbase;
-  k.gfill = m->gfill;
-  k.word = m->word;
-  k.w = m->weight;
-  k.slot = m->slot;
-  k.hstack = m->hstack;
-  k.hcount = m->hcount;
-  k.items = m->items;
-  k.ib = m->item_begin;
-  k.ie = m->item_end;
-  k.ig = m->item_group;
-  k.ovf_cap = m->ovf_cap;
-  k.ovf_count = m->ovf_count;
-  k.ovf_src = m->ovf_src;
-  k.ovf_dst = m->ovf_dst;
-  k.ovf_slot = m->ovf_slot;
-  k.ovf_w = m->ovf_weight;
-  k.status = m->status;
-  return k;
-}
-
-struct MPrune {
-  int kind;
-  float thr;
-  const float *unit_thr;
-  uint8_t *dead;
-  uint32_t *bm;
-  int64_t bm_words;
-  const int32_t *bm_level;
-  int32_t *pruned;
-};
-
-__device__ __forceinline__ bool mprune_pred(const MPrune &p, float w, int32_t dst) {
-  if (p.kind == PXB_PRUNE_ABS_BELOW) return fabsf(w) < p.thr;
-  if (p.kind == PXB_PRUNE_ABS_BELOW_DST) return fabsf(w) < __ldg(p.unit_thr + dst);
-  return false;
-}
-
-// The canonical record of a tombstone: dead byte, free bitmap bit, counter.
-__device__ __forceinline__ void tombstone(const MPrune &p, int32_t slot, int32_t src) {
-  p.dead[slot] = 1;
-  if (p.bm != nullptr) {
-    const int64_t row = p.bm_level ? p.bm_level[src] : 0;
-    atomicOr(p.bm + row * p.bm_words + (slot >> 5), 1u << (slot & 31));
-  }
-  if (p.pruned) atomicAdd(p.pruned, 1);
-}
 
 // The sum is accumulated exactly in fixed point, independent of order. A
 // chunk's shared accumulator is two 32-bit words per unit: lo in units of
@@ -271,9 +195,10 @@ __device__ __forceinline__ bool next_tile(const MirrorK &m, int64_t &t, int64_t 
 // by the build and the insert, which keep src < n and dst < n, so the loop
 // carries no range checks (an accumulator past n is dropped at the flush).
 template <int MONOID, int PK>
-__device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, const float *__restrict__ act,
-                                           const uint32_t *word_t, const float *w_t, int used, float *acc_s,
-                                           float *acc_g, int32_t g, int64_t gb, int64_t e0) {
+__device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, const LowkCut &cut,
+                                           const float *__restrict__ act, const uint32_t *word_t, const float *w_t,
+                                           int used, float *acc_s, float *acc_g, int32_t g, int64_t gb, int64_t e0,
+                                           int &pruned_here) {
   const uint32_t mask = (1u << m.cb) - 1u;
   const int chunk = 1 << m.cb;
   const uint32_t last = static_cast<uint32_t>(m.n - 1);
@@ -340,6 +265,13 @@ __device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, co
 #pragma unroll
         for (int j = 1; j < 8; ++j) mn = fminf(mn, fabsf(fs[j]));
         any = mn < p.thr;
+      } else if (PK == PXB_PRUNE_LOWEST_K) {
+        // below the threshold bin's end (an empty entry's zero weight
+        // passes and is skipped below; a NaN never does)
+        uint32_t mn = abs_bits(fs[0]);
+#pragma unroll
+        for (int j = 1; j < 8; ++j) mn = min(mn, abs_bits(fs[j]));
+        any = mn < cut.hi;
       } else {
         any = false;
 #pragma unroll
@@ -349,14 +281,21 @@ __device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, co
       if (any) {
         for (int j = 0; j < 8; ++j) {
           if (ws[j] == kEmpty) continue;
-          const float thr = PK == PXB_PRUNE_ABS_BELOW ? p.thr : __ldg(p.unit_thr + ((g << m.cb) | (ws[j] & mask)));
-          if (!(fabsf(fs[j]) < thr)) continue;
           const int64_t pos = e0 + (j < 4 ? q : q2) * 4 + (j & 3);
-          m.word[pos] = kEmpty;
-          m.w[pos] = 0.0f;
+          if (PK == PXB_PRUNE_LOWEST_K) {
+            const uint32_t b = abs_bits(fs[j]);
+            if (b >= cut.hi) continue;
+            if (b >= cut.lo) {  // the threshold bin: listed, selected after every sweep
+              lowk_list(p, cut.parity, b, m.slot[pos], static_cast<int32_t>(ws[j] >> m.cb), pos);
+              continue;
+            }
+            ++pruned_here;
+          } else {
+            const float thr = PK == PXB_PRUNE_ABS_BELOW ? p.thr : __ldg(p.unit_thr + ((g << m.cb) | (ws[j] & mask)));
+            if (!(fabsf(fs[j]) < thr)) continue;
+          }
           tombstone(p, m.slot[pos], static_cast<int32_t>(ws[j] >> m.cb));
-          const int32_t h = atomicAdd(m.hcount + g, 1);
-          m.hstack[gb + h] = static_cast<int32_t>(pos - gb);
+          empty_entry(m, pos, g, gb);
         }
       }
     }
@@ -472,6 +411,8 @@ __global__ void __launch_bounds__(kSweepThreads, PXB_SWEEP_MIN_CTAS) mirror_swee
   }
 
   // consumers
+  const LowkCut cut = lowk_cut(p);
+  int pruned_here = 0;
   int64_t t = t_lo, cur = -1;
   GroupCursor c{lo, 0, 0, 0};
   cursor_load(m, c);
@@ -489,9 +430,9 @@ __global__ void __launch_bounds__(kSweepThreads, PXB_SWEEP_MIN_CTAS) mirror_swee
     const int s = static_cast<int>(i % kStages);
     if (ok && !mbar_wait(full + s, (i / kStages) & 1)) ok = false;
     if (ok)
-      sweep_tile<MONOID, PK>(m, p, act, word_s + s * kTile, w_s + s * kTile, used, acc_s,
-                                acc + (static_cast<int64_t>(g) << m.cb), static_cast<int32_t>(g), c.base,
-                                t * kTile);
+      sweep_tile<MONOID, PK>(m, p, cut, act, word_s + s * kTile, w_s + s * kTile, used, acc_s,
+                             acc + (static_cast<int64_t>(g) << m.cb), static_cast<int32_t>(g), c.base, t * kTile,
+                             pruned_here);
     __syncwarp();
     if (lane == 0) mbar_arrive(empty + s);
     ++t;
@@ -502,13 +443,19 @@ __global__ void __launch_bounds__(kSweepThreads, PXB_SWEEP_MIN_CTAS) mirror_swee
     flush_reset<MONOID>(m, acc_s, acc, acc_fixed, cur);
   }
   if (!ok && lane == 0) atomicOr(m.status, 2);
+  if (PK == PXB_PRUNE_LOWEST_K) {
+    const int w_pruned = __reduce_add_sync(0xffffffffu, pruned_here);
+    if (lane == 0 && w_pruned) atomicAdd(p.lk.count + 2 * cut.parity + 1, static_cast<unsigned long long>(w_pruned));
+  }
 }
 
 // Edges the mirror had no room for: swept with global atomics.
-template <int MONOID, bool PRUNE>
+template <int MONOID, int PK>
 __global__ void mirror_overflow_kernel(MirrorK m, const float *__restrict__ act, float *__restrict__ acc,
                                        int64_t *__restrict__ acc_fixed, MPrune p) {
   const int64_t cnt = *m.ovf_count < m.ovf_cap ? *m.ovf_count : m.ovf_cap;
+  const LowkCut cut = lowk_cut(p);
+  int pruned_here = 0;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < cnt;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int32_t s = m.ovf_src[i], d = m.ovf_dst[i];
@@ -516,10 +463,25 @@ __global__ void mirror_overflow_kernel(MirrorK m, const float *__restrict__ act,
     const float w = m.ovf_w[i];
     if (MONOID == PXB_MONOID_SUM) fixed_add_global(acc_fixed + d, acc + d, __fmul_rn(w, act[s]));
     else atomic_combine<MONOID>(acc + d, __fmul_rn(w, act[s]));
-    if (PRUNE && mprune_pred(p, w, d)) {
+    if (PK == PXB_PRUNE_LOWEST_K) {
+      const uint32_t b = abs_bits(w);
+      if (b >= cut.hi) continue;
+      if (b >= cut.lo) {
+        lowk_list(p, cut.parity, b, m.ovf_slot[i], s, -1 - i);
+        continue;
+      }
+      ++pruned_here;
+      m.ovf_src[i] = -1;
+      tombstone(p, m.ovf_slot[i], s);
+    } else if (PK != PXB_PRUNE_NONE && mprune_pred(p, w, d)) {
       m.ovf_src[i] = -1;
       tombstone(p, m.ovf_slot[i], s);
     }
+  }
+  if (PK == PXB_PRUNE_LOWEST_K) {
+    const int w_pruned = __reduce_add_sync(0xffffffffu, pruned_here);
+    if ((threadIdx.x & 31) == 0 && w_pruned)
+      atomicAdd(p.lk.count + 2 * cut.parity + 1, static_cast<unsigned long long>(w_pruned));
   }
 }
 
@@ -584,7 +546,7 @@ __global__ void mirror_insert_finish_kernel(MirrorK m, int32_t *__restrict__ ins
   }
 }
 
-static int check_mirror(const char *fn, const pxb_mirror *m) {
+int check_mirror(const char *fn, const pxb_mirror *m) {
   PXB_REQUIRE(m != nullptr, "%s: mirror is NULL", fn);
   PXB_REQUIRE(m->chunk_bits >= 2 && m->chunk_bits <= 13, "%s: chunk_bits %d not in [2, 13]", fn, m->chunk_bits);
   PXB_REQUIRE(m->num_units > 0, "%s: num_units must be > 0", fn);
@@ -608,33 +570,20 @@ static int check_mirror(const char *fn, const pxb_mirror *m) {
 
 using namespace pxb;
 
-extern "C" int pxb_mirror_forward(const pxb_mirror *mirror, const float *act, int32_t monoid, float *acc,
-                                  int64_t *acc_fixed, int32_t prune_kind, float prune_threshold, const float *unit_threshold,
-                                  uint8_t *dead, uint32_t *free_bitmap, int64_t bitmap_words,
-                                  const int32_t *bitmap_level, int32_t *pruned_count, void *stream) {
-  int rc = check_mirror("pxb_mirror_forward", mirror);
-  if (rc) return rc;
-  PXB_REQUIRE(monoid >= 0 && monoid <= 2, "pxb_mirror_forward: unknown monoid %d", monoid);
-  PXB_REQUIRE(prune_kind >= 0 && prune_kind <= 2, "pxb_mirror_forward: unknown prune kind %d", prune_kind);
-  PXB_REQUIRE(act && acc, "pxb_mirror_forward: act/acc is NULL");
-  PXB_REQUIRE(prune_kind == PXB_PRUNE_NONE || dead, "pxb_mirror_forward: pruning needs the canonical dead column");
-  PXB_REQUIRE(prune_kind != PXB_PRUNE_ABS_BELOW_DST || unit_threshold,
-              "pxb_mirror_forward: per-destination threshold column is NULL");
-  PXB_REQUIRE(monoid != PXB_MONOID_SUM || acc_fixed != nullptr,
-              "pxb_mirror_forward: the sum needs its fixed-point accumulator acc_fixed");
-  PXB_REQUIRE((reinterpret_cast<uintptr_t>(acc_fixed) & 7u) == 0, "pxb_mirror_forward: acc_fixed must be 8-byte aligned");
-  MirrorK m = to_k(mirror);
-  MPrune p{prune_kind, prune_threshold, unit_threshold, dead, free_bitmap, bitmap_words, bitmap_level, pruned_count};
-  cudaStream_t st = as_stream(stream);
+namespace pxb {
+
+// The sweep and the overflow pass of one mirror, for any monoid and prune.
+static int mirror_forward_launch(const MirrorK &m, const float *act, int32_t monoid, float *acc, int64_t *acc_fixed,
+                                 const MPrune &p, cudaStream_t st) {
+  const int32_t prune_kind = p.kind;
   if (m.entries > 0) {
     const size_t acc_bytes = (monoid == PXB_MONOID_SUM ? 2 * sizeof(int32_t) : sizeof(float)) << m.cb;
     const size_t smem = 128 + size_t(kStages) * kTile * 8 + acc_bytes;
     const int threads = kSweepThreads;
-#define PXB_SWEEP_FN mirror_sweep_kernel
     const int64_t tiles = m.entries / kTile;
 #define PXB_MS(M, P)                                                                              \
   do {                                                                                            \
-    auto fn = PXB_SWEEP_FN<M, P>;                                                                 \
+    auto fn = mirror_sweep_kernel<M, P>;                                                          \
     PXB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));   \
     int per_sm = 0;                                                                               \
     PXB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem));          \
@@ -646,6 +595,7 @@ extern "C" int pxb_mirror_forward(const pxb_mirror *mirror, const float *act, in
   do {                                                                                            \
     if (prune_kind == PXB_PRUNE_ABS_BELOW) PXB_MS(M, PXB_PRUNE_ABS_BELOW);                        \
     else if (prune_kind == PXB_PRUNE_ABS_BELOW_DST) PXB_MS(M, PXB_PRUNE_ABS_BELOW_DST);           \
+    else if (prune_kind == PXB_PRUNE_LOWEST_K) PXB_MS(M, PXB_PRUNE_LOWEST_K);                     \
     else PXB_MS(M, PXB_PRUNE_NONE);                                                               \
   } while (0)
     if (monoid == PXB_MONOID_SUM) PXB_MS_K(PXB_MONOID_SUM);
@@ -653,19 +603,70 @@ extern "C" int pxb_mirror_forward(const pxb_mirror *mirror, const float *act, in
     else PXB_MS_K(PXB_MONOID_MIN);
 #undef PXB_MS_K
 #undef PXB_MS
-#undef PXB_SWEEP_FN
     PXB_LAUNCHED("mirror_sweep_kernel");
   }
   if (m.ovf_cap > 0) {
-    const bool pr = prune_kind != PXB_PRUNE_NONE;
 #define PXB_MO(M, P) mirror_overflow_kernel<M, P><<<sm_count(), 256, 0, st>>>(m, act, acc, acc_fixed, p)
-    if (monoid == PXB_MONOID_SUM) { if (pr) PXB_MO(PXB_MONOID_SUM, true); else PXB_MO(PXB_MONOID_SUM, false); }
-    else if (monoid == PXB_MONOID_MAX) { if (pr) PXB_MO(PXB_MONOID_MAX, true); else PXB_MO(PXB_MONOID_MAX, false); }
-    else { if (pr) PXB_MO(PXB_MONOID_MIN, true); else PXB_MO(PXB_MONOID_MIN, false); }
+#define PXB_MO_K(M)                                                                               \
+  do {                                                                                            \
+    if (prune_kind == PXB_PRUNE_ABS_BELOW) PXB_MO(M, PXB_PRUNE_ABS_BELOW);                        \
+    else if (prune_kind == PXB_PRUNE_ABS_BELOW_DST) PXB_MO(M, PXB_PRUNE_ABS_BELOW_DST);           \
+    else if (prune_kind == PXB_PRUNE_LOWEST_K) PXB_MO(M, PXB_PRUNE_LOWEST_K);                     \
+    else PXB_MO(M, PXB_PRUNE_NONE);                                                               \
+  } while (0)
+    if (monoid == PXB_MONOID_SUM) PXB_MO_K(PXB_MONOID_SUM);
+    else if (monoid == PXB_MONOID_MAX) PXB_MO_K(PXB_MONOID_MAX);
+    else PXB_MO_K(PXB_MONOID_MIN);
+#undef PXB_MO_K
 #undef PXB_MO
     PXB_LAUNCHED("mirror_overflow_kernel");
   }
   return PXB_OK;
+}
+
+static int mirror_forward_checks(const char *fn, const pxb_mirror *mirror, const float *act, int32_t monoid,
+                                 float *acc, int64_t *acc_fixed) {
+  int rc = check_mirror(fn, mirror);
+  if (rc) return rc;
+  PXB_REQUIRE(monoid >= 0 && monoid <= 2, "%s: unknown monoid %d", fn, monoid);
+  PXB_REQUIRE(act && acc, "%s: act/acc is NULL", fn);
+  PXB_REQUIRE(monoid != PXB_MONOID_SUM || acc_fixed != nullptr,
+              "%s: the sum needs its fixed-point accumulator acc_fixed", fn);
+  PXB_REQUIRE((reinterpret_cast<uintptr_t>(acc_fixed) & 7u) == 0, "%s: acc_fixed must be 8-byte aligned", fn);
+  return PXB_OK;
+}
+
+}  // namespace pxb
+
+extern "C" int pxb_mirror_forward(const pxb_mirror *mirror, const float *act, int32_t monoid, float *acc,
+                                  int64_t *acc_fixed, int32_t prune_kind, float prune_threshold, const float *unit_threshold,
+                                  uint8_t *dead, uint32_t *free_bitmap, int64_t bitmap_words,
+                                  const int32_t *bitmap_level, int32_t *pruned_count, void *stream) {
+  int rc = mirror_forward_checks("pxb_mirror_forward", mirror, act, monoid, acc, acc_fixed);
+  if (rc) return rc;
+  PXB_REQUIRE(prune_kind >= 0 && prune_kind <= 2, "pxb_mirror_forward: unknown prune kind %d", prune_kind);
+  PXB_REQUIRE(prune_kind == PXB_PRUNE_NONE || dead, "pxb_mirror_forward: pruning needs the canonical dead column");
+  PXB_REQUIRE(prune_kind != PXB_PRUNE_ABS_BELOW_DST || unit_threshold,
+              "pxb_mirror_forward: per-destination threshold column is NULL");
+  MPrune p{prune_kind, prune_threshold, unit_threshold, dead, free_bitmap, bitmap_words, bitmap_level, pruned_count,
+           LowkSweep{}};
+  return mirror_forward_launch(to_k(mirror), act, monoid, acc, acc_fixed, p, as_stream(stream));
+}
+
+extern "C" int pxb_mirror_forward_lowk(const pxb_mirror *mirror, const float *act, int32_t monoid, float *acc,
+                                       int64_t *acc_fixed, const pxb_lowk *lowk, uint8_t *dead, uint32_t *free_bitmap,
+                                       int64_t bitmap_words, const int32_t *bitmap_level, void *stream) {
+  int rc = mirror_forward_checks("pxb_mirror_forward_lowk", mirror, act, monoid, acc, acc_fixed);
+  if (rc) return rc;
+  PXB_REQUIRE(lowk != nullptr && lowk->plan && lowk->key && lowk->level && lowk->count && lowk->pos,
+              "pxb_mirror_forward_lowk: a lowk array is NULL");
+  PXB_REQUIRE(lowk->list_cap > 0, "pxb_mirror_forward_lowk: list_cap must be > 0");
+  PXB_REQUIRE(dead != nullptr, "pxb_mirror_forward_lowk: pruning needs the canonical dead column");
+  PXB_REQUIRE(lowk->slot_base >= 0 && lowk->slot_base < (int64_t(1) << 31),
+              "pxb_mirror_forward_lowk: slot_base out of range (global slots are keyed in 32 bits)");
+  MPrune p{PXB_PRUNE_LOWEST_K, 0.0f, nullptr, dead, free_bitmap, bitmap_words, bitmap_level, nullptr,
+           LowkSweep{lowk->plan, lowk->key, lowk->level, lowk->count, lowk->pos, lowk->list_cap, lowk->slot_base}};
+  return mirror_forward_launch(to_k(mirror), act, monoid, acc, acc_fixed, p, as_stream(stream));
 }
 
 extern "C" int pxb_mirror_insert(const pxb_mirror *mirror, int64_t k, const int32_t *src, const int32_t *dst,

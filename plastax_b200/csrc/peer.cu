@@ -87,7 +87,12 @@ __global__ void __launch_bounds__(256) scheme_a_apply_kernel(PeerK g, int32_t n,
       st_release_sys(g.flags[threadIdx.x] + g.rank, epoch);  // row A of peer threadIdx.x
     }
   }
-  if (threadIdx.x == 0) s_ok = wait_row(g.flags[g.rank], g.world, epoch, polls) ? 1 : 0;
+  if (threadIdx.x == 0) {
+    s_ok = wait_row(g.flags[g.rank], g.world, epoch, polls) ? 1 : 0;
+    // a block that gave up skips its share of the units: the step is
+    // incomplete whichever block finishes last
+    if (!s_ok) atomicOr(g.status, 1);
+  }
   __syncthreads();
   if (blockIdx.x == 0 && c.local != nullptr && threadIdx.x < static_cast<unsigned>(c.num_levels)) {
     // every rank's counts are here now: the ranks before this one and the total

@@ -578,7 +578,7 @@ def claim_commit(mode: int, b: Bucket, unit_level: torch.Tensor, tail_start: tor
                  growable: torch.Tensor, *, max_new: int = -1, shard_base: int = 0, global_cap: int | None = None,
                  level_before: torch.Tensor | None = None, level_totals: torch.Tensor | None = None,
                  extra: Mapping[str, torch.Tensor] | None = None, free_bitmap: torch.Tensor | None = None,
-                 placed: torch.Tensor | None = None) -> None:
+                 placed: torch.Tensor | None = None, committed: torch.Tensor | None = None) -> None:
     cap = _bucket(b)
     k = src.numel()
     if k != ws.k:
@@ -597,7 +597,7 @@ def claim_commit(mode: int, b: Bucket, unit_level: torch.Tensor, tail_start: tor
          ctypes.cast(cols, ctypes.c_void_p) if n_extra else None,
          ctypes.cast(nbytes, ctypes.c_void_p) if n_extra else None,
          ctypes.cast(vals, ctypes.c_void_p) if n_extra else None, ptr(ws.counts), ptr(ws.overflowed), ptr(placed),
-         ptr(ws.scratch), ctypes.c_size_t(ws.scratch.numel()), _stream())
+         ptr(committed), ptr(ws.scratch), ctypes.c_size_t(ws.scratch.numel()), _stream())
 
 
 def growth_flags(counts: torch.Tensor, *, reset: bool, grown: torch.Tensor | None,

@@ -43,7 +43,7 @@ class PeerGroup:
     """One rank's symmetric region and its peers' mappings (collective: every
     rank of `group` constructs it at the same point)."""
 
-    def __init__(self, num_units: int, device: torch.device, group=None) -> None:
+    def __init__(self, num_units: int, device: torch.device, group=None, lowk_cap: int = 0) -> None:
         import torch.distributed as dist
 
         self.dist = dist
@@ -58,7 +58,13 @@ class PeerGroup:
         self.off_act = _align(self.off_side + 4 * n)
         self.off_flags = _align(self.off_act + 4 * n)
         self.off_counts = _align(self.off_flags + 4 * 2 * self.world)
-        self.bytes = _align(self.off_counts + 4 * self.world * _lib.PEER_MAX_LEVELS)
+        # the exact lowest-|w| prune's lists (keys, claim domains, counters),
+        # double-buffered, read by every peer's selection
+        self.lowk_cap = int(lowk_cap)
+        self.off_lkey = _align(self.off_counts + 4 * self.world * _lib.PEER_MAX_LEVELS)
+        self.off_llevel = _align(self.off_lkey + 8 * 2 * self.lowk_cap)
+        self.off_lcount = _align(self.off_llevel + 4 * 2 * self.lowk_cap)
+        self.bytes = _align(self.off_lcount + 8 * 4)
         lib = _lib.lib()
         lib.pxb_set_device(self.dev.index)
         base = ctypes.c_void_p()
@@ -82,6 +88,7 @@ class PeerGroup:
         mk = lambda off: torch.tensor([b + off for b in self.bases], dtype=torch.int64, device=self.dev)  # noqa: E731
         self.p_fixed, self.p_side, self.p_act, self.p_flags, self.p_counts = (
             mk(self.off_fixed), mk(self.off_side), mk(self.off_act), mk(self.off_flags), mk(self.off_counts))
+        self.p_lkey, self.p_llevel, self.p_lcount = mk(self.off_lkey), mk(self.off_llevel), mk(self.off_lcount)
         self.words = torch.zeros(4, dtype=torch.int32, device=self.dev)  # epoch, done, status, pad
         w = self.words.data_ptr()
         self.struct = _lib.PeerGroup(self.rank, self.world, self.p_fixed.data_ptr(), self.p_side.data_ptr(),
@@ -91,6 +98,10 @@ class PeerGroup:
         self.acc_fixed = _view(self.base + self.off_fixed, n, torch.int64, self.dev)
         self.acc_side = _view(self.base + self.off_side, n, torch.float32, self.dev)
         self.act = _view(self.base + self.off_act, n, torch.float32, self.dev)
+        if self.lowk_cap > 0:
+            self.lowk_key = _view(self.base + self.off_lkey, 2 * self.lowk_cap, torch.int64, self.dev)
+            self.lowk_level = _view(self.base + self.off_llevel, 2 * self.lowk_cap, torch.int32, self.dev)
+            self.lowk_count = _view(self.base + self.off_lcount, 4, torch.int64, self.dev)
         self.closed = False
 
     @property
@@ -108,6 +119,7 @@ class PeerGroup:
             _lib.call("pxb_peer_close", ctypes.c_void_p(p))
         self.dist.barrier(group=self.group)
         self.acc_fixed = self.acc_side = self.act = None
+        self.lowk_key = self.lowk_level = self.lowk_count = None
         _lib.call("pxb_peer_free", ctypes.c_void_p(self.base))
         self.closed = True
 

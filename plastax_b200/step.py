@@ -91,7 +91,8 @@ def _dist():
 class StepFn:
     """A built step: preallocated buffers plus the phase sequence."""
 
-    def __init__(self, net: type[Network], static: NetworkStatic, device: torch.device) -> None:
+    def __init__(self, net: type[Network], static: NetworkStatic, device: torch.device,
+                 fuse_prune: bool = True) -> None:
         self.net, self.static, self.dev = net, static, device
         n = static.num_units
         fp = net.forward_pass
@@ -118,8 +119,16 @@ class StepFn:
         self.loss_b1 = torch.zeros(1, dtype=torch.float32, device=device)
         self.sharded = static.sharding is not None and static.num_shards > 1
         self.reduce_op = fp.combine.torch_reduce_op() if self.sharded else None
-        # fusion legality
-        self.fuse_prune = (isinstance(net.prune_conn, MagnitudePrune) and net.update_conn is None)
+        # fusion legality: a prune that reads only weights rides on the
+        # forward's read of every edge when no update_conn rewrites them; the
+        # exact lowest-|w| prune does so on a one-bucket mirror
+        pc = net.prune_conn
+        self.lowk_prune = (fuse_prune and isinstance(pc, LowestMagnitudePrune) and net.update_conn is None
+                           and net.prune_unit is None and self.num_buckets == 1)
+        self.fuse_prune = fuse_prune and (isinstance(pc, MagnitudePrune) or self.lowk_prune) \
+            and net.update_conn is None
+        self.lowk = None
+        self._lowk_fired = False
         self.fuse_update = (not self.pipeline and net.update_conn is not None and net.backward_pass is not None
                             and net.update_unit is None)
         self.opt = net.update_conn.struct() if net.update_conn is not None else None
@@ -136,6 +145,8 @@ class StepFn:
                            and net.prune_unit is None)  # unit pruning tombstones edges outside the sweep
         self.mirrors: list | None = None
         self.mirror_chunk_bits: int | None = None  # destination chunk of the mirror (None: the largest allowed)
+        # spare entries per mirror group for growth inserts (fraction, minimum)
+        self.mirror_slack, self.mirror_min_slack = 0.05, 64
         self.bitmaps: list[torch.Tensor] | None = None
         # the mirror's sum is exact fixed point (int64 accumulators beside
         # the float side for non-finite or huge products)
@@ -161,9 +172,10 @@ class StepFn:
         self.graph = None  # a captured CUDA graph of the step body (see capture)
         self.side = None
         self.unit_lifecycle = net.prune_unit is not None or net.add_unit is not None
-        if isinstance(net.prune_conn, LowestMagnitudePrune) and self.sharded:
-            raise NotImplementedError("the lowest-|w| prune under Scheme-A has no lowering (its selection spans "
-                                      "every rank's band)")
+        if isinstance(net.prune_conn, LowestMagnitudePrune) and self.sharded and not (
+                self.lowk_prune and self.peer_reduce):
+            raise NotImplementedError("the lowest-|w| prune under Scheme-A is lowered for a one-bucket PIPELINE "
+                                      "arena swept through its mirror (sum combine over peer memory) only")
         if self.unit_lifecycle and self.sharded:
             raise NotImplementedError("the unit lifecycle under Scheme-A has no lowering (single device only, as in "
                                       "the reference)")
@@ -201,12 +213,13 @@ class StepFn:
         level = state.units[LEVEL.name]
         self._level = level
         if self.use_mirror:
-            self.mirrors = [Mirror(b, st.num_units, chunk_bits=self.mirror_chunk_bits) for b in state.conns]
+            self.mirrors = [Mirror(b, st.num_units, chunk_bits=self.mirror_chunk_bits, slack=self.mirror_slack,
+                                   min_slack=self.mirror_min_slack) for b in state.conns]
         if self.peer_reduce:
             from plastax_b200.peers import PeerGroup
 
             if self.peers is None:
-                self.peers = PeerGroup(st.num_units, self.dev)
+                self.peers = PeerGroup(st.num_units, self.dev, lowk_cap=self._lowk_list_cap())
                 self.acc_fixed = self.peers.acc_fixed
                 self.acc = self.peers.acc_side
             # the activation column lives in the group's region: peers write it
@@ -216,6 +229,17 @@ class StepFn:
             mode = _lib.CLAIM_PIPELINE if self.pipeline else _lib.CLAIM_TOPOLOGICAL
             self.bitmaps = [K.free_bitmap_build(mode, b, level, state.tail_start, self.num_levels,
                                                 shard_base=st.shard_base(i)) for i, b in enumerate(state.conns)]
+        if self.lowk_prune:
+            from plastax_b200.lowk import LowestK
+
+            if self.lowk is None:
+                self.lowk = LowestK(self.net.prune_conn.k, self.dev, list_cap=self._lowk_list_cap(),
+                                    slot_base=st.shard_base(0), peers=self.peers)
+            combine = combine_min = None
+            if self.sharded:
+                combine = lambda h: _dist().all_reduce(h, op=_dist().ReduceOp.SUM)  # noqa: E731
+                combine_min = lambda h: _dist().all_reduce(h, op=_dist().ReduceOp.MIN)  # noqa: E731
+            self.lowk.build_hist(state.conns, combine=combine, combine_min=combine_min)
         uc = self.net.update_conn
         if uc is not None and uc.scale_field is not None:
             self.opt = uc.struct(state.units[uc.scale_field.name])
@@ -225,18 +249,66 @@ class StepFn:
         self._ahead_ready = False
         self._bound = id(state)
 
+    def _lowk_list_cap(self) -> int:
+        pc = self.net.prune_conn
+        if pc.list_capacity is not None:
+            return int(pc.list_capacity)
+        return max(1 << 16, int(pc.k))
+
+    def status_words(self) -> dict[str, int]:
+        """Every device status word of the step, read in one host sync
+        (only the words this step keeps): `mirror` (bit 0 an insert found no
+        room, bit 1 a sweep's bulk copy never completed), `peers` (bit 0 a
+        wait for a peer gave up), `select` (bit 0 a selection bin held more
+        keys than it ranks), `lowk` (bit 0 a prune list overflowed, bit 1
+        the prune's counts disagreed with its histogram)."""
+        words, names = [], []
+        if self.mirrors:
+            words.append(torch.stack([m.status[0] for m in self.mirrors]).amax().reshape(1))
+            names.append("mirror")
+        if self.peers is not None:
+            words.append(self.peers.status.reshape(1))
+            names.append("peers")
+        if getattr(self, "fs_status", None) is not None:
+            words.append(self.fs_status.reshape(1))
+            names.append("select")
+        if self.lowk is not None:
+            words.append(self.lowk.status.reshape(1))
+            names.append("lowk")
+        if not words:
+            return {}
+        vals = torch.cat([w.to(torch.int32) for w in words]).cpu().tolist()
+        return dict(zip(names, vals, strict=True))
+
+    def check_status(self) -> bool:
+        """Read every status word (one host sync) and raise PxbError for a
+        fault: a sweep whose bulk copy never completed, a peer wait that gave
+        up (the step is incomplete), a selection bin that overflowed (fewer
+        winners than k were listed), a lowest-|w| prune that overflowed its
+        list or disagreed with its histogram. Returns whether every mirror
+        still holds every live edge (False: `invalidate()` rebuilds them)."""
+        w = self.status_words()
+        faults = []
+        if w.get("mirror", 0) & 2:
+            faults.append("mirror sweep: a bulk copy never completed (status bit 1)")
+        if w.get("peers", 0) & 1:
+            faults.append("Scheme-A combine: a wait for a peer gave up; the step's activations are incomplete")
+        if w.get("select", 0) & 1:
+            faults.append("growth selection: a bin held more keys than it ranks; the winner list is incomplete")
+        if w.get("lowk", 0) & 1:
+            faults.append("lowest-|w| prune: the threshold bin held more edges than the list capacity "
+                          f"({self._lowk_list_cap()}); raise LowestMagnitudePrune(list_capacity=...)")
+        if w.get("lowk", 0) & 2:
+            faults.append("lowest-|w| prune: the swept counts disagree with the histogram (the arena changed "
+                          "outside the step without invalidate())")
+        if faults:
+            raise _lib.PxbError("; ".join(faults))
+        return not (w.get("mirror", 0) & 1)
+
     def mirrors_healthy(self) -> bool:
-        """Whether every mirror still holds every live edge (one host read).
-        An insert that found neither a hole, nor slack, nor room in the
-        overflow list sets bit 0 of the mirror's status: `invalidate()` then
-        rebuilds the mirror from the canonical arena. Bit 1 (a sweep gave up
-        waiting on its copies) is a device fault and raises."""
-        if not self.mirrors:
-            return True
-        codes = torch.cat([m.status for m in self.mirrors]).cpu()
-        if bool((codes & 2).any()):
-            raise RuntimeError("mirror sweep: a bulk copy never completed (status bit 1)")
-        return not bool((codes != 0).any())
+        """Whether every mirror still holds every live edge, after checking
+        every status word (`check_status`; one host read)."""
+        return self.check_status()
 
     def invalidate(self) -> None:
         """Drop the per-state indices (call after editing a state's columns
@@ -436,6 +508,7 @@ class StepFn:
         self.grown = torch.zeros((), dtype=torch.int32, device=dev)
         self.overflow = torch.zeros((), dtype=torch.bool, device=dev)
         self.placed = torch.empty(kk, dtype=torch.int32, device=dev)
+        self.committed = torch.zeros(kk, dtype=torch.uint8, device=dev)
         if self.sharded:
             G = st.num_shards
             self.gather_buf = torch.zeros((G, self.num_levels), dtype=torch.int32, device=dev)
@@ -464,7 +537,15 @@ class StepFn:
         bm, bm_level = self._bm(i)
         if self.use_mirror:
             m = self.mirrors[i]
-            if self.fuse_prune:
+            if self.lowk_prune:
+                if self._lowk_fires(state):
+                    self.lowk.make_plan()
+                    self.lowk.sweep(m, act, acc, acc_fixed, self.fwd_monoid, b["dead"], bm, bm_level)
+                    self._lowk_fired = True
+                    self.launches += 1
+                else:
+                    K.mirror_forward(m, act, acc, acc_fixed=acc_fixed, monoid=self.fwd_monoid)
+            elif self.fuse_prune:
                 K.mirror_forward(m, act, acc, acc_fixed=acc_fixed, monoid=self.fwd_monoid,
                                  prune_kind=_lib.PRUNE_ABS_BELOW, threshold=net.prune_conn.threshold,
                                  dead=b["dead"], free_bitmap=bm, bitmap_words=(b["dead"].numel() + 31) // 32,
@@ -551,6 +632,10 @@ class StepFn:
                 scheme_a_apply(self.peers, self.fwd_act, is_input=self.is_input, pruned=pruned,
                                level_counts=counts, level_before=self.level_before, level_totals=self.level_totals)
                 self.launches += 3
+                if self._lowk_fired:
+                    # every rank's sweep is complete: select the threshold
+                    # bin's edges, adding every rank's to the barrier's counts
+                    self._lowk_select(state, adjust=self._counts_on_barrier)
                 return
             self._forward_bucket(state, 0, act)
             K.unit_apply(self.acc, act, mode=0, act_kind=self.fwd_act, monoid=self.fwd_monoid,
@@ -719,8 +804,25 @@ class StepFn:
             self.launches += 1
         state.units_added, state.unit_overflow = self.units_added, self.unit_overflow
 
+    def _lowk_fires(self, state: NetworkState) -> bool:
+        every = self.net.prune_conn.every
+        return every <= 1 or state.step % every == 0
+
+    def _lowk_select(self, state: NetworkState, adjust: bool = False) -> None:
+        """The threshold bin's selection of the exact lowest-|w| prune (after
+        every rank's sweep); with `adjust` every rank's selected edges are
+        added to the per-domain counts that rode on the peer barrier."""
+        bm, bm_level = self._bm(0)
+        self.lowk.select(self.mirrors[0], state.conns[0]["dead"], bm, bm_level,
+                         num_levels=self.num_levels if adjust else 0,
+                         level_before=self.level_before if adjust else None,
+                         level_totals=self.level_totals if adjust else None)
+        self.launches += 1
+
     def _prune(self, state: NetworkState) -> None:
         pc = self.net.prune_conn
+        if self._lowk_fired and self.peers is None:
+            self._lowk_select(state)
         if pc is None or self.fuse_prune:
             return
         n = self.static.num_units
@@ -926,6 +1028,10 @@ class StepFn:
             if counts_ready:
                 # the counts pass ran after the sweep and rode on the peer barrier
                 before, totals = self.level_before, self.level_totals
+                if self._lowk_fired:
+                    # the lowest-|w| selection freed more slots since (its
+                    # edges are in before/totals): refresh this rank's tiles
+                    K.claim_prepare(mode, b, level, state.tail_start, ws, shard_base=base, free_bitmap=bm)
             else:
                 K.claim_prepare(mode, b, level, state.tail_start, ws, shard_base=base, free_bitmap=bm)
             if self.sharded and not counts_ready:
@@ -937,7 +1043,13 @@ class StepFn:
                 totals = self.gather_buf.sum(0, dtype=torch.int32)
             K.claim_commit(mode, b, level, state.tail_start, ws, cs, cd, cw, gb, max_new=max_new, shard_base=base,
                            global_cap=st.level_capacities[bk], level_before=before, level_totals=totals,
-                           extra=self.extra_defaults, free_bitmap=bm, placed=self.placed)
+                           extra=self.extra_defaults, free_bitmap=bm, placed=self.placed,
+                           committed=self.committed if self.lowk is not None else None)
+            if self.lowk is not None:
+                # the committed edges enter the prune's histogram (every rank
+                # adds every rank's: the histogram is the whole arena's)
+                self.lowk.hist_add(cw, self.committed, ws.counts, tally=fresh)
+                self.launches += 1
             if self.use_mirror:
                 K.mirror_insert(self.mirrors[bk], cs, cd, cw, self.placed)
             K.growth_flags(ws.counts, reset=fresh and bi == 0, grown=self.grown, overflow=self.overflow,
@@ -976,6 +1088,7 @@ class StepFn:
     def _body(self, state: NetworkState, inputs: StepInputs) -> GrowthRemainder | None:
         """The device work of one step (no host synchronisation)."""
         self._level = state.units[LEVEL.name]
+        self._lowk_fired = False
         if self.ahead:
             return self._body_ahead(state, inputs)
         # selection that reads nothing the step writes runs on the side
@@ -1146,10 +1259,7 @@ def make_step(net: type[Network], static: NetworkStatic, *, batch_size: int | No
         from plastax_b200.batched import BatchedStepFn
 
         return BatchedStepFn(net, static, batch_size, torch.device(device))
-    fn = StepFn(net, static, torch.device(device))
-    if fuse_prune is False:
-        fn.fuse_prune = False
-    return fn
+    return StepFn(net, static, torch.device(device), fuse_prune=fuse_prune is not False)
 
 
 def make_growth_retry(net: type[Network], static: NetworkStatic, *, device: torch.device | str = "cuda"):

@@ -145,13 +145,24 @@ class LowestMagnitudePrune(PruneConn):
     lowest-magnitude churn of the dynamic-sparse-training configurations
     (the reference states it as a predicate against a threshold the host
     computes into the globals; here the selection runs on the device and
-    prunes exactly min(k, live) edges). A NaN weight is never selected."""
+    prunes exactly min(k, live) edges). A NaN weight is never selected.
 
-    def __init__(self, k: int, every: int = 1) -> None:
+    On an arena with a destination-grouped mirror (no weight-rewriting
+    phase, one bucket) the prune rides on the forward sweep: only the edges
+    whose |w| shares the k-th smallest's histogram bin (the top 16 bits of
+    |w|) are listed and selected apart; `list_capacity` bounds that list
+    per rank (default max(65536, k)), and a firing whose threshold bin
+    holds more live edges than that raises an error instead of pruning
+    fewer than k."""
+
+    def __init__(self, k: int, every: int = 1, list_capacity: int | None = None) -> None:
         if int(k) < 0 or int(every) < 1:
             raise ValueError("LowestMagnitudePrune: k must be >= 0 and every >= 1")
+        if list_capacity is not None and int(list_capacity) < 1:
+            raise ValueError("LowestMagnitudePrune: list_capacity must be >= 1")
         self.k = int(k)
         self.every = int(every)
+        self.list_capacity = None if list_capacity is None else int(list_capacity)
 
 
 class ResetGlobal:

@@ -29,7 +29,7 @@ def _run(cuda, cfg, steps, sharded_bands=1, graph=False, ahead=True):
     b = {k: v.cpu().numpy().copy() for k, v in state.conns[0].items()}
     ref = ReservoirOracle(b, state.units["activation"].cpu().numpy().copy(), state.units["level"].cpu().numpy().copy(),
                           int(state.tail_start.item()), num_inputs=cfg.num_inputs, num_res=cfg.num_units,
-                          tau=cfg.tau, k=cfg.k, init_a=cfg.sigma * math.sqrt(3.0), seed=cfg.seed)
+                          tau=cfg.tau, k=cfg.k, init_a=cfg.sigma * math.sqrt(3.0), seed=cfg.seed, prune=cfg.prune)
     step = make_step(net, static, device=cuda)
     # the site-RNG selection runs one step ahead on the side stream by default
     assert step.ahead
@@ -51,11 +51,14 @@ def _run(cuda, cfg, steps, sharded_bands=1, graph=False, ahead=True):
     torch.cuda.synchronize()
 
 
-@pytest.mark.parametrize("log2,fan_in,churn", [(12, 16, 0.01), (14, 32, 0.001), (10, 8, 0.2)])
-def test_reservoir_churn_matches_oracle(cuda, log2, fan_in, churn):
+@pytest.mark.parametrize("log2,fan_in,churn,prune", [(12, 16, 0.01, "lowest_k"), (14, 32, 0.001, "lowest_k"),
+                                                     (10, 8, 0.2, "lowest_k"), (12, 16, 0.01, "threshold"),
+                                                     (10, 8, 0.2, "threshold")])
+def test_reservoir_churn_matches_oracle(cuda, log2, fan_in, churn, prune):
     from plastax_b200.configs import ReservoirConfig
 
-    _run(cuda, ReservoirConfig(num_units=1 << log2, fan_in=fan_in, churn=churn, capacity_align=256), steps=6)
+    _run(cuda, ReservoirConfig(num_units=1 << log2, fan_in=fan_in, churn=churn, capacity_align=256, prune=prune),
+         steps=6)
 
 
 def test_reservoir_churn_replayed_from_a_cuda_graph_matches_oracle(cuda):
@@ -85,10 +88,22 @@ def test_reservoir_overflow_into_tail_exhaustion(cuda):
     _run(cuda, cfg, steps=4)
 
 
+def _order_keys(w, slots):
+    """The prune's total order as int64 keys: bits(|w|) << 32 | slot."""
+    import torch
+
+    bits = (w.view(torch.int32) & 0x7FFFFFFF).to(torch.int64)
+    return (bits << 32) | slots.to(torch.int64)
+
+
 @pytest.mark.slow
-def test_full_size_step_properties(cuda):
-    """The benchmark's full-size step: live edges change by exactly
-    grown - pruned; every live id is in range; tail_start only grows."""
+def test_full_size_churn_properties(cuda):
+    """The benchmark's full-size churn step, 30 steps in a row (the first
+    eager, the rest replayed from the step's CUDA graph, as the benchmark
+    runs it): each prunes exactly k edges and grows exactly k (no overflow),
+    so the live-edge count stays constant; the pruned edges are the k
+    lowest of the (|w|, slot) order (checked on three steps: every survivor
+    orders after every pruned edge); every live id stays in range."""
     import torch
 
     from plastax_b200 import StepInputs, make_step
@@ -100,17 +115,33 @@ def test_full_size_step_properties(cuda):
     b = state.conns[0]
     live0 = int((b["dead"] == 0).sum())
     tail0 = int(state.tail_start.item())
-    for i in range(2):
-        dead_before = b["dead"].clone()
-        w = b["weight"]
-        pruned = int(((dead_before == 0) & (w.abs() < C5.tau)).sum())
+    slots = torch.arange(b["dead"].numel(), dtype=torch.int32, device=cuda)
+    x0 = torch.randn(C5.num_inputs, device=cuda)
+    for i in range(30):
+        check = i in (0, 11, 29)
+        if check:
+            live_b = b["dead"] == 0
+            before = {c: b[c].clone() for c in ("from_id", "to_id", "weight")}
+        if i == 1:
+            step.capture(state, StepInputs(x0))
         res = step(state, StepInputs(torch.randn(C5.num_inputs, device=cuda)))
-        live1 = int((b["dead"] == 0).sum())
-        grown = int(res.grown.item())
-        assert live1 == live0 - pruned + grown, (i, live0, pruned, grown, live1)
+        assert int(res.grown.item()) == C5.k and not bool(res.overflow.item()), i
+        assert int((b["dead"] == 0).sum()) == live0, i
+        if check:
+            # a live-before slot that is dead now, or holds another edge, was pruned
+            same = (b["from_id"] == before["from_id"]) & (b["to_id"] == before["to_id"]) & (
+                b["weight"].view(torch.int32) == before["weight"].view(torch.int32)) & (b["dead"] == 0)
+            gone = live_b & ~same
+            assert int(gone.sum()) == C5.k, i
+            keep = live_b & same & ~torch.isnan(before["weight"])
+            kg = _order_keys(before["weight"][gone], slots[gone])
+            kk = _order_keys(before["weight"][keep], slots[keep])
+            assert int(kg.max()) < int(kk.min()), i
+            del live_b, before, same, gone, keep, kg, kk
         liv = b["dead"] == 0
         assert int(b["from_id"][liv].min()) >= 0 and int(b["from_id"][liv].max()) < n
         assert int(b["to_id"][liv].min()) >= C5.num_inputs and int(b["to_id"][liv].max()) < n
         assert int(state.tail_start.item()) >= tail0
-        live0 = live1
-        del dead_before
+    assert step.check_status()
+    tot = step.lowk.totals.cpu().tolist()
+    assert tot == [30 * C5.k, 30 * C5.k, 0, 30]
