@@ -760,7 +760,12 @@ PXB_API int pxb_count_dead(int64_t cap, const uint8_t *dead, int32_t *out,
  * bit 0 is set when that list is full too (the mirror must be rebuilt), bit
  * 1 when a sweep's pipeline wait timed out (its result is incomplete). All
  * arrays are device memory owned by the caller; word and weight 16-byte
- * aligned. */
+ * aligned. defer_pos / defer_count (may be NULL): the sweep's deferred
+ * prunes -- sweep CTA c lists up to defer_seg entry positions it pruned at
+ * defer_pos[c * defer_seg ...] and their count at defer_count[c] (for c <
+ * defer_ctas), and a second pass writes their tombstones, so the sweep's
+ * pipeline never waits on the scattered writes of a tombstone; a CTA past
+ * defer_ctas, or past its segment, writes them in place. */
 typedef struct pxb_mirror {
   int32_t num_units;
   int32_t chunk_bits;
@@ -785,6 +790,10 @@ typedef struct pxb_mirror {
   float *ovf_weight;
   int32_t *status;
   int32_t *ins_count; /* [groups] zeroed scratch of pxb_mirror_insert */
+  int64_t *defer_pos;
+  int32_t *defer_count;
+  int64_t defer_seg;
+  int32_t defer_ctas;
 } pxb_mirror;
 
 /* Forward accumulate of the mirrored bucket (w * act[src] combined per

@@ -66,6 +66,7 @@ class Mirror(ctypes.Structure):
         ("hstack", c_ptr), ("hcount", c_ptr), ("items", c_i64), ("item_begin", c_ptr), ("item_end", c_ptr),
         ("item_group", c_ptr), ("ovf_cap", c_i64), ("ovf_count", c_ptr), ("ovf_src", c_ptr), ("ovf_dst", c_ptr),
         ("ovf_slot", c_ptr), ("ovf_weight", c_ptr), ("status", c_ptr), ("ins_count", c_ptr),
+        ("defer_pos", c_ptr), ("defer_count", c_ptr), ("defer_seg", c_i64), ("defer_ctas", c_i32),
     ]
 
 

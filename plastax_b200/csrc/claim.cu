@@ -354,11 +354,14 @@ __global__ void __launch_bounds__(kClaimWarps * 32) list_fill_kernel(
 }
 
 // list fill from the bitmaps: one warp per (tile, domain) that still owes
-// needed ranks; each lane owns consecutive words, a warp scan of their
-// popcounts gives each set bit its rank in slot order.
+// needed ranks. A tile is read 256 words at a time, eight consecutive words
+// per lane issued together (one memory round trip per 256 words, not one
+// per 32); a warp scan of the lanes' popcounts gives each set bit its rank
+// in slot order.
 __global__ void __launch_bounds__(kClaimWarps * 32) list_fill_bm_kernel(
     DomainArgs a, ClaimGeom g, const int32_t *__restrict__ tile_offsets, const int32_t *__restrict__ level_base,
     const int32_t *__restrict__ need, const int32_t *__restrict__ need_off, int32_t *__restrict__ list) {
+  constexpr int kWordsPerLane = 8;
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * kClaimWarps;
   const int64_t words_per_tile = int64_t(1) << (g.tile_shift - 5);
@@ -369,23 +372,32 @@ __global__ void __launch_bounds__(kClaimWarps * 32) list_fill_bm_kernel(
     const int32_t nl = need[l];
     if (run >= nl) continue;
     const uint32_t *row = a.bm + l * a.bm_words;
-    for (int64_t w0 = t * words_per_tile; w0 < (t + 1) * words_per_tile && w0 < a.bm_words && run < nl; w0 += 32) {
-      const int64_t w = w0 + lane;
-      uint32_t bits = (w < (t + 1) * words_per_tile && w < a.bm_words) ? row[w] : 0u;
-      if (__ballot_sync(0xffffffffu, bits != 0u) == 0u) continue;
-      const int pc = __popc(bits);
+    const int32_t off = need_off[l];
+    const int64_t w_end = (t + 1) * words_per_tile < a.bm_words ? (t + 1) * words_per_tile : a.bm_words;
+    for (int64_t w0 = t * words_per_tile; w0 < w_end && run < nl; w0 += 32 * kWordsPerLane) {
+      const int64_t wl = w0 + lane * kWordsPerLane;
+      uint32_t bits[kWordsPerLane];
+      int pc = 0;
+#pragma unroll
+      for (int q = 0; q < kWordsPerLane; ++q) {
+        bits[q] = wl + q < w_end ? __ldg(row + wl + q) : 0u;
+        pc += __popc(bits[q]);
+      }
       int incl = pc;
 #pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int o = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += o;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
       }
       int r = run + incl - pc;
-      while (bits && r < nl) {
-        const int b = __ffs(bits) - 1;
-        bits &= bits - 1;
-        list[need_off[l] + r] = static_cast<int32_t>(w * 32 + b);
-        ++r;
+#pragma unroll
+      for (int q = 0; q < kWordsPerLane; ++q) {
+        uint32_t b = bits[q];
+        while (b && r < nl) {
+          list[off + r] = static_cast<int32_t>((wl + q) * 32 + (__ffs(b) - 1));
+          b &= b - 1;
+          ++r;
+        }
       }
       run += __shfl_sync(0xffffffffu, incl, 31);
     }
@@ -418,6 +430,9 @@ __global__ void place_kernel(CandArgs c, WriteArgs w, const uint32_t *__restrict
                              uint8_t *__restrict__ overflowed) {
   const int64_t tail = w.topo ? 0 : *w.tail_start;
   const int64_t tail_free = w.topo ? 0 : w.global_cap - tail;
+  // the counts, tallied per thread and added once per warp (one address
+  // takes every candidate's increment otherwise)
+  int n_committed = 0, n_over = 0, n_tail = 0, n_resort = 0;
   for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < c.k;
        p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const uint32_t l = key[p];
@@ -446,13 +461,13 @@ __global__ void place_kernel(CandArgs c, WriteArgs w, const uint32_t *__restrict
     }
     if (committed) {
       if (w.committed) w.committed[i] = 1;
-      atomicAdd(counts + 0, 1);
-      if (to_tail) atomicAdd(counts + 2, 1);
+      ++n_committed;
+      if (to_tail) ++n_tail;
       const int32_t s = c.src[i], d = c.dst[i];
       const bool in = s >= 0 && s < c.num_units && d >= 0 && d < c.num_units;
-      if (in && c.level[d] <= c.level[s]) atomicAdd(counts + 3, 1);
+      if (in && c.level[d] <= c.level[s]) ++n_resort;
     } else {
-      atomicAdd(counts + 1, 1);
+      ++n_over;
     }
     if (slot >= 0 && slot < w.cap) {
       w.from[slot] = c.src[i];
@@ -470,6 +485,21 @@ __global__ void place_kernel(CandArgs c, WriteArgs w, const uint32_t *__restrict
       if (w.placed) w.placed[i] = static_cast<int32_t>(slot);
     }
   }
+  __shared__ int s_counts[4];
+  if (threadIdx.x < 4) s_counts[threadIdx.x] = 0;
+  __syncthreads();
+  n_committed = __reduce_add_sync(0xffffffffu, n_committed);
+  n_over = __reduce_add_sync(0xffffffffu, n_over);
+  n_tail = __reduce_add_sync(0xffffffffu, n_tail);
+  n_resort = __reduce_add_sync(0xffffffffu, n_resort);
+  if ((threadIdx.x & 31) == 0) {
+    if (n_committed) atomicAdd(&s_counts[0], n_committed);
+    if (n_over) atomicAdd(&s_counts[1], n_over);
+    if (n_tail) atomicAdd(&s_counts[2], n_tail);
+    if (n_resort) atomicAdd(&s_counts[3], n_resort);
+  }
+  __syncthreads();
+  if (threadIdx.x < 4 && s_counts[threadIdx.x]) atomicAdd(counts + threadIdx.x, s_counts[threadIdx.x]);
 }
 
 __global__ void finish_kernel(int topo, int64_t *tail_start, const int32_t *__restrict__ counts,

@@ -80,29 +80,46 @@ __global__ void __launch_bounds__(kPlanThreads) lowk_plan_kernel(uint32_t *__res
   __shared__ int s_bin, s_fbin;
   __shared__ long long s_below_c, s_below, s_in_bin;
   const int t = threadIdx.x;
-  uint32_t mine[kBinsPerThread];
+  // thread t holds coarse bins [64 t, 64 t + 64): sixteen 16-byte loads
+  const uint4 *h4 = reinterpret_cast<const uint4 *>(hist) + t * (kBinsPerThread / 4);
   long long sum = 0;
-#pragma unroll 8
-  for (int j = 0; j < kBinsPerThread; ++j) {
-    mine[j] = hist[t * kBinsPerThread + j];
-    sum += mine[j];
+#pragma unroll
+  for (int j = 0; j < kBinsPerThread / 4; ++j) {
+    const uint4 v = h4[j];
+    sum += static_cast<long long>(v.x) + v.y + v.z + v.w;
   }
   long long excl, total;
   Scan(scan_tmp).ExclusiveSum(sum, excl, total);
+  __shared__ int s_owner;
+  __shared__ long long s_owner_excl;
   if (t == 0) {
     s_bin = -1;
     s_fbin = -1;
+    s_owner = -1;
   }
   __syncthreads();
   if (k > 0 && total > k && excl < k && excl + sum >= k) {
-    long long c = excl;
-    for (int j = 0; j < kBinsPerThread; ++j) {
-      if (c + mine[j] >= k) {
-        s_bin = t * kBinsPerThread + j;
-        s_below_c = c;
-        break;
-      }
-      c += mine[j];
+    s_owner = t;
+    s_owner_excl = excl;
+  }
+  __syncthreads();
+  if (s_owner >= 0 && t < 32) {
+    // the owner's 64 bins, two per lane, ranked by a warp scan
+    const int o = s_owner;
+    const uint2 h2 = reinterpret_cast<const uint2 *>(hist + o * kBinsPerThread)[t];
+    long long incl = static_cast<long long>(h2.x) + h2.y;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const long long v = __shfl_up_sync(0xffffffffu, incl, d);
+      if (t >= d) incl += v;
+    }
+    const long long before = s_owner_excl + incl - h2.x - h2.y;
+    if (before < k && before + h2.x >= k) {
+      s_bin = o * kBinsPerThread + 2 * t;
+      s_below_c = before;
+    } else if (before + h2.x < k && before + h2.x + h2.y >= k) {
+      s_bin = o * kBinsPerThread + 2 * t + 1;
+      s_below_c = before + h2.x;
     }
   }
   __syncthreads();
@@ -169,20 +186,17 @@ __global__ void __launch_bounds__(kPlanThreads) lowk_plan_kernel(uint32_t *__res
     count[2 * p.parity + 1] = 0ull;
     if (fb >= 0 && !whole) fine[fb] -= static_cast<uint32_t>(take);
   }
-  // the coarse cut: bins wholly below the threshold's emptied, its own bin
-  // loses what its fine bins lose
+  // the coarse cut: bins wholly below the threshold's emptied (those from
+  // the floor's up: none below it holds an edge), its own bin loses what
+  // its fine bins lose
   if (k > 0) {
     const int cb = fb < 0 ? kLowkBins : b;
+    const int cfloor = static_cast<int>(min(old_floor >> (kLowkShift - kFineShift), static_cast<uint32_t>(kLowkBins)));
     const long long removed_in_b = fb < 0 ? 0 : (s_below - s_below_c) + (whole ? s_in_bin : take);
-#pragma unroll 8
-    for (int j = 0; j < kBinsPerThread; ++j) {
-      const int bin = t * kBinsPerThread + j;
-      if (bin < cb) {
-        if (mine[j]) hist[bin] = 0u;
-      } else if (bin == cb && removed_in_b > 0) {
-        hist[bin] = mine[j] - static_cast<uint32_t>(removed_in_b);
-      }
-    }
+    const int lo = max(cfloor, t * kBinsPerThread), hi = min(cb, (t + 1) * kBinsPerThread);
+    for (int bin = lo; bin < hi; ++bin) hist[bin] = 0u;
+    if (cb < kLowkBins && cb / kBinsPerThread == t && removed_in_b > 0)
+      hist[cb] -= static_cast<uint32_t>(removed_in_b);
   }
 }
 
@@ -214,30 +228,31 @@ struct SelectArgs {
   int32_t *level_before, *level_totals;
 };
 
-// The group holding mirror position pos: the last g with gbase[g] <= pos.
-__device__ __forceinline__ int64_t group_of(const MirrorK &m, int64_t pos) {
-  int64_t lo = 0, hi = m.groups - 1;
-  while (lo < hi) {
-    const int64_t mid = (lo + hi + 1) / 2;
-    if (m.gbase[mid] <= pos) lo = mid;
-    else hi = mid - 1;
-  }
-  return lo;
-}
-
 __device__ __forceinline__ const uint64_t *keys_of(const SelectArgs &a, int q) {
   return a.world == 1 ? a.my_key : a.peer_key[q];
 }
 
+// The select's keys staged in shared memory when every rank's list fits.
+constexpr int kStageKeys = 12288;  // 96 KB
+constexpr int kDigitBits = 10;
+constexpr int kDigits = 1 << kDigitBits;
+static_assert(kDigits == kSelectThreads, "one select thread per digit value");
+
 // One CTA: every rank's listed keys of this firing, the take-th smallest by
-// an 8-bit MSD radix select, this rank's listed edges up to it tombstoned.
+// an MSD radix select, this rank's listed edges up to it tombstoned. The
+// listed keys share their fine bin, i.e. key bits 63..39 (bits(|w|) >> 7
+// above the 32-bit slot), so four 10-bit digits over bits 38..0 decide; the
+// keys are read from shared memory when every rank's list fits there.
 __global__ void __launch_bounds__(kSelectThreads) lowk_select_kernel(SelectArgs a, MirrorK m) {
-  __shared__ unsigned int digit_hist[256];
-  __shared__ int64_t s_n[kMaxWorld];
-  __shared__ unsigned long long s_prefix, s_mask;
-  __shared__ long long s_want;
+  using Scan = cub::BlockScan<int, kSelectThreads>;
+  __shared__ typename Scan::TempStorage scan_tmp;
+  __shared__ unsigned int digit_hist[kDigits];
+  __shared__ int64_t s_n[kMaxWorld], s_off[kMaxWorld + 1];
+  __shared__ unsigned long long s_prefix;
+  __shared__ int s_want;
   __shared__ int s_sel[kMaxWorld * kMaxLevels];
   __shared__ int s_pruned;
+  extern __shared__ unsigned long long s_keys[];
   const int t = threadIdx.x;
   const int parity = a.plan->parity;
   const long long take = a.plan->take;
@@ -245,6 +260,7 @@ __global__ void __launch_bounds__(kSelectThreads) lowk_select_kernel(SelectArgs 
   if (t == 0) {
     long long listed = 0, below = 0;
     int status = 0;
+    s_off[0] = 0;
     for (int q = 0; q < a.world; ++q) {
       const unsigned long long *cnt = a.world == 1 ? a.my_count : a.peer_count[q];
       unsigned long long n = cnt[2 * parity];
@@ -253,59 +269,67 @@ __global__ void __launch_bounds__(kSelectThreads) lowk_select_kernel(SelectArgs 
         n = static_cast<unsigned long long>(a.cap);
       }
       s_n[q] = static_cast<int64_t>(n);
+      s_off[q + 1] = s_off[q] + static_cast<int64_t>(n);
       listed += static_cast<long long>(n);
       below += static_cast<long long>(cnt[2 * parity + 1]);
     }
     if (listed != a.plan->listed_expect || below != a.plan->below_expect) status |= 2;
     if (status) atomicOr(&a.plan->status, status);
-    s_prefix = 0ull;
-    s_mask = 0ull;
-    s_want = take;
     s_pruned = 0;
   }
   for (int i = t; i < kMaxWorld * kMaxLevels; i += kSelectThreads) s_sel[i] = 0;
   __syncthreads();
-  long long listed_total = 0;
-  for (int q = 0; q < a.world; ++q) listed_total += s_n[q];
+  const int64_t listed_total = s_off[a.world];
   if (take <= 0) {
     if (t == 0) a.plan->pruned = static_cast<int64_t>(a.my_count[2 * parity + 1]);
     return;
   }
+  const bool staged = listed_total <= kStageKeys;
+  if (staged) {
+    for (int q = 0; q < a.world; ++q) {
+      const uint64_t *keys = keys_of(a, q) + base;
+      for (int64_t i = t; i < s_n[q]; i += kSelectThreads) s_keys[s_off[q] + i] = keys[i];
+    }
+  }
   unsigned long long kstar = ~0ull;  // take >= every listed key: all of them
   if (take < listed_total) {
-    for (int shift = 56; shift >= 0; shift -= 8) {
-      for (int d = t; d < 256; d += kSelectThreads) digit_hist[d] = 0u;
+    // every listed key lies in the plan's fine bin: its bits 63..39
+    unsigned long long prefix = static_cast<unsigned long long>(a.plan->lo_bits >> kFineShift) << 39;
+    unsigned long long mask = ~0ull << 39;
+    int want = static_cast<int>(take);
+    for (int shift = 39 - kDigitBits; shift > -kDigitBits; shift -= kDigitBits) {
+      const int sh = shift > 0 ? shift : 0;
+      const int width = shift > 0 ? kDigitBits : kDigitBits + shift;
+      const unsigned long long dmask = (1ull << width) - 1ull;
+      digit_hist[t] = 0u;
       __syncthreads();
-      const unsigned long long prefix = s_prefix, mask = s_mask;
       for (int q = 0; q < a.world; ++q) {
         const uint64_t *keys = keys_of(a, q) + base;
         for (int64_t i = t; i < s_n[q]; i += kSelectThreads) {
-          const unsigned long long key = keys[i];
-          if ((key & mask) == prefix) atomicAdd(&digit_hist[(key >> shift) & 255u], 1u);
+          const unsigned long long key = staged ? s_keys[s_off[q] + i] : keys[i];
+          if ((key & mask) == prefix) atomicAdd(&digit_hist[(key >> sh) & dmask], 1u);
         }
       }
       __syncthreads();
-      if (t == 0) {
-        long long cum = 0;
-        const long long want = s_want;
-        int d = 0;
-        for (; d < 255; ++d) {
-          if (cum + digit_hist[d] >= want) break;
-          cum += digit_hist[d];
-        }
-        s_prefix = prefix | (static_cast<unsigned long long>(d) << shift);
-        s_mask = mask | (255ull << shift);
-        s_want = want - cum;
+      const int h = static_cast<int>(digit_hist[t]);
+      int excl;
+      Scan(scan_tmp).ExclusiveSum(h, excl);
+      if (excl < want && excl + h >= want) {
+        s_prefix = prefix | (static_cast<unsigned long long>(t) << sh);
+        s_want = want - excl;
       }
       __syncthreads();
+      prefix = s_prefix;
+      want = s_want;
+      mask |= dmask << sh;
     }
-    kstar = s_prefix;  // the keys are unique: exactly `take` of them are <= kstar
+    kstar = prefix;  // the keys are unique: exactly `take` of them are <= kstar
   }
   // this rank's selected edges leave the arena and the mirror
   int mine = 0;
   const uint64_t *my_keys = a.my_key + base;
   for (int64_t i = t; i < s_n[a.rank]; i += kSelectThreads) {
-    const unsigned long long key = my_keys[i];
+    const unsigned long long key = staged ? s_keys[s_off[a.rank] + i] : my_keys[i];
     if (key > kstar) continue;
     const int32_t slot = static_cast<int32_t>(static_cast<uint32_t>(key) - static_cast<uint32_t>(a.slot_base));
     const int64_t pos = a.my_pos[base + i];
@@ -332,13 +356,15 @@ __global__ void __launch_bounds__(kSelectThreads) lowk_select_kernel(SelectArgs 
       const uint64_t *keys = keys_of(a, q) + base;
       const int32_t *lv = a.world == 1 ? a.my_level : a.peer_level[q];
       for (int64_t i = t; i < s_n[q]; i += kSelectThreads) {
-        if (keys[i] > kstar) continue;
+        const unsigned long long key = staged ? s_keys[s_off[q] + i] : keys[i];
+        if (key > kstar) continue;
         const int l = lv[base + i];
         if (l >= 0 && l < a.num_levels) atomicAdd(&s_sel[q * kMaxLevels + l], 1);
       }
     }
   }
-  atomicAdd(&s_pruned, mine);
+  mine = __reduce_add_sync(0xffffffffu, mine);
+  if ((t & 31) == 0 && mine) atomicAdd(&s_pruned, mine);
   __syncthreads();
   if (a.level_totals != nullptr && t < a.num_levels) {
     int before = 0, total = 0;
@@ -353,29 +379,54 @@ __global__ void __launch_bounds__(kSelectThreads) lowk_select_kernel(SelectArgs 
   if (t == 0) a.plan->pruned = static_cast<int64_t>(a.my_count[2 * parity + 1]) + s_pruned;
 }
 
-__global__ void lowk_hist_add_kernel(uint32_t *__restrict__ hist, uint32_t *__restrict__ fine, int64_t k,
-                                     const float *__restrict__ weight, const uint8_t *__restrict__ committed,
-                                     pxb_lowk_plan *plan, const int32_t *claim_counts, long long *totals) {
+// The committed growth edges into both histograms. Their weights crowd a
+// few hundred coarse bins, so each CTA counts its edges' coarse bins in
+// shared memory (16-bit halves of 32-bit words) and adds each touched bin
+// once; the fine bins are spread thin and take their atomics directly.
+constexpr int kAddThreads = 1024;
+constexpr int kAddPer = 4;  // edges per thread: a CTA's count per bin stays below 2^16
+__global__ void __launch_bounds__(kAddThreads) lowk_hist_add_kernel(uint32_t *__restrict__ hist,
+                                                                   uint32_t *__restrict__ fine, int64_t k,
+                                                                   const float *__restrict__ weight,
+                                                                   const uint8_t *__restrict__ committed,
+                                                                   pxb_lowk_plan *plan, const int32_t *claim_counts,
+                                                                   long long *totals) {
+  extern __shared__ uint32_t s_half[];  // kLowkBins / 2 words
+  __shared__ uint32_t s_lowest;
   if (totals != nullptr && blockIdx.x == 0 && threadIdx.x == 0) {
-    totals[0] += plan->pruned;
+    atomicAdd(reinterpret_cast<unsigned long long *>(totals + 0), static_cast<unsigned long long>(plan->pruned));
     if (claim_counts != nullptr) {
-      totals[1] += claim_counts[0];
-      totals[2] += claim_counts[1];
+      atomicAdd(reinterpret_cast<unsigned long long *>(totals + 1), static_cast<unsigned long long>(claim_counts[0]));
+      atomicAdd(reinterpret_cast<unsigned long long *>(totals + 2), static_cast<unsigned long long>(claim_counts[1]));
     }
-    totals[3] += 1;
+    atomicAdd(reinterpret_cast<unsigned long long *>(totals + 3), 1ull);
   }
+  for (int i = threadIdx.x; i < kLowkBins / 2; i += kAddThreads) s_half[i] = 0u;
+  if (threadIdx.x == 0) s_lowest = 0xffffffffu;
+  __syncthreads();
   uint32_t lowest = 0xffffffffu;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < k;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    if (!committed[i]) continue;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kAddThreads * kAddPer;
+#pragma unroll
+  for (int j = 0; j < kAddPer; ++j) {
+    const int64_t i = base + j * kAddThreads + threadIdx.x;
+    if (i >= k || !committed[i]) continue;
     const uint32_t b = abs_bits(weight[i]);
     if (b > kInfBits) continue;
-    atomicAdd(hist + (b >> kLowkShift), 1u);
+    const uint32_t cbin = b >> kLowkShift;
+    atomicAdd(&s_half[cbin >> 1], (cbin & 1u) ? 0x10000u : 1u);
     atomicAdd(fine + (b >> kFineShift), 1u);
     lowest = min(lowest, b >> kFineShift);
   }
+  // the floor: one atomic per CTA (one address takes them all)
   lowest = __reduce_min_sync(0xffffffffu, lowest);
-  if ((threadIdx.x & 31) == 0 && lowest != 0xffffffffu) atomicMin(&plan->floor, lowest);
+  if ((threadIdx.x & 31) == 0 && lowest != 0xffffffffu) atomicMin(&s_lowest, lowest);
+  __syncthreads();
+  if (threadIdx.x == 0 && s_lowest != 0xffffffffu) atomicMin(&plan->floor, s_lowest);
+  for (int i = threadIdx.x; i < kLowkBins / 2; i += kAddThreads) {
+    const uint32_t v = s_half[i];
+    if (v & 0xffffu) atomicAdd(hist + 2 * i, v & 0xffffu);
+    if (v >> 16) atomicAdd(hist + 2 * i + 1, v >> 16);
+  }
 }
 
 static int check_lowk(const char *fn, const pxb_lowk *lk) {
@@ -449,7 +500,9 @@ extern "C" int pxb_lowk_select(const pxb_lowk *lowk, const pxb_mirror *mirror, u
   a.num_levels = num_levels;
   a.level_before = level_before;
   a.level_totals = level_totals;
-  lowk_select_kernel<<<1, kSelectThreads, 0, as_stream(stream)>>>(a, to_k(mirror));
+  const size_t smem = kStageKeys * sizeof(unsigned long long);
+  PXB_CUDA(cudaFuncSetAttribute(lowk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  lowk_select_kernel<<<1, kSelectThreads, smem, as_stream(stream)>>>(a, to_k(mirror));
   PXB_LAUNCHED("lowk_select_kernel");
   return PXB_OK;
 }
@@ -460,7 +513,11 @@ extern "C" int pxb_lowk_hist_add(const pxb_lowk *lowk, int64_t k, const float *w
   if (rc) return rc;
   PXB_REQUIRE(k >= 0, "pxb_lowk_hist_add: negative k");
   PXB_REQUIRE(k == 0 || (weight && committed), "pxb_lowk_hist_add: weight/committed is NULL");
-  lowk_hist_add_kernel<<<grid_for(k > 0 ? k : 1, 256, 4), 256, 0, as_stream(stream)>>>(
+  const size_t smem = kLowkBins / 2 * sizeof(uint32_t);
+  PXB_CUDA(cudaFuncSetAttribute(lowk_hist_add_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  const int64_t per_cta = int64_t(kAddThreads) * kAddPer;
+  const int grid = static_cast<int>(k > 0 ? (k + per_cta - 1) / per_cta : 1);
+  lowk_hist_add_kernel<<<grid, kAddThreads, smem, as_stream(stream)>>>(
       lowk->hist, lowk->fine, k, weight, committed, lowk->plan, claim_counts, reinterpret_cast<long long *>(totals));
   PXB_LAUNCHED("lowk_hist_add_kernel");
   return PXB_OK;

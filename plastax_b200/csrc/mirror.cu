@@ -194,11 +194,27 @@ __device__ __forceinline__ bool next_tile(const MirrorK &m, int64_t &t, int64_t 
 // tombstones are written after the combines. Mirror words are written only
 // by the build and the insert, which keep src < n and dst < n, so the loop
 // carries no range checks (an accumulator past n is dropped at the flush).
+// A pruned entry: its position goes on this CTA's deferred list (the
+// tombstone is written by mirror_defer_flush_kernel after the sweep), or,
+// when the list is full or absent, the tombstone is written here.
+__device__ __forceinline__ void prune_entry(const MirrorK &m, const MPrune &p, int64_t pos, int32_t src, int64_t g,
+                                            int64_t gb, int *defer_n, int64_t seg) {
+  if (defer_n != nullptr) {
+    const int i = atomicAdd(defer_n, 1);
+    if (i < seg) {
+      m.defer_pos[blockIdx.x * seg + i] = pos;
+      return;
+    }
+  }
+  tombstone(p, m.slot[pos], src);
+  empty_entry(m, pos, g, gb);
+}
+
 template <int MONOID, int PK>
 __device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, const LowkCut &cut,
                                            const float *__restrict__ act, const uint32_t *word_t, const float *w_t,
                                            int used, float *acc_s, float *acc_g, int32_t g, int64_t gb, int64_t e0,
-                                           int &pruned_here) {
+                                           int &pruned_here, int *defer_n, int64_t seg) {
   const uint32_t mask = (1u << m.cb) - 1u;
   const int chunk = 1 << m.cb;
   const uint32_t last = static_cast<uint32_t>(m.n - 1);
@@ -267,11 +283,12 @@ __device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, co
         any = mn < p.thr;
       } else if (PK == PXB_PRUNE_LOWEST_K) {
         // below the threshold bin's end (an empty entry's zero weight
-        // passes and is skipped below; a NaN never does)
-        uint32_t mn = abs_bits(fs[0]);
+        // passes and is skipped below; fminf drops a NaN, which is never
+        // pruned or listed)
+        float mn = fabsf(fs[0]);
 #pragma unroll
-        for (int j = 1; j < 8; ++j) mn = min(mn, abs_bits(fs[j]));
-        any = mn < cut.hi;
+        for (int j = 1; j < 8; ++j) mn = fminf(mn, fabsf(fs[j]));
+        any = mn <= cut.hi_le;
       } else {
         any = false;
 #pragma unroll
@@ -294,8 +311,7 @@ __device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, co
             const float thr = PK == PXB_PRUNE_ABS_BELOW ? p.thr : __ldg(p.unit_thr + ((g << m.cb) | (ws[j] & mask)));
             if (!(fabsf(fs[j]) < thr)) continue;
           }
-          tombstone(p, m.slot[pos], static_cast<int32_t>(ws[j] >> m.cb));
-          empty_entry(m, pos, g, gb);
+          prune_entry(m, p, pos, static_cast<int32_t>(ws[j] >> m.cb), g, gb, defer_n, seg);
         }
       }
     }
@@ -356,12 +372,19 @@ __global__ void __launch_bounds__(kSweepThreads, PXB_SWEEP_MIN_CTAS) mirror_swee
   float *w_s = reinterpret_cast<float *>(word_s + kStages * kTile);
   float *acc_s = w_s + kStages * kTile;
 
+  __shared__ int s_defer;
+  const bool defer = PK != PXB_PRUNE_NONE && m.defer_pos != nullptr && gridDim.x <= m.defer_ctas;
+  const int64_t seg = defer ? m.defer_total / gridDim.x : 0;
   const int64_t tiles = m.entries / kTile;
   const int64_t per = (tiles + gridDim.x - 1) / gridDim.x;
   const int64_t t_lo = blockIdx.x * per;
   const int64_t t_hi = t_lo + per < tiles ? t_lo + per : tiles;
-  if (t_lo >= t_hi) return;
+  if (t_lo >= t_hi) {
+    if (defer && threadIdx.x == 0) m.defer_count[blockIdx.x] = 0;
+    return;
+  }
   if (threadIdx.x == 0) {
+    s_defer = 0;
     for (int s = 0; s < kStages; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, kConsWarps);
@@ -432,7 +455,7 @@ __global__ void __launch_bounds__(kSweepThreads, PXB_SWEEP_MIN_CTAS) mirror_swee
     if (ok)
       sweep_tile<MONOID, PK>(m, p, cut, act, word_s + s * kTile, w_s + s * kTile, used, acc_s,
                              acc + (static_cast<int64_t>(g) << m.cb), static_cast<int32_t>(g), c.base, t * kTile,
-                             pruned_here);
+                             pruned_here, defer ? &s_defer : nullptr, seg);
     __syncwarp();
     if (lane == 0) mbar_arrive(empty + s);
     ++t;
@@ -441,6 +464,10 @@ __global__ void __launch_bounds__(kSweepThreads, PXB_SWEEP_MIN_CTAS) mirror_swee
   if (cur >= 0) {
     consumer_sync();
     flush_reset<MONOID>(m, acc_s, acc, acc_fixed, cur);
+  }
+  if (defer) {
+    consumer_sync();  // every consumer's deferred prunes are listed
+    if (threadIdx.x == 0) m.defer_count[blockIdx.x] = s_defer < seg ? s_defer : static_cast<int>(seg);
   }
   if (!ok && lane == 0) atomicOr(m.status, 2);
   if (PK == PXB_PRUNE_LOWEST_K) {
@@ -485,14 +512,120 @@ __global__ void mirror_overflow_kernel(MirrorK m, const float *__restrict__ act,
   }
 }
 
-// Insert, phase 1: each placed edge takes rank r in its destination group
-// (one atomicAdd on the group's insert counter); the r-th insert of a group
-// takes the group's r-th hole from the top of its stack, then its unused
-// slack, then the overflow list. Phase 2 retires the used holes and slack.
+// The sweep's deferred prunes: CTA c of the sweep listed defer_count[c]
+// entry positions (all inside its contiguous run of tiles, so in a few
+// groups); each gets its tombstone (canonical dead byte, free bitmap bit)
+// and leaves the mirror (emptied, pushed on its group's hole stack). The
+// pushes are counted per group in shared memory first and each group's run
+// of the stack reserved with one atomic, as one counter per group would
+// take every push of the run otherwise.
+constexpr int kFlushThreads = 256;
+constexpr int kFlushPer = 8;
+constexpr int kFlushGroups = 64;
+__global__ void __launch_bounds__(kFlushThreads) mirror_defer_flush_kernel(MirrorK m, MPrune p, int sweep_ctas) {
+  __shared__ int32_t s_cnt[kFlushGroups];
+  const int64_t seg = m.defer_total / sweep_ctas;
+  const int64_t tiles = m.entries / kTile;
+  const int64_t per = (tiles + sweep_ctas - 1) / sweep_ctas;
+  for (int c = blockIdx.x; c < sweep_ctas; c += gridDim.x) {
+    const int n = m.defer_count[c];
+    if (n == 0) continue;  // uniform over the CTA
+    const int64_t t_lo = c * per, t_hi = min(t_lo + per, tiles);
+    const int64_t g0 = group_of(m, t_lo * kTile), g1 = group_of(m, t_hi * kTile - 1);
+    const bool local = g1 - g0 < kFlushGroups;
+    for (int chunk = 0; chunk < n; chunk += kFlushThreads * kFlushPer) {
+      if (threadIdx.x < kFlushGroups) s_cnt[threadIdx.x] = 0;
+      __syncthreads();
+      int64_t pos[kFlushPer], grp[kFlushPer];
+      int rank[kFlushPer];
+#pragma unroll
+      for (int j = 0; j < kFlushPer; ++j) {
+        const int i = chunk + j * kFlushThreads + threadIdx.x;
+        pos[j] = -1;
+        if (i >= n) continue;
+        pos[j] = m.defer_pos[c * seg + i];
+        if (local) {
+          int64_t g = g0;  // the CTA's run spans a few groups
+          while (g < g1 && __ldg(m.gbase + g + 1) <= pos[j]) ++g;
+          grp[j] = g;
+          rank[j] = atomicAdd(&s_cnt[g - g0], 1);
+        } else {
+          grp[j] = group_of(m, pos[j]);
+        }
+      }
+      __syncthreads();
+      if (local && threadIdx.x < kFlushGroups && g0 + threadIdx.x <= g1) {
+        const int32_t cnt = s_cnt[threadIdx.x];
+        if (cnt) s_cnt[threadIdx.x] = atomicAdd(m.hcount + g0 + threadIdx.x, cnt);  // the run's first hole
+      }
+      __syncthreads();
+      // every load first (a store to word may alias a later entry's load,
+      // which would serialise the entries), then the writes
+      int32_t src[kFlushPer], slot[kFlushPer], row[kFlushPer];
+#pragma unroll
+      for (int j = 0; j < kFlushPer; ++j) {
+        if (pos[j] < 0) continue;
+        src[j] = static_cast<int32_t>(m.word[pos[j]] >> m.cb);
+        slot[j] = m.slot[pos[j]];
+      }
+#pragma unroll
+      for (int j = 0; j < kFlushPer; ++j)
+        if (pos[j] >= 0) row[j] = p.bm_level ? __ldg(p.bm_level + src[j]) : 0;
+#pragma unroll
+      for (int j = 0; j < kFlushPer; ++j) {
+        if (pos[j] < 0) continue;
+        p.dead[slot[j]] = 1;
+        if (p.bm != nullptr)
+          atomicOr(p.bm + static_cast<int64_t>(row[j]) * p.bm_words + (slot[j] >> 5), 1u << (slot[j] & 31));
+        if (p.pruned) atomicAdd(p.pruned, 1);
+        const int64_t gb = m.gbase[grp[j]];
+        m.word[pos[j]] = kEmpty;
+        m.w[pos[j]] = 0.0f;
+        const int32_t h = local ? s_cnt[grp[j] - g0] + rank[j] : atomicAdd(m.hcount + grp[j], 1);
+        m.hstack[gb + h] = static_cast<int32_t>(pos[j] - gb);
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Insert, phase 1: each placed edge takes rank r in its destination group;
+// the r-th insert of a group takes the group's r-th hole from the top of its
+// stack, then its unused slack, then the overflow list. Phase 2 retires the
+// used holes and slack.
+__device__ __forceinline__ void insert_at(const MirrorK &m, int32_t a, int32_t d, float w, int32_t s, int32_t g,
+                                          int32_t r) {
+  const int64_t gb = m.gbase[g], gcap = m.gbase[g + 1] - gb;
+  const int32_t holes = m.hcount[g];
+  int64_t pos = -1;
+  if (r < holes) {
+    pos = gb + m.hstack[gb + holes - 1 - r];
+  } else {
+    const int64_t f = static_cast<int64_t>(m.gfill[g]) + (r - holes);
+    if (f < gcap) pos = gb + f;
+  }
+  if (pos >= 0) {
+    m.word[pos] = (static_cast<uint32_t>(a) << m.cb) | (static_cast<uint32_t>(d) & ((1u << m.cb) - 1u));
+    m.w[pos] = w;
+    m.slot[pos] = s;
+  } else {
+    const int32_t o = atomicAdd(m.ovf_count, 1);
+    if (o < m.ovf_cap) {
+      m.ovf_src[o] = a;
+      m.ovf_dst[o] = d;
+      m.ovf_w[o] = w;
+      m.ovf_slot[o] = s;
+    } else {
+      atomicOr(m.status, 1);  // an edge is missing from the mirror: rebuild it
+    }
+  }
+}
+
+// One global counter per destination group takes every placed edge's rank
+// (the path for meshes of many groups).
 __global__ void mirror_insert_kernel(MirrorK m, int64_t k, const int32_t *__restrict__ src,
                                      const int32_t *__restrict__ dst, const float *__restrict__ w,
                                      const int32_t *__restrict__ placed, int32_t *__restrict__ ins_count) {
-  const uint32_t mask = (1u << m.cb) - 1u;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < k;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int32_t s = placed[i];
@@ -500,31 +633,46 @@ __global__ void mirror_insert_kernel(MirrorK m, int64_t k, const int32_t *__rest
     const int32_t a = src[i], d = dst[i];
     if (a < 0 || a >= m.n || d < 0 || d >= m.n) continue;
     const int32_t g = d >> m.cb;
-    const int64_t gb = m.gbase[g], gcap = m.gbase[g + 1] - gb;
-    const int32_t r = atomicAdd(ins_count + g, 1);
-    const int32_t holes = m.hcount[g];
-    int64_t pos = -1;
-    if (r < holes) {
-      pos = gb + m.hstack[gb + holes - 1 - r];
-    } else {
-      const int64_t f = static_cast<int64_t>(m.gfill[g]) + (r - holes);
-      if (f < gcap) pos = gb + f;
-    }
-    if (pos >= 0) {
-      m.word[pos] = (static_cast<uint32_t>(a) << m.cb) | (static_cast<uint32_t>(d) & mask);
-      m.w[pos] = w[i];
-      m.slot[pos] = s;
-    } else {
-      const int32_t o = atomicAdd(m.ovf_count, 1);
-      if (o < m.ovf_cap) {
-        m.ovf_src[o] = a;
-        m.ovf_dst[o] = d;
-        m.ovf_w[o] = w[i];
-        m.ovf_slot[o] = s;
-      } else {
-        atomicOr(m.status, 1);  // an edge is missing from the mirror: rebuild it
-      }
-    }
+    insert_at(m, a, d, w[i], s, g, atomicAdd(ins_count + g, 1));
+  }
+}
+
+// The same ranks with the groups counted per CTA first: each CTA takes
+// kInsertPer edges per thread, ranks them in shared memory, reserves each
+// group's run with one global atomic, then inserts (a global counter per
+// edge would serialise on the few hundred group counters).
+constexpr int kInsertThreads = 1024;
+constexpr int kInsertPer = 2;
+constexpr int kInsertMaxGroups = 8192;
+__global__ void __launch_bounds__(kInsertThreads) mirror_insert_grouped_kernel(
+    MirrorK m, int64_t k, const int32_t *__restrict__ src, const int32_t *__restrict__ dst,
+    const float *__restrict__ w, const int32_t *__restrict__ placed, int32_t *__restrict__ ins_count) {
+  __shared__ int32_t s_cnt[kInsertMaxGroups];
+  for (int64_t g = threadIdx.x; g < m.groups; g += kInsertThreads) s_cnt[g] = 0;
+  __syncthreads();
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kInsertThreads * kInsertPer;
+  int32_t grp[kInsertPer], rank[kInsertPer];
+#pragma unroll
+  for (int j = 0; j < kInsertPer; ++j) {
+    const int64_t i = base + j * kInsertThreads + threadIdx.x;
+    grp[j] = -1;
+    if (i >= k || placed[i] < 0) continue;
+    const int32_t a = src[i], d = dst[i];
+    if (a < 0 || a >= m.n || d < 0 || d >= m.n) continue;
+    grp[j] = d >> m.cb;
+    rank[j] = atomicAdd(&s_cnt[grp[j]], 1);
+  }
+  __syncthreads();
+  for (int64_t g = threadIdx.x; g < m.groups; g += kInsertThreads) {
+    const int32_t c = s_cnt[g];
+    if (c) s_cnt[g] = atomicAdd(ins_count + g, c);  // the CTA's first rank in group g
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kInsertPer; ++j) {
+    if (grp[j] < 0) continue;
+    const int64_t i = base + j * kInsertThreads + threadIdx.x;
+    insert_at(m, src[i], dst[i], w[i], placed[i], grp[j], s_cnt[grp[j]] + rank[j]);
   }
 }
 
@@ -576,6 +724,7 @@ namespace pxb {
 static int mirror_forward_launch(const MirrorK &m, const float *act, int32_t monoid, float *acc, int64_t *acc_fixed,
                                  const MPrune &p, cudaStream_t st) {
   const int32_t prune_kind = p.kind;
+  int sweep_grid = 0;
   if (m.entries > 0) {
     const size_t acc_bytes = (monoid == PXB_MONOID_SUM ? 2 * sizeof(int32_t) : sizeof(float)) << m.cb;
     const size_t smem = 128 + size_t(kStages) * kTile * 8 + acc_bytes;
@@ -588,8 +737,8 @@ static int mirror_forward_launch(const MirrorK &m, const float *act, int32_t mon
     int per_sm = 0;                                                                               \
     PXB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem));          \
     const int64_t full = int64_t(sm_count()) * (per_sm > 0 ? per_sm : 1);                        \
-    const int grid = static_cast<int>(tiles < full ? tiles : full);                               \
-    fn<<<grid, threads, smem, st>>>(m, act, acc, acc_fixed, p);                                   \
+    sweep_grid = static_cast<int>(tiles < full ? tiles : full);                                   \
+    fn<<<sweep_grid, threads, smem, st>>>(m, act, acc, acc_fixed, p);                             \
   } while (0)
 #define PXB_MS_K(M)                                                                               \
   do {                                                                                            \
@@ -604,6 +753,10 @@ static int mirror_forward_launch(const MirrorK &m, const float *act, int32_t mon
 #undef PXB_MS_K
 #undef PXB_MS
     PXB_LAUNCHED("mirror_sweep_kernel");
+    if (prune_kind != PXB_PRUNE_NONE && m.defer_pos != nullptr && sweep_grid <= m.defer_ctas) {
+      mirror_defer_flush_kernel<<<sweep_grid, kFlushThreads, 0, st>>>(m, p, sweep_grid);
+      PXB_LAUNCHED("mirror_defer_flush_kernel");
+    }
   }
   if (m.ovf_cap > 0) {
 #define PXB_MO(M, P) mirror_overflow_kernel<M, P><<<sm_count(), 256, 0, st>>>(m, act, acc, acc_fixed, p)
@@ -679,8 +832,15 @@ extern "C" int pxb_mirror_insert(const pxb_mirror *mirror, int64_t k, const int3
   PXB_REQUIRE(mirror->ins_count != nullptr, "pxb_mirror_insert: ins_count is NULL");
   cudaStream_t st = as_stream(stream);
   const MirrorK m = to_k(mirror);
-  mirror_insert_kernel<<<grid_for(k, 256, 8), 256, 0, st>>>(m, k, src, dst, weight, placed, mirror->ins_count);
-  PXB_LAUNCHED("mirror_insert_kernel");
+  if (m.groups <= kInsertMaxGroups) {
+    const int64_t per_cta = int64_t(kInsertThreads) * kInsertPer;
+    mirror_insert_grouped_kernel<<<static_cast<int>((k + per_cta - 1) / per_cta), kInsertThreads, 0, st>>>(
+        m, k, src, dst, weight, placed, mirror->ins_count);
+    PXB_LAUNCHED("mirror_insert_grouped_kernel");
+  } else {
+    mirror_insert_kernel<<<grid_for(k, 256, 8), 256, 0, st>>>(m, k, src, dst, weight, placed, mirror->ins_count);
+    PXB_LAUNCHED("mirror_insert_kernel");
+  }
   mirror_insert_finish_kernel<<<grid_for(m.groups, 256, 4), 256, 0, st>>>(m, mirror->ins_count);
   PXB_LAUNCHED("mirror_insert_finish_kernel");
   return PXB_OK;

@@ -27,6 +27,10 @@ struct MirrorK {
   int32_t *ovf_count, *ovf_src, *ovf_dst, *ovf_slot;
   float *ovf_w;
   int32_t *status;
+  int64_t *defer_pos;  // the sweep's deferred prunes (NULL: in place)
+  int32_t *defer_count;
+  int64_t defer_total;
+  int32_t defer_ctas;
 };
 
 inline MirrorK to_k(const pxb_mirror *m) {
@@ -53,7 +57,23 @@ inline MirrorK to_k(const pxb_mirror *m) {
   k.ovf_slot = m->ovf_slot;
   k.ovf_w = m->ovf_weight;
   k.status = m->status;
+  const bool defer = m->defer_pos != nullptr && m->defer_count != nullptr && m->defer_seg > 0 && m->defer_ctas > 0;
+  k.defer_pos = defer ? m->defer_pos : nullptr;
+  k.defer_count = defer ? m->defer_count : nullptr;
+  k.defer_total = defer ? m->defer_seg * m->defer_ctas : 0;
+  k.defer_ctas = defer ? m->defer_ctas : 0;
   return k;
+}
+
+// The group holding mirror position pos: the last g with gbase[g] <= pos.
+__device__ __forceinline__ int64_t group_of(const MirrorK &m, int64_t pos) {
+  int64_t lo = 0, hi = m.groups - 1;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) / 2;
+    if (m.gbase[mid] <= pos) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
 }
 
 int check_mirror(const char *fn, const pxb_mirror *m);
@@ -80,17 +100,23 @@ struct MPrune {
   LowkSweep lk;
 };
 
-// The plan's cut as one sweep reads it.
+// The plan's cut as one sweep reads it. hi_le is the float whose bits are
+// hi - 1: for a non-NaN w, bits(|w|) < hi exactly when |w| <= hi_le (the
+// bit order of non-negative floats is their value order; hi - 1 = +inf's
+// bits takes every non-NaN, and hi = 0 gives a NaN that takes none), so the
+// fast test is one float min over the entries with the free |.| modifier.
 struct LowkCut {
   uint32_t lo, hi;
+  float hi_le;
   int parity;
 };
 
 __device__ __forceinline__ LowkCut lowk_cut(const MPrune &p) {
-  LowkCut c{0u, 0u, 0};
+  LowkCut c{0u, 0u, 0.0f, 0};
   if (p.kind == PXB_PRUNE_LOWEST_K) {
     c.lo = p.lk.plan->lo_bits;
     c.hi = p.lk.plan->hi_bits;
+    c.hi_le = __uint_as_float(c.hi - 1u);
     c.parity = p.lk.plan->parity;
   }
   return c;

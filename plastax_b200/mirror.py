@@ -89,12 +89,22 @@ class Mirror:
         self.ovf_weight = torch.zeros(max(ovf_cap, 1), dtype=torch.float32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.ins_count = torch.zeros(groups, dtype=torch.int32, device=dev)
+        # the sweep's deferred prunes: one segment per sweep CTA (up to 8 per
+        # SM), together about one entry in 256 (a CTA whose segment fills up
+        # writes the rest of its tombstones in place)
+        from plastax_b200.kernels import sm_count
+
+        self.defer_ctas = 8 * sm_count()
+        self.defer_seg = max(256, entries // 256 // self.defer_ctas)
+        self.defer_pos = torch.empty(self.defer_ctas * self.defer_seg, dtype=torch.int64, device=dev)
+        self.defer_count = torch.zeros(self.defer_ctas, dtype=torch.int32, device=dev)
         p = lambda x: x.data_ptr()  # noqa: E731
         self.struct = _lib.Mirror(
             n, cb, groups, entries, p(self.gbase), p(self.gfill), p(self.word), p(self.weight), p(self.slot),
             p(self.hstack), p(self.hcount), len(ib), p(self.item_begin), p(self.item_end), p(self.item_group),
             self.ovf_cap, p(self.ovf_count), p(self.ovf_src), p(self.ovf_dst), p(self.ovf_slot), p(self.ovf_weight),
-            p(self.status), p(self.ins_count))
+            p(self.status), p(self.ins_count), p(self.defer_pos), p(self.defer_count), self.defer_seg,
+            self.defer_ctas)
 
     def healthy(self) -> bool:
         """False when an edge could not be mirrored (host read; synchronises)."""

@@ -219,7 +219,8 @@ class StepFn:
             from plastax_b200.peers import PeerGroup
 
             if self.peers is None:
-                self.peers = PeerGroup(st.num_units, self.dev, lowk_cap=self._lowk_list_cap())
+                self.peers = PeerGroup(st.num_units, self.dev,
+                                       lowk_cap=self._lowk_list_cap() if self.lowk_prune else 0)
                 self.acc_fixed = self.peers.acc_fixed
                 self.acc = self.peers.acc_side
             # the activation column lives in the group's region: peers write it

@@ -69,6 +69,25 @@ def _cfg():
     return ReservoirConfig(num_units=1 << 12, fan_in=16, churn=0.01, capacity_align=256)
 
 
+def _collect(q, procs, n, timeout=500.0):
+    """n results from the rank processes; fails as soon as a rank exits
+    with an error instead of waiting out the whole timeout."""
+    import queue
+
+    got, t0 = {}, time.monotonic()
+    while len(got) < n:
+        try:
+            r, out = q.get(timeout=2.0)
+            got[r] = out
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            if dead:
+                raise AssertionError(f"a rank exited with {dead[0]}")
+            if time.monotonic() - t0 > timeout:
+                raise AssertionError("the ranks did not report in time")
+    return got
+
+
 def _inputs(steps, m):
     return np.random.default_rng(8).standard_normal((steps, m)).astype(np.float32)
 
@@ -135,7 +154,7 @@ def test_two_rank_peer_step_equals_one_gpu_step(cuda):
     procs = [ctx.Process(target=_run, args=(r, 2, port, steps, q)) for r in range(2)]
     for p in procs:
         p.start()
-    got = dict(q.get(timeout=500) for _ in range(2))
+    got = _collect(q, procs, 2)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -222,7 +241,7 @@ def test_two_rank_per_connection_proposer_equals_one_gpu(cuda):
     procs = [ctx.Process(target=_run_per_conn, args=(r, 2, port, steps, q)) for r in range(2)]
     for p in procs:
         p.start()
-    got = dict(q.get(timeout=500) for _ in range(2))
+    got = _collect(q, procs, 2)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
