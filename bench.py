@@ -43,6 +43,10 @@ ROOT = pathlib.Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "propagated edges/sec per step (Scheme-A large reservoir churn step)"
+TRAINING = ("esn", "dst", "mlp", "mlp50", "units")
+# nominal FP32 (non-tensor) FMA peak of a B200: 148 SMs x 128 lanes x 2 FLOP
+# x 1.965 GHz (no measured figure exists for it; stated as nominal)
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 UNIT = "edges/s"
 # DRAM bytes (read + write) per swept mirror entry of the fused forward+prune
 # sweep, from one ncu capture of the 2^18-unit reservoir with the full-size
@@ -65,6 +69,11 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    ap.add_argument("--config", default="reservoir", choices=["reservoir", *TRAINING],
+                    help="reservoir: the Scheme-A large-reservoir churn step (the headline); esn: the streaming "
+                         "echo-state reservoir; dst: dynamic sparse training; mlp / mlp50: the sparse MLP at 10%% "
+                         "/ 50%% density, batch 256; units: the unit lifecycle (training configurations run as "
+                         "independent replicas when N > 1)")
     ap.add_argument("--units-log2", type=int, default=20, help="reservoir size (2**x units)")
     ap.add_argument("--fan-in", type=int, default=256)
     ap.add_argument("--chunk-bits", type=int, default=None,
@@ -569,8 +578,344 @@ def count_launches(step, state, x, dev) -> int:
         step.graph = graph
 
 
+# ---------------------------------------------------------------------------
+# the training configurations (one GPU; independent replicas when N > 1)
+# ---------------------------------------------------------------------------
+def training_case(kind: str, dev, steps: int):
+    """The network, state, step and per-step inputs of a training
+    configuration, with what its bench line reports; with dev None only the
+    inputs and the description (the reference arm builds its own host
+    state)."""
+    import torch
+
+    from plastax_b200 import configs as C
+    from plastax_b200 import make_step
+
+    g = np.random.default_rng(11)
+    case: dict = {"kind": kind}
+    if kind == "esn":
+        cfg = C.C1
+        xs = g.standard_normal(steps + cfg.delay).astype(np.float32)
+        case.update(x=xs[cfg.delay:, None], t=xs[:-cfg.delay, None], passes=1,
+                    desc={"workload": f"streaming echo-state reservoir: {cfg.units} tanh units, fan-in {cfg.fan_in}, "
+                                      f"spectral radius {cfg.rho}, 1 input, a linear readout trained by LMS "
+                                      f"(lr {cfg.lr}) on the input delayed {cfg.delay} steps",
+                          "propagation": "pipeline", "parallelism": "replicas"},
+                    bytes_per_slot={"forward": 13, "update": 17})
+        if dev is not None:
+            net, static, state = C.build_esn(cfg, dev)
+            step = make_step(net, static, device=dev)
+    elif kind == "dst":
+        cfg = C.C3
+        w1, w2 = C.dst_teacher(cfg)
+        x = g.standard_normal((steps, cfg.num_inputs)).astype(np.float32)
+        t = (np.tanh(x @ w1.T) @ w2.T).astype(np.float32)
+        case.update(x=x, t=t, passes=2, cfg=cfg,
+                    desc={"workload": f"dynamic sparse training: {cfg.num_inputs} inputs + {cfg.hidden} tanh + "
+                                      f"{cfg.num_outputs} linear outputs, 2^20 live edges of 2^21, MSE vs a "
+                                      f"64-256-8 teacher, SGD lr {cfg.lr}; every {cfg.every} steps the {cfg.k} "
+                                      f"lowest-|w| edges pruned and {cfg.k} regrown from {cfg.proposals} "
+                                      f"|grad*act|-scored proposals per unit",
+                          "propagation": "pipeline", "parallelism": "replicas"},
+                    bytes_per_slot={"forward": 13, "backward": 13, "update": 17})
+        if dev is not None:
+            net, static, state = C.build_dst(cfg, dev)
+            step = make_step(net, static, device=dev)
+    elif kind in ("mlp", "mlp50"):
+        cfg = C.C2 if kind == "mlp" else dataclasses_replace(C.C2, density=0.5)
+        xs, ts = zip(*(C.mlp_batch(cfg, g) for _ in range(min(steps, 16))))
+        reps = -(-steps // len(xs))
+        case.update(x=np.stack(xs * reps)[:steps], t=np.stack(ts * reps)[:steps], passes=2, batch=cfg.batch,
+                    desc={"workload": f"sparse MLP 784-1000-1000-10 at density {cfg.density} (batch {cfg.batch}, "
+                                      f"N(0,1) images, uniform one-hot labels), ReLU, softmax cross-entropy, SGD "
+                                      f"lr {cfg.lr}, exact batch-mean update",
+                          "propagation": "topological", "parallelism": "replicas", "global_batch": cfg.batch},
+                    bytes_per_slot={"forward": 13, "backward": 13, "update": 17})
+        case["cfg"] = cfg
+        if dev is not None:
+            net, static, state = C.build_mlp(cfg, dev)
+            step = make_step(net, static, batch_size=cfg.batch, device=dev)
+    elif kind == "units":
+        cfg = C.C4
+        x = g.standard_normal((steps, cfg.num_inputs)).astype(np.float32)
+        t = np.stack([x[i] @ C.units_target_map(cfg, i // cfg.resample) for i in range(steps)])[:, None]
+        case.update(x=x, t=t.astype(np.float32), passes=2,
+                    desc={"workload": f"unit lifecycle: {cfg.live_units} live of {cfg.unit_capacity} unit slots, "
+                                      f"edge capacity 2^{cfg.edge_capacity_log2}, ReLU, UPGD, a utility trace, "
+                                      f"every {cfg.interval} steps one spawn and the 1st-percentile units pruned, "
+                                      f"{cfg.proposals} deeper proposals per unit",
+                          "propagation": "topological", "parallelism": "replicas"},
+                    bytes_per_slot={"forward": 13, "backward": 13, "update": 17 + 16})
+        if dev is not None:
+            from plastax_b200 import Driver
+
+            net, static, state = C.build_units(cfg, dev)
+            step = Driver(net, static, state, device=dev)
+    else:
+        raise ValueError(kind)
+    if dev is not None:
+        case.update(net=net, static=static, state=state, step=step)
+    return case
+
+
+def dataclasses_replace(obj, **kw):
+    import dataclasses
+
+    return dataclasses.replace(obj, **kw)
+
+
+def _edge_pass_timers():
+    """CUDA-event timers around every edge-pass kernel the training steps
+    launch (the canonical and batched sweeps and updates)."""
+    import plastax_b200.kernels as K
+
+    names = ("forward_accumulate", "forward_prune", "backward_accumulate", "backward_update", "batched_forward",
+             "batched_backward", "batched_update")
+    timers = {}
+    for nm in names:
+        t = _EventTimer(getattr(K, nm))
+        t.on = False
+        setattr(K, nm, t)
+        timers[nm] = t
+    return timers
+
+
+def training_arm(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = _env_int("WORLD_SIZE", 1)
+    rank = _env_int("RANK", 0)
+    local = _env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from plastax_b200 import Driver, StepInputs
+
+    W, Kst = max(args.warmup, 3), args.steps
+    timers = _edge_pass_timers()
+    case = training_case(args.config, dev, W + 2 * Kst + 16)
+    step, state = case["step"], case["state"]
+    X = torch.from_numpy(case["x"]).to(dev)
+    T = torch.from_numpy(case["t"]).to(dev)
+    driver = isinstance(step, Driver)
+
+    def run(i, x, t):
+        if driver:
+            step.step(StepInputs(x, t))
+            return step.last_loss
+        return step(state, StepInputs(x, t)).loss
+
+    for i in range(W):
+        run(i, X[i], T[i])
+    torch.cuda.synchronize()
+    # the edge passes' device time, CUDA events on the launching stream, over
+    # eager steps (a graph replay hides per-kernel boundaries)
+    for t in timers.values():
+        t.on = True
+    n_eager = min(Kst, 20)
+    for i in range(n_eager):
+        run(W + i, X[W + i], T[W + i])
+    torch.cuda.synchronize()
+    for t in timers.values():
+        t.on = False
+    use_graph = (not driver) and hasattr(step, "capturable") and step.capturable()
+    if use_graph:
+        step.capture(state, StepInputs(X[0], T[0]))
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    for i in range(Kst):
+        run(W + i, X[W + i], T[W + i])
+    t1.record()
+    torch.cuda.synchronize()
+    clocks.pause()
+    elapsed_ms = t0.elapsed_time(t1)
+    # e2e: each step's inputs and targets from pinned host memory, the loss
+    # read back every step
+    hx = torch.from_numpy(case["x"][W + Kst:W + 2 * Kst]).pin_memory()
+    ht = torch.from_numpy(case["t"][W + Kst:W + 2 * Kst]).pin_memory()
+    back = torch.zeros(1, dtype=torch.float32).pin_memory()
+    if world > 1:
+        dist.barrier()
+    clocks.resume()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(Kst):
+        loss = run(i, hx[i].to(dev, non_blocking=True), ht[i].to(dev, non_blocking=True))
+        back.copy_(loss.reshape(1), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    if world > 1:
+        tt = torch.tensor([elapsed_ms, e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed_ms, e2e_ms = float(tt[0]), float(tt[1])
+    st = case["state"] if not driver else step.state
+    live = sum(int((b["dead"] == 0).sum()) for b in st.conns)
+    caps = sum(int(b["dead"].numel()) for b in st.conns)
+    batch = case.get("batch", 1)
+    per_step = live * case["passes"] * batch
+    value = world * per_step * Kst / (elapsed_ms / 1e3)
+    e2e = world * per_step * Kst / (e2e_ms / 1e3)
+    # the edge passes' roofline: algorithmic bytes over every slot of the
+    # swept buckets (the reference's passes read capacity), per pass kind
+    bps = case["bytes_per_slot"]
+    pass_bytes = {"forward_accumulate": bps.get("forward", 13), "forward_prune": bps.get("forward", 13),
+                  "backward_accumulate": bps.get("backward", 13), "backward_update": bps.get("update", 17),
+                  "batched_forward": bps.get("forward", 13), "batched_backward": bps.get("backward", 13),
+                  "batched_update": bps.get("update", 17)}
+    ms_total, bytes_total, launches = 0.0, 0, 0
+    for nm, t in timers.items():
+        ms = t.ms()
+        if not ms:
+            continue
+        ms_total += float(np.sum(ms))
+        launches += len(ms)
+    # bytes per eager step: every bucket swept once per pass kind present
+    kinds = [nm for nm, t in timers.items() if t.events]
+    for nm in kinds:
+        bytes_total += pass_bytes[nm] * caps * n_eager
+    achieved = bytes_total / (ms_total / 1e3) / 1e9 if ms_total else float("nan")
+    peak, peak_kind = measured_peak_hbm()
+    roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": None, "kernel": "edge passes (" + ", ".join(kinds) + ")",
+            "alg_bytes_per_step": bytes_total / n_eager, "kernel_ms_per_step": ms_total / n_eager,
+            "share_of_step": (ms_total / n_eager) / (elapsed_ms / Kst), "peak_kind": peak_kind,
+            "arena_slots": caps, "l2_resident": caps * 13 < 126e6}
+    if batch > 1:
+        flops = 3 * 2 * batch * live  # forward, backward and update products per edge per sample
+        tf = flops / ((ms_total / n_eager) / 1e3) / 1e12
+        roof["fp32"] = {"achieved_tflops": tf, "peak_tflops": FP32_NOMINAL_TFLOPS, "peak_kind": "nominal",
+                        "frac": tf / FP32_NOMINAL_TFLOPS, "flops_per_step": flops}
+    line = {
+        "metric": f"propagated edges/sec per step ({case['desc']['workload'].split(':')[0]})",
+        "value": value, "unit": "edges/s", "n_gpus": world, "steps": Kst, "warmup": W,
+        "ms_per_step": elapsed_ms / Kst, "us_per_step": 1e3 * elapsed_ms / Kst, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded network and inputs)",
+        "config": {**case["desc"], "live_edges": live, "edge_passes_per_step": case["passes"] * batch,
+                   "l2": "arena smaller than L2 (126 MB): every pass after the first reads L2"
+                   if roof["l2_resident"] else "arena larger than L2"},
+        "e2e": {"value": e2e, "unit": "edges/s", "h2d_bytes_per_step": int(hx[0].numel() * 4 + ht[0].numel() * 4),
+                "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms / Kst},
+        "roofline": roof, "clocks": clk, "cuda_graph": use_graph,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = training_cpu_baseline(args.config, case, max(1, args.cpu_steps))
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if driver:
+        step.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def training_cpu_baseline(kind: str, case: dict, steps: int) -> dict:
+    """The oracle's step of the same configuration on the host, a bounded
+    sample of steps (median), from the state the engine started from."""
+    import math
+
+    from plastax_b200 import configs as C
+
+    batch = case.get("batch", 1)
+    times = []
+    threads = host_threads()
+    if kind == "esn":
+        from oracle.steps import EsnOracle
+
+        cfg = C.C1
+        src, dst, w = C.esn_edges(cfg)
+        net, static, state = C.build_esn(cfg, "cpu")
+        b = {k: v.numpy().copy() for k, v in state.conns[0].items()}
+        ro = EsnOracle(b, state.units["activation"].numpy().copy(), input_id=0, output_id=cfg.units + 1, lr=cfg.lr)
+        n_steps = max(steps, 200)
+        for i in range(n_steps):
+            t0 = time.perf_counter()
+            ro.step(float(case["x"][i, 0]), float(case["t"][i, 0]))
+            times.append(time.perf_counter() - t0)
+        live, sample, cores = int((b["dead"] == 0).sum()), f"{n_steps} ESN steps of the oracle restatement", 1
+    elif kind == "dst":
+        from oracle.steps import DstOracle
+
+        cfg = case["cfg"]
+        net, static, state = C.build_dst(cfg, "cpu")
+        b = {k: v.numpy().copy() for k, v in state.conns[0].items()}
+        u = {k: v.numpy().copy() for k, v in state.units.items()}
+        ro = DstOracle(b, u["activation"], u["grad_pre_act"], u["level"], int(state.tail_start.item()),
+                       num_inputs=cfg.num_inputs, num_outputs=cfg.num_outputs, lr=cfg.lr, k=cfg.k, every=cfg.every,
+                       proposals=cfg.proposals, seed=cfg.seed, threads=threads)
+        n_steps = max(steps, 25)
+        for i in range(n_steps):
+            t0 = time.perf_counter()
+            ro.step(case["x"][i], case["t"][i])
+            times.append(time.perf_counter() - t0)
+        # the structural step every `every` steps, weighed in at its rate
+        struct = times[0]
+        plain = float(np.median(times[1:]))
+        per = plain + (struct - plain) / cfg.every
+        live = int((b["dead"] == 0).sum())
+        sample = (f"{n_steps} DST steps of the oracle restatement (the forward, backward and update single-threaded, "
+                  f"the structural phase on {threads} threads): median plain step plus the first (structural) "
+                  f"step's excess spread over {cfg.every} steps")
+        line = {"value": live * 2 / per, "unit": "edges/s", "cores": threads, "kind": "port", "sample": sample,
+                "ms_per_step": per * 1e3}
+        return line
+    elif kind in ("mlp", "mlp50"):
+        from oracle.batched import batched_step
+
+        net, static, state_h = C.build_mlp(case["cfg"], "cpu")
+        buckets = [{k: v.numpy().copy() for k, v in bk.items()} for bk in state_h.conns]
+        level = state_h.units["level"].numpy()
+        is_input = np.zeros(level.size, np.uint8)
+        is_input[list(static.input_ids)] = 1
+        n_steps = max(1, min(steps, 3))
+        for i in range(n_steps):
+            t0 = time.perf_counter()
+            batched_step(buckets, level, is_input, static.input_ids, static.output_ids, case["x"][i], case["t"][i],
+                         fwd_act="relu", bwd_act="relu", loss="softmax", opt=dict(kind="sgd", lr=0.01),
+                         out_act="identity")
+            times.append(time.perf_counter() - t0)
+        live = sum(int((bk["dead"] == 0).sum()) for bk in buckets)
+        sample, cores = f"{n_steps} batched steps of the numpy restatement (batch {batch})", 1
+    else:
+        return {"value": None, "unit": "edges/s", "cores": 0, "kind": "port",
+                "sample": "no oracle restatement of the whole unit-lifecycle step is timed"}
+    per = float(np.median(times))
+    return {"value": live * case["passes"] * batch / per, "unit": "edges/s", "cores": cores, "kind": "port",
+            "sample": sample, "ms_per_step": per * 1e3}
+
+
+def training_reference_arm(args) -> None:
+    rank = _env_int("RANK", 0)
+    if rank != 0:
+        return
+    case = training_case(args.config, None, max(args.steps, 200) + 32)
+    base = training_cpu_baseline(args.config, case, max(1, args.cpu_steps))
+    line = {"impl": "reference", "metric": f"propagated edges/sec per step "
+                                           f"({case['desc']['workload'].split(':')[0]})",
+            "value": base["value"], "unit": "edges/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": 0,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded network and inputs)", "config": case["desc"], "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "edges/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     args = parse()
+    if args.config != "reservoir":
+        (training_reference_arm if args.impl == "reference" else training_arm)(args)
+        return
     if args.impl == "reference":
         reference_arm(args)
         return

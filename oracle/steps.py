@@ -142,3 +142,96 @@ class EsnOracle:
         self.seed[self.output_id] = err
         orc.update_conn(self.b, self.seed, self.act, n, dict(kind="sgd", lr=self.lr))
         return float(np.float32(np.float32(0.5) * err * err))
+
+
+class DstOracle:
+    """The dynamic-sparse-training step (PIPELINE, the engine's phase order,
+    src/plastax/phases.py:87-176): inputs scattered; the forward from the
+    previous activations (tanh, the outputs linear); the MSE seed on the
+    outputs; the pipelined backward from the previous step's gradients
+    (grad = (acc + seed) * act'); SGD on every live edge
+    (w -= lr * grad[dst] * act[src]); every `every` steps the k live edges of
+    lowest |w| pruned, then per-unit proposals (P per unit, dst uniform over
+    the non-input units, score |grad[dst] * act[src]|) ranked in the total
+    order, the first k claimed with weight 0 (the pipeline claim).
+
+    `teacher_force(...)` overwrites the float state (weights, activations,
+    gradients) with another implementation's before a structural phase, so
+    the structure can be compared bit for bit while the float sums drift
+    apart within tolerance."""
+
+    def __init__(self, bucket: dict, act: np.ndarray, grad: np.ndarray, level: np.ndarray, tail_start: int, *,
+                 num_inputs: int, num_outputs: int, lr: float, k: int, every: int, proposals: int, seed: int = 0,
+                 threads: int = 1) -> None:
+        self.b, self.act, self.grad, self.level = bucket, act, grad, level
+        self.n = act.size
+        self.tail = int(tail_start)
+        self.num_inputs, self.num_outputs = num_inputs, num_outputs
+        self.out = np.arange(self.n - num_outputs, self.n)
+        self.lr, self.k, self.every, self.P, self.seed_ = lr, k, every, proposals, seed
+        self.threads = threads
+        self.is_input = np.zeros(self.n, np.uint8)
+        self.is_input[:num_inputs] = 1
+        self.seed = np.zeros(self.n, np.float32)
+        self.step_count = 0
+        self.last_counts = np.zeros(4, np.int32)
+        self.last_pruned = 0
+
+    def forward_phase(self, x: np.ndarray, t: np.ndarray) -> float:
+        n, b = self.n, self.b
+        self.act[: self.num_inputs] = x
+        acc = np.zeros(n, np.float32)
+        orc.forward_accumulate(b, self.act, n, "sum", acc)
+        new = self.act.copy()
+        orc.unit_apply(n, 0, "tanh", "sum", acc.copy(), None, None, None, 0, self.is_input, None, new)
+        new[self.out] = acc[self.out]
+        self.act[:] = new
+        diff = (self.act[self.out] - np.asarray(t, np.float32)).astype(np.float32)
+        self.seed[:] = 0
+        self.seed[self.out] = diff
+        loss = np.float32(0)
+        for d in diff:
+            loss = np.float32(loss + np.float32(np.float32(0.5) * d) * d)
+        acc = np.zeros(n, np.float32)
+        orc.backward_accumulate(b, self.grad, n, "sum", acc)
+        newg = self.grad.copy()
+        orc.unit_apply(n, 1, "tanh", "sum", acc.copy(), self.act, self.seed, None, 0, self.is_input, None, newg)
+        newg[self.out] = (acc[self.out] + self.seed[self.out]).astype(np.float32)
+        self.grad[:] = newg
+        orc.update_conn(b, self.grad, self.act, n, dict(kind="sgd", lr=self.lr))
+        return float(loss)
+
+    def fires(self) -> bool:
+        return self.step_count % self.every == 0
+
+    def teacher_force(self, weight: np.ndarray, act: np.ndarray, grad: np.ndarray) -> None:
+        self.b["weight"][:] = weight
+        self.act[:] = act
+        self.grad[:] = grad
+
+    def structural_phase(self) -> None:
+        n, b = self.n, self.b
+        self.last_pruned = orc.lowest_prune(b, self.k, self.threads)
+        src, dst, score = orc.propose_per_unit(n, self.P, self.seed_, self.step_count, self.num_inputs,
+                                               n - self.num_inputs, 2, self.level, grad=self.grad, act=self.act,
+                                               max_level_gap=1, threads=self.threads)
+        perm = orc.total_order(score, src, dst, threads=self.threads)
+        win = orc.select_step(perm, src, self.level, self.k)
+        cs, cd = src[win].copy(), dst[win].copy()
+        cw = np.zeros(cs.size, np.float32)
+        grow = np.isfinite(score[win]).astype(np.uint8)
+        if win.size < self.k:
+            pad = self.k - win.size
+            cs = np.concatenate([cs, np.zeros(pad, np.int32)])
+            cd = np.concatenate([cd, np.zeros(pad, np.int32)])
+            cw = np.concatenate([cw, np.zeros(pad, np.float32)])
+            grow = np.concatenate([grow, np.zeros(pad, np.uint8)])
+        self.last_counts, _, self.tail = orc.claim_pipeline(b, self.level, self.tail, cs, cd, cw, grow,
+                                                            threads=self.threads)
+
+    def step(self, x: np.ndarray, t: np.ndarray) -> float:
+        loss = self.forward_phase(x, t)
+        if self.fires():
+            self.structural_phase()
+        self.step_count += 1
+        return loss
