@@ -341,8 +341,10 @@ PXB_API int pxb_total_order(int64_t n, const float *score, const int32_t *src,
  * is a 16 MiB array inside this library, held on every GPU that loads it
  * until the process exits. At most 262,144 candidates; larger n is
  * rejected with PXB_EINVAL. The first call on a device looks the array up
- * (call it once before any stream capture); all calls share the array, so
- * calls that overlap on the GPU race. No counterpart in the reference. */
+ * (call it once before any stream capture) and keeps its address for the
+ * life of the process, so it is not valid after a reset of that device;
+ * all calls share the array, so calls that overlap on the GPU race. No
+ * counterpart in the reference. */
 PXB_API int pxb_total_order_noalloc(int64_t n, const float *score,
                                     const int32_t *src, const int32_t *dst,
                                     int32_t id_bound, int32_t *perm_out,

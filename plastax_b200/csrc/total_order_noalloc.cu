@@ -18,7 +18,11 @@
 // keeps the last call's contents; nothing in it needs to start at zero (the
 // keys are written before they are read and CUB initialises its own
 // temporary storage). Calls that overlap on the GPU (two streams, or two
-// host threads on one device) race on the array: serialise them.
+// host threads on one device) race on the array: serialise them. The cached
+// address belongs to the device's context as it was at the first call: after
+// cudaDeviceReset (or anything else that replaces the primary context) it no
+// longer names the array, so a process that resets a device must not call
+// this entry point on that device again.
 #include <mutex>
 
 #include "pxb_common.cuh"

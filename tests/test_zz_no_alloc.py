@@ -61,6 +61,25 @@ def test_noalloc_total_order_matches_scratch_version_twice(cuda, m, id_bound):
     assert outs[0].shape == outs[1].shape
 
 
+def test_noalloc_smaller_call_after_a_larger_one(cuda):
+    """Calls of different sizes and id bounds in a row: a small call after
+    the largest one (the array then holds the larger call's keys and CUB
+    state past the new n), then the largest again, each equal to the
+    scratch-taking version."""
+    import torch
+
+    from plastax_b200 import kernels
+
+    rng = np.random.default_rng(7)
+    for m, id_bound in [(MAX_N, 1_048_592), (3_000, 50), (100_000, 65_536), (MAX_N, 1_048_592), (17, 3)]:
+        score, src, dst = _inputs(rng, m, id_bound)
+        t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+        s_d, a_d, b_d = t(score), t(src), t(dst)
+        ref = kernels.total_order(s_d, a_d, b_d, id_bound).cpu().numpy()
+        got = _noalloc(s_d, a_d, b_d, id_bound, torch.empty(m, dtype=torch.int32, device=cuda))
+        np.testing.assert_array_equal(got, ref, err_msg=f"m={m} id_bound={id_bound}")
+
+
 def test_noalloc_rejects_more_than_its_array_holds(cuda):
     import torch
 
