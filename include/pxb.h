@@ -198,8 +198,13 @@ PXB_API int pxb_backward_update(int64_t cap, const int32_t *from_id,
 
 /* Fractional bits of the exact fixed-point sum accumulators (int64, units
  * of 2^-PXB_FIXED_FRAC_BITS) that pxb_mirror_forward fills and
- * pxb_unit_apply reads. */
-#define PXB_FIXED_FRAC_BITS 28
+ * pxb_unit_apply reads. With the mirror's 31-bit sum a product of
+ * magnitude >= 2^-7 adds exactly and a smaller one is rounded, an error of
+ * at most 2^-32 each (a destination with F in-edges sums within F * 2^-32 of
+ * the exact sum of its float32 products before the one final rounding:
+ * under 1e-6 for F <= 4294); with its 28-bit sum, >= 2^-4 exact and at most
+ * 2^-29 each (under 1e-6 for F <= 536). */
+#define PXB_FIXED_FRAC_BITS 31
 
 /* Activation codes of the apply entry points: the low byte is a
  * PXB_ACT_* kind; a non-zero second byte, kind + 1, is the kind of the
@@ -796,6 +801,11 @@ typedef struct pxb_mirror {
   int32_t *defer_count;
   int64_t defer_seg;
   int32_t defer_ctas;
+  int32_t sum_frac_bits; /* the sweep's shared-memory sum: 28 fractional bits
+                            (each product below 2^-4 rounded to 2^-28, an error
+                            of at most 2^-29; the words rarely wrap) or any
+                            other value for 31 (below 2^-7 to 2^-31, at most
+                            2^-32); acc_fixed is in 2^-31 units either way */
 } pxb_mirror;
 
 /* Forward accumulate of the mirrored bucket (w * act[src] combined per

@@ -41,7 +41,7 @@ CLAIM_LEVEL_MAJOR = 0x100
 LOSS_MSE, LOSS_SOFTMAX_CE = 0, 1
 MIRROR_TILE = 2048
 PEER_MAX_LEVELS = 8
-FIXED_FRAC_BITS = 28
+FIXED_FRAC_BITS = 31
 PAIR_ABS_PRODUCT, PAIR_PRODUCT, PAIR_MODULAR, PAIR_MODULAR_PREDICATE = 0, 1, 2, 3
 UNIT_UPDATE_AFFINE, UNIT_UPDATE_TRACE_ABS, UNIT_UPDATE_TRACE = 0, 1, 2
 SPAWN_FIELD_AT_LEAST, SPAWN_ARGMAX = 0, 1
@@ -67,6 +67,7 @@ class Mirror(ctypes.Structure):
         ("item_group", c_ptr), ("ovf_cap", c_i64), ("ovf_count", c_ptr), ("ovf_src", c_ptr), ("ovf_dst", c_ptr),
         ("ovf_slot", c_ptr), ("ovf_weight", c_ptr), ("status", c_ptr), ("ins_count", c_ptr),
         ("defer_pos", c_ptr), ("defer_count", c_ptr), ("defer_seg", c_i64), ("defer_ctas", c_i32),
+        ("sum_frac_bits", c_i32),
     ]
 
 

@@ -24,55 +24,67 @@ namespace pxb {
 
 // The sum is accumulated exactly in fixed point, independent of order. A
 // chunk's shared accumulator is two 32-bit words per unit: lo in units of
-// 2^-28 and hi in units of 1.0 (2^28 lo units); shared-memory integer
+// 2^-F and hi in units of 1.0 (2^F lo units), F = 28 or 31 fractional bits
+// (the mirror's choice, by its largest in-degree); shared-memory integer
 // atomics are native, where a float add is a compare-and-swap loop at a
 // third of the rate. A product of magnitude < 1 is rounded to the nearest
-// unit (exact when >= 2^-4) and added to lo; the adding thread sees a signed
-// wrap of lo exactly, from the value its atomic returns, and carries +-16 (2^32
-// units) into hi. A product in [1, 2^20) is a multiple of 2^-23, so its
-// fixed value is exact: the part above 2^28 units goes to hi, the rest to
-// lo. A product that is not finite or >= 2^20 goes to the float side
-// accumulator. The flush adds hi * 2^28 + lo to the unit's int64 global
-// accumulator; one rounding to float happens in the unit apply.
-constexpr int kFixBits = PXB_FIXED_FRAC_BITS;
-constexpr float kFixScale = 268435456.0f;  // 2^kFixBits
-static_assert(kFixBits == 28, "kFixScale and the carry below assume 28 fractional bits");
+// unit (exact when its 24-bit mantissa ends at or above 2^-F, i.e. when it is
+// >= 2^(23-F); an error of at most 2^-(F+1) below) and added to lo; the
+// adding thread sees a signed wrap of lo exactly, from the value its atomic
+// returns, and carries 2^(32-F) (2^32 units) into hi. With F = 28 the word
+// holds +-8 and wraps rarely; with F = 31 it holds +-1 and wraps (a carry)
+// more often, for an error bound 8x tighter. A product in [1, 2^20) is a
+// multiple of 2^-23, so its fixed value is exact: the part above 2^F units
+// goes to hi, the rest to lo. A product that is not finite or >= 2^20 goes
+// to the float side accumulator. The flush adds (hi * 2^F + lo) * 2^(31-F)
+// to the unit's int64 global accumulator, always in units of
+// 2^-PXB_FIXED_FRAC_BITS; one rounding to float happens in the unit apply.
+constexpr int kFixBits = PXB_FIXED_FRAC_BITS;  // the global accumulator's unit
+static_assert(kFixBits == 31, "the flush's shift and fix_scale assume a global unit of 2^-31");
 
+template <int F>
+__device__ __forceinline__ float fix_scale() {
+  return F == 31 ? 2147483648.0f : 268435456.0f;
+}
+
+template <int F>
 __device__ __forceinline__ void lo_add(int32_t *lo, int32_t *hi, int32_t v) {
   const int32_t old = atomicAdd(lo, v);
   const int32_t now = static_cast<int32_t>(static_cast<uint32_t>(old) + static_cast<uint32_t>(v));
-  if (((old ^ now) & (v ^ now)) < 0) atomicAdd(hi, v > 0 ? 16 : -16);
+  constexpr int32_t carry = 1 << (32 - F);  // 2^32 lo units, in units of 1.0
+  if (((old ^ now) & (v ^ now)) < 0) atomicAdd(hi, v > 0 ? carry : -carry);
 }
 
+template <int F>
 __device__ __forceinline__ void fixed_add(int32_t *lo, int32_t *hi, float *gf, float p) {
   const float ap = fabsf(p);
   if (ap < 1.0f) {
-    lo_add(lo, hi, __float2int_rn(p * kFixScale));
+    lo_add<F>(lo, hi, __float2int_rn(p * fix_scale<F>()));
   } else if (ap < 1048576.0f) {
-    const long long v = __float2ll_rn(p * kFixScale);
-    atomicAdd(hi, static_cast<int32_t>(v >> kFixBits));
-    lo_add(lo, hi, static_cast<int32_t>(v & ((1ll << kFixBits) - 1)));
+    const long long v = __float2ll_rn(p * fix_scale<F>());
+    atomicAdd(hi, static_cast<int32_t>(v >> F));
+    lo_add<F>(lo, hi, static_cast<int32_t>(v & ((1ll << F) - 1)));
   } else {
     atomicAdd(gf, p);
   }
 }
 
 // The same contribution straight into the global accumulators (the
-// overflow list's edges).
+// overflow list's edges), in their unit of 2^-31.
 __device__ __forceinline__ void fixed_add_global(int64_t *af, float *gf, float p) {
   if (fabsf(p) < 1048576.0f) {
     atomicAdd(reinterpret_cast<unsigned long long *>(af),
-              static_cast<unsigned long long>(__float2ll_rn(p * kFixScale)));
+              static_cast<unsigned long long>(__float2ll_rn(p * fix_scale<kFixBits>())));
   } else {
     atomicAdd(gf, p);
   }
 }
 
-template <int MONOID>
+template <int MONOID, int F>
 __device__ __forceinline__ void smem_combine(float *acc_s, int chunk, float *acc_g, uint32_t dl, float v) {
   if (MONOID == PXB_MONOID_SUM) {
     int32_t *lo = reinterpret_cast<int32_t *>(acc_s);
-    fixed_add(lo + dl, lo + chunk + dl, acc_g + dl, v);
+    fixed_add<F>(lo + dl, lo + chunk + dl, acc_g + dl, v);
   } else if (MONOID == PXB_MONOID_MAX) {
     atomic_max_f32(acc_s + dl, v);
   } else {
@@ -210,7 +222,7 @@ __device__ __forceinline__ void prune_entry(const MirrorK &m, const MPrune &p, i
   empty_entry(m, pos, g, gb);
 }
 
-template <int MONOID, int PK>
+template <int MONOID, int PK, int F>
 __device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, const LowkCut &cut,
                                            const float *__restrict__ act, const uint32_t *word_t, const float *w_t,
                                            int used, float *acc_s, float *acc_g, int32_t g, int64_t gb, int64_t e0,
@@ -259,17 +271,18 @@ __device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, co
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t dl = ws[j] & mask;
-          lo_add(lo + dl, lo + chunk + dl, __float2int_rn(pv[j] * kFixScale));
+          lo_add<F>(lo + dl, lo + chunk + dl, __float2int_rn(pv[j] * fix_scale<F>()));
         }
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          if (ws[j] != kEmpty) fixed_add(lo + (ws[j] & mask), lo + chunk + (ws[j] & mask), acc_g + (ws[j] & mask), pv[j]);
+          if (ws[j] != kEmpty)
+            fixed_add<F>(lo + (ws[j] & mask), lo + chunk + (ws[j] & mask), acc_g + (ws[j] & mask), pv[j]);
       }
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (ws[j] != kEmpty) smem_combine<MONOID>(acc_s, chunk, acc_g, ws[j] & mask, __fmul_rn(fs[j], av[j]));
+        if (ws[j] != kEmpty) smem_combine<MONOID, F>(acc_s, chunk, acc_g, ws[j] & mask, __fmul_rn(fs[j], av[j]));
     }
     if (PK != PXB_PRUNE_NONE) {
       // the predicate is rare: one test of the smallest |w| (fminf drops a
@@ -320,7 +333,7 @@ __device__ __forceinline__ void sweep_tile(const MirrorK &m, const MPrune &p, co
 
 // Flush (unless g < 0) and reset the chunk accumulators; each consumer thread
 // flushes and resets the same indices, so one barrier before and one after.
-template <int MONOID>
+template <int MONOID, int F>
 __device__ __forceinline__ void flush_reset(const MirrorK &m, float *acc_s, float *__restrict__ acc,
                                             int64_t *__restrict__ acc_fixed, int64_t g) {
   const int chunk = 1 << m.cb;
@@ -335,7 +348,7 @@ __device__ __forceinline__ void flush_reset(const MirrorK &m, float *acc_s, floa
         const int32_t ls[4] = {l.x, l.y, l.z, l.w}, hs[4] = {h.x, h.y, h.z, h.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const long long tot = (static_cast<long long>(hs[j]) << kFixBits) + ls[j];
+          const long long tot = ((static_cast<long long>(hs[j]) << F) + ls[j]) * (1ll << (kFixBits - F));
           if (tot != 0 && base + 4 * u + j < m.n)
             atomicAdd(reinterpret_cast<unsigned long long *>(acc_fixed + base + 4 * u + j),
                       static_cast<unsigned long long>(tot));
@@ -361,7 +374,7 @@ __device__ __forceinline__ void flush_reset(const MirrorK &m, float *acc_s, floa
   }
 }
 
-template <int MONOID, int PK>
+template <int MONOID, int PK, int F>
 __global__ void __launch_bounds__(kSweepThreads, PXB_SWEEP_MIN_CTAS) mirror_sweep_kernel(MirrorK m, const float *__restrict__ act,
                                                                         float *__restrict__ acc,
                                                                         int64_t *__restrict__ acc_fixed, MPrune p) {
@@ -446,14 +459,14 @@ __global__ void __launch_bounds__(kSweepThreads, PXB_SWEEP_MIN_CTAS) mirror_swee
     const int64_t g = c.g;
     if (g != cur) {
       consumer_sync();
-      flush_reset<MONOID>(m, acc_s, acc, acc_fixed, cur);
+      flush_reset<MONOID, F>(m, acc_s, acc, acc_fixed, cur);
       consumer_sync();
       cur = g;
     }
     const int s = static_cast<int>(i % kStages);
     if (ok && !mbar_wait(full + s, (i / kStages) & 1)) ok = false;
     if (ok)
-      sweep_tile<MONOID, PK>(m, p, cut, act, word_s + s * kTile, w_s + s * kTile, used, acc_s,
+      sweep_tile<MONOID, PK, F>(m, p, cut, act, word_s + s * kTile, w_s + s * kTile, used, acc_s,
                              acc + (static_cast<int64_t>(g) << m.cb), static_cast<int32_t>(g), c.base, t * kTile,
                              pruned_here, defer ? &s_defer : nullptr, seg);
     __syncwarp();
@@ -463,7 +476,7 @@ __global__ void __launch_bounds__(kSweepThreads, PXB_SWEEP_MIN_CTAS) mirror_swee
   }
   if (cur >= 0) {
     consumer_sync();
-    flush_reset<MONOID>(m, acc_s, acc, acc_fixed, cur);
+    flush_reset<MONOID, F>(m, acc_s, acc, acc_fixed, cur);
   }
   if (defer) {
     consumer_sync();  // every consumer's deferred prunes are listed
@@ -732,7 +745,8 @@ static int mirror_forward_launch(const MirrorK &m, const float *act, int32_t mon
     const int64_t tiles = m.entries / kTile;
 #define PXB_MS(M, P)                                                                              \
   do {                                                                                            \
-    auto fn = mirror_sweep_kernel<M, P>;                                                          \
+    auto fn = (M == PXB_MONOID_SUM && m.sum_frac == 28) ? mirror_sweep_kernel<M, P, 28>           \
+                                                        : mirror_sweep_kernel<M, P, 31>;          \
     PXB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));   \
     int per_sm = 0;                                                                               \
     PXB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem));          \

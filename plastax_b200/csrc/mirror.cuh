@@ -31,6 +31,7 @@ struct MirrorK {
   int32_t *defer_count;
   int64_t defer_total;
   int32_t defer_ctas;
+  int32_t sum_frac;  // fractional bits of the sweep's shared sum words: 28 or 31
 };
 
 inline MirrorK to_k(const pxb_mirror *m) {
@@ -62,6 +63,7 @@ inline MirrorK to_k(const pxb_mirror *m) {
   k.defer_count = defer ? m->defer_count : nullptr;
   k.defer_total = defer ? m->defer_seg * m->defer_ctas : 0;
   k.defer_ctas = defer ? m->defer_ctas : 0;
+  k.sum_frac = m->sum_frac_bits == 28 ? 28 : 31;
   return k;
 }
 

@@ -66,7 +66,7 @@ __device__ bool wait_row(const uint32_t *row, int world, uint32_t epoch, uint32_
   return true;
 }
 
-constexpr float kFixUnitP = 1.0f / float(1 << PXB_FIXED_FRAC_BITS);
+constexpr float kFixUnitP = 1.0f / float(1ll << PXB_FIXED_FRAC_BITS);
 constexpr int kPeerMaxLevels = PXB_PEER_MAX_LEVELS;
 
 __global__ void __launch_bounds__(256) scheme_a_apply_kernel(PeerK g, int32_t n, int32_t act_kind,

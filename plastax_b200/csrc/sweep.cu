@@ -316,7 +316,7 @@ __global__ void unit_apply_kernel(int32_t n, int mode, int act_kind, int monoid,
     // of two), plus the float side (non-finite or huge products, normally 0)
     const long long f = acc_fixed[i];
     if (f != 0) {
-      a = __fadd_rn(__fmul_rn(__ll2float_rn(f), 1.0f / float(1 << PXB_FIXED_FRAC_BITS)), a);
+      a = __fadd_rn(__fmul_rn(__ll2float_rn(f), 1.0f / float(1ll << PXB_FIXED_FRAC_BITS)), a);
       acc_fixed[i] = 0;
     }
   }

@@ -21,10 +21,16 @@ import torch
 from plastax_b200 import _lib
 
 
+# the largest in-degree at which a mirror sums with 28 fractional bits: the
+# rounding error of a destination is then at most 400 * 2^-29 = 7.5e-7
+# (under 1e-6 with room for the in-degrees churn adds after the build)
+FAST_SUM_FAN_IN = 400
+
+
 class Mirror:
     def __init__(self, bucket: dict[str, torch.Tensor], num_units: int, *, slack: float = 0.05,
                  min_slack: int = 64, item_entries: int = 1 << 16, ovf_cap: int = 1 << 20,
-                 chunk_bits: int | None = None) -> None:
+                 chunk_bits: int | None = None, sum_frac_bits: int | None = None) -> None:
         dev = bucket["dead"].device
         n = int(num_units)
         src_bits = max(1, (n - 1).bit_length())
@@ -46,6 +52,8 @@ class Mirror:
         order = torch.sort(g, stable=True).indices  # group, then slot order
         live, f, t, g = live[order], f[order], t[order], g[order]
         counts = torch.bincount(g, minlength=groups)
+        # the largest in-degree: the fixed-point sum's error bound grows with it
+        self.max_in_degree = int(torch.bincount(t, minlength=n).max().item()) if t.numel() else 0
         counts_h = counts.cpu().numpy().astype(np.int64)
         spare = np.maximum(min_slack, np.ceil(counts_h * slack).astype(np.int64))
         tile = _lib.MIRROR_TILE
@@ -98,13 +106,21 @@ class Mirror:
         self.defer_seg = max(256, entries // 256 // self.defer_ctas)
         self.defer_pos = torch.empty(self.defer_ctas * self.defer_seg, dtype=torch.int64, device=dev)
         self.defer_count = torch.zeros(self.defer_ctas, dtype=torch.int32, device=dev)
+        # the sweep's fixed-point sum: 28 fractional bits while every unit's
+        # in-degree leaves room for growth under the 1e-6 bound (F * 2^-29),
+        # else 31 (F * 2^-32); 28 bits wrap the 32-bit words far less often
+        if sum_frac_bits is None:
+            sum_frac_bits = 28 if self.max_in_degree <= FAST_SUM_FAN_IN else 31
+        if sum_frac_bits not in (28, 31):
+            raise ValueError(f"mirror: sum_frac_bits must be 28 or 31, got {sum_frac_bits}")
+        self.sum_frac_bits = int(sum_frac_bits)
         p = lambda x: x.data_ptr()  # noqa: E731
         self.struct = _lib.Mirror(
             n, cb, groups, entries, p(self.gbase), p(self.gfill), p(self.word), p(self.weight), p(self.slot),
             p(self.hstack), p(self.hcount), len(ib), p(self.item_begin), p(self.item_end), p(self.item_group),
             self.ovf_cap, p(self.ovf_count), p(self.ovf_src), p(self.ovf_dst), p(self.ovf_slot), p(self.ovf_weight),
             p(self.status), p(self.ins_count), p(self.defer_pos), p(self.defer_count), self.defer_seg,
-            self.defer_ctas)
+            self.defer_ctas, self.sum_frac_bits)
 
     def healthy(self) -> bool:
         """False when an edge could not be mirrored (host read; synchronises)."""

@@ -50,6 +50,12 @@ from plastax_b200.traits import (
 from plastax_b200.types import ACTIVATION, LEVEL, PRUNED, Propagation
 
 
+# the largest in-degree for which the mirror's fixed-point sum stays within
+# 1e-6 of the exact sum of its float32 products in every case (each product
+# below 2^-7 is rounded to 2^-31, an error of at most 2^-32)
+FIXED_EXACT_FAN_IN = int(1e-6 * 2 ** 32)
+
+
 @dataclasses.dataclass(frozen=True)
 class StepInputs:
     """Clamped inputs + targets for one step (src/plastax/phases.py:68-83).
@@ -215,6 +221,14 @@ class StepFn:
         if self.use_mirror:
             self.mirrors = [Mirror(b, st.num_units, chunk_bits=self.mirror_chunk_bits, slack=self.mirror_slack,
                                    min_slack=self.mirror_min_slack) for b in state.conns]
+            fan = max(m.max_in_degree for m in self.mirrors)
+            if self.acc_fixed is not None and fan > FIXED_EXACT_FAN_IN:
+                import warnings
+
+                warnings.warn(f"a unit has {fan} in-edges: the mirror's fixed-point sum rounds each product below "
+                              f"2^-7 to 2^-31, so its error bound ({fan} * 2^-32) exceeds 1e-6; the sum is still "
+                              f"independent of order but may differ from the correctly rounded sum by more",
+                              stacklevel=2)
         if self.peer_reduce:
             from plastax_b200.peers import PeerGroup
 

@@ -461,7 +461,7 @@ def _canonical_multiset(hb):
 
 
 def _fixed_total(kern, acc, acc_fixed):
-    """acc_fixed * 2^-28 + acc rounded once, through the unit apply."""
+    """acc_fixed * 2^-31 + acc rounded once, through the unit apply."""
     import torch
 
     out = torch.empty_like(acc)
@@ -562,9 +562,11 @@ def test_mirror_tracks_claims(cuda, slack, ovf):
     assert m.healthy()
 
 
-def test_mirror_sum_is_exact_fixed_point(cuda):
+@pytest.mark.parametrize("frac", [28, 31])
+def test_mirror_sum_is_exact_fixed_point(cuda, frac):
     """The mirror's sum equals the int64 sum of every float32 product rounded
-    (half to even) to 2^-28, bit for bit, whatever the atomic order: large
+    (half to even) to 2^-frac (in the accumulator's 2^-31 units), bit for bit,
+    whatever the atomic order, with either of the sweep's fractions: large
     products (|p| >= 1), partials far beyond the 32-bit word's +-8 range (the
     carry into the high word), tiny products (rounded), one non-finite
     product (the float side), and two sweeps that must agree exactly."""
@@ -585,11 +587,11 @@ def test_mirror_sum_is_exact_fixed_point(cuda):
     act[b["from_id"][7]] = np.float32(2.0)
     db = to_device(b, cuda)
     t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
-    m = Mirror(db, n)
+    m = Mirror(db, n, sum_frac_bits=frac)
     live = b["dead"] == 0
     p = (b["weight"][live] * act[b["from_id"][live]]).astype(np.float32)
     big = np.abs(p) >= np.float32(2.0 ** 20)
-    units = np.rint(p[~big].astype(np.float64) * 2.0 ** 28).astype(np.int64)
+    units = np.rint(p[~big].astype(np.float64) * 2.0 ** frac).astype(np.int64) << (31 - frac)
     want_fixed = np.zeros(n, np.int64)
     np.add.at(want_fixed, b["to_id"][live][~big], units)
     got = []
@@ -602,11 +604,49 @@ def test_mirror_sum_is_exact_fixed_point(cuda):
         np.add.at(side, b["to_id"][live][big], p[big])
         np.testing.assert_array_equal(acc.cpu().numpy(), side)
         got.append(_fixed_total(kern, acc, acc_fixed))
-    assert int((np.abs(want_fixed) > (8 << 28)).sum()) > 0, "no unit exceeded the 32-bit word's range"
+    assert int((np.abs(want_fixed) > (1 << (62 - frac))).sum()) > 0, "no unit exceeded the 32-bit word's range"
     np.testing.assert_array_equal(got[0], got[1])
     # one rounding of the exact sum, then the float side added as a float
-    want = want_fixed.astype(np.float32) * np.float32(2.0 ** -28) + side
+    want = want_fixed.astype(np.float32) * np.float32(2.0 ** -31) + side
     np.testing.assert_array_equal(got[0], want)
+
+
+def test_mirror_sum_of_thousands_of_small_products(cuda):
+    """One destination takes 4,608 in-edges whose products all lie below 2^-7
+    (so the fixed-point sum rounds every one of them), each 3/4 of a 2^-31 unit,
+    so every rounding goes the same way (a quarter unit up); another takes
+    4,096 random small products of both signs. The mirror of such a fan-in
+    sums with 31 fractional bits, and both sums stay within 1e-5 relative /
+    1e-6 absolute of the oracle's correctly rounded sum (the rounding error is
+    at most in-degree * 2^-32: 9.5e-7 for 4,096 in-edges)."""
+    import torch
+
+    from plastax_b200.mirror import Mirror
+
+    kern = _k()
+    rng = np.random.default_rng(29)
+    n, per = 4000, 4096
+    cap = 2 * per + 512 + 20_000
+    src = rng.integers(0, n, cap).astype(np.int32)
+    dst = np.concatenate([np.full(per + 512, 5), np.full(per, 9), rng.integers(0, n, 20_000)]).astype(np.int32)
+    act = np.ones(n, np.float32)
+    w = np.empty(cap, np.float32)
+    w[:per + 512] = np.float32(3 * 2.0 ** -34)  # 0.75 units of 2^-31: rounds up by 2^-33 every time
+    w[per + 512:2 * per + 512] = (rng.standard_normal(per) * 2.0 ** -9).astype(np.float32)
+    w[2 * per + 512:] = (rng.standard_normal(20_000) * 0.05).astype(np.float32)
+    b = {"from_id": src, "to_id": dst, "dead": np.zeros(cap, np.uint8), "weight": w}
+    db = to_device(b, cuda)
+    t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    m = Mirror(db, n)
+    assert m.max_in_degree >= per and m.sum_frac_bits == 31  # the high fan-in takes the 31-bit sum
+    acc = torch.zeros(n, dtype=torch.float32, device=cuda)
+    acc_fixed = torch.zeros(n, dtype=torch.int64, device=cuda)
+    kern.mirror_forward(m, t(act), acc, acc_fixed=acc_fixed)
+    got = _fixed_total(kern, acc, acc_fixed)
+    want = np.zeros(n, np.float32)
+    orc.forward_accumulate(b, act, n, "sum", want)
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-6)
+    assert abs(float(got[5]) - float(want[5])) > 0, "the first destination's products must be rounded"
 
 
 @pytest.mark.parametrize("n,k,levels,kind,opts", [

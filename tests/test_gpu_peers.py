@@ -33,7 +33,7 @@ def test_peer_wait_gives_up_and_reports(cuda):
     side = [torch.zeros(n, dtype=torch.float32, device=cuda) for _ in range(world)]
     act = [torch.full((n,), 7.0, dtype=torch.float32, device=cuda) for _ in range(world)]
     flags = [torch.zeros(2 * world, dtype=torch.int32, device=cuda) for _ in range(world)]
-    fixed[0][5] = 3 << 28
+    fixed[0][5] = 3 << 31
     arr = lambda ts: torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device=cuda)  # noqa: E731
     p_fixed, p_side, p_act, p_flags = arr(fixed), arr(side), arr(act), arr(flags)
     words = torch.zeros(4, dtype=torch.int32, device=cuda)
