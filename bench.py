@@ -85,6 +85,9 @@ def parse() -> argparse.Namespace:
                          "capped at 13 (11 for the full-size reservoir)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--phase-times", action="store_true",
+                    help="add the step's main-stream phases (CUDA events over the eager steps; the phase ends at "
+                         "the named boundary) to the line: rank 0's and the max over ranks")
     ap.add_argument("--kernel-breakdown", action="store_true",
                     help="after the timing, print (stderr, rank 0) every kernel's device time per step over five "
                          "graph replays, from the profiler's activity records")
@@ -375,9 +378,13 @@ def engine_arm(args) -> None:
     ins_t = _EventTimer(K.mirror_insert)
     K.mirror_insert = ins_t
     n_eager = min(Kst, 10)
+    if args.phase_times:
+        step.phase_marks = []
     for i in range(n_eager):
         step(state, StepInputs(inputs_dev[W + i]))
     torch.cuda.synchronize()
+    phases = step.phase_times() if args.phase_times else None
+    step.phase_marks = None
     sweep_t.on = ins_t.on = False
     if sel_t is not None:
         sel_t.on = False
@@ -495,6 +502,14 @@ def engine_arm(args) -> None:
         "cuda_graph": use_graph,
         "gpu_launches": launches_per_step * Kst,
     }
+    if phases is not None:
+        names = sorted(phases)
+        vec = torch.tensor([phases[n] for n in names], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(vec, op=dist.ReduceOp.MAX)
+        line["phases_ms"] = {"rank0": phases, "max_over_ranks": dict(zip(names, vec.tolist(), strict=True)),
+                             "note": "eager steps (launch gaps included), main stream; each phase ends at its "
+                                     "named boundary"}
     if args.kernel_breakdown:
         kernel_breakdown(step, state, inputs_dev[0], rank)
     # a CUDA graph holding NCCL calls must be released before the process

@@ -856,8 +856,43 @@ __global__ void __launch_bounds__(1024) fs_threshold_bin_kernel(FsGeom g, const 
     }
 }
 
-// The full bins: each (level, bin) pair ranked and emitted at its final
-// position.
+// The full bins of at most kFsWarpCap members, one warp per (level, bin)
+// pair: the bin's keys in the warp's shared memory, each lane ranking a
+// quarter of them against all (broadcast reads), then emitting them at their
+// final position. Eight bins are in flight per CTA (a CTA per bin would
+// take them one after another, each a chain of loads and barriers).
+constexpr int kFsWarpCap = 512;
+constexpr int kFsWarps = kFsThreads / 32;
+__global__ void __launch_bounds__(kFsThreads) fs_bins_warp_kernel(FsGeom g, InitArgs ia, FsScratch o,
+                                                                  int32_t *s_out, int32_t *d_out, float *w_out,
+                                                                  uint8_t *grow_out) {
+  __shared__ uint64_t keys_s[kFsWarps][kFsWarpCap];
+  const FsInfo *info = o.info;
+  const int32_t tb = info->tb < g.nb ? info->tb : g.nb;
+  const int64_t pairs = static_cast<int64_t>(g.L) * tb;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t *ks = keys_s[w];
+  for (int64_t q = static_cast<int64_t>(blockIdx.x) * kFsWarps + w; q < pairs;
+       q += static_cast<int64_t>(gridDim.x) * kFsWarps) {
+    const int32_t l = static_cast<int32_t>(q / tb), b = static_cast<int32_t>(q % tb);
+    const int32_t m = static_cast<int32_t>(o.hist[l * g.nb + b]);
+    if (m == 0 || m > kFsWarpCap) continue;  // larger bins: fs_bins_kernel
+    const uint32_t t0 = o.toff[l * g.nb + b];
+    for (int e = lane; e < m; e += 32) ks[e] = o.bk[t0 + e];
+    __syncwarp();
+    const int64_t base = static_cast<int64_t>(info->F[l]) + (t0 - info->T[l]);
+    for (int e = lane; e < m; e += 32) {
+      const uint64_t ke = ks[e];
+      int32_t r = 0;
+      for (int f = 0; f < m; ++f) r += ks[f] < ke ? 1 : 0;
+      fs_emit(g, o, ia, ke, o.bi[t0 + e], base + r, s_out, d_out, w_out, grow_out);
+    }
+    __syncwarp();
+  }
+}
+
+// The full bins larger than a warp's share, each (level, bin) pair ranked
+// by a CTA and emitted at its final position.
 __global__ void __launch_bounds__(kFsThreads) fs_bins_kernel(FsGeom g, InitArgs ia, FsScratch o, int32_t *s_out,
                                                              int32_t *d_out, float *w_out, uint8_t *grow_out,
                                                              int32_t *rank_scratch, int32_t *status) {
@@ -868,7 +903,7 @@ __global__ void __launch_bounds__(kFsThreads) fs_bins_kernel(FsGeom g, InitArgs 
   for (int64_t q = blockIdx.x; q < pairs; q += gridDim.x) {
     const int32_t l = static_cast<int32_t>(q / tb), b = static_cast<int32_t>(q % tb);
     const int32_t m = static_cast<int32_t>(o.hist[l * g.nb + b]);
-    if (m == 0) continue;
+    if (m <= kFsWarpCap) continue;  // fs_bins_warp_kernel's
     const uint32_t t0 = o.toff[l * g.nb + b];
     int32_t *rank = rank_scratch + t0;
     if (!fs_rank(o.bk + t0, m, keys_s, rank)) {
@@ -1216,7 +1251,10 @@ extern "C" int pxb_propose_select_unique(int32_t num_units, uint64_t network_see
   PXB_LAUNCHED("fs_scatter_kernel");
   fs_threshold_bin_kernel<<<1, 1024, 0, st>>>(g, level, ia, o, src_out, dst_out, weight_out, growable_out, status);
   PXB_LAUNCHED("fs_threshold_bin_kernel");
-  fs_bins_kernel<<<sm_count() * 8, kFsThreads, 0, st>>>(g, ia, o, src_out, dst_out, weight_out, growable_out,
+  fs_bins_warp_kernel<<<sm_count() * 8, kFsThreads, 0, st>>>(g, ia, o, src_out, dst_out, weight_out,
+                                                               growable_out);
+  PXB_LAUNCHED("fs_bins_warp_kernel");
+  fs_bins_kernel<<<sm_count() * 2, kFsThreads, 0, st>>>(g, ia, o, src_out, dst_out, weight_out, growable_out,
                                                         o.bi + (g.k > 0 ? g.k : 1), status);
   PXB_LAUNCHED("fs_bins_kernel");
   return PXB_OK;

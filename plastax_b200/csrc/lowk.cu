@@ -232,8 +232,9 @@ __device__ __forceinline__ const uint64_t *keys_of(const SelectArgs &a, int q) {
   return a.world == 1 ? a.my_key : a.peer_key[q];
 }
 
-// The select's keys staged in shared memory when every rank's list fits.
-constexpr int kStageKeys = 12288;  // 96 KB
+// The select's keys and claim domains staged in shared memory when every
+// rank's list fits.
+constexpr int kStageKeys = 12288;  // 96 KB of keys + 48 KB of domains
 constexpr int kDigitBits = 10;
 constexpr int kDigits = 1 << kDigitBits;
 static_assert(kDigits == kSelectThreads, "one select thread per digit value");
@@ -252,26 +253,33 @@ __global__ void __launch_bounds__(kSelectThreads) lowk_select_kernel(SelectArgs 
   __shared__ int s_want;
   __shared__ int s_sel[kMaxWorld * kMaxLevels];
   __shared__ int s_pruned;
+  __shared__ long long s_below[kMaxWorld];
   extern __shared__ unsigned long long s_keys[];
+  int32_t *s_levels = reinterpret_cast<int32_t *>(s_keys + kStageKeys);
   const int t = threadIdx.x;
   const int parity = a.plan->parity;
   const long long take = a.plan->take;
   const int64_t base = static_cast<int64_t>(parity) * a.cap;
+  // every rank's counters read at once (one thread per rank: remote loads
+  // one after another would each take a full NVLink round trip)
+  if (t < a.world) {
+    const unsigned long long *cnt = a.world == 1 ? a.my_count : a.peer_count[t];
+    s_n[t] = static_cast<int64_t>(cnt[2 * parity]);
+    s_below[t] = static_cast<long long>(cnt[2 * parity + 1]);
+  }
+  __syncthreads();
   if (t == 0) {
     long long listed = 0, below = 0;
     int status = 0;
     s_off[0] = 0;
     for (int q = 0; q < a.world; ++q) {
-      const unsigned long long *cnt = a.world == 1 ? a.my_count : a.peer_count[q];
-      unsigned long long n = cnt[2 * parity];
-      if (n > static_cast<unsigned long long>(a.cap)) {
+      if (s_n[q] > a.cap) {
         status |= 1;
-        n = static_cast<unsigned long long>(a.cap);
+        s_n[q] = a.cap;
       }
-      s_n[q] = static_cast<int64_t>(n);
-      s_off[q + 1] = s_off[q] + static_cast<int64_t>(n);
-      listed += static_cast<long long>(n);
-      below += static_cast<long long>(cnt[2 * parity + 1]);
+      s_off[q + 1] = s_off[q] + s_n[q];
+      listed += s_n[q];
+      below += s_below[q];
     }
     if (listed != a.plan->listed_expect || below != a.plan->below_expect) status |= 2;
     if (status) atomicOr(&a.plan->status, status);
@@ -286,10 +294,17 @@ __global__ void __launch_bounds__(kSelectThreads) lowk_select_kernel(SelectArgs 
   }
   const bool staged = listed_total <= kStageKeys;
   if (staged) {
-    for (int q = 0; q < a.world; ++q) {
-      const uint64_t *keys = keys_of(a, q) + base;
-      for (int64_t i = t; i < s_n[q]; i += kSelectThreads) s_keys[s_off[q] + i] = keys[i];
+    // one flattened pass over every rank's list: each thread's loads are
+    // independent of one another, so they are in flight together
+    const int32_t *levels0 = a.world == 1 ? a.my_level : nullptr;
+    for (int64_t j = t; j < listed_total; j += kSelectThreads) {
+      int q = 0;
+      while (j >= s_off[q + 1]) ++q;
+      const int64_t i = j - s_off[q];
+      s_keys[j] = keys_of(a, q)[base + i];
+      s_levels[j] = (levels0 != nullptr ? levels0 : a.peer_level[q])[base + i];
     }
+    __syncthreads();
   }
   unsigned long long kstar = ~0ull;  // take >= every listed key: all of them
   if (take < listed_total) {
@@ -358,7 +373,7 @@ __global__ void __launch_bounds__(kSelectThreads) lowk_select_kernel(SelectArgs 
       for (int64_t i = t; i < s_n[q]; i += kSelectThreads) {
         const unsigned long long key = staged ? s_keys[s_off[q] + i] : keys[i];
         if (key > kstar) continue;
-        const int l = lv[base + i];
+        const int l = staged ? s_levels[s_off[q] + i] : lv[base + i];
         if (l >= 0 && l < a.num_levels) atomicAdd(&s_sel[q * kMaxLevels + l], 1);
       }
     }
@@ -500,7 +515,7 @@ extern "C" int pxb_lowk_select(const pxb_lowk *lowk, const pxb_mirror *mirror, u
   a.num_levels = num_levels;
   a.level_before = level_before;
   a.level_totals = level_totals;
-  const size_t smem = kStageKeys * sizeof(unsigned long long);
+  const size_t smem = kStageKeys * (sizeof(unsigned long long) + sizeof(int32_t));
   PXB_CUDA(cudaFuncSetAttribute(lowk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   lowk_select_kernel<<<1, kSelectThreads, smem, as_stream(stream)>>>(a, to_k(mirror));
   PXB_LAUNCHED("lowk_select_kernel");

@@ -135,6 +135,9 @@ class StepFn:
             and net.update_conn is None
         self.lowk = None
         self._lowk_fired = False
+        # CUDA events at the phase boundaries of eager steps, when a caller
+        # sets a list here (a profiling aid: `phase_times()` reads them)
+        self.phase_marks: list | None = None
         self.fuse_update = (not self.pipeline and net.update_conn is not None and net.backward_pass is not None
                             and net.update_unit is None)
         self.opt = net.update_conn.struct() if net.update_conn is not None else None
@@ -263,6 +266,27 @@ class StepFn:
         self.step_dev.fill_(state.step)
         self._ahead_ready = False
         self._bound = id(state)
+
+    def _mark(self, name: str) -> None:
+        if self.phase_marks is not None and self.graph is None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.phase_marks.append((name, ev))
+
+    def phase_times(self) -> dict[str, float]:
+        """Mean milliseconds of each phase over the marked eager steps (the
+        span from the previous mark to the named one; synchronises), and
+        clears the marks."""
+        marks, self.phase_marks = self.phase_marks or [], []
+        torch.cuda.synchronize(self.dev)
+        tot: dict[str, float] = {}
+        cnt: dict[str, int] = {}
+        for (_, a), (name, b) in zip(marks, marks[1:]):
+            if name == "start":
+                continue
+            tot[name] = tot.get(name, 0.0) + a.elapsed_time(b)
+            cnt[name] = cnt.get(name, 0) + 1
+        return {k: tot[k] / cnt[k] for k in tot}
 
     def _lowk_list_cap(self) -> int:
         pc = self.net.prune_conn
@@ -632,6 +656,7 @@ class StepFn:
                 from plastax_b200.peers import scheme_a_apply
 
                 self._accumulate_bucket(state, 0, act, self.acc, self.acc_fixed)
+                self._mark("sweep")
                 # with the prune in the sweep nothing touches the arena before
                 # the claim: its per-domain free counts are final here and ride
                 # on the combine's barrier instead of an all-gather
@@ -646,15 +671,19 @@ class StepFn:
                     counts = ws.level_counts
                 scheme_a_apply(self.peers, self.fwd_act, is_input=self.is_input, pruned=pruned,
                                level_counts=counts, level_before=self.level_before, level_totals=self.level_totals)
+                self._mark("combine")
                 self.launches += 3
                 if self._lowk_fired:
                     # every rank's sweep is complete: select the threshold
                     # bin's edges, adding every rank's to the barrier's counts
                     self._lowk_select(state, adjust=self._counts_on_barrier)
+                    self._mark("select")
                 return
             self._forward_bucket(state, 0, act)
+            self._mark("sweep")
             K.unit_apply(self.acc, act, mode=0, act_kind=self.fwd_act, monoid=self.fwd_monoid,
                          is_input=self.is_input, pruned=pruned, acc_fixed=self.acc_fixed)
+            self._mark("apply")
             self.launches += 3
             return
         level = units[LEVEL.name]
@@ -1060,13 +1089,16 @@ class StepFn:
                            global_cap=st.level_capacities[bk], level_before=before, level_totals=totals,
                            extra=self.extra_defaults, free_bitmap=bm, placed=self.placed,
                            committed=self.committed if self.lowk is not None else None)
+            self._mark("claim")
             if self.lowk is not None:
                 # the committed edges enter the prune's histogram (every rank
                 # adds every rank's: the histogram is the whole arena's)
                 self.lowk.hist_add(cw, self.committed, ws.counts, tally=fresh)
                 self.launches += 1
+                self._mark("hist_add")
             if self.use_mirror:
                 K.mirror_insert(self.mirrors[bk], cs, cd, cw, self.placed)
+                self._mark("insert")
             K.growth_flags(ws.counts, reset=fresh and bi == 0, grown=self.grown, overflow=self.overflow,
                            needs_resort=state.needs_resort)
             self.launches += 12
@@ -1134,6 +1166,7 @@ class StepFn:
         and the side stream selects the next step's while the passes, the
         claim and the insert run (it joins at the end of the step)."""
         main = torch.cuda.current_stream(self.dev)
+        self._mark("start")
         if not self._ahead_ready:  # the first step of a bound state selects its own
             self._select(state, out=self.claim_next, step_dev=self.step_dev)
             self._ahead_ready = True
@@ -1144,6 +1177,7 @@ class StepFn:
         with torch.cuda.stream(self.side):
             self._select(state, out=self.claim_next, step_dev=self.sel_step_dev)
         self._scatter_inputs(state, inputs)
+        self._mark("inputs")
         self._forward(state)
         self._loss(state, inputs)
         self._backward(state)
@@ -1152,7 +1186,9 @@ class StepFn:
         self._prune(state)
         remainder = self._add_conn(state, selected=True)
         self.step_dev += 1
+        self._mark("flags")
         main.wait_stream(self.side)
+        self._mark("side_join")
         return remainder
 
     def capturable(self) -> bool:
