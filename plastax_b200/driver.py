@@ -215,9 +215,11 @@ class Driver:
         self._loop_key = None
 
     def _check_mirrors(self) -> None:
-        """Rebuild the step's mirrors when one lost an edge (its inserts found
-        no room): the canonical arena stays complete, so a rebuild restores
-        the sweep's input exactly."""
+        """Read every device status word of the step (raising PxbError for a
+        fault: a bulk copy or peer wait that gave up, a selection bin or
+        prune list that overflowed) and rebuild the step's mirrors when one
+        lost an edge (its inserts found no room): the canonical arena stays
+        complete, so a rebuild restores the sweep's input exactly."""
         fn = self._step
         if isinstance(fn, StepFn) and not fn.mirrors_healthy():
             self._drop_loop()
@@ -283,6 +285,7 @@ class Driver:
         if self._since_check < self._check_every:
             return
         self._since_check = 0
+        self._check_mirrors()
         if bool(self._overflowed.item()):
             self._overflowed.zero_()
             ac = self._net.add_conn

@@ -173,6 +173,27 @@ def test_list_overflow_raises(cuda):
         step.check_status()
 
 
+@pytest.mark.parametrize("check_every", [1, 3])
+def test_driver_raises_on_a_status_word(cuda, check_every):
+    """The Driver reads the step's status words on its checks (every step,
+    or every check_every-th) and raises instead of stepping on."""
+    import plastax_b200 as px
+
+    rng = np.random.default_rng(2)
+    n, e = 1000, 20_000
+    src, dst = rng.integers(0, n, e), rng.integers(4, n, e)
+    w = np.full(e, 0.25, np.float32)
+    Net = _net(100, list_capacity=64)
+    static, state = px.NetworkBuilder.from_edges(Net, n, src, dst, weights=w, input_ids=(0, 1, 2, 3),
+                                                 output_ids=(), device=cuda)
+    drv = px.Driver(Net, static, state, check_every=check_every, device=cuda)
+    x = px.StepInputs(np.zeros(4, np.float32))
+    with pytest.raises(px.PxbError, match="list capacity"):
+        for _ in range(check_every):
+            drv.step(x)
+    drv.close()
+
+
 def test_firing_every_third_step(cuda):
     import torch
 
