@@ -734,6 +734,12 @@ PXB_API int pxb_free_bitmap_build(int32_t mode, int64_t cap, const int32_t *from
                           int64_t shard_base, const int64_t *tail_start,
                           uint32_t *bitmap, void *stream);
 
+/* The end of a step (device values, each may be NULL): *grown = 0 and
+ * *overflow = 0 for a step that claimed nothing (src/plastax/phases.py:
+ * 4953-5132 report zero then), and the device step counter the proposals
+ * read under graph replay advanced by one (src/plastax/step.py:226-229). */
+PXB_API int pxb_step_end(int32_t *step, int32_t *grown, uint8_t *overflow, void *stream);
+
 /* The step's growth flags from a claim's counts_out (device): grown (+)=
  * counts[0], overflow |= counts[1] > 0, needs_resort |= counts[3] > 0; with
  * reset != 0 grown and overflow start from 0 (the step's first bucket).
@@ -1012,6 +1018,61 @@ PXB_API int pxb_scheme_a_apply(const pxb_peer_group *group, int32_t num_units,
                                const int32_t *level_counts, int32_t num_levels,
                                int32_t *level_before, int32_t *level_totals,
                                uint32_t wait_polls, void *stream);
+
+/* ------------------------------------------------------------------ */
+/* The fused pipeline training step                                     */
+/* ------------------------------------------------------------------ */
+/* One PIPELINE step of a single-device net whose forward and backward sum
+ * over one bucket, as three kernels: (1) one pass over the arena
+ * accumulating both the forward (into destinations, from the previous
+ * activations) and the backward (into sources, from the previous
+ * gradients) in exact fixed point in shared memory, each CTA holding
+ * every unit's two accumulators; a thread-block cluster reduces its CTAs'
+ * accumulators through distributed shared memory into one int64 row per
+ * cluster; (2) per unit: the rows summed (exact) and rounded once, the
+ * forward apply (inputs and pruned units kept), the MSE seed of the outputs
+ * (act - target), the backward apply (every unit but the pruned, inputs
+ * included), and the loss summed in output order by the last CTA; (3) one
+ * pass over the arena applying the optimizer to every live edge with the
+ * edge gradient update_grad[dst] * act[src] (the new columns).
+ * Replaces, for such nets, src/plastax/sweep.py:300-340 (forward sweep),
+ * :402-450 (backward sweep), src/plastax/phases.py:488-532 (update_conn) and
+ * the MSE seed of scripts/parity/reference.py:338-352, in the order of
+ * src/plastax/step.py:45-237. Every value equals the unfused passes' within
+ * the fixed-point sum's bound (each product rounded to 2^-32 at most). */
+typedef struct pxb_pipeline_train {
+  int64_t cap;                 /* the bucket */
+  const int32_t *from_id, *to_id;
+  const uint8_t *dead;
+  float *weight;
+  float *opt_m, *opt_v, *opt_t; /* optimizer columns (NULL where unused) */
+  int32_t num_units;
+  float *act;          /* in: previous activations, inputs scattered; out: new */
+  float *grad;         /* in: previous gradients; out: new (NULL: no backward) */
+  float *seed;         /* the loss seed column (NULL: no loss) */
+  const uint8_t *roles;    /* 1 input, 2 output (own activation), 0 hidden */
+  const uint8_t *pruned;   /* or NULL */
+  int32_t fwd_act, bwd_act; /* PXB_ACT_CODE codes; bwd_act ignored without grad */
+  int32_t num_outputs;
+  const int32_t *target_of; /* [num_units]: output index of a unit, -1 if none */
+  const int32_t *output_ids; /* [num_outputs], the loss's summation order */
+  const float *target;       /* [num_outputs], device (NULL: no loss) */
+  float *loss;               /* device scalar, or NULL */
+  float *update_grad;        /* the column the edge gradient reads at dst */
+  pxb_optimizer opt;         /* any kind but PXB_OPT_UPGD */
+  void *scratch;             /* pxb_pipeline_train_scratch_bytes(num_units) */
+  const int64_t *tail_start; /* device: slots at or past it are never live (a
+                                PIPELINE arena's tail), so neither pass reads
+                                them; NULL: the whole capacity */
+} pxb_pipeline_train;
+
+/* The largest num_units the step takes (every CTA holds every unit's
+ * accumulators in shared memory), with or without a backward. */
+PXB_API int32_t pxb_pipeline_train_max_units(int32_t with_backward);
+/* Device scratch the step needs (*bytes); zero it once before the first
+ * call (the step leaves it zeroed where it must be). */
+PXB_API int pxb_pipeline_train_scratch_bytes(int32_t num_units, size_t *bytes);
+PXB_API int pxb_pipeline_train_step(const pxb_pipeline_train *t, void *stream);
 
 #ifdef __cplusplus
 }

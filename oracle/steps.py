@@ -195,7 +195,9 @@ class DstOracle:
         acc = np.zeros(n, np.float32)
         orc.backward_accumulate(b, self.grad, n, "sum", acc)
         newg = self.grad.copy()
-        orc.unit_apply(n, 1, "tanh", "sum", acc.copy(), self.act, self.seed, None, 0, self.is_input, None, newg)
+        # every unit, inputs included (src/plastax/sweep.py:402-450); the
+        # linear outputs' derivative is 1
+        orc.unit_apply(n, 1, "tanh", "sum", acc.copy(), self.act, self.seed, None, 0, None, None, newg)
         newg[self.out] = (acc[self.out] + self.seed[self.out]).astype(np.float32)
         self.grad[:] = newg
         orc.update_conn(b, self.grad, self.act, n, dict(kind="sgd", lr=self.lr))

@@ -142,6 +142,39 @@ class Optimizer(ctypes.Structure):
     ]
 
 
+class PipelineTrain(ctypes.Structure):
+    """`pxb_pipeline_train`: the fused pipeline training step's bucket, unit
+    columns, loss and optimizer."""
+
+    _fields_ = [
+        ("cap", c_i64),
+        ("from_id", c_ptr),
+        ("to_id", c_ptr),
+        ("dead", c_ptr),
+        ("weight", c_ptr),
+        ("opt_m", c_ptr),
+        ("opt_v", c_ptr),
+        ("opt_t", c_ptr),
+        ("num_units", c_i32),
+        ("act", c_ptr),
+        ("grad", c_ptr),
+        ("seed", c_ptr),
+        ("roles", c_ptr),
+        ("pruned", c_ptr),
+        ("fwd_act", c_i32),
+        ("bwd_act", c_i32),
+        ("num_outputs", c_i32),
+        ("target_of", c_ptr),
+        ("output_ids", c_ptr),
+        ("target", c_ptr),
+        ("loss", c_ptr),
+        ("update_grad", c_ptr),
+        ("opt", Optimizer),
+        ("scratch", c_ptr),
+        ("tail_start", c_ptr),
+    ]
+
+
 # name -> (restype, argtypes); every int-returning entry point is checked.
 _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_abi_version": (c_i32, []),
@@ -229,6 +262,7 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_mirror_forward_lowk": (c_i32, [c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr]),
     "pxb_lowk_select": (c_i32, [c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_i32, c_ptr, c_ptr, c_ptr]),
     "pxb_lowk_hist_add": (c_i32, [c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
+    "pxb_step_end": (c_i32, [c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_growth_flags": (c_i32, [c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_peer_alloc": (c_i32, [c_size, ctypes.POINTER(c_ptr), c_ptr]),
     "pxb_peer_open": (c_i32, [c_ptr, ctypes.POINTER(c_ptr)]),
@@ -257,6 +291,9 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_kill_unit_edges": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_unit_add": (c_i32, [c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_unit_importance": (c_i32, [c_i32, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr]),
+    "pxb_pipeline_train_max_units": (c_i32, [c_i32]),
+    "pxb_pipeline_train_scratch_bytes": (c_i32, [c_i32, ctypes.POINTER(c_size)]),
+    "pxb_pipeline_train_step": (c_i32, [c_ptr, c_ptr]),
     "pxb_propose_grid": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_i32, c_i32,
                                  c_i32, c_i32, c_ptr, c_ptr, c_ptr, c_ptr]),
 }

@@ -157,8 +157,9 @@ class BatchedStepFn:
             K.batch_mean(self.seed_b, units[loss.seed_field.name])
         # structural phases once, on the reduced state
         self._prune(state)
+        inner._clear_flags = False
         remainder = inner._add_conn(state)
-        inner.step_dev += 1
+        inner._step_end()
         state.step += 1
         grown = state.grown if state.grown is not None else torch.zeros((), dtype=torch.int32, device=self.dev)
         overflow = state.overflow if state.overflow is not None else torch.zeros((), dtype=torch.bool,

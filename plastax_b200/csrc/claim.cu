@@ -522,9 +522,24 @@ __global__ void growth_flags_kernel(const int32_t *__restrict__ counts, int32_t 
   if (needs_resort) *needs_resort = static_cast<uint8_t>(*needs_resort | (counts[3] > 0 ? 1 : 0));
 }
 
+// The end of a step: the growth flags of a step that claimed nothing
+// cleared (when given) and the device step counter advanced, in one launch.
+__global__ void step_end_kernel(int32_t *step, int32_t *grown, uint8_t *overflow) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  if (grown) *grown = 0;
+  if (overflow) *overflow = 0;
+  if (step) *step += 1;
+}
+
 }  // namespace pxb
 
 using namespace pxb;
+
+extern "C" int pxb_step_end(int32_t *step, int32_t *grown, uint8_t *overflow, void *stream) {
+  step_end_kernel<<<1, 32, 0, as_stream(stream)>>>(step, grown, overflow);
+  PXB_LAUNCHED("step_end_kernel");
+  return PXB_OK;
+}
 
 extern "C" int pxb_growth_flags(const int32_t *counts, int32_t reset, int32_t *grown, uint8_t *overflow,
                                 uint8_t *needs_resort, void *stream) {

@@ -18,6 +18,7 @@
 // - the claim's placed edges are inserted by pxb_mirror_insert: a hole of
 //   the destination's group if one is left, else the group's never-used
 //   slack, else an overflow list that the forward sweeps with atomics.
+#include "fixed.cuh"
 #include "mirror.cuh"
 
 namespace pxb {
@@ -41,33 +42,6 @@ namespace pxb {
 // 2^-PXB_FIXED_FRAC_BITS; one rounding to float happens in the unit apply.
 constexpr int kFixBits = PXB_FIXED_FRAC_BITS;  // the global accumulator's unit
 static_assert(kFixBits == 31, "the flush's shift and fix_scale assume a global unit of 2^-31");
-
-template <int F>
-__device__ __forceinline__ float fix_scale() {
-  return F == 31 ? 2147483648.0f : 268435456.0f;
-}
-
-template <int F>
-__device__ __forceinline__ void lo_add(int32_t *lo, int32_t *hi, int32_t v) {
-  const int32_t old = atomicAdd(lo, v);
-  const int32_t now = static_cast<int32_t>(static_cast<uint32_t>(old) + static_cast<uint32_t>(v));
-  constexpr int32_t carry = 1 << (32 - F);  // 2^32 lo units, in units of 1.0
-  if (((old ^ now) & (v ^ now)) < 0) atomicAdd(hi, v > 0 ? carry : -carry);
-}
-
-template <int F>
-__device__ __forceinline__ void fixed_add(int32_t *lo, int32_t *hi, float *gf, float p) {
-  const float ap = fabsf(p);
-  if (ap < 1.0f) {
-    lo_add<F>(lo, hi, __float2int_rn(p * fix_scale<F>()));
-  } else if (ap < 1048576.0f) {
-    const long long v = __float2ll_rn(p * fix_scale<F>());
-    atomicAdd(hi, static_cast<int32_t>(v >> F));
-    lo_add<F>(lo, hi, static_cast<int32_t>(v & ((1ll << F) - 1)));
-  } else {
-    atomicAdd(gf, p);
-  }
-}
 
 // The same contribution straight into the global accumulators (the
 // overflow list's edges), in their unit of 2^-31.

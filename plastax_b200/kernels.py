@@ -165,6 +165,18 @@ def unit_apply(acc: torch.Tensor, out: torch.Tensor, *, mode: int, act_kind: str
          ctypes.c_int32(target_level), ptr(is_input), ptr(pruned), ptr(out), _stream())
 
 
+def step_end(step: torch.Tensor, grown: torch.Tensor | None = None, overflow: torch.Tensor | None = None) -> None:
+    """Clear the growth flags (when given) and advance the device step
+    counter, one launch."""
+    call("pxb_step_end", ptr(step), ptr(grown), ptr(overflow), _stream())
+
+
+def pipeline_train(desc: _lib.PipelineTrain) -> None:
+    """The fused pipeline training step (forward + backward accumulation,
+    applies and seed, update) over the descriptor's bucket."""
+    call("pxb_pipeline_train_step", ctypes.byref(desc), _stream())
+
+
 def mse_loss(output_ids: torch.Tensor, act: torch.Tensor, target: torch.Tensor, seed: torch.Tensor,
              loss_out: torch.Tensor | None) -> None:
     call("pxb_mse_loss", ctypes.c_int32(output_ids.numel()), ptr(output_ids), ptr(act), ptr(target), ptr(seed),

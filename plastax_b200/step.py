@@ -26,6 +26,7 @@ before every apply, and the claim all-gathers the per-domain free counts.
 
 from __future__ import annotations
 
+import ctypes
 import dataclasses
 import os
 from typing import Any
@@ -98,7 +99,7 @@ class StepFn:
     """A built step: preallocated buffers plus the phase sequence."""
 
     def __init__(self, net: type[Network], static: NetworkStatic, device: torch.device,
-                 fuse_prune: bool = True) -> None:
+                 fuse_prune: bool = True, fuse_train: bool = True) -> None:
         self.net, self.static, self.dev = net, static, device
         n = static.num_units
         fp = net.forward_pass
@@ -121,6 +122,11 @@ class StepFn:
             is_input[list(static.output_ids)] = 2
         is_input[list(static.input_ids)] = 1
         self.is_input = torch.from_numpy(is_input).to(device)
+        # the pipeline backward applies to every unit, inputs included
+        # (src/plastax/sweep.py:402-450), so its roles mark only the outputs
+        self.bwd_roles = None
+        if out_bwd is not None:
+            self.bwd_roles = torch.from_numpy(np.where(is_input == 1, 0, is_input).astype(np.uint8)).to(device)
         self.loss_buf = torch.zeros(1, dtype=torch.float32, device=device)
         self.loss_b1 = torch.zeros(1, dtype=torch.float32, device=device)
         self.sharded = static.sharding is not None and static.num_shards > 1
@@ -179,6 +185,12 @@ class StepFn:
         self._bound: int | None = None
         self.step_dev = torch.zeros(1, dtype=torch.int32, device=device)
         self.graph = None  # a captured CUDA graph of the step body (see capture)
+        # with auto_graphs, steps whose work depends on periodic phases replay
+        # one captured graph per signature (see _replay_or_capture)
+        self.auto_graphs = False
+        self._graphs: dict = {}
+        self._sig_seen: dict = {}
+        self._clear_flags = False  # the step claimed nothing: its end clears grown / overflow
         self.side = None
         self.unit_lifecycle = net.prune_unit is not None or net.add_unit is not None
         if isinstance(net.prune_conn, LowestMagnitudePrune) and self.sharded and not (
@@ -208,7 +220,80 @@ class StepFn:
         if self.ahead:
             self.claim_next = tuple(torch.empty_like(t) for t in self.claim_in)
             self.sel_step_dev = torch.zeros(1, dtype=torch.int32, device=device)
+        self._init_train_fused(fuse_train)
         self.launches = 0
+
+    def _init_train_fused(self, fuse_train: bool) -> None:
+        """Whether a step's propagation and update run as the fused pipeline
+        training step (pxb_pipeline_train_step): a single-device PIPELINE net
+        with one bucket, sum forward and backward, an MSE loss or none, an
+        update_conn other than UPGD and no unit-side phase in between."""
+        net, n = self.net, self.static.num_units
+        uc, bp, loss = net.update_conn, net.backward_pass, net.loss
+        self.train_fused = bool(
+            fuse_train and self.pipeline and not self.sharded and self.num_buckets == 1 and uc is not None
+            and uc.kind != "upgd" and uc.scale_field is None and net.update_unit is None
+            and not self.unit_lifecycle and self.fwd_monoid == "sum"
+            and (bp is None or bp.combine.lowered() == "sum")
+            and (loss is None or isinstance(loss, MSELoss))
+            and (loss is None or bp is None or bp.seed_field.name == loss.seed_field.name)
+            and torch.device(self.dev).type == "cuda"
+            and n <= int(_lib.lib().pxb_pipeline_train_max_units(int(bp is not None))))
+        self.train_desc = None
+        if not self.train_fused:
+            return
+        size = _lib.query_size("pxb_pipeline_train_scratch_bytes", ctypes.c_int32(n))
+        self.train_scratch = torch.zeros(size, dtype=torch.uint8, device=self.dev)
+        target_of = np.full(n, -1, np.int32)
+        target_of[list(self.static.output_ids)] = np.arange(len(self.static.output_ids), dtype=np.int32)
+        self.train_target_of = torch.from_numpy(target_of).to(self.dev)
+
+    def _bind_train(self, state: NetworkState) -> None:
+        """The fused training step's descriptor for `state` (its columns)."""
+        net, units, b = self.net, state.units, state.conns[0]
+        bp, loss, uc = net.backward_pass, net.loss, net.update_conn
+        m, v, t = (b.get(c) for c in self.opt_cols)
+        pruned = units.get(PRUNED.name)
+        d = _lib.PipelineTrain()
+        d.cap = int(b["dead"].numel())
+        d.from_id, d.to_id, d.dead, d.weight = (K.ptr(b[c]) for c in ("from_id", "to_id", "dead", "weight"))
+        d.opt_m, d.opt_v, d.opt_t = K.ptr(m), K.ptr(v), K.ptr(t)
+        d.num_units = self.static.num_units
+        d.act = K.ptr(units[ACTIVATION.name])
+        d.grad = K.ptr(units[bp.grad_field.name]) if bp is not None else None
+        d.seed = K.ptr(units[loss.seed_field.name]) if loss is not None else None
+        d.roles = K.ptr(self.is_input)
+        d.pruned = K.ptr(pruned)
+        d.fwd_act = _lib.act_code(self.fwd_act)
+        d.bwd_act = _lib.act_code(self.bwd_act) if bp is not None else 0
+        d.num_outputs = len(self.static.output_ids)
+        d.target_of = K.ptr(self.train_target_of)
+        d.output_ids = K.ptr(self.output_ids)
+        d.loss = K.ptr(self.loss_buf) if loss is not None else None
+        d.update_grad = K.ptr(units[uc.grad_field.name])
+        d.opt = self.opt
+        d.scratch = K.ptr(self.train_scratch)
+        # a PIPELINE arena's slots past tail_start were never claimed
+        d.tail_start = K.ptr(state.tail_start) if state.tail_start is not None else None
+        self.train_desc = d
+
+    def _train(self, state: NetworkState, inputs: StepInputs) -> None:
+        """Forward, loss, backward and update_conn as the fused pipeline
+        training step (three kernels; the same values as the separate
+        passes, with both sums exact in fixed point)."""
+        d = self.train_desc
+        t = None
+        if self.net.loss is not None:
+            t = inputs.targets
+            if t is None:
+                raise ValueError("a network with a loss needs StepInputs.targets")
+            if not isinstance(t, torch.Tensor):
+                t = torch.from_numpy(np.ascontiguousarray(t, np.float32))
+            t = t.to(self.dev, non_blocking=True).reshape(-1)
+        d.target = K.ptr(t)
+        K.pipeline_train(d)
+        self._mark("train")
+        self.launches += 3
 
     # -- per-state device indices ---------------------------------------------
     def _bind(self, state: NetworkState) -> None:
@@ -263,12 +348,14 @@ class StepFn:
             self.opt = uc.struct(state.units[uc.scale_field.name])
         if self.unit_lifecycle:
             self._bind_units(state)
+        if self.train_fused:
+            self._bind_train(state)
         self.step_dev.fill_(state.step)
         self._ahead_ready = False
         self._bound = id(state)
 
     def _mark(self, name: str) -> None:
-        if self.phase_marks is not None and self.graph is None:
+        if self.phase_marks is not None and self.graph is None and not torch.cuda.is_current_stream_capturing():
             ev = torch.cuda.Event(enable_timing=True)
             ev.record()
             self.phase_marks.append((name, ev))
@@ -727,7 +814,8 @@ class StepFn:
         if self.pipeline:
             K.backward_accumulate(state.conns[0], grad, self.acc, "sum")
             self._combine_partials(self.acc)
-            K.unit_apply(self.acc, grad, mode=1, act_kind=self.bwd_act, act=act, seed=seed, pruned=pruned)
+            K.unit_apply(self.acc, grad, mode=1, act_kind=self.bwd_act, act=act, seed=seed, is_input=self.bwd_roles,
+                         pruned=pruned)
             self.launches += 3
             return
         level = units[LEVEL.name]
@@ -1024,8 +1112,9 @@ class StepFn:
         st = self.static
         level = state.units[LEVEL.name]
         if not self._fires(state) or self.k == 0:
-            self.grown.zero_()
-            self.overflow.zero_()
+            # cleared by the step's end (pxb_step_end), one launch with the
+            # step counter
+            self._clear_flags = True
             state.grown, state.overflow = self.grown, self.overflow
             return None
         if not selected:
@@ -1136,6 +1225,7 @@ class StepFn:
         """The device work of one step (no host synchronisation)."""
         self._level = state.units[LEVEL.name]
         self._lowk_fired = False
+        self._clear_flags = False
         if self.ahead:
             return self._body_ahead(state, inputs)
         # selection that reads nothing the step writes runs on the side
@@ -1146,19 +1236,28 @@ class StepFn:
             with torch.cuda.stream(self.side):
                 self._select(state)
         self._scatter_inputs(state, inputs)
-        self._forward(state)
-        self._loss(state, inputs)
-        self._backward(state)
-        self._update_unit(state)
-        self._update_conn(state)
+        if self.train_fused:
+            self._train(state, inputs)
+        else:
+            self._forward(state)
+            self._loss(state, inputs)
+            self._backward(state)
+            self._update_unit(state)
+            self._update_conn(state)
         self._prune_unit(state)
         self._prune(state)
         self._add_unit(state)
         if early:
             torch.cuda.current_stream(self.dev).wait_stream(self.side)
         remainder = self._add_conn(state, selected=early)
-        self.step_dev += 1
+        self._step_end()
         return remainder
+
+    def _step_end(self) -> None:
+        clear = self._clear_flags
+        self._clear_flags = False
+        K.step_end(self.step_dev, self.grown if clear else None, self.overflow if clear else None)
+        self.launches += 1
 
     def _body_ahead(self, state: NetworkState, inputs: StepInputs) -> GrowthRemainder | None:
         """The step with its selection computed one step earlier: this step's
@@ -1178,14 +1277,17 @@ class StepFn:
             self._select(state, out=self.claim_next, step_dev=self.sel_step_dev)
         self._scatter_inputs(state, inputs)
         self._mark("inputs")
-        self._forward(state)
-        self._loss(state, inputs)
-        self._backward(state)
-        self._update_unit(state)
-        self._update_conn(state)
+        if self.train_fused:
+            self._train(state, inputs)
+        else:
+            self._forward(state)
+            self._loss(state, inputs)
+            self._backward(state)
+            self._update_unit(state)
+            self._update_conn(state)
         self._prune(state)
         remainder = self._add_conn(state, selected=True)
-        self.step_dev += 1
+        self._step_end()
         self._mark("flags")
         main.wait_stream(self.side)
         self._mark("side_join")
@@ -1201,6 +1303,81 @@ class StepFn:
         if isinstance(self.net.prune_conn, LowestMagnitudePrune) and self.net.prune_conn.every > 1:
             return False
         return ac is None or (ac.trigger == "every_step" and interval <= 1 and ac.on_overflow != "error")
+
+    def _signature(self, state: NetworkState) -> tuple[bool, bool, bool]:
+        """Which periodic phases this step runs: (growth on its trigger or
+        interval, add_unit on its interval, a lowest-|w| prune on its
+        period). Steps of one signature run the same device work."""
+        net = self.net
+        interval = int(getattr(net, "structural_interval", 1))
+        unit = net.add_unit is not None and (interval <= 1 or state.step % interval == 0)
+        grow = self.ac is not None and self._fires(state)
+        pc = net.prune_conn
+        low = isinstance(pc, LowestMagnitudePrune) and (pc.every <= 1 or state.step % pc.every == 0)
+        return (grow, unit, low)
+
+    def period(self) -> int:
+        """The least common multiple of the periodic phases' periods: every
+        signature occurs within this many steps."""
+        import math
+
+        net, ps = self.net, [1]
+        interval = int(getattr(net, "structural_interval", 1))
+        if interval > 1:
+            ps.append(interval)
+        trig = getattr(self.ac, "trigger", None)
+        if isinstance(trig, tuple) and trig and trig[0] == "every":
+            ps.append(int(trig[1]))
+        pc = net.prune_conn
+        if isinstance(pc, LowestMagnitudePrune) and pc.every > 1:
+            ps.append(int(pc.every))
+        return math.lcm(*ps)
+
+    def _graph_safe(self, sig: tuple[bool, bool, bool]) -> bool:
+        """Whether a step of this signature may be captured: no host read
+        inside it (an overflow that must raise), no unit spawn."""
+        grow, unit, _ = sig
+        if unit:
+            return False
+        return not (grow and self.ac is not None and self.ac.on_overflow == "error")
+
+    def _replay_or_capture(self, state: NetworkState, inputs: StepInputs):
+        """With `auto_graphs`, a step of a signature seen before replays
+        that signature's graph (captured here at its second occurrence);
+        returns (ran, remainder). Without it, counts the signature."""
+        sig = self._signature(state)
+        entry = self._graphs.get(sig)
+        if entry is None or entry[0] != id(state):
+            if (not self.auto_graphs or self._sig_seen.get((sig, id(state)), 0) < 1
+                    or not self._graph_safe(sig)):
+                self._sig_seen[(sig, id(state))] = self._sig_seen.get((sig, id(state)), 0) + 1
+                return False, None
+            x = torch.as_tensor(inputs.inputs, dtype=torch.float32).to(self.dev).reshape(-1).clone()
+            t = None if inputs.targets is None else torch.as_tensor(inputs.targets, dtype=torch.float32).to(
+                self.dev).reshape(-1).clone()
+            gin = StepInputs(x, t)
+            torch.cuda.synchronize(self.dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                rem = self._body(state, gin)
+            entry = (id(state), g, gin, rem)
+            self._graphs[sig] = entry
+        _, g, gin, rem = entry
+        self._copy_in(gin, inputs)
+        g.replay()
+        return True, rem
+
+    @staticmethod
+    def _copy_in(buf: StepInputs, inputs: StepInputs) -> None:
+        x = inputs.inputs
+        if not isinstance(x, torch.Tensor):
+            x = torch.from_numpy(np.ascontiguousarray(x, np.float32))
+        buf.inputs.copy_(x.reshape(-1), non_blocking=True)
+        if inputs.targets is not None and buf.targets is not None:
+            t = inputs.targets
+            if not isinstance(t, torch.Tensor):
+                t = torch.from_numpy(np.ascontiguousarray(t, np.float32))
+            buf.targets.copy_(t.reshape(-1), non_blocking=True)
 
     def capture(self, state: NetworkState, inputs: StepInputs, *, keep_graph: bool = False) -> None:
         """Capture one step of `state` as a CUDA graph; later calls with the
@@ -1231,6 +1408,8 @@ class StepFn:
         self.graph = None
         self._graph_rem = None
         self._graph_in = None
+        self._graphs = {}
+        self._sig_seen = {}
 
     def close(self) -> None:
         """Release the graph and the peer-memory group (collective under
@@ -1255,7 +1434,11 @@ class StepFn:
             self.graph.replay()
             remainder = self._graph_rem
         else:
-            remainder = self._body(state, inputs)
+            # eager steps are counted per signature even before auto_graphs
+            # is set, so a later capture needs no further eager occurrence
+            ran, remainder = (self._replay_or_capture(state, inputs) if not self.capturable() else (False, None))
+            if not ran:
+                remainder = self._body(state, inputs)
         state.step += 1
         grown = state.grown if state.grown is not None else torch.zeros((), dtype=torch.int32, device=self.dev)
         overflow = state.overflow if state.overflow is not None else torch.zeros((), dtype=torch.bool,
@@ -1287,10 +1470,13 @@ def gather_arena(conns, static: NetworkStatic, out: dict | None = None, group=No
 
 
 def make_step(net: type[Network], static: NetworkStatic, *, batch_size: int | None = None, layout: str = "auto",
-              fuse_prune: str | bool = "auto", growth: str = "auto", device: torch.device | str = "cuda") -> StepFn:
+              fuse_prune: str | bool = "auto", growth: str = "auto", device: torch.device | str = "cuda",
+              fuse_train: bool = True) -> StepFn:
     """Build the step for `net` on `static` (src/plastax/step.py:76-237).
 
     Raises ValueError for an unknown knob, as the reference does.
+    `fuse_train=False` keeps a PIPELINE net's forward, loss, backward and
+    update as separate passes where the fused training step would apply.
     """
     if layout not in ("auto", "edges", "csr", "triton", "xla"):
         raise ValueError(f"make_step: unknown layout {layout!r}")
@@ -1310,7 +1496,7 @@ def make_step(net: type[Network], static: NetworkStatic, *, batch_size: int | No
         from plastax_b200.batched import BatchedStepFn
 
         return BatchedStepFn(net, static, batch_size, torch.device(device))
-    return StepFn(net, static, torch.device(device), fuse_prune=fuse_prune is not False)
+    return StepFn(net, static, torch.device(device), fuse_prune=fuse_prune is not False, fuse_train=fuse_train)
 
 
 def make_growth_retry(net: type[Network], static: NetworkStatic, *, device: torch.device | str = "cuda"):
