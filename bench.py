@@ -88,6 +88,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--phase-times", action="store_true",
                     help="add the step's main-stream phases (CUDA events over the eager steps; the phase ends at "
                          "the named boundary) to the line: rank 0's and the max over ranks")
+    ap.add_argument("--select-fork", default="auto", choices=["auto", "start", "sweep"],
+                    help="where the next step's growth selection forks onto the side stream: at the step's start "
+                         "or after the propagation (auto: after it under Scheme-A)")
     ap.add_argument("--kernel-breakdown", action="store_true",
                     help="after the timing, print (stderr, rank 0) every kernel's device time per step over five "
                          "graph replays, from the profiler's activity records")
@@ -348,6 +351,8 @@ def engine_arm(args) -> None:
     torch.cuda.synchronize()
     step = make_step(net, static, device=dev)
     step.mirror_chunk_bits = args.chunk_bits
+    if args.select_fork != "auto":
+        step.select_after_sweep = args.select_fork == "sweep"
     W, Kst = max(args.warmup, 3), args.steps
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234)

@@ -1032,9 +1032,9 @@ PXB_API int pxb_scheme_a_apply(const pxb_peer_group *group, int32_t num_units,
  * cluster; (2) per unit: the rows summed (exact) and rounded once, the
  * forward apply (inputs and pruned units kept), the MSE seed of the outputs
  * (act - target), the backward apply (every unit but the pruned, inputs
- * included), and the loss summed in output order by the last CTA; (3) one
- * pass over the arena applying the optimizer to every live edge with the
- * edge gradient update_grad[dst] * act[src] (the new columns).
+ * included); (3) one pass over the arena applying the optimizer to every
+ * live edge with the edge gradient update_grad[dst] * act[src] (the new
+ * columns), one warp of it summing the loss in output order.
  * Replaces, for such nets, src/plastax/sweep.py:300-340 (forward sweep),
  * :402-450 (backward sweep), src/plastax/phases.py:488-532 (update_conn) and
  * the MSE seed of scripts/parity/reference.py:338-352, in the order of

@@ -44,11 +44,14 @@ constexpr int kFixBits = PXB_FIXED_FRAC_BITS;  // the global accumulator's unit
 static_assert(kFixBits == 31, "the flush's shift and fix_scale assume a global unit of 2^-31");
 
 // The same contribution straight into the global accumulators (the
-// overflow list's edges), in their unit of 2^-31.
-__device__ __forceinline__ void fixed_add_global(int64_t *af, float *gf, float p) {
+// overflow list's edges), in their unit of 2^-31, rounded as the mirror's
+// shared words round it (to 2^-frac): an edge sums to the same value
+// whether it sits in a group or in the overflow list.
+__device__ __forceinline__ void fixed_add_global(int64_t *af, float *gf, float p, int frac) {
   if (fabsf(p) < 1048576.0f) {
-    atomicAdd(reinterpret_cast<unsigned long long *>(af),
-              static_cast<unsigned long long>(__float2ll_rn(p * fix_scale<kFixBits>())));
+    const float scale = frac == 28 ? fix_scale<28>() : fix_scale<31>();
+    const long long v = __float2ll_rn(p * scale) * (1ll << (kFixBits - frac));
+    atomicAdd(reinterpret_cast<unsigned long long *>(af), static_cast<unsigned long long>(v));
   } else {
     atomicAdd(gf, p);
   }
@@ -475,7 +478,7 @@ __global__ void mirror_overflow_kernel(MirrorK m, const float *__restrict__ act,
     const int32_t s = m.ovf_src[i], d = m.ovf_dst[i];
     if (s < 0 || s >= m.n || d < 0 || d >= m.n) continue;
     const float w = m.ovf_w[i];
-    if (MONOID == PXB_MONOID_SUM) fixed_add_global(acc_fixed + d, acc + d, __fmul_rn(w, act[s]));
+    if (MONOID == PXB_MONOID_SUM) fixed_add_global(acc_fixed + d, acc + d, __fmul_rn(w, act[s]), m.sum_frac);
     else atomic_combine<MONOID>(acc + d, __fmul_rn(w, act[s]));
     if (PK == PXB_PRUNE_LOWEST_K) {
       const uint32_t b = abs_bits(w);

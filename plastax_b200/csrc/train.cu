@@ -26,7 +26,7 @@ constexpr int kTrainFrac = 31;        // fractional bits of the shared words
 constexpr int kAccThreads = 1024;     // accumulate kernel: one CTA per SM
 constexpr int kMaxRows = 40;          // clusters (int64 rows) at most
 constexpr int kApplyThreads = 256;
-constexpr int kUpdateThreads = 1024;
+constexpr int kUpdateThreads = 512;
 constexpr int64_t kSmemCap = 227 * 1024;
 
 static_assert(PXB_FIXED_FRAC_BITS == kTrainFrac, "the rows are in the global accumulator's unit");
@@ -34,7 +34,6 @@ static_assert(PXB_FIXED_FRAC_BITS == kTrainFrac, "the rows are in the global acc
 struct Scratch {
   int64_t *rows;   // [kMaxRows][2N]: forward sums, then backward sums
   float *side;     // [2N]: the float side of each sum (kept zero between steps)
-  uint32_t *ticket;
 };
 
 inline Scratch scratch_of(void *base, int32_t n) {
@@ -43,8 +42,6 @@ inline Scratch scratch_of(void *base, int32_t n) {
   s.rows = reinterpret_cast<int64_t *>(p);
   p += sizeof(int64_t) * kMaxRows * 2 * static_cast<int64_t>(n);
   s.side = reinterpret_cast<float *>(p);
-  p += sizeof(float) * 2 * static_cast<int64_t>(n);
-  s.ticket = reinterpret_cast<uint32_t *>(p);
   return s;
 }
 
@@ -170,6 +167,13 @@ struct ApplyArgs {
   float *loss;
 };
 
+struct LossArgs {
+  int32_t num_outputs;
+  const int32_t *output_ids;
+  const float *seed;
+  float *loss;
+};
+
 constexpr int kRowLanes = 8;  // lanes summing one unit's rows
 constexpr int kApplyUnits = kApplyThreads / kRowLanes;
 
@@ -198,8 +202,7 @@ __device__ __forceinline__ float round_sum(long long f, float *side) {
 
 // Kernel 2: per unit the forward apply (inputs and pruned kept,
 // src/plastax/sweep.py:332-338), the MSE seed of an output, the backward
-// apply (every unit but the pruned, :444-449); the last CTA sums the loss in
-// output order (as pxb_mse_loss).
+// apply (every unit but the pruned, :444-449).
 template <bool BWD>
 __global__ void __launch_bounds__(kApplyThreads) train_apply_kernel(ApplyArgs a, Scratch sc) {
   const int lane = threadIdx.x % kRowLanes;
@@ -236,25 +239,6 @@ __global__ void __launch_bounds__(kApplyThreads) train_apply_kernel(ApplyArgs a,
       }
     }
   }
-  if (a.loss == nullptr) return;
-  // the last CTA to finish sums the loss (no CTA waits for another)
-  __shared__ bool last;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const uint32_t t = atomicAdd(sc.ticket, 1u);
-    last = t == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!last || threadIdx.x != 0) return;
-  __threadfence();
-  float total = 0.0f;
-  for (int32_t i = 0; i < a.num_outputs; ++i) {
-    const float d = *reinterpret_cast<volatile float *>(a.seed + a.output_ids[i]);
-    total = __fadd_rn(total, __fmul_rn(__fmul_rn(0.5f, d), d));
-  }
-  a.loss[0] = total;
-  *sc.ticket = 0;
 }
 
 __device__ __forceinline__ void update_edge(const OptParams &p, float *__restrict__ weight, float *m_col,
@@ -266,29 +250,64 @@ __device__ __forceinline__ void update_edge(const OptParams &p, float *__restric
   weight[s] = w;
 }
 
-// Kernel 3: the optimizer on every live edge, grid-stride over 4-slot
-// groups with 16-byte loads.
-__global__ void __launch_bounds__(kUpdateThreads)
+// The MSE loss in output order (as pxb_mse_loss), by one warp: the seeds
+// loaded 32 at a time, summed in order by lane 0.
+__device__ __forceinline__ void loss_warp(const LossArgs &l) {
+  const int lane = threadIdx.x & 31;
+  float total = 0.0f;
+  for (int32_t base = 0; base < l.num_outputs; base += 32) {
+    const int32_t i = base + lane;
+    const float d = i < l.num_outputs ? l.seed[l.output_ids[i]] : 0.0f;
+    const float sq = __fmul_rn(__fmul_rn(0.5f, d), d);
+    const int cnt = l.num_outputs - base < 32 ? l.num_outputs - base : 32;
+    for (int j = 0; j < cnt; ++j) {
+      const float v = __shfl_sync(0xffffffffu, sq, j);
+      if (lane == 0) total = __fadd_rn(total, v);
+    }
+  }
+  if (lane == 0) l.loss[0] = total;
+}
+
+// Kernel 3: the optimizer on every live edge below the tail, grid-stride
+// over 4-slot groups with 16-byte loads, two groups in flight per thread;
+// block 0's first warp also sums the loss (the seeds are final: the apply
+// kernel has completed).
+__global__ void __launch_bounds__(kUpdateThreads, 2)
     train_update_kernel(int64_t cap, const int32_t *__restrict__ from, const int32_t *__restrict__ to,
                         const uint8_t *__restrict__ dead, float *__restrict__ weight, float *m_col, float *v_col,
                         float *t_col, const float *__restrict__ act, const float *__restrict__ ug, uint32_t n,
-                        const int64_t *__restrict__ tail, OptParams p) {
+                        const int64_t *__restrict__ tail, OptParams p, LossArgs l) {
+  if (l.loss != nullptr && blockIdx.x == 0 && threadIdx.x < 32) loss_warp(l);
   if (tail != nullptr) {
     const int64_t ts = *tail;
     cap = ts < 0 ? 0 : (ts < cap ? ts : cap);
   }
   const int64_t groups = cap >> 2;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups; g += stride) {
-    const int64_t s = g << 2;
-    const int4 f = *reinterpret_cast<const int4 *>(from + s);
-    const int4 t = *reinterpret_cast<const int4 *>(to + s);
-    const float4 w = *reinterpret_cast<const float4 *>(weight + s);
-    const uint32_t d = *reinterpret_cast<const uint32_t *>(dead + s);
-    update_edge(p, weight, m_col, v_col, t_col, act, ug, n, s, d & 0xff, f.x, t.x, w.x);
-    update_edge(p, weight, m_col, v_col, t_col, act, ug, n, s + 1, (d >> 8) & 0xff, f.y, t.y, w.y);
-    update_edge(p, weight, m_col, v_col, t_col, act, ug, n, s + 2, (d >> 16) & 0xff, f.z, t.z, w.z);
-    update_edge(p, weight, m_col, v_col, t_col, act, ug, n, s + 3, d >> 24, f.w, t.w, w.w);
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups; g += 2 * stride) {
+    const bool two = g + stride < groups;
+    const int64_t s0 = g << 2, s1 = (g + stride) << 2;
+    const int4 f0 = *reinterpret_cast<const int4 *>(from + s0);
+    const int4 t0 = *reinterpret_cast<const int4 *>(to + s0);
+    const float4 w0 = *reinterpret_cast<const float4 *>(weight + s0);
+    const uint32_t d0 = *reinterpret_cast<const uint32_t *>(dead + s0);
+    int4 f1 = make_int4(-1, -1, -1, -1), t1 = f1;
+    float4 w1 = make_float4(0.f, 0.f, 0.f, 0.f);
+    uint32_t d1 = 0x01010101u;
+    if (two) {
+      f1 = *reinterpret_cast<const int4 *>(from + s1);
+      t1 = *reinterpret_cast<const int4 *>(to + s1);
+      w1 = *reinterpret_cast<const float4 *>(weight + s1);
+      d1 = *reinterpret_cast<const uint32_t *>(dead + s1);
+    }
+    update_edge(p, weight, m_col, v_col, t_col, act, ug, n, s0, d0 & 0xff, f0.x, t0.x, w0.x);
+    update_edge(p, weight, m_col, v_col, t_col, act, ug, n, s0 + 1, (d0 >> 8) & 0xff, f0.y, t0.y, w0.y);
+    update_edge(p, weight, m_col, v_col, t_col, act, ug, n, s0 + 2, (d0 >> 16) & 0xff, f0.z, t0.z, w0.z);
+    update_edge(p, weight, m_col, v_col, t_col, act, ug, n, s0 + 3, d0 >> 24, f0.w, t0.w, w0.w);
+    update_edge(p, weight, m_col, v_col, t_col, act, ug, n, s1, d1 & 0xff, f1.x, t1.x, w1.x);
+    update_edge(p, weight, m_col, v_col, t_col, act, ug, n, s1 + 1, (d1 >> 8) & 0xff, f1.y, t1.y, w1.y);
+    update_edge(p, weight, m_col, v_col, t_col, act, ug, n, s1 + 2, (d1 >> 16) & 0xff, f1.z, t1.z, w1.z);
+    update_edge(p, weight, m_col, v_col, t_col, act, ug, n, s1 + 3, d1 >> 24, f1.w, t1.w, w1.w);
   }
   const int64_t rest = groups << 2;
   const int64_t s = rest + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
@@ -442,16 +461,16 @@ extern "C" int pxb_pipeline_train_step(const pxb_pipeline_train *t, void *stream
   if (bwd) train_apply_kernel<true><<<agrid, kApplyThreads, 0, st>>>(a, sc);
   else train_apply_kernel<false><<<agrid, kApplyThreads, 0, st>>>(a, sc);
   PXB_LAUNCHED("train_apply_kernel");
-  if (t->cap == 0) return PXB_OK;
+  const LossArgs l{t->num_outputs, t->output_ids, t->seed, t->loss};
   const OptParams p{o.kind, o.lr, o.b1, o.b2, o.eps, o.weight_decay, nullptr};
   const int64_t groups = (t->cap + 3) / 4;
-  int ugrid = static_cast<int>((groups + kUpdateThreads - 1) / kUpdateThreads);
-  const int cap_grid = sm_count() * 2;
+  int ugrid = static_cast<int>((groups + 2 * kUpdateThreads - 1) / (2 * kUpdateThreads));
+  const int cap_grid = sm_count() * 2;  // one wave: two CTAs per SM
   if (ugrid > cap_grid) ugrid = cap_grid;
   if (ugrid < 1) ugrid = 1;
   train_update_kernel<<<ugrid, kUpdateThreads, 0, st>>>(t->cap, t->from_id, t->to_id, t->dead, t->weight, t->opt_m,
                                                         t->opt_v, t->opt_t, t->act, t->update_grad,
-                                                        static_cast<uint32_t>(n), t->tail_start, p);
+                                                        static_cast<uint32_t>(n), t->tail_start, p, l);
   PXB_LAUNCHED("train_update_kernel");
   return PXB_OK;
 }

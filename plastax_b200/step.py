@@ -217,6 +217,10 @@ class StepFn:
         # runs a whole step ahead, beside this step's passes and claim
         self.ahead = self.side is not None and self.capturable() and self.ac is not None and self.k > 0
         self._ahead_ready = False
+        # where the next step's selection forks from the step (see _body_ahead):
+        # after the propagation under Scheme-A, where the sweep is short and
+        # the latency-bound claim leaves SMs idle; at the start on one GPU
+        self.select_after_sweep = self.sharded
         if self.ahead:
             self.claim_next = tuple(torch.empty_like(t) for t in self.claim_in)
             self.sel_step_dev = torch.zeros(1, dtype=torch.int32, device=device)
@@ -1272,19 +1276,31 @@ class StepFn:
         for dst_t, src_t in zip(self.claim_in, self.claim_next, strict=True):
             dst_t.copy_(src_t)
         torch.add(self.step_dev, 1, out=self.sel_step_dev)
-        self.side.wait_stream(main)
-        with torch.cuda.stream(self.side):
-            self._select(state, out=self.claim_next, step_dev=self.sel_step_dev)
+
+        def select_next():
+            self.side.wait_stream(main)
+            with torch.cuda.stream(self.side):
+                self._select(state, out=self.claim_next, step_dev=self.sel_step_dev)
+
+        # the next step's selection reads only levels and the step counter;
+        # it overlaps either the whole step or only what follows the
+        # propagation (the persistent sweep holds every SM while it runs)
+        if not self.select_after_sweep:
+            select_next()
         self._scatter_inputs(state, inputs)
         self._mark("inputs")
         if self.train_fused:
             self._train(state, inputs)
         else:
             self._forward(state)
+            if self.select_after_sweep:
+                select_next()
             self._loss(state, inputs)
             self._backward(state)
             self._update_unit(state)
             self._update_conn(state)
+        if self.select_after_sweep and self.train_fused:
+            select_next()
         self._prune(state)
         remainder = self._add_conn(state, selected=True)
         self._step_end()
