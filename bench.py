@@ -91,6 +91,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--select-fork", default="auto", choices=["auto", "start", "sweep"],
                     help="where the next step's growth selection forks onto the side stream: at the step's start "
                          "or after the propagation (auto: after it under Scheme-A)")
+    ap.add_argument("--trace", default=None,
+                    help="with --kernel-breakdown: write the replays' kernel timeline as a Chrome trace to this path "
+                         "('{rank}' is replaced by the rank)")
     ap.add_argument("--kernel-breakdown", action="store_true",
                     help="after the timing, print (stderr, rank 0) every kernel's device time per step over five "
                          "graph replays, from the profiler's activity records")
@@ -304,10 +307,14 @@ class _EventTimer:
     """CUDA events around every call of a wrapped function, on the stream
     it launches on (torch's current stream)."""
 
-    def __init__(self, fn) -> None:
+    def __init__(self, fn, lead_cycles: int = 0) -> None:
         self.fn = fn
         self.events: list[tuple] = []
         self.on = True
+        # a spin of this many GPU cycles queued before the start event keeps
+        # the GPU busy while the host enqueues the call, so the events time
+        # the kernels and not the host's launch gaps
+        self.lead_cycles = lead_cycles
 
     def __call__(self, *a, **kw):
         import torch
@@ -315,6 +322,8 @@ class _EventTimer:
         if not self.on:
             return self.fn(*a, **kw)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if self.lead_cycles:
+            torch.cuda._sleep(self.lead_cycles)
         s.record()
         out = self.fn(*a, **kw)
         e.record()
@@ -516,7 +525,7 @@ def engine_arm(args) -> None:
                              "note": "eager steps (launch gaps included), main stream; each phase ends at its "
                                      "named boundary"}
     if args.kernel_breakdown:
-        kernel_breakdown(step, state, inputs_dev[0], rank)
+        kernel_breakdown(lambda: step(state, StepInputs(inputs_dev[0])), rank, trace=args.trace)
     # a CUDA graph holding NCCL calls must be released before the process
     # group is destroyed, or the exit waits forever; the peer-memory group is
     # unmapped collectively
@@ -548,24 +557,26 @@ def engine_arm(args) -> None:
         dist.destroy_process_group()
 
 
-def kernel_breakdown(step, state, x, rank: int, replays: int = 5) -> None:
-    """Every kernel's device time per step over `replays` graph replays (or
-    eager steps), from the profiler's activity records; rank 0 prints it to
-    stderr. Every rank runs the same steps (collectives stay matched)."""
+def kernel_breakdown(run_step, rank: int, replays: int = 5, trace: str | None = None) -> dict:
+    """Every kernel's device time per step over `replays` calls of
+    `run_step` (graph replays, or eager steps), from the profiler's activity
+    records; rank 0 prints it to stderr and returns {kernel: us per step}.
+    Every rank runs the same steps (collectives stay matched)."""
     import collections
     import sys
 
     import torch
     from torch.profiler import ProfilerActivity, profile
 
-    from plastax_b200 import StepInputs
-
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         for _ in range(replays):
-            step(state, StepInputs(x))
+            run_step()
         torch.cuda.synchronize()
+    if trace:
+        # every rank's kernel timeline (start, duration, stream) as a Chrome trace
+        prof.export_chrome_trace(trace.replace("{rank}", str(rank)))
     if rank != 0:
-        return
+        return {}
     tot: dict = collections.defaultdict(lambda: [0, 0.0])
     for evt in prof.events():
         if evt.device_type == torch.autograd.DeviceType.CUDA:
@@ -575,6 +586,7 @@ def kernel_breakdown(step, state, x, rank: int, replays: int = 5) -> None:
     print(f"kernel breakdown: {replays} steps, device time per step", file=sys.stderr)
     for name, (cnt, us) in sorted(tot.items(), key=lambda kv: -kv[1][1]):
         print(f"  {cnt / replays:5.1f}/step {us / replays:10.1f} us  {name}", file=sys.stderr)
+    return {name: us / replays for name, (_, us) in tot.items()}
 
 
 def count_launches(step, state, x, dev) -> int:
@@ -698,7 +710,7 @@ def _edge_pass_timers():
              "batched_backward", "batched_update", "pipeline_train")
     timers = {}
     for nm in names:
-        t = _EventTimer(getattr(K, nm))
+        t = _EventTimer(getattr(K, nm), lead_cycles=200_000)
         t.on = False
         setattr(K, nm, t)
         timers[nm] = t
@@ -772,6 +784,10 @@ def training_arm(args) -> None:
     torch.cuda.synchronize()
     clocks.pause()
     elapsed_ms = t0.elapsed_time(t1)
+    breakdown = None
+    if args.kernel_breakdown:
+        # the same replays' kernels, warm, from the profiler's activity records
+        breakdown = kernel_breakdown(lambda: run(0, X[0], T[0]), rank, replays=20, trace=args.trace)
     # e2e: each step's inputs and targets from pinned host memory, the loss
     # read back every step
     hx = torch.from_numpy(case["x"][W + Kst:W + 2 * Kst]).pin_memory()
@@ -854,6 +870,8 @@ def training_arm(args) -> None:
                 "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms / Kst},
         "roofline": roof, "clocks": clk, "cuda_graph": use_graph,
     }
+    if breakdown:
+        line["kernels_us_per_step"] = {k: round(v, 2) for k, v in sorted(breakdown.items(), key=lambda kv: -kv[1])}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = training_cpu_baseline(args.config, case, max(1, args.cpu_steps))
     if rank == 0:

@@ -113,11 +113,25 @@ __global__ void __launch_bounds__(256) scheme_a_apply_kernel(PeerK g, int32_t n,
     for (int32_t u = lo + blockIdx.x * blockDim.x + threadIdx.x; u < hi; u += gridDim.x * blockDim.x) {
       const uint8_t role = is_input != nullptr ? is_input[u] : 0;
       if (role == 1 || (pruned != nullptr && pruned[u])) continue;
+      // every rank's partials in flight at once (eight at a time), then
+      // combined in rank order
       long long f = 0;
       float side = 0.0f;
-      for (int q = 0; q < g.world; ++q) {
-        f += g.acc_fixed[q][u];
-        side = __fadd_rn(side, g.acc_side[q][u]);
+      for (int q0 = 0; q0 < g.world; q0 += 8) {
+        long long fq[8];
+        float sq[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int q = q0 + j;
+          fq[j] = q < g.world ? g.acc_fixed[q][u] : 0;
+          sq[j] = q < g.world ? g.acc_side[q][u] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (q0 + j >= g.world) break;
+          f += fq[j];
+          side = __fadd_rn(side, sq[j]);
+        }
       }
       const float x = f != 0 ? __fadd_rn(__fmul_rn(__ll2float_rn(f), kFixUnitP), side) : side;
       const float a = act_fn(unit_act_kind(act_kind, role), x);

@@ -61,10 +61,13 @@ def _check(t: torch.Tensor, dtype: torch.dtype, n: int | None, what: str) -> Non
         raise ValueError(f"{what}: expected {n} elements, got {t.numel()}")
 
 
-def _bucket(b: Bucket) -> int:
+def _bucket(b: Bucket, names=None) -> int:
+    """The bucket's capacity, after checking the columns a call reads
+    (`names`, default every canonical column)."""
     cap = b["dead"].numel()
     for name, dt in _DTYPES.items():
-        _check(b[name], dt, cap, f"bucket column {name!r}")
+        if names is None or name in names:
+            _check(b[name], dt, cap, f"bucket column {name!r}")
     return cap
 
 
@@ -414,8 +417,9 @@ def propose_per_conn(b: Bucket, proposals: int, network_seed: int, step: int, nu
                      src_level_bound: int = 0, step_dev: torch.Tensor | None = None,
                      scratch: torch.Tensor | None = None,
                      out: tuple | None = None) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Per-connection proposals over one (bucket-major) arena `b`."""
-    cap = _bucket(b)
+    """Per-connection proposals over one (bucket-major) arena `b` (its
+    from_id, to_id and dead columns)."""
+    cap = _bucket(b, ("from_id", "to_id", "dead"))
     dev = level.device
     total = cap * proposals
     if out is None:
