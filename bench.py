@@ -91,6 +91,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--select-fork", default="auto", choices=["auto", "start", "sweep"],
                     help="where the next step's growth selection forks onto the side stream: at the step's start "
                          "or after the propagation (auto: after it under Scheme-A)")
+    ap.add_argument("--graph-priority", action="store_true",
+                    help="replay the step's graph with the side stream's selection at low priority")
     ap.add_argument("--trace", default=None,
                     help="with --kernel-breakdown: write the replays' kernel timeline as a Chrome trace to this path "
                          "('{rank}' is replaced by the rank)")
@@ -362,6 +364,7 @@ def engine_arm(args) -> None:
     step.mirror_chunk_bits = args.chunk_bits
     if args.select_fork != "auto":
         step.select_after_sweep = args.select_fork == "sweep"
+    step.graph_priority = args.graph_priority
     W, Kst = max(args.warmup, 3), args.steps
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234)

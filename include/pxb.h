@@ -519,6 +519,16 @@ PXB_API int pxb_loop_build(void *step_graph, const pxb_loop_desc *desc, void **l
 PXB_API int pxb_loop_launch(void *loop, void *stream);
 PXB_API int pxb_loop_destroy(void *loop);
 
+/* A captured step graph (a cudaGraph_t) instantiated for replay, with
+ * node_priority != 0 honouring each kernel node's priority (the priority of
+ * the stream it was captured on), so low-priority side-stream work yields
+ * SMs to the step's main stream; launch it on a stream, destroy it once.
+ * The reference replays a jitted step (src/plastax/step.py:226-237); these
+ * replace its dispatch, not a computation. */
+PXB_API int pxb_graph_instantiate(void *graph, int32_t node_priority, void **exec_out);
+PXB_API int pxb_graph_launch(void *exec, void *stream);
+PXB_API int pxb_graph_exec_destroy(void *exec);
+
 /* ------------------------------------------------------------------ */
 /* unit lifecycle (src/plastax/phases.py:1148-1193, :1245-1425)        */
 /* ------------------------------------------------------------------ */

@@ -282,6 +282,9 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_loop_build": (c_i32, [c_ptr, c_ptr, ctypes.POINTER(c_ptr)]),
     "pxb_loop_launch": (c_i32, [c_ptr, c_ptr]),
     "pxb_loop_destroy": (c_i32, [c_ptr]),
+    "pxb_graph_instantiate": (c_i32, [c_ptr, c_i32, ctypes.POINTER(c_ptr)]),
+    "pxb_graph_launch": (c_i32, [c_ptr, c_ptr]),
+    "pxb_graph_exec_destroy": (c_i32, [c_ptr]),
     "pxb_lowest_keys": (c_i32, [c_i64, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr]),
     "pxb_prune_selected": (c_i32, [c_i64, c_ptr, c_ptr, c_i64, c_i64, c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr]),
     "pxb_unit_update": (c_i32, [c_i32, c_i32, c_ptr, c_ptr, c_f32, c_f32, c_ptr, c_ptr]),

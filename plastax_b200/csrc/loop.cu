@@ -151,3 +151,27 @@ extern "C" int pxb_loop_destroy(void *loop) {
   }
   return PXB_OK;
 }
+
+// A captured step graph instantiated with the kernels' own priorities: the
+// side stream's selection (captured at low priority) then yields SMs to the
+// main stream's kernels whenever both have CTAs waiting.
+extern "C" int pxb_graph_instantiate(void *graph, int32_t node_priority, void **exec_out) {
+  PXB_REQUIRE(graph && exec_out, "pxb_graph_instantiate: a pointer is NULL");
+  cudaGraphExec_t exec = nullptr;
+  const unsigned long long flags = node_priority ? cudaGraphInstantiateFlagUseNodePriority : 0;
+  PXB_CUDA(cudaGraphInstantiateWithFlags(&exec, static_cast<cudaGraph_t>(graph), flags));
+  *exec_out = exec;
+  return PXB_OK;
+}
+
+extern "C" int pxb_graph_launch(void *exec, void *stream) {
+  PXB_REQUIRE(exec != nullptr, "pxb_graph_launch: exec is NULL");
+  PXB_CUDA(cudaGraphLaunch(static_cast<cudaGraphExec_t>(exec), as_stream(stream)));
+  return PXB_OK;
+}
+
+extern "C" int pxb_graph_exec_destroy(void *exec) {
+  PXB_REQUIRE(exec != nullptr, "pxb_graph_exec_destroy: exec is NULL");
+  PXB_CUDA(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(exec)));
+  return PXB_OK;
+}

@@ -185,6 +185,8 @@ class StepFn:
         self._bound: int | None = None
         self.step_dev = torch.zeros(1, dtype=torch.int32, device=device)
         self.graph = None  # a captured CUDA graph of the step body (see capture)
+        self.graph_priority = False  # capture main / side streams at high / low priority (see capture)
+        self._graph_exec = None
         # with auto_graphs, steps whose work depends on periodic phases replay
         # one captured graph per signature (see _replay_or_capture)
         self.auto_graphs = False
@@ -1411,16 +1413,33 @@ class StepFn:
             self.dev).reshape(-1).clone()
         self._graph_in = StepInputs(x, t)
         torch.cuda.synchronize(self.dev)
-        g = torch.cuda.CUDAGraph(keep_graph=keep_graph)
-        with torch.cuda.graph(g):
+        self._drop_exec()
+        prio = self.graph_priority and self.side is not None
+        g = torch.cuda.CUDAGraph(keep_graph=keep_graph or prio)
+        # with graph_priority the main stream's kernels are captured at high
+        # priority, the side stream's (the next step's selection) at the
+        # lowest, and the graph is instantiated to honour them
+        cap = torch.cuda.Stream(device=self.dev, priority=-1) if prio else None
+        with torch.cuda.graph(g, stream=cap):
             self._graph_rem = self._body(state, self._graph_in)
+        if prio:
+            exec_ = ctypes.c_void_p()
+            _lib.call("pxb_graph_instantiate", ctypes.c_void_p(g.raw_cuda_graph()), ctypes.c_int32(1),
+                      ctypes.byref(exec_))
+            self._graph_exec = exec_
         self.graph = g
         self._graph_state = id(state)
         self._graph_kept = keep_graph
 
+    def _drop_exec(self) -> None:
+        if getattr(self, "_graph_exec", None) is not None:
+            _lib.call("pxb_graph_exec_destroy", self._graph_exec)
+        self._graph_exec = None
+
     def release_graph(self) -> None:
         """Drop the captured graph and its buffers. A graph that holds NCCL
         calls must be released before the process group is destroyed."""
+        self._drop_exec()
         self.graph = None
         self._graph_rem = None
         self._graph_in = None
@@ -1447,7 +1466,10 @@ class StepFn:
                 if not isinstance(t, torch.Tensor):
                     t = torch.from_numpy(np.ascontiguousarray(t, np.float32))
                 self._graph_in.targets.copy_(t.reshape(-1), non_blocking=True)
-            self.graph.replay()
+            if self._graph_exec is not None:
+                _lib.call("pxb_graph_launch", self._graph_exec, K._stream())
+            else:
+                self.graph.replay()
             remainder = self._graph_rem
         else:
             # eager steps are counted per signature even before auto_graphs

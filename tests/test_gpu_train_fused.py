@@ -66,16 +66,19 @@ def _compare(a, b, what):
                                            err_msg=f"{what}: conn column {col}")
 
 
-@pytest.mark.parametrize("opt_kind", ["sgd", "momentum", "adam", "rmsprop"])
-def test_fused_step_equals_the_separate_passes(cuda, opt_kind):
+@pytest.mark.parametrize("opt_kind,n", [("sgd", 3000), ("momentum", 3000), ("adam", 3000), ("rmsprop", 3000),
+                                        ("sgd", 9000), ("adam", 14000)])
+def test_fused_step_equals_the_separate_passes(cuda, opt_kind, n):
+    """From 3,000 units up to 14,000, near the largest count whose four
+    accumulator words per unit fit one CTA's shared memory."""
     import plastax_b200 as px
 
     opt = {"sgd": px.optim.sgd(0.01), "momentum": px.optim.momentum(0.01, 0.9), "adam": px.optim.adam(0.003),
            "rmsprop": px.optim.rmsprop(0.003)}[opt_kind]
     Net = _net(opt)
     rng = np.random.default_rng(7)
-    n, n_in, n_out = 3000, 16, 8
-    src, dst, w = _edges(rng, n, 90_000, n_in)
+    n_in, n_out = 16, 8
+    src, dst, w = _edges(rng, n, 30 * n, n_in)
     (_, sa, fa), (_, sb, fb) = _pair(cuda, Net, n, src, dst, w, n_in, n_out)
     for i in range(6):
         x = rng.standard_normal(n_in).astype(np.float32)
