@@ -233,6 +233,10 @@ PXB_API int pxb_unit_apply(int32_t num_units, int32_t mode, int32_t act_kind,
 
 /* Fill n floats with a value (accumulator identity reset). */
 PXB_API int pxb_fill_f32(int64_t n, float value, float *out, void *stream);
+/* A forward's accumulators before a sweep, in one launch: acc[0..n) = value
+ * (the monoid's identity) and acc_fixed[0..n) = 0 when acc_fixed is given
+ * (the identity_accumulator of src/plastax/sweep.py:334). */
+PXB_API int pxb_clear_accumulators(int64_t n, float value, float *acc, int64_t *acc_fixed, void *stream);
 
 /* Mean-squared-error loss over the outputs (scripts/parity/reference.py:338):
  * seed[out[k]] = act[out[k]] - target[k]; loss_out[0] = 0.5 * sum diff^2

@@ -182,6 +182,7 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_sm_count": (c_i32, [c_ptr]),
     "pxb_set_device": (c_i32, [c_i32]),
     "pxb_get_device": (c_i32, [c_ptr]),
+    "pxb_clear_accumulators": (c_i32, [c_i64, c_f32, c_ptr, c_ptr, c_ptr]),
     "pxb_fill_f32": (c_i32, [c_i64, c_f32, c_ptr, c_ptr]),
     "pxb_forward_accumulate": (c_i32, [c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i32, c_i32, c_ptr, c_ptr]),
     "pxb_forward_prune": (

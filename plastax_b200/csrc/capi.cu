@@ -34,6 +34,16 @@ int sm_count() {
   return cache[dev];
 }
 
+// A forward's accumulators reset in one pass: the float column to the
+// monoid's identity and the fixed-point column to zero.
+__global__ void clear_acc_kernel(int64_t n, float v, float *__restrict__ acc, int64_t *__restrict__ fixed) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n; i += stride) {
+    acc[i] = v;
+    if (fixed != nullptr) fixed[i] = 0;
+  }
+}
+
 __global__ void fill_f32_kernel(int64_t n, float v, float *__restrict__ out) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
@@ -71,5 +81,14 @@ extern "C" int pxb_fill_f32(int64_t n, float value, float *out, void *stream) {
   PXB_REQUIRE(out != nullptr, "pxb_fill_f32: out is NULL");
   pxb::fill_f32_kernel<<<pxb::grid_for(n, 1024, 4), 256, 0, pxb::as_stream(stream)>>>(n, value, out);
   PXB_LAUNCHED("fill_f32_kernel");
+  return PXB_OK;
+}
+
+extern "C" int pxb_clear_accumulators(int64_t n, float value, float *acc, int64_t *acc_fixed, void *stream) {
+  PXB_REQUIRE(n >= 0, "pxb_clear_accumulators: negative n");
+  if (n == 0) return PXB_OK;
+  PXB_REQUIRE(acc != nullptr, "pxb_clear_accumulators: acc is NULL");
+  pxb::clear_acc_kernel<<<pxb::grid_for(n, 1024, 4), 256, 0, pxb::as_stream(stream)>>>(n, value, acc, acc_fixed);
+  PXB_LAUNCHED("clear_acc_kernel");
   return PXB_OK;
 }

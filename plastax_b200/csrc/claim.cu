@@ -522,6 +522,17 @@ __global__ void growth_flags_kernel(const int32_t *__restrict__ counts, int32_t 
   if (needs_resort) *needs_resort = static_cast<uint8_t>(*needs_resort | (counts[3] > 0 ? 1 : 0));
 }
 
+// The commit's counters and level runs cleared in one launch (a memset
+// node per array costs a gap of microseconds before the next kernel).
+__global__ void claim_reset_kernel(int32_t *counts, int32_t *level_first, int32_t *level_end, int32_t levels) {
+  for (int i = threadIdx.x; i < 8; i += blockDim.x) counts[i] = 0;
+  if (level_first != nullptr)
+    for (int i = threadIdx.x; i <= levels; i += blockDim.x) {
+      level_first[i] = 0;
+      level_end[i] = 0;
+    }
+}
+
 // The end of a step: the growth flags of a step that claimed nothing
 // cleared (when given) and the device step counter advanced, in one launch.
 __global__ void step_end_kernel(int32_t *step, int32_t *grown, uint8_t *overflow) {
@@ -672,7 +683,8 @@ extern "C" int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id, int
     w.extra_vals[e] = extra_vals[e];
   }
   cudaStream_t st = as_stream(stream);
-  PXB_CUDA(cudaMemsetAsync(o.counts, 0, 8 * 4, st));
+  claim_reset_kernel<<<1, 128, 0, st>>>(o.counts, k > 0 ? o.level_first : nullptr, o.level_end, num_levels);
+  PXB_LAUNCHED("claim_reset_kernel");
   if (k > 0) {
     CandArgs c{topo, k, cand_src, cand_dst, growable, unit_level, num_units, num_levels, max_new};
     const int grid = grid_for(k, 256, 8);
@@ -704,8 +716,6 @@ extern "C" int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id, int
       PXB_CUDA(cub::DeviceRadixSort::SortPairs(o.cub_tmp, tb, o.ckey_in, o.ckey_out, o.cidx_in, o.cidx_out,
                                                static_cast<int>(k), 0, key_bits, st));
     }
-    PXB_CUDA(cudaMemsetAsync(o.level_first, 0, (num_levels + 1) * 4, st));
-    PXB_CUDA(cudaMemsetAsync(o.level_end, 0, (num_levels + 1) * 4, st));
     level_runs_kernel<<<grid, 256, 0, st>>>(k, o.ckey_out, o.level_first, o.level_end);
     PXB_LAUNCHED("level_runs_kernel");
     TotalsArgs t{o.level_local, level_before, level_totals};

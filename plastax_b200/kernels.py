@@ -71,6 +71,15 @@ def _bucket(b: Bucket, names=None) -> int:
     return cap
 
 
+def clear_accumulators(acc: torch.Tensor, value: float, acc_fixed: torch.Tensor | None = None) -> None:
+    """acc = value and acc_fixed = 0, one launch."""
+    _check(acc, torch.float32, None, "accumulator")
+    if acc_fixed is not None:
+        _check(acc_fixed, torch.int64, acc.numel(), "fixed-point accumulator")
+    call("pxb_clear_accumulators", ctypes.c_int64(acc.numel()), ctypes.c_float(value), ptr(acc), ptr(acc_fixed),
+         _stream())
+
+
 def fill(t: torch.Tensor, value: float) -> None:
     _check(t, torch.float32, None, "fill target")
     call("pxb_fill_f32", ctypes.c_int64(t.numel()), ctypes.c_float(value), ptr(t), _stream())

@@ -223,6 +223,16 @@ class StepFn:
         # after the propagation under Scheme-A, where the sweep is short and
         # the latency-bound claim leaves SMs idle; at the start on one GPU
         self.select_after_sweep = self.sharded
+        # with the prune and growth firing every step, the next step's plan
+        # of the lowest-|w| prune is made right after this step's claim, on
+        # its own stream beside the mirror insert (it reads the histograms
+        # the claim's committed edges update, nothing the insert writes)
+        pc = net.prune_conn
+        self.plan_ahead = bool(self.lowk_prune and pc.every <= 1 and self.ac is not None and self.k > 0
+                               and self.capturable() and torch.device(device).type == "cuda")
+        self.plan_stream = torch.cuda.Stream(device=device) if self.plan_ahead else None
+        self._plan_ready = False
+        self._plan_pending = False
         if self.ahead:
             self.claim_next = tuple(torch.empty_like(t) for t in self.claim_in)
             self.sel_step_dev = torch.zeros(1, dtype=torch.int32, device=device)
@@ -358,6 +368,7 @@ class StepFn:
             self._bind_train(state)
         self.step_dev.fill_(state.step)
         self._ahead_ready = False
+        self._plan_ready = False
         self._bound = id(state)
 
     def _mark(self, name: str) -> None:
@@ -671,7 +682,9 @@ class StepFn:
             m = self.mirrors[i]
             if self.lowk_prune:
                 if self._lowk_fires(state):
-                    self.lowk.make_plan()
+                    if not self._plan_ready:
+                        self.lowk.make_plan()
+                    self._plan_ready = False
                     self.lowk.sweep(m, act, acc, acc_fixed, self.fwd_monoid, b["dead"], bm, bm_level)
                     self._lowk_fired = True
                     self.launches += 1
@@ -741,9 +754,7 @@ class StepFn:
         act = units[ACTIVATION.name]
         pruned = units.get(PRUNED.name)
         fp = net.forward_pass
-        K.fill(self.acc, self.fwd_identity)
-        if self.acc_fixed is not None:
-            self.acc_fixed.zero_()
+        K.clear_accumulators(self.acc, self.fwd_identity, self.acc_fixed)
         if self.pipeline:
             if self.peers is not None:
                 from plastax_b200.peers import scheme_a_apply
@@ -1188,7 +1199,16 @@ class StepFn:
             if self.lowk is not None:
                 # the committed edges enter the prune's histogram (every rank
                 # adds every rank's: the histogram is the whole arena's)
-                self.lowk.hist_add(cw, self.committed, ws.counts, tally=fresh)
+                if self.plan_ahead and fresh:
+                    main = torch.cuda.current_stream(self.dev)
+                    self.plan_stream.wait_stream(main)
+                    with torch.cuda.stream(self.plan_stream):
+                        self.lowk.hist_add(cw, self.committed, ws.counts, tally=fresh)
+                        self.lowk.make_plan()
+                    self._plan_pending = True
+                    self.launches += 2
+                else:
+                    self.lowk.hist_add(cw, self.committed, ws.counts, tally=fresh)
                 self.launches += 1
                 self._mark("hist_add")
             if self.use_mirror:
@@ -1260,6 +1280,11 @@ class StepFn:
         return remainder
 
     def _step_end(self) -> None:
+        if self._plan_pending:
+            # the next step's plan is made: join its stream
+            torch.cuda.current_stream(self.dev).wait_stream(self.plan_stream)
+            self._plan_pending = False
+            self._plan_ready = True
         clear = self._clear_flags
         self._clear_flags = False
         K.step_end(self.step_dev, self.grown if clear else None, self.overflow if clear else None)
@@ -1275,8 +1300,8 @@ class StepFn:
         if not self._ahead_ready:  # the first step of a bound state selects its own
             self._select(state, out=self.claim_next, step_dev=self.step_dev)
             self._ahead_ready = True
-        for dst_t, src_t in zip(self.claim_in, self.claim_next, strict=True):
-            dst_t.copy_(src_t)
+        # one multi-tensor copy kernel instead of a memcpy per column
+        torch._foreach_copy_(list(self.claim_in), list(self.claim_next))
         torch.add(self.step_dev, 1, out=self.sel_step_dev)
 
         def select_next():
@@ -1408,6 +1433,9 @@ class StepFn:
             raise ValueError("this step's work depends on the step count (trigger or interval); it cannot be "
                              "replayed from one graph")
         self._bind(state)
+        if self.plan_ahead and not self._plan_ready:
+            raise ValueError("capture a step after at least one eager step of the bound state (the graph "
+                             "expects the prune's plan made by the step before it)")
         x = torch.as_tensor(inputs.inputs, dtype=torch.float32).to(self.dev).reshape(-1).clone()
         t = None if inputs.targets is None else torch.as_tensor(inputs.targets, dtype=torch.float32).to(
             self.dev).reshape(-1).clone()
