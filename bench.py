@@ -643,8 +643,12 @@ def training_case(kind: str, dev, steps: int):
                           "propagation": "pipeline", "parallelism": "replicas"},
                     bytes_per_slot={"forward": 13, "update": 17})
         if dev is not None:
+            from plastax_b200 import Driver
+
+            # streamed through Driver.scan: K steps as one device loop
             net, static, state = C.build_esn(cfg, dev)
-            step = make_step(net, static, device=dev)
+            step = Driver(net, static, state, device=dev)
+            case["scan"] = True
     elif kind == "dst":
         cfg = C.C3
         w1, w2 = C.dst_teacher(cfg)
@@ -762,8 +766,14 @@ def training_arm(args) -> None:
     torch.cuda.synchronize()
     for t in timers.values():
         t.on = False
+    scan = bool(case.get("scan"))
     use_graph = (not driver) and hasattr(step, "capturable") and step.capturable()
-    if use_graph:
+    if scan:
+        # the chunk's loop graph is built by a first scan of the same shape
+        step.scan(StepInputs(X[W:W + Kst], T[W:W + Kst]))
+        torch.cuda.synchronize()
+        use_graph = "Driver.scan: the chunk's steps as one device loop"
+    elif use_graph:
         step.capture(state, StepInputs(X[0], T[0]))
     elif not driver and hasattr(step, "auto_graphs"):
         # one graph per signature of the periodic phases, each captured at
@@ -781,8 +791,11 @@ def training_arm(args) -> None:
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     t0.record()
-    for i in range(Kst):
-        run(W + i, X[W + i], T[W + i])
+    if scan:
+        step.scan(StepInputs(X[W:W + Kst], T[W:W + Kst]))
+    else:
+        for i in range(Kst):
+            run(W + i, X[W + i], T[W + i])
     t1.record()
     torch.cuda.synchronize()
     clocks.pause()
