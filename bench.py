@@ -966,9 +966,33 @@ def training_cpu_baseline(kind: str, case: dict, steps: int) -> dict:
             times.append(time.perf_counter() - t0)
         live = sum(int((bk["dead"] == 0).sum()) for bk in buckets)
         sample, cores = f"{n_steps} batched steps of the numpy restatement (batch {batch})", 1
+    elif kind == "units":
+        from oracle.steps import UnitsOracle
+
+        cfg = C.C4
+        net, static, state = C.build_units(cfg, "cpu")
+        buckets = [{k: v.numpy().copy() for k, v in bk.items()} for bk in state.conns]
+        units = {k: v.numpy().copy() for k, v in state.units.items()}
+        ro = UnitsOracle(buckets, units, input_ids=static.input_ids, output_ids=static.output_ids,
+                         num_levels=static.num_levels, net=net)
+        n_steps = max(steps, 11)
+        for i in range(n_steps):
+            t0 = time.perf_counter()
+            ro.step(case["x"][i], case["t"][i])
+            times.append(time.perf_counter() - t0)
+        # the structural step (a unit spawned) every `interval` steps, weighed in at its rate
+        plain = float(np.median([tt for i, tt in enumerate(times) if i % cfg.interval]))
+        struct = float(np.mean([tt for i, tt in enumerate(times) if i % cfg.interval == 0]))
+        per_step = plain + (struct - plain) / cfg.interval
+        live = sum(int((bk["dead"] == 0).sum()) for bk in buckets)
+        sample = (f"{n_steps} unit-lifecycle steps of the oracle restatement, single-threaded (UPGD's scale, the "
+                  f"forward and backward level by level, the trace, UPGD, the quantile prune, the spawn every "
+                  f"{cfg.interval} steps; the regrowth not included): median plain step plus the spawn steps' "
+                  f"excess spread over {cfg.interval} steps")
+        return {"value": live * case["passes"] / per_step, "unit": "edges/s", "cores": 1, "kind": "port",
+                "sample": sample, "ms_per_step": per_step * 1e3}
     else:
-        return {"value": None, "unit": "edges/s", "cores": 0, "kind": "port",
-                "sample": "no oracle restatement of the whole unit-lifecycle step is timed"}
+        raise ValueError(kind)
     per = float(np.median(times))
     return {"value": live * case["passes"] * batch / per, "unit": "edges/s", "cores": cores, "kind": "port",
             "sample": sample, "ms_per_step": per * 1e3}

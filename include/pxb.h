@@ -1053,7 +1053,9 @@ PXB_API int pxb_scheme_a_apply(const pxb_peer_group *group, int32_t num_units,
  * :402-450 (backward sweep), src/plastax/phases.py:488-532 (update_conn) and
  * the MSE seed of scripts/parity/reference.py:338-352, in the order of
  * src/plastax/step.py:45-237. Every value equals the unfused passes' within
- * the fixed-point sum's bound (each product rounded to 2^-32 at most). */
+ * the fixed-point sum's bound (each product rounded to 2^-32 at most). An
+ * arena of at most 65,536 slots takes all three phases in one launch of one
+ * thread-block cluster (its hardware barrier between them). */
 typedef struct pxb_pipeline_train {
   int64_t cap;                 /* the bucket */
   const int32_t *from_id, *to_id;

@@ -237,3 +237,78 @@ class DstOracle:
             self.structural_phase()
         self.step_count += 1
         return loss
+
+
+class UnitsOracle:
+    """The unit-lifecycle step (TOPOLOGICAL, single device; the engine's phase
+    order, src/plastax/phases.py:87-176): UPGD's local scale (the max of each
+    destination's incoming utilities, examples/upgd.py:83-128); the forward
+    level by level (ReLU, the output linear); the MSE seed; the backward level
+    by level; the utility trace update; UPGD on every live edge; the units
+    below the utility quantile pruned; every `interval` steps one unit
+    spawned from the highest-utility parent. Growth is not part of it: the
+    per-unit proposals run every `interval` steps on a few thousand units and
+    the step's cost is the propagation. Composed from the oracle's parts,
+    each checked on its own against the GPU."""
+
+    def __init__(self, buckets: list[dict], units: dict, *, input_ids, output_ids, num_levels: int, net,
+                 trace: str = "utility") -> None:
+        from oracle import units as ou
+        from oracle import upgd as og
+
+        self.ou, self.og = ou, og
+        self.b, self.u = buckets, units
+        self.n = units["activation"].size
+        self.inputs, self.outputs = np.asarray(input_ids), np.asarray(output_ids)
+        self.L = num_levels
+        self.net = net
+        self.trace = trace
+        self.is_input = np.zeros(self.n, np.uint8)
+        self.is_input[self.inputs] = 1
+        self.exempt = np.zeros(self.n, bool)
+        self.exempt[np.concatenate([self.inputs, self.outputs])] = True
+        self.defaults = {k: np.zeros((), v.dtype) for k, v in units.items() if k not in ("level", "pruned")}
+        uc = net.update_conn
+        self.kw = dict(lr=uc.lr, beta=uc.b1, sigma=uc.b2, eps=uc.eps)
+        self.interval = int(net.structural_interval)
+        self.count = 0
+
+    def step(self, x: np.ndarray, t: np.ndarray) -> float:
+        ou, og, u, n = self.ou, self.og, self.u, self.n
+        level, pruned, act = u["level"], u["pruned"], u["activation"]
+        nb, out = len(self.b), self.outputs
+        eta = og.eta_local(self.b, n, "upgd/util", u["upgd/eta"], self.is_input.astype(bool))
+        u["upgd/eta"][:] = eta
+        act[self.inputs] = x
+        # bucket l holds the edges into level l + 1
+        acc = np.zeros(n, np.float32)
+        for lv in range(nb):
+            orc.forward_accumulate(self.b[lv], act, n, "sum", acc)
+            pre = acc[out].copy()
+            orc.unit_apply(n, 0, "relu", "sum", acc, None, None, level, lv + 1, self.is_input, pruned, act)
+            top = level[out] == lv + 1
+            act[out[top]] = pre[top]  # the linear output
+        seed = u["loss_grad"]
+        seed[:] = 0
+        diff = (act[out] - np.asarray(t, np.float32)).astype(np.float32)
+        seed[out] = diff
+        loss = np.float32(0)
+        for d in diff:
+            loss = np.float32(loss + np.float32(np.float32(0.5) * d) * d)
+        grad = u["grad_pre_act"]
+        acc = np.zeros(n, np.float32)
+        for lv in range(nb, 0, -1):
+            if lv < nb:
+                orc.backward_accumulate(self.b[lv], grad, n, "sum", acc)
+            pre = acc[out].copy()
+            orc.unit_apply(n, 1, "relu", "sum", acc, act, seed, level, lv, self.is_input, pruned, grad)
+            top = level[out] == lv
+            grad[out[top]] = (pre[top] + seed[out[top]]).astype(np.float32)
+        ou.update_unit(u, pruned, self.net.update_unit)
+        for b in self.b:
+            og.update(b, grad, act, eta, **self.kw)
+        ou.prune_unit(u, pruned, self.exempt, self.defaults, self.b, self.net.prune_unit)
+        if self.interval <= 1 or self.count % self.interval == 0:
+            ou.add_unit(u, pruned, level, self.defaults, self.net.add_unit, int(self.net.max_levels))
+        self.count += 1
+        return float(loss)

@@ -599,6 +599,11 @@ constexpr int kFsSlowCap = 1 << 16;
 constexpr int kFsThreads = 256;
 constexpr int kFsMaxBinBits = 13;
 constexpr int kFsMaxIpt = (1 << kFsMaxBinBits) / 1024;
+// One (level, bin) counter per 32-byte sector: the propose pass's million
+// returning atomics spread over every L2 slice instead of queueing on the
+// few lines a packed array of counters occupies.
+constexpr int kFsHistStride = 8;
+__host__ __device__ __forceinline__ int64_t fs_hidx(int64_t lb) { return lb * kFsHistStride; }
 
 struct FsGeom {
   int32_t n, L, nb;
@@ -654,7 +659,8 @@ __global__ void __launch_bounds__(kFsThreads) fs_propose_kernel(ProposeArgs a, F
     o.dst[c] = dst;
     // the count's old value is the candidate's slot inside its (level, bin):
     // the scatter needs no atomic of its own
-    o.byrank[c] = static_cast<int32_t>(atomicAdd(o.hist + fs_level(g, a.level, src) * g.nb + fs_bin(g, key), 1u));
+    o.byrank[c] = static_cast<int32_t>(
+        atomicAdd(o.hist + fs_hidx(static_cast<int64_t>(fs_level(g, a.level, src)) * g.nb + fs_bin(g, key)), 1u));
   }
 }
 
@@ -680,7 +686,7 @@ __global__ void __launch_bounds__(1024) fs_threshold_kernel(FsGeom g, FsScratch 
   for (int l = 0; l < g.L; ++l) {
 #pragma unroll
     for (int j = 0; j < kFsMaxIpt; ++j)
-      if (j < ipt && b0 + j < g.nb) tot[j] += static_cast<int32_t>(o.hist[l * g.nb + b0 + j]);
+      if (j < ipt && b0 + j < g.nb) tot[j] += static_cast<int32_t>(o.hist[fs_hidx(l * g.nb + b0 + j)]);
   }
   int32_t mine = 0;
 #pragma unroll
@@ -708,7 +714,7 @@ __global__ void __launch_bounds__(1024) fs_threshold_kernel(FsGeom g, FsScratch 
     int32_t lm = 0;
 #pragma unroll
     for (int j = 0; j < kFsMaxIpt; ++j) {
-      v[j] = (j < ipt && b0 + j < tb) ? static_cast<int32_t>(o.hist[l * g.nb + b0 + j]) : 0;
+      v[j] = (j < ipt && b0 + j < tb) ? static_cast<int32_t>(o.hist[fs_hidx(l * g.nb + b0 + j)]) : 0;
       lm += v[j];
     }
     int32_t lex, lagg;
@@ -875,7 +881,7 @@ __global__ void __launch_bounds__(kFsThreads) fs_bins_warp_kernel(FsGeom g, Init
   for (int64_t q = static_cast<int64_t>(blockIdx.x) * kFsWarps + w; q < pairs;
        q += static_cast<int64_t>(gridDim.x) * kFsWarps) {
     const int32_t l = static_cast<int32_t>(q / tb), b = static_cast<int32_t>(q % tb);
-    const int32_t m = static_cast<int32_t>(o.hist[l * g.nb + b]);
+    const int32_t m = static_cast<int32_t>(o.hist[fs_hidx(static_cast<int64_t>(l) * g.nb + b)]);
     if (m == 0 || m > kFsWarpCap) continue;  // larger bins: fs_bins_kernel
     const uint32_t t0 = o.toff[l * g.nb + b];
     for (int e = lane; e < m; e += 32) ks[e] = o.bk[t0 + e];
@@ -902,7 +908,7 @@ __global__ void __launch_bounds__(kFsThreads) fs_bins_kernel(FsGeom g, InitArgs 
   const int64_t pairs = static_cast<int64_t>(g.L) * tb;
   for (int64_t q = blockIdx.x; q < pairs; q += gridDim.x) {
     const int32_t l = static_cast<int32_t>(q / tb), b = static_cast<int32_t>(q % tb);
-    const int32_t m = static_cast<int32_t>(o.hist[l * g.nb + b]);
+    const int32_t m = static_cast<int32_t>(o.hist[fs_hidx(static_cast<int64_t>(l) * g.nb + b)]);
     if (m <= kFsWarpCap) continue;  // fs_bins_warp_kernel's
     const uint32_t t0 = o.toff[l * g.nb + b];
     int32_t *rank = rank_scratch + t0;
@@ -946,7 +952,7 @@ static void fs_layout(const FsGeom &g, char *base, FsScratch *o) {
   o->bk = reinterpret_cast<uint64_t *>(take(kk * 8));
   o->bi = reinterpret_cast<int32_t *>(take(kk * 4 * 2));  // indices, then ranks
   o->byrank = reinterpret_cast<int32_t *>(take(n * 4));
-  o->hist = reinterpret_cast<uint32_t *>(take(hb * 4));
+  o->hist = reinterpret_cast<uint32_t *>(take(hb * 4 * kFsHistStride));
   o->toff = reinterpret_cast<uint32_t *>(take(hb * 4));
   o->info = reinterpret_cast<FsInfo *>(take(sizeof(FsInfo)));
   o->total = off;
@@ -1241,7 +1247,7 @@ extern "C" int pxb_propose_select_unique(int32_t num_units, uint64_t network_see
   if (step_dev == nullptr) a.keyed_hi = philox32(network_seed, (static_cast<uint64_t>(static_cast<uint32_t>(step)) << 8) | 1u);
   InitArgs ia{init_kind, init_a, init_b, init_salt};
   cudaStream_t st = as_stream(stream);
-  PXB_CUDA(cudaMemsetAsync(o.hist, 0, size_t(g.L) * g.nb * 4, st));
+  PXB_CUDA(cudaMemsetAsync(o.hist, 0, size_t(g.L) * g.nb * 4 * kFsHistStride, st));
   const int grid = grid_for(num_units, kFsThreads, 8);
   fs_propose_kernel<<<grid, kFsThreads, 0, st>>>(a, g, o);
   PXB_LAUNCHED("fs_propose_kernel");

@@ -64,33 +64,14 @@ __device__ __forceinline__ void acc_edge(int32_t *fwd, int32_t *bwd, float *side
   if (BWD) fixed_add<kTrainFrac>(bwd + f, bwd + n + f, side_b + f, __fmul_rn(w, __ldg(grad + t)));
 }
 
-// Kernel 1: every CTA sweeps a contiguous slot range into its shared
-// accumulators (forward lo[N] hi[N], backward lo[N] hi[N]); the cluster's
-// CTAs then split the units and each sums its share over every CTA of the
-// cluster (distributed shared memory) into the cluster's int64 row.
+// One CTA's sweep of slots [lo, hi) into its shared accumulators (lo a
+// multiple of four slots, so the column bases stay 16-byte aligned).
 template <bool BWD>
-__global__ void __launch_bounds__(kAccThreads, 1)
-    train_accumulate_kernel(int64_t cap, const int32_t *__restrict__ from, const int32_t *__restrict__ to,
-                            const uint8_t *__restrict__ dead, const float *__restrict__ weight,
-                            const float *__restrict__ act, const float *__restrict__ grad, int32_t n,
-                            const int64_t *__restrict__ tail, Scratch sc) {
-  extern __shared__ int32_t smem[];
-  int32_t *fwd = smem;              // lo[n], hi[n]
-  int32_t *bwd = smem + 2 * n;      // lo[n], hi[n] (BWD)
-  const int words = (BWD ? 4 : 2) * n;
-  for (int i = threadIdx.x; i < words; i += blockDim.x) smem[i] = 0;
-  __syncthreads();
-  float *side_f = sc.side, *side_b = sc.side + n;
-
-  // the swept slots: the capacity, or up to the arena's tail
-  int64_t limit = cap;
-  if (tail != nullptr) {
-    const int64_t ts = *tail;
-    limit = ts < 0 ? 0 : (ts < cap ? ts : cap);
-  }
-  const int64_t per_cta = ((limit + gridDim.x - 1) / gridDim.x + 3) & ~int64_t(3);
-  const int64_t lo = static_cast<int64_t>(blockIdx.x) * per_cta;
-  const int64_t hi = lo + per_cta < limit ? lo + per_cta : limit;
+__device__ __forceinline__ void sweep_slots(int32_t *fwd, int32_t *bwd, float *side_f, float *side_b, int32_t n,
+                                            const float *__restrict__ act, const float *__restrict__ grad,
+                                            const int32_t *__restrict__ from, const int32_t *__restrict__ to,
+                                            const uint8_t *__restrict__ dead, const float *__restrict__ weight,
+                                            int64_t lo, int64_t hi) {
   // 16-byte loads of four slots (per_cta and the column bases are multiples
   // of four slots / 16 bytes), two groups in flight per thread
   const int64_t vec_end = lo + ((hi > lo ? hi - lo : 0) & ~int64_t(3));
@@ -132,6 +113,37 @@ __global__ void __launch_bounds__(kAccThreads, 1)
   }
   for (int64_t s = vec_end + threadIdx.x; s < hi; s += blockDim.x)
     acc_edge<BWD>(fwd, bwd, side_f, side_b, n, act, grad, dead[s], from[s], to[s], weight[s]);
+
+}
+
+// Kernel 1: every CTA sweeps a contiguous slot range into its shared
+// accumulators (forward lo[N] hi[N], backward lo[N] hi[N]); the cluster's
+// CTAs then split the units and each sums its share over every CTA of the
+// cluster (distributed shared memory) into the cluster's int64 row.
+template <bool BWD>
+__global__ void __launch_bounds__(kAccThreads, 1)
+    train_accumulate_kernel(int64_t cap, const int32_t *__restrict__ from, const int32_t *__restrict__ to,
+                            const uint8_t *__restrict__ dead, const float *__restrict__ weight,
+                            const float *__restrict__ act, const float *__restrict__ grad, int32_t n,
+                            const int64_t *__restrict__ tail, Scratch sc) {
+  extern __shared__ int32_t smem[];
+  int32_t *fwd = smem;              // lo[n], hi[n]
+  int32_t *bwd = smem + 2 * n;      // lo[n], hi[n] (BWD)
+  const int words = (BWD ? 4 : 2) * n;
+  for (int i = threadIdx.x; i < words; i += blockDim.x) smem[i] = 0;
+  __syncthreads();
+  float *side_f = sc.side, *side_b = sc.side + n;
+
+  // the swept slots: the capacity, or up to the arena's tail
+  int64_t limit = cap;
+  if (tail != nullptr) {
+    const int64_t ts = *tail;
+    limit = ts < 0 ? 0 : (ts < cap ? ts : cap);
+  }
+  const int64_t per_cta = ((limit + gridDim.x - 1) / gridDim.x + 3) & ~int64_t(3);
+  const int64_t lo = static_cast<int64_t>(blockIdx.x) * per_cta;
+  const int64_t hi = lo + per_cta < limit ? lo + per_cta : limit;
+  sweep_slots<BWD>(fwd, bwd, side_f, side_b, n, act, grad, from, to, dead, weight, lo, hi);
 
   cg::cluster_group cluster = cg::this_cluster();
   cluster.sync();  // every CTA of the cluster has swept
@@ -200,6 +212,40 @@ __device__ __forceinline__ float round_sum(long long f, float *side) {
   return a;
 }
 
+// One unit's applies from its exact sums (ff forward, fb backward): the
+// forward apply (inputs and pruned kept, src/plastax/sweep.py:332-338), the
+// MSE seed of an output, the backward apply (every unit but the pruned,
+// :444-449). side_f / side_b are the unit's float sides (read and reset).
+template <bool BWD>
+__device__ __forceinline__ void apply_unit(const ApplyArgs &a, int32_t u, long long ff, long long fb, float *side_f,
+                                           float *side_b) {
+  const uint8_t role = a.roles ? a.roles[u] : 0;
+  const bool pr = a.pruned != nullptr && a.pruned[u];
+  const float fa = round_sum(ff, side_f);
+  float act = a.act[u];
+  if (role != 1 && !pr) {
+    act = act_fn(unit_act_kind(a.fwd_act, role), fa);
+    a.act[u] = act;
+  }
+  float s = 0.0f;
+  if (a.seed != nullptr) {
+    const int32_t j = a.target_of[u];
+    if (j >= 0 && a.target != nullptr) {
+      s = __fsub_rn(act, a.target[j]);
+      a.seed[u] = s;
+    } else {
+      s = a.seed[u];
+    }
+  }
+  if (BWD) {
+    const float ba = round_sum(fb, side_b);
+    if (!pr) {
+      const uint8_t brole = role == 1 ? 0 : role;
+      a.grad[u] = __fmul_rn(__fadd_rn(ba, s), act_prime_from_act(unit_act_kind(a.bwd_act, brole), act));
+    }
+  }
+}
+
 // Kernel 2: per unit the forward apply (inputs and pruned kept,
 // src/plastax/sweep.py:332-338), the MSE seed of an output, the backward
 // apply (every unit but the pruned, :444-449).
@@ -212,41 +258,20 @@ __global__ void __launch_bounds__(kApplyThreads) train_apply_kernel(ApplyArgs a,
   const long long ff = rows_sum(sc.rows, a.rows, stride, u, lane, in);
   long long fb = 0;
   if (BWD) fb = rows_sum(sc.rows + a.n, a.rows, stride, u, lane, in);
-  if (in && lane == 0) {
-    const uint8_t role = a.roles ? a.roles[u] : 0;
-    const bool pr = a.pruned != nullptr && a.pruned[u];
-    const float fa = round_sum(ff, sc.side + u);
-    float act = a.act[u];
-    if (role != 1 && !pr) {
-      act = act_fn(unit_act_kind(a.fwd_act, role), fa);
-      a.act[u] = act;
-    }
-    float s = 0.0f;
-    if (a.seed != nullptr) {
-      const int32_t j = a.target_of[u];
-      if (j >= 0 && a.target != nullptr) {
-        s = __fsub_rn(act, a.target[j]);
-        a.seed[u] = s;
-      } else {
-        s = a.seed[u];
-      }
-    }
-    if (BWD) {
-      const float ba = round_sum(fb, sc.side + a.n + u);
-      if (!pr) {
-        const uint8_t brole = role == 1 ? 0 : role;
-        a.grad[u] = __fmul_rn(__fadd_rn(ba, s), act_prime_from_act(unit_act_kind(a.bwd_act, brole), act));
-      }
-    }
-  }
+  if (in && lane == 0) apply_unit<BWD>(a, u, ff, fb, sc.side + u, sc.side + a.n + u);
 }
 
+// COHERENT: the unit columns were written earlier in the same kernel (by
+// other CTAs of its cluster), so they are read through L2, not the
+// read-only path.
+template <bool COHERENT = false>
 __device__ __forceinline__ void update_edge(const OptParams &p, float *__restrict__ weight, float *m_col,
                                             float *v_col, float *t_col, const float *__restrict__ act,
                                             const float *__restrict__ ug, uint32_t n, int64_t s, uint8_t d,
                                             int32_t f, int32_t t, float w) {
   if (!live_edge(d, f, t, n)) return;
-  opt_step(p, __fmul_rn(__ldg(ug + t), __ldg(act + f)), w, m_col, v_col, t_col, s, f, t);
+  const float g = COHERENT ? __fmul_rn(__ldcg(ug + t), __ldcg(act + f)) : __fmul_rn(__ldg(ug + t), __ldg(act + f));
+  opt_step(p, g, w, m_col, v_col, t_col, s, f, t);
   weight[s] = w;
 }
 
@@ -257,7 +282,7 @@ __device__ __forceinline__ void loss_warp(const LossArgs &l) {
   float total = 0.0f;
   for (int32_t base = 0; base < l.num_outputs; base += 32) {
     const int32_t i = base + lane;
-    const float d = i < l.num_outputs ? l.seed[l.output_ids[i]] : 0.0f;
+    const float d = i < l.num_outputs ? __ldcg(l.seed + l.output_ids[i]) : 0.0f;  // through L2: written by other CTAs
     const float sq = __fmul_rn(__fmul_rn(0.5f, d), d);
     const int cnt = l.num_outputs - base < 32 ? l.num_outputs - base : 32;
     for (int j = 0; j < cnt; ++j) {
@@ -312,6 +337,64 @@ __global__ void __launch_bounds__(kUpdateThreads, 2)
   const int64_t rest = groups << 2;
   const int64_t s = rest + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (s < cap) update_edge(p, weight, m_col, v_col, t_col, act, ug, n, s, dead[s], from[s], to[s], weight[s]);
+}
+
+// The whole step in one launch for a small arena: one cluster of
+// kSmallCluster CTAs. Each CTA sweeps its slot range into its shared
+// accumulators; after a cluster barrier each CTA applies its share of the
+// units, summing every CTA's accumulators through distributed shared memory;
+// after a second barrier (its release / acquire orders the unit columns'
+// global writes for the whole cluster) each CTA updates the slots it swept
+// and one warp sums the loss. The barriers are the cluster's hardware
+// barrier: every thread of every CTA takes both.
+constexpr int kSmallCluster = 8;
+constexpr int64_t kSmallSlots = 1 << 16;  // the arenas this path takes
+
+template <bool BWD>
+__global__ void __launch_bounds__(kAccThreads, 1)
+    train_cluster_kernel(int64_t cap, const int32_t *__restrict__ from, const int32_t *__restrict__ to,
+                         const uint8_t *__restrict__ dead, float *__restrict__ weight, float *m_col, float *v_col,
+                         float *t_col, const int64_t *__restrict__ tail, ApplyArgs a, const float *ug, OptParams p,
+                         LossArgs l, Scratch sc) {
+  extern __shared__ int32_t smem[];
+  const int32_t n = a.n;
+  int32_t *fwd = smem;
+  int32_t *bwd = smem + 2 * n;
+  const int words = (BWD ? 4 : 2) * n;
+  for (int i = threadIdx.x; i < words; i += blockDim.x) smem[i] = 0;
+  __syncthreads();
+  int64_t limit = cap;
+  if (tail != nullptr) {
+    const int64_t ts = *tail;
+    limit = ts < 0 ? 0 : (ts < cap ? ts : cap);
+  }
+  cg::cluster_group cluster = cg::this_cluster();
+  const int cs = static_cast<int>(cluster.num_blocks());
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int64_t per = ((limit + cs - 1) / cs + 3) & ~int64_t(3);
+  const int64_t lo = rank * per;
+  const int64_t hi = lo + per < limit ? lo + per : limit;
+  sweep_slots<BWD>(fwd, bwd, sc.side, sc.side + n, n, a.act, a.grad, from, to, dead, weight, lo, hi);
+  cluster.sync();  // every CTA has swept
+  const int32_t share = (n + cs - 1) / cs;
+  const int32_t u0 = rank * share;
+  const int32_t u1 = u0 + share < n ? u0 + share : n;
+  for (int32_t u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
+    long long ff = 0, fb = 0;
+#pragma unroll
+    for (int q = 0; q < kSmallCluster; ++q) {
+      if (q >= cs) break;
+      const int32_t *peer = cluster.map_shared_rank(smem, q);
+      ff += (static_cast<long long>(peer[n + u]) << kTrainFrac) + peer[u];
+      if (BWD) fb += (static_cast<long long>(peer[3 * n + u]) << kTrainFrac) + peer[2 * n + u];
+    }
+    apply_unit<BWD>(a, u, ff, fb, sc.side + u, sc.side + n + u);
+  }
+  cluster.sync();  // every unit is applied; no CTA reads a peer's shared memory after this
+  if (l.loss != nullptr && rank == 0 && threadIdx.x < 32) loss_warp(l);
+  for (int64_t s = lo + threadIdx.x; s < hi; s += blockDim.x)
+    update_edge<true>(p, weight, m_col, v_col, t_col, a.act, ug, static_cast<uint32_t>(n), s, dead[s], from[s],
+                      to[s], weight[s]);
 }
 
 int32_t max_units(bool bwd) {
@@ -450,6 +533,33 @@ extern "C" int pxb_pipeline_train_step(const pxb_pipeline_train *t, void *stream
   PXB_REQUIRE(!t->loss || t->seed, "pxb_pipeline_train_step: the loss needs the seed column");
   cudaStream_t st = as_stream(stream);
   const Scratch sc = scratch_of(t->scratch, n);
+  const OptParams p{o.kind, o.lr, o.b1, o.b2, o.eps, o.weight_decay, nullptr};
+  const LossArgs l{t->num_outputs, t->output_ids, t->seed, t->loss};
+  if (t->cap <= kSmallSlots) {
+    // a small arena: the whole step as one cluster
+    ApplyArgs a{n,         0,          t->num_outputs, t->act,     t->grad,       t->seed,
+                t->roles,  t->pruned,  t->fwd_act,     t->bwd_act, t->target_of,  t->output_ids,
+                t->target, t->loss};
+    const size_t smem = static_cast<size_t>(bwd ? 4 : 2) * n * sizeof(int32_t);
+    auto kern = bwd ? train_cluster_kernel<true> : train_cluster_kernel<false>;
+    PXB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kSmallCluster);
+    cfg.blockDim = dim3(kAccThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = kSmallCluster;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    PXB_CUDA(cudaLaunchKernelEx(&cfg, kern, t->cap, t->from_id, t->to_id, t->dead, t->weight, t->opt_m, t->opt_v,
+                                t->opt_t, t->tail_start, a, static_cast<const float *>(t->update_grad), p, l, sc));
+    PXB_LAUNCHED("train_cluster_kernel");
+    return PXB_OK;
+  }
   int rows = 0;
   int rc = bwd ? launch_accumulate<true>(t, sc, st, &rows) : launch_accumulate<false>(t, sc, st, &rows);
   if (rc) return rc;
@@ -461,8 +571,6 @@ extern "C" int pxb_pipeline_train_step(const pxb_pipeline_train *t, void *stream
   if (bwd) train_apply_kernel<true><<<agrid, kApplyThreads, 0, st>>>(a, sc);
   else train_apply_kernel<false><<<agrid, kApplyThreads, 0, st>>>(a, sc);
   PXB_LAUNCHED("train_apply_kernel");
-  const LossArgs l{t->num_outputs, t->output_ids, t->seed, t->loss};
-  const OptParams p{o.kind, o.lr, o.b1, o.b2, o.eps, o.weight_decay, nullptr};
   const int64_t groups = (t->cap + 3) / 4;
   int ugrid = static_cast<int>((groups + 2 * kUpdateThreads - 1) / (2 * kUpdateThreads));
   const int cap_grid = sm_count() * 2;  // one wave: two CTAs per SM
