@@ -317,6 +317,7 @@ class _EventTimer:
         # the GPU busy while the host enqueues the call, so the events time
         # the kernels and not the host's launch gaps
         self.lead_cycles = lead_cycles
+        self.slots: list[int] = []
 
     def __call__(self, *a, **kw):
         import torch
@@ -330,6 +331,10 @@ class _EventTimer:
         out = self.fn(*a, **kw)
         e.record()
         self.events.append((s, e))
+        # the slots the call sweeps: its bucket's capacity (or the fused
+        # step's descriptor's)
+        a0 = a[0] if a else None
+        self.slots.append(int(a0["dead"].numel()) if isinstance(a0, dict) else int(getattr(a0, "cap", 0)))
         return out
 
     def ms(self) -> list[float]:
@@ -694,7 +699,9 @@ def training_case(kind: str, dev, steps: int):
             from plastax_b200 import Driver
 
             net, static, state = C.build_units(cfg, dev)
-            step = Driver(net, static, state, device=dev)
+            # the Driver's exactness checks every 10 steps (its check_every),
+            # the plain steps replayed from one graph per signature
+            step = Driver(net, static, state, device=dev, check_every=cfg.interval, graphs=True)
     else:
         raise ValueError(kind)
     if dev is not None:
@@ -761,11 +768,19 @@ def training_arm(args) -> None:
     for t in timers.values():
         t.on = True
     n_eager = min(Kst, 20)
+    inner = getattr(step, "_step", None) if driver else None
+    if inner is not None and hasattr(inner, "auto_graphs"):
+        inner.auto_graphs = False  # the timed steps run eagerly
+    timed_steps = 0  # eager steps whose edge passes were timed (a replayed graph's are not)
     for i in range(n_eager):
+        before = sum(len(t.events) for t in timers.values())
         run(W + i, X[W + i], T[W + i])
+        timed_steps += sum(len(t.events) for t in timers.values()) > before
     torch.cuda.synchronize()
     for t in timers.values():
         t.on = False
+    if inner is not None and hasattr(inner, "auto_graphs"):
+        inner.auto_graphs = bool(getattr(step, "_graphs", False))
     scan = bool(case.get("scan"))
     use_graph = (not driver) and hasattr(step, "capturable") and step.capturable()
     if scan:
@@ -857,20 +872,25 @@ def training_arm(args) -> None:
     swept = caps
     if st.tail_start is not None and "pipeline_train" in kinds:
         swept = min(caps, int(st.tail_start.item()))
+    # every timed call's algorithmic bytes over the slots it swept (calls
+    # replayed inside a graph are not timed and not counted)
     for nm in kinds:
-        bytes_total += pass_bytes[nm] * (swept if nm == "pipeline_train" else caps) * n_eager
+        for sl in timers[nm].slots:
+            bytes_total += pass_bytes[nm] * (min(sl, swept) if nm == "pipeline_train" else sl)
     achieved = bytes_total / (ms_total / 1e3) / 1e9 if ms_total else float("nan")
+    timed_steps = max(1, timed_steps)
     peak, peak_kind = measured_peak_hbm()
     roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "traffic": None, "kernel": "edge passes (" + ", ".join(kinds) + ")",
-            "alg_bytes_per_step": bytes_total / n_eager, "kernel_ms_per_step": ms_total / n_eager,
-            "share_of_step": (ms_total / n_eager) / (elapsed_ms / Kst), "peak_kind": peak_kind,
+            "alg_bytes_per_step": bytes_total / timed_steps, "kernel_ms_per_step": ms_total / timed_steps,
+            "share_of_step": (ms_total / timed_steps) / (elapsed_ms / Kst), "peak_kind": peak_kind,
+            "timed_eager_steps": timed_steps,
             "arena_slots": caps, "swept_slots": swept, "l2_resident": caps * 13 < 126e6,
             # the same step as the reference's separate passes over capacity
             "reference_pass_bytes_per_step": caps * sum(bps.values())}
     if batch > 1:
         flops = 3 * 2 * batch * live  # forward, backward and update products per edge per sample
-        tf = flops / ((ms_total / n_eager) / 1e3) / 1e12
+        tf = flops / ((ms_total / timed_steps) / 1e3) / 1e12
         roof["fp32"] = {"achieved_tflops": tf, "peak_tflops": FP32_NOMINAL_TFLOPS, "peak_kind": "nominal",
                         "frac": tf / FP32_NOMINAL_TFLOPS, "flops_per_step": flops}
     line = {

@@ -67,38 +67,40 @@ __global__ void kill_unit_edges_kernel(int64_t cap, const int32_t *__restrict__ 
   }
 }
 
-// Candidate values of the quantile: live, non-exempt units.
+// Candidate values of the quantile: live, non-exempt units (+inf for the
+// rest, so they sort last), counted per CTA into `count` (zeroed before).
 __global__ void quantile_gather_kernel(int32_t n, const float *__restrict__ field, const uint8_t *__restrict__ pruned,
-                                       const uint8_t *__restrict__ exempt, float *__restrict__ vals) {
-  for (int32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const bool cand = !(pruned != nullptr && pruned[i]) && !(exempt != nullptr && exempt[i]);
-    // excluded units sort after every candidate (+inf; a NaN value too)
-    const float v = field[i];
-    vals[i] = cand && !isnan(v) ? v : __int_as_float(0x7f800000);
-  }
-}
-
-__global__ void quantile_pick_kernel(int32_t n, const uint8_t *__restrict__ pruned, const uint8_t *__restrict__ exempt,
-                                     const float *__restrict__ field, const float *__restrict__ sorted, float q,
-                                     float *__restrict__ out) {
+                                       const uint8_t *__restrict__ exempt, float *__restrict__ vals,
+                                       int32_t *__restrict__ count) {
   __shared__ int32_t s_count;
   if (threadIdx.x == 0) s_count = 0;
   __syncthreads();
   int32_t local = 0;
-  for (int32_t i = threadIdx.x; i < n; i += blockDim.x)
-    local += (!(pruned != nullptr && pruned[i]) && !(exempt != nullptr && exempt[i]) && !isnan(field[i])) ? 1 : 0;
-  atomicAdd(&s_count, local);
+  for (int32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const bool cand = !(pruned != nullptr && pruned[i]) && !(exempt != nullptr && exempt[i]);
+    const float v = field[i];
+    vals[i] = cand && !isnan(v) ? v : __int_as_float(0x7f800000);
+    local += (cand && !isnan(v)) ? 1 : 0;
+  }
+  local = __reduce_add_sync(0xffffffffu, local);
+  if ((threadIdx.x & 31) == 0 && local) atomicAdd(&s_count, local);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const int32_t m = s_count;
-    if (m == 0) {
-      *out = -__int_as_float(0x7f800000);
-    } else {
-      int64_t r = static_cast<int64_t>(floor(static_cast<double>(q) * m));
-      if (r > m - 1) r = m - 1;
-      if (r < 0) r = 0;
-      *out = sorted[r];
-    }
+  if (threadIdx.x == 0 && s_count) atomicAdd(count, s_count);
+}
+
+// The quantile from the sorted candidates and their count (one thread):
+// the floor(q * m)-th smallest, -inf without a candidate.
+__global__ void quantile_pick_kernel(const int32_t *__restrict__ count, const float *__restrict__ sorted, float q,
+                                     float *__restrict__ out) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const int32_t m = *count;
+  if (m == 0) {
+    *out = -__int_as_float(0x7f800000);
+  } else {
+    int64_t r = static_cast<int64_t>(floor(static_cast<double>(q) * m));
+    if (r > m - 1) r = m - 1;
+    if (r < 0) r = 0;
+    *out = sorted[r];
   }
 }
 
@@ -236,7 +238,7 @@ extern "C" int pxb_unit_quantile_scratch_bytes(int32_t num_units, size_t *bytes)
   PXB_CUDA(cub::DeviceRadixSort::SortKeys(nullptr, tmp, static_cast<const float *>(nullptr),
                                           static_cast<float *>(nullptr), num_units > 0 ? num_units : 1));
   const size_t col = (size_t(num_units > 0 ? num_units : 1) * 4 + 255) / 256 * 256;
-  *bytes = 2 * col + tmp;
+  *bytes = 2 * col + 256 + tmp;  // values, sorted values, the candidates' count, the sort's temp
   return PXB_OK;
 }
 
@@ -252,14 +254,17 @@ extern "C" int pxb_unit_quantile(int32_t num_units, const float *field, const ui
   const size_t col = (size_t(num_units > 0 ? num_units : 1) * 4 + 255) / 256 * 256;
   float *vals = static_cast<float *>(scratch);
   float *sorted = reinterpret_cast<float *>(static_cast<char *>(scratch) + col);
-  void *tmp = static_cast<char *>(scratch) + 2 * col;
-  size_t tb = scratch_bytes - 2 * col;
+  int32_t *count = reinterpret_cast<int32_t *>(static_cast<char *>(scratch) + 2 * col);
+  void *tmp = static_cast<char *>(scratch) + 2 * col + 256;
+  size_t tb = scratch_bytes - 2 * col - 256;
+  PXB_CUDA(cudaMemsetAsync(count, 0, sizeof(int32_t), st));
   if (num_units > 0) {
-    quantile_gather_kernel<<<grid_for(num_units, 256, 4), 256, 0, st>>>(num_units, field, pruned, exempt, vals);
+    quantile_gather_kernel<<<grid_for(num_units, 256, 4), 256, 0, st>>>(num_units, field, pruned, exempt, vals,
+                                                                       count);
     PXB_LAUNCHED("quantile_gather_kernel");
     PXB_CUDA(cub::DeviceRadixSort::SortKeys(tmp, tb, vals, sorted, num_units, 0, 32, st));
   }
-  quantile_pick_kernel<<<1, 256, 0, st>>>(num_units, pruned, exempt, field, sorted, q, out);
+  quantile_pick_kernel<<<1, 32, 0, st>>>(count, sorted, q, out);
   PXB_LAUNCHED("quantile_pick_kernel");
   return PXB_OK;
 }

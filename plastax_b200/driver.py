@@ -78,13 +78,17 @@ class Driver:
 
     def __init__(self, net: type[Network], static: NetworkStatic, state: NetworkState, *, check_every: int = 1,
                  batch_size: int | None = None, layout: str = "auto", fuse_prune: str | bool = "auto",
-                 growth: str = "auto", device: torch.device | str = "cuda") -> None:
+                 growth: str = "auto", device: torch.device | str = "cuda", graphs: bool = False) -> None:
         if check_every < 1:
             raise ValueError(f"Driver: check_every must be >= 1, got {check_every}")
         self._net, self._static, self._state = net, static, state
         self._batch_size, self._layout, self._fuse_prune, self._growth = batch_size, layout, fuse_prune, growth
         self.dev = torch.device(device)
         self._resorts = net.propagation is Propagation.TOPOLOGICAL
+        # with graphs, a step whose periodic phases (growth, unit spawn,
+        # prune) follow a schedule replays one CUDA graph per signature
+        # (StepFn.auto_graphs); the steps that read the host stay eager
+        self._graphs = graphs
         self._check_every = check_every
         self._since_check = 0
         self._overflowed = torch.zeros((), dtype=torch.bool, device=self.dev)
@@ -226,8 +230,11 @@ class Driver:
             fn.invalidate()
 
     def _make_step(self):
-        return make_step(self._net, self._static, batch_size=self._batch_size, layout=self._layout,
-                         fuse_prune=self._fuse_prune, growth=self._growth, device=self.dev)
+        fn = make_step(self._net, self._static, batch_size=self._batch_size, layout=self._layout,
+                       fuse_prune=self._fuse_prune, growth=self._growth, device=self.dev)
+        if self._graphs and isinstance(fn, StepFn):
+            fn.auto_graphs = True
+        return fn
 
     def _rebuild(self) -> None:
         self._drop_loop()

@@ -1389,7 +1389,7 @@ class StepFn:
         that signature's graph (captured here at its second occurrence);
         returns (ran, remainder). Without it, counts the signature."""
         sig = self._signature(state)
-        entry = self._graphs.get(sig)
+        entry = self._graphs.get(sig) if self.auto_graphs else None
         if entry is None or entry[0] != id(state):
             if (not self.auto_graphs or self._sig_seen.get((sig, id(state)), 0) < 1
                     or not self._graph_safe(sig)):

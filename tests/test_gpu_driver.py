@@ -126,3 +126,59 @@ def test_scan_steps_and_validation(cuda):
     with pytest.raises(ValueError, match="record"):
         drv.scan(px.StepInputs(x, t), record="grown")
     drv.close()
+
+
+def test_driver_graphs_follow_the_eager_steps(cuda):
+    """Driver(graphs=True) on a unit-lifecycle net (a unit spawned every 10
+    steps, the units below the utility quantile pruned, UPGD, growth on the
+    interval): the steps between spawns replay one captured graph per
+    signature, the spawn steps run eagerly, and the run follows the all-eager
+    Driver: the same pruned units and spawns, weights within 1e-4."""
+    import torch
+
+    import plastax_b200 as px
+
+    TRACE = px.FieldSpec.float32("utility")
+    n_in, hidden, cap = 32, 2048, 4096
+
+    class Net(px.Network):
+        forward_pass = px.ForwardPass("relu")
+        backward_pass = px.BackwardPass("relu")
+        loss = px.MSELoss()
+        update_conn = px.optim.upgd(lr=0.01, beta=0.99, sigma=0.001)
+        update_unit = px.TraceUnitUpdate(TRACE, "activation", 0.05)
+        prune_unit = px.FieldBelowPrune(TRACE, quantile=0.01)
+        add_unit = px.ArgmaxSpawn(TRACE, offset=1)
+        add_conn = px.ProposeAddConn(proposals_per_proposer=8, max_new_per_level=64, dst_lo=n_in,
+                                     score="uniform", max_level_gap=2, direction="deeper")
+        extra_unit_fields = (TRACE,)
+        unit_capacity = cap
+        structural_interval = 10
+
+    rng = np.random.default_rng(4)
+    n = n_in + hidden + 1
+    src = np.concatenate([rng.integers(0, n_in, 8000), rng.integers(n_in, n_in + hidden, 4000)])
+    dst = np.concatenate([rng.integers(n_in, n_in + hidden, 8000), np.full(4000, n - 1)])
+    w = (rng.standard_normal(src.size) * 0.1).astype(np.float32)
+    xs = rng.standard_normal((25, n_in)).astype(np.float32)
+    runs = []
+    for graphs in (False, True):
+        static, state = px.NetworkBuilder.from_edges(Net, n, src, dst, weights=w, input_ids=tuple(range(n_in)),
+                                                     output_ids=(n - 1,), capacity_headroom=0.5, device=cuda)
+        drv = px.Driver(Net, static, state, device=cuda, graphs=graphs)
+        spawned = 0
+        for i in range(25):
+            drv.step(px.StepInputs(xs[i], np.array([xs[i, :4].sum()], np.float32)))
+            spawned += int(drv.state.units_added.item())
+        torch.cuda.synchronize()
+        if graphs:
+            assert len(drv._step._graphs) >= 1, "no step signature was captured"
+        runs.append((drv, spawned))
+    (a, sa), (b, sb) = runs
+    assert sa == sb == 3
+    np.testing.assert_array_equal(a.state.units["pruned"].cpu().numpy(), b.state.units["pruned"].cpu().numpy())
+    for ba, bb in zip(a.state.conns, b.state.conns, strict=True):
+        np.testing.assert_array_equal(ba["dead"].cpu().numpy(), bb["dead"].cpu().numpy())
+        np.testing.assert_allclose(ba["weight"].cpu().numpy(), bb["weight"].cpu().numpy(), rtol=1e-4, atol=1e-5)
+    a.close()
+    b.close()
