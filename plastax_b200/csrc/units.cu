@@ -88,20 +88,67 @@ __global__ void quantile_gather_kernel(int32_t n, const float *__restrict__ fiel
   if (threadIdx.x == 0 && s_count) atomicAdd(count, s_count);
 }
 
-// The quantile from the sorted candidates and their count (one thread):
-// the floor(q * m)-th smallest, -inf without a candidate.
-__global__ void quantile_pick_kernel(const int32_t *__restrict__ count, const float *__restrict__ sorted, float q,
-                                     float *__restrict__ out) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+// The quantile by a radix select (one CTA): the floor(q * m)-th smallest of
+// the m candidates (values with the order of their float bits: the
+// order a radix sort of floats gives, -0 before +0), three digit passes of
+// 11, 11 and 10 bits over every value, -inf without a candidate. Exactly
+// the element a full sort would put at that position.
+constexpr int kQsThreads = 1024;
+__device__ __forceinline__ uint32_t float_order(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float order_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+__global__ void __launch_bounds__(kQsThreads) quantile_select_kernel(int32_t n, const float *__restrict__ vals,
+                                                                     const int32_t *__restrict__ count, float q,
+                                                                     float *__restrict__ out) {
+  using Scan = cub::BlockScan<uint32_t, kQsThreads>;
+  __shared__ typename Scan::TempStorage scan_tmp;
+  __shared__ uint32_t hist[2048];
+  __shared__ uint32_t s_prefix, s_rank;
   const int32_t m = *count;
   if (m == 0) {
-    *out = -__int_as_float(0x7f800000);
-  } else {
+    if (threadIdx.x == 0) *out = -__int_as_float(0x7f800000);
+    return;
+  }
+  if (threadIdx.x == 0) {
     int64_t r = static_cast<int64_t>(floor(static_cast<double>(q) * m));
     if (r > m - 1) r = m - 1;
     if (r < 0) r = 0;
-    *out = sorted[r];
+    s_prefix = 0u;
+    s_rank = static_cast<uint32_t>(r);
   }
+  const int shifts[3] = {21, 10, 0}, widths[3] = {11, 11, 10};
+  uint32_t known = 0u;  // the mask of the key bits fixed so far
+  for (int pass = 0; pass < 3; ++pass) {
+    const int sh = shifts[pass], wd = widths[pass];
+    for (int i = threadIdx.x; i < 2048; i += kQsThreads) hist[i] = 0u;
+    __syncthreads();
+    const uint32_t prefix = s_prefix;
+    for (int32_t i = threadIdx.x; i < n; i += kQsThreads) {
+      const uint32_t k = float_order(vals[i]);
+      if ((k & known) == prefix) atomicAdd(&hist[(k >> sh) & ((1u << wd) - 1u)], 1u);
+    }
+    __syncthreads();
+    const uint32_t h0 = hist[2 * threadIdx.x], h1 = hist[2 * threadIdx.x + 1];
+    uint32_t ex, total;
+    Scan(scan_tmp).ExclusiveSum(h0 + h1, ex, total);
+    const uint32_t rank = s_rank;
+    __syncthreads();  // every thread has read s_rank
+    if (rank >= ex && rank < ex + h0) {
+      s_prefix = prefix | (static_cast<uint32_t>(2 * threadIdx.x) << sh);
+      s_rank = rank - ex;
+    } else if (rank >= ex + h0 && rank < ex + h0 + h1) {
+      s_prefix = prefix | (static_cast<uint32_t>(2 * threadIdx.x + 1) << sh);
+      s_rank = rank - ex - h0;
+    }
+    known |= ((1u << wd) - 1u) << sh;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *out = order_float(s_prefix);
 }
 
 // add_unit in one CTA: the free slots (PRUNED at the start of the phase,
@@ -234,11 +281,8 @@ extern "C" int pxb_unit_update(int32_t num_units, int32_t kind, float *field, co
 
 extern "C" int pxb_unit_quantile_scratch_bytes(int32_t num_units, size_t *bytes) {
   PXB_REQUIRE(bytes && num_units >= 0, "pxb_unit_quantile_scratch_bytes: bad arguments");
-  size_t tmp = 0;
-  PXB_CUDA(cub::DeviceRadixSort::SortKeys(nullptr, tmp, static_cast<const float *>(nullptr),
-                                          static_cast<float *>(nullptr), num_units > 0 ? num_units : 1));
   const size_t col = (size_t(num_units > 0 ? num_units : 1) * 4 + 255) / 256 * 256;
-  *bytes = 2 * col + 256 + tmp;  // values, sorted values, the candidates' count, the sort's temp
+  *bytes = col + 256;  // the candidates' values, their count
   return PXB_OK;
 }
 
@@ -253,18 +297,15 @@ extern "C" int pxb_unit_quantile(int32_t num_units, const float *field, const ui
   cudaStream_t st = as_stream(stream);
   const size_t col = (size_t(num_units > 0 ? num_units : 1) * 4 + 255) / 256 * 256;
   float *vals = static_cast<float *>(scratch);
-  float *sorted = reinterpret_cast<float *>(static_cast<char *>(scratch) + col);
-  int32_t *count = reinterpret_cast<int32_t *>(static_cast<char *>(scratch) + 2 * col);
-  void *tmp = static_cast<char *>(scratch) + 2 * col + 256;
-  size_t tb = scratch_bytes - 2 * col - 256;
+  int32_t *count = reinterpret_cast<int32_t *>(static_cast<char *>(scratch) + col);
   PXB_CUDA(cudaMemsetAsync(count, 0, sizeof(int32_t), st));
   if (num_units > 0) {
     quantile_gather_kernel<<<grid_for(num_units, 256, 4), 256, 0, st>>>(num_units, field, pruned, exempt, vals,
                                                                        count);
     PXB_LAUNCHED("quantile_gather_kernel");
-    PXB_CUDA(cub::DeviceRadixSort::SortKeys(tmp, tb, vals, sorted, num_units, 0, 32, st));
   }
-  quantile_pick_kernel<<<1, 32, 0, st>>>(count, sorted, q, out);
+  quantile_select_kernel<<<1, kQsThreads, 0, st>>>(num_units, vals, count, q, out);
+  PXB_LAUNCHED("quantile_select_kernel");
   PXB_LAUNCHED("quantile_pick_kernel");
   return PXB_OK;
 }
