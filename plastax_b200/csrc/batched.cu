@@ -312,13 +312,21 @@ __global__ void batch_mean_scalar_kernel(int32_t batch, const float *__restrict_
   loss[0] = __fdiv_rn(total, static_cast<float>(batch));
 }
 
-// out[u] = (sum_b x[u, b] in sample order) / B.
+// out[u] = (sum_b x[u, b] in sample order) / B, one warp per unit: the row
+// read 32 samples at a time (coalesced), the sum still taken one sample
+// after another (every lane adds the broadcast values in order).
 __global__ void batch_mean_rows_kernel(int32_t n, int32_t batch, const float *__restrict__ x, float *__restrict__ out) {
-  for (int32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < n; u += gridDim.x * blockDim.x) {
-    const float *row = x + static_cast<int64_t>(u) * batch;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t u = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; u < n; u += warps) {
+    const float *row = x + u * batch;
     float total = 0.0f;
-    for (int32_t b = 0; b < batch; ++b) total = __fadd_rn(total, row[b]);
-    out[u] = __fdiv_rn(total, static_cast<float>(batch));
+    for (int32_t b0 = 0; b0 < batch; b0 += 32) {
+      const float v = b0 + lane < batch ? row[b0 + lane] : 0.0f;
+      const int cnt = batch - b0 < 32 ? batch - b0 : 32;
+      for (int j = 0; j < cnt; ++j) total = __fadd_rn(total, __shfl_sync(0xffffffffu, v, j));
+    }
+    if (lane == 0) out[u] = __fdiv_rn(total, static_cast<float>(batch));
   }
 }
 
@@ -430,7 +438,7 @@ extern "C" int pxb_batch_mean(int32_t num_units, int32_t batch, const float *x, 
   PXB_REQUIRE(num_units >= 0 && batch >= 1, "pxb_batch_mean: bad sizes");
   if (num_units == 0) return PXB_OK;
   PXB_REQUIRE(x && out, "pxb_batch_mean: a pointer is NULL");
-  batch_mean_rows_kernel<<<grid_for(num_units, 256, 8), 256, 0, as_stream(stream)>>>(num_units, batch, x, out);
+  batch_mean_rows_kernel<<<grid_for(num_units, 8, 8), 256, 0, as_stream(stream)>>>(num_units, batch, x, out);
   PXB_LAUNCHED("batch_mean_rows_kernel");
   return PXB_OK;
 }
