@@ -644,6 +644,50 @@ PXB_API int pxb_propose_select_unique(
     int32_t *dst_out, float *weight_out, uint8_t *growable_out,
     int32_t *status, void *scratch, size_t scratch_bytes, void *stream);
 
+/* The same selection with the ranking of the full bins shared out over the
+ * ranks of a Scheme-A group (replaces the claim all-gather's replicated
+ * selection, src/plastax/phases.py:3046-3053, for this form). Every rank
+ * draws every proposal and finds the same threshold bin; rank r ranks the
+ * full (level, bin) pairs q = level * threshold_bin + bin with
+ * q % world == r and stores each of their winners into every rank's columns
+ * (peer memory, e.g. pxb_peer_open mappings), and each rank stores the
+ * threshold bin's winners and the zero fill past min(k, n) into its own.
+ * After every rank's call has completed and a barrier has ordered it before
+ * the reads (the combine's flags of pxb_scheme_a_apply, for a selection a
+ * step ahead), every rank's columns hold the list pxb_propose_select_unique
+ * returns. Each column holds `blocks` lists of k entries; a call fills list
+ * (step mod blocks), the step read from step_dev when it is set, so a
+ * captured graph rotates through them (three lists let a rank select step
+ * t + 1's while a slower peer still claims step t - 1's).
+ * pxb_select_take copies one list out. */
+#define PXB_SELECT_MAX_WORLD 8
+typedef struct pxb_select_shard {
+  int32_t rank, world; /* 1 <= world <= PXB_SELECT_MAX_WORLD */
+  int32_t blocks;      /* lists per column, >= 1 */
+  int32_t pad;
+  int32_t *src_out[PXB_SELECT_MAX_WORLD]; /* rank q's columns, blocks * k entries */
+  int32_t *dst_out[PXB_SELECT_MAX_WORLD];
+  float *weight_out[PXB_SELECT_MAX_WORLD];
+  uint8_t *growable_out[PXB_SELECT_MAX_WORLD];
+} pxb_select_shard;
+PXB_API int pxb_propose_select_unique_sharded(
+    int32_t num_units, uint64_t network_seed, int32_t step, int32_t dst_lo,
+    int32_t dst_n, int32_t score_kind, const int32_t *level,
+    const uint8_t *pruned, int32_t max_level_gap, int32_t direction,
+    int32_t allow_self_loops, int32_t src_level_bound,
+    const int32_t *step_dev, int64_t k, int32_t num_levels, int32_t init_kind,
+    float init_a, float init_b, uint32_t init_salt, const pxb_select_shard *shard,
+    int32_t *status, void *scratch, size_t scratch_bytes, void *stream);
+
+/* List (step mod blocks) of four columns of `blocks` lists of k entries
+ * (the step read from step_dev) copied into the claim's input columns, in
+ * one launch. */
+PXB_API int pxb_select_take(int64_t k, int32_t blocks, const int32_t *step_dev,
+                            const int32_t *src_col, const int32_t *dst_col,
+                            const float *weight_col, const uint8_t *growable_col,
+                            int32_t *src_out, int32_t *dst_out, float *weight_out,
+                            uint8_t *growable_out, void *stream);
+
 /* Growth dedupe (src/plastax/phases.py:4111-4205): the step's candidate
  * pairs in a hash table (scratch of pxb_dedupe_scratch_bytes(n), reset by
  * every pxb_pair_table_build). pxb_pair_table_mark passes over a bucket,
@@ -880,8 +924,8 @@ PXB_API int pxb_mirror_insert(const pxb_mirror *mirror, int64_t k,
  *   1. pxb_lowk_make_plan: from the histograms, the fine threshold bin b* of
  *      the k-th smallest key -- every edge in a bin below b* is pruned; of
  *      the bin itself the `take` smallest keys, unless the whole bin is
- *      needed (two launches: one CTA plans, a grid empties the fine bins
- *      the plan prunes);
+ *      needed (two launches: 64 CTAs sum the coarse bins and the last to
+ *      finish plans, a grid empties the fine bins the plan prunes);
  *   2. pxb_mirror_forward_lowk: the forward sweep; an edge below the bin is
  *      tombstoned there (as the fused threshold prune does), an edge in the
  *      bin is listed (key, source level, mirror position);
@@ -906,6 +950,7 @@ PXB_API int pxb_mirror_insert(const pxb_mirror *mirror, int64_t k,
 #define PXB_LOWK_BINS 65536
 #define PXB_LOWK_FINE_SHIFT 7
 #define PXB_LOWK_FINE_BINS 16777216
+#define PXB_LOWK_PLAN_SCRATCH 256
 
 typedef struct pxb_lowk_plan { /* device memory, written by pxb_lowk_make_plan */
   uint32_t lo_bits;     /* every live edge with bits(|w|) < lo_bits is pruned  */
@@ -942,6 +987,8 @@ typedef struct pxb_lowk {
   uint64_t *const *peer_key;
   int32_t *const *peer_level;
   unsigned long long *const *peer_count;
+  uint32_t *plan_scratch; /* [PXB_LOWK_PLAN_SCRATCH] device words for the plan's
+                             partial sums; zero them once before the first plan */
 } pxb_lowk;
 
 /* Both histograms += every live slot of a bucket whose weight is not NaN,
@@ -950,7 +997,7 @@ typedef struct pxb_lowk {
 PXB_API int pxb_lowk_hist_build(const pxb_lowk *lowk, int64_t cap,
                                 const uint8_t *dead, const float *weight,
                                 void *stream);
-/* Step 1 above; one CTA. */
+/* Step 1 above (64 CTAs; the last one to finish plans). */
 PXB_API int pxb_lowk_make_plan(const pxb_lowk *lowk, void *stream);
 /* Step 2 above: pxb_mirror_forward with the plan's prune; bitmap_level
  * (PIPELINE, else NULL) names the claim domain of a pruned or listed slot. */
@@ -960,6 +1007,24 @@ PXB_API int pxb_mirror_forward_lowk(const pxb_mirror *mirror, const float *act,
                                     uint8_t *dead, uint32_t *free_bitmap,
                                     int64_t bitmap_words,
                                     const int32_t *bitmap_level, void *stream);
+/* Step 2 in two parts, so the tombstones of the edges below the bin can be
+ * written beside step 3 on one GPU: pxb_mirror_forward_lowk_deferred runs the
+ * sweep and the mirror's overflow pass and leaves the sweep's deferred
+ * tombstones, which pxb_mirror_defer_flush (same mirror, monoid and lowk;
+ * any stream ordered after the sweep) writes. Together they do what
+ * pxb_mirror_forward_lowk does. */
+PXB_API int pxb_mirror_forward_lowk_deferred(const pxb_mirror *mirror,
+                                             const float *act, int32_t monoid,
+                                             float *acc, int64_t *acc_fixed,
+                                             const pxb_lowk *lowk, uint8_t *dead,
+                                             uint32_t *free_bitmap,
+                                             int64_t bitmap_words,
+                                             const int32_t *bitmap_level,
+                                             void *stream);
+PXB_API int pxb_mirror_defer_flush(const pxb_mirror *mirror, int32_t monoid,
+                                   const pxb_lowk *lowk, uint8_t *dead,
+                                   uint32_t *free_bitmap, int64_t bitmap_words,
+                                   const int32_t *bitmap_level, void *stream);
 /* Step 3 above; one CTA. level_before / level_totals ([num_levels], may be
  * NULL) receive every rank's selected edges per claim domain. */
 PXB_API int pxb_lowk_select(const pxb_lowk *lowk, const pxb_mirror *mirror,

@@ -33,6 +33,7 @@ ACT = {"identity": 0, "tanh": 1, "relu": 2, "sigmoid": 3}
 PRUNE_NONE, PRUNE_ABS_BELOW, PRUNE_ABS_BELOW_DST, PRUNE_LOWEST_K = 0, 1, 2, 3
 LOWK_BINS, LOWK_SHIFT = 65536, 15
 LOWK_FINE_BINS, LOWK_FINE_SHIFT = 1 << 24, 7
+LOWK_PLAN_SCRATCH = 256
 OPT = {"sgd": 0, "momentum": 1, "adam": 2, "rmsprop": 3, "upgd": 4}
 SCORE_UNIFORM, SCORE_UNIFORM_Q256, SCORE_GRAD_ACT = 0, 1, 2
 INIT_CONST, INIT_DYADIC, INIT_HASH_UNIFORM = 0, 1, 2
@@ -87,7 +88,20 @@ class Lowk(ctypes.Structure):
         ("rank", c_i32), ("world", c_i32), ("k", c_i64), ("list_cap", c_i64), ("slot_base", c_i64),
         ("hist", c_ptr), ("fine", c_ptr), ("plan", c_ptr), ("key", c_ptr), ("level", c_ptr), ("count", c_ptr),
         ("pos", c_ptr),
-        ("peer_key", c_ptr), ("peer_level", c_ptr), ("peer_count", c_ptr),
+        ("peer_key", c_ptr), ("peer_level", c_ptr), ("peer_count", c_ptr), ("plan_scratch", c_ptr),
+    ]
+
+
+SELECT_MAX_WORLD = 8
+
+
+class SelectShard(ctypes.Structure):
+    """`pxb_select_shard`: the ranks' winner columns of a shared selection."""
+
+    _fields_ = [
+        ("rank", c_i32), ("world", c_i32), ("blocks", c_i32), ("pad", c_i32),
+        ("src_out", c_ptr * SELECT_MAX_WORLD), ("dst_out", c_ptr * SELECT_MAX_WORLD),
+        ("weight_out", c_ptr * SELECT_MAX_WORLD), ("growable_out", c_ptr * SELECT_MAX_WORLD),
     ]
 
 
@@ -255,12 +269,19 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         c_i32, [c_i32, ctypes.c_uint64, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32,
                 c_ptr, c_i64, c_i32, c_i32, c_f32, c_f32, ctypes.c_uint32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr,
                 c_ptr, c_size, c_ptr]),
+    "pxb_propose_select_unique_sharded": (
+        c_i32, [c_i32, ctypes.c_uint64, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32,
+                c_ptr, c_i64, c_i32, c_i32, c_f32, c_f32, ctypes.c_uint32, c_ptr, c_ptr, c_ptr, c_size, c_ptr]),
+    "pxb_select_take": (c_i32, [c_i64, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_mirror_forward": (
         c_i32, [c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_i32, c_f32, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr]),
     "pxb_mirror_insert": (c_i32, [c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_lowk_hist_build": (c_i32, [c_ptr, c_i64, c_ptr, c_ptr, c_ptr]),
     "pxb_lowk_make_plan": (c_i32, [c_ptr, c_ptr]),
     "pxb_mirror_forward_lowk": (c_i32, [c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr]),
+    "pxb_mirror_forward_lowk_deferred": (c_i32, [c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr,
+                                                 c_ptr]),
+    "pxb_mirror_defer_flush": (c_i32, [c_ptr, c_i32, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr]),
     "pxb_lowk_select": (c_i32, [c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_i32, c_ptr, c_ptr, c_ptr]),
     "pxb_lowk_hist_add": (c_i32, [c_ptr, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_step_end": (c_i32, [c_ptr, c_ptr, c_ptr, c_ptr]),

@@ -30,6 +30,20 @@ namespace pxb {
 
 static inline size_t align_up_c(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// The level-major commit (candidates listed levels ascending, no per-step
+// cap) in four launches: per-block level counts, one plan block, the slot
+// lists, the placement. A claiming candidate's position, its level's run
+// and its spill rank all follow from the level counts, so no partition,
+// run or scan pass over the candidates is needed.
+constexpr int kLmThreads = 512;
+constexpr int kLmMaxLevels = 64;
+constexpr int kLmMaxBlocks = 1024;
+// [blocks][levels] counts, [blocks] offsets, [levels] spill bases
+static inline int64_t lm_words(int32_t num_levels) {
+  const int64_t l = num_levels < kLmMaxLevels ? num_levels : kLmMaxLevels;
+  return int64_t(kLmMaxBlocks) * l + kLmMaxBlocks + l;
+}
+
 constexpr int kClaimWarps = 8;         // warps per CTA in the tile kernels
 constexpr int kMaxLevels = 1024;       // per-warp shared counters
 constexpr int64_t kMaxMatrix = int64_t(1) << 24;
@@ -65,6 +79,7 @@ struct ClaimScratch {
   int32_t *cidx_in, *cidx_out;            // [k]
   int32_t *flag, *rank;                   // [k]
   int32_t *counts;                        // [8]
+  int32_t *lm;                            // level-major path: per-block level counts, offsets, spill bases
   void *cub_tmp;
   size_t cub_bytes, total;
 };
@@ -94,6 +109,7 @@ static int claim_scratch(const ClaimGeom &g, int64_t k, char *base, ClaimScratch
   o->flag = reinterpret_cast<int32_t *>(take(kk * 4));
   o->rank = reinterpret_cast<int32_t *>(take(kk * 4));
   o->counts = reinterpret_cast<int32_t *>(take(8 * 4));
+  o->lm = reinterpret_cast<int32_t *>(take(lm_words(g.num_levels) * 4));
   size_t t1 = 0, t2 = 0, t3 = 0, t4 = 0;
   if (cub::DeviceScan::ExclusiveSum(nullptr, t1, o->tile_counts, o->tile_offsets, static_cast<int>(m)) !=
       cudaSuccess)
@@ -314,6 +330,93 @@ __global__ void need_kernel(int32_t num_levels, const int32_t *__restrict__ firs
   need_off[num_levels] = acc;
 }
 
+struct LmGeom {
+  int64_t chunk;   // candidates per block, a multiple of kLmThreads
+  int32_t blocks;  // <= kLmMaxBlocks
+};
+
+static LmGeom lm_geom(int64_t k) {
+  LmGeom lg;
+  int64_t chunk = int64_t(kLmThreads) * 4;
+  if ((k + chunk - 1) / chunk > kLmMaxBlocks) chunk = (k + kLmMaxBlocks - 1) / kLmMaxBlocks;
+  chunk = (chunk + kLmThreads - 1) / kLmThreads * kLmThreads;
+  lg.chunk = chunk;
+  lg.blocks = static_cast<int32_t>((k + chunk - 1) / chunk);
+  if (lg.blocks < 1) lg.blocks = 1;
+  return lg;
+}
+
+// Pass 1: each block's claiming candidates per level (a warp adds each
+// level it saw once).
+__global__ void __launch_bounds__(kLmThreads) lm_count_kernel(CandArgs c, LmGeom lg, int32_t *__restrict__ lm) {
+  __shared__ int32_t cnt[kLmMaxLevels];
+  const int L = c.num_levels;
+  for (int l = threadIdx.x; l < L; l += blockDim.x) cnt[l] = 0;
+  __syncthreads();
+  const int64_t lo = static_cast<int64_t>(blockIdx.x) * lg.chunk;
+  const int64_t hi = lo + lg.chunk < c.k ? lo + lg.chunk : c.k;
+  for (int64_t base = lo; base < hi; base += blockDim.x) {
+    const int64_t i = base + threadIdx.x;
+    const bool g = i < hi && c.growable[i] != 0;
+    const int32_t l = g ? cand_level(c, i) : -1;
+    const unsigned active = __ballot_sync(0xffffffffu, g);
+    if (g) {
+      const unsigned peers = __match_any_sync(active, l);
+      if ((threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&cnt[l], __popc(peers));
+    }
+  }
+  __syncthreads();
+  for (int l = threadIdx.x; l < L; l += blockDim.x) lm[static_cast<int64_t>(blockIdx.x) * L + l] = cnt[l];
+}
+
+// One block: each block's first claiming position, the level runs, this
+// rank's needs per level and the spill bases; the commit's counters cleared.
+__global__ void __launch_bounds__(1024) lm_plan_kernel(CandArgs c, LmGeom lg, TotalsArgs t, int32_t *__restrict__ lm,
+                                                       int32_t *__restrict__ first, int32_t *__restrict__ end,
+                                                       int32_t *__restrict__ need, int32_t *__restrict__ need_off,
+                                                       int32_t *__restrict__ counts) {
+  using Scan = cub::BlockScan<int32_t, 1024>;
+  __shared__ typename Scan::TempStorage ts;
+  __shared__ int32_t cnt[kLmMaxLevels];
+  const int L = c.num_levels;
+  const int b = threadIdx.x;
+  int32_t *off = lm + static_cast<int64_t>(kLmMaxBlocks) * L;
+  int32_t *spill_base = off + kLmMaxBlocks;
+  for (int l = threadIdx.x; l < L; l += blockDim.x) cnt[l] = 0;
+  if (threadIdx.x < 8) counts[threadIdx.x] = 0;
+  __syncthreads();
+  int32_t tot = 0;
+  for (int l = 0; l < L; ++l) {
+    const int32_t v = b < lg.blocks ? lm[static_cast<int64_t>(b) * L + l] : 0;
+    tot += v;
+    const int32_t w = __reduce_add_sync(0xffffffffu, v);
+    if ((threadIdx.x & 31) == 0 && w) atomicAdd(&cnt[l], w);
+  }
+  int32_t ex, agg;
+  Scan(ts).ExclusiveSum(tot, ex, agg);
+  if (b < lg.blocks) off[b] = ex;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int32_t run = 0, acc = 0, spill = 0;
+    for (int l = 0; l < L; ++l) {
+      const int32_t kl = cnt[l], total = total_of(t, l);
+      first[l] = run;
+      end[l] = run + kl;
+      run += kl;
+      int32_t own = kl < total ? kl : total;
+      int32_t n = own - before_of(t, l);
+      if (n < 0) n = 0;
+      if (n > t.level_local[l]) n = t.level_local[l];
+      need[l] = n;
+      need_off[l] = acc;
+      acc += n;
+      spill_base[l] = spill;
+      if (kl > total) spill += kl - total;
+    }
+    need_off[L] = acc;
+  }
+}
+
 // list fill: the needed free slots of each domain, in slot order.
 __global__ void __launch_bounds__(kClaimWarps * 32) list_fill_kernel(
     DomainArgs a, ClaimGeom g, const int32_t *__restrict__ tile_offsets, const int32_t *__restrict__ level_base,
@@ -421,27 +524,23 @@ struct WriteArgs {
   uint8_t *committed;  // per candidate: 1 when committed on any rank, or NULL
 };
 
-// One thread per sorted claim position: choose the slot and write.
-__global__ void place_kernel(CandArgs c, WriteArgs w, const uint32_t *__restrict__ key,
-                             const int32_t *__restrict__ idx, const int32_t *__restrict__ first, TotalsArgs t,
-                             const int32_t *__restrict__ spill_rank, const int32_t *__restrict__ need,
-                             const int32_t *__restrict__ need_off, const int32_t *__restrict__ list,
-                             const float *__restrict__ cand_w, int32_t *__restrict__ counts,
-                             uint8_t *__restrict__ overflowed) {
-  const int64_t tail = w.topo ? 0 : *w.tail_start;
-  const int64_t tail_free = w.topo ? 0 : w.global_cap - tail;
-  // the counts, tallied per thread and added once per warp (one address
-  // takes every candidate's increment otherwise)
+struct PlaceTally {
+  int committed = 0, over = 0, tail = 0, resort = 0;
+};
+
+// Claiming candidate i of level l, own_rank-th of its level: its slot (its
+// level's own domain, else the tail at its spill rank), the columns written
+// when this rank holds the slot, the tallies. `spill_rank(i)` is read only
+// past the level's free count.
+template <class SpillRank>
+__device__ __forceinline__ void place_one(const CandArgs &c, const WriteArgs &w, const TotalsArgs &t, int64_t tail,
+                                          int64_t tail_free, int32_t i, uint32_t l, int32_t own_rank,
+                                          SpillRank spill_rank, const int32_t *__restrict__ need,
+                                          const int32_t *__restrict__ need_off, const int32_t *__restrict__ list,
+                                          const float *__restrict__ cand_w, uint8_t *__restrict__ overflowed,
+                                          PlaceTally &tl) {
   int n_committed = 0, n_over = 0, n_tail = 0, n_resort = 0;
-  for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < c.k;
-       p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const uint32_t l = key[p];
-    const int32_t i = idx[p];
-    if (overflowed) overflowed[i] = 0;
-    if (w.placed) w.placed[i] = -1;
-    if (w.committed) w.committed[i] = 0;
-    if (l >= static_cast<uint32_t>(c.num_levels)) continue;
-    const int32_t own_rank = static_cast<int32_t>(p) - first[l];
+  {
     int64_t slot = -1;
     bool committed = false, to_tail = false;
     if (own_rank < total_of(t, l)) {
@@ -449,7 +548,7 @@ __global__ void place_kernel(CandArgs c, WriteArgs w, const uint32_t *__restrict
       const int32_t r = own_rank - before_of(t, l);
       if (r >= 0 && r < need[l]) slot = list[need_off[l] + r];
     } else {
-      const int64_t sr = spill_rank[p];
+      const int64_t sr = spill_rank();
       if (sr < tail_free) {
         committed = true;
         to_tail = true;
@@ -485,13 +584,22 @@ __global__ void place_kernel(CandArgs c, WriteArgs w, const uint32_t *__restrict
       if (w.placed) w.placed[i] = static_cast<int32_t>(slot);
     }
   }
+  tl.committed += n_committed;
+  tl.over += n_over;
+  tl.tail += n_tail;
+  tl.resort += n_resort;
+}
+
+// The tallies added once per warp, then once per block (one address takes
+// every candidate's increment otherwise).
+__device__ __forceinline__ void add_tallies(PlaceTally tl, int32_t *__restrict__ counts) {
   __shared__ int s_counts[4];
   if (threadIdx.x < 4) s_counts[threadIdx.x] = 0;
   __syncthreads();
-  n_committed = __reduce_add_sync(0xffffffffu, n_committed);
-  n_over = __reduce_add_sync(0xffffffffu, n_over);
-  n_tail = __reduce_add_sync(0xffffffffu, n_tail);
-  n_resort = __reduce_add_sync(0xffffffffu, n_resort);
+  const int n_committed = __reduce_add_sync(0xffffffffu, tl.committed);
+  const int n_over = __reduce_add_sync(0xffffffffu, tl.over);
+  const int n_tail = __reduce_add_sync(0xffffffffu, tl.tail);
+  const int n_resort = __reduce_add_sync(0xffffffffu, tl.resort);
   if ((threadIdx.x & 31) == 0) {
     if (n_committed) atomicAdd(&s_counts[0], n_committed);
     if (n_over) atomicAdd(&s_counts[1], n_over);
@@ -500,6 +608,79 @@ __global__ void place_kernel(CandArgs c, WriteArgs w, const uint32_t *__restrict
   }
   __syncthreads();
   if (threadIdx.x < 4 && s_counts[threadIdx.x]) atomicAdd(counts + threadIdx.x, s_counts[threadIdx.x]);
+}
+
+// One thread per sorted claim position: choose the slot and write.
+__global__ void place_kernel(CandArgs c, WriteArgs w, const uint32_t *__restrict__ key,
+                             const int32_t *__restrict__ idx, const int32_t *__restrict__ first, TotalsArgs t,
+                             const int32_t *__restrict__ spill_rank, const int32_t *__restrict__ need,
+                             const int32_t *__restrict__ need_off, const int32_t *__restrict__ list,
+                             const float *__restrict__ cand_w, int32_t *__restrict__ counts,
+                             uint8_t *__restrict__ overflowed) {
+  const int64_t tail = w.topo ? 0 : *w.tail_start;
+  const int64_t tail_free = w.topo ? 0 : w.global_cap - tail;
+  PlaceTally tl;
+  for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < c.k;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t l = key[p];
+    const int32_t i = idx[p];
+    if (overflowed) overflowed[i] = 0;
+    if (w.placed) w.placed[i] = -1;
+    if (w.committed) w.committed[i] = 0;
+    if (l >= static_cast<uint32_t>(c.num_levels)) continue;
+    place_one(c, w, t, tail, tail_free, i, l, static_cast<int32_t>(p) - first[l],
+              [&] { return static_cast<int64_t>(spill_rank[p]); }, need, need_off, list, cand_w, overflowed, tl);
+  }
+  add_tallies(tl, counts);
+}
+
+// The level-major placement: candidate i's position among the claiming
+// candidates is its block's offset plus its rank inside the block (a block
+// scan per 512), its level's run starts at first[l], and past the level's
+// free count its spill rank is the spill base of its level plus its rank
+// among the level's spills.
+__global__ void __launch_bounds__(kLmThreads) lm_place_kernel(CandArgs c, WriteArgs w, LmGeom lg,
+                                                              const int32_t *__restrict__ lm,
+                                                              const int32_t *__restrict__ first, TotalsArgs t,
+                                                              const int32_t *__restrict__ need,
+                                                              const int32_t *__restrict__ need_off,
+                                                              const int32_t *__restrict__ list,
+                                                              const float *__restrict__ cand_w,
+                                                              int32_t *__restrict__ counts,
+                                                              uint8_t *__restrict__ overflowed) {
+  using Scan = cub::BlockScan<int32_t, kLmThreads>;
+  __shared__ typename Scan::TempStorage ts;
+  const int L = c.num_levels;
+  const int32_t *off = lm + static_cast<int64_t>(kLmMaxBlocks) * L;
+  const int32_t *spill_base = off + kLmMaxBlocks;
+  const int64_t tail = w.topo ? 0 : *w.tail_start;
+  const int64_t tail_free = w.topo ? 0 : w.global_cap - tail;
+  const int64_t lo = static_cast<int64_t>(blockIdx.x) * lg.chunk;
+  const int64_t hi = lo + lg.chunk < c.k ? lo + lg.chunk : c.k;
+  int32_t carry = off[blockIdx.x];
+  PlaceTally tl;
+  for (int64_t base = lo; base < hi; base += blockDim.x) {
+    const int64_t i = base + threadIdx.x;
+    const bool in = i < hi;
+    const bool g = in && c.growable[i] != 0;
+    int32_t ex, agg;
+    Scan(ts).ExclusiveSum(g ? 1 : 0, ex, agg);
+    if (in) {
+      if (overflowed) overflowed[i] = 0;
+      if (w.placed) w.placed[i] = -1;
+      if (w.committed) w.committed[i] = 0;
+    }
+    if (g) {
+      const int32_t l = cand_level(c, i);
+      const int32_t own_rank = carry + ex - first[l];
+      place_one(c, w, t, tail, tail_free, static_cast<int32_t>(i), static_cast<uint32_t>(l), own_rank,
+                [&] { return static_cast<int64_t>(spill_base[l]) + (own_rank - total_of(t, l)); }, need, need_off,
+                list, cand_w, overflowed, tl);
+    }
+    carry += agg;
+    __syncthreads();  // the scan's storage is reused
+  }
+  add_tallies(tl, counts);
 }
 
 __global__ void finish_kernel(int topo, int64_t *tail_start, const int32_t *__restrict__ counts,
@@ -683,6 +864,36 @@ extern "C" int pxb_claim_commit(int32_t mode, int64_t cap, int32_t *from_id, int
     w.extra_vals[e] = extra_vals[e];
   }
   cudaStream_t st = as_stream(stream);
+  if (k > 0 && level_major && max_new < 0 && num_levels <= kLmMaxLevels) {
+    // the level-major list without a per-step cap: four launches (the
+    // plan clears the counters)
+    CandArgs c{topo, k, cand_src, cand_dst, growable, unit_level, num_units, num_levels, max_new};
+    const LmGeom lg = lm_geom(k);
+    TotalsArgs t{o.level_local, level_before, level_totals};
+    lm_count_kernel<<<lg.blocks, kLmThreads, 0, st>>>(c, lg, o.lm);
+    PXB_LAUNCHED("lm_count_kernel");
+    lm_plan_kernel<<<1, 1024, 0, st>>>(c, lg, t, o.lm, o.level_first, o.level_end, o.need, o.need_off, o.counts);
+    PXB_LAUNCHED("lm_plan_kernel");
+    if (cap > 0) {
+      DomainArgs a{topo, cap, from_id, dead, unit_level, num_units, num_levels, shard_base, tail_start,
+                   free_bitmap, (cap + 31) / 32};
+      if (free_bitmap != nullptr) {
+        list_fill_bm_kernel<<<grid_for(g.tiles * g.num_levels, kClaimWarps, 4), kClaimWarps * 32, 0, st>>>(
+            a, g, o.tile_offsets, o.level_base, o.need, o.need_off, o.list);
+        PXB_LAUNCHED("list_fill_bm_kernel");
+      } else {
+        list_fill_kernel<<<grid_for(g.tiles, kClaimWarps, 4), kClaimWarps * 32, 0, st>>>(
+            a, g, o.tile_offsets, o.level_base, o.need, o.need_off, o.list);
+        PXB_LAUNCHED("list_fill_kernel");
+      }
+    }
+    lm_place_kernel<<<lg.blocks, kLmThreads, 0, st>>>(c, w, lg, o.lm, o.level_first, t, o.need, o.need_off, o.list,
+                                                       cand_weight, o.counts, overflowed_out);
+    PXB_LAUNCHED("lm_place_kernel");
+    finish_kernel<<<1, 32, 0, st>>>(topo, tail_start, o.counts, counts_out);
+    PXB_LAUNCHED("finish_kernel");
+    return PXB_OK;
+  }
   claim_reset_kernel<<<1, 128, 0, st>>>(o.counts, k > 0 ? o.level_first : nullptr, o.level_end, num_levels);
   PXB_LAUNCHED("claim_reset_kernel");
   if (k > 0) {

@@ -626,6 +626,33 @@ struct FsScratch {
   size_t total;
 };
 
+// Where the winners go: `world` ranks' columns of `blocks` lists of k
+// entries each (one rank and one list for the plain selection). Rank `rank`
+// ranks the full (level, bin) pairs q with q % world == rank and stores
+// their winners into every rank's columns; the threshold bin and the zero
+// fill are computed by every rank and stored into its own only.
+constexpr int kSelMaxWorld = PXB_SELECT_MAX_WORLD;
+struct FsOut {
+  int32_t rank, world, blocks, step;  // step: the list's step when step_dev is NULL
+  const int32_t *step_dev;
+  int32_t *s[kSelMaxWorld];
+  int32_t *d[kSelMaxWorld];
+  float *w[kSelMaxWorld];
+  uint8_t *g[kSelMaxWorld];
+};
+
+// Offset of this launch's list inside a column: (step mod blocks) * k.
+__device__ __forceinline__ int64_t fs_list_base(const FsOut &out, int64_t k) {
+  if (out.blocks <= 1) return 0;
+  const int32_t st = out.step_dev != nullptr ? *out.step_dev : out.step;
+  const int32_t b = ((st % out.blocks) + out.blocks) % out.blocks;
+  return static_cast<int64_t>(b) * k;
+}
+
+__device__ __forceinline__ bool fs_owns(int32_t rank, int32_t world, int64_t pair) {
+  return world <= 1 || pair % world == rank;
+}
+
 __device__ __forceinline__ uint64_t fs_key(const FsGeom &g, int kind, float score, int32_t src) {
   const uint64_t s = static_cast<uint32_t>(src);
   if (!(score >= 0.0f)) return (uint64_t(1) << (g.key_bits - 1)) | (s << g.score_bits);
@@ -743,14 +770,16 @@ __global__ void __launch_bounds__(1024) fs_threshold_kernel(FsGeom g, FsScratch 
 }
 
 __global__ void __launch_bounds__(kFsThreads) fs_scatter_kernel(FsGeom g, const int32_t *__restrict__ level,
-                                                                 FsScratch o) {
+                                                                 FsScratch o, int32_t rank, int32_t world) {
   const int32_t tb = o.info->tb;
   for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < g.n;
        c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const uint64_t key = o.keys[c];
     const int32_t b = fs_bin(g, key);
     if (b < tb) {
-      const int32_t slot = fs_level(g, level, fs_src(g, key)) * g.nb + b;
+      const int32_t l = fs_level(g, level, fs_src(g, key));
+      if (!fs_owns(rank, world, static_cast<int64_t>(l) * tb + b)) continue;  // another rank ranks this pair
+      const int32_t slot = l * g.nb + b;
       const uint32_t pos = o.toff[slot] + static_cast<uint32_t>(o.byrank[c]);
       o.bk[pos] = key;
       o.bi[pos] = static_cast<int32_t>(c);
@@ -783,27 +812,33 @@ __device__ __forceinline__ bool fs_rank(const uint64_t *keys_g, int32_t m, uint6
   return true;
 }
 
+// Winner `key` (candidate c) at list position pos: into this rank's list,
+// or into every rank's when `every` (a full bin this rank ranks).
 __device__ __forceinline__ void fs_emit(const FsGeom &g, const FsScratch &o, const InitArgs &ia, uint64_t key,
-                                        int32_t c, int64_t pos, int32_t *s_out, int32_t *d_out, float *w_out,
-                                        uint8_t *grow_out) {
+                                        int32_t c, int64_t pos, const FsOut &out, bool every) {
   const int32_t s = fs_src(g, key), d = o.dst[c];
-  s_out[pos] = s;
-  d_out[pos] = d;
-  w_out[pos] = init_weight(ia, s, d);
-  grow_out[pos] = fs_valid(g, key) ? 1 : 0;
+  const float w = init_weight(ia, s, d);
+  const uint8_t grow = fs_valid(g, key) ? 1 : 0;
+  const int q0 = every ? 0 : out.rank, q1 = every ? out.world : out.rank + 1;
+  for (int q = q0; q < q1; ++q) {
+    out.s[q][pos] = s;
+    out.d[q][pos] = d;
+    out.w[q][pos] = w;
+    out.g[q][pos] = grow;
+  }
 }
 
 // One block: the threshold bin's best r, their level counts, the level
 // bases of the final list, and the zero fill past min(k, n).
 __global__ void __launch_bounds__(1024) fs_threshold_bin_kernel(FsGeom g, const int32_t *__restrict__ level,
-                                                                InitArgs ia, FsScratch o, int32_t *s_out,
-                                                                int32_t *d_out, float *w_out, uint8_t *grow_out,
+                                                                InitArgs ia, FsScratch o, FsOut out,
                                                                 int32_t *status) {
   using Scan = cub::BlockScan<int32_t, 1024>;
   __shared__ typename Scan::TempStorage ts;
   __shared__ uint64_t keys_s[kFsRankCap];
   __shared__ int32_t s_carry;
   FsInfo *info = o.info;
+  const int64_t list = fs_list_base(out, g.k);
   const int32_t m = info->tcount;
   int32_t r = info->r;
   int32_t *rank = o.ti + g.n;  // member ranks, then level positions (the scratch holds 3n)
@@ -846,14 +881,14 @@ __global__ void __launch_bounds__(1024) fs_threshold_bin_kernel(FsGeom g, const 
     const int32_t e = o.byrank[p];
     const uint64_t key = o.tk[e];
     const int32_t l = fs_level(g, level, fs_src(g, key));
-    fs_emit(g, o, ia, key, o.ti[e], F[l] + info->C[l] + rank[g.n + p], s_out, d_out, w_out, grow_out);
+    fs_emit(g, o, ia, key, o.ti[e], list + F[l] + info->C[l] + rank[g.n + p], out, false);
   }
   const int64_t filled = r == info->r ? info->count : run;
   for (int64_t p = filled + threadIdx.x; p < g.k; p += blockDim.x) {
-    s_out[p] = 0;
-    d_out[p] = 0;
-    w_out[p] = 0.0f;
-    grow_out[p] = 0;
+    out.s[out.rank][list + p] = 0;
+    out.d[out.rank][list + p] = 0;
+    out.w[out.rank][list + p] = 0.0f;
+    out.g[out.rank][list + p] = 0;
   }
   if (threadIdx.x == 0)
     for (int l = 0; l < g.L; ++l) {
@@ -869,44 +904,51 @@ __global__ void __launch_bounds__(1024) fs_threshold_bin_kernel(FsGeom g, const 
 // take them one after another, each a chain of loads and barriers).
 constexpr int kFsWarpCap = 512;
 constexpr int kFsWarps = kFsThreads / 32;
-__global__ void __launch_bounds__(kFsThreads) fs_bins_warp_kernel(FsGeom g, InitArgs ia, FsScratch o,
-                                                                  int32_t *s_out, int32_t *d_out, float *w_out,
-                                                                  uint8_t *grow_out) {
+__global__ void __launch_bounds__(kFsThreads) fs_bins_warp_kernel(FsGeom g, InitArgs ia, FsScratch o, FsOut out) {
   __shared__ uint64_t keys_s[kFsWarps][kFsWarpCap];
   const FsInfo *info = o.info;
   const int32_t tb = info->tb < g.nb ? info->tb : g.nb;
   const int64_t pairs = static_cast<int64_t>(g.L) * tb;
+  const int64_t list = fs_list_base(out, g.k);
+  const int32_t world = out.world > 1 ? out.world : 1, me = out.world > 1 ? out.rank : 0;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint64_t *ks = keys_s[w];
-  for (int64_t q = static_cast<int64_t>(blockIdx.x) * kFsWarps + w; q < pairs;
-       q += static_cast<int64_t>(gridDim.x) * kFsWarps) {
+  // this rank's pairs: q = me, me + world, ...
+  for (int64_t j = static_cast<int64_t>(blockIdx.x) * kFsWarps + w; j * world + me < pairs;
+       j += static_cast<int64_t>(gridDim.x) * kFsWarps) {
+    const int64_t q = j * world + me;
     const int32_t l = static_cast<int32_t>(q / tb), b = static_cast<int32_t>(q % tb);
     const int32_t m = static_cast<int32_t>(o.hist[fs_hidx(static_cast<int64_t>(l) * g.nb + b)]);
     if (m == 0 || m > kFsWarpCap) continue;  // larger bins: fs_bins_kernel
     const uint32_t t0 = o.toff[l * g.nb + b];
     for (int e = lane; e < m; e += 32) ks[e] = o.bk[t0 + e];
     __syncwarp();
-    const int64_t base = static_cast<int64_t>(info->F[l]) + (t0 - info->T[l]);
+    const int64_t base = list + static_cast<int64_t>(info->F[l]) + (t0 - info->T[l]);
     for (int e = lane; e < m; e += 32) {
       const uint64_t ke = ks[e];
       int32_t r = 0;
       for (int f = 0; f < m; ++f) r += ks[f] < ke ? 1 : 0;
-      fs_emit(g, o, ia, ke, o.bi[t0 + e], base + r, s_out, d_out, w_out, grow_out);
+      fs_emit(g, o, ia, ke, o.bi[t0 + e], base + r, out, true);
     }
     __syncwarp();
   }
+  // the peers' stores are made visible before the kernel ends (a later
+  // release on this GPU's stream publishes them)
+  if (world > 1) __threadfence_system();
 }
 
 // The full bins larger than a warp's share, each (level, bin) pair ranked
 // by a CTA and emitted at its final position.
-__global__ void __launch_bounds__(kFsThreads) fs_bins_kernel(FsGeom g, InitArgs ia, FsScratch o, int32_t *s_out,
-                                                             int32_t *d_out, float *w_out, uint8_t *grow_out,
+__global__ void __launch_bounds__(kFsThreads) fs_bins_kernel(FsGeom g, InitArgs ia, FsScratch o, FsOut out,
                                                              int32_t *rank_scratch, int32_t *status) {
   __shared__ uint64_t keys_s[kFsRankCap];
   const FsInfo *info = o.info;
   const int32_t tb = info->tb < g.nb ? info->tb : g.nb;
   const int64_t pairs = static_cast<int64_t>(g.L) * tb;
-  for (int64_t q = blockIdx.x; q < pairs; q += gridDim.x) {
+  const int64_t list = fs_list_base(out, g.k);
+  const int32_t world = out.world > 1 ? out.world : 1, me = out.world > 1 ? out.rank : 0;
+  for (int64_t j = blockIdx.x; j * world + me < pairs; j += gridDim.x) {
+    const int64_t q = j * world + me;
     const int32_t l = static_cast<int32_t>(q / tb), b = static_cast<int32_t>(q % tb);
     const int32_t m = static_cast<int32_t>(o.hist[fs_hidx(static_cast<int64_t>(l) * g.nb + b)]);
     if (m <= kFsWarpCap) continue;  // fs_bins_warp_kernel's
@@ -916,11 +958,12 @@ __global__ void __launch_bounds__(kFsThreads) fs_bins_kernel(FsGeom g, InitArgs 
       if (threadIdx.x == 0 && status) atomicOr(status, 1);
       continue;
     }
-    const int64_t base = static_cast<int64_t>(info->F[l]) + (t0 - info->T[l]);
+    const int64_t base = list + static_cast<int64_t>(info->F[l]) + (t0 - info->T[l]);
     for (int e = threadIdx.x; e < m; e += blockDim.x)
-      fs_emit(g, o, ia, o.bk[t0 + e], o.bi[t0 + e], base + rank[e], s_out, d_out, w_out, grow_out);
+      fs_emit(g, o, ia, o.bk[t0 + e], o.bi[t0 + e], base + rank[e], out, true);
     __syncthreads();
   }
+  if (world > 1) __threadfence_system();
 }
 
 static int fs_geom(int32_t num_units, int64_t k, int32_t num_levels, int32_t score_kind, FsGeom *g) {
@@ -1213,6 +1256,60 @@ extern "C" int pxb_select_unique_scratch_bytes(int32_t num_units, int64_t k, int
   return PXB_OK;
 }
 
+// The fused selection's launches (both entry points): the proposals and
+// threshold bin on every rank, the full bins this rank ranks, the winners
+// into `out`.
+static int fs_run(const char *fn, int32_t num_units, uint64_t network_seed, int32_t step, int32_t dst_lo,
+                  int32_t dst_n, int32_t score_kind, const int32_t *level, const uint8_t *pruned,
+                  int32_t max_level_gap, int32_t direction, int32_t allow_self_loops, int32_t src_level_bound,
+                  const int32_t *step_dev, int64_t k, int32_t num_levels, int32_t init_kind, float init_a,
+                  float init_b, uint32_t init_salt, FsOut out, int32_t *status, void *scratch,
+                  size_t scratch_bytes, void *stream) {
+  PXB_REQUIRE(num_units >= 1 && k >= 0, "%s: bad sizes", fn);
+  PXB_REQUIRE(num_levels >= 1 && num_levels <= kFsMaxLevels, "%s: num_levels %d not in [1, %d]", fn, num_levels,
+              kFsMaxLevels);
+  PXB_REQUIRE(score_kind == PXB_SCORE_UNIFORM || score_kind == PXB_SCORE_UNIFORM_Q256,
+              "%s: the score must be uniform or uniform_q256", fn);
+  PXB_REQUIRE(dst_n >= 1 && dst_lo >= 0 && int64_t(dst_lo) + dst_n <= num_units,
+              "%s: destinations [%d, %lld) exceed the %d units", fn, dst_lo,
+              static_cast<long long>(dst_lo) + dst_n, num_units);
+  PXB_REQUIRE(init_kind >= 0 && init_kind <= 2, "%s: unknown init kind %d", fn, init_kind);
+  if (k == 0) return PXB_OK;
+  PXB_REQUIRE(level && scratch, "%s: a pointer is NULL", fn);
+  for (int q = 0; q < out.world; ++q)
+    PXB_REQUIRE(out.s[q] && out.d[q] && out.w[q] && out.g[q], "%s: rank %d's output column is NULL", fn, q);
+  FsGeom g;
+  if (fs_geom(num_units, k, num_levels, score_kind, &g) != PXB_OK) {
+    set_error("%s: %d units need too many key bits", fn, num_units);
+    return PXB_EINVAL;
+  }
+  FsScratch o;
+  fs_layout(g, static_cast<char *>(scratch), &o);
+  PXB_REQUIRE(o.total <= scratch_bytes, "%s: scratch has %zu bytes, needs %zu", fn, scratch_bytes, o.total);
+  ProposeArgs a{num_units, 1, 0, network_seed, step_dev, dst_lo, dst_n, score_kind, nullptr, nullptr, level,
+                pruned, max_level_gap, direction, allow_self_loops, -1, src_level_bound};
+  if (step_dev == nullptr) a.keyed_hi = philox32(network_seed, (static_cast<uint64_t>(static_cast<uint32_t>(step)) << 8) | 1u);
+  InitArgs ia{init_kind, init_a, init_b, init_salt};
+  out.step = step;
+  out.step_dev = step_dev;
+  cudaStream_t st = as_stream(stream);
+  PXB_CUDA(cudaMemsetAsync(o.hist, 0, size_t(g.L) * g.nb * 4 * kFsHistStride, st));
+  const int grid = grid_for(num_units, kFsThreads, 8);
+  fs_propose_kernel<<<grid, kFsThreads, 0, st>>>(a, g, o);
+  PXB_LAUNCHED("fs_propose_kernel");
+  fs_threshold_kernel<<<1, 1024, 0, st>>>(g, o);
+  PXB_LAUNCHED("fs_threshold_kernel");
+  fs_scatter_kernel<<<grid, kFsThreads, 0, st>>>(g, level, o, out.rank, out.world);
+  PXB_LAUNCHED("fs_scatter_kernel");
+  fs_threshold_bin_kernel<<<1, 1024, 0, st>>>(g, level, ia, o, out, status);
+  PXB_LAUNCHED("fs_threshold_bin_kernel");
+  fs_bins_warp_kernel<<<sm_count() * 8, kFsThreads, 0, st>>>(g, ia, o, out);
+  PXB_LAUNCHED("fs_bins_warp_kernel");
+  fs_bins_kernel<<<sm_count() * 2, kFsThreads, 0, st>>>(g, ia, o, out, o.bi + (g.k > 0 ? g.k : 1), status);
+  PXB_LAUNCHED("fs_bins_kernel");
+  return PXB_OK;
+}
+
 extern "C" int pxb_propose_select_unique(int32_t num_units, uint64_t network_seed, int32_t step, int32_t dst_lo,
                                          int32_t dst_n, int32_t score_kind, const int32_t *level,
                                          const uint8_t *pruned, int32_t max_level_gap, int32_t direction,
@@ -1221,48 +1318,78 @@ extern "C" int pxb_propose_select_unique(int32_t num_units, uint64_t network_see
                                          float init_a, float init_b, uint32_t init_salt, int32_t *src_out,
                                          int32_t *dst_out, float *weight_out, uint8_t *growable_out,
                                          int32_t *status, void *scratch, size_t scratch_bytes, void *stream) {
-  PXB_REQUIRE(num_units >= 1 && k >= 0, "pxb_propose_select_unique: bad sizes");
-  PXB_REQUIRE(num_levels >= 1 && num_levels <= kFsMaxLevels, "pxb_propose_select_unique: num_levels %d not in [1, %d]",
-              num_levels, kFsMaxLevels);
-  PXB_REQUIRE(score_kind == PXB_SCORE_UNIFORM || score_kind == PXB_SCORE_UNIFORM_Q256,
-              "pxb_propose_select_unique: the score must be uniform or uniform_q256");
-  PXB_REQUIRE(dst_n >= 1 && dst_lo >= 0 && int64_t(dst_lo) + dst_n <= num_units,
-              "pxb_propose_select_unique: destinations [%d, %lld) exceed the %d units", dst_lo,
-              static_cast<long long>(dst_lo) + dst_n, num_units);
-  PXB_REQUIRE(init_kind >= 0 && init_kind <= 2, "pxb_propose_select_unique: unknown init kind %d", init_kind);
-  if (k == 0) return PXB_OK;
-  PXB_REQUIRE(level && src_out && dst_out && weight_out && growable_out && scratch,
-              "pxb_propose_select_unique: a pointer is NULL");
-  FsGeom g;
-  if (fs_geom(num_units, k, num_levels, score_kind, &g) != PXB_OK) {
-    set_error("pxb_propose_select_unique: %d units need too many key bits", num_units);
-    return PXB_EINVAL;
+  FsOut out{};
+  out.rank = 0;
+  out.world = 1;
+  out.blocks = 1;
+  out.s[0] = src_out;
+  out.d[0] = dst_out;
+  out.w[0] = weight_out;
+  out.g[0] = growable_out;
+  return fs_run("pxb_propose_select_unique", num_units, network_seed, step, dst_lo, dst_n, score_kind, level,
+                pruned, max_level_gap, direction, allow_self_loops, src_level_bound, step_dev, k, num_levels,
+                init_kind, init_a, init_b, init_salt, out, status, scratch, scratch_bytes, stream);
+}
+
+extern "C" int pxb_propose_select_unique_sharded(int32_t num_units, uint64_t network_seed, int32_t step,
+                                                 int32_t dst_lo, int32_t dst_n, int32_t score_kind,
+                                                 const int32_t *level, const uint8_t *pruned, int32_t max_level_gap,
+                                                 int32_t direction, int32_t allow_self_loops,
+                                                 int32_t src_level_bound, const int32_t *step_dev, int64_t k,
+                                                 int32_t num_levels, int32_t init_kind, float init_a, float init_b,
+                                                 uint32_t init_salt, const pxb_select_shard *shard, int32_t *status,
+                                                 void *scratch, size_t scratch_bytes, void *stream) {
+  PXB_REQUIRE(shard != nullptr, "pxb_propose_select_unique_sharded: shard is NULL");
+  PXB_REQUIRE(shard->world >= 1 && shard->world <= kSelMaxWorld && shard->rank >= 0 && shard->rank < shard->world,
+              "pxb_propose_select_unique_sharded: rank %d of world %d (at most %d ranks)", shard->rank, shard->world,
+              kSelMaxWorld);
+  PXB_REQUIRE(shard->blocks >= 1, "pxb_propose_select_unique_sharded: blocks %d < 1", shard->blocks);
+  FsOut out{};
+  out.rank = shard->rank;
+  out.world = shard->world;
+  out.blocks = shard->blocks;
+  for (int q = 0; q < shard->world; ++q) {
+    out.s[q] = shard->src_out[q];
+    out.d[q] = shard->dst_out[q];
+    out.w[q] = shard->weight_out[q];
+    out.g[q] = shard->growable_out[q];
   }
-  FsScratch o;
-  fs_layout(g, static_cast<char *>(scratch), &o);
-  PXB_REQUIRE(o.total <= scratch_bytes, "pxb_propose_select_unique: scratch has %zu bytes, needs %zu",
-              scratch_bytes, o.total);
-  ProposeArgs a{num_units, 1, 0, network_seed, step_dev, dst_lo, dst_n, score_kind, nullptr, nullptr, level,
-                pruned, max_level_gap, direction, allow_self_loops, -1, src_level_bound};
-  if (step_dev == nullptr) a.keyed_hi = philox32(network_seed, (static_cast<uint64_t>(static_cast<uint32_t>(step)) << 8) | 1u);
-  InitArgs ia{init_kind, init_a, init_b, init_salt};
-  cudaStream_t st = as_stream(stream);
-  PXB_CUDA(cudaMemsetAsync(o.hist, 0, size_t(g.L) * g.nb * 4 * kFsHistStride, st));
-  const int grid = grid_for(num_units, kFsThreads, 8);
-  fs_propose_kernel<<<grid, kFsThreads, 0, st>>>(a, g, o);
-  PXB_LAUNCHED("fs_propose_kernel");
-  fs_threshold_kernel<<<1, 1024, 0, st>>>(g, o);
-  PXB_LAUNCHED("fs_threshold_kernel");
-  fs_scatter_kernel<<<grid, kFsThreads, 0, st>>>(g, level, o);
-  PXB_LAUNCHED("fs_scatter_kernel");
-  fs_threshold_bin_kernel<<<1, 1024, 0, st>>>(g, level, ia, o, src_out, dst_out, weight_out, growable_out, status);
-  PXB_LAUNCHED("fs_threshold_bin_kernel");
-  fs_bins_warp_kernel<<<sm_count() * 8, kFsThreads, 0, st>>>(g, ia, o, src_out, dst_out, weight_out,
-                                                               growable_out);
-  PXB_LAUNCHED("fs_bins_warp_kernel");
-  fs_bins_kernel<<<sm_count() * 2, kFsThreads, 0, st>>>(g, ia, o, src_out, dst_out, weight_out, growable_out,
-                                                        o.bi + (g.k > 0 ? g.k : 1), status);
-  PXB_LAUNCHED("fs_bins_kernel");
+  return fs_run("pxb_propose_select_unique_sharded", num_units, network_seed, step, dst_lo, dst_n, score_kind,
+                level, pruned, max_level_gap, direction, allow_self_loops, src_level_bound, step_dev, k,
+                num_levels, init_kind, init_a, init_b, init_salt, out, status, scratch, scratch_bytes, stream);
+}
+
+__global__ void select_take_kernel(int64_t k, int32_t blocks, const int32_t *__restrict__ step_dev,
+                                   const int32_t *__restrict__ s_col, const int32_t *__restrict__ d_col,
+                                   const float *__restrict__ w_col, const uint8_t *__restrict__ g_col,
+                                   int32_t *__restrict__ s_out, int32_t *__restrict__ d_out, float *__restrict__ w_out,
+                                   uint8_t *__restrict__ g_out) {
+  int64_t base = 0;
+  if (blocks > 1) {
+    const int32_t st = *step_dev;
+    base = static_cast<int64_t>(((st % blocks) + blocks) % blocks) * k;
+  }
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < k;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    s_out[i] = s_col[base + i];
+    d_out[i] = d_col[base + i];
+    w_out[i] = w_col[base + i];
+    g_out[i] = g_col[base + i];
+  }
+}
+
+extern "C" int pxb_select_take(int64_t k, int32_t blocks, const int32_t *step_dev, const int32_t *src_col,
+                               const int32_t *dst_col, const float *weight_col, const uint8_t *growable_col,
+                               int32_t *src_out, int32_t *dst_out, float *weight_out, uint8_t *growable_out,
+                               void *stream) {
+  PXB_REQUIRE(k >= 0 && blocks >= 1, "pxb_select_take: bad sizes");
+  if (k == 0) return PXB_OK;
+  PXB_REQUIRE(blocks == 1 || step_dev != nullptr, "pxb_select_take: %d lists need step_dev", blocks);
+  PXB_REQUIRE(src_col && dst_col && weight_col && growable_col && src_out && dst_out && weight_out && growable_out,
+              "pxb_select_take: a pointer is NULL");
+  select_take_kernel<<<grid_for(k, 256, 8), 256, 0, as_stream(stream)>>>(
+      k, blocks, step_dev, src_col, dst_col, weight_col, growable_col, src_out, dst_out, weight_out, growable_out);
+  PXB_LAUNCHED("select_take_kernel");
   return PXB_OK;
 }
 

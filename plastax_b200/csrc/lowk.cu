@@ -20,6 +20,7 @@
 // claim's per-domain counts that rode on that barrier. The lists are
 // double-buffered by the plan's parity, so a rank a step ahead never
 // overwrites a list a peer still reads.
+#include <cub/block/block_reduce.cuh>
 #include <cub/block/block_scan.cuh>
 
 #include "mirror.cuh"
@@ -33,8 +34,11 @@ constexpr int kFinePer = 1 << (kLowkShift - kFineShift);  // fine bins per coars
 constexpr uint32_t kFineBins = PXB_LOWK_FINE_BINS;
 constexpr uint32_t kInfBits = 0x7f800000u;  // +inf; anything above is a NaN
 constexpr uint32_t kAllBits = kInfBits + 1;   // a cut that prunes every non-NaN edge
-constexpr int kPlanThreads = 1024;
-constexpr int kBinsPerThread = kLowkBins / kPlanThreads;
+constexpr int kPlanThreads = 256;
+constexpr int kBinsPerCta = 4 * kPlanThreads;  // one uint4 of coarse bins per plan thread
+constexpr int kPlanCtas = kLowkBins / kBinsPerCta;
+static_assert(2 * kPlanCtas + 1 <= PXB_LOWK_PLAN_SCRATCH, "the plan's partials and arrival counter fit its scratch");
+static_assert(kPlanCtas <= kPlanThreads, "one last-CTA thread per partial");
 constexpr int kSelectThreads = 1024;
 constexpr int kMaxWorld = 64;
 constexpr int kMaxLevels = PXB_PEER_MAX_LEVELS;
@@ -67,69 +71,89 @@ __global__ void lowk_hist_build_kernel(int64_t cap, const uint8_t *__restrict__ 
   if ((threadIdx.x & 31) == 0 && lowest != 0xffffffffu) atomicMin(&plan->floor, lowest);
 }
 
-// One CTA: the fine threshold bin of the k-th smallest key (the coarse bin
-// first, then its fine bins), the plan, the coarse histogram's cut and the
-// fine bin's part; the fine bins wholly pruned are emptied by
-// lowk_zero_kernel from the plan's [zero_lo, zero_hi). This rank's list
-// counters of the new parity are reset.
+// The plan: the fine threshold bin of the k-th smallest key, the coarse
+// histogram's cut and the fine bin's part; the fine bins wholly pruned are
+// emptied by lowk_zero_kernel from the plan's [zero_lo, zero_hi). This
+// rank's list counters of the new parity are reset.
+//
+// kPlanCtas CTAs each sum 1024 coarse bins (one 16-byte load per thread)
+// into a partial; the last CTA to arrive scans the partials, then the 1024
+// bins of the range holding the k-th key, then that coarse bin's fine bins.
+// One CTA reading the whole 256 KB histogram is bound by the loads a single
+// SM keeps in flight; here each CTA reads 4 KB and the last one 9 KB more.
 __global__ void __launch_bounds__(kPlanThreads) lowk_plan_kernel(uint32_t *__restrict__ hist,
                                                                  uint32_t *__restrict__ fine, pxb_lowk_plan *plan,
-                                                                 int64_t k, unsigned long long *count) {
+                                                                 int64_t k, unsigned long long *count,
+                                                                 uint32_t *scratch) {
   using Scan = cub::BlockScan<long long, kPlanThreads>;
-  __shared__ typename Scan::TempStorage scan_tmp;
-  __shared__ int s_bin, s_fbin;
-  __shared__ long long s_below_c, s_below, s_in_bin;
+  using Reduce = cub::BlockReduce<long long, kPlanThreads>;
+  __shared__ union {
+    typename Scan::TempStorage scan;
+    typename Reduce::TempStorage reduce;
+  } tmp;
+  __shared__ int s_last, s_range, s_bin, s_fbin;
+  __shared__ long long s_range_excl, s_below_c, s_below, s_in_bin;
+  unsigned long long *part = reinterpret_cast<unsigned long long *>(scratch);
+  unsigned int *arrived = scratch + 2 * kPlanCtas;
   const int t = threadIdx.x;
-  // thread t holds coarse bins [64 t, 64 t + 64): sixteen 16-byte loads
-  const uint4 *h4 = reinterpret_cast<const uint4 *>(hist) + t * (kBinsPerThread / 4);
-  long long sum = 0;
-#pragma unroll
-  for (int j = 0; j < kBinsPerThread / 4; ++j) {
-    const uint4 v = h4[j];
-    sum += static_cast<long long>(v.x) + v.y + v.z + v.w;
+  {
+    const uint4 v = reinterpret_cast<const uint4 *>(hist)[blockIdx.x * kPlanThreads + t];
+    const long long mine = static_cast<long long>(v.x) + v.y + v.z + v.w;
+    const long long sum = Reduce(tmp.reduce).Sum(mine);
+    if (t == 0) {
+      part[blockIdx.x] = static_cast<unsigned long long>(sum);
+      __threadfence();
+      s_last = atomicAdd(arrived, 1u) == kPlanCtas - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
   }
-  long long excl, total;
-  Scan(scan_tmp).ExclusiveSum(sum, excl, total);
-  __shared__ int s_owner;
-  __shared__ long long s_owner_excl;
+  // the last CTA: every partial is visible (fence before each arrival)
+  __threadfence();
   if (t == 0) {
+    *arrived = 0u;  // ready for the next plan
+    s_range = -1;
     s_bin = -1;
     s_fbin = -1;
-    s_owner = -1;
+  }
+  const long long p = t < kPlanCtas ? static_cast<long long>(__ldcg(part + t)) : 0;
+  long long excl, total;
+  __syncthreads();
+  Scan(tmp.scan).ExclusiveSum(p, excl, total);
+  if (k > 0 && total > k && t < kPlanCtas && excl < k && excl + p >= k) {
+    s_range = t;
+    s_range_excl = excl;
   }
   __syncthreads();
-  if (k > 0 && total > k && excl < k && excl + sum >= k) {
-    s_owner = t;
-    s_owner_excl = excl;
-  }
-  __syncthreads();
-  if (s_owner >= 0 && t < 32) {
-    // the owner's 64 bins, two per lane, ranked by a warp scan
-    const int o = s_owner;
-    const uint2 h2 = reinterpret_cast<const uint2 *>(hist + o * kBinsPerThread)[t];
-    long long incl = static_cast<long long>(h2.x) + h2.y;
+  const int rg = s_range;
+  if (rg >= 0) {
+    // the range's 1024 coarse bins, four per thread
+    const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(hist) + rg * kPlanThreads + t);
+    const long long mine = static_cast<long long>(v.x) + v.y + v.z + v.w;
+    long long bex, btot;
+    Scan(tmp.scan).ExclusiveSum(mine, bex, btot);
+    const long long before = s_range_excl + bex;
+    if (before < k && before + mine >= k) {
+      const uint32_t h[4] = {v.x, v.y, v.z, v.w};
+      long long run = before;
 #pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const long long v = __shfl_up_sync(0xffffffffu, incl, d);
-      if (t >= d) incl += v;
+      for (int j = 0; j < 4; ++j) {
+        if (run < k && run + h[j] >= k) {
+          s_bin = rg * kBinsPerCta + 4 * t + j;
+          s_below_c = run;
+        }
+        run += h[j];
+      }
     }
-    const long long before = s_owner_excl + incl - h2.x - h2.y;
-    if (before < k && before + h2.x >= k) {
-      s_bin = o * kBinsPerThread + 2 * t;
-      s_below_c = before;
-    } else if (before + h2.x < k && before + h2.x + h2.y >= k) {
-      s_bin = o * kBinsPerThread + 2 * t + 1;
-      s_below_c = before + h2.x;
-    }
+    __syncthreads();
   }
-  __syncthreads();
   const int b = s_bin;
   if (b >= 0) {
     // the coarse bin's fine bins, one per thread
-    const uint32_t f = t < kFinePer ? fine[static_cast<int64_t>(b) * kFinePer + t] : 0u;
+    const uint32_t f = t < kFinePer ? __ldcg(fine + static_cast<int64_t>(b) * kFinePer + t) : 0u;
     long long fexcl, ftotal;
-    __syncthreads();  // scan_tmp is reused
-    Scan(scan_tmp).ExclusiveSum(static_cast<long long>(f), fexcl, ftotal);
+    __syncthreads();  // the scan's storage is reused
+    Scan(tmp.scan).ExclusiveSum(static_cast<long long>(f), fexcl, ftotal);
     const long long want = k - s_below_c;  // the rank inside the coarse bin, 1-based
     if (t < kFinePer && fexcl < want && fexcl + f >= want) {
       s_fbin = b * kFinePer + t;
@@ -159,31 +183,31 @@ __global__ void __launch_bounds__(kPlanThreads) lowk_plan_kernel(uint32_t *__res
   }
   __syncthreads();  // every thread has read plan->floor
   if (t == 0) {
-    pxb_lowk_plan p = *plan;
-    p.parity ^= 1;
+    pxb_lowk_plan pl = *plan;
+    pl.parity ^= 1;
     if (k <= 0) {
-      p.lo_bits = p.hi_bits = 0u;
-      p.below_expect = 0;
+      pl.lo_bits = pl.hi_bits = 0u;
+      pl.below_expect = 0;
     } else if (fb < 0) {
-      p.lo_bits = p.hi_bits = kAllBits;
-      p.below_expect = total;
+      pl.lo_bits = pl.hi_bits = kAllBits;
+      pl.below_expect = total;
     } else {
       const uint32_t end = static_cast<uint32_t>(fb + 1) << kFineShift;
       const uint32_t hi = end < kAllBits ? end : kAllBits;
-      p.lo_bits = whole ? hi : static_cast<uint32_t>(fb) << kFineShift;
-      p.hi_bits = hi;
-      p.below_expect = whole ? k : s_below;
+      pl.lo_bits = whole ? hi : static_cast<uint32_t>(fb) << kFineShift;
+      pl.hi_bits = hi;
+      pl.below_expect = whole ? k : s_below;
     }
-    p.take = take;
-    p.listed_expect = take > 0 ? s_in_bin : 0;
-    p.pruned = 0;
-    if (stale) p.status |= 2;
-    p.zero_lo = old_floor < cut ? old_floor : cut;
-    p.zero_hi = cut;
-    if (k > 0) p.floor = cut > old_floor ? cut : old_floor;
-    *plan = p;
-    count[2 * p.parity] = 0ull;
-    count[2 * p.parity + 1] = 0ull;
+    pl.take = take;
+    pl.listed_expect = take > 0 ? s_in_bin : 0;
+    pl.pruned = 0;
+    if (stale) pl.status |= 2;
+    pl.zero_lo = old_floor < cut ? old_floor : cut;
+    pl.zero_hi = cut;
+    if (k > 0) pl.floor = cut > old_floor ? cut : old_floor;
+    *plan = pl;
+    count[2 * pl.parity] = 0ull;
+    count[2 * pl.parity + 1] = 0ull;
     if (fb >= 0 && !whole) fine[fb] -= static_cast<uint32_t>(take);
   }
   // the coarse cut: bins wholly below the threshold's emptied (those from
@@ -192,11 +216,9 @@ __global__ void __launch_bounds__(kPlanThreads) lowk_plan_kernel(uint32_t *__res
   if (k > 0) {
     const int cb = fb < 0 ? kLowkBins : b;
     const int cfloor = static_cast<int>(min(old_floor >> (kLowkShift - kFineShift), static_cast<uint32_t>(kLowkBins)));
+    for (int bin = cfloor + t; bin < cb; bin += kPlanThreads) hist[bin] = 0u;
     const long long removed_in_b = fb < 0 ? 0 : (s_below - s_below_c) + (whole ? s_in_bin : take);
-    const int lo = max(cfloor, t * kBinsPerThread), hi = min(cb, (t + 1) * kBinsPerThread);
-    for (int bin = lo; bin < hi; ++bin) hist[bin] = 0u;
-    if (cb < kLowkBins && cb / kBinsPerThread == t && removed_in_b > 0)
-      hist[cb] -= static_cast<uint32_t>(removed_in_b);
+    if (t == 0 && cb < kLowkBins && removed_in_b > 0) hist[cb] -= static_cast<uint32_t>(removed_in_b);
   }
 }
 
@@ -446,7 +468,7 @@ __global__ void __launch_bounds__(kAddThreads) lowk_hist_add_kernel(uint32_t *__
 
 static int check_lowk(const char *fn, const pxb_lowk *lk) {
   PXB_REQUIRE(lk != nullptr, "%s: lowk is NULL", fn);
-  PXB_REQUIRE(lk->hist && lk->fine && lk->plan && lk->key && lk->level && lk->count && lk->pos,
+  PXB_REQUIRE(lk->hist && lk->fine && lk->plan && lk->key && lk->level && lk->count && lk->pos && lk->plan_scratch,
               "%s: a lowk array is NULL", fn);
   PXB_REQUIRE(lk->world >= 1 && lk->world <= kMaxWorld && lk->rank >= 0 && lk->rank < lk->world,
               "%s: rank %d / world %d out of range (world <= %d)", fn, lk->rank, lk->world, kMaxWorld);
@@ -478,7 +500,8 @@ extern "C" int pxb_lowk_make_plan(const pxb_lowk *lowk, void *stream) {
   int rc = check_lowk("pxb_lowk_make_plan", lowk);
   if (rc) return rc;
   cudaStream_t st = as_stream(stream);
-  lowk_plan_kernel<<<1, kPlanThreads, 0, st>>>(lowk->hist, lowk->fine, lowk->plan, lowk->k, lowk->count);
+  lowk_plan_kernel<<<kPlanCtas, kPlanThreads, 0, st>>>(lowk->hist, lowk->fine, lowk->plan, lowk->k, lowk->count,
+                                                        lowk->plan_scratch);
   PXB_LAUNCHED("lowk_plan_kernel");
   lowk_zero_kernel<<<grid_for(int64_t(1) << 20, 256, 4), 256, 0, st>>>(lowk->fine, lowk->plan);
   PXB_LAUNCHED("lowk_zero_kernel");

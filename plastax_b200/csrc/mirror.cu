@@ -711,8 +711,41 @@ using namespace pxb;
 namespace pxb {
 
 // The sweep and the overflow pass of one mirror, for any monoid and prune.
+// The sweep's grid for (monoid, prune kind): every CTA resident at once, no
+// more CTAs than tiles. The deferred tombstones are segmented by it, so the
+// flush recomputes it the same way.
+template <int M, int P>
+static int sweep_grid_of(const MirrorK &m, int *grid) {
+  const size_t acc_bytes = (M == PXB_MONOID_SUM ? 2 * sizeof(int32_t) : sizeof(float)) << m.cb;
+  const size_t smem = 128 + size_t(kStages) * kTile * 8 + acc_bytes;
+  auto fn = (M == PXB_MONOID_SUM && m.sum_frac == 28) ? mirror_sweep_kernel<M, P, 28> : mirror_sweep_kernel<M, P, 31>;
+  PXB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  int per_sm = 0;
+  PXB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kSweepThreads, smem));
+  const int64_t full = int64_t(sm_count()) * (per_sm > 0 ? per_sm : 1);
+  const int64_t tiles = m.entries / kTile;
+  *grid = static_cast<int>(tiles < full ? tiles : full);
+  return PXB_OK;
+}
+
+// The lowest-|w| sweep's deferred tombstones (the sweep of the same mirror
+// and monoid ran before on the stream).
+static int lowk_flush_launch(const MirrorK &m, int32_t monoid, const MPrune &p, cudaStream_t st) {
+  if (m.entries <= 0 || m.defer_pos == nullptr) return PXB_OK;
+  int grid = 0;
+  int rc = monoid == PXB_MONOID_SUM   ? sweep_grid_of<PXB_MONOID_SUM, PXB_PRUNE_LOWEST_K>(m, &grid)
+           : monoid == PXB_MONOID_MAX ? sweep_grid_of<PXB_MONOID_MAX, PXB_PRUNE_LOWEST_K>(m, &grid)
+                                      : sweep_grid_of<PXB_MONOID_MIN, PXB_PRUNE_LOWEST_K>(m, &grid);
+  if (rc) return rc;
+  if (grid > 0 && grid <= m.defer_ctas) {
+    mirror_defer_flush_kernel<<<grid, kFlushThreads, 0, st>>>(m, p, grid);
+    PXB_LAUNCHED("mirror_defer_flush_kernel");
+  }
+  return PXB_OK;
+}
+
 static int mirror_forward_launch(const MirrorK &m, const float *act, int32_t monoid, float *acc, int64_t *acc_fixed,
-                                 const MPrune &p, cudaStream_t st) {
+                                 const MPrune &p, cudaStream_t st, bool flush = true) {
   const int32_t prune_kind = p.kind;
   int sweep_grid = 0;
   if (m.entries > 0) {
@@ -744,7 +777,7 @@ static int mirror_forward_launch(const MirrorK &m, const float *act, int32_t mon
 #undef PXB_MS_K
 #undef PXB_MS
     PXB_LAUNCHED("mirror_sweep_kernel");
-    if (prune_kind != PXB_PRUNE_NONE && m.defer_pos != nullptr && sweep_grid <= m.defer_ctas) {
+    if (flush && prune_kind != PXB_PRUNE_NONE && m.defer_pos != nullptr && sweep_grid <= m.defer_ctas) {
       mirror_defer_flush_kernel<<<sweep_grid, kFlushThreads, 0, st>>>(m, p, sweep_grid);
       PXB_LAUNCHED("mirror_defer_flush_kernel");
     }
@@ -797,9 +830,9 @@ extern "C" int pxb_mirror_forward(const pxb_mirror *mirror, const float *act, in
   return mirror_forward_launch(to_k(mirror), act, monoid, acc, acc_fixed, p, as_stream(stream));
 }
 
-extern "C" int pxb_mirror_forward_lowk(const pxb_mirror *mirror, const float *act, int32_t monoid, float *acc,
-                                       int64_t *acc_fixed, const pxb_lowk *lowk, uint8_t *dead, uint32_t *free_bitmap,
-                                       int64_t bitmap_words, const int32_t *bitmap_level, void *stream) {
+static int forward_lowk(const pxb_mirror *mirror, const float *act, int32_t monoid, float *acc, int64_t *acc_fixed,
+                        const pxb_lowk *lowk, uint8_t *dead, uint32_t *free_bitmap, int64_t bitmap_words,
+                        const int32_t *bitmap_level, int flush, void *stream) {
   int rc = mirror_forward_checks("pxb_mirror_forward_lowk", mirror, act, monoid, acc, acc_fixed);
   if (rc) return rc;
   PXB_REQUIRE(lowk != nullptr && lowk->plan && lowk->key && lowk->level && lowk->count && lowk->pos,
@@ -810,7 +843,36 @@ extern "C" int pxb_mirror_forward_lowk(const pxb_mirror *mirror, const float *ac
               "pxb_mirror_forward_lowk: slot_base out of range (global slots are keyed in 32 bits)");
   MPrune p{PXB_PRUNE_LOWEST_K, 0.0f, nullptr, dead, free_bitmap, bitmap_words, bitmap_level, nullptr,
            LowkSweep{lowk->plan, lowk->key, lowk->level, lowk->count, lowk->pos, lowk->list_cap, lowk->slot_base}};
-  return mirror_forward_launch(to_k(mirror), act, monoid, acc, acc_fixed, p, as_stream(stream));
+  return mirror_forward_launch(to_k(mirror), act, monoid, acc, acc_fixed, p, as_stream(stream), flush != 0);
+}
+
+extern "C" int pxb_mirror_defer_flush(const pxb_mirror *mirror, int32_t monoid, const pxb_lowk *lowk, uint8_t *dead,
+                                      uint32_t *free_bitmap, int64_t bitmap_words, const int32_t *bitmap_level,
+                                      void *stream) {
+  int rc = check_mirror("pxb_mirror_defer_flush", mirror);
+  if (rc) return rc;
+  PXB_REQUIRE(monoid >= 0 && monoid <= 2, "pxb_mirror_defer_flush: unknown monoid %d", monoid);
+  PXB_REQUIRE(lowk != nullptr && lowk->plan && lowk->key && lowk->level && lowk->count && lowk->pos,
+              "pxb_mirror_defer_flush: a lowk array is NULL");
+  PXB_REQUIRE(dead != nullptr, "pxb_mirror_defer_flush: dead is NULL");
+  MPrune p{PXB_PRUNE_LOWEST_K, 0.0f, nullptr, dead, free_bitmap, bitmap_words, bitmap_level, nullptr,
+           LowkSweep{lowk->plan, lowk->key, lowk->level, lowk->count, lowk->pos, lowk->list_cap, lowk->slot_base}};
+  return lowk_flush_launch(to_k(mirror), monoid, p, as_stream(stream));
+}
+
+extern "C" int pxb_mirror_forward_lowk(const pxb_mirror *mirror, const float *act, int32_t monoid, float *acc,
+                                       int64_t *acc_fixed, const pxb_lowk *lowk, uint8_t *dead, uint32_t *free_bitmap,
+                                       int64_t bitmap_words, const int32_t *bitmap_level, void *stream) {
+  return forward_lowk(mirror, act, monoid, acc, acc_fixed, lowk, dead, free_bitmap, bitmap_words, bitmap_level, 1,
+                      stream);
+}
+
+extern "C" int pxb_mirror_forward_lowk_deferred(const pxb_mirror *mirror, const float *act, int32_t monoid,
+                                                float *acc, int64_t *acc_fixed, const pxb_lowk *lowk, uint8_t *dead,
+                                                uint32_t *free_bitmap, int64_t bitmap_words,
+                                                const int32_t *bitmap_level, void *stream) {
+  return forward_lowk(mirror, act, monoid, acc, acc_fixed, lowk, dead, free_bitmap, bitmap_words, bitmap_level, 0,
+                      stream);
 }
 
 extern "C" int pxb_mirror_insert(const pxb_mirror *mirror, int64_t k, const int32_t *src, const int32_t *dst,

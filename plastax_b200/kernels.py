@@ -512,25 +512,54 @@ def propose_select_unique(num_units: int, network_seed: int, step: int, *, dst_l
                           max_level_gap: int = 1, direction: int = 0, allow_self_loops: bool = False,
                           src_level_bound: int = 0, step_dev: torch.Tensor | None = None,
                           status: torch.Tensor | None = None, scratch: torch.Tensor | None = None,
-                          out: tuple | None = None) -> tuple[torch.Tensor, ...]:
+                          out: tuple | None = None, shard=None) -> tuple[torch.Tensor, ...] | None:
     """One proposal per unit scored by the site RNG: proposals, the first k of
     the total order listed levels ascending, gathered as the claim's inputs
-    (src, dst, init weight, growable)."""
+    (src, dst, init weight, growable). With `shard` (a `_lib.SelectShard`)
+    this rank ranks its share of the full bins and stores their winners into
+    every rank's columns (`out` is then unused and None is returned)."""
     dev = level.device
-    if out is None:
-        out = (torch.empty(k, dtype=torch.int32, device=dev), torch.empty(k, dtype=torch.int32, device=dev),
-               torch.empty(k, dtype=torch.float32, device=dev), torch.empty(k, dtype=torch.uint8, device=dev))
     if scratch is None:
         need = select_unique_scratch(num_units, k, num_levels, score_kind)
         scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    head = (ctypes.c_int32(num_units), ctypes.c_uint64(network_seed), ctypes.c_int32(step), ctypes.c_int32(dst_lo),
+            ctypes.c_int32(dst_n), ctypes.c_int32(score_kind), ptr(level), ptr(pruned),
+            ctypes.c_int32(max_level_gap), ctypes.c_int32(direction), ctypes.c_int32(1 if allow_self_loops else 0),
+            ctypes.c_int32(src_level_bound), ptr(step_dev), ctypes.c_int64(k), ctypes.c_int32(num_levels),
+            ctypes.c_int32(init_kind), ctypes.c_float(init_a), ctypes.c_float(init_b), ctypes.c_uint32(init_salt))
+    if shard is not None:
+        call("pxb_propose_select_unique_sharded", *head, ctypes.byref(shard), ptr(status), ptr(scratch),
+             ctypes.c_size_t(scratch.numel()), _stream())
+        return None
+    if out is None:
+        out = (torch.empty(k, dtype=torch.int32, device=dev), torch.empty(k, dtype=torch.int32, device=dev),
+               torch.empty(k, dtype=torch.float32, device=dev), torch.empty(k, dtype=torch.uint8, device=dev))
     s, d, w, g = out
-    call("pxb_propose_select_unique", ctypes.c_int32(num_units), ctypes.c_uint64(network_seed), ctypes.c_int32(step),
-         ctypes.c_int32(dst_lo), ctypes.c_int32(dst_n), ctypes.c_int32(score_kind), ptr(level), ptr(pruned),
-         ctypes.c_int32(max_level_gap), ctypes.c_int32(direction), ctypes.c_int32(1 if allow_self_loops else 0),
-         ctypes.c_int32(src_level_bound), ptr(step_dev), ctypes.c_int64(k), ctypes.c_int32(num_levels),
-         ctypes.c_int32(init_kind), ctypes.c_float(init_a), ctypes.c_float(init_b), ctypes.c_uint32(init_salt),
-         ptr(s), ptr(d), ptr(w), ptr(g), ptr(status), ptr(scratch), ctypes.c_size_t(scratch.numel()), _stream())
+    call("pxb_propose_select_unique", *head, ptr(s), ptr(d), ptr(w), ptr(g), ptr(status), ptr(scratch),
+         ctypes.c_size_t(scratch.numel()), _stream())
     return s, d, w, g
+
+
+def select_shard(rank: int, world: int, blocks: int, columns: list) -> "_lib.SelectShard":
+    """The `pxb_select_shard` of a shared selection: `columns[q]` is rank q's
+    (src, dst, weight, growable) device pointers, each column holding
+    `blocks` lists of k entries."""
+    if not 1 <= world <= _lib.SELECT_MAX_WORLD or len(columns) != world:
+        raise ValueError(f"a shared selection takes 1..{_lib.SELECT_MAX_WORLD} ranks' columns, got {len(columns)}")
+    sh = _lib.SelectShard()
+    sh.rank, sh.world, sh.blocks = int(rank), int(world), int(blocks)
+    for q, (s, d, w, g) in enumerate(columns):
+        sh.src_out[q], sh.dst_out[q], sh.weight_out[q], sh.growable_out[q] = int(s), int(d), int(w), int(g)
+    return sh
+
+
+def select_take(k: int, blocks: int, step_dev: torch.Tensor | None, cols: tuple, out: tuple) -> None:
+    """List (step mod blocks) of the four columns `cols` (blocks * k entries
+    each) copied into `out` (the claim's inputs), in one launch."""
+    s, d, w, g = cols
+    so, do, wo, go = out
+    call("pxb_select_take", ctypes.c_int64(k), ctypes.c_int32(blocks), ptr(step_dev), ptr(s), ptr(d), ptr(w), ptr(g),
+         ptr(so), ptr(do), ptr(wo), ptr(go), _stream())
 
 
 def select_step_scratch(n: int, k: int) -> int:

@@ -3,7 +3,7 @@
 `LowestK` owns the prune's device state for one StepFn: the coarse and fine
 histograms of bits(|w|) (>> 15 and >> 7; 256 KB and 64 MB) over the live
 non-NaN edges (the whole arena, replicated on every Scheme-A rank), the
-plan the one-CTA plan kernel writes before each
+plan the plan kernel writes before each
 sweep, the double-buffered lists of the threshold bin's edges (inside the
 peer region under Scheme-A, so every rank's selection reads every rank's
 list) and running churn totals. Each firing is: `plan()` before the sweep,
@@ -44,6 +44,8 @@ class LowestK:
         # zero_hi, pad)
         self.plan = torch.zeros(8, dtype=torch.int64, device=dev)
         self.pos = torch.empty(2 * self.list_cap, dtype=torch.int64, device=dev)
+        # the plan kernel's partial sums and arrival counter (zero between plans)
+        self.plan_scratch = torch.zeros(_lib.LOWK_PLAN_SCRATCH, dtype=torch.int32, device=dev)
         # running {pruned by this rank, committed, overflowed, firings}
         self.totals = torch.zeros(4, dtype=torch.int64, device=dev)
         self.peers = peers
@@ -60,7 +62,8 @@ class LowestK:
             pk, pl, pc = peers.p_lkey.data_ptr(), peers.p_llevel.data_ptr(), peers.p_lcount.data_ptr()
         self.struct = _lib.Lowk(rank, world, self.k, self.list_cap, int(slot_base), self.hist.data_ptr(),
                                 self.fine.data_ptr(), self.plan.data_ptr(), self.key.data_ptr(), self.level.data_ptr(),
-                                self.count.data_ptr(), self.pos.data_ptr(), pk, pl, pc)
+                                self.count.data_ptr(), self.pos.data_ptr(), pk, pl, pc,
+                                self.plan_scratch.data_ptr())
 
     # -- histogram -------------------------------------------------------------
     def build_hist(self, buckets, combine=None, combine_min=None) -> None:
@@ -87,10 +90,21 @@ class LowestK:
         _lib.call("pxb_lowk_make_plan", ctypes.byref(self.struct), _stream())
 
     def sweep(self, m, act: torch.Tensor, acc: torch.Tensor, acc_fixed: torch.Tensor | None, monoid: str,
-              dead: torch.Tensor, free_bitmap: torch.Tensor | None, bitmap_level: torch.Tensor | None) -> None:
-        _lib.call("pxb_mirror_forward_lowk", ctypes.byref(m.struct), ptr(act), ctypes.c_int32(_lib.MONOID[monoid]),
+              dead: torch.Tensor, free_bitmap: torch.Tensor | None, bitmap_level: torch.Tensor | None,
+              flush: bool = True) -> None:
+        """The forward sweep with the prune; with `flush` False the sweep's
+        deferred tombstones are left for `flush()`."""
+        name = "pxb_mirror_forward_lowk" if flush else "pxb_mirror_forward_lowk_deferred"
+        _lib.call(name, ctypes.byref(m.struct), ptr(act), ctypes.c_int32(_lib.MONOID[monoid]),
                   ptr(acc), ptr(acc_fixed), ctypes.byref(self.struct), ptr(dead), ptr(free_bitmap),
                   ctypes.c_int64((dead.numel() + 31) // 32), ptr(bitmap_level), _stream())
+
+    def flush(self, m, monoid: str, dead: torch.Tensor, free_bitmap: torch.Tensor | None,
+              bitmap_level: torch.Tensor | None) -> None:
+        """The deferred tombstones of the last `sweep(..., flush=False)`."""
+        _lib.call("pxb_mirror_defer_flush", ctypes.byref(m.struct), ctypes.c_int32(_lib.MONOID[monoid]),
+                  ctypes.byref(self.struct), ptr(dead), ptr(free_bitmap), ctypes.c_int64((dead.numel() + 31) // 32),
+                  ptr(bitmap_level), _stream())
 
     def select(self, m, dead: torch.Tensor, free_bitmap: torch.Tensor | None, bitmap_level: torch.Tensor | None,
                *, num_levels: int = 0, level_before: torch.Tensor | None = None,

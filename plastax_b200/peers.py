@@ -35,7 +35,7 @@ class _Raw:
 
 
 def _view(ptr: int, n: int, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
-    typestr = {torch.int64: "<i8", torch.float32: "<f4", torch.int32: "<i4"}[dtype]
+    typestr = {torch.int64: "<i8", torch.float32: "<f4", torch.int32: "<i4", torch.uint8: "|u1"}[dtype]
     return torch.as_tensor(_Raw(ptr, n, typestr), device=device)
 
 
@@ -43,7 +43,8 @@ class PeerGroup:
     """One rank's symmetric region and its peers' mappings (collective: every
     rank of `group` constructs it at the same point)."""
 
-    def __init__(self, num_units: int, device: torch.device, group=None, lowk_cap: int = 0) -> None:
+    def __init__(self, num_units: int, device: torch.device, group=None, lowk_cap: int = 0, win_k: int = 0,
+                 win_blocks: int = 3) -> None:
         import torch.distributed as dist
 
         self.dist = dist
@@ -64,7 +65,16 @@ class PeerGroup:
         self.off_lkey = _align(self.off_counts + 4 * self.world * _lib.PEER_MAX_LEVELS)
         self.off_llevel = _align(self.off_lkey + 8 * 2 * self.lowk_cap)
         self.off_lcount = _align(self.off_llevel + 4 * 2 * self.lowk_cap)
-        self.bytes = _align(self.off_lcount + 8 * 4)
+        # the growth selection's winner columns (src, dst, weight, growable),
+        # `win_blocks` lists of `win_k` each, written by every rank's share of
+        # the selection
+        self.win_k, self.win_blocks = int(win_k), int(win_blocks)
+        wn = self.win_k * self.win_blocks
+        self.off_wsrc = _align(self.off_lcount + 8 * 4)
+        self.off_wdst = _align(self.off_wsrc + 4 * wn)
+        self.off_ww = _align(self.off_wdst + 4 * wn)
+        self.off_wgrow = _align(self.off_ww + 4 * wn)
+        self.bytes = _align(self.off_wgrow + wn)
         lib = _lib.lib()
         lib.pxb_set_device(self.dev.index)
         base = ctypes.c_void_p()
@@ -102,6 +112,15 @@ class PeerGroup:
             self.lowk_key = _view(self.base + self.off_lkey, 2 * self.lowk_cap, torch.int64, self.dev)
             self.lowk_level = _view(self.base + self.off_llevel, 2 * self.lowk_cap, torch.int32, self.dev)
             self.lowk_count = _view(self.base + self.off_lcount, 4, torch.int64, self.dev)
+        self.win_cols = None
+        if wn > 0:
+            self.win_cols = (_view(self.base + self.off_wsrc, wn, torch.int32, self.dev),
+                             _view(self.base + self.off_wdst, wn, torch.int32, self.dev),
+                             _view(self.base + self.off_ww, wn, torch.float32, self.dev),
+                             _view(self.base + self.off_wgrow, wn, torch.uint8, self.dev))
+            # every rank's columns, as this rank addresses them
+            self.win_ptrs = [(b + self.off_wsrc, b + self.off_wdst, b + self.off_ww, b + self.off_wgrow)
+                             for b in self.bases]
         self.closed = False
 
     @property
@@ -120,6 +139,7 @@ class PeerGroup:
         self.dist.barrier(group=self.group)
         self.acc_fixed = self.acc_side = self.act = None
         self.lowk_key = self.lowk_level = self.lowk_count = None
+        self.win_cols = None
         _lib.call("pxb_peer_free", ctypes.c_void_p(self.base))
         self.closed = True
 

@@ -221,8 +221,13 @@ class StepFn:
         self._ahead_ready = False
         # where the next step's selection forks from the step (see _body_ahead):
         # after the propagation under Scheme-A, where the sweep is short and
-        # the latency-bound claim leaves SMs idle; at the start on one GPU
+        # the latency-bound claim leaves SMs idle; on one GPU from just
+        # before the sweep, captured after its launch, so the sweep takes the
+        # SMs first and the selection fills them as its CTAs retire (forked
+        # at the step's start, the proposals held the SMs the sweep waited for)
         self.select_after_sweep = self.sharded
+        self.select_at_launch = not self.sharded
+        self._sweep_fork = None
         # with the prune and growth firing every step, the next step's plan
         # of the lowest-|w| prune is made right after this step's claim, on
         # its own stream beside the mirror insert (it reads the histograms
@@ -233,10 +238,28 @@ class StepFn:
         self.plan_stream = torch.cuda.Stream(device=device) if self.plan_ahead else None
         self._plan_ready = False
         self._plan_pending = False
-        if self.ahead:
-            self.claim_next = tuple(torch.empty_like(t) for t in self.claim_in)
-            self.sel_step_dev = torch.zeros(1, dtype=torch.int32, device=device)
+        # on one GPU with propagation only, the sweep's deferred tombstones
+        # are written on their own stream beside the apply and the threshold
+        # bin's selection: they touch other slots and mirror entries, and
+        # the prune phase waits for them before anything reads the arena
+        self.flush_split = bool(self.lowk_prune and not self.sharded and net.backward_pass is None
+                                and net.update_conn is None and not self.unit_lifecycle
+                                and torch.device(device).type == "cuda")
+        self.flush_stream = torch.cuda.Stream(device=device) if self.flush_split else None
+        self._flush_pending = False
         self._init_train_fused(fuse_train)
+        # under Scheme-A the selection a step ahead is shared out: each rank
+        # ranks its share of the full bins into every rank's winner columns
+        # (peer memory, bound with the group), which the next step reads
+        # after its combine's barrier; three lists, so a rank selecting step
+        # t + 1's never overwrites one a slower peer has yet to take
+        self.shard_select = bool(self.ahead and self.sharded and self.fast_select and self.peer_reduce
+                                 and not self.train_fused and static.num_shards <= _lib.SELECT_MAX_WORLD)
+        self.win_blocks = 3 if self.shard_select else 1
+        self.sel_shard = None
+        if self.ahead:
+            self.claim_next = None if self.shard_select else tuple(torch.empty_like(t) for t in self.claim_in)
+            self.sel_step_dev = torch.zeros(1, dtype=torch.int32, device=device)
         self.launches = 0
 
     def _init_train_fused(self, fuse_train: bool) -> None:
@@ -338,9 +361,14 @@ class StepFn:
 
             if self.peers is None:
                 self.peers = PeerGroup(st.num_units, self.dev,
-                                       lowk_cap=self._lowk_list_cap() if self.lowk_prune else 0)
+                                       lowk_cap=self._lowk_list_cap() if self.lowk_prune else 0,
+                                       win_k=self.k if self.shard_select else 0, win_blocks=self.win_blocks)
                 self.acc_fixed = self.peers.acc_fixed
                 self.acc = self.peers.acc_side
+                if self.shard_select:
+                    self.claim_next = self.peers.win_cols
+                    self.sel_shard = K.select_shard(self.peers.rank, self.peers.world, self.win_blocks,
+                                                    self.peers.win_ptrs)
             # the activation column lives in the group's region: peers write it
             self.peers.act.copy_(state.units[ACTIVATION.name])
             state.units[ACTIVATION.name] = self.peers.act
@@ -680,16 +708,31 @@ class StepFn:
         bm, bm_level = self._bm(i)
         if self.use_mirror:
             m = self.mirrors[i]
-            if self.lowk_prune:
-                if self._lowk_fires(state):
-                    if not self._plan_ready:
-                        self.lowk.make_plan()
-                    self._plan_ready = False
-                    self.lowk.sweep(m, act, acc, acc_fixed, self.fwd_monoid, b["dead"], bm, bm_level)
-                    self._lowk_fired = True
+            lowk = self.lowk_prune and self._lowk_fires(state)
+            if lowk and not self._plan_ready:
+                self.lowk.make_plan()
+            # a side branch forked from just before the sweep and captured
+            # after it: it depends on nothing the sweep does, and the sweep's
+            # launch comes first
+            fork, self._sweep_fork = self._sweep_fork, None
+            ev = None
+            if fork is not None:
+                ev = torch.cuda.Event()
+                ev.record()
+            if lowk:
+                self._plan_ready = False
+                self.lowk.sweep(m, act, acc, acc_fixed, self.fwd_monoid, b["dead"], bm, bm_level,
+                                flush=not self.flush_split)
+                self._lowk_fired = True
+                self.launches += 1
+                if self.flush_split:
+                    self.flush_stream.wait_stream(torch.cuda.current_stream(self.dev))
+                    with torch.cuda.stream(self.flush_stream):
+                        self.lowk.flush(m, self.fwd_monoid, b["dead"], bm, bm_level)
+                    self._flush_pending = True
                     self.launches += 1
-                else:
-                    K.mirror_forward(m, act, acc, acc_fixed=acc_fixed, monoid=self.fwd_monoid)
+            elif self.lowk_prune:
+                K.mirror_forward(m, act, acc, acc_fixed=acc_fixed, monoid=self.fwd_monoid)
             elif self.fuse_prune:
                 K.mirror_forward(m, act, acc, acc_fixed=acc_fixed, monoid=self.fwd_monoid,
                                  prune_kind=_lib.PRUNE_ABS_BELOW, threshold=net.prune_conn.threshold,
@@ -702,6 +745,8 @@ class StepFn:
                             threshold=net.prune_conn.threshold, free_bitmap=bm, bitmap_level=bm_level)
         else:
             K.forward_accumulate(b, act, acc, self.fwd_monoid)
+        if self.use_mirror and fork is not None:
+            fork(ev)
 
     def _forward_bucket(self, state: NetworkState, i: int, act: torch.Tensor) -> None:
         """Bucket i's forward partial, reduced across shards, in the carried
@@ -972,6 +1017,10 @@ class StepFn:
         pc = self.net.prune_conn
         if self._lowk_fired and self.peers is None:
             self._lowk_select(state)
+        if self._flush_pending:
+            # the sweep's tombstones are written: the arena is whole again
+            torch.cuda.current_stream(self.dev).wait_stream(self.flush_stream)
+            self._flush_pending = False
         if pc is None or self.fuse_prune:
             return
         n = self.static.num_units
@@ -1049,13 +1098,15 @@ class StepFn:
         dst_n = ac.dst_n if ac.dst_n is not None else n - ac.dst_lo
         grad = units.get(ac.grad_field.name) if ac.score == "grad_act" else None
         if self.fast_select:
+            # the step-ahead list under Scheme-A: this rank's share, into every rank's columns
+            shard = self.sel_shard if self.shard_select and out is self.claim_next else None
             K.propose_select_unique(n, st.seed, state.step, dst_lo=ac.dst_lo, dst_n=dst_n, score_kind=self.score_kind,
                                     level=level, k=self.k, num_levels=st.num_levels, init_kind=self.init_kind,
                                     init_a=self.init_a, pruned=pruned, max_level_gap=ac.max_level_gap,
                                     direction=self.direction, allow_self_loops=ac.allow_self_loops,
                                     src_level_bound=0 if self.pipeline else self.num_buckets,
                                     step_dev=step_dev, status=self.fs_status, scratch=self.fs_scratch,
-                                    out=out)
+                                    out=out, shard=shard)
             self.launches += 6
             return
         window = dict(level=level, grad=grad, act=units[ACTIVATION.name], pruned=pruned,
@@ -1300,19 +1351,28 @@ class StepFn:
         if not self._ahead_ready:  # the first step of a bound state selects its own
             self._select(state, out=self.claim_next, step_dev=self.step_dev)
             self._ahead_ready = True
-        # one multi-tensor copy kernel instead of a memcpy per column
-        torch._foreach_copy_(list(self.claim_in), list(self.claim_next))
+        if not self.shard_select:
+            # the list the previous step selected, its four columns in one launch
+            K.select_take(self.k, 1, None, self.claim_next, self.claim_in)
+            self.launches += 1
         torch.add(self.step_dev, 1, out=self.sel_step_dev)
 
-        def select_next():
-            self.side.wait_stream(main)
+        def select_next(ev=None):
+            if ev is None:
+                self.side.wait_stream(main)
+            else:
+                self.side.wait_event(ev)
             with torch.cuda.stream(self.side):
                 self._select(state, out=self.claim_next, step_dev=self.sel_step_dev)
 
         # the next step's selection reads only levels and the step counter;
-        # it overlaps either the whole step or only what follows the
-        # propagation (the persistent sweep holds every SM while it runs)
-        if not self.select_after_sweep:
+        # it overlaps either the whole step, the step from the sweep's launch
+        # on, or only what follows the propagation (the persistent sweep
+        # holds every SM while it runs)
+        at_launch = self.select_at_launch and self.use_mirror and not self.train_fused
+        if at_launch:
+            self._sweep_fork = select_next
+        elif not self.select_after_sweep:
             select_next()
         self._scatter_inputs(state, inputs)
         self._mark("inputs")
@@ -1320,6 +1380,15 @@ class StepFn:
             self._train(state, inputs)
         else:
             self._forward(state)
+            if at_launch and self._sweep_fork is not None:
+                # no sweep ran through the mirror: fork here
+                self._sweep_fork = None
+                select_next()
+            if self.shard_select:
+                # every rank's share of this step's list was stored before its
+                # combine signalled: the barrier orders them before this read
+                K.select_take(self.k, self.win_blocks, self.step_dev, self.claim_next, self.claim_in)
+                self.launches += 1
             if self.select_after_sweep:
                 select_next()
             self._loss(state, inputs)

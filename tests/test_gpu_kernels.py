@@ -387,8 +387,8 @@ def test_claim_topological(cuda, cap, k, dead_frac, use_bitmap):
 
 
 @pytest.mark.parametrize("shards", [2, 4])
-@pytest.mark.parametrize("pipeline", [True, False])
-def test_claim_scheme_a_bands_match_one_device(cuda, shards, pipeline):
+@pytest.mark.parametrize("pipeline,level_major", [(True, False), (True, True), (False, False)])
+def test_claim_scheme_a_bands_match_one_device(cuda, shards, pipeline, level_major):
     """The Scheme-A claim over G capacity bands (each band claimed with the
     all-gathered per-domain counts of the bands before it) writes exactly the
     single-device claim (src/plastax/phases.py:2868-2874)."""
@@ -399,7 +399,7 @@ def test_claim_scheme_a_bands_match_one_device(cuda, shards, pipeline):
     n, cap, k = 4000, 64_000, 6000
     b, level, tail, src, dst, w, grow, age = _claim_case(rng, cap, n, k, pipeline=pipeline, dead_frac=0.05,
                                                          tail_frac=0.03)
-    mode = 0 if pipeline else 1
+    mode = (0 if pipeline else 1) | (0x100 if level_major else 0)
     nl = int(level.max()) + 1 if pipeline else 1
     ref_b = {kk: v.copy() for kk, v in b.items()}
     if pipeline:
