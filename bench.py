@@ -437,10 +437,15 @@ def engine_arm(args) -> None:
     elapsed_ms = t0.elapsed_time(t1)
     churn_dev = (step.lowk.totals - totals0) if step.lowk is not None else None
 
-    # e2e: host inputs in pinned memory, H2D inside the region, D2H of the
-    # step's overflow flag + grown count
+    # e2e: host inputs, H2D inside the region, D2H of the step's grown count
+    # and overflow flag read by the host every step (as the Driver reads the
+    # flag); with a graph both copies are nodes of the step's graph
+    # (StepFn.capture(host_io=True)), from and into pinned buffers
     host_in = torch.randn((Kst, cfg.num_inputs), generator=torch.Generator().manual_seed(7)).pin_memory()
     readback = torch.zeros(2, dtype=torch.int32).pin_memory()
+    if use_graph:
+        step.capture(state, StepInputs(inputs_dev[0]), host_io=True)
+        readback = step.host_flags
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -451,10 +456,12 @@ def engine_arm(args) -> None:
     short = 0
     for i in range(Kst):
         res = step(state, StepInputs(host_in[i]))
-        out = torch.stack([res.grown.to(torch.int32), res.overflow.to(torch.int32)])
-        readback.copy_(out, non_blocking=True)
+        if not use_graph:
+            out = torch.stack([res.grown.to(torch.int32), res.overflow.to(torch.int32)])
+            readback.copy_(out, non_blocking=True)
         torch.cuda.current_stream().synchronize()  # the Driver reads the flag every step
-        short += int(readback[0]) != cfg.k or int(readback[1]) != 0
+        grown_i, over_i = readback.tolist()
+        short += grown_i != cfg.k or over_i != 0
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)

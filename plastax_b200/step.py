@@ -185,6 +185,7 @@ class StepFn:
         self._bound: int | None = None
         self.step_dev = torch.zeros(1, dtype=torch.int32, device=device)
         self.graph = None  # a captured CUDA graph of the step body (see capture)
+        self._host_io = False  # the graph copies the step's host inputs and flags (see capture)
         self.graph_priority = False  # capture main / side streams at high / low priority (see capture)
         self._graph_exec = None
         # with auto_graphs, steps whose work depends on periodic phases replay
@@ -1491,13 +1492,22 @@ class StepFn:
                 t = torch.from_numpy(np.ascontiguousarray(t, np.float32))
             buf.targets.copy_(t.reshape(-1), non_blocking=True)
 
-    def capture(self, state: NetworkState, inputs: StepInputs, *, keep_graph: bool = False) -> None:
+    def capture(self, state: NetworkState, inputs: StepInputs, *, keep_graph: bool = False,
+                host_io: bool = False) -> None:
         """Capture one step of `state` as a CUDA graph; later calls with the
         same state replay it (inputs and targets are copied into the graph's
         input buffers first). Call after at least one eager step, so every
         kernel and index is initialised; the shapes of `inputs` (and
         targets) are fixed from then on. `keep_graph` keeps the cudaGraph_t
-        (`self.graph.raw_cuda_graph()`), for a device-side loop over it."""
+        (`self.graph.raw_cuda_graph()`), for a device-side loop over it.
+
+        With `host_io` the step's host traffic is part of the graph: a call
+        copies host inputs into pinned staging buffers (a host copy), the
+        graph copies them to the device first and ends by copying the step's
+        growth flags (grown, overflow as int32) into the pinned
+        `self.host_flags`, valid once the stream has synchronised. A call
+        waits until the previous replay is complete before it refills the
+        staging buffers."""
         if not self.capturable():
             raise ValueError("this step's work depends on the step count (trigger or interval); it cannot be "
                              "replayed from one graph")
@@ -1509,6 +1519,14 @@ class StepFn:
         t = None if inputs.targets is None else torch.as_tensor(inputs.targets, dtype=torch.float32).to(
             self.dev).reshape(-1).clone()
         self._graph_in = StepInputs(x, t)
+        self._host_io = bool(host_io)
+        if self._host_io:
+            self._host_in = StepInputs(torch.empty(x.numel(), dtype=torch.float32).pin_memory(),
+                                       None if t is None else torch.empty(t.numel(), dtype=torch.float32).pin_memory())
+            self._flags_dev = torch.zeros(2, dtype=torch.int32, device=self.dev)
+            self.host_flags = torch.zeros(2, dtype=torch.int32).pin_memory()
+            self._io_done = torch.cuda.Event()
+            zero = torch.zeros((), dtype=torch.int32, device=self.dev)
         torch.cuda.synchronize(self.dev)
         self._drop_exec()
         prio = self.graph_priority and self.side is not None
@@ -1518,7 +1536,16 @@ class StepFn:
         # lowest, and the graph is instantiated to honour them
         cap = torch.cuda.Stream(device=self.dev, priority=-1) if prio else None
         with torch.cuda.graph(g, stream=cap):
+            if self._host_io:
+                self._graph_in.inputs.copy_(self._host_in.inputs, non_blocking=True)
+                if t is not None:
+                    self._graph_in.targets.copy_(self._host_in.targets, non_blocking=True)
             self._graph_rem = self._body(state, self._graph_in)
+            if self._host_io:
+                grown = state.grown if state.grown is not None else zero
+                overflow = state.overflow if state.overflow is not None else zero
+                torch.stack([grown.to(torch.int32), overflow.to(torch.int32)], out=self._flags_dev)
+                self.host_flags.copy_(self._flags_dev, non_blocking=True)
         if prio:
             exec_ = ctypes.c_void_p()
             _lib.call("pxb_graph_instantiate", ctypes.c_void_p(g.raw_cuda_graph()), ctypes.c_int32(1),
@@ -1540,6 +1567,7 @@ class StepFn:
         self.graph = None
         self._graph_rem = None
         self._graph_in = None
+        self._host_io = False
         self._graphs = {}
         self._sig_seen = {}
 
@@ -1557,16 +1585,24 @@ class StepFn:
             x = inputs.inputs
             if not isinstance(x, torch.Tensor):
                 x = torch.from_numpy(np.ascontiguousarray(x, np.float32))
-            self._graph_in.inputs.copy_(x.reshape(-1), non_blocking=True)
-            if inputs.targets is not None and self._graph_in.targets is not None:
+            dst = self._graph_in
+            if self._host_io:
+                # the graph copies from the staging buffers: the previous
+                # replay must have read them
+                self._io_done.synchronize()
+                dst = self._host_in
+            dst.inputs.copy_(x.reshape(-1), non_blocking=not self._host_io)
+            if inputs.targets is not None and dst.targets is not None:
                 t = inputs.targets
                 if not isinstance(t, torch.Tensor):
                     t = torch.from_numpy(np.ascontiguousarray(t, np.float32))
-                self._graph_in.targets.copy_(t.reshape(-1), non_blocking=True)
+                dst.targets.copy_(t.reshape(-1), non_blocking=not self._host_io)
             if self._graph_exec is not None:
                 _lib.call("pxb_graph_launch", self._graph_exec, K._stream())
             else:
                 self.graph.replay()
+            if self._host_io:
+                self._io_done.record()
             remainder = self._graph_rem
         else:
             # eager steps are counted per signature even before auto_graphs
