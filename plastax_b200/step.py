@@ -256,11 +256,20 @@ class StepFn:
         # t + 1's never overwrites one a slower peer has yet to take
         self.shard_select = bool(self.ahead and self.sharded and self.fast_select and self.peer_reduce
                                  and not self.train_fused and static.num_shards <= _lib.SELECT_MAX_WORLD)
-        self.win_blocks = 3 if self.shard_select else 1
+        # on one GPU with the tombstones on their own stream, the list's take
+        # and the accumulators' clear move from before the sweep into the
+        # flush's shadow (after the threshold bin's selection); the lists
+        # alternate by step parity so the side stream's next list never
+        # overwrites the one still to be taken
+        self.late_io = bool(self.flush_split and self.plan_ahead and self.ahead and not self.shard_select)
+        self.win_blocks = 3 if self.shard_select else (2 if self.late_io else 1)
         self.sel_shard = None
         if self.ahead:
-            self.claim_next = None if self.shard_select else tuple(torch.empty_like(t) for t in self.claim_in)
+            self.claim_next = None if self.shard_select else tuple(
+                torch.empty(self.win_blocks * t.numel(), dtype=t.dtype, device=device) for t in self.claim_in)
             self.sel_step_dev = torch.zeros(1, dtype=torch.int32, device=device)
+            if self.late_io:
+                self.sel_shard = K.select_shard(0, 1, self.win_blocks, [tuple(c.data_ptr() for c in self.claim_next)])
         self.launches = 0
 
     def _init_train_fused(self, fuse_train: bool) -> None:
@@ -396,6 +405,8 @@ class StepFn:
         if self.train_fused:
             self._bind_train(state)
         self.step_dev.fill_(state.step)
+        if self.late_io:
+            K.clear_accumulators(self.acc, self.fwd_identity, self.acc_fixed)
         self._ahead_ready = False
         self._plan_ready = False
         self._bound = id(state)
@@ -800,7 +811,8 @@ class StepFn:
         act = units[ACTIVATION.name]
         pruned = units.get(PRUNED.name)
         fp = net.forward_pass
-        K.clear_accumulators(self.acc, self.fwd_identity, self.acc_fixed)
+        if not self.late_io:  # else cleared by the previous step (and at bind)
+            K.clear_accumulators(self.acc, self.fwd_identity, self.acc_fixed)
         if self.pipeline:
             if self.peers is not None:
                 from plastax_b200.peers import scheme_a_apply
@@ -1018,6 +1030,12 @@ class StepFn:
         pc = self.net.prune_conn
         if self._lowk_fired and self.peers is None:
             self._lowk_select(state)
+        if self.late_io:
+            # beside the tombstones: this step's list into the claim's inputs,
+            # the accumulators cleared for the next sweep (the apply has read them)
+            K.select_take(self.k, self.win_blocks, self.step_dev, self.claim_next, self.claim_in)
+            K.clear_accumulators(self.acc, self.fwd_identity, self.acc_fixed)
+            self.launches += 2
         if self._flush_pending:
             # the sweep's tombstones are written: the arena is whole again
             torch.cuda.current_stream(self.dev).wait_stream(self.flush_stream)
@@ -1100,7 +1118,7 @@ class StepFn:
         grad = units.get(ac.grad_field.name) if ac.score == "grad_act" else None
         if self.fast_select:
             # the step-ahead list under Scheme-A: this rank's share, into every rank's columns
-            shard = self.sel_shard if self.shard_select and out is self.claim_next else None
+            shard = self.sel_shard if self.sel_shard is not None and out is self.claim_next else None
             K.propose_select_unique(n, st.seed, state.step, dst_lo=ac.dst_lo, dst_n=dst_n, score_kind=self.score_kind,
                                     level=level, k=self.k, num_levels=st.num_levels, init_kind=self.init_kind,
                                     init_a=self.init_a, pruned=pruned, max_level_gap=ac.max_level_gap,
@@ -1352,7 +1370,7 @@ class StepFn:
         if not self._ahead_ready:  # the first step of a bound state selects its own
             self._select(state, out=self.claim_next, step_dev=self.step_dev)
             self._ahead_ready = True
-        if not self.shard_select:
+        if not self.shard_select and not self.late_io:
             # the list the previous step selected, its four columns in one launch
             K.select_take(self.k, 1, None, self.claim_next, self.claim_in)
             self.launches += 1
