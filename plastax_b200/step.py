@@ -811,7 +811,7 @@ class StepFn:
         act = units[ACTIVATION.name]
         pruned = units.get(PRUNED.name)
         fp = net.forward_pass
-        if not self.late_io:  # else cleared by the previous step (and at bind)
+        if not (self.late_io and self.ahead):  # else cleared by the previous step (and at bind)
             K.clear_accumulators(self.acc, self.fwd_identity, self.acc_fixed)
         if self.pipeline:
             if self.peers is not None:
@@ -1030,7 +1030,7 @@ class StepFn:
         pc = self.net.prune_conn
         if self._lowk_fired and self.peers is None:
             self._lowk_select(state)
-        if self.late_io:
+        if self.late_io and self.ahead:
             # beside the tombstones: this step's list into the claim's inputs,
             # the accumulators cleared for the next sweep (the apply has read them)
             K.select_take(self.k, self.win_blocks, self.step_dev, self.claim_next, self.claim_in)
