@@ -913,6 +913,7 @@ __global__ void __launch_bounds__(kFsThreads) fs_bins_warp_kernel(FsGeom g, Init
   const int32_t world = out.world > 1 ? out.world : 1, me = out.world > 1 ? out.rank : 0;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint64_t *ks = keys_s[w];
+  bool stored = false;
   // this rank's pairs: q = me, me + world, ...
   for (int64_t j = static_cast<int64_t>(blockIdx.x) * kFsWarps + w; j * world + me < pairs;
        j += static_cast<int64_t>(gridDim.x) * kFsWarps) {
@@ -929,12 +930,14 @@ __global__ void __launch_bounds__(kFsThreads) fs_bins_warp_kernel(FsGeom g, Init
       int32_t r = 0;
       for (int f = 0; f < m; ++f) r += ks[f] < ke ? 1 : 0;
       fs_emit(g, o, ia, ke, o.bi[t0 + e], base + r, out, true);
+      stored = true;
     }
     __syncwarp();
   }
   // the peers' stores are made visible before the kernel ends (a later
-  // release on this GPU's stream publishes them)
-  if (world > 1) __threadfence_system();
+  // release on this GPU's stream publishes them); a thread that stored
+  // nothing skips the system-wide fence
+  if (world > 1 && stored) __threadfence_system();
 }
 
 // The full bins larger than a warp's share, each (level, bin) pair ranked
@@ -947,6 +950,7 @@ __global__ void __launch_bounds__(kFsThreads) fs_bins_kernel(FsGeom g, InitArgs 
   const int64_t pairs = static_cast<int64_t>(g.L) * tb;
   const int64_t list = fs_list_base(out, g.k);
   const int32_t world = out.world > 1 ? out.world : 1, me = out.world > 1 ? out.rank : 0;
+  bool stored = false;
   for (int64_t j = blockIdx.x; j * world + me < pairs; j += gridDim.x) {
     const int64_t q = j * world + me;
     const int32_t l = static_cast<int32_t>(q / tb), b = static_cast<int32_t>(q % tb);
@@ -959,11 +963,13 @@ __global__ void __launch_bounds__(kFsThreads) fs_bins_kernel(FsGeom g, InitArgs 
       continue;
     }
     const int64_t base = list + static_cast<int64_t>(info->F[l]) + (t0 - info->T[l]);
-    for (int e = threadIdx.x; e < m; e += blockDim.x)
+    for (int e = threadIdx.x; e < m; e += blockDim.x) {
       fs_emit(g, o, ia, o.bk[t0 + e], o.bi[t0 + e], base + rank[e], out, true);
+      stored = true;
+    }
     __syncthreads();
   }
-  if (world > 1) __threadfence_system();
+  if (world > 1 && stored) __threadfence_system();
 }
 
 static int fs_geom(int32_t num_units, int64_t k, int32_t num_levels, int32_t score_kind, FsGeom *g) {
