@@ -110,32 +110,55 @@ __global__ void __launch_bounds__(256) scheme_a_apply_kernel(PeerK g, int32_t n,
     const int32_t per = (n + g.world - 1) / g.world;
     const int32_t lo = g.rank * per;
     const int32_t hi = lo + per < n ? lo + per : n;
-    for (int32_t u = lo + blockIdx.x * blockDim.x + threadIdx.x; u < hi; u += gridDim.x * blockDim.x) {
-      const uint8_t role = is_input != nullptr ? is_input[u] : 0;
-      if (role == 1 || (pruned != nullptr && pruned[u])) continue;
-      // every rank's partials in flight at once (eight at a time), then
-      // combined in rank order
-      long long f = 0;
-      float side = 0.0f;
-      for (int q0 = 0; q0 < g.world; q0 += 8) {
-        long long fq[8];
-        float sq[8];
+    const int32_t stride = gridDim.x * blockDim.x;
+    // kUnits units per thread at a time, every rank's partials of all of
+    // them (kRanks ranks at a time) loaded before any is used: a remote load
+    // is a round trip over NVLink, so the loads of one thread overlap
+    constexpr int kUnits = 4, kRanks = 4;
+    for (int32_t u0 = lo + blockIdx.x * blockDim.x + threadIdx.x; u0 < hi; u0 += kUnits * stride) {
+      long long f[kUnits];
+      float side[kUnits];
+      uint8_t role[kUnits], gone[kUnits];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int q = q0 + j;
-          fq[j] = q < g.world ? g.acc_fixed[q][u] : 0;
-          sq[j] = q < g.world ? g.acc_side[q][u] : 0.0f;
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (q0 + j >= g.world) break;
-          f += fq[j];
-          side = __fadd_rn(side, sq[j]);
-        }
+      for (int i = 0; i < kUnits; ++i) {
+        const int32_t u = u0 + i * stride;
+        const bool in = u < hi;
+        role[i] = in && is_input != nullptr ? is_input[u] : 0;
+        gone[i] = in && pruned != nullptr ? pruned[u] : 0;
+        f[i] = 0;
+        side[i] = 0.0f;
       }
-      const float x = f != 0 ? __fadd_rn(__fmul_rn(__ll2float_rn(f), kFixUnitP), side) : side;
-      const float a = act_fn(unit_act_kind(act_kind, role), x);
-      for (int q = 0; q < g.world; ++q) g.act[q][u] = a;
+      for (int q0 = 0; q0 < g.world; q0 += kRanks) {
+        long long fq[kUnits][kRanks];
+        float sq[kUnits][kRanks];
+#pragma unroll
+        for (int i = 0; i < kUnits; ++i) {
+          const int32_t u = u0 + i * stride;
+#pragma unroll
+          for (int j = 0; j < kRanks; ++j) {
+            const bool v = u < hi && q0 + j < g.world;
+            fq[i][j] = v ? g.acc_fixed[q0 + j][u] : 0;
+            sq[i][j] = v ? g.acc_side[q0 + j][u] : 0.0f;
+          }
+        }
+        // combined in rank order (the float side partials' order is fixed)
+#pragma unroll
+        for (int i = 0; i < kUnits; ++i)
+#pragma unroll
+          for (int j = 0; j < kRanks; ++j)
+            if (q0 + j < g.world) {
+              f[i] += fq[i][j];
+              side[i] = __fadd_rn(side[i], sq[i][j]);
+            }
+      }
+#pragma unroll
+      for (int i = 0; i < kUnits; ++i) {
+        const int32_t u = u0 + i * stride;
+        if (u >= hi || role[i] == 1 || gone[i]) continue;
+        const float x = f[i] != 0 ? __fadd_rn(__fmul_rn(__ll2float_rn(f[i]), kFixUnitP), side[i]) : side[i];
+        const float a = act_fn(unit_act_kind(act_kind, role[i]), x);
+        for (int q = 0; q < g.world; ++q) g.act[q][u] = a;
+      }
     }
   }
   __threadfence_system();

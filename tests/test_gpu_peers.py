@@ -248,3 +248,54 @@ def test_two_rank_per_connection_proposer_equals_one_gpu(cuda):
     assert got[0]["grown"] == got[1]["grown"] == int(state.grown.item()) > 0
     for col in want:
         np.testing.assert_array_equal(np.concatenate([got[0][col], got[1][col]]), want[col], err_msg=col)
+
+
+@pytest.mark.parametrize("world", [2, 5])
+def test_combine_of_emulated_ranks_on_one_gpu(cuda, world):
+    """Every rank's combine (scheme_a_apply_kernel) run one after another on
+    one GPU over `world` emulated regions, every flag set beforehand so no
+    wait depends on another kernel: each rank reduces its slice of the
+    units from every region (exact int64 sum, the float side added in rank
+    order), skips inputs and pruned units, and stores the activation into
+    every region."""
+    import torch
+
+    from plastax_b200 import _lib
+    from plastax_b200.peers import scheme_a_apply
+
+    n = 10_001
+    rng = np.random.default_rng(17)
+    fixed = [torch.from_numpy(rng.integers(-(1 << 33), 1 << 33, n)).to(cuda) for _ in range(world)]
+    side = [torch.from_numpy((rng.standard_normal(n) * 1e-3).astype(np.float32)).to(cuda) for _ in range(world)]
+    for q in range(world):  # units whose fixed-point sum is zero take the side sum alone
+        fixed[q][:50] = 0
+    act = [torch.full((n,), 7.0, dtype=torch.float32, device=cuda) for _ in range(world)]
+    flags = [torch.ones(2 * world, dtype=torch.int32, device=cuda) for _ in range(world)]
+    role = np.zeros(n, np.uint8)
+    role[rng.choice(n, 300, replace=False)] = 1
+    pruned = (rng.random(n) < 0.05).astype(np.uint8)
+    arr = lambda ts: torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device=cuda)  # noqa: E731
+    p_fixed, p_side, p_act, p_flags = arr(fixed), arr(side), arr(act), arr(flags)
+    words = [torch.zeros(4, dtype=torch.int32, device=cuda) for _ in range(world)]
+    for r in range(world):
+        w = words[r].data_ptr()
+
+        class G:
+            struct = _lib.PeerGroup(r, world, p_fixed.data_ptr(), p_side.data_ptr(), p_act.data_ptr(),
+                                    p_flags.data_ptr(), None, w, w + 4, w + 8)
+
+        G.n = n
+        scheme_a_apply(G, "identity", is_input=torch.from_numpy(role).to(cuda),
+                       pruned=torch.from_numpy(pruned).to(cuda), wait_polls=1000)
+    torch.cuda.synchronize()
+    assert [int(wd[2].item()) for wd in words] == [0] * world
+    f = sum(x.cpu().numpy() for x in fixed)
+    s = np.zeros(n, np.float32)
+    for q in range(world):
+        s = (s + side[q].cpu().numpy()).astype(np.float32)
+    want = np.where(f != 0, (f.astype(np.float32) * np.float32(2.0 ** -_lib.FIXED_FRAC_BITS)) + s, s)
+    want = want.astype(np.float32)
+    skip = (role == 1) | (pruned == 1)
+    want[skip] = 7.0
+    for q in range(world):
+        np.testing.assert_array_equal(act[q].cpu().numpy(), want, err_msg=f"region {q}")
