@@ -88,9 +88,10 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--phase-times", action="store_true",
                     help="add the step's main-stream phases (CUDA events over the eager steps; the phase ends at "
                          "the named boundary) to the line: rank 0's and the max over ranks")
-    ap.add_argument("--select-fork", default="auto", choices=["auto", "start", "sweep", "launch"],
+    ap.add_argument("--select-fork", default="auto", choices=["auto", "start", "sweep", "launch", "post"],
                     help="where the next step's growth selection forks onto the side stream: at the step's start, "
-                         "after the propagation, or from just before the sweep with the sweep launched first "
+                         "after the propagation, from just before the sweep with the sweep launched first "
+                         "(launch), or from the sweep's end before its tombstones and the combine (post) "
                          "(auto: after the propagation under Scheme-A, at the sweep's launch on one GPU)")
     ap.add_argument("--graph-priority", action="store_true",
                     help="replay the step's graph with the side stream's selection at low priority")
@@ -371,6 +372,7 @@ def engine_arm(args) -> None:
     if args.select_fork != "auto":
         step.select_after_sweep = args.select_fork == "sweep"
         step.select_at_launch = args.select_fork == "launch"
+        step.select_post_sweep = args.select_fork == "post"
     step.graph_priority = args.graph_priority
     W, Kst = max(args.warmup, 3), args.steps
     gen = torch.Generator(device=dev)

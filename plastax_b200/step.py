@@ -229,6 +229,10 @@ class StepFn:
         self.select_after_sweep = self.sharded
         self.select_at_launch = not self.sharded
         self._sweep_fork = None
+        # or from the lowest-|w| sweep's end, before its tombstones and the
+        # combine (the selection then overlaps the latency-bound combine)
+        self.select_post_sweep = False
+        self._post_fork = None
         # with the prune and growth firing every step, the next step's plan
         # of the lowest-|w| prune is made right after this step's claim, on
         # its own stream beside the mirror insert (it reads the histograms
@@ -733,10 +737,17 @@ class StepFn:
                 ev.record()
             if lowk:
                 self._plan_ready = False
+                post, self._post_fork = self._post_fork, None
+                split = self.flush_split or post is not None
                 self.lowk.sweep(m, act, acc, acc_fixed, self.fwd_monoid, b["dead"], bm, bm_level,
-                                flush=not self.flush_split)
+                                flush=not split)
                 self._lowk_fired = True
                 self.launches += 1
+                if post is not None:
+                    post()  # the next step's selection, from the sweep's end
+                if not self.flush_split and split:
+                    self.lowk.flush(m, self.fwd_monoid, b["dead"], bm, bm_level)
+                    self.launches += 1
                 if self.flush_split:
                     self.flush_stream.wait_stream(torch.cuda.current_stream(self.dev))
                     with torch.cuda.stream(self.flush_stream):
@@ -1389,8 +1400,11 @@ class StepFn:
         # on, or only what follows the propagation (the persistent sweep
         # holds every SM while it runs)
         at_launch = self.select_at_launch and self.use_mirror and not self.train_fused
+        post = self.select_post_sweep and not at_launch and self.use_mirror and not self.train_fused
         if at_launch:
             self._sweep_fork = select_next
+        elif post:
+            self._post_fork = select_next
         elif not self.select_after_sweep:
             select_next()
         self._scatter_inputs(state, inputs)
@@ -1399,16 +1413,16 @@ class StepFn:
             self._train(state, inputs)
         else:
             self._forward(state)
-            if at_launch and self._sweep_fork is not None:
-                # no sweep ran through the mirror: fork here
-                self._sweep_fork = None
+            if (at_launch and self._sweep_fork is not None) or (post and self._post_fork is not None):
+                # no sweep ran through the mirror (or without the lowest-|w| prune): fork here
+                self._sweep_fork = self._post_fork = None
                 select_next()
             if self.shard_select:
                 # every rank's share of this step's list was stored before its
                 # combine signalled: the barrier orders them before this read
                 K.select_take(self.k, self.win_blocks, self.step_dev, self.claim_next, self.claim_in)
                 self.launches += 1
-            if self.select_after_sweep:
+            if self.select_after_sweep and not (at_launch or post):
                 select_next()
             self._loss(state, inputs)
             self._backward(state)

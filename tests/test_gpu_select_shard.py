@@ -106,9 +106,10 @@ def test_shared_selection_rotates_with_the_device_step(cuda):
 
 
 def test_selection_forked_at_the_sweep_launch_changes_nothing(cuda):
-    """The next step's selection forked from just before the sweep (captured
-    after its launch) is only a scheduling choice: eager steps and graph
-    replays equal the steps that fork it at the step's start."""
+    """Where the next step's selection forks (the step's start, just before
+    the sweep with the sweep launched first, the sweep's end, or after the
+    propagation) is only a scheduling choice: eager steps and graph replays
+    are equal."""
     import torch
 
     from plastax_b200 import StepInputs, make_step
@@ -117,12 +118,13 @@ def test_selection_forked_at_the_sweep_launch_changes_nothing(cuda):
     cfg = ReservoirConfig(num_units=1 << 12, fan_in=16, churn=0.01, capacity_align=256)
     xs = np.random.default_rng(8).standard_normal((7, cfg.num_inputs)).astype(np.float32)
     got = []
-    for at_launch in (False, True):
+    for mode in ("start", "launch", "post", "sweep"):
         net, static, state = build_reservoir(cfg, cuda)
         step = make_step(net, static, device=cuda)
         assert step.ahead
-        step.select_after_sweep = False
-        step.select_at_launch = at_launch
+        step.select_after_sweep = mode == "sweep"
+        step.select_at_launch = mode == "launch"
+        step.select_post_sweep = mode == "post"
         for i in range(len(xs)):
             x = StepInputs(torch.from_numpy(xs[i]).to(cuda))
             if i == 3:
@@ -133,5 +135,6 @@ def test_selection_forked_at_the_sweep_launch_changes_nothing(cuda):
         got.append({**{c: v.cpu().numpy() for c, v in state.conns[0].items()},
                     "activation": state.units["activation"].cpu().numpy()})
         step.close()
-    for c in got[0]:
-        np.testing.assert_array_equal(got[1][c], got[0][c], err_msg=c)
+    for j in range(1, len(got)):
+        for c in got[0]:
+            np.testing.assert_array_equal(got[j][c], got[0][c], err_msg=f"{c} (fork mode {j})")
