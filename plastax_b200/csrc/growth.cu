@@ -904,6 +904,7 @@ __global__ void __launch_bounds__(1024) fs_threshold_bin_kernel(FsGeom g, const 
 // take them one after another, each a chain of loads and barriers).
 constexpr int kFsWarpCap = 512;
 constexpr int kFsWarps = kFsThreads / 32;
+constexpr int kFsLaneKeys = 4;
 __global__ void __launch_bounds__(kFsThreads) fs_bins_warp_kernel(FsGeom g, InitArgs ia, FsScratch o, FsOut out) {
   __shared__ uint64_t keys_s[kFsWarps][kFsWarpCap];
   const FsInfo *info = o.info;
@@ -925,12 +926,30 @@ __global__ void __launch_bounds__(kFsThreads) fs_bins_warp_kernel(FsGeom g, Init
     for (int e = lane; e < m; e += 32) ks[e] = o.bk[t0 + e];
     __syncwarp();
     const int64_t base = list + static_cast<int64_t>(info->F[l]) + (t0 - info->T[l]);
-    for (int e = lane; e < m; e += 32) {
-      const uint64_t ke = ks[e];
-      int32_t r = 0;
-      for (int f = 0; f < m; ++f) r += ks[f] < ke ? 1 : 0;
-      fs_emit(g, o, ia, ke, o.bi[t0 + e], base + r, out, true);
-      stored = true;
+    // each lane ranks up to kFsLaneKeys of the bin's keys at once: one
+    // shared-memory read of key f serves all of them
+    for (int e0 = lane; e0 < m; e0 += 32 * kFsLaneKeys) {
+      uint64_t ke[kFsLaneKeys];
+      int32_t r[kFsLaneKeys];
+#pragma unroll
+      for (int i = 0; i < kFsLaneKeys; ++i) {
+        const int e = e0 + 32 * i;
+        ke[i] = e < m ? ks[e] : ~0ull;  // the keys are unique: a padding key is never emitted
+        r[i] = 0;
+      }
+      for (int f = 0; f < m; ++f) {
+        const uint64_t kf = ks[f];
+#pragma unroll
+        for (int i = 0; i < kFsLaneKeys; ++i) r[i] += kf < ke[i] ? 1 : 0;
+      }
+#pragma unroll
+      for (int i = 0; i < kFsLaneKeys; ++i) {
+        const int e = e0 + 32 * i;
+        if (e < m) {
+          fs_emit(g, o, ia, ke[i], o.bi[t0 + e], base + r[i], out, true);
+          stored = true;
+        }
+      }
     }
     __syncwarp();
   }
