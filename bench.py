@@ -92,7 +92,7 @@ def parse() -> argparse.Namespace:
                     help="where the next step's growth selection forks onto the side stream: at the step's start, "
                          "after the propagation, from just before the sweep with the sweep launched first "
                          "(launch), or from the sweep's end before its tombstones and the combine (post) "
-                         "(auto: after the propagation under Scheme-A, at the sweep's launch on one GPU)")
+                         "(auto: at the sweep's end under Scheme-A, at the sweep's launch on one GPU)")
     ap.add_argument("--graph-priority", action="store_true",
                     help="replay the step's graph with the side stream's selection at low priority")
     ap.add_argument("--trace", default=None,

@@ -229,9 +229,11 @@ class StepFn:
         self.select_after_sweep = self.sharded
         self.select_at_launch = not self.sharded
         self._sweep_fork = None
-        # or from the lowest-|w| sweep's end, before its tombstones and the
-        # combine (the selection then overlaps the latency-bound combine)
-        self.select_post_sweep = False
+        # under Scheme-A from the lowest-|w| sweep's end, before its tombstones
+        # and the combine: the selection then overlaps the latency-bound
+        # combine and ends before the claim (forked after the propagation it
+        # outlasted the step by ~10 us at N=2)
+        self.select_post_sweep = self.sharded
         self._post_fork = None
         # with the prune and growth firing every step, the next step's plan
         # of the lowest-|w| prune is made right after this step's claim, on
