@@ -219,6 +219,40 @@ __global__ void level_totals_kernel(ClaimGeom g, const int32_t *__restrict__ til
   }
 }
 
+// The (domain, tile) matrix's exclusive scan and the per-domain totals in
+// one block, for a matrix of at most kPrepScanMax entries (one launch where
+// the library scan takes two and the totals a third).
+constexpr int kPrepScanThreads = 1024;
+constexpr int64_t kPrepScanMax = int64_t(kPrepScanThreads) * 64;
+__global__ void __launch_bounds__(kPrepScanThreads) prep_scan_kernel(ClaimGeom g, const int32_t *__restrict__ counts,
+                                                                     int32_t *__restrict__ offsets,
+                                                                     int32_t *__restrict__ level_local,
+                                                                     int32_t *__restrict__ level_base,
+                                                                     int32_t *__restrict__ out) {
+  using Scan = cub::BlockScan<int32_t, kPrepScanThreads>;
+  __shared__ typename Scan::TempStorage ts;
+  const int64_t m = g.tiles * g.num_levels;
+  const int64_t per = (m + kPrepScanThreads - 1) / kPrepScanThreads;
+  const int64_t lo = threadIdx.x * per, hi = lo + per < m ? lo + per : m;
+  int32_t mine = 0;
+  for (int64_t j = lo; j < hi; ++j) mine += counts[j];
+  int32_t ex, agg;
+  Scan(ts).ExclusiveSum(mine, ex, agg);
+  for (int64_t j = lo; j < hi; ++j) {
+    offsets[j] = ex;
+    ex += counts[j];
+  }
+  __syncthreads();  // the offsets are written
+  for (int l = threadIdx.x; l < g.num_levels; l += blockDim.x) {
+    const int64_t a = static_cast<int64_t>(l) * g.tiles, z = a + g.tiles - 1;
+    const int32_t base = offsets[a];
+    const int32_t n = offsets[z] + counts[z] - base;
+    level_base[l] = base;
+    level_local[l] = n;
+    if (out) out[l] = n;
+  }
+}
+
 struct CandArgs {
   int topo;
   int64_t k;
@@ -788,7 +822,9 @@ extern "C" int pxb_claim_prepare(int32_t mode, int64_t cap, const int32_t *from_
               o.total);
   cudaStream_t st = as_stream(stream);
   const int64_t m = g.tiles * g.num_levels;
-  PXB_CUDA(cudaMemsetAsync(o.tile_counts, 0, m * 4, st));
+  // the bitmap count writes every (domain, tile) entry; the byte count and
+  // an empty band need the zeros
+  if (free_bitmap == nullptr || cap == 0) PXB_CUDA(cudaMemsetAsync(o.tile_counts, 0, m * 4, st));
   if (cap > 0) {
     DomainArgs a{topo, cap, from_id, dead, unit_level, num_units, num_levels, shard_base, tail_start,
                  free_bitmap, (cap + 31) / 32};
@@ -799,6 +835,12 @@ extern "C" int pxb_claim_prepare(int32_t mode, int64_t cap, const int32_t *from_
       tile_count_kernel<<<grid_for(g.tiles, kClaimWarps, 4), kClaimWarps * 32, 0, st>>>(a, g, o.tile_counts);
       PXB_LAUNCHED("tile_count_kernel");
     }
+  }
+  if (m <= kPrepScanMax) {
+    prep_scan_kernel<<<1, kPrepScanThreads, 0, st>>>(g, o.tile_counts, o.tile_offsets, o.level_local, o.level_base,
+                                                     level_counts);
+    PXB_LAUNCHED("prep_scan_kernel");
+    return PXB_OK;
   }
   size_t tb = o.cub_bytes;
   PXB_CUDA(cub::DeviceScan::ExclusiveSum(o.cub_tmp, tb, o.tile_counts, o.tile_offsets, static_cast<int>(m), st));
