@@ -235,6 +235,10 @@ class StepFn:
         # outlasted the step by ~10 us at N=2)
         self.select_post_sweep = self.sharded
         self._post_fork = None
+        # work that needs every rank's combine but not the threshold bin's
+        # selection (the list take) runs beside that one-CTA selection
+        self._after_combine = None
+        self._take_pending = False
         # with the prune and growth firing every step, the next step's plan
         # of the lowest-|w| prune is made right after this step's claim, on
         # its own stream beside the mirror insert (it reads the histograms
@@ -848,6 +852,9 @@ class StepFn:
                                level_counts=counts, level_before=self.level_before, level_totals=self.level_totals)
                 self._mark("combine")
                 self.launches += 3
+                if self._after_combine is not None:
+                    hook, self._after_combine = self._after_combine, None
+                    hook()
                 if self._lowk_fired:
                     # every rank's sweep is complete: select the threshold
                     # bin's edges, adding every rank's to the barrier's counts
@@ -1203,9 +1210,27 @@ class StepFn:
                          out=out)
         self.launches += 4 + 5
 
+    def _take(self) -> None:
+        """This step's shared list into the claim's inputs, on the plan
+        stream (idle between the step's start and its claim) when there is
+        one; the claim joins it."""
+        main = torch.cuda.current_stream(self.dev)
+        if self.plan_stream is not None:
+            self.plan_stream.wait_stream(main)
+            with torch.cuda.stream(self.plan_stream):
+                K.select_take(self.k, self.win_blocks, self.step_dev, self.claim_next, self.claim_in)
+        else:
+            K.select_take(self.k, self.win_blocks, self.step_dev, self.claim_next, self.claim_in)
+        self._take_pending = True
+        self.launches += 1
+
     def _add_conn(self, state: NetworkState, selected: bool = False) -> GrowthRemainder | None:
         """Growth: the selection (unless it already ran on the side stream)
         and the claim into the post-prune arena."""
+        if self._take_pending:
+            if self.plan_stream is not None:
+                torch.cuda.current_stream(self.dev).wait_stream(self.plan_stream)
+            self._take_pending = False
         ac = self.ac
         if ac is None:
             return None
@@ -1397,6 +1422,10 @@ class StepFn:
             with torch.cuda.stream(self.side):
                 self._select(state, out=self.claim_next, step_dev=self.sel_step_dev)
 
+        if self.shard_select:
+            # every rank's share of this step's list was stored before its
+            # combine signalled: the barrier orders them before the take
+            self._after_combine = self._take
         # the next step's selection reads only levels and the step counter;
         # it overlaps either the whole step, the step from the sweep's launch
         # on, or only what follows the propagation (the persistent sweep
@@ -1419,11 +1448,10 @@ class StepFn:
                 # no sweep ran through the mirror (or without the lowest-|w| prune): fork here
                 self._sweep_fork = self._post_fork = None
                 select_next()
-            if self.shard_select:
-                # every rank's share of this step's list was stored before its
-                # combine signalled: the barrier orders them before this read
-                K.select_take(self.k, self.win_blocks, self.step_dev, self.claim_next, self.claim_in)
-                self.launches += 1
+            if self.shard_select and not self._take_pending:
+                # no combine ran: take the list here
+                self._after_combine = None
+                self._take()
             if self.select_after_sweep and not (at_launch or post):
                 select_next()
             self._loss(state, inputs)
