@@ -221,9 +221,12 @@ __global__ void level_totals_kernel(ClaimGeom g, const int32_t *__restrict__ til
 
 // The (domain, tile) matrix's exclusive scan and the per-domain totals in
 // one block, for a matrix of at most kPrepScanMax entries (one launch where
-// the library scan takes two and the totals a third).
+// the library scan takes two and the totals a third). Each thread reads a
+// contiguous run, so the loads of a warp spread over as many lines as it
+// has lanes: past a few entries per thread the library's multi-block scan
+// is faster (64 per thread measured 30 us against its 6).
 constexpr int kPrepScanThreads = 1024;
-constexpr int64_t kPrepScanMax = int64_t(kPrepScanThreads) * 64;
+constexpr int64_t kPrepScanMax = int64_t(kPrepScanThreads) * 4;
 __global__ void __launch_bounds__(kPrepScanThreads) prep_scan_kernel(ClaimGeom g, const int32_t *__restrict__ counts,
                                                                      int32_t *__restrict__ offsets,
                                                                      int32_t *__restrict__ level_local,
