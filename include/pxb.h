@@ -238,6 +238,14 @@ PXB_API int pxb_fill_f32(int64_t n, float value, float *out, void *stream);
  * (the identity_accumulator of src/plastax/sweep.py:334). */
 PXB_API int pxb_clear_accumulators(int64_t n, float value, float *acc, int64_t *acc_fixed, void *stream);
 
+/* A step's host traffic without copies (a step graph's first and last
+ * kernels): act[ids[i]] = src[i] for i < n, and out[0] = *grown,
+ * out[1] = *overflow (0 for a NULL flag). src and out may be pinned host
+ * memory, through the device pointer pxb_host_device_pointer returns. */
+PXB_API int pxb_scatter_inputs(int32_t n, const int64_t *ids, const float *src, float *act, void *stream);
+PXB_API int pxb_flags_out(const int32_t *grown, const uint8_t *overflow, int32_t *out, void *stream);
+PXB_API int pxb_host_device_pointer(void *host, void **dev_out);
+
 /* Mean-squared-error loss over the outputs (scripts/parity/reference.py:338):
  * seed[out[k]] = act[out[k]] - target[k]; loss_out[0] = 0.5 * sum diff^2
  * (summed in output order). */

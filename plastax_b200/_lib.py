@@ -272,6 +272,9 @@ _SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pxb_propose_select_unique_sharded": (
         c_i32, [c_i32, ctypes.c_uint64, c_i32, c_i32, c_i32, c_i32, c_ptr, c_ptr, c_i32, c_i32, c_i32, c_i32,
                 c_ptr, c_i64, c_i32, c_i32, c_f32, c_f32, ctypes.c_uint32, c_ptr, c_ptr, c_ptr, c_size, c_ptr]),
+    "pxb_scatter_inputs": (c_i32, [c_i32, c_ptr, c_ptr, c_ptr, c_ptr]),
+    "pxb_flags_out": (c_i32, [c_ptr, c_ptr, c_ptr, c_ptr]),
+    "pxb_host_device_pointer": (c_i32, [c_ptr, ctypes.POINTER(c_ptr)]),
     "pxb_select_take": (c_i32, [c_i64, c_i32, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "pxb_mirror_forward": (
         c_i32, [c_ptr, c_ptr, c_i32, c_ptr, c_ptr, c_i32, c_f32, c_ptr, c_ptr, c_ptr, c_i64, c_ptr, c_ptr, c_ptr]),

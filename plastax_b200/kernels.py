@@ -729,3 +729,27 @@ def mirror_forward(m, act: torch.Tensor, acc: torch.Tensor, *, acc_fixed: torch.
 def mirror_insert(m, src: torch.Tensor, dst: torch.Tensor, weight: torch.Tensor, placed: torch.Tensor) -> None:
     call("pxb_mirror_insert", ctypes.byref(m.struct), ctypes.c_int64(src.numel()), ptr(src), ptr(dst), ptr(weight),
          ptr(placed), _stream())
+
+
+def host_device_pointer(t: torch.Tensor) -> int:
+    """The device address of a pinned host tensor (kernels read and write it
+    over the bus)."""
+    out = ctypes.c_void_p()
+    try:
+        call("pxb_host_device_pointer", ctypes.c_void_p(t.data_ptr()), ctypes.byref(out))
+    except _lib.PxbError:
+        # a block of the caching host allocator: under unified addressing
+        # the host address is the device address
+        return int(t.data_ptr())
+    return int(out.value)
+
+
+def scatter_inputs(ids: torch.Tensor, src_ptr: int, act: torch.Tensor) -> None:
+    """act[ids[i]] = src[i], src a device address (pinned host memory through
+    `host_device_pointer`, or device memory)."""
+    call("pxb_scatter_inputs", ctypes.c_int32(ids.numel()), ptr(ids), ctypes.c_void_p(src_ptr), ptr(act), _stream())
+
+
+def flags_out(grown: torch.Tensor | None, overflow: torch.Tensor | None, out_ptr: int) -> None:
+    """out[0] = grown, out[1] = overflow as int32, out a device address."""
+    call("pxb_flags_out", ptr(grown), ptr(overflow), ctypes.c_void_p(out_ptr), _stream())

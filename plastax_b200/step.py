@@ -186,6 +186,7 @@ class StepFn:
         self.step_dev = torch.zeros(1, dtype=torch.int32, device=device)
         self.graph = None  # a captured CUDA graph of the step body (see capture)
         self._host_io = False  # the graph copies the step's host inputs and flags (see capture)
+        self._io_src = None  # while capturing a host-I/O graph: the staging buffer's device address
         self.graph_priority = False  # capture main / side streams at high / low priority (see capture)
         self._graph_exec = None
         # with auto_graphs, steps whose work depends on periodic phases replay
@@ -720,6 +721,10 @@ class StepFn:
         x = inputs.inputs
         if not isinstance(x, torch.Tensor):
             x = torch.from_numpy(np.ascontiguousarray(x, np.float32))
+        if self._io_src is not None:
+            # a host-I/O graph: the kernel reads the pinned staging buffer
+            K.scatter_inputs(self.input_ids, self._io_src, state.units[ACTIVATION.name])
+            return
         x = x.to(self.dev, non_blocking=True).reshape(-1)
         state.units[ACTIVATION.name].index_copy_(0, self.input_ids, x)
 
@@ -1585,10 +1590,10 @@ class StepFn:
         if self._host_io:
             self._host_in = StepInputs(torch.empty(x.numel(), dtype=torch.float32).pin_memory(),
                                        None if t is None else torch.empty(t.numel(), dtype=torch.float32).pin_memory())
-            self._flags_dev = torch.zeros(2, dtype=torch.int32, device=self.dev)
             self.host_flags = torch.zeros(2, dtype=torch.int32).pin_memory()
             self._io_done = torch.cuda.Event()
-            zero = torch.zeros((), dtype=torch.int32, device=self.dev)
+            in_dev = K.host_device_pointer(self._host_in.inputs)
+            flags_dev = K.host_device_pointer(self.host_flags)
         torch.cuda.synchronize(self.dev)
         self._drop_exec()
         prio = self.graph_priority and self.side is not None
@@ -1599,15 +1604,18 @@ class StepFn:
         cap = torch.cuda.Stream(device=self.dev, priority=-1) if prio else None
         with torch.cuda.graph(g, stream=cap):
             if self._host_io:
-                self._graph_in.inputs.copy_(self._host_in.inputs, non_blocking=True)
+                # the first kernel reads the inputs from the pinned staging
+                # buffer and the last writes the flags into the pinned ones:
+                # no copy nodes (targets, when any, are copied)
+                self._io_src = in_dev
                 if t is not None:
                     self._graph_in.targets.copy_(self._host_in.targets, non_blocking=True)
-            self._graph_rem = self._body(state, self._graph_in)
+            try:
+                self._graph_rem = self._body(state, self._graph_in)
+            finally:
+                self._io_src = None
             if self._host_io:
-                grown = state.grown if state.grown is not None else zero
-                overflow = state.overflow if state.overflow is not None else zero
-                torch.stack([grown.to(torch.int32), overflow.to(torch.int32)], out=self._flags_dev)
-                self.host_flags.copy_(self._flags_dev, non_blocking=True)
+                K.flags_out(state.grown, state.overflow, flags_dev)
         if prio:
             exec_ = ctypes.c_void_p()
             _lib.call("pxb_graph_instantiate", ctypes.c_void_p(g.raw_cuda_graph()), ctypes.c_int32(1),
