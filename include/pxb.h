@@ -932,8 +932,8 @@ PXB_API int pxb_mirror_insert(const pxb_mirror *mirror, int64_t k,
  *   1. pxb_lowk_make_plan: from the histograms, the fine threshold bin b* of
  *      the k-th smallest key -- every edge in a bin below b* is pruned; of
  *      the bin itself the `take` smallest keys, unless the whole bin is
- *      needed (one launch: 64 CTAs sum the coarse bins, the last to finish
- *      plans and empties the fine bins the plan prunes);
+ *      needed (two launches: 64 CTAs sum the coarse bins and the last to
+ *      finish plans, a grid empties the fine bins the plan prunes);
  *   2. pxb_mirror_forward_lowk: the forward sweep; an edge below the bin is
  *      tombstoned there (as the fused threshold prune does), an edge in the
  *      bin is listed (key, source level, mirror position);

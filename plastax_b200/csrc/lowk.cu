@@ -72,9 +72,9 @@ __global__ void lowk_hist_build_kernel(int64_t cap, const uint8_t *__restrict__ 
 }
 
 // The plan: the fine threshold bin of the k-th smallest key, the coarse
-// histogram's cut and the fine bin's part, the fine bins wholly pruned
-// emptied ([zero_lo, zero_hi) of the plan). This rank's list counters of the
-// new parity are reset.
+// histogram's cut and the fine bin's part; the fine bins wholly pruned are
+// emptied by lowk_zero_kernel from the plan's [zero_lo, zero_hi). This
+// rank's list counters of the new parity are reset.
 //
 // kPlanCtas CTAs each sum 1024 coarse bins (one 16-byte load per thread)
 // into a partial; the last CTA to arrive scans the partials, then the 1024
@@ -220,11 +220,15 @@ __global__ void __launch_bounds__(kPlanThreads) lowk_plan_kernel(uint32_t *__res
     const long long removed_in_b = fb < 0 ? 0 : (s_below - s_below_c) + (whole ? s_in_bin : take);
     if (t == 0 && cb < kLowkBins && removed_in_b > 0) hist[cb] -= static_cast<uint32_t>(removed_in_b);
   }
-  // the fine bins pruned wholly, [zero_lo, zero_hi): a step's cut moves a
-  // few bins past the last one, so this CTA empties them (the first plan
-  // after a build, from the lowest bin seen, takes longer once)
-  const uint32_t zlo = old_floor < cut ? old_floor : cut;
-  for (uint32_t i = zlo + t; i < cut; i += kPlanThreads) fine[i] = 0u;
+}
+
+// The fine bins the plan prunes wholly: [zero_lo, zero_hi) (between the
+// lowest bin that may hold an edge and the threshold bin).
+__global__ void lowk_zero_kernel(uint32_t *__restrict__ fine, const pxb_lowk_plan *plan) {
+  const uint32_t lo = plan->zero_lo, hi = plan->zero_hi;
+  for (int64_t i = lo + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < hi;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    fine[i] = 0u;
 }
 
 struct SelectArgs {
@@ -499,6 +503,8 @@ extern "C" int pxb_lowk_make_plan(const pxb_lowk *lowk, void *stream) {
   lowk_plan_kernel<<<kPlanCtas, kPlanThreads, 0, st>>>(lowk->hist, lowk->fine, lowk->plan, lowk->k, lowk->count,
                                                         lowk->plan_scratch);
   PXB_LAUNCHED("lowk_plan_kernel");
+  lowk_zero_kernel<<<grid_for(int64_t(1) << 20, 256, 4), 256, 0, st>>>(lowk->fine, lowk->plan);
+  PXB_LAUNCHED("lowk_zero_kernel");
   return PXB_OK;
 }
 
