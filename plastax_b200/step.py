@@ -1593,6 +1593,7 @@ class StepFn:
             self.host_flags = torch.zeros(2, dtype=torch.int32).pin_memory()
             self._io_done = torch.cuda.Event()
             in_dev = K.host_device_pointer(self._host_in.inputs)
+            self._host_in_np = self._host_in.inputs.numpy()  # host copies without torch's dispatch
             flags_dev = K.host_device_pointer(self.host_flags)
         torch.cuda.synchronize(self.dev)
         self._drop_exec()
@@ -1657,11 +1658,16 @@ class StepFn:
                 x = torch.from_numpy(np.ascontiguousarray(x, np.float32))
             dst = self._graph_in
             if self._host_io:
-                # the graph copies from the staging buffers: the previous
-                # replay must have read them
+                # the graph reads the staging buffers: the previous replay
+                # must have read them
                 self._io_done.synchronize()
                 dst = self._host_in
-            dst.inputs.copy_(x.reshape(-1), non_blocking=not self._host_io)
+                if x.device.type == "cpu":
+                    self._host_in_np[:] = x.reshape(-1).numpy()
+                else:
+                    dst.inputs.copy_(x.reshape(-1))
+            else:
+                dst.inputs.copy_(x.reshape(-1), non_blocking=True)
             if inputs.targets is not None and dst.targets is not None:
                 t = inputs.targets
                 if not isinstance(t, torch.Tensor):
